@@ -1,0 +1,266 @@
+"""CPU/fp32 restatement of the Genie-TK triangle hot path -- TEST INFRASTRUCTURE ONLY.
+
+This module is the parity oracle. Only ``tests/``, ``__graft_entry__.smoke()`` and
+the CPU-baseline leg of ``bench.py`` may import it, and only as the checker (or, for
+the baseline, as the timed CPU implementation). The product path in
+``genie-tk_b200/genie_tk`` never imports it.
+
+It restates, in plain fp32 PyTorch tensor algebra, the math of the reference's only
+working implementation (the PyTorch path of northws/Genie-TK). Every function cites
+the reference lines it follows (paths relative to the reference project root).
+
+Pinning: the restatement is checked against golden vectors produced by the
+reference's own modules (``tests/golden/make_golden.py`` imports the reference's
+``src/genie_tk`` after a mechanical docstring repair and records inputs, weights
+and outputs); ``tests/test_oracle_golden.py`` asserts agreement.
+
+Parameters are plain ``dict[str, Tensor]`` keyed exactly like the reference modules'
+``state_dict`` (``linear_a_p.weight``, ``mha.linear_q.weight``, ...), so a state dict
+can be moved between the reference, this oracle and the B200 package unchanged.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Dict, List, Optional
+
+import torch
+
+Params = Dict[str, torch.Tensor]
+
+LN_EPS = 1e-5  # nn.LayerNorm default, used at triangle_mul.py:72-73, triangle_attention.py:70
+
+
+def layer_norm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float = LN_EPS) -> torch.Tensor:
+    """LayerNorm over the last axis with the biased variance (what nn.LayerNorm computes)."""
+    mu = x.mean(dim=-1, keepdim=True)
+    var = (x - mu).square().mean(dim=-1, keepdim=True)
+    return (x - mu) * torch.rsqrt(var + eps) * weight + bias
+
+
+def linear(x: torch.Tensor, p: Params, name: str) -> torch.Tensor:
+    """``nn.Linear`` with weight ``[out, in]`` (primitives.py:43-62)."""
+    y = x @ p[name + ".weight"].t()
+    b = p.get(name + ".bias")
+    return y if b is None else y + b
+
+
+# --------------------------------------------------------------------------------------
+# Triangle multiplicative update -- src/genie_tk/triangle_mul.py:103-132
+# --------------------------------------------------------------------------------------
+
+def trimul_forward(z: torch.Tensor, mask: Optional[torch.Tensor], p: Params, outgoing: bool) -> torch.Tensor:
+    """Update (not z + update) of the triangle multiplicative block.
+
+    Steps (triangle_mul.py): default all-ones mask (:105-106); LN_in (:111);
+    gated, masked projections a and b (:114-117); the per-channel contraction
+    outgoing ``x[b,i,j,c] = sum_k a[b,i,k,c] b[b,j,k,c]`` (:77-89) or incoming
+    ``x[b,i,j,c] = sum_k a[b,k,i,c] b[b,k,j,c]`` (:91-101); LN_out then linear_z
+    (:126-127); output gate sigmoid(linear_g(LN_in(z))) (:130-132).
+    """
+    z = z.float()
+    if mask is None:
+        mask = torch.ones(z.shape[:-1], dtype=z.dtype, device=z.device)
+    m = mask.to(z.dtype).unsqueeze(-1)
+    zn = layer_norm(z, p["layer_norm_in.weight"], p["layer_norm_in.bias"])
+    a = linear(zn, p, "linear_a_p") * torch.sigmoid(linear(zn, p, "linear_a_g")) * m
+    b = linear(zn, p, "linear_b_p") * torch.sigmoid(linear(zn, p, "linear_b_g")) * m
+    if outgoing:
+        x = torch.einsum("bikc,bjkc->bijc", a, b)
+    else:
+        x = torch.einsum("bkic,bkjc->bijc", a, b)
+    x = layer_norm(x, p["layer_norm_out.weight"], p["layer_norm_out.bias"])
+    x = linear(x, p, "linear_z")
+    g = torch.sigmoid(linear(zn, p, "linear_g"))
+    return x * g
+
+
+# --------------------------------------------------------------------------------------
+# Triangle attention -- src/genie_tk/triangle_attention.py:100-143 and
+# src/genie_tk/primitives.py:114-178
+# --------------------------------------------------------------------------------------
+
+def triatt_forward(z: torch.Tensor, mask: Optional[torch.Tensor], p: Params, starting: bool,
+                   no_heads: int, inf: float = 1e9, chunk_rows: int = 0) -> torch.Tensor:
+    """Update of the triangle attention block around the starting (or ending) node.
+
+    Steps: default mask (:106-107); ending node transposes x and mask (:110-112); LN
+    (:115); additive mask bias ``inf*(mask-1)`` on keys, broadcast over heads and
+    queries (:118); triangle bias ``linear(x)`` permuted to ``[*,H,I,J]`` and shared
+    by every row i (:121-129); gated multi-head attention (primitives.py:134-176):
+    q,k,v without bias, scores ``q k^T / sqrt(d)`` then ``+ mask_bias + tri_bias``
+    in that order, softmax over keys, ``@ v``, gate ``sigmoid(linear_g(x))``, then
+    ``linear_o``; ending node transposes back (:140-141).
+
+    ``chunk_rows`` > 0 evaluates the rows i in chunks to bound memory (the math per
+    row is independent); 0 evaluates all rows at once like the reference.
+    """
+    x = z.float()
+    if mask is None:
+        mask = torch.ones(x.shape[:-1], dtype=x.dtype, device=x.device)
+    mask = mask.to(x.dtype)
+    if not starting:
+        x = x.transpose(-2, -3)
+        mask = mask.transpose(-1, -2)
+    x = layer_norm(x, p["layer_norm.weight"], p["layer_norm.bias"])
+    hd = p["mha.linear_q.weight"].shape[0]
+    d = hd // no_heads
+    scale = 1.0 / math.sqrt(d)
+    # triangle bias [B, H, J, K] (query j, key k), identical for every row i
+    tri = linear(x, p, "linear").permute(0, 3, 1, 2)
+    B, N = x.shape[0], x.shape[1]
+    out = torch.empty_like(x)
+    step = N if chunk_rows <= 0 else chunk_rows
+    for r0 in range(0, N, step):
+        xs = x[:, r0:r0 + step]                                   # [B, R, J, C]
+        R = xs.shape[1]
+        q = linear(xs, p, "mha.linear_q").view(B, R, N, no_heads, d).transpose(-2, -3)
+        k = linear(xs, p, "mha.linear_k").view(B, R, N, no_heads, d).transpose(-2, -3)
+        v = linear(xs, p, "mha.linear_v").view(B, R, N, no_heads, d).transpose(-2, -3)
+        s = torch.matmul(q, k.transpose(-1, -2)) * scale          # [B, R, H, J, K]
+        mb = (inf * (mask[:, r0:r0 + step] - 1.0))[:, :, None, None, :]
+        s = s + mb
+        s = s + tri[:, None]
+        a = torch.softmax(s, dim=-1)
+        o = torch.matmul(a, v).transpose(-2, -3).reshape(B, R, N, hd)
+        o = o * torch.sigmoid(linear(xs, p, "mha.linear_g"))
+        out[:, r0:r0 + step] = linear(o, p, "mha.linear_o")
+    if not starting:
+        out = out.transpose(-2, -3)
+    return out
+
+
+# --------------------------------------------------------------------------------------
+# The pair stack -- the explicit residual chain of examples/basic_usage.py:44-78, which
+# equals PairTransformLayer.forward (pair_transform.py:162-195) minus PairTransition
+# and the final mask multiply.
+# --------------------------------------------------------------------------------------
+
+STACK_OPS = ("tri_mul_out", "tri_mul_in", "tri_att_start", "tri_att_end")
+
+
+def stack_forward(z: torch.Tensor, mask: Optional[torch.Tensor], layers: List[Dict[str, Params]],
+                  no_heads: int, chunk_rows: int = 0) -> torch.Tensor:
+    """``z += TriMulOut(z); z += TriMulIn(z); z += TriAttStart(z); z += TriAttEnd(z)`` per layer."""
+    z = z.float().clone()
+    for lp in layers:
+        z = z + trimul_forward(z, mask, lp["tri_mul_out"], outgoing=True)
+        z = z + trimul_forward(z, mask, lp["tri_mul_in"], outgoing=False)
+        z = z + triatt_forward(z, mask, lp["tri_att_start"], starting=True, no_heads=no_heads,
+                               chunk_rows=chunk_rows)
+        z = z + triatt_forward(z, mask, lp["tri_att_end"], starting=False, no_heads=no_heads,
+                               chunk_rows=chunk_rows)
+    return z
+
+
+# --------------------------------------------------------------------------------------
+# Seeded parameters and inputs of the benchmark configurations.
+# Weights ~ N(0, 1/fan_in) in the reference layout [out, in]; biases 0 unless a gate
+# bias of 1 is requested; LayerNorm gamma=1, beta=0 unless ``ln_random``.
+# --------------------------------------------------------------------------------------
+
+def _w(gen: torch.Generator, out_f: int, in_f: int) -> torch.Tensor:
+    return torch.randn(out_f, in_f, generator=gen) / math.sqrt(in_f)
+
+
+def make_trimul_params(c_z: int, c: int, gen: torch.Generator, gate_bias: float = 0.0,
+                       ln_random: bool = False, bias_random: bool = False) -> Params:
+    """Parameters of TriangleMultiplicativeUpdate (triangle_mul.py:64-73), in module order."""
+    p: Params = {}
+    for name, (o, i), gate in (("linear_a_p", (c, c_z), False), ("linear_a_g", (c, c_z), True),
+                               ("linear_b_p", (c, c_z), False), ("linear_b_g", (c, c_z), True),
+                               ("linear_g", (c_z, c_z), True), ("linear_z", (c_z, c), False)):
+        p[name + ".weight"] = _w(gen, o, i)
+        if bias_random:
+            p[name + ".bias"] = 0.1 * torch.randn(o, generator=gen)
+        else:
+            p[name + ".bias"] = torch.full((o,), gate_bias if gate else 0.0)
+    for name, n in (("layer_norm_in", c_z), ("layer_norm_out", c)):
+        if ln_random:
+            p[name + ".weight"] = 1.0 + 0.1 * torch.randn(n, generator=gen)
+            p[name + ".bias"] = 0.1 * torch.randn(n, generator=gen)
+        else:
+            p[name + ".weight"] = torch.ones(n)
+            p[name + ".bias"] = torch.zeros(n)
+    return p
+
+
+def make_triatt_params(c_in: int, c_hidden: int, no_heads: int, gen: torch.Generator,
+                       gate_bias: float = 0.0, ln_random: bool = False,
+                       bias_random: bool = False) -> Params:
+    """Parameters of TriangleAttention (triangle_attention.py:70-82, primitives.py:319-328)."""
+    p: Params = {}
+    if ln_random:
+        p["layer_norm.weight"] = 1.0 + 0.1 * torch.randn(c_in, generator=gen)
+        p["layer_norm.bias"] = 0.1 * torch.randn(c_in, generator=gen)
+    else:
+        p["layer_norm.weight"] = torch.ones(c_in)
+        p["layer_norm.bias"] = torch.zeros(c_in)
+    p["linear.weight"] = _w(gen, no_heads, c_in)
+    p["mha.linear_q.weight"] = _w(gen, c_hidden, c_in)
+    p["mha.linear_k.weight"] = _w(gen, c_hidden, c_in)
+    p["mha.linear_v.weight"] = _w(gen, c_hidden, c_in)
+    p["mha.linear_o.weight"] = _w(gen, c_in, c_hidden)
+    p["mha.linear_o.bias"] = 0.1 * torch.randn(c_in, generator=gen) if bias_random else torch.zeros(c_in)
+    p["mha.linear_g.weight"] = _w(gen, c_hidden, c_in)
+    p["mha.linear_g.bias"] = (0.1 * torch.randn(c_hidden, generator=gen) if bias_random
+                              else torch.full((c_hidden,), gate_bias))
+    return p
+
+
+def make_pair(B: int, N: int, c_z: int, seed: int) -> torch.Tensor:
+    """Pair tensor z ~ N(0, 1) from ``torch.manual_seed(seed)`` semantics (own generator)."""
+    gen = torch.Generator().manual_seed(seed)
+    return torch.randn(B, N, N, c_z, generator=gen)
+
+
+def config_inputs(cfg: int, N: Optional[int] = None, B: Optional[int] = None):
+    """Inputs, mask and parameters of benchmark configuration ``cfg`` (1..5).
+
+    ``N``/``B`` override the size (for small parity cases with the same recipe).
+    The z tensor uses seed ``cfg-1``; weights come from a generator seeded with
+    ``1000 + cfg`` (drawn in module order).
+    """
+    defaults = {1: (1, 128), 2: (2, 384), 3: (1, 512), 4: (1, 768), 5: (1, 1024)}
+    b0, n0 = defaults[cfg]
+    B = b0 if B is None else B
+    N = n0 if N is None else N
+    z = make_pair(B, N, 128, seed=cfg - 1)
+    mask = torch.ones(B, N, N)
+    gen = torch.Generator().manual_seed(1000 + cfg)
+    if cfg == 1:
+        params = make_trimul_params(128, 128, gen)
+    elif cfg == 2:
+        if B > 1:
+            pad = min(64, N // 2)
+            mask[1, -pad:, :] = 0
+            mask[1, :, -pad:] = 0
+        params = make_trimul_params(128, 128, gen, gate_bias=1.0)
+    elif cfg in (3, 4):
+        if cfg == 3:
+            pad = min(32, N // 4)
+            mask[:, -pad:, :] = 0
+            mask[:, :, -pad:] = 0
+        params = make_triatt_params(128, 128, 4, gen, gate_bias=1.0)
+    else:
+        params = []
+        for _ in range(8):
+            params.append({
+                "tri_mul_out": make_trimul_params(128, 128, gen, gate_bias=1.0),
+                "tri_mul_in": make_trimul_params(128, 128, gen, gate_bias=1.0),
+                "tri_att_start": make_triatt_params(128, 128, 4, gen, gate_bias=1.0),
+                "tri_att_end": make_triatt_params(128, 128, 4, gen, gate_bias=1.0),
+            })
+    return z, mask, params
+
+
+def flops_per_pair(op: str, N: int, c_z: int = 128, c: int = 128, H: int = 4, d: int = 32) -> float:
+    """Algorithmic FLOPs per pair (i, j) of one op (reference math, multiply-add = 2)."""
+    if op == "trimul":
+        return 2.0 * N * c + 2.0 * c_z * (4 * c + c_z) + 2.0 * c * c_z
+    if op == "triatt":
+        hd = H * d
+        return 4.0 * N * H * d + 2.0 * (3 * c_z * hd + c_z * hd + hd * c_z + c_z * H)
+    if op == "layer":
+        return 2 * flops_per_pair("trimul", N, c_z, c, H, d) + 2 * flops_per_pair("triatt", N, c_z, c, H, d)
+    raise ValueError(op)

@@ -1,0 +1,132 @@
+"""Generate the golden vectors in this directory from the reference's own modules.
+
+Run in a container where the reference is mounted (it is read from
+``$GTK_REFERENCE_ROOT``, default ``/root/reference``)::
+
+    python tests/golden/make_golden.py
+
+The reference package is imported from a repaired copy (``oracle/reference_copy.py``:
+mechanical docstring repair only). For every case the script builds the reference
+module, loads seeded parameters (``oracle.triangle_oracle.make_*_params``) into it
+with ``load_state_dict``, runs ``module(z, mask)`` in fp32 on the CPU and stores
+inputs, outputs and (for small channel counts) the parameters themselves. For the
+128-channel cases the parameters are regenerated from their seed by the tests and
+pinned by a stored checksum, which keeps the fixtures small.
+"""
+
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, REPO)
+
+from oracle import triangle_oracle as O  # noqa: E402
+from oracle.reference_copy import import_reference  # noqa: E402
+
+
+def param_checksum(p):
+    keys = sorted(p)
+    return np.array([[float(p[k].double().sum()), float(p[k].double().square().sum())] for k in keys])
+
+
+# name -> (op, B, N, c_z, c_hidden, heads, seed, store_params, mask_kind, param_kwargs)
+CASES = {
+    "trimul_out_small": ("trimul_out", 2, 12, 32, 16, 0, 11, True, "ragged", dict(ln_random=True, bias_random=True)),
+    "trimul_in_small": ("trimul_in", 2, 12, 32, 16, 0, 12, True, "ragged", dict(ln_random=True, bias_random=True)),
+    "triatt_start_small": ("triatt_start", 2, 10, 32, 16, 4, 13, True, "rowdead", dict(ln_random=True, bias_random=True)),
+    "triatt_end_small": ("triatt_end", 2, 10, 32, 16, 4, 14, True, "rowdead", dict(ln_random=True, bias_random=True)),
+    "trimul_out_c128": ("trimul_out", 1, 16, 128, 128, 0, 21, False, "ones", dict(ln_random=True, bias_random=True)),
+    "trimul_in_c128": ("trimul_in", 2, 16, 128, 128, 0, 22, False, "pad", dict(gate_bias=1.0)),
+    "triatt_start_c128": ("triatt_start", 1, 16, 128, 128, 4, 23, False, "pad", dict(ln_random=True, bias_random=True)),
+    "triatt_end_c128": ("triatt_end", 1, 16, 128, 128, 4, 24, False, "rowdead", dict(gate_bias=1.0)),
+}
+
+
+def make_mask(kind, B, N, gen):
+    m = torch.ones(B, N, N)
+    if kind == "ragged":
+        m = (torch.rand(B, N, N, generator=gen) > 0.2).float()
+    elif kind == "pad":
+        m[-1, -3:, :] = 0
+        m[-1, :, -3:] = 0
+    elif kind == "rowdead":
+        m[:, 2, :] = 0           # a fully masked row (uniform softmax in the reference)
+        m[:, :, N - 1] = 0       # and a masked key column
+    return m
+
+
+def build_params(op, c_z, c, H, seed, kw):
+    gen = torch.Generator().manual_seed(seed)
+    if op.startswith("trimul"):
+        return O.make_trimul_params(c_z, c, gen, **kw)
+    return O.make_triatt_params(c_z, c, H, gen, **kw)
+
+
+def main():
+    ref = import_reference()
+    torch.set_grad_enabled(False)
+    for name, (op, B, N, c_z, c, H, seed, store_params, mkind, kw) in CASES.items():
+        gen = torch.Generator().manual_seed(seed)
+        z = torch.randn(B, N, N, c_z, generator=gen)
+        mask = make_mask(mkind, B, N, gen)
+        p = build_params(op, c_z, c, H, seed + 100, kw)
+        if op == "trimul_out":
+            mod = ref.TriangleMultiplicationOutgoing(c_z, c, use_fused_kernel=False)
+        elif op == "trimul_in":
+            mod = ref.TriangleMultiplicationIncoming(c_z, c, use_fused_kernel=False)
+        elif op == "triatt_start":
+            mod = ref.TriangleAttentionStartingNode(c_z, c, H, use_fused_kernel=False)
+        else:
+            mod = ref.TriangleAttentionEndingNode(c_z, c, H, use_fused_kernel=False)
+        missing = set(mod.state_dict()) ^ set(p)
+        assert not missing, missing
+        mod.load_state_dict(p)
+        mod.eval()
+        out = mod(z, mask)
+        rec = dict(op=np.array(op), B=B, N=N, c_z=c_z, c_hidden=c, heads=H, param_seed=seed + 100,
+                   z=z.numpy(), mask=mask.numpy(), out=out.numpy(),
+                   param_keys=np.array(sorted(p)), param_checksum=param_checksum(p),
+                   param_kwargs=np.array(repr(kw)))
+        if store_params:
+            for k, v in p.items():
+                rec["p:" + k] = v.numpy()
+        np.savez_compressed(os.path.join(HERE, name + ".npz"), **rec)
+        print(f"{name}: out |max| {out.abs().max():.4f}")
+
+    # A 2-layer stack (the explicit 4-op residual chain) at c_z = 128, N = 8.
+    B, N = 1, 8
+    gen = torch.Generator().manual_seed(31)
+    z0 = torch.randn(B, N, N, 128, generator=gen)
+    mask = torch.ones(B, N, N)
+    pgen = torch.Generator().manual_seed(131)
+    layers = []
+    for _ in range(2):
+        layers.append({
+            "tri_mul_out": O.make_trimul_params(128, 128, pgen, gate_bias=1.0),
+            "tri_mul_in": O.make_trimul_params(128, 128, pgen, gate_bias=1.0),
+            "tri_att_start": O.make_triatt_params(128, 128, 4, pgen, gate_bias=1.0),
+            "tri_att_end": O.make_triatt_params(128, 128, 4, pgen, gate_bias=1.0),
+        })
+    z = z0.clone()
+    for lp in layers:
+        mods = [ref.TriangleMultiplicationOutgoing(128, 128, use_fused_kernel=False),
+                ref.TriangleMultiplicationIncoming(128, 128, use_fused_kernel=False),
+                ref.TriangleAttentionStartingNode(128, 128, 4, use_fused_kernel=False),
+                ref.TriangleAttentionEndingNode(128, 128, 4, use_fused_kernel=False)]
+        for m, key in zip(mods, O.STACK_OPS):
+            m.load_state_dict(lp[key])
+            z = z + m(z, mask)
+    cks = np.concatenate([param_checksum(lp[k]) for lp in layers for k in O.STACK_OPS])
+    np.savez_compressed(os.path.join(HERE, "stack2_c128.npz"), z=z0.numpy(), mask=mask.numpy(), out=z.numpy(),
+                        param_seed=131, n_layers=2, param_checksum=cks)
+    print(f"stack2_c128: out |max| {z.abs().max():.4f}")
+
+
+if __name__ == "__main__":
+    main()
