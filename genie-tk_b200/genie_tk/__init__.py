@@ -1,0 +1,35 @@
+"""genie_tk (B200): drop-in triangle hot path of northws/Genie-TK on hand-written sm_100a kernels.
+
+Public API as in the reference's src/genie_tk/__init__.py:13-50, plus the fused
+``TrianglePairStack`` and the ``ops`` module (thin wrappers over the C ABI).
+"""
+
+__version__ = "0.1.0"
+
+from .triangle_mul import (  # noqa: F401
+    TriangleMultiplicativeUpdate,
+    TriangleMultiplicationOutgoing,
+    TriangleMultiplicationIncoming,
+)
+from .triangle_attention import (  # noqa: F401
+    TriangleAttention,
+    TriangleAttentionStartingNode,
+    TriangleAttentionEndingNode,
+)
+from .pair_transform import PairTransformLayer, PairTransformNet  # noqa: F401
+from .stack import TrianglePairStack  # noqa: F401
+from .utils import has_cuda_kernels, get_device_info  # noqa: F401
+
+__all__ = [
+    "TriangleMultiplicativeUpdate",
+    "TriangleMultiplicationOutgoing",
+    "TriangleMultiplicationIncoming",
+    "TriangleAttention",
+    "TriangleAttentionStartingNode",
+    "TriangleAttentionEndingNode",
+    "PairTransformLayer",
+    "PairTransformNet",
+    "TrianglePairStack",
+    "has_cuda_kernels",
+    "get_device_info",
+]

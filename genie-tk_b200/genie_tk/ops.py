@@ -1,0 +1,231 @@
+"""Thin PyTorch-facing wrappers over the C ABI (``include/genie_tk_b200.h``).
+
+PyTorch is used here only for device memory and streams: every tensor handed to the
+library is a CUDA tensor of the right dtype and layout, outputs and workspaces are
+allocated with ``torch.empty`` on the current stream, and the kernels are enqueued on
+``torch.cuda.current_stream()``. Nothing here computes on the CPU; a CPU tensor, an
+unsupported shape or a missing library raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Dict, Optional
+
+import torch
+
+from . import _lib
+
+SUPPORTED_C = 128
+SUPPORTED_HEADS = 4
+
+_status_bufs: Dict[int, torch.Tensor] = {}
+_workspaces: Dict[tuple, torch.Tensor] = {}
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(device: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def status_buffer(device: torch.device) -> torch.Tensor:
+    """Per-device uint32 status word the kernels OR their timeout bits into."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    buf = _status_bufs.get(idx)
+    if buf is None:
+        buf = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        _status_bufs[idx] = buf
+    return buf
+
+
+def check_status(device: torch.device, reset: bool = True) -> int:
+    """Synchronise and return the device status word (0 = no kernel timed out)."""
+    buf = status_buffer(device)
+    val = int(buf.item())
+    if reset and val:
+        buf.zero_()
+    return val
+
+
+def workspace(device: torch.device, nbytes: int, tag: str = "ws") -> torch.Tensor:
+    """A cached uint8 scratch buffer of at least ``nbytes`` on ``device`` (grown, never shrunk)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    key = (idx, tag)
+    buf = _workspaces.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=torch.device("cuda", idx))
+        _workspaces[key] = buf
+    return buf
+
+
+def release_workspaces() -> None:
+    _workspaces.clear()
+
+
+def _require_cuda(t: torch.Tensor, name: str, dtype=None) -> None:
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise RuntimeError(f"genie_tk (B200): {name} must be a CUDA tensor; this package has no CPU path")
+    if dtype is not None and t.dtype != dtype:
+        raise TypeError(f"genie_tk (B200): {name} must be {dtype}, got {t.dtype}")
+
+
+def prepare_pair(z: torch.Tensor, mask: Optional[torch.Tensor], c_expected: int):
+    """Validate a pair tensor [B, N, N, C] and its mask; return contiguous fp32 views."""
+    _require_cuda(z, "z")
+    if z.dim() != 4 or z.shape[1] != z.shape[2]:
+        raise ValueError(f"pair tensor must be [B, N, N, C], got {tuple(z.shape)}")
+    if z.shape[-1] != c_expected:
+        raise NotImplementedError(f"genie_tk (B200): channel count {z.shape[-1]} not supported (need {c_expected})")
+    zf = z.contiguous() if z.dtype == torch.float32 else z.float().contiguous()
+    mf = None
+    if mask is not None:
+        _require_cuda(mask, "mask")
+        if tuple(mask.shape) != tuple(z.shape[:3]):
+            raise ValueError(f"mask must be [B, N, N], got {tuple(mask.shape)}")
+        mf = mask.float().contiguous() if mask.dtype != torch.float32 else mask.contiguous()
+    return zf, mf
+
+
+# --------------------------------------------------------------------------------------
+# Triangle multiplicative update
+# --------------------------------------------------------------------------------------
+
+TRIMUL_KEYS = ("layer_norm_in.weight", "layer_norm_in.bias", "linear_a_p.weight", "linear_a_p.bias",
+               "linear_a_g.weight", "linear_a_g.bias", "linear_b_p.weight", "linear_b_p.bias",
+               "linear_b_g.weight", "linear_b_g.bias", "linear_g.weight", "linear_g.bias",
+               "linear_z.weight", "linear_z.bias", "layer_norm_out.weight", "layer_norm_out.bias")
+
+
+def pack_trimul(params: Dict[str, torch.Tensor], device: torch.device) -> torch.Tensor:
+    """Pack fp32 module parameters (reference state_dict keys) into the kernels' buffer."""
+    lib = _lib.load()
+    nbytes = lib.gtk_trimul_packed_bytes(SUPPORTED_C, SUPPORTED_C)
+    tensors = []
+    for k in TRIMUL_KEYS:
+        t = params[k].detach()
+        _require_cuda(t, k)
+        tensors.append(t.float().contiguous())
+    if tuple(tensors[2].shape) != (SUPPORTED_C, SUPPORTED_C) or tuple(tensors[12].shape) != (SUPPORTED_C, SUPPORTED_C):
+        raise NotImplementedError("genie_tk (B200): triangle multiplication needs c_z = c_hidden = 128")
+    packed = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    st = _lib.TrimulParams(*[ctypes.c_void_p(t.data_ptr()) for t in tensors])
+    _lib.check(lib.gtk_trimul_pack(ctypes.byref(st), SUPPORTED_C, SUPPORTED_C, _ptr(packed), nbytes, _stream(device)),
+               "gtk_trimul_pack")
+    packed._gtk_keepalive = tensors  # fp32 copies must live until the pack kernel ran
+    return packed
+
+
+def trimul_forward(z: torch.Tensor, mask: Optional[torch.Tensor], packed: torch.Tensor, outgoing: bool,
+                   out: Optional[torch.Tensor] = None, add_residual: bool = False) -> torch.Tensor:
+    """update (or z + update) of the triangle multiplicative block; fp32 [B, N, N, 128]."""
+    lib = _lib.load()
+    zf, mf = prepare_pair(z, mask, SUPPORTED_C)
+    B, N = zf.shape[0], zf.shape[1]
+    if out is None:
+        out = torch.empty_like(zf)
+    _require_cuda(out, "out", torch.float32)
+    nbytes = lib.gtk_trimul_workspace_bytes(B, N, SUPPORTED_C, SUPPORTED_C)
+    ws = workspace(zf.device, nbytes)
+    rc = lib.gtk_trimul_forward(int(outgoing), _ptr(zf), _ptr(mf), _ptr(packed), _ptr(out), int(add_residual),
+                                _ptr(ws), ws.numel(), B, N, SUPPORTED_C, SUPPORTED_C,
+                                _ptr(status_buffer(zf.device)), _stream(zf.device))
+    _lib.check(rc, "gtk_trimul_forward")
+    return out
+
+
+def plane_pitch(N: int) -> int:
+    return int(_lib.load().gtk_plane_pitch(N))
+
+
+def trimul_project(z: torch.Tensor, mask: Optional[torch.Tensor], packed: torch.Tensor):
+    """Stage K1: a, b planes [B, R, 128, ld] (fp16) for the pair rows of z [B, R, N, 128]."""
+    lib = _lib.load()
+    _require_cuda(z, "z", torch.float32)
+    B, R, N = z.shape[0], z.shape[1], z.shape[2]
+    ld = plane_pitch(N)
+    a = torch.empty(B, R, SUPPORTED_C, ld, dtype=torch.float16, device=z.device)
+    b = torch.empty_like(a)
+    _lib.check(lib.gtk_trimul_project(_ptr(z.contiguous()), _ptr(mask), _ptr(packed), _ptr(a), _ptr(b), ld, B, R, N,
+                                      _ptr(status_buffer(z.device)), _stream(z.device)), "gtk_trimul_project")
+    return a, b
+
+
+def trimul_contract(a: torch.Tensor, b: torch.Tensor, outgoing: bool, M: int, Nj: int, K: int,
+                    out: Optional[torch.Tensor] = None, out_scale: float = 1.0) -> torch.Tensor:
+    """Stage K2 on fp16 plane buffers a [B, *, C, lda], b [B, *, C, ldb]; returns x * out_scale
+    as fp16 planes [B, M, C, ldx]."""
+    lib = _lib.load()
+    _require_cuda(a, "a", torch.float16)
+    _require_cuda(b, "b", torch.float16)
+    B, C = a.shape[0], a.shape[2]
+    if out is None:
+        out = torch.empty(B, M, C, plane_pitch(Nj), dtype=torch.float16, device=a.device)
+    _lib.check(lib.gtk_trimul_contract(int(outgoing), _ptr(a), _ptr(b), _ptr(out), B, C, M, Nj, K, a.shape[3],
+                                       b.shape[3], out.shape[3], float(out_scale), _ptr(status_buffer(a.device)),
+                                       _stream(a.device)), "gtk_trimul_contract")
+    return out
+
+
+def trimul_finish(z: torch.Tensor, x: torch.Tensor, packed: torch.Tensor, x_scale: float,
+                  out: Optional[torch.Tensor] = None, add_residual: bool = False) -> torch.Tensor:
+    """Stage K2e: LN_out + linear_z + gate (+ residual) for z [B, R, N, 128] and x planes
+    written with ``out_scale = x_scale``."""
+    lib = _lib.load()
+    _require_cuda(z, "z", torch.float32)
+    B, R, N = z.shape[0], z.shape[1], z.shape[2]
+    if out is None:
+        out = torch.empty_like(z)
+    _lib.check(lib.gtk_trimul_finish(_ptr(z), _ptr(x), x.shape[3], float(x_scale), _ptr(packed), _ptr(out),
+                                     int(add_residual), B, R, N, _ptr(status_buffer(z.device)), _stream(z.device)),
+               "gtk_trimul_finish")
+    return out
+
+
+# --------------------------------------------------------------------------------------
+# Triangle attention
+# --------------------------------------------------------------------------------------
+
+TRIATT_KEYS = ("layer_norm.weight", "layer_norm.bias", "linear.weight", "mha.linear_q.weight",
+               "mha.linear_k.weight", "mha.linear_v.weight", "mha.linear_g.weight", "mha.linear_g.bias",
+               "mha.linear_o.weight", "mha.linear_o.bias")
+
+
+def pack_triatt(params: Dict[str, torch.Tensor], device: torch.device, heads: int) -> torch.Tensor:
+    lib = _lib.load()
+    c_in = params["layer_norm.weight"].shape[0]
+    c_hidden = params["mha.linear_q.weight"].shape[0]
+    if c_in != SUPPORTED_C or c_hidden != SUPPORTED_C or heads != SUPPORTED_HEADS:
+        raise NotImplementedError("genie_tk (B200): triangle attention needs c_in = c_hidden = 128 and 4 heads")
+    nbytes = lib.gtk_triatt_packed_bytes(c_in, c_hidden, heads)
+    tensors = []
+    for k in TRIATT_KEYS:
+        t = params[k].detach()
+        _require_cuda(t, k)
+        tensors.append(t.float().contiguous())
+    packed = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    st = _lib.TriattParams(*[ctypes.c_void_p(t.data_ptr()) for t in tensors])
+    _lib.check(lib.gtk_triatt_pack(ctypes.byref(st), c_in, c_hidden, heads, _ptr(packed), nbytes, _stream(device)),
+               "gtk_triatt_pack")
+    packed._gtk_keepalive = tensors
+    return packed
+
+
+def triatt_forward(z: torch.Tensor, mask: Optional[torch.Tensor], packed: torch.Tensor, starting: bool,
+                   inf: float = 1e9, out: Optional[torch.Tensor] = None, add_residual: bool = False) -> torch.Tensor:
+    """update (or z + update) of triangle attention around the starting / ending node."""
+    lib = _lib.load()
+    zf, mf = prepare_pair(z, mask, SUPPORTED_C)
+    B, N = zf.shape[0], zf.shape[1]
+    if out is None:
+        out = torch.empty_like(zf)
+    _require_cuda(out, "out", torch.float32)
+    nbytes = lib.gtk_triatt_workspace_bytes(B, N, SUPPORTED_C, SUPPORTED_C, SUPPORTED_HEADS)
+    ws = workspace(zf.device, nbytes)
+    rc = lib.gtk_triatt_forward(int(starting), _ptr(zf), _ptr(mf), _ptr(packed), _ptr(out), int(add_residual),
+                                _ptr(ws), ws.numel(), B, N, SUPPORTED_C, SUPPORTED_C, SUPPORTED_HEADS, float(inf),
+                                _ptr(status_buffer(zf.device)), _stream(zf.device))
+    _lib.check(rc, "gtk_triatt_forward")
+    return out

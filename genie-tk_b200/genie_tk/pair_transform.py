@@ -1,0 +1,137 @@
+"""Pair transform layer / network (reference src/genie_tk/pair_transform.py).
+
+The four triangle blocks run on the B200 kernels with the residual add fused into
+their epilogues (``add_residual=True``) whenever the residual can be taken in place.
+``PairTransition`` (LN -> 4x expand -> ReLU -> project) and the row/column dropout
+are outside the triangle hot path; they are evaluated with cuBLAS-backed PyTorch ops
+on the same CUDA tensors.
+"""
+
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+import torch.nn as nn
+from torch import Tensor
+
+from .primitives import Linear
+from .triangle_attention import TriangleAttentionEndingNode, TriangleAttentionStartingNode
+from .triangle_mul import TriangleMultiplicationIncoming, TriangleMultiplicationOutgoing
+
+
+class DropoutRowwise(nn.Module):
+    """Dropout with one mask shared across rows (reference pair_transform.py:26-42)."""
+
+    def __init__(self, p: float):
+        super().__init__()
+        self.p = p
+        self.dropout = nn.Dropout(p)
+
+    def forward(self, x: Tensor) -> Tensor:
+        if not self.training or self.p == 0:
+            return x
+        shape = list(x.shape)
+        shape[-3] = 1
+        return x * self.dropout(x.new_ones(shape))
+
+
+class DropoutColumnwise(nn.Module):
+    """Dropout with one mask shared across columns (reference pair_transform.py:45-61)."""
+
+    def __init__(self, p: float):
+        super().__init__()
+        self.p = p
+        self.dropout = nn.Dropout(p)
+
+    def forward(self, x: Tensor) -> Tensor:
+        if not self.training or self.p == 0:
+            return x
+        shape = list(x.shape)
+        shape[-2] = 1
+        return x * self.dropout(x.new_ones(shape))
+
+
+class PairTransition(nn.Module):
+    """Pair feed-forward (reference pair_transform.py:64-84)."""
+
+    def __init__(self, c_p: int, n: int = 4):
+        super().__init__()
+        self.c_p = c_p
+        self.n = n
+        self.layer_norm = nn.LayerNorm(c_p)
+        self.linear_1 = Linear(c_p, c_p * n)
+        self.relu = nn.ReLU()
+        self.linear_2 = Linear(c_p * n, c_p, init="final")
+
+    def forward(self, p: Tensor, mask: Optional[Tensor] = None) -> Tensor:
+        if not p.is_cuda:
+            raise RuntimeError("genie_tk (B200): PairTransition runs on CUDA tensors only")
+        return self.linear_2(self.relu(self.linear_1(self.layer_norm(p))))
+
+
+class PairTransformLayer(nn.Module):
+    """One pair transform layer (reference pair_transform.py:87-195)."""
+
+    def __init__(self, c_p: int, include_mul_update: bool = True, include_tri_att: bool = True,
+                 c_hidden_mul: int = 128, c_hidden_tri_att: int = 32, n_head_tri: int = 4,
+                 tri_dropout: float = 0.25, pair_transition_n: int = 4, use_fused_kernel: bool = True):
+        super().__init__()
+        self.include_mul_update = include_mul_update
+        self.include_tri_att = include_tri_att
+        if include_mul_update:
+            self.tri_mul_out = TriangleMultiplicationOutgoing(c_z=c_p, c_hidden=c_hidden_mul,
+                                                              use_fused_kernel=use_fused_kernel)
+            self.tri_mul_in = TriangleMultiplicationIncoming(c_z=c_p, c_hidden=c_hidden_mul,
+                                                             use_fused_kernel=use_fused_kernel)
+        if include_tri_att:
+            self.tri_att_start = TriangleAttentionStartingNode(c_in=c_p, c_hidden=c_hidden_tri_att,
+                                                               no_heads=n_head_tri, use_fused_kernel=use_fused_kernel)
+            self.tri_att_end = TriangleAttentionEndingNode(c_in=c_p, c_hidden=c_hidden_tri_att, no_heads=n_head_tri,
+                                                           use_fused_kernel=use_fused_kernel)
+        self.pair_transition = PairTransition(c_p, pair_transition_n)
+        self.dropout_row = DropoutRowwise(tri_dropout)
+        self.dropout_col = DropoutColumnwise(tri_dropout)
+
+    def _fused_residual(self) -> bool:
+        return not (self.training and self.dropout_row.p > 0)
+
+    def forward(self, inputs: Tuple[Tensor, Tensor]) -> Tuple[Tensor, Tensor]:
+        p, p_mask = inputs
+        if not p.is_cuda:
+            raise RuntimeError("genie_tk (B200): PairTransformLayer runs on CUDA tensors only")
+        dtype = p.dtype
+        p = p.float().clone()
+        blocks = []
+        if self.include_mul_update:
+            blocks += [(self.tri_mul_out, self.dropout_row), (self.tri_mul_in, self.dropout_row)]
+        if self.include_tri_att:
+            blocks += [(self.tri_att_start, self.dropout_row), (self.tri_att_end, self.dropout_col)]
+        for block, drop in blocks:
+            if self._fused_residual():
+                block(p, p_mask, out=p, add_residual=True)
+            else:
+                p = p + drop(block(p, p_mask))
+        p = p + self.pair_transition(p, p_mask)
+        p = p * p_mask.unsqueeze(-1).to(p.dtype)
+        return (p.to(dtype), p_mask)
+
+
+class PairTransformNet(nn.Module):
+    """Stack of PairTransformLayers (reference pair_transform.py:198-258)."""
+
+    def __init__(self, c_p: int, n_layers: int, include_mul_update: bool = True, include_tri_att: bool = True,
+                 c_hidden_mul: int = 128, c_hidden_tri_att: int = 32, n_head_tri: int = 4,
+                 tri_dropout: float = 0.25, pair_transition_n: int = 4, use_fused_kernel: bool = True):
+        super().__init__()
+        self.layers = nn.ModuleList([
+            PairTransformLayer(c_p=c_p, include_mul_update=include_mul_update, include_tri_att=include_tri_att,
+                               c_hidden_mul=c_hidden_mul, c_hidden_tri_att=c_hidden_tri_att, n_head_tri=n_head_tri,
+                               tri_dropout=tri_dropout, pair_transition_n=pair_transition_n,
+                               use_fused_kernel=use_fused_kernel)
+            for _ in range(n_layers)])
+
+    def forward(self, p: Tensor, p_mask: Tensor) -> Tensor:
+        for layer in self.layers:
+            p, p_mask = layer((p, p_mask))
+        return p

@@ -1,0 +1,95 @@
+"""Triangle multiplicative update (AlphaFold2 Algorithms 11 & 12) on the B200 kernels.
+
+Drop-in for src/genie_tk/triangle_mul.py of northws/Genie-TK: same class names,
+constructor arguments, parameter names (``state_dict`` compatible) and
+``forward(z, mask=None) -> update`` on pair tensors ``[B, N, N, c_z]``. The whole
+forward (reference ``_forward_pytorch``, triangle_mul.py:103-132) runs as three sm_100a
+kernels behind ``gtk_trimul_forward``; there is no PyTorch compute path here.
+"""
+
+from __future__ import annotations
+
+from functools import partialmethod
+from typing import Optional
+
+import torch
+import torch.nn as nn
+from torch import Tensor
+
+from . import ops
+from .primitives import Linear
+
+
+class _PackCache:
+    """Packed bf16 weights, rebuilt when a parameter tensor or its version changes."""
+
+    def __init__(self):
+        self.key = None
+        self.packed = None
+
+    def get(self, module: nn.Module, build):
+        params = list(module.parameters())
+        key = tuple((p.data_ptr(), p._version, p.device) for p in params)
+        if key != self.key:
+            self.packed = build()
+            self.key = key
+        return self.packed
+
+
+class TriangleMultiplicativeUpdate(nn.Module):
+    """Triangle multiplicative update (reference triangle_mul.py:33-185).
+
+    Args:
+        c_z: pair channels (128 on the B200 kernels)
+        c_hidden: hidden channels of the projections (128)
+        _outgoing: Algorithm 11 (True) or 12 (False)
+        use_fused_kernel: kept for signature compatibility; the fused kernels are the
+            only implementation in this package
+    """
+
+    def __init__(self, c_z: int, c_hidden: int, _outgoing: bool = True, use_fused_kernel: bool = True):
+        super().__init__()
+        self.c_z = c_z
+        self.c_hidden = c_hidden
+        self._outgoing = _outgoing
+        self.use_fused_kernel = use_fused_kernel
+        self.linear_a_p = Linear(c_z, c_hidden)
+        self.linear_a_g = Linear(c_z, c_hidden, init="gating")
+        self.linear_b_p = Linear(c_z, c_hidden)
+        self.linear_b_g = Linear(c_z, c_hidden, init="gating")
+        self.linear_g = Linear(c_z, c_z, init="gating")
+        self.linear_z = Linear(c_hidden, c_z, init="final")
+        self.layer_norm_in = nn.LayerNorm(c_z)
+        self.layer_norm_out = nn.LayerNorm(c_hidden)
+        self.sigmoid = nn.Sigmoid()
+        self._pack = _PackCache()
+
+    def packed_weights(self, device: torch.device) -> Tensor:
+        sd = {k: v for k, v in self.state_dict(keep_vars=True).items()}
+        return self._pack.get(self, lambda: ops.pack_trimul(sd, device))
+
+    def forward(self, z: Tensor, mask: Optional[Tensor] = None, *, out: Optional[Tensor] = None,
+                add_residual: bool = False) -> Tensor:
+        """Return the update for ``z`` ``[B, N, N, c_z]`` (``mask`` ``[B, N, N]``).
+
+        ``add_residual=True`` returns ``z + update`` (``out=z`` updates in place, fp32).
+        """
+        if not z.is_cuda:
+            raise RuntimeError("genie_tk (B200): TriangleMultiplicativeUpdate runs on CUDA tensors only")
+        if self.c_z != ops.SUPPORTED_C or self.c_hidden != ops.SUPPORTED_C:
+            raise NotImplementedError("genie_tk (B200): triangle multiplication needs c_z = c_hidden = 128")
+        packed = self.packed_weights(z.device)
+        res = ops.trimul_forward(z, mask, packed, self._outgoing, out=out, add_residual=add_residual)
+        return res if res.dtype == z.dtype or out is not None else res.to(z.dtype)
+
+
+class TriangleMultiplicationOutgoing(TriangleMultiplicativeUpdate):
+    """Algorithm 11: z_ij += sum_k a_ik * b_jk (reference triangle_mul.py:188-195)."""
+
+    __init__ = partialmethod(TriangleMultiplicativeUpdate.__init__, _outgoing=True)
+
+
+class TriangleMultiplicationIncoming(TriangleMultiplicativeUpdate):
+    """Algorithm 12: z_ij += sum_k a_ki * b_kj (reference triangle_mul.py:198-205)."""
+
+    __init__ = partialmethod(TriangleMultiplicativeUpdate.__init__, _outgoing=False)

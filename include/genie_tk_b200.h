@@ -1,0 +1,144 @@
+/*
+ * genie_tk_b200 -- C ABI of the B200 (sm_100a) triangle hot path.
+ *
+ * This is the drop-in replacement for the reference's native boundary, the pybind11
+ * module `genie_tk._C` declared in kernels/bindings.cpp:13-65 and bound at
+ * kernels/bindings.cpp:69-101 of northws/Genie-TK. Plain C types only: device
+ * pointers, sizes and an opaque CUDA stream (`cudaStream_t` passed as `void*`).
+ *
+ * Conventions
+ *  - Every entry point returns GTK_OK (0) or a negative GTK_ERR_* code; the message
+ *    of the last failure on the calling thread is gtk_last_error_string().
+ *  - The caller owns all memory. Outputs, packed weights and workspaces are allocated
+ *    by the caller (sizes from the *_bytes queries); the library never allocates
+ *    device memory and never synchronises the device. Work is enqueued on `stream`.
+ *  - Pair tensors use the reference layout [B, N, N, C], row-major, fp32; masks are
+ *    fp32 [B, N, N] (NULL = all ones); parameters are the fp32 nn.Linear / LayerNorm
+ *    tensors of the reference modules ([out, in] weights).
+ *  - `status` (optional, may be NULL) is a device uint32 word. A kernel whose bounded
+ *    wait ran out ORs a GTK_STATUS_* bit into it and exits cleanly instead of hanging.
+ *    Read it after synchronising the stream.
+ *  - Supported shapes: c_z = c_hidden = 128 for the multiplicative update; c_in = 128,
+ *    c_hidden = 128 (4 heads x 32) for attention; any B >= 1 and N >= 1. Other shapes
+ *    return GTK_ERR_UNSUPPORTED.
+ *  - Thread safety: entry points may be called concurrently on different streams.
+ */
+#ifndef GENIE_TK_B200_H_
+#define GENIE_TK_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define GTK_API __attribute__((visibility("default")))
+#else
+#define GTK_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GTK_OK 0
+#define GTK_ERR_INVALID_ARG (-1)
+#define GTK_ERR_UNSUPPORTED (-2)
+#define GTK_ERR_ALIGNMENT (-3)
+#define GTK_ERR_WORKSPACE (-4)
+#define GTK_ERR_CUDA (-5)
+#define GTK_ERR_TMAP (-6)
+#define GTK_ERR_DEVICE (-7)
+
+#define GTK_STATUS_TIMEOUT_PRODUCER 0x1u
+#define GTK_STATUS_TIMEOUT_MMA 0x2u
+#define GTK_STATUS_TIMEOUT_CONSUMER 0x4u
+#define GTK_STATUS_TIMEOUT_DRAIN 0x8u
+
+/* Library version (major*10000 + minor*100 + patch). */
+GTK_API int gtk_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+GTK_API const char* gtk_last_error_string(void);
+
+/* ---------------------------------------------------------------------------------
+ * Triangle multiplicative update (Algorithms 11/12).
+ * Replaces `_C.triangle_mul_outgoing` / `_C.triangle_mul_incoming`
+ * (kernels/bindings.cpp:16-26, bound at :73-79) together with the PyTorch glue
+ * around them in `TriangleMultiplicativeUpdate._forward_cuda`
+ * (src/genie_tk/triangle_mul.py:134-169): LN_in, gated masked projections,
+ * the per-channel contraction, LN_out, linear_z and the output gate.
+ * ------------------------------------------------------------------------------- */
+
+/* fp32 device pointers to the parameters of a reference TriangleMultiplicativeUpdate
+ * (src/genie_tk/triangle_mul.py:64-73); weights [out, in]. */
+typedef struct gtk_trimul_params {
+  const float* ln_in_w;
+  const float* ln_in_b;
+  const float* a_p_w;
+  const float* a_p_b;
+  const float* a_g_w;
+  const float* a_g_b;
+  const float* b_p_w;
+  const float* b_p_b;
+  const float* b_g_w;
+  const float* b_g_b;
+  const float* g_w;
+  const float* g_b;
+  const float* z_w;
+  const float* z_b;
+  const float* ln_out_w;
+  const float* ln_out_b;
+} gtk_trimul_params;
+
+/* Bytes of the packed (bf16 / folded) weight buffer. */
+GTK_API size_t gtk_trimul_packed_bytes(int c_z, int c_hidden);
+
+/* Convert module parameters into the packed buffer the kernels read. Re-run after
+ * the parameters change. `packed` must be 256-B aligned. */
+GTK_API int gtk_trimul_pack(const gtk_trimul_params* params, int c_z, int c_hidden, void* packed, size_t packed_bytes,
+                    void* stream);
+
+/* Bytes of scratch space gtk_trimul_forward needs for (B, N). */
+GTK_API size_t gtk_trimul_workspace_bytes(int64_t B, int64_t N, int c_z, int c_hidden);
+
+/* out = update(z)                 (add_residual = 0; the reference module's return value)
+ * out = z + update(z)             (add_residual = 1; out may equal z for in-place use)
+ * outgoing = 1: x_ij = sum_k a_ik b_jk; outgoing = 0: x_ij = sum_k a_ki b_kj.
+ * z, out: fp32 [B, N, N, c_z]; mask: fp32 [B, N, N] or NULL. */
+GTK_API int gtk_trimul_forward(int outgoing, const float* z, const float* mask, const void* packed, float* out,
+                       int add_residual, void* workspace, size_t workspace_bytes, int64_t B, int64_t N, int c_z,
+                       int c_hidden, uint32_t* status, void* stream);
+
+/* Stage entry points (used by tests and by the multi-GPU driver).
+ *
+ * Plane buffers hold one fp16 N-wide row per (pair row, channel):
+ *   X[b][r][c][col], element offset ((b*R + r)*C + c)*ld + col,
+ * with the pitch `ld` (elements) a multiple of 8 and >= the column count.
+ * gtk_plane_pitch(N) gives the pitch the forward entry points use. */
+GTK_API int64_t gtk_plane_pitch(int64_t N);
+
+/* LN_in + gated projections + mask for `rows` pair rows of z ([B, rows, N, c_z]);
+ * writes a and b planes [B, rows, c, ld]. mask: [B, rows, N] or NULL. */
+GTK_API int gtk_trimul_project(const float* z, const float* mask, const void* packed, void* a_planes, void* b_planes,
+                       int64_t ld, int64_t B, int64_t rows, int64_t N, uint32_t* status, void* stream);
+
+/* Per-channel contraction on plane buffers, for every (b, c):
+ *  outgoing: x[b][i][c][j] = sum_k a[b][i][c][k] * bb[b][j][c][k]  (a: [B,M,C,lda], bb: [B,Nj,C,ldb])
+ *  incoming: x[b][i][c][j] = sum_k a[b][k][c][i] * bb[b][k][c][j]  (a: [B,K,C,lda], bb: [B,K,C,ldb])
+ * x: [B, M, C, ldx] holds the fp32 sums times out_scale, rounded to fp16 (saturating);
+ * the forward path uses out_scale = 1/K. i < M, j < Nj, k < K. */
+GTK_API int gtk_trimul_contract(int outgoing, const void* a_planes, const void* b_planes, void* x_planes,
+                                int64_t B, int64_t C, int64_t M, int64_t Nj, int64_t K, int64_t lda, int64_t ldb,
+                                int64_t ldx, float out_scale, uint32_t* status, void* stream);
+
+/* LN_out + linear_z + output gate (+ residual) for `rows` pair rows:
+ * out[b,r,j,:] = gate(z[b,r,j]) * linear_z(LN_out(x[b][r][:][j] / x_scale)) (+ z[b,r,j] if add_residual);
+ * x_scale is the out_scale the x planes were written with. */
+GTK_API int gtk_trimul_finish(const float* z, const void* x_planes, int64_t ldx, float x_scale, const void* packed,
+                              float* out, int add_residual, int64_t B, int64_t rows, int64_t N, uint32_t* status,
+                              void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GENIE_TK_B200_H_ */
