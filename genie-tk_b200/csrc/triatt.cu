@@ -1,0 +1,912 @@
+// Triangle attention around the starting / ending node (AlphaFold2 Algorithms 13/14)
+// on sm_100a.
+//
+// Reference math: src/genie_tk/triangle_attention.py:100-143 and the gated attention of
+// src/genie_tk/primitives.py:114-178. For every row i of the (possibly transposed) pair
+// tensor, H independent attentions over the N positions of that row:
+//   s[j,k] = q_ij.k_ik / sqrt(d) + inf*(mask[i,k]-1) + bias[h,j,k],  bias = LN(z)[j,k].w_h
+//   o[i,j] = softmax_k(s) v_i,  update = linear_o(o * sigmoid(linear_g(LN(z))))
+// Three kernels per call:
+//  K3 triatt_project_kernel LN + one 128x512x128 tcgen05 GEMM per 128-pair tile for q
+//                           (pre-scaled by log2(e)/sqrt(d)), k, v and the gate, plus the
+//                           4-head triangle bias on CUDA cores from the fp32 LN output.
+//  K4 triatt_core_kernel    flash-style attention: S = Q K^T and O += P V on tcgen05 with
+//                           S, P and O in TMEM, online softmax in base 2 with the bias
+//                           and mask bias folded into the logits; the N^3 score tensor is
+//                           never formed. A CTA owns one 128-query tile of one head for 4
+//                           rows i, so each bias tile loaded to shared memory serves 4 rows.
+//                           The epilogue normalises O and applies the gate.
+//  K4e triatt_finish_kernel linear_o (tcgen05) + bias + optional residual add.
+// The ending node is the starting node on z^T: K3 reads and K4e writes the pair tensor
+// through transposed TMA descriptors, and K4 reads the mask with swapped strides.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <string>
+
+#include "gtk_host.h"
+#include "gtk_sm100.cuh"
+
+namespace gtk {
+
+constexpr int kHeads = 4;
+constexpr int kHeadDim = 32;
+constexpr float kLog2e = 1.4426950408889634f;
+
+// ----------------------------------------------------------------------------------
+// Packed weights (fp16 operands, fp32 vectors):
+//   W3 fp16 [512][128]: rows 0-127 linear_q * log2(e)/sqrt(d), 128-255 linear_k,
+//                       256-383 linear_v, 384-511 linear_g
+//   W4 fp16 [128][128]: linear_o
+//   vec fp32: ln_w[128], ln_b[128], w_bias[4][128] * log2(e), b_g[128], b_o[128]
+// ----------------------------------------------------------------------------------
+namespace tapack {
+constexpr size_t kW3 = 0;
+constexpr size_t kW4 = 512 * 128 * 2;
+constexpr size_t kVec = kW4 + 128 * 128 * 2;
+constexpr int kVLnW = 0, kVLnB = 128, kVWb = 256, kVBg = 768, kVBo = 896, kVecFloats = 1024;
+constexpr size_t kBytes = kVec + kVecFloats * 4;
+}  // namespace tapack
+
+__global__ void triatt_pack_kernel(gtk_triatt_params p, uint8_t* packed, float q_scale) {
+  __half* w3 = reinterpret_cast<__half*>(packed + tapack::kW3);
+  __half* w4 = reinterpret_cast<__half*>(packed + tapack::kW4);
+  float* vec = reinterpret_cast<float*>(packed + tapack::kVec);
+  const int tid = blockIdx.x * blockDim.x + threadIdx.x;
+  const int nthreads = gridDim.x * blockDim.x;
+  for (int e = tid; e < 512 * 128; e += nthreads) {
+    const int r = e >> 7, c = e & 127;
+    float v;
+    if (r < 128) v = p.q_w[r * 128 + c] * q_scale;
+    else if (r < 256) v = p.k_w[(r - 128) * 128 + c];
+    else if (r < 384) v = p.v_w[(r - 256) * 128 + c];
+    else v = p.g_w[(r - 384) * 128 + c];
+    w3[e] = f16_sat(v);
+  }
+  for (int e = tid; e < 128 * 128; e += nthreads) w4[e] = f16_sat(p.o_w[e]);
+  for (int e = tid; e < 128; e += nthreads) {
+    vec[tapack::kVLnW + e] = p.ln_w[e];
+    vec[tapack::kVLnB + e] = p.ln_b[e];
+    vec[tapack::kVBg + e] = p.g_b[e];
+    vec[tapack::kVBo + e] = p.o_b[e];
+    for (int h = 0; h < kHeads; ++h) vec[tapack::kVWb + h * 128 + e] = p.bias_w[h * 128 + e] * kLog2e;
+  }
+}
+
+__device__ __forceinline__ float ex2f(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// LayerNorm of one row (as ln_row_to_operand) that also returns the four triangle-bias
+// dot products of the fp32 normalised row with w_bias (already scaled by log2 e).
+__device__ __forceinline__ void ln_row_bias(const uint8_t* ztile, uint8_t* atile, int p, const float* lnw,
+                                            const float* lnb, const float* wb, float (&acc)[4]) {
+  float s = 0.f;
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+#pragma unroll
+    for (int ch = 0; ch < 8; ++ch) {
+      const float4 v = lds_f4(ztile + q * 16384 + swz128(p, ch));
+      s += (v.x + v.y) + (v.z + v.w);
+    }
+  const float mean = s * (1.f / 128.f);
+  float ss = 0.f;
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+#pragma unroll
+    for (int ch = 0; ch < 8; ++ch) {
+      const float4 v = lds_f4(ztile + q * 16384 + swz128(p, ch));
+      const float a = v.x - mean, b = v.y - mean, c = v.z - mean, d = v.w - mean;
+      ss += (a * a + b * b) + (c * c + d * d);
+    }
+  const float rstd = rsqrtf(ss * (1.f / 128.f) + 1e-5f);
+#pragma unroll
+  for (int h = 0; h < 4; ++h) acc[h] = 0.f;
+#pragma unroll 2
+  for (int kh = 0; kh < 2; ++kh)
+#pragma unroll
+    for (int ch = 0; ch < 8; ++ch) {
+      const int c = kh * 64 + ch * 8;
+      const int q = c >> 5, zc = (c & 31) >> 2;
+      const float4 v0 = lds_f4(ztile + q * 16384 + swz128(p, zc));
+      const float4 v1 = lds_f4(ztile + q * 16384 + swz128(p, zc + 1));
+      float y[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) y[e] = (y[e] - mean) * rstd * lnw[c + e] + lnb[c + e];
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const float4 w0 = *reinterpret_cast<const float4*>(wb + h * 128 + c);
+        const float4 w1 = *reinterpret_cast<const float4*>(wb + h * 128 + c + 4);
+        acc[h] += y[0] * w0.x + y[1] * w0.y + y[2] * w0.z + y[3] * w0.w + y[4] * w1.x + y[5] * w1.y +
+                  y[6] * w1.z + y[7] * w1.w;
+      }
+      uint4 o;
+      o.x = pack_f16x2(y[0], y[1]);
+      o.y = pack_f16x2(y[2], y[3]);
+      o.z = pack_f16x2(y[4], y[5]);
+      o.w = pack_f16x2(y[6], y[7]);
+      sts_u4(atile + kh * 16384 + swz128(p, ch), o);
+    }
+}
+
+// ----------------------------------------------------------------------------------
+// K3: LN + q/k/v/g projections + triangle bias. One CTA per 128-pair tile (row i of the
+// problem, columns j0..j0+127). Shared memory: W3 128 KB | z 64 KB | A 32 KB | barriers.
+// Outputs: q, k, v fp16 [B*N(i)][H][N(j)][32]; g fp16 [B*N*N][128] (sigmoid applied);
+// bias fp16 [B][H][N][ldn] (log2 units).
+// ----------------------------------------------------------------------------------
+namespace k3 {
+constexpr uint32_t kW = 0, kZ = 131072, kA = 196608, kBar = 229376;
+constexpr uint32_t kSmem = kBar + 64 + 1024;
+}  // namespace k3
+
+__global__ void __launch_bounds__(128, 1)
+    triatt_project_kernel(const __grid_constant__ CUtensorMap z_map, const __grid_constant__ CUtensorMap w_map,
+                          const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap k_map,
+                          const __grid_constant__ CUtensorMap v_map, const __grid_constant__ CUtensorMap g_map,
+                          const float* __restrict__ vec, __half* __restrict__ bias, int N, int ldn,
+                          uint32_t* status) {
+  extern __shared__ uint8_t dsmem[];
+  uint8_t* smem = align1024(dsmem);
+  uint64_t* zbar = reinterpret_cast<uint64_t*>(smem + k3::kBar);
+  uint64_t* wbar = zbar + 1;
+  uint64_t* mbar = zbar + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(zbar + 3);
+  CtaGuard* guard = reinterpret_cast<CtaGuard*>(tslot + 1);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int j0 = blockIdx.x * 128, i = blockIdx.y, b = blockIdx.z;
+  const int bi = b * N + i;
+
+  if (tid == 0) {
+    guard->abort = 0;
+    mbar_init(zbar, 1);
+    mbar_init(wbar, 1);
+    mbar_init(mbar, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tslot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  if (tid == 0) {
+    mbar_arrive_expect_tx(zbar, 65536);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) tma_load_4d(smem + k3::kZ + q * 16384, &z_map, zbar, q * 32, j0, i, b);
+    mbar_arrive_expect_tx(wbar, 131072);
+#pragma unroll
+    for (int kh = 0; kh < 2; ++kh)
+#pragma unroll
+      for (int rb = 0; rb < 4; ++rb)
+        tma_load_2d(smem + k3::kW + kh * 65536 + rb * 16384, &w_map, wbar, kh * 64, rb * 128);
+  }
+
+  const int p = tid;
+  float bacc[4] = {0.f, 0.f, 0.f, 0.f};
+  if (mbar_wait(zbar, 0, guard, status, kStatusTimeoutConsumer)) {
+    ln_row_bias(smem + k3::kZ, smem + k3::kA, p, vec + tapack::kVLnW, vec + tapack::kVLnB, vec + tapack::kVWb, bacc);
+  }
+  fence_proxy_async_smem();
+  __syncthreads();
+  // the z tile is dead: keep b_g there for the epilogue
+  float* sbg = reinterpret_cast<float*>(smem + k3::kZ);
+  sbg[tid] = vec[tapack::kVBg + tid];
+
+  if (tid == 0 && !guard->abort) {
+    if (mbar_wait(wbar, 0, guard, status, kStatusTimeoutMma)) {
+      tc_fence_after();
+      const uint32_t idesc = make_idesc_f16(128, 256, 0, 0);
+      const uint32_t a0 = smem_u32(smem + k3::kA), w0 = smem_u32(smem + k3::kW);
+#pragma unroll
+      for (int nh = 0; nh < 2; ++nh)
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const int kh = ks >> 2, kin = ks & 3;
+          umma_ss(tmem + nh * 256, make_sdesc(a0 + kh * 16384 + kin * 32, 16, 1024, Swz::k128),
+                  make_sdesc(w0 + kh * 65536 + nh * 32768 + kin * 32, 16, 1024, Swz::k128), idesc, ks > 0 ? 1u : 0u);
+        }
+      umma_commit(mbar);
+    }
+  }
+  __syncthreads();
+  const bool ok = __all_sync(0xffffffffu, mbar_wait(mbar, 0, guard, status, kStatusTimeoutConsumer));
+  tc_fence_after();
+  if (ok) {
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    // q, k, v: [4 heads][128 j][32 d] fp16, 64-B swizzled, at W + {0, 32, 64} KB
+#pragma unroll 1
+    for (int which = 0; which < 3; ++which) {
+      uint8_t* stage = smem + k3::kW + which * 32768;
+#pragma unroll 1
+      for (int h = 0; h < kHeads; ++h) {
+        uint32_t v[32];
+        tmem_ld32(tmem + lane_base + which * 128 + h * 32, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) {
+          uint4 o;
+          o.x = pack_f16x2(__uint_as_float(v[ch * 8 + 0]), __uint_as_float(v[ch * 8 + 1]));
+          o.y = pack_f16x2(__uint_as_float(v[ch * 8 + 2]), __uint_as_float(v[ch * 8 + 3]));
+          o.z = pack_f16x2(__uint_as_float(v[ch * 8 + 4]), __uint_as_float(v[ch * 8 + 5]));
+          o.w = pack_f16x2(__uint_as_float(v[ch * 8 + 6]), __uint_as_float(v[ch * 8 + 7]));
+          sts_u4(stage + h * 8192 + swz64(p, ch), o);
+        }
+      }
+    }
+    // gate: sigmoid(linear_g + b_g) -> [128 j][128] fp16 as two 128-B-swizzled halves at W + 96 KB
+    uint8_t* gstage = smem + k3::kW + 98304;
+#pragma unroll 1
+    for (int cc = 0; cc < 4; ++cc) {
+      uint32_t v[32];
+      tmem_ld32(tmem + lane_base + 384 + cc * 32, v);
+      tmem_wait_ld();
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        float gv[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) gv[e] = sigmoidf_fast(__uint_as_float(v[u * 8 + e]) + sbg[cc * 32 + u * 8 + e]);
+        uint4 o;
+        o.x = pack_f16x2(gv[0], gv[1]);
+        o.y = pack_f16x2(gv[2], gv[3]);
+        o.z = pack_f16x2(gv[4], gv[5]);
+        o.w = pack_f16x2(gv[6], gv[7]);
+        sts_u4(gstage + (cc >> 1) * 16384 + swz128(p, (cc & 1) * 4 + u), o);
+      }
+    }
+    if (j0 + p < N) {
+#pragma unroll
+      for (int h = 0; h < kHeads; ++h)
+        bias[(static_cast<size_t>(b * kHeads + h) * N + i) * ldn + j0 + p] = f16_sat(bacc[h]);
+    }
+  }
+  fence_proxy_async_smem();
+  __syncthreads();
+  if (tid == 0) {
+    if (ok && !guard->abort) {
+#pragma unroll
+      for (int h = 0; h < kHeads; ++h) {
+        tma_store_4d(&q_map, smem + k3::kW + h * 8192, 0, j0, h, bi);
+        tma_store_4d(&k_map, smem + k3::kW + 32768 + h * 8192, 0, j0, h, bi);
+        tma_store_4d(&v_map, smem + k3::kW + 65536 + h * 8192, 0, j0, h, bi);
+      }
+#pragma unroll
+      for (int kh = 0; kh < 2; ++kh) tma_store_3d(&g_map, smem + k3::kW + 98304 + kh * 16384, kh * 64, j0, bi);
+      tma_store_commit();
+      tma_store_wait_read();
+    } else {
+      mbar_wait_drain(zbar, 0);
+      mbar_wait_drain(wbar, 0);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ----------------------------------------------------------------------------------
+// K4: flash-style core. CTA = (query tile jt, head h, batch b, group of kR rows i).
+// Warp 0: producer (TMA for Q, K, V, bias; all lanes stage the mask bias of each step).
+// Warp 1: TMEM allocator + MMA issuer (lane 0). Warps 2-5: softmax, thread = query row j.
+// Step t = kt * kR + r handles key tile kt of row r. TMEM columns: O_r at 32r (0-127),
+// S double buffer at 128 + 128*sb, P (fp16, packed in pairs) double buffer at 384 + 64*pb.
+// ----------------------------------------------------------------------------------
+namespace k4 {
+constexpr int kR = 4;
+constexpr int kKVS = 4;
+constexpr uint32_t kQ = 0;
+constexpr uint32_t kKV = 32768;
+constexpr uint32_t kKVStage = 17408;  // K 8 KB | V 8 KB | mask bias 128 fp32 (512 B) | pad
+constexpr uint32_t kBias = kKV + kKVS * kKVStage;
+constexpr uint32_t kBiasStage = 32768;
+constexpr uint32_t kBar = kBias + 2 * kBiasStage;
+constexpr uint32_t kSmem = kBar + 256 + 1024;
+constexpr int kThreads = 192;
+}  // namespace k4
+
+struct K4Bars {
+  uint64_t q_full;
+  uint64_t kv_full[k4::kKVS];
+  uint64_t kv_empty[k4::kKVS];
+  uint64_t bias_full[2];
+  uint64_t bias_empty[2];
+  uint64_t s_full[2];
+  uint64_t s_free[2];
+  uint64_t p_full[2];
+  uint64_t p_free[2];
+  uint64_t o_ready[k4::kR];
+  uint64_t o_final;
+  uint32_t tslot;
+  CtaGuard guard;
+};
+static_assert(sizeof(K4Bars) <= 256, "K4 barrier block");
+
+__global__ void __launch_bounds__(k4::kThreads, 1)
+    triatt_core_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap k_map,
+                       const __grid_constant__ CUtensorMap v_map, const __grid_constant__ CUtensorMap bias_map,
+                       const float* __restrict__ mask, int64_t mask_si, int64_t mask_sk, float mask_scale,
+                       const __half* __restrict__ gate, __half* __restrict__ og, int N, int n_igroups,
+                       uint32_t* status) {
+  using namespace k4;
+  extern __shared__ uint8_t dsmem[];
+  uint8_t* smem = align1024(dsmem);
+  K4Bars* bars = reinterpret_cast<K4Bars*>(smem + kBar);
+  CtaGuard* guard = &bars->guard;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int jt = blockIdx.x, h = blockIdx.y;
+  const int b = blockIdx.z / n_igroups, ig = blockIdx.z % n_igroups;
+  const int KT = (N + 127) / 128;
+  const int T = KT * kR;
+
+  if (tid == 0) {
+    guard->abort = 0;
+    mbar_init(&bars->q_full, 1);
+    for (int s = 0; s < kKVS; ++s) {
+      mbar_init(&bars->kv_full[s], 33);  // expect_tx arrival + 32 producer lanes after staging the mask bias
+      mbar_init(&bars->kv_empty[s], 1);
+    }
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(&bars->bias_full[x], 1);
+      mbar_init(&bars->bias_empty[x], 128);
+      mbar_init(&bars->s_full[x], 1);
+      mbar_init(&bars->s_free[x], 128);
+      mbar_init(&bars->p_full[x], 128);
+      mbar_init(&bars->p_free[x], 1);
+    }
+    for (int r = 0; r < kR; ++r) mbar_init(&bars->o_ready[r], 1);
+    mbar_init(&bars->o_final, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&bars->tslot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tslot;
+
+  if (warp == 0) {
+    // ------------------------------ producer ------------------------------
+    int issued_kv = 0, issued_bias = 0;
+    bool ok = true;
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&bars->q_full, kR * 8192);
+#pragma unroll
+      for (int r = 0; r < kR; ++r) {
+        const int i = min(ig * kR + r, N - 1);
+        tma_load_4d(smem + kQ + r * 8192, &q_map, &bars->q_full, 0, jt * 128, h, b * N + i);
+      }
+    }
+    for (int kt = 0; kt < KT && ok; ++kt) {
+      const int bs = kt & 1;
+      if (kt >= 2) {
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait(&bars->bias_empty[bs], ((kt >> 1) - 1) & 1, guard, status, kStatusTimeoutProducer));
+        if (!ok) break;
+      }
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&bars->bias_full[bs], kBiasStage);
+#pragma unroll
+        for (int kh = 0; kh < 2; ++kh)
+          tma_load_3d(smem + kBias + bs * kBiasStage + kh * 16384, &bias_map, &bars->bias_full[bs],
+                      kt * 128 + kh * 64, jt * 128, b * kHeads + h);
+      }
+      ++issued_bias;
+      for (int r = 0; r < kR; ++r) {
+        const int t = kt * kR + r, s = t % kKVS;
+        const int i = min(ig * kR + r, N - 1);
+        if (t >= kKVS) {
+          ok = __all_sync(0xffffffffu, mbar_wait(&bars->kv_empty[s], ((t / kKVS) - 1) & 1, guard, status,
+                                                 kStatusTimeoutProducer));
+          if (!ok) break;
+        }
+        uint8_t* stage = smem + kKV + s * kKVStage;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&bars->kv_full[s], 16384);
+          tma_load_4d(stage, &k_map, &bars->kv_full[s], 0, kt * 128, h, b * N + i);
+          tma_load_4d(stage + 8192, &v_map, &bars->kv_full[s], 0, kt * 128, h, b * N + i);
+        }
+        float* mb = reinterpret_cast<float*>(stage + 16384);
+        const float* mrow = mask ? mask + static_cast<int64_t>(b) * N * N + static_cast<int64_t>(i) * mask_si : nullptr;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int kk = kt * 128 + lane * 4 + e;
+          float v;
+          if (kk >= N) v = -INFINITY;
+          else if (mrow) v = (mrow[static_cast<int64_t>(kk) * mask_sk] - 1.f) * mask_scale;
+          else v = 0.f;
+          mb[lane * 4 + e] = v;
+        }
+        mbar_arrive(&bars->kv_full[s]);
+        ++issued_kv;
+      }
+    }
+    if (!ok && lane == 0) {
+      // drain copies still landing in shared memory
+      for (int t = (issued_kv > kKVS ? issued_kv - kKVS : 0); t < issued_kv; ++t)
+        mbar_wait_drain(&bars->kv_full[t % kKVS], (t / kKVS) & 1);
+      for (int kt = (issued_bias > 2 ? issued_bias - 2 : 0); kt < issued_bias; ++kt)
+        mbar_wait_drain(&bars->bias_full[kt & 1], (kt >> 1) & 1);
+      mbar_wait_drain(&bars->q_full, 0);
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer ------------------------------
+    if (lane == 0) {
+      const uint32_t id_s = make_idesc_f16(128, 128, 0, 0);
+      const uint32_t id_o = make_idesc_f16(128, 32, 0, 1);
+      bool ok = mbar_wait(&bars->q_full, 0, guard, status, kStatusTimeoutMma);
+      auto issue_pv = [&](int tp) -> bool {
+        const int rp = tp % kR, kp = tp / kR, sp = tp % kKVS, pb = tp & 1;
+        if (!mbar_wait(&bars->p_full[pb], (tp >> 1) & 1, guard, status, kStatusTimeoutMma)) return false;
+        tc_fence_after();
+        const uint32_t vaddr = smem_u32(smem + kKV + sp * kKVStage + 8192);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          umma_ts(tmem + rp * 32, tmem + 384 + pb * 64 + ks * 8, make_sdesc(vaddr + ks * 1024, 16, 512, Swz::k64),
+                  id_o, (kp > 0 || ks > 0) ? 1u : 0u);
+        umma_commit(&bars->kv_empty[sp]);
+        umma_commit(&bars->p_free[pb]);
+        umma_commit(&bars->o_ready[rp]);
+        return true;
+      };
+      for (int t = 0; t < T && ok; ++t) {
+        const int r = t % kR, s = t % kKVS, sb = t & 1;
+        ok = mbar_wait(&bars->kv_full[s], (t / kKVS) & 1, guard, status, kStatusTimeoutMma);
+        if (ok && t >= 2) ok = mbar_wait(&bars->s_free[sb], ((t >> 1) - 1) & 1, guard, status, kStatusTimeoutMma);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t qaddr = smem_u32(smem + kQ + r * 8192);
+        const uint32_t kaddr = smem_u32(smem + kKV + s * kKVStage);
+#pragma unroll
+        for (int ks = 0; ks < 2; ++ks)
+          umma_ss(tmem + 128 + sb * 128, make_sdesc(qaddr + ks * 32, 16, 512, Swz::k64),
+                  make_sdesc(kaddr + ks * 32, 16, 512, Swz::k64), id_s, ks > 0 ? 1u : 0u);
+        umma_commit(&bars->s_full[sb]);
+        if (t >= 1) ok = issue_pv(t - 1);
+      }
+      if (ok) issue_pv(T - 1);
+      umma_commit(&bars->o_final);  // also drains whatever was issued before an abort
+    }
+  } else {
+    // ------------------------------ softmax ------------------------------
+    const int quarter = warp & 3;
+    const int jrow = quarter * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    float m_run[kR], l_run[kR];
+#pragma unroll
+    for (int r = 0; r < kR; ++r) {
+      m_run[r] = -INFINITY;
+      l_run[r] = 0.f;
+    }
+    bool ok = true;
+    for (int kt = 0; kt < KT && ok; ++kt) {
+      const int bs = kt & 1;
+      ok = __all_sync(0xffffffffu,
+                      mbar_wait(&bars->bias_full[bs], (kt >> 1) & 1, guard, status, kStatusTimeoutConsumer));
+      if (!ok) break;
+      const uint8_t* btile = smem + kBias + bs * kBiasStage;
+#pragma unroll
+      for (int r = 0; r < kR; ++r) {
+        const int t = kt * kR + r, s = t % kKVS, sb = t & 1;
+        bool w = mbar_wait(&bars->kv_full[s], (t / kKVS) & 1, guard, status, kStatusTimeoutConsumer);
+        w = w && mbar_wait(&bars->s_full[sb], (t >> 1) & 1, guard, status, kStatusTimeoutConsumer);
+        ok = __all_sync(0xffffffffu, w);
+        if (!ok) break;
+        tc_fence_after();
+        uint32_t sv[128];
+        tmem_ld32(tmem + lane_off + 128 + sb * 128 + 0, *reinterpret_cast<uint32_t(*)[32]>(sv + 0));
+        tmem_ld32(tmem + lane_off + 128 + sb * 128 + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
+        tmem_ld32(tmem + lane_off + 128 + sb * 128 + 64, *reinterpret_cast<uint32_t(*)[32]>(sv + 64));
+        tmem_ld32(tmem + lane_off + 128 + sb * 128 + 96, *reinterpret_cast<uint32_t(*)[32]>(sv + 96));
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&bars->s_free[sb]);
+
+        const float* mb = reinterpret_cast<const float*>(smem + kKV + s * kKVStage + 16384);
+        float mx = -INFINITY;
+#pragma unroll
+        for (int kh = 0; kh < 2; ++kh)
+#pragma unroll
+          for (int ch = 0; ch < 8; ++ch) {
+            const uint4 bw = *reinterpret_cast<const uint4*>(btile + kh * 16384 + swz128(jrow, ch));
+            const float4 m0 = *reinterpret_cast<const float4*>(mb + kh * 64 + ch * 8);
+            const float4 m1 = *reinterpret_cast<const float4*>(mb + kh * 64 + ch * 8 + 4);
+            const __half2* bh = reinterpret_cast<const __half2*>(&bw);
+            const float2 b0 = __half22float2(bh[0]), b1 = __half22float2(bh[1]);
+            const float2 b2 = __half22float2(bh[2]), b3 = __half22float2(bh[3]);
+            const float bb[8] = {b0.x + m0.x, b0.y + m0.y, b1.x + m0.z, b1.y + m0.w,
+                                 b2.x + m1.x, b2.y + m1.y, b3.x + m1.z, b3.y + m1.w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const int k = kh * 64 + ch * 8 + e;
+              const float x = __uint_as_float(sv[k]) + bb[e];
+              sv[k] = __float_as_uint(x);
+              mx = fmaxf(mx, x);
+            }
+          }
+        const float m_new = fmaxf(m_run[r], mx);
+        const float alpha = ex2f(m_run[r] - m_new);
+        float sum = 0.f;
+#pragma unroll
+        for (int k2 = 0; k2 < 64; ++k2) {
+          const float p0 = ex2f(__uint_as_float(sv[2 * k2]) - m_new);
+          const float p1 = ex2f(__uint_as_float(sv[2 * k2 + 1]) - m_new);
+          sum += p0 + p1;
+          sv[k2] = pack_f16x2(p0, p1);
+        }
+        l_run[r] = l_run[r] * alpha + sum;
+        m_run[r] = m_new;
+        if (kt > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+          // O_r must hold the sum through key tile kt-1 before it is rescaled.
+          ok = __all_sync(0xffffffffu, mbar_wait(&bars->o_ready[r], (kt - 1) & 1, guard, status,
+                                                 kStatusTimeoutConsumer));
+          if (!ok) break;
+          tc_fence_after();
+          uint32_t ov[32];
+          tmem_ld32(tmem + lane_off + r * 32, ov);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+          tmem_st32(tmem + lane_off + r * 32, ov);
+        }
+        if (t >= 2) {
+          ok = __all_sync(0xffffffffu, mbar_wait(&bars->p_free[sb], ((t >> 1) - 1) & 1, guard, status,
+                                                 kStatusTimeoutConsumer));
+          if (!ok) break;
+        }
+        tc_fence_after();
+        tmem_st32(tmem + lane_off + 384 + sb * 64, *reinterpret_cast<uint32_t(*)[32]>(sv + 0));
+        tmem_st32(tmem + lane_off + 384 + sb * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&bars->p_full[sb]);
+      }
+      if (ok) mbar_arrive(&bars->bias_empty[bs]);
+    }
+    // epilogue: O / l, times the gate, to og
+    const bool fin = __all_sync(0xffffffffu, ok && mbar_wait(&bars->o_final, 0, guard, status,
+                                                             kStatusTimeoutConsumer) && !guard->abort);
+    if (fin) {
+      tc_fence_after();
+      const int j = jt * 128 + jrow;
+#pragma unroll 1
+      for (int r = 0; r < kR; ++r) {
+        uint32_t ov[32];
+        tmem_ld32(tmem + lane_off + r * 32, ov);
+        tmem_wait_ld();
+        const int i = ig * kR + r;
+        if (i < N && j < N) {
+          const float inv = 1.f / l_run[r];
+          const size_t pair = (static_cast<size_t>(b) * N + i) * N + j;
+          const uint4* gp = reinterpret_cast<const uint4*>(gate + pair * 128 + h * kHeadDim);
+          uint4* op = reinterpret_cast<uint4*>(og + pair * 128 + h * kHeadDim);
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch) {
+            const uint4 gw = gp[ch];
+            const __half2* gh = reinterpret_cast<const __half2*>(&gw);
+            uint32_t o4[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 gf = __half22float2(gh[e]);
+              o4[e] = pack_f16x2(__uint_as_float(ov[ch * 8 + 2 * e]) * inv * gf.x,
+                                 __uint_as_float(ov[ch * 8 + 2 * e + 1]) * inv * gf.y);
+            }
+            op[ch] = make_uint4(o4[0], o4[1], o4[2], o4[3]);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ----------------------------------------------------------------------------------
+// K4e: update = og W_o^T + b_o (+ residual), written through the (possibly transposed)
+// pair descriptor. Shared memory: og 32 KB | W4 32 KB | z 64 KB | barriers.
+// ----------------------------------------------------------------------------------
+namespace k4e {
+constexpr uint32_t kA = 0, kW = 32768, kZ = 65536, kBar = 131072;
+constexpr uint32_t kSmem = kBar + 64 + 1024;
+}  // namespace k4e
+
+__global__ void __launch_bounds__(128, 1)
+    triatt_finish_kernel(const __grid_constant__ CUtensorMap og_map, const __grid_constant__ CUtensorMap w_map,
+                         const __grid_constant__ CUtensorMap z_map, const __grid_constant__ CUtensorMap out_map,
+                         const float* __restrict__ vec, int N, int add_residual, uint32_t* status) {
+  extern __shared__ uint8_t dsmem[];
+  uint8_t* smem = align1024(dsmem);
+  uint64_t* lbar = reinterpret_cast<uint64_t*>(smem + k4e::kBar);
+  uint64_t* mbar = lbar + 1;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(lbar + 2);
+  CtaGuard* guard = reinterpret_cast<CtaGuard*>(tslot + 1);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int j0 = blockIdx.x * 128, i = blockIdx.y, b = blockIdx.z;
+
+  if (tid == 0) {
+    guard->abort = 0;
+    mbar_init(lbar, 1);
+    mbar_init(mbar, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tslot, 128);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  if (tid == 0) {
+    mbar_arrive_expect_tx(lbar, 32768 + 32768 + (add_residual ? 65536 : 0));
+#pragma unroll
+    for (int kh = 0; kh < 2; ++kh) {
+      tma_load_3d(smem + k4e::kA + kh * 16384, &og_map, lbar, kh * 64, j0, b * N + i);
+      tma_load_2d(smem + k4e::kW + kh * 16384, &w_map, lbar, kh * 64, 0);
+    }
+    if (add_residual) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) tma_load_4d(smem + k4e::kZ + q * 16384, &z_map, lbar, q * 32, j0, i, b);
+    }
+    if (mbar_wait(lbar, 0, guard, status, kStatusTimeoutMma)) {
+      tc_fence_after();
+      const uint32_t a0 = smem_u32(smem + k4e::kA), w0 = smem_u32(smem + k4e::kW);
+      const uint32_t idesc = make_idesc_f16(128, 128, 0, 0);
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const int kh = ks >> 2, kin = ks & 3;
+        umma_ss(tmem, make_sdesc(a0 + kh * 16384 + kin * 32, 16, 1024, Swz::k128),
+                make_sdesc(w0 + kh * 16384 + kin * 32, 16, 1024, Swz::k128), idesc, ks > 0 ? 1u : 0u);
+      }
+      umma_commit(mbar);
+    }
+  }
+  const bool ok = __all_sync(0xffffffffu, mbar_wait(mbar, 0, guard, status, kStatusTimeoutConsumer) &&
+                                              mbar_wait(lbar, 0, guard, status, kStatusTimeoutConsumer));
+  tc_fence_after();
+  if (ok) {
+    const int p = tid;
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const float* bo = vec + tapack::kVBo;
+#pragma unroll 1
+    for (int cc = 0; cc < 4; ++cc) {
+      uint32_t v[32];
+      tmem_ld32(tmem + lane_base + cc * 32, v);
+      tmem_wait_ld();
+      uint8_t* zq = smem + k4e::kZ + cc * 16384;
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        float4 o;
+        const int n = cc * 32 + ch * 4;
+        o.x = __uint_as_float(v[ch * 4 + 0]) + bo[n + 0];
+        o.y = __uint_as_float(v[ch * 4 + 1]) + bo[n + 1];
+        o.z = __uint_as_float(v[ch * 4 + 2]) + bo[n + 2];
+        o.w = __uint_as_float(v[ch * 4 + 3]) + bo[n + 3];
+        if (add_residual) {
+          const float4 zv = lds_f4(zq + swz128(p, ch));
+          o.x += zv.x;
+          o.y += zv.y;
+          o.z += zv.z;
+          o.w += zv.w;
+        }
+        *reinterpret_cast<float4*>(zq + swz128(p, ch)) = o;
+      }
+    }
+  }
+  fence_proxy_async_smem();
+  __syncthreads();
+  if (tid == 0) {
+    if (ok && !guard->abort) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) tma_store_4d(&out_map, smem + k4e::kZ + q * 16384, q * 32, j0, i, b);
+      tma_store_commit();
+      tma_store_wait_read();
+    } else {
+      mbar_wait_drain(lbar, 0);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 128);
+  }
+}
+
+// ----------------------------------------------------------------------------------
+// Host side
+// ----------------------------------------------------------------------------------
+struct TriattWs {
+  size_t q, k, v, g, og, bias, total;
+};
+
+static TriattWs triatt_layout(int64_t B, int64_t N) {
+  TriattWs w;
+  const size_t pair16 = round_up(static_cast<size_t>(B) * N * N * 128 * 2, 256);
+  const size_t bias = round_up(static_cast<size_t>(B) * kHeads * N * round_up(N, 8) * 2, 256);
+  w.q = 0;
+  w.k = w.q + pair16;
+  w.v = w.k + pair16;
+  w.g = w.v + pair16;
+  w.og = w.g + pair16;
+  w.bias = w.og + pair16;
+  w.total = w.bias + bias;
+  return w;
+}
+
+// q / k / v: [B*N(i)][H][N(j)][32] fp16, box (32, 128, 1, 1), 64-B swizzle.
+static int make_head_map(CUtensorMap* m, const void* base, int64_t B, int64_t N) {
+  uint64_t dims[4] = {32, static_cast<uint64_t>(N), static_cast<uint64_t>(kHeads), static_cast<uint64_t>(B * N)};
+  uint64_t strides[3] = {64, static_cast<uint64_t>(N) * 64, static_cast<uint64_t>(N) * 64 * kHeads};
+  uint32_t box[4] = {32, 128, 1, 1};
+  return encode_tmap(m, TmaType::kF16, 4, base, dims, strides, box, 64);
+}
+
+// g / og: [B*N(i)][N(j)][128] fp16, box (64, 128, 1), 128-B swizzle.
+static int make_hidden_map(CUtensorMap* m, const void* base, int64_t B, int64_t N) {
+  uint64_t dims[3] = {128, static_cast<uint64_t>(N), static_cast<uint64_t>(B * N)};
+  uint64_t strides[2] = {256, static_cast<uint64_t>(N) * 256};
+  uint32_t box[3] = {64, 128, 1};
+  return encode_tmap(m, TmaType::kF16, 3, base, dims, strides, box, 128);
+}
+
+// bias: [B*H][N(j)][ldn] fp16, box (64 k, 128 j, 1), 128-B swizzle.
+static int make_bias_map(CUtensorMap* m, const void* base, int64_t B, int64_t N) {
+  const uint64_t ldn = round_up(static_cast<uint64_t>(N), 8);
+  uint64_t dims[3] = {static_cast<uint64_t>(N), static_cast<uint64_t>(N), static_cast<uint64_t>(B * kHeads)};
+  uint64_t strides[2] = {ldn * 2, ldn * 2 * N};
+  uint32_t box[3] = {64, 128, 1};
+  return encode_tmap(m, TmaType::kF16, 3, base, dims, strides, box, 128);
+}
+
+static int triatt_check(int c_in, int c_hidden, int heads) {
+  if (c_in != 128 || c_hidden != 128 || heads != kHeads)
+    return fail(GTK_ERR_UNSUPPORTED, "triatt: only c_in = c_hidden = 128 with 4 heads of 32 is implemented");
+  return GTK_OK;
+}
+
+}  // namespace gtk
+
+using namespace gtk;
+
+extern "C" {
+
+size_t gtk_triatt_packed_bytes(int c_in, int c_hidden, int heads) {
+  if (c_in != 128 || c_hidden != 128 || heads != kHeads) return 0;
+  return tapack::kBytes;
+}
+
+int gtk_triatt_pack(const gtk_triatt_params* params, int c_in, int c_hidden, int heads, void* packed,
+                    size_t packed_bytes, void* stream) {
+  if (int e = triatt_check(c_in, c_hidden, heads)) return e;
+  if (!params) return fail(GTK_ERR_INVALID_ARG, "params is NULL");
+  if (int e = check_ptr(packed, "packed", 256)) return e;
+  if (packed_bytes < tapack::kBytes) return fail(GTK_ERR_WORKSPACE, "packed buffer too small");
+  const float* const* pp = reinterpret_cast<const float* const*>(params);
+  for (int i = 0; i < 10; ++i)
+    if (!pp[i]) return fail(GTK_ERR_INVALID_ARG, "a triatt parameter pointer is NULL");
+  if (int e = check_device()) return e;
+  const float q_scale = kLog2e / std::sqrt(static_cast<float>(c_hidden / heads));
+  triatt_pack_kernel<<<64, 256, 0, static_cast<cudaStream_t>(stream)>>>(*params, static_cast<uint8_t*>(packed),
+                                                                         q_scale);
+  return check_launch("triatt_pack_kernel");
+}
+
+size_t gtk_triatt_workspace_bytes(int64_t B, int64_t N, int c_in, int c_hidden, int heads) {
+  if (c_in != 128 || c_hidden != 128 || heads != kHeads || B < 1 || N < 1) return 0;
+  return triatt_layout(B, N).total;
+}
+
+int gtk_triatt_workspace_offsets(int64_t B, int64_t N, int64_t* offsets) {
+  if (!offsets || B < 1 || N < 1) return fail(GTK_ERR_INVALID_ARG, "triatt_workspace_offsets: bad arguments");
+  const TriattWs w = triatt_layout(B, N);
+  offsets[0] = static_cast<int64_t>(w.q);
+  offsets[1] = static_cast<int64_t>(w.k);
+  offsets[2] = static_cast<int64_t>(w.v);
+  offsets[3] = static_cast<int64_t>(w.g);
+  offsets[4] = static_cast<int64_t>(w.og);
+  offsets[5] = static_cast<int64_t>(w.bias);
+  return GTK_OK;
+}
+
+int gtk_triatt_project(int starting, const float* z, const void* packed, void* workspace, int64_t B, int64_t N,
+                       uint32_t* status, void* stream) {
+  if (!dims_ok(B, 65535) || !dims_ok(N, 65535)) return fail(GTK_ERR_INVALID_ARG, "triatt_project: bad B/N");
+  if (int e = check_ptr(z, "z")) return e;
+  if (int e = check_ptr(packed, "packed", 256)) return e;
+  if (int e = check_ptr(workspace, "workspace", 256)) return e;
+  if (int e = check_device()) return e;
+  const TriattWs w = triatt_layout(B, N);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const uint8_t* pk = static_cast<const uint8_t*>(packed);
+  CUtensorMap zm, wm, qm, km, vm, gm;
+  if (int e = make_pair_map(&zm, z, B, N, N, !starting)) return e;
+  if (int e = make_weight_map(&wm, pk + tapack::kW3, 512, 128)) return e;
+  if (int e = make_head_map(&qm, ws + w.q, B, N)) return e;
+  if (int e = make_head_map(&km, ws + w.k, B, N)) return e;
+  if (int e = make_head_map(&vm, ws + w.v, B, N)) return e;
+  if (int e = make_hidden_map(&gm, ws + w.g, B, N)) return e;
+  if (int e = ensure_smem(reinterpret_cast<const void*>(triatt_project_kernel), k3::kSmem)) return e;
+  dim3 grid(static_cast<unsigned>((N + 127) / 128), static_cast<unsigned>(N), static_cast<unsigned>(B));
+  triatt_project_kernel<<<grid, 128, k3::kSmem, static_cast<cudaStream_t>(stream)>>>(
+      zm, wm, qm, km, vm, gm, reinterpret_cast<const float*>(pk + tapack::kVec),
+      reinterpret_cast<__half*>(ws + w.bias), static_cast<int>(N), static_cast<int>(round_up(N, 8)), status);
+  return check_launch("triatt_project_kernel");
+}
+
+int gtk_triatt_core(int starting, const float* mask, void* workspace, int64_t B, int64_t N, float inf,
+                    uint32_t* status, void* stream) {
+  if (!dims_ok(B, 65535) || !dims_ok(N, 65535)) return fail(GTK_ERR_INVALID_ARG, "triatt_core: bad B/N");
+  if (int e = check_ptr(workspace, "workspace", 256)) return e;
+  if (mask && (reinterpret_cast<uintptr_t>(mask) & 3)) return fail(GTK_ERR_ALIGNMENT, "mask is misaligned");
+  if (int e = check_device()) return e;
+  const TriattWs w = triatt_layout(B, N);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  CUtensorMap qm, km, vm, bm;
+  if (int e = make_head_map(&qm, ws + w.q, B, N)) return e;
+  if (int e = make_head_map(&km, ws + w.k, B, N)) return e;
+  if (int e = make_head_map(&vm, ws + w.v, B, N)) return e;
+  if (int e = make_bias_map(&bm, ws + w.bias, B, N)) return e;
+  if (int e = ensure_smem(reinterpret_cast<const void*>(triatt_core_kernel), k4::kSmem)) return e;
+  const int n_ig = static_cast<int>((N + k4::kR - 1) / k4::kR);
+  if (static_cast<int64_t>(B) * n_ig > 2147483647) return fail(GTK_ERR_INVALID_ARG, "triatt_core: grid too large");
+  dim3 grid(static_cast<unsigned>((N + 127) / 128), kHeads, static_cast<unsigned>(B * n_ig));
+  const int64_t si = starting ? N : 1, sk = starting ? 1 : N;
+  triatt_core_kernel<<<grid, k4::kThreads, k4::kSmem, static_cast<cudaStream_t>(stream)>>>(
+      qm, km, vm, bm, mask, si, sk, inf * kLog2e, reinterpret_cast<const __half*>(ws + w.g),
+      reinterpret_cast<__half*>(ws + w.og), static_cast<int>(N), n_ig, status);
+  return check_launch("triatt_core_kernel");
+}
+
+int gtk_triatt_finish(int starting, const float* z, const void* packed, void* workspace, float* out, int add_residual,
+                      int64_t B, int64_t N, uint32_t* status, void* stream) {
+  if (!dims_ok(B, 65535) || !dims_ok(N, 65535)) return fail(GTK_ERR_INVALID_ARG, "triatt_finish: bad B/N");
+  if (int e = check_ptr(out, "out")) return e;
+  if (add_residual)
+    if (int e = check_ptr(z, "z")) return e;
+  if (int e = check_ptr(packed, "packed", 256)) return e;
+  if (int e = check_ptr(workspace, "workspace", 256)) return e;
+  if (int e = check_device()) return e;
+  const TriattWs w = triatt_layout(B, N);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const uint8_t* pk = static_cast<const uint8_t*>(packed);
+  CUtensorMap am, wm, zm, om;
+  if (int e = make_hidden_map(&am, ws + w.og, B, N)) return e;
+  if (int e = make_weight_map(&wm, pk + tapack::kW4, 128, 128)) return e;
+  if (int e = make_pair_map(&zm, add_residual ? z : out, B, N, N, !starting)) return e;
+  if (int e = make_pair_map(&om, out, B, N, N, !starting)) return e;
+  if (int e = ensure_smem(reinterpret_cast<const void*>(triatt_finish_kernel), k4e::kSmem)) return e;
+  dim3 grid(static_cast<unsigned>((N + 127) / 128), static_cast<unsigned>(N), static_cast<unsigned>(B));
+  triatt_finish_kernel<<<grid, 128, k4e::kSmem, static_cast<cudaStream_t>(stream)>>>(
+      am, wm, zm, om, reinterpret_cast<const float*>(pk + tapack::kVec), static_cast<int>(N), add_residual, status);
+  return check_launch("triatt_finish_kernel");
+}
+
+int gtk_triatt_forward(int starting, const float* z, const float* mask, const void* packed, float* out,
+                       int add_residual, void* workspace, size_t workspace_bytes, int64_t B, int64_t N, int c_in,
+                       int c_hidden, int heads, float inf, uint32_t* status, void* stream) {
+  if (int e = triatt_check(c_in, c_hidden, heads)) return e;
+  if (!dims_ok(B, 65535) || !dims_ok(N, 65535)) return fail(GTK_ERR_INVALID_ARG, "triatt: bad B/N");
+  if (workspace_bytes < triatt_layout(B, N).total) return fail(GTK_ERR_WORKSPACE, "triatt: workspace too small");
+  if (int e = gtk_triatt_project(starting, z, packed, workspace, B, N, status, stream)) return e;
+  if (int e = gtk_triatt_core(starting, mask, workspace, B, N, inf, status, stream)) return e;
+  return gtk_triatt_finish(starting, z, packed, workspace, out, add_residual, B, N, status, stream);
+}
+
+}  // extern "C"

@@ -229,3 +229,54 @@ def triatt_forward(z: torch.Tensor, mask: Optional[torch.Tensor], packed: torch.
                                 _ptr(status_buffer(zf.device)), _stream(zf.device))
     _lib.check(rc, "gtk_triatt_forward")
     return out
+
+
+def triatt_workspace(B: int, N: int, device: torch.device):
+    """The forward workspace and the byte offsets of q, k, v, g, og, bias inside it."""
+    lib = _lib.load()
+    nbytes = lib.gtk_triatt_workspace_bytes(B, N, SUPPORTED_C, SUPPORTED_C, SUPPORTED_HEADS)
+    offs = (ctypes.c_int64 * 6)()
+    _lib.check(lib.gtk_triatt_workspace_offsets(B, N, offs), "gtk_triatt_workspace_offsets")
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    return ws, {k: int(offs[n]) for n, k in enumerate(("q", "k", "v", "g", "og", "bias"))}
+
+
+def triatt_stage_views(ws: torch.Tensor, offs, B: int, N: int):
+    """fp16 views of the attention intermediates inside a workspace (problem orientation)."""
+    def view(name, nelem, shape):
+        o = offs[name]
+        return ws[o:o + 2 * nelem].view(torch.float16).view(*shape)
+    H, d = SUPPORTED_HEADS, SUPPORTED_C // SUPPORTED_HEADS
+    ldn = plane_pitch(N)
+    return {
+        "q": view("q", B * N * H * N * d, (B, N, H, N, d)),
+        "k": view("k", B * N * H * N * d, (B, N, H, N, d)),
+        "v": view("v", B * N * H * N * d, (B, N, H, N, d)),
+        "g": view("g", B * N * N * SUPPORTED_C, (B, N, N, SUPPORTED_C)),
+        "og": view("og", B * N * N * SUPPORTED_C, (B, N, N, SUPPORTED_C)),
+        "bias": view("bias", B * H * N * ldn, (B, H, N, ldn)),
+    }
+
+
+def triatt_project(z: torch.Tensor, packed: torch.Tensor, starting: bool, ws: torch.Tensor) -> None:
+    lib = _lib.load()
+    _require_cuda(z, "z", torch.float32)
+    B, N = z.shape[0], z.shape[1]
+    _lib.check(lib.gtk_triatt_project(int(starting), _ptr(z), _ptr(packed), _ptr(ws), B, N,
+                                      _ptr(status_buffer(z.device)), _stream(z.device)), "gtk_triatt_project")
+
+
+def triatt_core(mask: Optional[torch.Tensor], starting: bool, ws: torch.Tensor, B: int, N: int,
+                inf: float = 1e9) -> None:
+    lib = _lib.load()
+    _lib.check(lib.gtk_triatt_core(int(starting), _ptr(mask), _ptr(ws), B, N, float(inf),
+                                   _ptr(status_buffer(ws.device)), _stream(ws.device)), "gtk_triatt_core")
+
+
+def triatt_finish(z: Optional[torch.Tensor], packed: torch.Tensor, starting: bool, ws: torch.Tensor,
+                  out: torch.Tensor, add_residual: bool = False) -> torch.Tensor:
+    lib = _lib.load()
+    B, N = out.shape[0], out.shape[1]
+    _lib.check(lib.gtk_triatt_finish(int(starting), _ptr(z), _ptr(packed), _ptr(ws), _ptr(out), int(add_residual), B,
+                                     N, _ptr(status_buffer(out.device)), _stream(out.device)), "gtk_triatt_finish")
+    return out

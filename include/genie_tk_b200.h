@@ -137,6 +137,55 @@ GTK_API int gtk_trimul_finish(const float* z, const void* x_planes, int64_t ldx,
                               float* out, int add_residual, int64_t B, int64_t rows, int64_t N, uint32_t* status,
                               void* stream);
 
+/* ---------------------------------------------------------------------------------
+ * Triangle attention around the starting / ending node (Algorithms 13/14).
+ * Replaces `_C.triangle_attention_starting` / `_C.triangle_attention_ending`
+ * (kernels/bindings.cpp:30-46, bound at :82-90) together with the PyTorch code of
+ * `TriangleAttention._forward_cuda` (src/genie_tk/triangle_attention.py:145-179), which
+ * in the reference always falls back to `_forward_pytorch` (:100-143): LN, triangle bias,
+ * mask bias inf*(mask-1), gated 4-head attention, linear_o. The ending node is computed
+ * on z^T through transposed descriptors; the result is in z's orientation.
+ * ------------------------------------------------------------------------------- */
+
+/* fp32 device pointers to the parameters of a reference TriangleAttention
+ * (src/genie_tk/triangle_attention.py:70-82, src/genie_tk/primitives.py:319-328). */
+typedef struct gtk_triatt_params {
+  const float* ln_w;   /* layer_norm.weight [c_in] */
+  const float* ln_b;   /* layer_norm.bias [c_in] */
+  const float* bias_w; /* linear.weight [heads, c_in] (triangle bias, no bias term) */
+  const float* q_w;    /* mha.linear_q.weight [c_hidden, c_in] */
+  const float* k_w;    /* mha.linear_k.weight */
+  const float* v_w;    /* mha.linear_v.weight */
+  const float* g_w;    /* mha.linear_g.weight [c_hidden, c_in] */
+  const float* g_b;    /* mha.linear_g.bias [c_hidden] */
+  const float* o_w;    /* mha.linear_o.weight [c_in, c_hidden] */
+  const float* o_b;    /* mha.linear_o.bias [c_in] */
+} gtk_triatt_params;
+
+GTK_API size_t gtk_triatt_packed_bytes(int c_in, int c_hidden, int heads);
+GTK_API int gtk_triatt_pack(const gtk_triatt_params* params, int c_in, int c_hidden, int heads, void* packed,
+                            size_t packed_bytes, void* stream);
+GTK_API size_t gtk_triatt_workspace_bytes(int64_t B, int64_t N, int c_in, int c_hidden, int heads);
+
+/* out = update(z) or z + update(z) (add_residual; out may equal z). `inf` is the module's
+ * mask constant (1e9 in the reference). z, out fp32 [B, N, N, 128]; mask fp32 [B, N, N] or NULL. */
+GTK_API int gtk_triatt_forward(int starting, const float* z, const float* mask, const void* packed, float* out,
+                               int add_residual, void* workspace, size_t workspace_bytes, int64_t B, int64_t N,
+                               int c_in, int c_hidden, int heads, float inf, uint32_t* status, void* stream);
+
+/* Stage entry points over the forward workspace. offsets[6] receives the byte offsets of
+ * q, k, v ([B*N][H][N][32] fp16, q scaled by log2(e)/sqrt(32)), g ([B*N*N][128] fp16,
+ * sigmoid applied), og ([B*N*N][128] fp16, gated attention output) and the triangle bias
+ * ([B][H][N][round_up(N,8)] fp16, in log2 units). All in the orientation of the problem
+ * (z^T for the ending node). */
+GTK_API int gtk_triatt_workspace_offsets(int64_t B, int64_t N, int64_t* offsets);
+GTK_API int gtk_triatt_project(int starting, const float* z, const void* packed, void* workspace, int64_t B,
+                               int64_t N, uint32_t* status, void* stream);
+GTK_API int gtk_triatt_core(int starting, const float* mask, void* workspace, int64_t B, int64_t N, float inf,
+                            uint32_t* status, void* stream);
+GTK_API int gtk_triatt_finish(int starting, const float* z, const void* packed, void* workspace, float* out,
+                              int add_residual, int64_t B, int64_t N, uint32_t* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
