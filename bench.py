@@ -1,0 +1,434 @@
+#!/usr/bin/env python
+"""Benchmark of the triangle pair stack (BASELINE metric: pair-stack layers*N^2/s at N=1024).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: B=1, N=1024, c_z=128, 8 layers of
+[TriMulOut, TriMulIn, TriAttStart, TriAttEnd] with residual adds, all-ones mask, synthetic
+z ~ N(0,1) and weights ~ N(0, 1/fan_in) (gate biases 1). One step = one full 8-layer
+stack forward. The pair tensor (512 MB fp32) is larger than the 126 MB L2, so no flush is
+needed between steps. The stack runs as one CUDA graph of 96 kernel launches; CUDA events
+recorded between the kernels (captured into the graph) give each kernel's device time.
+
+* ``value``: layers*N^2/s over all ranks with inputs resident in HBM (device timing, CUDA
+  events, max over ranks).
+* ``e2e``: the same metric through the public API with host buffers: every step copies z
+  from pinned host memory, runs the stack and copies the full result back.
+* ``roofline``: the dominant kernel against MEASURED_PEAKS.json.
+* ``cpu_baseline``: the reference math (the fp32 PyTorch oracle) on this host's cores, on
+  a row sample of one N=1024 layer (rank 0 at N=1 only).
+
+``--impl reference`` times that CPU implementation alone (rank 0), one layer sample per step.
+
+With --gpus N > 1 every rank currently runs an independent replica of the whole workload
+("parallelism": "replicas"); the row-sharded path is reported separately when present.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import shutil
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "genie-tk_b200"))
+sys.path.insert(0, REPO)
+
+import torch  # noqa: E402
+
+METRIC = "pair-stack layers*N^2/sec at N=1024, c_z=128"
+UNIT = "layers*N^2/s"
+
+# algorithmic work per launch (B=1): FLOPs for tensor-bound kernels, bytes for HBM-bound ones
+def kernel_work(name: str, N: int, B: int = 1):
+    P = B * N * N
+    if name == "triatt_core":
+        return "tensor", 4.0 * B * N ** 3 * 4 * 32          # QK^T + PV, H=4, d=32
+    if name == "trimul_contract":
+        return "tensor", 2.0 * B * N ** 3 * 128             # 128 channel GEMMs of N^3
+    if name == "trimul_project":
+        return "hbm", P * (512 + 4 + 2 * 128 * 2)           # z fp32 + mask in, a, b fp16 out
+    if name == "trimul_finish":
+        return "hbm", P * (128 * 2 + 512 + 512)             # x fp16 + z fp32 in, z fp32 out
+    if name == "triatt_project":
+        return "hbm", P * (512 + 4 * 128 * 2 + 4 * 2)       # z in; q, k, v, g fp16 + bias out
+    if name == "triatt_finish":
+        return "hbm", P * (128 * 2 + 512 + 512)             # og fp16 + z in, z out
+    raise KeyError(name)
+
+
+def layer_flops(N: int) -> float:
+    return 1536.0 * N + 722944.0  # per pair; see oracle.triangle_oracle.flops_per_pair("layer")
+
+
+def load_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "source": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self):
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        exe = shutil.which("nvidia-smi")
+        if not exe:
+            return
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        self.f = open(self.path, "w")
+        self.proc = subprocess.Popen([exe, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                      "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+
+    def stop(self, gpus):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.f.close()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9 or not parts[0].isdigit() or int(parts[0]) not in gpus:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    mx.append(float(parts[2]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, parts[5:9]):
+                    if v.lower().startswith("active"):
+                        reasons.add(n)
+        os.unlink(self.path)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def make_stack(n_layers: int, device, seed: int = 1005):
+    """Random-init weights of the cfg5 architecture: N(0, 1/fan_in), gate biases 1."""
+    import genie_tk
+    stack = genie_tk.TrianglePairStack(n_layers).to(device)
+    gen = torch.Generator(device="cpu").manual_seed(seed)
+    with torch.no_grad():
+        for name, p in stack.named_parameters():
+            kind = name.split(".")[-1]
+            if kind == "weight" and p.dim() == 2:
+                p.copy_(torch.randn(p.shape, generator=gen) / math.sqrt(p.shape[1]))
+            elif kind == "weight":
+                p.fill_(1.0)       # LayerNorm gamma
+            elif name.endswith("linear_a_g.bias") or name.endswith("linear_b_g.bias") or \
+                    name.endswith("linear_g.bias"):
+                p.fill_(1.0)       # gate biases
+            else:
+                p.zero_()
+    return stack
+
+
+def cpu_sample(N: int, rows: int, threads: int):
+    """One N x N layer of the reference math on the host cores, from a row sample."""
+    from oracle import triangle_oracle as O
+    torch.set_num_threads(threads)
+    gen = torch.Generator().manual_seed(4)
+    z = torch.randn(1, N, N, 128, generator=gen)
+    mask = torch.ones(1, N, N)
+    pg = torch.Generator().manual_seed(1005)
+    lp = {"tri_mul_out": O.make_trimul_params(128, 128, pg, gate_bias=1.0),
+          "tri_mul_in": O.make_trimul_params(128, 128, pg, gate_bias=1.0),
+          "tri_att_start": O.make_triatt_params(128, 128, 4, pg, gate_bias=1.0),
+          "tri_att_end": O.make_triatt_params(128, 128, 4, pg, gate_bias=1.0)}
+    return lambda: O.time_layer_sample(z, mask, lp, 4, rows)
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return None
+    N = args.N
+    threads = os.cpu_count() or 1
+    fn = cpu_sample(N, args.cpu_rows, threads)
+    for _ in range(args.warmup):
+        fn()
+    ests, measured = [], 0.0
+    for _ in range(args.steps):
+        est, parts, tot = fn()
+        ests.append(est)
+        measured += tot
+    layer_s = statistics.mean(ests)
+    value = N * N / layer_s
+    sample = (f"one {N}x{N} layer (4 ops) of the reference fp32 PyTorch math per step: row-independent parts "
+              f"over all pairs plus {args.cpu_rows} output rows per op, per-row part scaled to {N} rows")
+    return {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": layer_s * 1e3 * args.layers,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": {"workload": f"cfg5 triangle pair stack, B=1 N={N} c_z=128, "
+                                                        f"{args.layers} layers (CPU row sample)",
+                                            "global_batch": 1, "seq_len": N, "parallelism": "cpu"},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample,
+                             "cpu": cpu_model(), "measured_s": measured},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def run_ours(args, rank, world, device):
+    import genie_tk
+    from genie_tk import ops, stack as stack_mod
+    N, L, B = args.N, args.layers, 1
+    torch.manual_seed(4)
+    gen = torch.Generator(device="cpu").manual_seed(4)
+    z_host = torch.randn(B, N, N, 128, generator=gen).pin_memory()
+    mask = torch.ones(B, N, N, device=device)
+    z0 = z_host.to(device)
+    z = torch.empty_like(z0)
+    stack = make_stack(L, device)
+    stack.prepare(B, N, device)
+
+    # capture one stack step into a graph, with an event between every pair of kernels
+    labels = []
+    events = []
+
+    def hook(label):
+        # a kernel runs between the event recorded with its label and the next event
+        if label != "end":
+            labels.append((label, len(events)))
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        events.append(ev)
+
+    stack.forward_into(z0, z, mask)  # tensor maps / attributes cached outside capture
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream(device=device)
+    s.wait_stream(torch.cuda.current_stream(device))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph, stream=s):
+            stack._run(z0, z, mask, hook)
+    torch.cuda.current_stream(device).wait_stream(s)
+    torch.cuda.synchronize()
+    n_kernels = len(labels)
+    assert n_kernels == L * stack_mod.KERNELS_PER_LAYER
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    ops.check_status(device)
+
+    sampler = ClockSampler()
+    if rank == 0:
+        sampler.start()
+    per_kernel = {}
+    timing_mode = "graph-events"
+    barrier()
+    torch.cuda.synchronize()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_stop = torch.cuda.Event(enable_timing=True)
+    t_start.record()
+    for _ in range(args.steps):
+        graph.replay()
+        if timing_mode == "graph-events":
+            # harvest this replay's per-kernel times (events are overwritten by the next replay)
+            try:
+                events[-1].synchronize()
+                for lab, e in labels:
+                    per_kernel.setdefault(lab, []).append(events[e].elapsed_time(events[e + 1]))
+            except RuntimeError:
+                timing_mode = "eager-events"
+                per_kernel = {}
+    t_stop.record()
+    torch.cuda.synchronize()
+    barrier()
+    elapsed_ms = t_start.elapsed_time(t_stop)
+    clocks = sampler.stop(set(range(world))) if rank == 0 else None
+    if timing_mode == "eager-events":
+        for _ in range(args.steps):
+            labels.clear()
+            events.clear()
+            stack._run(z0, z, mask, hook)
+            torch.cuda.synchronize()
+            for lab, e in labels:
+                per_kernel.setdefault(lab, []).append(events[e].elapsed_time(events[e + 1]))
+    status = ops.check_status(device)
+    if world > 1:
+        t = torch.tensor([elapsed_ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+    ms_per_step = elapsed_ms / args.steps
+    value = world * B * L * N * N / (ms_per_step / 1e3)
+
+    # end to end through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        out_host = torch.empty_like(z_host).pin_memory()
+        cur = torch.cuda.current_stream(device)
+        for _ in range(1):
+            z0.copy_(z_host, non_blocking=True)
+            graph.replay()
+            out_host.copy_(z, non_blocking=True)
+        torch.cuda.synchronize()
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(cur)
+        for _ in range(args.steps):
+            z0.copy_(z_host, non_blocking=True)
+            graph.replay()
+            out_host.copy_(z, non_blocking=True)
+        e1.record(cur)
+        torch.cuda.synchronize()
+        barrier()
+        e_ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([e_ms], device=device)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            e_ms = float(t.item())
+        e2e = {"value": world * B * L * N * N / (e_ms / args.steps / 1e3), "unit": UNIT,
+               "h2d_bytes_per_step": z_host.numel() * 4, "d2h_bytes_per_step": out_host.numel() * 4,
+               "ms_per_step": e_ms / args.steps}
+
+    peaks = load_peaks()
+    kernels = {}
+    total_k = sum(sum(v) for v in per_kernel.values())
+    for lab, times in per_kernel.items():
+        launches = len(times)
+        avg = sum(times) / launches
+        bound, work = kernel_work(lab, N, B)
+        if bound == "tensor":
+            ach = work / (avg / 1e3) / 1e12
+            peak = peaks["bf16_tflops"]
+            unit = "TFLOP/s"
+        else:
+            ach = work / (avg / 1e3) / 1e9
+            peak = peaks["hbm_gbs"]
+            unit = "GB/s"
+        kernels[lab] = {"launches_per_step": launches // args.steps, "avg_ms": round(avg, 4),
+                        "share": round(sum(times) / total_k, 4), "bound": bound, "achieved": round(ach, 1),
+                        "unit": unit, "frac": round(ach / peak, 4)}
+    dom = max(kernels, key=lambda k: kernels[k]["share"])
+    dk = kernels[dom]
+    traffic = read_traffic(dom)
+    roofline = {"kernel": dom, "bound": dk["bound"], "achieved": dk["achieved"],
+                "peak": peaks["bf16_tflops"] if dk["bound"] == "tensor" else peaks["hbm_gbs"],
+                "unit": dk["unit"], "frac": dk["frac"], "traffic": traffic,
+                "peak_source": peaks["source"] + " (MEASURED_PEAKS.json burst)" if peaks["source"] == "measured"
+                else "fallback"}
+    stack_tflops = B * N * N * L * layer_flops(N) / (ms_per_step / 1e3) / 1e12 * world
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16 tensor-core operands, f32 accumulate / f32 residual stream",
+            "data": "synthetic (z ~ N(0,1), weights ~ N(0,1/fan_in), all-ones mask)",
+            "config": {"workload": f"cfg5 triangle pair stack: B={B}, N={N}, c_z=128, c=128, H=4, d=32, "
+                                   f"{L} layers x [TriMulOut, TriMulIn, TriAttStart, TriAttEnd]",
+                       "global_batch": B * world, "seq_len": N, "layers": L,
+                       "parallelism": "replicas" if world > 1 else "single-gpu",
+                       "l2": "inputs larger than L2 (z is 512 MB fp32); no flush"},
+            "stack_tflops": round(stack_tflops, 1),
+            "stack_frac_of_bf16_peak": round(stack_tflops / peaks["bf16_tflops"] / world, 4),
+            "e2e": e2e, "gpu_launches": n_kernels * args.steps, "roofline": roofline, "kernels": kernels,
+            "kernel_timing": timing_mode,
+            "clocks": clocks, "status_word": status}
+    return line
+
+
+def read_traffic(kernel):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary, if present."""
+    path = os.path.join(REPO, "profiles", "traffic.txt")
+    try:
+        with open(path) as f:
+            for line in f:
+                parts = line.split()
+                if len(parts) >= 2 and parts[0] == kernel:
+                    return float(parts[1])
+    except OSError:
+        pass
+    return None
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--N", type=int, default=1024)
+    ap.add_argument("--layers", type=int, default=8)
+    ap.add_argument("--cpu-rows", type=int, default=16)
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        line = run_reference(args, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return 0
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    line = run_ours(args, rank, world, device)
+    if rank == 0 and world == 1 and not args.no_cpu:
+        fn = cpu_sample(args.N, args.cpu_rows, os.cpu_count() or 1)
+        est, parts, measured = fn()
+        line["cpu_baseline"] = {"value": args.N * args.N / est, "unit": UNIT, "cores": os.cpu_count() or 1,
+                                "kind": "port", "cpu": cpu_model(), "measured_s": round(measured, 2),
+                                "sample": f"one {args.N}x{args.N} layer of the reference fp32 PyTorch math "
+                                          f"(oracle port): row-independent parts over all pairs plus "
+                                          f"{args.cpu_rows} output rows per op, per-row part scaled to "
+                                          f"{args.N} rows"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

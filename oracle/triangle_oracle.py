@@ -49,15 +49,9 @@ def linear(x: torch.Tensor, p: Params, name: str) -> torch.Tensor:
 # Triangle multiplicative update -- src/genie_tk/triangle_mul.py:103-132
 # --------------------------------------------------------------------------------------
 
-def trimul_forward(z: torch.Tensor, mask: Optional[torch.Tensor], p: Params, outgoing: bool) -> torch.Tensor:
-    """Update (not z + update) of the triangle multiplicative block.
-
-    Steps (triangle_mul.py): default all-ones mask (:105-106); LN_in (:111);
-    gated, masked projections a and b (:114-117); the per-channel contraction
-    outgoing ``x[b,i,j,c] = sum_k a[b,i,k,c] b[b,j,k,c]`` (:77-89) or incoming
-    ``x[b,i,j,c] = sum_k a[b,k,i,c] b[b,k,j,c]`` (:91-101); LN_out then linear_z
-    (:126-127); output gate sigmoid(linear_g(LN_in(z))) (:130-132).
-    """
+def trimul_prepare(z: torch.Tensor, mask: Optional[torch.Tensor], p: Params):
+    """Row-independent part: default mask (triangle_mul.py:105-106), LN_in (:111) and the
+    gated, masked projections a, b for every pair (:114-117)."""
     z = z.float()
     if mask is None:
         mask = torch.ones(z.shape[:-1], dtype=z.dtype, device=z.device)
@@ -65,14 +59,29 @@ def trimul_forward(z: torch.Tensor, mask: Optional[torch.Tensor], p: Params, out
     zn = layer_norm(z, p["layer_norm_in.weight"], p["layer_norm_in.bias"])
     a = linear(zn, p, "linear_a_p") * torch.sigmoid(linear(zn, p, "linear_a_g")) * m
     b = linear(zn, p, "linear_b_p") * torch.sigmoid(linear(zn, p, "linear_b_g")) * m
+    return zn, a, b
+
+
+def trimul_rows(zn: torch.Tensor, a: torch.Tensor, b: torch.Tensor, p: Params, outgoing: bool,
+                r0: int = 0, r1: Optional[int] = None) -> torch.Tensor:
+    """Output rows [r0, r1): the contraction, outgoing ``x[b,i,j,c] = sum_k a[b,i,k,c] b[b,j,k,c]``
+    (triangle_mul.py:77-89) or incoming ``x[b,i,j,c] = sum_k a[b,k,i,c] b[b,k,j,c]`` (:91-101),
+    then LN_out and linear_z (:126-127) and the output gate (:130-132)."""
+    r1 = zn.shape[1] if r1 is None else r1
     if outgoing:
-        x = torch.einsum("bikc,bjkc->bijc", a, b)
+        x = torch.einsum("bikc,bjkc->bijc", a[:, r0:r1], b)
     else:
-        x = torch.einsum("bkic,bkjc->bijc", a, b)
+        x = torch.einsum("bkic,bkjc->bijc", a[:, :, r0:r1], b)
     x = layer_norm(x, p["layer_norm_out.weight"], p["layer_norm_out.bias"])
     x = linear(x, p, "linear_z")
-    g = torch.sigmoid(linear(zn, p, "linear_g"))
+    g = torch.sigmoid(linear(zn[:, r0:r1], p, "linear_g"))
     return x * g
+
+
+def trimul_forward(z: torch.Tensor, mask: Optional[torch.Tensor], p: Params, outgoing: bool) -> torch.Tensor:
+    """Update (not z + update) of the triangle multiplicative block (triangle_mul.py:103-132)."""
+    zn, a, b = trimul_prepare(z, mask, p)
+    return trimul_rows(zn, a, b, p, outgoing)
 
 
 # --------------------------------------------------------------------------------------
@@ -80,21 +89,10 @@ def trimul_forward(z: torch.Tensor, mask: Optional[torch.Tensor], p: Params, out
 # src/genie_tk/primitives.py:114-178
 # --------------------------------------------------------------------------------------
 
-def triatt_forward(z: torch.Tensor, mask: Optional[torch.Tensor], p: Params, starting: bool,
-                   no_heads: int, inf: float = 1e9, chunk_rows: int = 0) -> torch.Tensor:
-    """Update of the triangle attention block around the starting (or ending) node.
-
-    Steps: default mask (:106-107); ending node transposes x and mask (:110-112); LN
-    (:115); additive mask bias ``inf*(mask-1)`` on keys, broadcast over heads and
-    queries (:118); triangle bias ``linear(x)`` permuted to ``[*,H,I,J]`` and shared
-    by every row i (:121-129); gated multi-head attention (primitives.py:134-176):
-    q,k,v without bias, scores ``q k^T / sqrt(d)`` then ``+ mask_bias + tri_bias``
-    in that order, softmax over keys, ``@ v``, gate ``sigmoid(linear_g(x))``, then
-    ``linear_o``; ending node transposes back (:140-141).
-
-    ``chunk_rows`` > 0 evaluates the rows i in chunks to bound memory (the math per
-    row is independent); 0 evaluates all rows at once like the reference.
-    """
+def triatt_prepare(z: torch.Tensor, mask: Optional[torch.Tensor], p: Params, starting: bool):
+    """Row-independent part: default mask (:106-107); ending node transposes x and mask
+    (:110-112); LN (:115); triangle bias ``linear(x)`` permuted to ``[*,H,J,K]`` (query j,
+    key k), shared by every row i (:121-129)."""
     x = z.float()
     if mask is None:
         mask = torch.ones(x.shape[:-1], dtype=x.dtype, device=x.device)
@@ -103,28 +101,46 @@ def triatt_forward(z: torch.Tensor, mask: Optional[torch.Tensor], p: Params, sta
         x = x.transpose(-2, -3)
         mask = mask.transpose(-1, -2)
     x = layer_norm(x, p["layer_norm.weight"], p["layer_norm.bias"])
+    tri = linear(x, p, "linear").permute(0, 3, 1, 2)
+    return x, mask, tri
+
+
+def triatt_rows(x: torch.Tensor, mask: torch.Tensor, tri: torch.Tensor, p: Params, no_heads: int,
+                inf: float = 1e9, r0: int = 0, r1: Optional[int] = None) -> torch.Tensor:
+    """Rows [r0, r1) of the gated multi-head attention (primitives.py:134-176): q,k,v
+    without bias, scores ``q k^T / sqrt(d)`` then ``+ inf*(mask-1)`` on keys (:118) and
+    ``+ tri_bias``, in that order; softmax over keys; ``@ v``; gate
+    ``sigmoid(linear_g(x))``; ``linear_o``. Result in the problem orientation."""
+    r1 = x.shape[1] if r1 is None else r1
     hd = p["mha.linear_q.weight"].shape[0]
     d = hd // no_heads
     scale = 1.0 / math.sqrt(d)
-    # triangle bias [B, H, J, K] (query j, key k), identical for every row i
-    tri = linear(x, p, "linear").permute(0, 3, 1, 2)
-    B, N = x.shape[0], x.shape[1]
-    out = torch.empty_like(x)
+    B, N = x.shape[0], x.shape[2]
+    xs = x[:, r0:r1]
+    R = xs.shape[1]
+    q = linear(xs, p, "mha.linear_q").view(B, R, N, no_heads, d).transpose(-2, -3)
+    k = linear(xs, p, "mha.linear_k").view(B, R, N, no_heads, d).transpose(-2, -3)
+    v = linear(xs, p, "mha.linear_v").view(B, R, N, no_heads, d).transpose(-2, -3)
+    s = torch.matmul(q, k.transpose(-1, -2)) * scale          # [B, R, H, J, K]
+    s = s + (inf * (mask[:, r0:r1] - 1.0))[:, :, None, None, :]
+    s = s + tri[:, None]
+    a = torch.softmax(s, dim=-1)
+    o = torch.matmul(a, v).transpose(-2, -3).reshape(B, R, N, hd)
+    o = o * torch.sigmoid(linear(xs, p, "mha.linear_g"))
+    return linear(o, p, "mha.linear_o")
+
+
+def triatt_forward(z: torch.Tensor, mask: Optional[torch.Tensor], p: Params, starting: bool,
+                   no_heads: int, inf: float = 1e9, chunk_rows: int = 0) -> torch.Tensor:
+    """Update of the triangle attention block around the starting (or ending) node
+    (triangle_attention.py:100-143). ``chunk_rows`` > 0 evaluates the rows i in chunks
+    to bound memory (rows are independent); 0 evaluates all rows at once like the
+    reference. The ending node transposes back (:140-141)."""
+    x, m, tri = triatt_prepare(z, mask, p, starting)
+    N = x.shape[1]
     step = N if chunk_rows <= 0 else chunk_rows
-    for r0 in range(0, N, step):
-        xs = x[:, r0:r0 + step]                                   # [B, R, J, C]
-        R = xs.shape[1]
-        q = linear(xs, p, "mha.linear_q").view(B, R, N, no_heads, d).transpose(-2, -3)
-        k = linear(xs, p, "mha.linear_k").view(B, R, N, no_heads, d).transpose(-2, -3)
-        v = linear(xs, p, "mha.linear_v").view(B, R, N, no_heads, d).transpose(-2, -3)
-        s = torch.matmul(q, k.transpose(-1, -2)) * scale          # [B, R, H, J, K]
-        mb = (inf * (mask[:, r0:r0 + step] - 1.0))[:, :, None, None, :]
-        s = s + mb
-        s = s + tri[:, None]
-        a = torch.softmax(s, dim=-1)
-        o = torch.matmul(a, v).transpose(-2, -3).reshape(B, R, N, hd)
-        o = o * torch.sigmoid(linear(xs, p, "mha.linear_g"))
-        out[:, r0:r0 + step] = linear(o, p, "mha.linear_o")
+    out = torch.cat([triatt_rows(x, m, tri, p, no_heads, inf, r0, min(N, r0 + step))
+                     for r0 in range(0, N, step)], dim=1)
     if not starting:
         out = out.transpose(-2, -3)
     return out
@@ -264,3 +280,36 @@ def flops_per_pair(op: str, N: int, c_z: int = 128, c: int = 128, H: int = 4, d:
     if op == "layer":
         return 2 * flops_per_pair("trimul", N, c_z, c, H, d) + 2 * flops_per_pair("triatt", N, c_z, c, H, d)
     raise ValueError(op)
+
+
+def time_layer_sample(z: torch.Tensor, mask: Optional[torch.Tensor], lp: Dict[str, Params], no_heads: int,
+                      rows: int):
+    """Wall-clock estimate of one full stack layer on this host, from a row sample.
+
+    Each op is timed in two measured parts: its row-independent part (``*_prepare``:
+    LayerNorm, the a/b projections or the triangle bias over all N^2 pairs) and the
+    per-row part for ``rows`` output rows (``*_rows``). The per-row cost is linear in
+    the number of rows, so the layer time is ``sum(t_prepare + t_rows * N / rows)``.
+    Returns (estimated layer seconds, {op: (t_prepare, t_rows)}, measured seconds).
+    """
+    import time
+    N = z.shape[1]
+    parts = {}
+    total = 0.0
+    with torch.no_grad():
+        for name in STACK_OPS:
+            p = lp[name]
+            t0 = time.perf_counter()
+            if name.startswith("tri_mul"):
+                zn, a, b = trimul_prepare(z, mask, p)
+                t1 = time.perf_counter()
+                trimul_rows(zn, a, b, p, name == "tri_mul_out", 0, rows)
+            else:
+                x, m, tri = triatt_prepare(z, mask, p, name == "tri_att_start")
+                t1 = time.perf_counter()
+                triatt_rows(x, m, tri, p, no_heads, 1e9, 0, rows)
+            t2 = time.perf_counter()
+            parts[name] = (t1 - t0, t2 - t1)
+            total += t2 - t0
+    est = sum(f + r * N / rows for f, r in parts.values())
+    return est, parts, total
