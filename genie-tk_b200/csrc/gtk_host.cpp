@@ -113,6 +113,18 @@ int check_device() {
   return GTK_OK;
 }
 
+int num_sms() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (!cache[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
+}
+
 // 4D map over a pair tensor [B, R, N, 128] (fp32): dims (c, j, r, b), box (32, 128, 1, 1),
 // 128-B swizzle. `transposed` walks z[b, j, r] instead (the ending-node view).
 int make_pair_map(CUtensorMap* m, const float* base, int64_t B, int64_t R, int64_t N, bool transposed) {

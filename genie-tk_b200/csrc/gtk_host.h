@@ -38,6 +38,9 @@ int ensure_smem(const void* kernel, int bytes);
 // Current device must be sm_100 (B200 family). Cached per device.
 int check_device();
 
+// Streaming multiprocessors of the current device (cached per device).
+int num_sms();
+
 inline uint64_t round_up(uint64_t x, uint64_t m) { return (x + m - 1) / m * m; }
 
 // 4D map over a pair tensor [B, R, N, 128] fp32: dims (c, j, r, b), box (32, 128, 1, 1),

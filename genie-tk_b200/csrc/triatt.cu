@@ -296,22 +296,36 @@ __global__ void __launch_bounds__(128, 1)
 
 // ----------------------------------------------------------------------------------
 // K4: flash-style core. CTA = (query tile jt, head h, batch b, group of kR rows i).
-// Warp 0: producer (TMA for Q, K, V, bias; all lanes stage the mask bias of each step).
-// Warp 1: TMEM allocator + MMA issuer (lane 0). Warps 2-5: softmax, thread = query row j.
-// Step t = kt * kR + r handles key tile kt of row r. TMEM columns: O_r at 32r (0-127),
-// S double buffer at 128 + 128*sb, P (fp16, packed in pairs) double buffer at 384 + 64*pb.
+//   warp 0      producer: TMA for Q (once), K, V (4-stage ring) and the bias tile
+//               (2 stages, shared by the kR rows); all lanes stage the mask bias of each
+//               step plus a flag telling whether the step has any masked / absent key;
+//   warp 1      TMEM allocator + MMA issuer (lane 0);
+//   warps 2-5   softmax warpgroup 0 (rows r = 0, 2), warps 6-9 warpgroup 1 (r = 1, 3);
+//               thread = query row j of the tile.
+// Step t = kt * kR + r handles key tile kt of row r and uses S/P buffer t & 1, i.e. each
+// warpgroup owns one S buffer and one P buffer, and the two run concurrently.
+// The triangle bias is added by the tensor core: S = Q K^T + I * Bias, where I is a
+// resident 128x128 identity and the bias tile [j][k] is the MN-major B operand (K = j),
+// so the softmax threads only add the mask bias (on flagged steps), take the max,
+// exponentiate (base 2; q and the bias carry log2 e) and pack P.
+// TMEM columns: O_r at 32r (0-127), S at 128 + 128*sb, P (fp16 pairs) at 384 + 64*pb.
+// The running max is raised lazily (only when a tile's max exceeds it by > 8, in log2
+// units), so O is rescaled rarely; P then stays <= 2^8, well inside fp16.
 // ----------------------------------------------------------------------------------
 namespace k4 {
 constexpr int kR = 4;
 constexpr int kKVS = 4;
+constexpr int kThreads = 320;
 constexpr uint32_t kQ = 0;
-constexpr uint32_t kKV = 32768;
-constexpr uint32_t kKVStage = 17408;  // K 8 KB | V 8 KB | mask bias 128 fp32 (512 B) | pad
+constexpr uint32_t kI = 32768;
+constexpr uint32_t kKV = 65536;
+constexpr uint32_t kKVStage = 17408;  // K 8 KB | V 8 KB | mask bias 128 fp32 | flag
+constexpr uint32_t kMB = 16384, kFlag = 16896;
 constexpr uint32_t kBias = kKV + kKVS * kKVStage;
 constexpr uint32_t kBiasStage = 32768;
 constexpr uint32_t kBar = kBias + 2 * kBiasStage;
 constexpr uint32_t kSmem = kBar + 256 + 1024;
-constexpr int kThreads = 192;
+constexpr float kLazy = 8.0f;
 }  // namespace k4
 
 struct K4Bars {
@@ -330,6 +344,20 @@ struct K4Bars {
   CtaGuard guard;
 };
 static_assert(sizeof(K4Bars) <= 256, "K4 barrier block");
+
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+__device__ __forceinline__ float2 add_f32x2(float2 a, float2 b) {
+  float2 d;
+  asm("add.f32x2 %0, %1, %2;"
+      : "=l"(reinterpret_cast<uint64_t&>(d))
+      : "l"(reinterpret_cast<const uint64_t&>(a)), "l"(reinterpret_cast<const uint64_t&>(b)));
+  return d;
+}
 
 __global__ void __launch_bounds__(k4::kThreads, 1)
     triatt_core_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap k_map,
@@ -357,7 +385,7 @@ __global__ void __launch_bounds__(k4::kThreads, 1)
     }
     for (int x = 0; x < 2; ++x) {
       mbar_init(&bars->bias_full[x], 1);
-      mbar_init(&bars->bias_empty[x], 128);
+      mbar_init(&bars->bias_empty[x], 1);
       mbar_init(&bars->s_full[x], 1);
       mbar_init(&bars->s_free[x], 128);
       mbar_init(&bars->p_full[x], 128);
@@ -367,6 +395,18 @@ __global__ void __launch_bounds__(k4::kThreads, 1)
     mbar_init(&bars->o_final, 1);
     fence_barrier_init();
   }
+  // resident 128x128 fp16 identity (K-major, two 128-B-swizzled K halves)
+  for (int e = tid; e < 128 * 16; e += kThreads) {
+    const int m = e >> 4, kh = (e >> 3) & 1, ch = e & 7;
+    const int d = m - (kh * 64 + ch * 8);
+    uint4 w = make_uint4(0u, 0u, 0u, 0u);
+    if (d >= 0 && d < 8) {
+      const uint32_t one = (d & 1) ? 0x3C000000u : 0x00003C00u;
+      if (d < 2) w.x = one; else if (d < 4) w.y = one; else if (d < 6) w.z = one; else w.w = one;
+    }
+    sts_u4(smem + kI + kh * 16384 + swz128(m, ch), w);
+  }
+  fence_proxy_async_smem();
   if (warp == 1) {
     tmem_alloc(&bars->tslot, 512);
     tmem_relinquish();
@@ -417,8 +457,9 @@ __global__ void __launch_bounds__(k4::kThreads, 1)
           tma_load_4d(stage, &k_map, &bars->kv_full[s], 0, kt * 128, h, b * N + i);
           tma_load_4d(stage + 8192, &v_map, &bars->kv_full[s], 0, kt * 128, h, b * N + i);
         }
-        float* mb = reinterpret_cast<float*>(stage + 16384);
+        float* mb = reinterpret_cast<float*>(stage + kMB);
         const float* mrow = mask ? mask + static_cast<int64_t>(b) * N * N + static_cast<int64_t>(i) * mask_si : nullptr;
+        bool any = false;
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int kk = kt * 128 + lane * 4 + e;
@@ -427,13 +468,15 @@ __global__ void __launch_bounds__(k4::kThreads, 1)
           else if (mrow) v = (mrow[static_cast<int64_t>(kk) * mask_sk] - 1.f) * mask_scale;
           else v = 0.f;
           mb[lane * 4 + e] = v;
+          any |= (v != 0.f);
         }
+        any = __any_sync(0xffffffffu, any);
+        if (lane == 0) *reinterpret_cast<int*>(stage + kFlag) = any ? 1 : 0;
         mbar_arrive(&bars->kv_full[s]);
         ++issued_kv;
       }
     }
     if (!ok && lane == 0) {
-      // drain copies still landing in shared memory
       for (int t = (issued_kv > kKVS ? issued_kv - kKVS : 0); t < issued_kv; ++t)
         mbar_wait_drain(&bars->kv_full[t % kKVS], (t / kKVS) & 1);
       for (int kt = (issued_bias > 2 ? issued_bias - 2 : 0); kt < issued_bias; ++kt)
@@ -444,7 +487,9 @@ __global__ void __launch_bounds__(k4::kThreads, 1)
     // ------------------------------ MMA issuer ------------------------------
     if (lane == 0) {
       const uint32_t id_s = make_idesc_f16(128, 128, 0, 0);
+      const uint32_t id_b = make_idesc_f16(128, 128, 0, 1);
       const uint32_t id_o = make_idesc_f16(128, 32, 0, 1);
+      const uint32_t iaddr = smem_u32(smem + kI);
       bool ok = mbar_wait(&bars->q_full, 0, guard, status, kStatusTimeoutMma);
       auto issue_pv = [&](int tp) -> bool {
         const int rp = tp % kR, kp = tp / kR, sp = tp % kKVS, pb = tp & 1;
@@ -461,18 +506,26 @@ __global__ void __launch_bounds__(k4::kThreads, 1)
         return true;
       };
       for (int t = 0; t < T && ok; ++t) {
-        const int r = t % kR, s = t % kKVS, sb = t & 1;
+        const int r = t % kR, s = t % kKVS, sb = t & 1, kt = t / kR, bs = kt & 1;
         ok = mbar_wait(&bars->kv_full[s], (t / kKVS) & 1, guard, status, kStatusTimeoutMma);
+        if (ok && r == 0) ok = mbar_wait(&bars->bias_full[bs], (kt >> 1) & 1, guard, status, kStatusTimeoutMma);
         if (ok && t >= 2) ok = mbar_wait(&bars->s_free[sb], ((t >> 1) - 1) & 1, guard, status, kStatusTimeoutMma);
         if (!ok) break;
         tc_fence_after();
         const uint32_t qaddr = smem_u32(smem + kQ + r * 8192);
         const uint32_t kaddr = smem_u32(smem + kKV + s * kKVStage);
+        const uint32_t baddr = smem_u32(smem + kBias + bs * kBiasStage);
+        const uint32_t dcol = tmem + 128 + sb * 128;
 #pragma unroll
         for (int ks = 0; ks < 2; ++ks)
-          umma_ss(tmem + 128 + sb * 128, make_sdesc(qaddr + ks * 32, 16, 512, Swz::k64),
-                  make_sdesc(kaddr + ks * 32, 16, 512, Swz::k64), id_s, ks > 0 ? 1u : 0u);
+          umma_ss(dcol, make_sdesc(qaddr + ks * 32, 16, 512, Swz::k64), make_sdesc(kaddr + ks * 32, 16, 512, Swz::k64),
+                  id_s, ks > 0 ? 1u : 0u);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          umma_ss(dcol, make_sdesc(iaddr + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024, Swz::k128),
+                  make_sdesc(baddr + ks * 2048, 16384, 1024, Swz::k128), id_b, 1u);
         umma_commit(&bars->s_full[sb]);
+        if (r == kR - 1) umma_commit(&bars->bias_empty[bs]);
         if (t >= 1) ok = issue_pv(t - 1);
       }
       if (ok) issue_pv(T - 1);
@@ -480,73 +533,90 @@ __global__ void __launch_bounds__(k4::kThreads, 1)
     }
   } else {
     // ------------------------------ softmax ------------------------------
+    const int wg = (warp - 2) >> 2;  // 0 or 1: owns rows wg and wg + 2, S/P buffer wg
     const int quarter = warp & 3;
     const int jrow = quarter * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    float m_run[kR], l_run[kR];
-#pragma unroll
-    for (int r = 0; r < kR; ++r) {
-      m_run[r] = -INFINITY;
-      l_run[r] = 0.f;
-    }
+    const int sb = wg;
+    float m_run0 = -INFINITY, m_run1 = -INFINITY, l_run0 = 0.f, l_run1 = 0.f;
     bool ok = true;
     for (int kt = 0; kt < KT && ok; ++kt) {
-      const int bs = kt & 1;
-      ok = __all_sync(0xffffffffu,
-                      mbar_wait(&bars->bias_full[bs], (kt >> 1) & 1, guard, status, kStatusTimeoutConsumer));
-      if (!ok) break;
-      const uint8_t* btile = smem + kBias + bs * kBiasStage;
 #pragma unroll
-      for (int r = 0; r < kR; ++r) {
-        const int t = kt * kR + r, s = t % kKVS, sb = t & 1;
+      for (int rr = 0; rr < 2; ++rr) {
+        const int r = wg + 2 * rr;
+        const int t = kt * kR + r, s = t % kKVS;
         bool w = mbar_wait(&bars->kv_full[s], (t / kKVS) & 1, guard, status, kStatusTimeoutConsumer);
         w = w && mbar_wait(&bars->s_full[sb], (t >> 1) & 1, guard, status, kStatusTimeoutConsumer);
         ok = __all_sync(0xffffffffu, w);
         if (!ok) break;
         tc_fence_after();
-        uint32_t sv[128];
-        tmem_ld32(tmem + lane_off + 128 + sb * 128 + 0, *reinterpret_cast<uint32_t(*)[32]>(sv + 0));
-        tmem_ld32(tmem + lane_off + 128 + sb * 128 + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
-        tmem_ld32(tmem + lane_off + 128 + sb * 128 + 64, *reinterpret_cast<uint32_t(*)[32]>(sv + 64));
-        tmem_ld32(tmem + lane_off + 128 + sb * 128 + 96, *reinterpret_cast<uint32_t(*)[32]>(sv + 96));
-        tmem_wait_ld();
+        const uint8_t* stage = smem + kKV + s * kKVStage;
+        const bool masked = *reinterpret_cast<const volatile int*>(stage + kFlag) != 0;
+        const float* mb = reinterpret_cast<const float*>(stage + kMB);
+        const uint32_t scol = tmem + lane_off + 128 + sb * 128;
+        // pass 1: row max over the 128 keys, two 32-column chunks per TMEM round trip
+        float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t sv[64];
+          tmem_ld32(scol + half * 64, *reinterpret_cast<uint32_t(*)[32]>(sv + 0));
+          tmem_ld32(scol + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
+          tmem_wait_ld();
+          if (masked) {
+#pragma unroll
+            for (int k = 0; k < 64; ++k) sv[k] = __float_as_uint(__uint_as_float(sv[k]) + mb[half * 64 + k]);
+          }
+#pragma unroll
+          for (int k = 0; k < 64; k += 4) {
+            mx0 = max3f(mx0, __uint_as_float(sv[k]), __uint_as_float(sv[k + 1]));
+            mx1 = max3f(mx1, __uint_as_float(sv[k + 2]), __uint_as_float(sv[k + 3]));
+          }
+        }
+        const float mx = fmaxf(mx0, mx1);
+        const float m_old = rr == 0 ? m_run0 : m_run1;
+        const float m_new = (mx > m_old + kLazy) ? mx : m_old;
+        const float alpha = (m_new == m_old) ? 1.f : ex2f(m_old - m_new);
+        const float2 negm = make_float2(-m_new, -m_new);
+        float2 acc = make_float2(0.f, 0.f);
+        // pass 2: P = 2^(s - m) as fp16 pairs; S is read again from TMEM
+        if (t >= 2) {
+          ok = __all_sync(0xffffffffu, mbar_wait(&bars->p_free[sb], ((t >> 1) - 1) & 1, guard, status,
+                                                 kStatusTimeoutConsumer));
+          if (!ok) break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t sv[64];
+          tmem_ld32(scol + half * 64, *reinterpret_cast<uint32_t(*)[32]>(sv + 0));
+          tmem_ld32(scol + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
+          tmem_wait_ld();
+          if (masked) {
+#pragma unroll
+            for (int k = 0; k < 64; ++k) sv[k] = __float_as_uint(__uint_as_float(sv[k]) + mb[half * 64 + k]);
+          }
+#pragma unroll
+          for (int k2 = 0; k2 < 32; ++k2) {
+            float2 x = add_f32x2(make_float2(__uint_as_float(sv[2 * k2]), __uint_as_float(sv[2 * k2 + 1])), negm);
+            x.x = ex2f(x.x);
+            x.y = ex2f(x.y);
+            acc = add_f32x2(acc, x);
+            __half2 hp = __floats2half2_rn(x.x, x.y);
+            sv[k2] = *reinterpret_cast<uint32_t*>(&hp);
+          }
+          tmem_st32(tmem + lane_off + 384 + sb * 64 + half * 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 0));
+        }
+        tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&bars->s_free[sb]);
-
-        const float* mb = reinterpret_cast<const float*>(smem + kKV + s * kKVStage + 16384);
-        float mx = -INFINITY;
-#pragma unroll
-        for (int kh = 0; kh < 2; ++kh)
-#pragma unroll
-          for (int ch = 0; ch < 8; ++ch) {
-            const uint4 bw = *reinterpret_cast<const uint4*>(btile + kh * 16384 + swz128(jrow, ch));
-            const float4 m0 = *reinterpret_cast<const float4*>(mb + kh * 64 + ch * 8);
-            const float4 m1 = *reinterpret_cast<const float4*>(mb + kh * 64 + ch * 8 + 4);
-            const __half2* bh = reinterpret_cast<const __half2*>(&bw);
-            const float2 b0 = __half22float2(bh[0]), b1 = __half22float2(bh[1]);
-            const float2 b2 = __half22float2(bh[2]), b3 = __half22float2(bh[3]);
-            const float bb[8] = {b0.x + m0.x, b0.y + m0.y, b1.x + m0.z, b1.y + m0.w,
-                                 b2.x + m1.x, b2.y + m1.y, b3.x + m1.z, b3.y + m1.w};
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const int k = kh * 64 + ch * 8 + e;
-              const float x = __uint_as_float(sv[k]) + bb[e];
-              sv[k] = __float_as_uint(x);
-              mx = fmaxf(mx, x);
-            }
-          }
-        const float m_new = fmaxf(m_run[r], mx);
-        const float alpha = ex2f(m_run[r] - m_new);
-        float sum = 0.f;
-#pragma unroll
-        for (int k2 = 0; k2 < 64; ++k2) {
-          const float p0 = ex2f(__uint_as_float(sv[2 * k2]) - m_new);
-          const float p1 = ex2f(__uint_as_float(sv[2 * k2 + 1]) - m_new);
-          sum += p0 + p1;
-          sv[k2] = pack_f16x2(p0, p1);
+        const float sum = acc.x + acc.y;
+        if (rr == 0) {
+          l_run0 = l_run0 * alpha + sum;
+          m_run0 = m_new;
+        } else {
+          l_run1 = l_run1 * alpha + sum;
+          m_run1 = m_new;
         }
-        l_run[r] = l_run[r] * alpha + sum;
-        m_run[r] = m_new;
         if (kt > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
           // O_r must hold the sum through key tile kt-1 before it is rescaled.
           ok = __all_sync(0xffffffffu, mbar_wait(&bars->o_ready[r], (kt - 1) & 1, guard, status,
@@ -559,35 +629,27 @@ __global__ void __launch_bounds__(k4::kThreads, 1)
 #pragma unroll
           for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
           tmem_st32(tmem + lane_off + r * 32, ov);
+          tmem_wait_st();
         }
-        if (t >= 2) {
-          ok = __all_sync(0xffffffffu, mbar_wait(&bars->p_free[sb], ((t >> 1) - 1) & 1, guard, status,
-                                                 kStatusTimeoutConsumer));
-          if (!ok) break;
-        }
-        tc_fence_after();
-        tmem_st32(tmem + lane_off + 384 + sb * 64, *reinterpret_cast<uint32_t(*)[32]>(sv + 0));
-        tmem_st32(tmem + lane_off + 384 + sb * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
-        tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&bars->p_full[sb]);
       }
-      if (ok) mbar_arrive(&bars->bias_empty[bs]);
     }
-    // epilogue: O / l, times the gate, to og
+    // epilogue: O / l, times the gate, to og (rows wg and wg + 2)
     const bool fin = __all_sync(0xffffffffu, ok && mbar_wait(&bars->o_final, 0, guard, status,
                                                              kStatusTimeoutConsumer) && !guard->abort);
     if (fin) {
       tc_fence_after();
       const int j = jt * 128 + jrow;
-#pragma unroll 1
-      for (int r = 0; r < kR; ++r) {
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        const int r = wg + 2 * rr;
         uint32_t ov[32];
         tmem_ld32(tmem + lane_off + r * 32, ov);
         tmem_wait_ld();
         const int i = ig * kR + r;
         if (i < N && j < N) {
-          const float inv = 1.f / l_run[r];
+          const float inv = 1.f / (rr == 0 ? l_run0 : l_run1);
           const size_t pair = (static_cast<size_t>(b) * N + i) * N + j;
           const uint4* gp = reinterpret_cast<const uint4*>(gate + pair * 128 + h * kHeadDim);
           uint4* op = reinterpret_cast<uint4*>(og + pair * 128 + h * kHeadDim);

@@ -82,130 +82,211 @@ __global__ void trimul_pack_kernel(gtk_trimul_params p, uint8_t* packed) {
 }
 
 // ----------------------------------------------------------------------------------
-// K1: LN_in + gated projections + mask -> a, b planes.
-// One CTA per 128-pair tile (pair row r, columns j0..j0+127). 128 threads; thread p owns
-// pair j0+p (TMEM lane p). Shared memory: W1 128 KB | A 32 KB | z 64 KB | vec | barriers.
+// K1: persistent, warp-specialised LN_in + gated projections + mask -> a, b planes.
+// Tile = 128 consecutive pairs (b, r, j0..j0+127); CTAs loop over tiles. 288 threads:
+//   warps 0-3  LayerNorm producers: warp w normalises pairs 32w..32w+31 one row at a
+//              time (coalesced 512-B loads, shuffle reductions) into the fp16 operand
+//              tile A[s] (double buffered), and stages the tile's mask values;
+//   warp 8     lane 0: loads the 128 KB of packed weights once, then issues the MMAs;
+//   warps 4-7  epilogue: thread = channel c (TMEM lane), reads 32-pair slabs of the
+//              projection / gate accumulators, applies bias, sigmoid and mask, and writes
+//              64 contiguous bytes of its channel-plane row per slab.
+// MMA (transposed so that channels sit on TMEM lanes): D[c][j] = W_chunk[c][:] . A[j][:],
+// M = 128 channels, N = 128 pairs, K = 128. Chunks (a_p, a_g) -> TMEM columns 0-255
+// (half 0), (b_p, b_g) -> 256-511 (half 1); the epilogue of half 0 overlaps the MMAs of
+// half 1, and the LayerNorm of the next tile overlaps both.
 // ----------------------------------------------------------------------------------
 namespace k1 {
-constexpr uint32_t kW = 0, kA = 131072, kZ = 163840, kBar = 229376;
-constexpr uint32_t kSmem = kBar + 64 + 1024;
+constexpr int kThreads = 288;
+constexpr uint32_t kW = 0, kA = 131072, kMask = 196608, kBar = 197632;
+constexpr uint32_t kSmem = kBar + 128 + 1024;
 }  // namespace k1
 
-__global__ void __launch_bounds__(128, 1)
-    trimul_project_kernel(const __grid_constant__ CUtensorMap z_map, const __grid_constant__ CUtensorMap w_map,
-                          const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap b_map,
-                          const float* __restrict__ mask, const float* __restrict__ vec, int N, int rows,
+struct K1Bars {
+  uint64_t wbar;
+  uint64_t a_full[2], a_empty[2];
+  uint64_t d_full[2], d_empty[2];
+  uint64_t m_empty[2];
+  uint64_t drain;
+  uint32_t tslot;
+  CtaGuard guard;
+};
+static_assert(sizeof(K1Bars) <= 128, "K1 barrier block");
+
+__global__ void __launch_bounds__(k1::kThreads, 1)
+    trimul_project_kernel(const __grid_constant__ CUtensorMap w_map, const float* __restrict__ z,
+                          const float* __restrict__ mask, const float* __restrict__ vec, __half* __restrict__ a_out,
+                          __half* __restrict__ b_out, int64_t ld, int N, int rows, int n_jt, int n_tiles,
                           uint32_t* status) {
   extern __shared__ uint8_t dsmem[];
   uint8_t* smem = align1024(dsmem);
-  uint64_t* zbar = reinterpret_cast<uint64_t*>(smem + k1::kBar);
-  uint64_t* wbar = zbar + 1;
-  uint64_t* mbar = zbar + 2;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(zbar + 3);
-  CtaGuard* guard = reinterpret_cast<CtaGuard*>(tslot + 1);
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int j0 = blockIdx.x * 128, r = blockIdx.y, b = blockIdx.z;
+  K1Bars* bars = reinterpret_cast<K1Bars*>(smem + k1::kBar);
+  CtaGuard* guard = &bars->guard;
+  float* mask_s = reinterpret_cast<float*>(smem + k1::kMask);  // [2][128]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   if (tid == 0) {
     guard->abort = 0;
-    mbar_init(zbar, 1);
-    mbar_init(wbar, 1);
-    mbar_init(mbar, 1);
+    mbar_init(&bars->wbar, 1);
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(&bars->a_full[x], 128);
+      mbar_init(&bars->a_empty[x], 1);
+      mbar_init(&bars->d_full[x], 1);
+      mbar_init(&bars->d_empty[x], 128);
+      mbar_init(&bars->m_empty[x], 128);
+    }
+    mbar_init(&bars->drain, 1);
     fence_barrier_init();
   }
-  if (warp == 0) {
-    tmem_alloc(tslot, 512);
+  if (warp == 8) {
+    tmem_alloc(&bars->tslot, 512);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tslot;
+  const uint32_t tmem = bars->tslot;
 
-  if (tid == 0) {
-    mbar_arrive_expect_tx(zbar, 65536);
+  if (warp < 4) {
+    // ------------------------- LayerNorm producers -------------------------
+    const float4 gw = reinterpret_cast<const float4*>(vec + tmpack::kVLnW)[lane];
+    const float4 gb = reinterpret_cast<const float4*>(vec + tmpack::kVLnB)[lane];
+    int it = 0;
+    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+      const int s = it & 1;
+      const int jt = tile % n_jt, rb = tile / n_jt;
+      const int r = rb % rows, b = rb / rows, j0 = jt * 128;
+      if (it >= 2) {
+        const uint32_t par = ((it >> 1) - 1) & 1;
+        bool w = mbar_wait(&bars->a_empty[s], par, guard, status, kStatusTimeoutProducer);
+        w = w && mbar_wait(&bars->m_empty[s], par, guard, status, kStatusTimeoutProducer);
+        if (!__all_sync(0xffffffffu, w)) break;
+      }
+      const size_t rowbase = (static_cast<size_t>(b) * rows + r) * N;
+      const int jm = j0 + warp * 32 + lane;
+      mask_s[s * 128 + warp * 32 + lane] = jm < N ? (mask ? mask[rowbase + jm] : 1.f) : 0.f;
+      float4 v[32];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) tma_load_4d(smem + k1::kZ + q * 16384, &z_map, zbar, q * 32, j0, r, b);
-    mbar_arrive_expect_tx(wbar, 131072);
+      for (int k = 0; k < 32; ++k) {
+        const int j = j0 + warp * 32 + k;
+        v[k] = j < N ? __ldg(reinterpret_cast<const float4*>(z + (rowbase + j) * 128) + lane)
+                     : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      uint8_t* at = smem + k1::kA + s * 32768 + (lane >> 4) * 16384;
 #pragma unroll
-    for (int kh = 0; kh < 2; ++kh)
-#pragma unroll
-      for (int rb = 0; rb < 4; ++rb)
-        tma_load_2d(smem + k1::kW + kh * 65536 + rb * 16384, &w_map, wbar, kh * 64, rb * 128);
-  }
-
-  const int p = tid;
-  const int j = j0 + p;
-  float mval = 0.f;
-  if (j < N) mval = mask ? mask[(static_cast<size_t>(b) * rows + r) * N + j] : 1.f;
-
-  if (mbar_wait(zbar, 0, guard, status, kStatusTimeoutConsumer)) {
-    ln_row_to_operand(smem + k1::kZ, smem + k1::kA, p, vec + tmpack::kVLnW, vec + tmpack::kVLnB);
-  }
-  fence_proxy_async_smem();
-  __syncthreads();
-  // The z tile is dead now: keep the projection biases there for the epilogue.
-  float* sb1 = reinterpret_cast<float*>(smem + k1::kZ);
-  reinterpret_cast<float4*>(sb1)[tid] = reinterpret_cast<const float4*>(vec + tmpack::kVB1)[tid];
-
-  if (tid == 0 && !guard->abort) {
-    if (mbar_wait(wbar, 0, guard, status, kStatusTimeoutMma)) {
-      tc_fence_after();
-      const uint32_t idesc = make_idesc_f16(128, 256, 0, 0);
-      const uint32_t a0 = smem_u32(smem + k1::kA), w0 = smem_u32(smem + k1::kW);
-#pragma unroll
-      for (int nh = 0; nh < 2; ++nh)
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-          const int kh = ks >> 2, kin = ks & 3;
-          const uint64_t ad = make_sdesc(a0 + kh * 16384 + kin * 32, 16, 1024, Swz::k128);
-          const uint64_t bd = make_sdesc(w0 + kh * 65536 + nh * 32768 + kin * 32, 16, 1024, Swz::k128);
-          umma_ss(tmem + nh * 256, ad, bd, idesc, ks > 0 ? 1u : 0u);
-        }
-      umma_commit(mbar);
+      for (int k = 0; k < 32; ++k) {
+        const float mean = warp_sum((v[k].x + v[k].y) + (v[k].z + v[k].w)) * (1.f / 128.f);
+        const float dx = v[k].x - mean, dy = v[k].y - mean, dz = v[k].z - mean, dw = v[k].w - mean;
+        const float var = warp_sum((dx * dx + dy * dy) + (dz * dz + dw * dw)) * (1.f / 128.f);
+        const float rstd = rsqrtf(var + 1e-5f);
+        uint2 o;
+        o.x = pack_f16x2(dx * rstd * gw.x + gb.x, dy * rstd * gw.y + gb.y);
+        o.y = pack_f16x2(dz * rstd * gw.z + gb.z, dw * rstd * gw.w + gb.w);
+        const int p = warp * 32 + k;
+        *reinterpret_cast<uint2*>(at + swz128(p, (lane & 15) >> 1) + (lane & 1) * 8) = o;
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&bars->a_full[s]);
     }
-  }
-  __syncthreads();
-  const bool ok = __all_sync(0xffffffffu, mbar_wait(mbar, 0, guard, status, kStatusTimeoutConsumer));
-  tc_fence_after();
-  if (ok) {
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-#pragma unroll 1
-    for (int which = 0; which < 2; ++which) {
-      __half* stage = reinterpret_cast<__half*>(smem + k1::kW + which * 32768);
-#pragma unroll 1
-      for (int cc = 0; cc < 4; ++cc) {
-        uint32_t pr[32], gr[32];
-        tmem_ld32(tmem + lane_base + which * 256 + cc * 32, pr);
-        tmem_ld32(tmem + lane_base + which * 256 + 128 + cc * 32, gr);
-        tmem_wait_ld();
+  } else if (warp == 8) {
+    // ------------------------- weights + MMA issuer -------------------------
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&bars->wbar, 131072);
 #pragma unroll
-        for (int t = 0; t < 32; ++t) {
-          const int c = cc * 32 + t;
-          const float pv = __uint_as_float(pr[t]) + sb1[which * 256 + c];
-          const float gv = __uint_as_float(gr[t]) + sb1[which * 256 + 128 + c];
-          stage[c * 128 + p] = f16_sat(pv * sigmoidf_fast(gv) * mval);
+      for (int kh = 0; kh < 2; ++kh)
+#pragma unroll
+        for (int rb = 0; rb < 4; ++rb)
+          tma_load_2d(smem + k1::kW + kh * 65536 + rb * 16384, &w_map, &bars->wbar, kh * 64, rb * 128);
+      bool ok = mbar_wait(&bars->wbar, 0, guard, status, kStatusTimeoutMma);
+      const uint32_t idesc = make_idesc_f16(128, 128, 0, 0);
+      const uint32_t w0 = smem_u32(smem + k1::kW);
+      int it = 0;
+      for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++it) {
+        const int s = it & 1;
+        ok = mbar_wait(&bars->a_full[s], (it >> 1) & 1, guard, status, kStatusTimeoutMma);
+        const uint32_t a0 = smem_u32(smem + k1::kA + s * 32768);
+        for (int h = 0; ok && h < 2; ++h) {
+          if (it >= 1) ok = mbar_wait(&bars->d_empty[h], (it - 1) & 1, guard, status, kStatusTimeoutMma);
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const int chunk = 2 * h + q;
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks) {
+              const int kh = ks >> 2, kin = ks & 3;
+              umma_ss(tmem + h * 256 + q * 128,
+                      make_sdesc(w0 + kh * 65536 + chunk * 16384 + kin * 32, 16, 1024, Swz::k128),
+                      make_sdesc(a0 + kh * 16384 + kin * 32, 16, 1024, Swz::k128), idesc, ks > 0 ? 1u : 0u);
+            }
+          }
+          umma_commit(&bars->d_full[h]);
         }
+        if (ok) umma_commit(&bars->a_empty[s]);
+      }
+      if (!ok) {
+        umma_commit(&bars->drain);
+        mbar_wait_drain(&bars->drain, 0);
+        mbar_wait_drain(&bars->wbar, 0);
       }
     }
-  }
-  fence_proxy_async_smem();
-  __syncthreads();
-  if (tid == 0) {
-    if (!guard->abort) {
-      tma_store_4d(&a_map, smem + k1::kW, j0, 0, r, b);
-      tma_store_4d(&b_map, smem + k1::kW + 32768, j0, 0, r, b);
-      tma_store_commit();
-      tma_store_wait_read();
-    } else {
-      // drain loads that may still be landing before shared memory is released
-      mbar_wait_drain(zbar, 0);
-      mbar_wait_drain(wbar, 0);
+  } else {
+    // ------------------------- epilogue: thread = channel -------------------------
+    const int q4 = warp & 3;
+    const int c = q4 * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
+    const float bias_p0 = vec[tmpack::kVB1 + c], bias_p1 = vec[tmpack::kVB1 + 256 + c];
+    const float bias_g0 = vec[tmpack::kVB1 + 128 + c], bias_g1 = vec[tmpack::kVB1 + 384 + c];
+    int it = 0;
+    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+      const int s = it & 1;
+      const int jt = tile % n_jt, rb = tile / n_jt;
+      const int r = rb % rows, b = rb / rows, j0 = jt * 128;
+      const float* ms = mask_s + s * 128;
+      bool ok = true;
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars->d_full[h], it & 1, guard, status, kStatusTimeoutConsumer));
+        if (!ok) break;
+        tc_fence_after();
+        __half* dst = (h ? b_out : a_out) + ((static_cast<size_t>(b) * rows + r) * 128 + c) * ld;
+        const float bp = h ? bias_p1 : bias_p0, bg = h ? bias_g1 : bias_g0;
+#pragma unroll 1
+        for (int jc = 0; jc < 4; ++jc) {
+          uint32_t pv[32], gv[32];
+          tmem_ld32(tmem + lane_off + h * 256 + jc * 32, pv);
+          tmem_ld32(tmem + lane_off + h * 256 + 128 + jc * 32, gv);
+          tmem_wait_ld();
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int jj = j0 + jc * 32 + u * 8;
+            const float4 m0 = *reinterpret_cast<const float4*>(ms + jc * 32 + u * 8);
+            const float4 m1 = *reinterpret_cast<const float4*>(ms + jc * 32 + u * 8 + 4);
+            const float mv[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+            float o[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              o[e] = (__uint_as_float(pv[u * 8 + e]) + bp) * sigmoid_tanh(__uint_as_float(gv[u * 8 + e]) + bg) * mv[e];
+            if (jj < ld) {
+              uint4 w;
+              w.x = pack_f16x2(o[0], o[1]);
+              w.y = pack_f16x2(o[2], o[3]);
+              w.z = pack_f16x2(o[4], o[5]);
+              w.w = pack_f16x2(o[6], o[7]);
+              *reinterpret_cast<uint4*>(dst + jj) = w;
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&bars->d_empty[h]);
+      }
+      if (!ok) break;
+      mbar_arrive(&bars->m_empty[s]);
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == 8) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -541,18 +622,20 @@ int gtk_trimul_project(const float* z, const float* mask, const void* packed, vo
   if (int e = check_ptr(packed, "packed", 256)) return e;
   if (int e = check_ptr(a_planes, "a_planes")) return e;
   if (int e = check_ptr(b_planes, "b_planes")) return e;
+  if (mask && (reinterpret_cast<uintptr_t>(mask) & 3)) return fail(GTK_ERR_ALIGNMENT, "mask is misaligned");
   if (int e = check_device()) return e;
-  CUtensorMap zm, wm, am, bm;
+  const int64_t n_jt = (N + 127) / 128;
+  const int64_t n_tiles = B * rows * n_jt;
+  if (n_tiles > 2147483647) return fail(GTK_ERR_INVALID_ARG, "trimul_project: too many tiles");
+  CUtensorMap wm;
   const uint8_t* pk = static_cast<const uint8_t*>(packed);
-  if (int e = make_pair_map(&zm, z, B, rows, N, false)) return e;
   if (int e = make_weight_map(&wm, pk + tmpack::kW1, 512, 128)) return e;
-  if (int e = make_plane_map(&am, a_planes, B, rows, 128, N, ld, 128, 128, 1, 0)) return e;
-  if (int e = make_plane_map(&bm, b_planes, B, rows, 128, N, ld, 128, 128, 1, 0)) return e;
   if (int e = ensure_smem(reinterpret_cast<const void*>(trimul_project_kernel), k1::kSmem)) return e;
-  dim3 grid(static_cast<unsigned>((N + 127) / 128), static_cast<unsigned>(rows), static_cast<unsigned>(B));
-  trimul_project_kernel<<<grid, 128, k1::kSmem, static_cast<cudaStream_t>(stream)>>>(
-      zm, wm, am, bm, mask, reinterpret_cast<const float*>(pk + tmpack::kVec), static_cast<int>(N),
-      static_cast<int>(rows), status);
+  const int grid = static_cast<int>(n_tiles < num_sms() ? n_tiles : num_sms());
+  trimul_project_kernel<<<grid, k1::kThreads, k1::kSmem, static_cast<cudaStream_t>(stream)>>>(
+      wm, z, mask, reinterpret_cast<const float*>(pk + tmpack::kVec), static_cast<__half*>(a_planes),
+      static_cast<__half*>(b_planes), ld, static_cast<int>(N), static_cast<int>(rows), static_cast<int>(n_jt),
+      static_cast<int>(n_tiles), status);
   return check_launch("trimul_project_kernel");
 }
 
