@@ -296,18 +296,21 @@ __global__ void __launch_bounds__(128, 1)
 
 // ----------------------------------------------------------------------------------
 // K4: flash-style core. CTA = (query tile jt, head h, batch b, group of kR rows i).
-//   warp 0      producer: TMA for Q (once), K, V (4-stage ring) and the bias tile
+//   warps 0-3   softmax warpgroup 0 (rows r = 0, 2), warps 4-7 warpgroup 1 (r = 1, 3);
+//               thread = query row j of the tile; 224 registers each (setmaxnreg);
+//   warp 8      producer: TMA for Q (once), K, V (4-stage ring) and the bias tile
 //               (2 stages, shared by the kR rows); all lanes stage the mask bias of each
 //               step plus a flag telling whether the step has any masked / absent key;
-//   warp 1      TMEM allocator + MMA issuer (lane 0);
-//   warps 2-5   softmax warpgroup 0 (rows r = 0, 2), warps 6-9 warpgroup 1 (r = 1, 3);
-//               thread = query row j of the tile.
-// Step t = kt * kR + r handles key tile kt of row r and uses S/P buffer t & 1, i.e. each
-// warpgroup owns one S buffer and one P buffer, and the two run concurrently.
-// The triangle bias is added by the tensor core: S = Q K^T + I * Bias, where I is a
-// resident 128x128 identity and the bias tile [j][k] is the MN-major B operand (K = j),
-// so the softmax threads only add the mask bias (on flagged steps), take the max,
-// exponentiate (base 2; q and the bias carry log2 e) and pack P.
+//   warp 9      TMEM allocator + MMA issuer (lane 0); warps 10-11 only donate registers.
+// Step t = kt * kR + r handles key tile kt of row r and uses S/P buffer t & 1, so each
+// warpgroup owns one S and one P buffer and the two run concurrently. A warpgroup reads
+// its whole S row slice into registers at once and frees the buffer, so the tensor core
+// computes S(t+2) while the softmax of step t runs; the MMA issuer is a non-blocking
+// state machine that issues S up to two steps ahead of P V.
+// The triangle bias is added by the tensor core: S = Q K^T + I * Bias, with I a resident
+// 128x128 identity and the bias tile [j][k] the MN-major B operand (K = j), so the
+// softmax threads only add the mask bias (on flagged steps), take the max, exponentiate
+// (base 2; q and the bias carry log2 e) and pack P.
 // TMEM columns: O_r at 32r (0-127), S at 128 + 128*sb, P (fp16 pairs) at 384 + 64*pb.
 // The running max is raised lazily (only when a tile's max exceeds it by > 8, in log2
 // units), so O is rescaled rarely; P then stays <= 2^8, well inside fp16.
@@ -315,7 +318,11 @@ __global__ void __launch_bounds__(128, 1)
 namespace k4 {
 constexpr int kR = 4;
 constexpr int kKVS = 4;
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;
+// Register split: the kernel is launched with 168 registers per thread (384 x 168 =
+// 64512 per CTA); softmax warps raise to 224, warps 8-11 drop to 56: 256*224 + 128*56 = 64512.
+constexpr int kLaunchRegs = 168, kSoftmaxRegs = 224, kOtherRegs = 56;
+static_assert(256 * kSoftmaxRegs + 128 * kOtherRegs <= kThreads * kLaunchRegs, "register split");
 constexpr uint32_t kQ = 0;
 constexpr uint32_t kI = 32768;
 constexpr uint32_t kKV = 65536;
@@ -357,6 +364,15 @@ __device__ __forceinline__ float2 add_f32x2(float2 a, float2 b) {
       : "=l"(reinterpret_cast<uint64_t&>(d))
       : "l"(reinterpret_cast<const uint64_t&>(a)), "l"(reinterpret_cast<const uint64_t&>(b)));
   return d;
+}
+
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
 }
 
 __global__ void __launch_bounds__(k4::kThreads, 1)
@@ -407,7 +423,7 @@ __global__ void __launch_bounds__(k4::kThreads, 1)
     sts_u4(smem + kI + kh * 16384 + swz128(m, ch), w);
   }
   fence_proxy_async_smem();
-  if (warp == 1) {
+  if (warp == 9) {
     tmem_alloc(&bars->tslot, 512);
     tmem_relinquish();
   }
@@ -416,128 +432,154 @@ __global__ void __launch_bounds__(k4::kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = bars->tslot;
 
-  if (warp == 0) {
-    // ------------------------------ producer ------------------------------
-    int issued_kv = 0, issued_bias = 0;
-    bool ok = true;
-    if (lane == 0) {
-      mbar_arrive_expect_tx(&bars->q_full, kR * 8192);
-#pragma unroll
-      for (int r = 0; r < kR; ++r) {
-        const int i = min(ig * kR + r, N - 1);
-        tma_load_4d(smem + kQ + r * 8192, &q_map, &bars->q_full, 0, jt * 128, h, b * N + i);
-      }
-    }
-    for (int kt = 0; kt < KT && ok; ++kt) {
-      const int bs = kt & 1;
-      if (kt >= 2) {
-        ok = __all_sync(0xffffffffu,
-                        mbar_wait(&bars->bias_empty[bs], ((kt >> 1) - 1) & 1, guard, status, kStatusTimeoutProducer));
-        if (!ok) break;
-      }
+  if (warp >= 8) {
+    setmaxnreg_dec<kOtherRegs>();
+    if (warp == 8) {
+      // ------------------------------ producer ------------------------------
+      int issued_kv = 0, issued_bias = 0;
+      bool ok = true;
       if (lane == 0) {
-        mbar_arrive_expect_tx(&bars->bias_full[bs], kBiasStage);
+        mbar_arrive_expect_tx(&bars->q_full, kR * 8192);
 #pragma unroll
-        for (int kh = 0; kh < 2; ++kh)
-          tma_load_3d(smem + kBias + bs * kBiasStage + kh * 16384, &bias_map, &bars->bias_full[bs],
-                      kt * 128 + kh * 64, jt * 128, b * kHeads + h);
+        for (int r = 0; r < kR; ++r) {
+          const int i = min(ig * kR + r, N - 1);
+          tma_load_4d(smem + kQ + r * 8192, &q_map, &bars->q_full, 0, jt * 128, h, b * N + i);
+        }
       }
-      ++issued_bias;
-      for (int r = 0; r < kR; ++r) {
-        const int t = kt * kR + r, s = t % kKVS;
-        const int i = min(ig * kR + r, N - 1);
-        if (t >= kKVS) {
-          ok = __all_sync(0xffffffffu, mbar_wait(&bars->kv_empty[s], ((t / kKVS) - 1) & 1, guard, status,
+      for (int kt = 0; kt < KT && ok; ++kt) {
+        const int bs = kt & 1;
+        if (kt >= 2) {
+          ok = __all_sync(0xffffffffu, mbar_wait(&bars->bias_empty[bs], ((kt >> 1) - 1) & 1, guard, status,
                                                  kStatusTimeoutProducer));
           if (!ok) break;
         }
-        uint8_t* stage = smem + kKV + s * kKVStage;
         if (lane == 0) {
-          mbar_arrive_expect_tx(&bars->kv_full[s], 16384);
-          tma_load_4d(stage, &k_map, &bars->kv_full[s], 0, kt * 128, h, b * N + i);
-          tma_load_4d(stage + 8192, &v_map, &bars->kv_full[s], 0, kt * 128, h, b * N + i);
-        }
-        float* mb = reinterpret_cast<float*>(stage + kMB);
-        const float* mrow = mask ? mask + static_cast<int64_t>(b) * N * N + static_cast<int64_t>(i) * mask_si : nullptr;
-        bool any = false;
+          mbar_arrive_expect_tx(&bars->bias_full[bs], kBiasStage);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int kk = kt * 128 + lane * 4 + e;
-          float v;
-          if (kk >= N) v = -INFINITY;
-          else if (mrow) v = (mrow[static_cast<int64_t>(kk) * mask_sk] - 1.f) * mask_scale;
-          else v = 0.f;
-          mb[lane * 4 + e] = v;
-          any |= (v != 0.f);
+          for (int kh = 0; kh < 2; ++kh)
+            tma_load_3d(smem + kBias + bs * kBiasStage + kh * 16384, &bias_map, &bars->bias_full[bs],
+                        kt * 128 + kh * 64, jt * 128, b * kHeads + h);
         }
-        any = __any_sync(0xffffffffu, any);
-        if (lane == 0) *reinterpret_cast<int*>(stage + kFlag) = any ? 1 : 0;
-        mbar_arrive(&bars->kv_full[s]);
-        ++issued_kv;
+        ++issued_bias;
+        for (int r = 0; r < kR; ++r) {
+          const int t = kt * kR + r, s = t % kKVS;
+          const int i = min(ig * kR + r, N - 1);
+          if (t >= kKVS) {
+            ok = __all_sync(0xffffffffu, mbar_wait(&bars->kv_empty[s], ((t / kKVS) - 1) & 1, guard, status,
+                                                   kStatusTimeoutProducer));
+            if (!ok) break;
+          }
+          uint8_t* stage = smem + kKV + s * kKVStage;
+          if (lane == 0) {
+            mbar_arrive_expect_tx(&bars->kv_full[s], 16384);
+            tma_load_4d(stage, &k_map, &bars->kv_full[s], 0, kt * 128, h, b * N + i);
+            tma_load_4d(stage + 8192, &v_map, &bars->kv_full[s], 0, kt * 128, h, b * N + i);
+          }
+          float* mb = reinterpret_cast<float*>(stage + kMB);
+          const float* mrow =
+              mask ? mask + static_cast<int64_t>(b) * N * N + static_cast<int64_t>(i) * mask_si : nullptr;
+          bool any = false;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int kk = kt * 128 + lane * 4 + e;
+            float v;
+            if (kk >= N) v = -INFINITY;
+            else if (mrow) v = (mrow[static_cast<int64_t>(kk) * mask_sk] - 1.f) * mask_scale;
+            else v = 0.f;
+            mb[lane * 4 + e] = v;
+            any |= (v != 0.f);
+          }
+          any = __any_sync(0xffffffffu, any);
+          if (lane == 0) *reinterpret_cast<int*>(stage + kFlag) = any ? 1 : 0;
+          mbar_arrive(&bars->kv_full[s]);
+          ++issued_kv;
+        }
       }
-    }
-    if (!ok && lane == 0) {
-      for (int t = (issued_kv > kKVS ? issued_kv - kKVS : 0); t < issued_kv; ++t)
-        mbar_wait_drain(&bars->kv_full[t % kKVS], (t / kKVS) & 1);
-      for (int kt = (issued_bias > 2 ? issued_bias - 2 : 0); kt < issued_bias; ++kt)
-        mbar_wait_drain(&bars->bias_full[kt & 1], (kt >> 1) & 1);
-      mbar_wait_drain(&bars->q_full, 0);
-    }
-  } else if (warp == 1) {
-    // ------------------------------ MMA issuer ------------------------------
-    if (lane == 0) {
+      if (!ok && lane == 0) {
+        for (int t = (issued_kv > kKVS ? issued_kv - kKVS : 0); t < issued_kv; ++t)
+          mbar_wait_drain(&bars->kv_full[t % kKVS], (t / kKVS) & 1);
+        for (int kt = (issued_bias > 2 ? issued_bias - 2 : 0); kt < issued_bias; ++kt)
+          mbar_wait_drain(&bars->bias_full[kt & 1], (kt >> 1) & 1);
+        mbar_wait_drain(&bars->q_full, 0);
+      }
+    } else if (warp == 9 && lane == 0) {
+      // ------------------------------ MMA issuer ------------------------------
       const uint32_t id_s = make_idesc_f16(128, 128, 0, 0);
       const uint32_t id_b = make_idesc_f16(128, 128, 0, 1);
       const uint32_t id_o = make_idesc_f16(128, 32, 0, 1);
       const uint32_t iaddr = smem_u32(smem + kI);
       bool ok = mbar_wait(&bars->q_full, 0, guard, status, kStatusTimeoutMma);
-      auto issue_pv = [&](int tp) -> bool {
-        const int rp = tp % kR, kp = tp / kR, sp = tp % kKVS, pb = tp & 1;
-        if (!mbar_wait(&bars->p_full[pb], (tp >> 1) & 1, guard, status, kStatusTimeoutMma)) return false;
-        tc_fence_after();
-        const uint32_t vaddr = smem_u32(smem + kKV + sp * kKVStage + 8192);
+      int ns = 0, npv = 0;  // next S step, next P V step
+      uint64_t t0 = global_timer_ns();
+      uint32_t spins = 0;
+      while (ok && npv < T) {
+        bool progress = false;
+        // S(ns): needs its K stage, the bias tile of its key tile, and its S buffer freed by step ns-2
+        if (ns < T && ns < npv + 2 + 1) {
+          const int s = ns % kKVS, sb = ns & 1, kt = ns / kR, bs = kt & 1, r = ns % kR;
+          if (mbar_test_wait(smem_u32(&bars->kv_full[s]), (ns / kKVS) & 1) &&
+              (r != 0 || mbar_test_wait(smem_u32(&bars->bias_full[bs]), (kt >> 1) & 1)) &&
+              (ns < 2 || mbar_test_wait(smem_u32(&bars->s_free[sb]), ((ns >> 1) - 1) & 1))) {
+            tc_fence_after();
+            const uint32_t qaddr = smem_u32(smem + kQ + r * 8192);
+            const uint32_t kaddr = smem_u32(smem + kKV + s * kKVStage);
+            const uint32_t baddr = smem_u32(smem + kBias + bs * kBiasStage);
+            const uint32_t dcol = tmem + 128 + sb * 128;
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks)
-          umma_ts(tmem + rp * 32, tmem + 384 + pb * 64 + ks * 8, make_sdesc(vaddr + ks * 1024, 16, 512, Swz::k64),
-                  id_o, (kp > 0 || ks > 0) ? 1u : 0u);
-        umma_commit(&bars->kv_empty[sp]);
-        umma_commit(&bars->p_free[pb]);
-        umma_commit(&bars->o_ready[rp]);
-        return true;
-      };
-      for (int t = 0; t < T && ok; ++t) {
-        const int r = t % kR, s = t % kKVS, sb = t & 1, kt = t / kR, bs = kt & 1;
-        ok = mbar_wait(&bars->kv_full[s], (t / kKVS) & 1, guard, status, kStatusTimeoutMma);
-        if (ok && r == 0) ok = mbar_wait(&bars->bias_full[bs], (kt >> 1) & 1, guard, status, kStatusTimeoutMma);
-        if (ok && t >= 2) ok = mbar_wait(&bars->s_free[sb], ((t >> 1) - 1) & 1, guard, status, kStatusTimeoutMma);
-        if (!ok) break;
-        tc_fence_after();
-        const uint32_t qaddr = smem_u32(smem + kQ + r * 8192);
-        const uint32_t kaddr = smem_u32(smem + kKV + s * kKVStage);
-        const uint32_t baddr = smem_u32(smem + kBias + bs * kBiasStage);
-        const uint32_t dcol = tmem + 128 + sb * 128;
+            for (int ks = 0; ks < 2; ++ks)
+              umma_ss(dcol, make_sdesc(qaddr + ks * 32, 16, 512, Swz::k64),
+                      make_sdesc(kaddr + ks * 32, 16, 512, Swz::k64), id_s, ks > 0 ? 1u : 0u);
 #pragma unroll
-        for (int ks = 0; ks < 2; ++ks)
-          umma_ss(dcol, make_sdesc(qaddr + ks * 32, 16, 512, Swz::k64), make_sdesc(kaddr + ks * 32, 16, 512, Swz::k64),
-                  id_s, ks > 0 ? 1u : 0u);
+            for (int ks = 0; ks < 8; ++ks)
+              umma_ss(dcol, make_sdesc(iaddr + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024, Swz::k128),
+                      make_sdesc(baddr + ks * 2048, 16384, 1024, Swz::k128), id_b, 1u);
+            umma_commit(&bars->s_full[sb]);
+            if (r == kR - 1) umma_commit(&bars->bias_empty[bs]);
+            ++ns;
+            progress = true;
+          }
+        }
+        // P V(npv): needs P written by the softmax of step npv
+        if (npv < ns) {
+          const int rp = npv % kR, kp = npv / kR, sp = npv % kKVS, pb = npv & 1;
+          if (mbar_test_wait(smem_u32(&bars->p_full[pb]), (npv >> 1) & 1)) {
+            tc_fence_after();
+            const uint32_t vaddr = smem_u32(smem + kKV + sp * kKVStage + 8192);
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks)
-          umma_ss(dcol, make_sdesc(iaddr + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024, Swz::k128),
-                  make_sdesc(baddr + ks * 2048, 16384, 1024, Swz::k128), id_b, 1u);
-        umma_commit(&bars->s_full[sb]);
-        if (r == kR - 1) umma_commit(&bars->bias_empty[bs]);
-        if (t >= 1) ok = issue_pv(t - 1);
+            for (int ks = 0; ks < 8; ++ks)
+              umma_ts(tmem + rp * 32, tmem + 384 + pb * 64 + ks * 8,
+                      make_sdesc(vaddr + ks * 1024, 16, 512, Swz::k64), id_o, (kp > 0 || ks > 0) ? 1u : 0u);
+            umma_commit(&bars->kv_empty[sp]);
+            umma_commit(&bars->p_free[pb]);
+            umma_commit(&bars->o_ready[rp]);
+            ++npv;
+            progress = true;
+          }
+        }
+        if (progress) {
+          t0 = global_timer_ns();
+          spins = 0;
+        } else if ((++spins & 63u) == 0) {
+          if (guard->abort) {
+            ok = false;
+          } else if (global_timer_ns() - t0 > kWaitLimitNs) {
+            guard->abort = 1;
+            if (status) atomicOr(status, kStatusTimeoutMma);
+            ok = false;
+          }
+        }
       }
-      if (ok) issue_pv(T - 1);
       umma_commit(&bars->o_final);  // also drains whatever was issued before an abort
     }
   } else {
     // ------------------------------ softmax ------------------------------
-    const int wg = (warp - 2) >> 2;  // 0 or 1: owns rows wg and wg + 2, S/P buffer wg
+    setmaxnreg_inc<kSoftmaxRegs>();
+    const int wg = warp >> 2;  // 0 or 1: owns rows wg and wg + 2, S/P buffer wg
     const int quarter = warp & 3;
     const int jrow = quarter * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const int sb = wg;
+    const uint32_t scol = tmem + lane_off + 128 + sb * 128;
     float m_run0 = -INFINITY, m_run1 = -INFINITY, l_run0 = 0.f, l_run1 = 0.f;
     bool ok = true;
     for (int kt = 0; kt < KT && ok; ++kt) {
@@ -550,65 +592,48 @@ __global__ void __launch_bounds__(k4::kThreads, 1)
         ok = __all_sync(0xffffffffu, w);
         if (!ok) break;
         tc_fence_after();
+        uint32_t sv[128];
+        tmem_ld32(scol + 0, *reinterpret_cast<uint32_t(*)[32]>(sv + 0));
+        tmem_ld32(scol + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
+        tmem_ld32(scol + 64, *reinterpret_cast<uint32_t(*)[32]>(sv + 64));
+        tmem_ld32(scol + 96, *reinterpret_cast<uint32_t(*)[32]>(sv + 96));
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&bars->s_free[sb]);  // the tensor core may now compute S(t + 2)
+
         const uint8_t* stage = smem + kKV + s * kKVStage;
-        const bool masked = *reinterpret_cast<const volatile int*>(stage + kFlag) != 0;
-        const float* mb = reinterpret_cast<const float*>(stage + kMB);
-        const uint32_t scol = tmem + lane_off + 128 + sb * 128;
-        // pass 1: row max over the 128 keys, two 32-column chunks per TMEM round trip
-        float mx0 = -INFINITY, mx1 = -INFINITY;
+        if (*reinterpret_cast<const volatile int*>(stage + kFlag)) {
+          const float* mb = reinterpret_cast<const float*>(stage + kMB);
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t sv[64];
-          tmem_ld32(scol + half * 64, *reinterpret_cast<uint32_t(*)[32]>(sv + 0));
-          tmem_ld32(scol + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
-          tmem_wait_ld();
-          if (masked) {
-#pragma unroll
-            for (int k = 0; k < 64; ++k) sv[k] = __float_as_uint(__uint_as_float(sv[k]) + mb[half * 64 + k]);
-          }
-#pragma unroll
-          for (int k = 0; k < 64; k += 4) {
-            mx0 = max3f(mx0, __uint_as_float(sv[k]), __uint_as_float(sv[k + 1]));
-            mx1 = max3f(mx1, __uint_as_float(sv[k + 2]), __uint_as_float(sv[k + 3]));
+          for (int k4i = 0; k4i < 32; ++k4i) {
+            const float4 m4 = *reinterpret_cast<const float4*>(mb + k4i * 4);
+            sv[k4i * 4 + 0] = __float_as_uint(__uint_as_float(sv[k4i * 4 + 0]) + m4.x);
+            sv[k4i * 4 + 1] = __float_as_uint(__uint_as_float(sv[k4i * 4 + 1]) + m4.y);
+            sv[k4i * 4 + 2] = __float_as_uint(__uint_as_float(sv[k4i * 4 + 2]) + m4.z);
+            sv[k4i * 4 + 3] = __float_as_uint(__uint_as_float(sv[k4i * 4 + 3]) + m4.w);
           }
         }
-        const float mx = fmaxf(mx0, mx1);
+        float mx0 = __uint_as_float(sv[0]), mx1 = __uint_as_float(sv[1]);
+#pragma unroll
+        for (int k = 2; k < 126; k += 4) {
+          mx0 = max3f(mx0, __uint_as_float(sv[k]), __uint_as_float(sv[k + 1]));
+          mx1 = max3f(mx1, __uint_as_float(sv[k + 2]), __uint_as_float(sv[k + 3]));
+        }
+        const float mx = max3f(mx0, mx1, fmaxf(__uint_as_float(sv[126]), __uint_as_float(sv[127])));
         const float m_old = rr == 0 ? m_run0 : m_run1;
         const float m_new = (mx > m_old + kLazy) ? mx : m_old;
         const float alpha = (m_new == m_old) ? 1.f : ex2f(m_old - m_new);
         const float2 negm = make_float2(-m_new, -m_new);
         float2 acc = make_float2(0.f, 0.f);
-        // pass 2: P = 2^(s - m) as fp16 pairs; S is read again from TMEM
-        if (t >= 2) {
-          ok = __all_sync(0xffffffffu, mbar_wait(&bars->p_free[sb], ((t >> 1) - 1) & 1, guard, status,
-                                                 kStatusTimeoutConsumer));
-          if (!ok) break;
+#pragma unroll
+        for (int k2 = 0; k2 < 64; ++k2) {
+          float2 x = add_f32x2(make_float2(__uint_as_float(sv[2 * k2]), __uint_as_float(sv[2 * k2 + 1])), negm);
+          x.x = ex2f(x.x);
+          x.y = ex2f(x.y);
+          acc = add_f32x2(acc, x);
+          __half2 hp = __floats2half2_rn(x.x, x.y);
+          sv[k2] = *reinterpret_cast<uint32_t*>(&hp);
         }
-        tc_fence_after();
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t sv[64];
-          tmem_ld32(scol + half * 64, *reinterpret_cast<uint32_t(*)[32]>(sv + 0));
-          tmem_ld32(scol + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
-          tmem_wait_ld();
-          if (masked) {
-#pragma unroll
-            for (int k = 0; k < 64; ++k) sv[k] = __float_as_uint(__uint_as_float(sv[k]) + mb[half * 64 + k]);
-          }
-#pragma unroll
-          for (int k2 = 0; k2 < 32; ++k2) {
-            float2 x = add_f32x2(make_float2(__uint_as_float(sv[2 * k2]), __uint_as_float(sv[2 * k2 + 1])), negm);
-            x.x = ex2f(x.x);
-            x.y = ex2f(x.y);
-            acc = add_f32x2(acc, x);
-            __half2 hp = __floats2half2_rn(x.x, x.y);
-            sv[k2] = *reinterpret_cast<uint32_t*>(&hp);
-          }
-          tmem_st32(tmem + lane_off + 384 + sb * 64 + half * 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 0));
-        }
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(&bars->s_free[sb]);
         const float sum = acc.x + acc.y;
         if (rr == 0) {
           l_run0 = l_run0 * alpha + sum;
@@ -629,8 +654,16 @@ __global__ void __launch_bounds__(k4::kThreads, 1)
 #pragma unroll
           for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
           tmem_st32(tmem + lane_off + r * 32, ov);
-          tmem_wait_st();
         }
+        if (t >= 2) {
+          ok = __all_sync(0xffffffffu, mbar_wait(&bars->p_free[sb], ((t >> 1) - 1) & 1, guard, status,
+                                                 kStatusTimeoutConsumer));
+          if (!ok) break;
+        }
+        tc_fence_after();
+        tmem_st32(tmem + lane_off + 384 + sb * 64, *reinterpret_cast<uint32_t(*)[32]>(sv + 0));
+        tmem_st32(tmem + lane_off + 384 + sb * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
+        tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&bars->p_full[sb]);
       }
@@ -672,7 +705,7 @@ __global__ void __launch_bounds__(k4::kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -926,6 +959,21 @@ int gtk_triatt_core(int starting, const float* mask, void* workspace, int64_t B,
   if (int e = make_head_map(&vm, ws + w.v, B, N)) return e;
   if (int e = make_bias_map(&bm, ws + w.bias, B, N)) return e;
   if (int e = ensure_smem(reinterpret_cast<const void*>(triatt_core_kernel), k4::kSmem)) return e;
+  {
+    // The kernel redistributes registers between warp roles (setmaxnreg); that is only safe
+    // when it is launched with exactly the per-thread count the split was computed for.
+    static int regs = -1;
+    if (regs < 0) {
+      cudaFuncAttributes fa;
+      if (cudaFuncGetAttributes(&fa, reinterpret_cast<const void*>(triatt_core_kernel)) != cudaSuccess)
+        return fail(GTK_ERR_CUDA, "cudaFuncGetAttributes(triatt_core_kernel) failed");
+      regs = fa.numRegs;
+    }
+    if (regs != k4::kLaunchRegs)
+      return fail(GTK_ERR_CUDA, "triatt_core_kernel built with " + std::to_string(regs) +
+                                    " registers/thread; its register split needs " +
+                                    std::to_string(k4::kLaunchRegs));
+  }
   const int n_ig = static_cast<int>((N + k4::kR - 1) / k4::kR);
   if (static_cast<int64_t>(B) * n_ig > 2147483647) return fail(GTK_ERR_INVALID_ARG, "triatt_core: grid too large");
   dim3 grid(static_cast<unsigned>((N + 127) / 128), kHeads, static_cast<unsigned>(B * n_ig));
