@@ -20,6 +20,7 @@
 // The ending node is the starting node on z^T: K3 reads and K4e writes the pair tensor
 // through transposed TMA descriptors, and K4 reads the mask with swapped strides.
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -137,7 +138,8 @@ __device__ __forceinline__ void ln_row_bias(const uint8_t* ztile, uint8_t* atile
 // K3: LN + q/k/v/g projections + triangle bias. One CTA per 128-pair tile (row i of the
 // problem, columns j0..j0+127). Shared memory: W3 128 KB | z 64 KB | A 32 KB | barriers.
 // Outputs: q, k, v fp16 [B*N(i)][H][N(j)][32]; g fp16 [B*N*N][128] (sigmoid applied);
-// bias fp16 [B][H][N][ldn] (log2 units).
+// bias bf16 [B][H][N][ldn] (log2 units; bf16 so that the attention core widens it with
+// integer shifts instead of conversion instructions).
 // ----------------------------------------------------------------------------------
 namespace k3 {
 constexpr uint32_t kW = 0, kZ = 131072, kA = 196608, kBar = 229376;
@@ -148,7 +150,7 @@ __global__ void __launch_bounds__(128, 1)
     triatt_project_kernel(const __grid_constant__ CUtensorMap z_map, const __grid_constant__ CUtensorMap w_map,
                           const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap k_map,
                           const __grid_constant__ CUtensorMap v_map, const __grid_constant__ CUtensorMap g_map,
-                          const float* __restrict__ vec, __half* __restrict__ bias, int N, int ldn,
+                          const float* __restrict__ vec, __nv_bfloat16* __restrict__ bias, int N, int ldn,
                           uint32_t* status) {
   extern __shared__ uint8_t dsmem[];
   uint8_t* smem = align1024(dsmem);
@@ -264,7 +266,7 @@ __global__ void __launch_bounds__(128, 1)
     if (j0 + p < N) {
 #pragma unroll
       for (int h = 0; h < kHeads; ++h)
-        bias[(static_cast<size_t>(b * kHeads + h) * N + i) * ldn + j0 + p] = f16_sat(bacc[h]);
+        bias[(static_cast<size_t>(b * kHeads + h) * N + i) * ldn + j0 + p] = __float2bfloat16_rn(bacc[h]);
     }
   }
   fence_proxy_async_smem();
@@ -307,10 +309,9 @@ __global__ void __launch_bounds__(128, 1)
 // its whole S row slice into registers at once and frees the buffer, so the tensor core
 // computes S(t+2) while the softmax of step t runs; the MMA issuer is a non-blocking
 // state machine that issues S up to two steps ahead of P V.
-// The triangle bias is added by the tensor core: S = Q K^T + I * Bias, with I a resident
-// 128x128 identity and the bias tile [j][k] the MN-major B operand (K = j), so the
-// softmax threads only add the mask bias (on flagged steps), take the max, exponentiate
-// (base 2; q and the bias carry log2 e) and pack P.
+// The softmax threads add the bf16 triangle bias row (widened by integer shifts) and, on
+// flagged steps, the mask bias, take the max, exponentiate (base 2; q and the bias carry
+// log2 e) and pack P. The tensor core only computes Q K^T and P V.
 // TMEM columns: O_r at 32r (0-127), S at 128 + 128*sb, P (fp16 pairs) at 384 + 64*pb.
 // The running max is raised lazily (only when a tile's max exceeds it by > 8, in log2
 // units), so O is rescaled rarely; P then stays <= 2^8, well inside fp16.
@@ -401,7 +402,7 @@ __global__ void __launch_bounds__(k4::kThreads, 1)
     }
     for (int x = 0; x < 2; ++x) {
       mbar_init(&bars->bias_full[x], 1);
-      mbar_init(&bars->bias_empty[x], 1);
+      mbar_init(&bars->bias_empty[x], 256);  // both softmax warpgroups
       mbar_init(&bars->s_full[x], 1);
       mbar_init(&bars->s_free[x], 128);
       mbar_init(&bars->p_full[x], 128);
@@ -411,18 +412,6 @@ __global__ void __launch_bounds__(k4::kThreads, 1)
     mbar_init(&bars->o_final, 1);
     fence_barrier_init();
   }
-  // resident 128x128 fp16 identity (K-major, two 128-B-swizzled K halves)
-  for (int e = tid; e < 128 * 16; e += kThreads) {
-    const int m = e >> 4, kh = (e >> 3) & 1, ch = e & 7;
-    const int d = m - (kh * 64 + ch * 8);
-    uint4 w = make_uint4(0u, 0u, 0u, 0u);
-    if (d >= 0 && d < 8) {
-      const uint32_t one = (d & 1) ? 0x3C000000u : 0x00003C00u;
-      if (d < 2) w.x = one; else if (d < 4) w.y = one; else if (d < 6) w.z = one; else w.w = one;
-    }
-    sts_u4(smem + kI + kh * 16384 + swz128(m, ch), w);
-  }
-  fence_proxy_async_smem();
   if (warp == 9) {
     tmem_alloc(&bars->tslot, 512);
     tmem_relinquish();
@@ -505,36 +494,27 @@ __global__ void __launch_bounds__(k4::kThreads, 1)
     } else if (warp == 9 && lane == 0) {
       // ------------------------------ MMA issuer ------------------------------
       const uint32_t id_s = make_idesc_f16(128, 128, 0, 0);
-      const uint32_t id_b = make_idesc_f16(128, 128, 0, 1);
       const uint32_t id_o = make_idesc_f16(128, 32, 0, 1);
-      const uint32_t iaddr = smem_u32(smem + kI);
       bool ok = mbar_wait(&bars->q_full, 0, guard, status, kStatusTimeoutMma);
       int ns = 0, npv = 0;  // next S step, next P V step
       uint64_t t0 = global_timer_ns();
       uint32_t spins = 0;
       while (ok && npv < T) {
         bool progress = false;
-        // S(ns): needs its K stage, the bias tile of its key tile, and its S buffer freed by step ns-2
+        // S(ns): needs its K stage and its S buffer freed by step ns-2
         if (ns < T && ns < npv + 2 + 1) {
-          const int s = ns % kKVS, sb = ns & 1, kt = ns / kR, bs = kt & 1, r = ns % kR;
+          const int s = ns % kKVS, sb = ns & 1, r = ns % kR;
           if (mbar_test_wait(smem_u32(&bars->kv_full[s]), (ns / kKVS) & 1) &&
-              (r != 0 || mbar_test_wait(smem_u32(&bars->bias_full[bs]), (kt >> 1) & 1)) &&
               (ns < 2 || mbar_test_wait(smem_u32(&bars->s_free[sb]), ((ns >> 1) - 1) & 1))) {
             tc_fence_after();
             const uint32_t qaddr = smem_u32(smem + kQ + r * 8192);
             const uint32_t kaddr = smem_u32(smem + kKV + s * kKVStage);
-            const uint32_t baddr = smem_u32(smem + kBias + bs * kBiasStage);
             const uint32_t dcol = tmem + 128 + sb * 128;
 #pragma unroll
             for (int ks = 0; ks < 2; ++ks)
               umma_ss(dcol, make_sdesc(qaddr + ks * 32, 16, 512, Swz::k64),
                       make_sdesc(kaddr + ks * 32, 16, 512, Swz::k64), id_s, ks > 0 ? 1u : 0u);
-#pragma unroll
-            for (int ks = 0; ks < 8; ++ks)
-              umma_ss(dcol, make_sdesc(iaddr + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024, Swz::k128),
-                      make_sdesc(baddr + ks * 2048, 16384, 1024, Swz::k128), id_b, 1u);
             umma_commit(&bars->s_full[sb]);
-            if (r == kR - 1) umma_commit(&bars->bias_empty[bs]);
             ++ns;
             progress = true;
           }
@@ -583,6 +563,11 @@ __global__ void __launch_bounds__(k4::kThreads, 1)
     float m_run0 = -INFINITY, m_run1 = -INFINITY, l_run0 = 0.f, l_run1 = 0.f;
     bool ok = true;
     for (int kt = 0; kt < KT && ok; ++kt) {
+      const int bs = kt & 1;
+      ok = __all_sync(0xffffffffu,
+                      mbar_wait(&bars->bias_full[bs], (kt >> 1) & 1, guard, status, kStatusTimeoutConsumer));
+      if (!ok) break;
+      const uint8_t* brow = smem + kBias + bs * kBiasStage;
 #pragma unroll
       for (int rr = 0; rr < 2; ++rr) {
         const int r = wg + 2 * rr;
@@ -601,6 +586,22 @@ __global__ void __launch_bounds__(k4::kThreads, 1)
         tc_fence_before();
         mbar_arrive(&bars->s_free[sb]);  // the tensor core may now compute S(t + 2)
 
+        // + triangle bias row j (bf16 -> fp32 by shifting into the high half)
+#pragma unroll
+        for (int kh = 0; kh < 2; ++kh)
+#pragma unroll
+          for (int ch = 0; ch < 8; ++ch) {
+            const uint4 bw = *reinterpret_cast<const uint4*>(brow + kh * 16384 + swz128(jrow, ch));
+            const uint32_t wv[4] = {bw.x, bw.y, bw.z, bw.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int k = kh * 64 + ch * 8 + 2 * e;
+              const float2 x = add_f32x2(make_float2(__uint_as_float(sv[k]), __uint_as_float(sv[k + 1])),
+                                         make_float2(bf16_lo(wv[e]), bf16_hi(wv[e])));
+              sv[k] = __float_as_uint(x.x);
+              sv[k + 1] = __float_as_uint(x.y);
+            }
+          }
         const uint8_t* stage = smem + kKV + s * kKVStage;
         if (*reinterpret_cast<const volatile int*>(stage + kFlag)) {
           const float* mb = reinterpret_cast<const float*>(stage + kMB);
@@ -667,6 +668,7 @@ __global__ void __launch_bounds__(k4::kThreads, 1)
         tc_fence_before();
         mbar_arrive(&bars->p_full[sb]);
       }
+      if (ok) mbar_arrive(&bars->bias_empty[bs]);
     }
     // epilogue: O / l, times the gate, to og (rows wg and wg + 2)
     const bool fin = __all_sync(0xffffffffu, ok && mbar_wait(&bars->o_final, 0, guard, status,
@@ -861,13 +863,13 @@ static int make_hidden_map(CUtensorMap* m, const void* base, int64_t B, int64_t 
   return encode_tmap(m, TmaType::kF16, 3, base, dims, strides, box, 128);
 }
 
-// bias: [B*H][N(j)][ldn] fp16, box (64 k, 128 j, 1), 128-B swizzle.
+// bias: [B*H][N(j)][ldn] bf16, box (64 k, 128 j, 1), 128-B swizzle.
 static int make_bias_map(CUtensorMap* m, const void* base, int64_t B, int64_t N) {
   const uint64_t ldn = round_up(static_cast<uint64_t>(N), 8);
   uint64_t dims[3] = {static_cast<uint64_t>(N), static_cast<uint64_t>(N), static_cast<uint64_t>(B * kHeads)};
   uint64_t strides[2] = {ldn * 2, ldn * 2 * N};
   uint32_t box[3] = {64, 128, 1};
-  return encode_tmap(m, TmaType::kF16, 3, base, dims, strides, box, 128);
+  return encode_tmap(m, TmaType::kBF16, 3, base, dims, strides, box, 128);
 }
 
 static int triatt_check(int c_in, int c_hidden, int heads) {
@@ -941,7 +943,7 @@ int gtk_triatt_project(int starting, const float* z, const void* packed, void* w
   dim3 grid(static_cast<unsigned>((N + 127) / 128), static_cast<unsigned>(N), static_cast<unsigned>(B));
   triatt_project_kernel<<<grid, 128, k3::kSmem, static_cast<cudaStream_t>(stream)>>>(
       zm, wm, qm, km, vm, gm, reinterpret_cast<const float*>(pk + tapack::kVec),
-      reinterpret_cast<__half*>(ws + w.bias), static_cast<int>(N), static_cast<int>(round_up(N, 8)), status);
+      reinterpret_cast<__nv_bfloat16*>(ws + w.bias), static_cast<int>(N), static_cast<int>(round_up(N, 8)), status);
   return check_launch("triatt_project_kernel");
 }
 

@@ -242,10 +242,11 @@ def triatt_workspace(B: int, N: int, device: torch.device):
 
 
 def triatt_stage_views(ws: torch.Tensor, offs, B: int, N: int):
-    """fp16 views of the attention intermediates inside a workspace (problem orientation)."""
-    def view(name, nelem, shape):
+    """Views of the attention intermediates inside a workspace (problem orientation): q, k, v,
+    g, og fp16; the triangle bias bf16."""
+    def view(name, nelem, shape, dtype=torch.float16):
         o = offs[name]
-        return ws[o:o + 2 * nelem].view(torch.float16).view(*shape)
+        return ws[o:o + 2 * nelem].view(dtype).view(*shape)
     H, d = SUPPORTED_HEADS, SUPPORTED_C // SUPPORTED_HEADS
     ldn = plane_pitch(N)
     return {
@@ -254,7 +255,7 @@ def triatt_stage_views(ws: torch.Tensor, offs, B: int, N: int):
         "v": view("v", B * N * H * N * d, (B, N, H, N, d)),
         "g": view("g", B * N * N * SUPPORTED_C, (B, N, N, SUPPORTED_C)),
         "og": view("og", B * N * N * SUPPORTED_C, (B, N, N, SUPPORTED_C)),
-        "bias": view("bias", B * H * N * ldn, (B, H, N, ldn)),
+        "bias": view("bias", B * H * N * ldn, (B, H, N, ldn), torch.bfloat16),
     }
 
 

@@ -57,7 +57,9 @@ def test_stages_match_oracle(starting):
     ref = _oracle_intermediates(z, mask, p, starting)
     for name in ("q", "k", "v", "g"):
         assert_parity(got[name], ref[name], max_abs=1e-2, mean_abs=1e-3, what=name)
-    assert_parity(got["bias"][..., :N], ref["bias"], max_abs=1e-2, mean_abs=1e-3, what="bias")
+    # the bias is stored as bf16 (8-bit mantissa): bound it relative to its magnitude
+    bias_err = (got["bias"][..., :N].float() - ref["bias"]).abs()
+    assert (bias_err <= 2.0 ** -8 * ref["bias"].abs() + 1e-3).all(), float(bias_err.max())
     assert_parity(got["og"], ref["og"], max_abs=1e-2, mean_abs=1e-3, what="og")
     assert_status_clean(dev)
 
