@@ -82,215 +82,238 @@ __device__ __forceinline__ float ex2f(float x) {
   return y;
 }
 
-// LayerNorm of one row (as ln_row_to_operand) that also returns the four triangle-bias
-// dot products of the fp32 normalised row with w_bias (already scaled by log2 e).
-__device__ __forceinline__ void ln_row_bias(const uint8_t* ztile, uint8_t* atile, int p, const float* lnw,
-                                            const float* lnb, const float* wb, float (&acc)[4]) {
-  float s = 0.f;
-#pragma unroll
-  for (int q = 0; q < 4; ++q)
-#pragma unroll
-    for (int ch = 0; ch < 8; ++ch) {
-      const float4 v = lds_f4(ztile + q * 16384 + swz128(p, ch));
-      s += (v.x + v.y) + (v.z + v.w);
-    }
-  const float mean = s * (1.f / 128.f);
-  float ss = 0.f;
-#pragma unroll
-  for (int q = 0; q < 4; ++q)
-#pragma unroll
-    for (int ch = 0; ch < 8; ++ch) {
-      const float4 v = lds_f4(ztile + q * 16384 + swz128(p, ch));
-      const float a = v.x - mean, b = v.y - mean, c = v.z - mean, d = v.w - mean;
-      ss += (a * a + b * b) + (c * c + d * d);
-    }
-  const float rstd = rsqrtf(ss * (1.f / 128.f) + 1e-5f);
-#pragma unroll
-  for (int h = 0; h < 4; ++h) acc[h] = 0.f;
-#pragma unroll 2
-  for (int kh = 0; kh < 2; ++kh)
-#pragma unroll
-    for (int ch = 0; ch < 8; ++ch) {
-      const int c = kh * 64 + ch * 8;
-      const int q = c >> 5, zc = (c & 31) >> 2;
-      const float4 v0 = lds_f4(ztile + q * 16384 + swz128(p, zc));
-      const float4 v1 = lds_f4(ztile + q * 16384 + swz128(p, zc + 1));
-      float y[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-#pragma unroll
-      for (int e = 0; e < 8; ++e) y[e] = (y[e] - mean) * rstd * lnw[c + e] + lnb[c + e];
-#pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        const float4 w0 = *reinterpret_cast<const float4*>(wb + h * 128 + c);
-        const float4 w1 = *reinterpret_cast<const float4*>(wb + h * 128 + c + 4);
-        acc[h] += y[0] * w0.x + y[1] * w0.y + y[2] * w0.z + y[3] * w0.w + y[4] * w1.x + y[5] * w1.y +
-                  y[6] * w1.z + y[7] * w1.w;
-      }
-      uint4 o;
-      o.x = pack_f16x2(y[0], y[1]);
-      o.y = pack_f16x2(y[2], y[3]);
-      o.z = pack_f16x2(y[4], y[5]);
-      o.w = pack_f16x2(y[6], y[7]);
-      sts_u4(atile + kh * 16384 + swz128(p, ch), o);
-    }
+// Sum of four per-lane values over the warp, transposed: afterwards lanes 8h..8h+7 hold
+// the warp total of value h (6 shuffles instead of 4 x 5).
+__device__ __forceinline__ float warp_sum4_transposed(float v0, float v1, float v2, float v3, int lane) {
+  const bool hi16 = lane & 16;
+  float a = hi16 ? v2 : v0, b = hi16 ? v3 : v1;          // keep {0,1} or {2,3}
+  const float sa = hi16 ? v0 : v2, sb = hi16 ? v1 : v3;  // send the other pair
+  a += __shfl_xor_sync(0xffffffffu, sa, 16);
+  b += __shfl_xor_sync(0xffffffffu, sb, 16);
+  const bool hi8 = lane & 8;
+  float c = hi8 ? b : a;
+  c += __shfl_xor_sync(0xffffffffu, hi8 ? a : b, 8);
+  c += __shfl_xor_sync(0xffffffffu, c, 4);
+  c += __shfl_xor_sync(0xffffffffu, c, 2);
+  c += __shfl_xor_sync(0xffffffffu, c, 1);
+  return c;
 }
 
 // ----------------------------------------------------------------------------------
-// K3: LN + q/k/v/g projections + triangle bias. One CTA per 128-pair tile (row i of the
-// problem, columns j0..j0+127). Shared memory: W3 128 KB | z 64 KB | A 32 KB | barriers.
-// Outputs: q, k, v fp16 [B*N(i)][H][N(j)][32]; g fp16 [B*N*N][128] (sigmoid applied);
-// bias bf16 [B][H][N][ldn] (log2 units; bf16 so that the attention core widens it with
-// integer shifts instead of conversion instructions).
+// K3: persistent LN + q/k/v/g projections + triangle bias. Tile = 128 consecutive pairs
+// (b, row i of the problem, j0..j0+127); CTAs loop over tiles. 288 threads:
+//   warps 0-3  LayerNorm producers: warp per pair (coalesced 512-B loads of z, or of z^T
+//              for the ending node), fp16 operand A[s] (double buffered), and the four
+//              triangle-bias dot products of the fp32 LN output (stored as bf16, log2 e);
+//   warp 8     lane 0: loads the 128 KB of weights once, then issues the MMAs;
+//   warps 4-7  epilogue: thread = pair (TMEM lane): q, k, v rows of 64 B per head and the
+//              sigmoid gate row of 256 B, written straight to global memory.
+// TMEM: half 0 = (q, k) columns 0-255, half 1 = (v, g) columns 256-511; the epilogue of
+// one half overlaps the MMAs of the other and the LayerNorm of the next tile.
+// Outputs: q, k, v fp16 [B*N(i)][H][N(j)][32]; g fp16 [B*N*N][128]; bias bf16
+// [B][H][N][ldn] (log2 units; bf16 so that the attention core widens it with shifts).
 // ----------------------------------------------------------------------------------
 namespace k3 {
-constexpr uint32_t kW = 0, kZ = 131072, kA = 196608, kBar = 229376;
-constexpr uint32_t kSmem = kBar + 64 + 1024;
+constexpr int kThreads = 288;
+constexpr uint32_t kW = 0, kA = 131072, kBar = 196608;
+constexpr uint32_t kSmem = kBar + 128 + 1024;
+static_assert(kSmem <= 232448, "K3 shared memory");
 }  // namespace k3
 
-__global__ void __launch_bounds__(128, 1)
-    triatt_project_kernel(const __grid_constant__ CUtensorMap z_map, const __grid_constant__ CUtensorMap w_map,
-                          const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap k_map,
-                          const __grid_constant__ CUtensorMap v_map, const __grid_constant__ CUtensorMap g_map,
-                          const float* __restrict__ vec, __nv_bfloat16* __restrict__ bias, int N, int ldn,
-                          uint32_t* status) {
+struct K3Bars {
+  uint64_t wbar;
+  uint64_t a_full[2], a_empty[2];
+  uint64_t d_full[2], d_empty[2];
+  uint64_t drain;
+  uint32_t tslot;
+  CtaGuard guard;
+};
+static_assert(sizeof(K3Bars) <= 128, "K3 barrier block");
+
+__global__ void __launch_bounds__(k3::kThreads, 1)
+    triatt_project_kernel(const __grid_constant__ CUtensorMap w_map, const float* __restrict__ z, int starting,
+                          const float* __restrict__ vec, __half* __restrict__ q_out, __half* __restrict__ k_out,
+                          __half* __restrict__ v_out, __half* __restrict__ g_out, __nv_bfloat16* __restrict__ bias,
+                          int N, int ldn, int n_jt, int n_tiles, uint32_t* status) {
   extern __shared__ uint8_t dsmem[];
   uint8_t* smem = align1024(dsmem);
-  uint64_t* zbar = reinterpret_cast<uint64_t*>(smem + k3::kBar);
-  uint64_t* wbar = zbar + 1;
-  uint64_t* mbar = zbar + 2;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(zbar + 3);
-  CtaGuard* guard = reinterpret_cast<CtaGuard*>(tslot + 1);
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int j0 = blockIdx.x * 128, i = blockIdx.y, b = blockIdx.z;
-  const int bi = b * N + i;
+  K3Bars* bars = reinterpret_cast<K3Bars*>(smem + k3::kBar);
+  CtaGuard* guard = &bars->guard;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   if (tid == 0) {
     guard->abort = 0;
-    mbar_init(zbar, 1);
-    mbar_init(wbar, 1);
-    mbar_init(mbar, 1);
+    mbar_init(&bars->wbar, 1);
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(&bars->a_full[x], 128);
+      mbar_init(&bars->a_empty[x], 1);
+      mbar_init(&bars->d_full[x], 1);
+      mbar_init(&bars->d_empty[x], 128);
+    }
+    mbar_init(&bars->drain, 1);
     fence_barrier_init();
   }
-  if (warp == 0) {
-    tmem_alloc(tslot, 512);
+  if (warp == 8) {
+    tmem_alloc(&bars->tslot, 512);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tslot;
+  const uint32_t tmem = bars->tslot;
 
-  if (tid == 0) {
-    mbar_arrive_expect_tx(zbar, 65536);
+  if (warp < 4) {
+    // ------------------------- LayerNorm + bias producers -------------------------
+    const float4 gw = reinterpret_cast<const float4*>(vec + tapack::kVLnW)[lane];
+    const float4 gb = reinterpret_cast<const float4*>(vec + tapack::kVLnB)[lane];
+    float4 wb[kHeads];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) tma_load_4d(smem + k3::kZ + q * 16384, &z_map, zbar, q * 32, j0, i, b);
-    mbar_arrive_expect_tx(wbar, 131072);
+    for (int h = 0; h < kHeads; ++h) wb[h] = reinterpret_cast<const float4*>(vec + tapack::kVWb + h * 128)[lane];
+    int it = 0;
+    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+      const int s = it & 1;
+      const int jt = tile % n_jt, bi = tile / n_jt;  // bi = b * N + i
+      const int i = bi % N, b = bi / N, j0 = jt * 128;
+      if (it >= 2) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&bars->a_empty[s], ((it >> 1) - 1) & 1, guard, status,
+                                               kStatusTimeoutProducer)))
+          break;
+      }
+      uint8_t* at = smem + k3::kA + s * 32768 + (lane >> 4) * 16384;
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        float4 v[16];
 #pragma unroll
-    for (int kh = 0; kh < 2; ++kh)
+        for (int k = 0; k < 16; ++k) {
+          const int j = j0 + warp * 32 + half * 16 + k;
+          const size_t pr =
+              starting ? (static_cast<size_t>(b) * N + i) * N + j : (static_cast<size_t>(b) * N + j) * N + i;
+          v[k] = j < N ? __ldg(reinterpret_cast<const float4*>(z + pr * 128) + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
 #pragma unroll
-      for (int rb = 0; rb < 4; ++rb)
-        tma_load_2d(smem + k3::kW + kh * 65536 + rb * 16384, &w_map, wbar, kh * 64, rb * 128);
-  }
-
-  const int p = tid;
-  float bacc[4] = {0.f, 0.f, 0.f, 0.f};
-  if (mbar_wait(zbar, 0, guard, status, kStatusTimeoutConsumer)) {
-    ln_row_bias(smem + k3::kZ, smem + k3::kA, p, vec + tapack::kVLnW, vec + tapack::kVLnB, vec + tapack::kVWb, bacc);
-  }
-  fence_proxy_async_smem();
-  __syncthreads();
-  // the z tile is dead: keep b_g there for the epilogue
-  float* sbg = reinterpret_cast<float*>(smem + k3::kZ);
-  sbg[tid] = vec[tapack::kVBg + tid];
-
-  if (tid == 0 && !guard->abort) {
-    if (mbar_wait(wbar, 0, guard, status, kStatusTimeoutMma)) {
-      tc_fence_after();
+        for (int k = 0; k < 16; ++k) {
+          const float mean = warp_sum((v[k].x + v[k].y) + (v[k].z + v[k].w)) * (1.f / 128.f);
+          const float dx = v[k].x - mean, dy = v[k].y - mean, dz = v[k].z - mean, dw = v[k].w - mean;
+          const float var = warp_sum((dx * dx + dy * dy) + (dz * dz + dw * dw)) * (1.f / 128.f);
+          const float rstd = rsqrtf(var + 1e-5f);
+          const float y0 = dx * rstd * gw.x + gb.x, y1 = dy * rstd * gw.y + gb.y;
+          const float y2 = dz * rstd * gw.z + gb.z, y3 = dw * rstd * gw.w + gb.w;
+          uint2 o;
+          o.x = pack_f16x2(y0, y1);
+          o.y = pack_f16x2(y2, y3);
+          const int pr = warp * 32 + half * 16 + k;
+          *reinterpret_cast<uint2*>(at + swz128(pr, (lane & 15) >> 1) + (lane & 1) * 8) = o;
+          float pb[kHeads];
+#pragma unroll
+          for (int h = 0; h < kHeads; ++h) pb[h] = y0 * wb[h].x + y1 * wb[h].y + y2 * wb[h].z + y3 * wb[h].w;
+          const float tot = warp_sum4_transposed(pb[0], pb[1], pb[2], pb[3], lane);
+          const int j = j0 + pr;
+          if ((lane & 7) == 0 && j < N)
+            bias[(static_cast<size_t>(b * kHeads + (lane >> 3)) * N + i) * ldn + j] = __float2bfloat16_rn(tot);
+        }
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&bars->a_full[s]);
+    }
+  } else if (warp == 8) {
+    // ------------------------- weights + MMA issuer -------------------------
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&bars->wbar, 131072);
+#pragma unroll
+      for (int kh = 0; kh < 2; ++kh)
+#pragma unroll
+        for (int rb = 0; rb < 4; ++rb)
+          tma_load_2d(smem + k3::kW + kh * 65536 + rb * 16384, &w_map, &bars->wbar, kh * 64, rb * 128);
+      bool ok = mbar_wait(&bars->wbar, 0, guard, status, kStatusTimeoutMma);
       const uint32_t idesc = make_idesc_f16(128, 256, 0, 0);
-      const uint32_t a0 = smem_u32(smem + k3::kA), w0 = smem_u32(smem + k3::kW);
+      const uint32_t w0 = smem_u32(smem + k3::kW);
+      int it = 0;
+      for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++it) {
+        const int s = it & 1;
+        ok = mbar_wait(&bars->a_full[s], (it >> 1) & 1, guard, status, kStatusTimeoutMma);
+        const uint32_t a0 = smem_u32(smem + k3::kA + s * 32768);
+        for (int h = 0; ok && h < 2; ++h) {
+          if (it >= 1) ok = mbar_wait(&bars->d_empty[h], (it - 1) & 1, guard, status, kStatusTimeoutMma);
+          if (!ok) break;
+          tc_fence_after();
 #pragma unroll
-      for (int nh = 0; nh < 2; ++nh)
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-          const int kh = ks >> 2, kin = ks & 3;
-          umma_ss(tmem + nh * 256, make_sdesc(a0 + kh * 16384 + kin * 32, 16, 1024, Swz::k128),
-                  make_sdesc(w0 + kh * 65536 + nh * 32768 + kin * 32, 16, 1024, Swz::k128), idesc, ks > 0 ? 1u : 0u);
+          for (int ks = 0; ks < 8; ++ks) {
+            const int kh = ks >> 2, kin = ks & 3;
+            umma_ss(tmem + h * 256, make_sdesc(a0 + kh * 16384 + kin * 32, 16, 1024, Swz::k128),
+                    make_sdesc(w0 + kh * 65536 + h * 32768 + kin * 32, 16, 1024, Swz::k128), idesc, ks > 0 ? 1u : 0u);
+          }
+          umma_commit(&bars->d_full[h]);
         }
-      umma_commit(mbar);
+        if (ok) umma_commit(&bars->a_empty[s]);
+      }
+      if (!ok) {
+        umma_commit(&bars->drain);
+        mbar_wait_drain(&bars->drain, 0);
+        mbar_wait_drain(&bars->wbar, 0);
+      }
     }
-  }
-  __syncthreads();
-  const bool ok = __all_sync(0xffffffffu, mbar_wait(mbar, 0, guard, status, kStatusTimeoutConsumer));
-  tc_fence_after();
-  if (ok) {
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-    // q, k, v: [4 heads][128 j][32 d] fp16, 64-B swizzled, at W + {0, 32, 64} KB
+  } else {
+    // ------------------------- epilogue: thread = pair -------------------------
+    const int q4 = warp & 3;
+    const int p = q4 * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
+    const float* bg = vec + tapack::kVBg;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+      const int jt = tile % n_jt, bi = tile / n_jt;
+      const int j = jt * 128 + p;
+      const bool valid = j < N;
+      bool ok = true;
 #pragma unroll 1
-    for (int which = 0; which < 3; ++which) {
-      uint8_t* stage = smem + k3::kW + which * 32768;
+      for (int h = 0; h < 2; ++h) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars->d_full[h], it & 1, guard, status, kStatusTimeoutConsumer));
+        if (!ok) break;
+        tc_fence_after();
 #pragma unroll 1
-      for (int h = 0; h < kHeads; ++h) {
-        uint32_t v[32];
-        tmem_ld32(tmem + lane_base + which * 128 + h * 32, v);
-        tmem_wait_ld();
+        for (int cc = 0; cc < 4; ++cc) {
+          uint32_t x0[32], x1[32];
+          tmem_ld32(tmem + lane_off + h * 256 + cc * 32, x0);
+          tmem_ld32(tmem + lane_off + h * 256 + 128 + cc * 32, x1);
+          tmem_wait_ld();
+          if (!valid) continue;
+          // first 128 columns of the half: q (h = 0) or v (h = 1), head cc: 64 contiguous bytes
+          __half* dst0 = (h == 0 ? q_out : v_out) + ((static_cast<size_t>(bi) * kHeads + cc) * N + j) * kHeadDim;
+          uint4* d0 = reinterpret_cast<uint4*>(dst0);
 #pragma unroll
-        for (int ch = 0; ch < 4; ++ch) {
-          uint4 o;
-          o.x = pack_f16x2(__uint_as_float(v[ch * 8 + 0]), __uint_as_float(v[ch * 8 + 1]));
-          o.y = pack_f16x2(__uint_as_float(v[ch * 8 + 2]), __uint_as_float(v[ch * 8 + 3]));
-          o.z = pack_f16x2(__uint_as_float(v[ch * 8 + 4]), __uint_as_float(v[ch * 8 + 5]));
-          o.w = pack_f16x2(__uint_as_float(v[ch * 8 + 6]), __uint_as_float(v[ch * 8 + 7]));
-          sts_u4(stage + h * 8192 + swz64(p, ch), o);
+          for (int u = 0; u < 4; ++u)
+            d0[u] = make_uint4(pack_f16x2(__uint_as_float(x0[u * 8 + 0]), __uint_as_float(x0[u * 8 + 1])),
+                               pack_f16x2(__uint_as_float(x0[u * 8 + 2]), __uint_as_float(x0[u * 8 + 3])),
+                               pack_f16x2(__uint_as_float(x0[u * 8 + 4]), __uint_as_float(x0[u * 8 + 5])),
+                               pack_f16x2(__uint_as_float(x0[u * 8 + 6]), __uint_as_float(x0[u * 8 + 7])));
+          if (h == 0) {
+            uint4* d1 = reinterpret_cast<uint4*>(k_out + ((static_cast<size_t>(bi) * kHeads + cc) * N + j) * kHeadDim);
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              d1[u] = make_uint4(pack_f16x2(__uint_as_float(x1[u * 8 + 0]), __uint_as_float(x1[u * 8 + 1])),
+                                 pack_f16x2(__uint_as_float(x1[u * 8 + 2]), __uint_as_float(x1[u * 8 + 3])),
+                                 pack_f16x2(__uint_as_float(x1[u * 8 + 4]), __uint_as_float(x1[u * 8 + 5])),
+                                 pack_f16x2(__uint_as_float(x1[u * 8 + 6]), __uint_as_float(x1[u * 8 + 7])));
+          } else {
+            uint4* d1 = reinterpret_cast<uint4*>(g_out + (static_cast<size_t>(bi) * N + j) * 128 + cc * 32);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              float gv[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) gv[e] = sigmoid_tanh(__uint_as_float(x1[u * 8 + e]) + bg[cc * 32 + u * 8 + e]);
+              d1[u] = make_uint4(pack_f16x2(gv[0], gv[1]), pack_f16x2(gv[2], gv[3]), pack_f16x2(gv[4], gv[5]),
+                                 pack_f16x2(gv[6], gv[7]));
+            }
+          }
         }
+        tc_fence_before();
+        mbar_arrive(&bars->d_empty[h]);
       }
-    }
-    // gate: sigmoid(linear_g + b_g) -> [128 j][128] fp16 as two 128-B-swizzled halves at W + 96 KB
-    uint8_t* gstage = smem + k3::kW + 98304;
-#pragma unroll 1
-    for (int cc = 0; cc < 4; ++cc) {
-      uint32_t v[32];
-      tmem_ld32(tmem + lane_base + 384 + cc * 32, v);
-      tmem_wait_ld();
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        float gv[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) gv[e] = sigmoidf_fast(__uint_as_float(v[u * 8 + e]) + sbg[cc * 32 + u * 8 + e]);
-        uint4 o;
-        o.x = pack_f16x2(gv[0], gv[1]);
-        o.y = pack_f16x2(gv[2], gv[3]);
-        o.z = pack_f16x2(gv[4], gv[5]);
-        o.w = pack_f16x2(gv[6], gv[7]);
-        sts_u4(gstage + (cc >> 1) * 16384 + swz128(p, (cc & 1) * 4 + u), o);
-      }
-    }
-    if (j0 + p < N) {
-#pragma unroll
-      for (int h = 0; h < kHeads; ++h)
-        bias[(static_cast<size_t>(b * kHeads + h) * N + i) * ldn + j0 + p] = __float2bfloat16_rn(bacc[h]);
-    }
-  }
-  fence_proxy_async_smem();
-  __syncthreads();
-  if (tid == 0) {
-    if (ok && !guard->abort) {
-#pragma unroll
-      for (int h = 0; h < kHeads; ++h) {
-        tma_store_4d(&q_map, smem + k3::kW + h * 8192, 0, j0, h, bi);
-        tma_store_4d(&k_map, smem + k3::kW + 32768 + h * 8192, 0, j0, h, bi);
-        tma_store_4d(&v_map, smem + k3::kW + 65536 + h * 8192, 0, j0, h, bi);
-      }
-#pragma unroll
-      for (int kh = 0; kh < 2; ++kh) tma_store_3d(&g_map, smem + k3::kW + 98304 + kh * 16384, kh * 64, j0, bi);
-      tma_store_commit();
-      tma_store_wait_read();
-    } else {
-      mbar_wait_drain(zbar, 0);
-      mbar_wait_drain(wbar, 0);
+      if (!ok) break;
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == 8) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -714,115 +737,179 @@ __global__ void __launch_bounds__(k4::kThreads, 1)
 }
 
 // ----------------------------------------------------------------------------------
-// K4e: update = og W_o^T + b_o (+ residual), written through the (possibly transposed)
-// pair descriptor. Shared memory: og 32 KB | W4 32 KB | z 64 KB | barriers.
+// K4e: persistent update = og W_o^T + b_o (+ residual), written through the (possibly
+// transposed) pair descriptor. Tile = 128 pairs of row i of the problem. 192 threads:
+//   warps 0-3  epilogue: thread = pair (TMEM lane); bias, residual, 32-channel fp32 slabs
+//              staged in shared memory and written with TMA stores (2 slab buffers);
+//   warp 4     lane 0: TMA producer (W_o once, og tiles double buffered);
+//   warp 5     lane 0: MMA issuer (TMEM double buffered, 128 columns per tile).
+// Shared memory: W4 32 KB | og 2 x 32 KB | out slabs 2 x 16 KB | b_o | barriers.
 // ----------------------------------------------------------------------------------
 namespace k4e {
-constexpr uint32_t kA = 0, kW = 32768, kZ = 65536, kBar = 131072;
-constexpr uint32_t kSmem = kBar + 64 + 1024;
+constexpr int kThreads = 192;
+constexpr uint32_t kW = 0, kA = 32768, kO = 98304, kVec = 131072, kBar = 131072 + 512;
+constexpr uint32_t kSmem = kBar + 128 + 1024;
+static_assert(kSmem <= 232448, "K4e shared memory");
 }  // namespace k4e
 
-__global__ void __launch_bounds__(128, 1)
+struct K4eBars {
+  uint64_t wbar;
+  uint64_t a_full[2], a_empty[2];
+  uint64_t d_full[2], d_empty[2];
+  uint64_t drain;
+  uint32_t tslot;
+  CtaGuard guard;
+};
+static_assert(sizeof(K4eBars) <= 128, "K4e barrier block");
+
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+__global__ void __launch_bounds__(k4e::kThreads, 1)
     triatt_finish_kernel(const __grid_constant__ CUtensorMap og_map, const __grid_constant__ CUtensorMap w_map,
-                         const __grid_constant__ CUtensorMap z_map, const __grid_constant__ CUtensorMap out_map,
-                         const float* __restrict__ vec, int N, int add_residual, uint32_t* status) {
+                         const __grid_constant__ CUtensorMap out_map, const float* __restrict__ z, int starting,
+                         const float* __restrict__ vec, int N, int add_residual, int n_jt, int n_tiles,
+                         uint32_t* status) {
   extern __shared__ uint8_t dsmem[];
   uint8_t* smem = align1024(dsmem);
-  uint64_t* lbar = reinterpret_cast<uint64_t*>(smem + k4e::kBar);
-  uint64_t* mbar = lbar + 1;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(lbar + 2);
-  CtaGuard* guard = reinterpret_cast<CtaGuard*>(tslot + 1);
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int j0 = blockIdx.x * 128, i = blockIdx.y, b = blockIdx.z;
+  K4eBars* bars = reinterpret_cast<K4eBars*>(smem + k4e::kBar);
+  CtaGuard* guard = &bars->guard;
+  float* sbo = reinterpret_cast<float*>(smem + k4e::kVec);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   if (tid == 0) {
     guard->abort = 0;
-    mbar_init(lbar, 1);
-    mbar_init(mbar, 1);
+    mbar_init(&bars->wbar, 1);
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(&bars->a_full[x], 1);
+      mbar_init(&bars->a_empty[x], 1);
+      mbar_init(&bars->d_full[x], 1);
+      mbar_init(&bars->d_empty[x], 128);
+    }
+    mbar_init(&bars->drain, 1);
     fence_barrier_init();
   }
-  if (warp == 0) {
-    tmem_alloc(tslot, 128);
+  if (tid < 128) sbo[tid] = vec[tapack::kVBo + tid];
+  if (warp == 5) {
+    tmem_alloc(&bars->tslot, 256);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tslot;
+  const uint32_t tmem = bars->tslot;
 
-  if (tid == 0) {
-    mbar_arrive_expect_tx(lbar, 32768 + 32768 + (add_residual ? 65536 : 0));
+  if (warp == 4) {
+    // ------------------------------ TMA producer ------------------------------
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&bars->wbar, 32768);
 #pragma unroll
-    for (int kh = 0; kh < 2; ++kh) {
-      tma_load_3d(smem + k4e::kA + kh * 16384, &og_map, lbar, kh * 64, j0, b * N + i);
-      tma_load_2d(smem + k4e::kW + kh * 16384, &w_map, lbar, kh * 64, 0);
-    }
-    if (add_residual) {
-#pragma unroll
-      for (int q = 0; q < 4; ++q) tma_load_4d(smem + k4e::kZ + q * 16384, &z_map, lbar, q * 32, j0, i, b);
-    }
-    if (mbar_wait(lbar, 0, guard, status, kStatusTimeoutMma)) {
-      tc_fence_after();
-      const uint32_t a0 = smem_u32(smem + k4e::kA), w0 = smem_u32(smem + k4e::kW);
-      const uint32_t idesc = make_idesc_f16(128, 128, 0, 0);
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const int kh = ks >> 2, kin = ks & 3;
-        umma_ss(tmem, make_sdesc(a0 + kh * 16384 + kin * 32, 16, 1024, Swz::k128),
-                make_sdesc(w0 + kh * 16384 + kin * 32, 16, 1024, Swz::k128), idesc, ks > 0 ? 1u : 0u);
-      }
-      umma_commit(mbar);
-    }
-  }
-  const bool ok = __all_sync(0xffffffffu, mbar_wait(mbar, 0, guard, status, kStatusTimeoutConsumer) &&
-                                              mbar_wait(lbar, 0, guard, status, kStatusTimeoutConsumer));
-  tc_fence_after();
-  if (ok) {
-    const int p = tid;
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-    const float* bo = vec + tapack::kVBo;
-#pragma unroll 1
-    for (int cc = 0; cc < 4; ++cc) {
-      uint32_t v[32];
-      tmem_ld32(tmem + lane_base + cc * 32, v);
-      tmem_wait_ld();
-      uint8_t* zq = smem + k4e::kZ + cc * 16384;
-#pragma unroll
-      for (int ch = 0; ch < 8; ++ch) {
-        float4 o;
-        const int n = cc * 32 + ch * 4;
-        o.x = __uint_as_float(v[ch * 4 + 0]) + bo[n + 0];
-        o.y = __uint_as_float(v[ch * 4 + 1]) + bo[n + 1];
-        o.z = __uint_as_float(v[ch * 4 + 2]) + bo[n + 2];
-        o.w = __uint_as_float(v[ch * 4 + 3]) + bo[n + 3];
-        if (add_residual) {
-          const float4 zv = lds_f4(zq + swz128(p, ch));
-          o.x += zv.x;
-          o.y += zv.y;
-          o.z += zv.z;
-          o.w += zv.w;
+      for (int kh = 0; kh < 2; ++kh) tma_load_2d(smem + k4e::kW + kh * 16384, &w_map, &bars->wbar, kh * 64, 0);
+      bool ok = true;
+      int it = 0, issued = 0;
+      for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+        const int s = it & 1;
+        const int jt = tile % n_jt, bi = tile / n_jt;
+        if (it >= 2 && !mbar_wait(&bars->a_empty[s], ((it >> 1) - 1) & 1, guard, status, kStatusTimeoutProducer)) {
+          ok = false;
+          break;
         }
-        *reinterpret_cast<float4*>(zq + swz128(p, ch)) = o;
+        mbar_arrive_expect_tx(&bars->a_full[s], 32768);
+#pragma unroll
+        for (int kh = 0; kh < 2; ++kh)
+          tma_load_3d(smem + k4e::kA + s * 32768 + kh * 16384, &og_map, &bars->a_full[s], kh * 64, jt * 128, bi);
+        ++issued;
+      }
+      if (!ok) {
+        for (int t = (issued > 2 ? issued - 2 : 0); t < issued; ++t) mbar_wait_drain(&bars->a_full[t & 1], (t >> 1) & 1);
+      }
+      mbar_wait_drain(&bars->wbar, 0);
+    }
+  } else if (warp == 5) {
+    // ------------------------------ MMA issuer ------------------------------
+    if (lane == 0) {
+      bool ok = mbar_wait(&bars->wbar, 0, guard, status, kStatusTimeoutMma);
+      const uint32_t idesc = make_idesc_f16(128, 128, 0, 0);
+      const uint32_t w0 = smem_u32(smem + k4e::kW);
+      int it = 0;
+      for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++it) {
+        const int s = it & 1;
+        ok = mbar_wait(&bars->a_full[s], (it >> 1) & 1, guard, status, kStatusTimeoutMma);
+        if (ok && it >= 2) ok = mbar_wait(&bars->d_empty[s], ((it >> 1) - 1) & 1, guard, status, kStatusTimeoutMma);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(smem + k4e::kA + s * 32768);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const int kh = ks >> 2, kin = ks & 3;
+          umma_ss(tmem + s * 128, make_sdesc(a0 + kh * 16384 + kin * 32, 16, 1024, Swz::k128),
+                  make_sdesc(w0 + kh * 16384 + kin * 32, 16, 1024, Swz::k128), idesc, ks > 0 ? 1u : 0u);
+        }
+        umma_commit(&bars->d_full[s]);
+        umma_commit(&bars->a_empty[s]);
+      }
+      if (!ok) {
+        umma_commit(&bars->drain);
+        mbar_wait_drain(&bars->drain, 0);
       }
     }
-  }
-  fence_proxy_async_smem();
-  __syncthreads();
-  if (tid == 0) {
-    if (ok && !guard->abort) {
+  } else {
+    // ------------------------- epilogue: thread = pair -------------------------
+    const int p = tid;  // warps 0-3
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    const bool issuer = (tid == 0);
+    int it = 0, slab = 0;
+    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+      const int s = it & 1;
+      const int jt = tile % n_jt, bi = tile / n_jt;
+      const int i = bi % N, b = bi / N, j0 = jt * 128;
+      if (!__all_sync(0xffffffffu, mbar_wait(&bars->d_full[s], (it >> 1) & 1, guard, status, kStatusTimeoutConsumer)))
+        break;
+      tc_fence_after();
+      const int j = j0 + p;
+      const bool valid = j < N;
+      const size_t zpair = starting ? (static_cast<size_t>(b) * N + i) * N + j : (static_cast<size_t>(b) * N + j) * N + i;
+#pragma unroll 1
+      for (int cc = 0; cc < 4; ++cc, ++slab) {
+        uint32_t d[32];
+        tmem_ld32(tmem + lane_off + s * 128 + cc * 32, d);
+        float4 res[8];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) tma_store_4d(&out_map, smem + k4e::kZ + q * 16384, q * 32, j0, i, b);
-      tma_store_commit();
-      tma_store_wait_read();
-    } else {
-      mbar_wait_drain(lbar, 0);
+        for (int q = 0; q < 8; ++q)
+          res[q] = (add_residual && valid) ? __ldg(reinterpret_cast<const float4*>(z + zpair * 128 + cc * 32) + q)
+                                           : make_float4(0.f, 0.f, 0.f, 0.f);
+        tmem_wait_ld();
+        if (issuer) tma_store_wait_read_le1();
+        named_bar_sync(1, 128);
+        uint8_t* ob = smem + k4e::kO + (slab & 1) * 16384;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const int n = cc * 32 + q * 4;
+          float4 o;
+          o.x = __uint_as_float(d[q * 4 + 0]) + sbo[n + 0] + res[q].x;
+          o.y = __uint_as_float(d[q * 4 + 1]) + sbo[n + 1] + res[q].y;
+          o.z = __uint_as_float(d[q * 4 + 2]) + sbo[n + 2] + res[q].z;
+          o.w = __uint_as_float(d[q * 4 + 3]) + sbo[n + 3] + res[q].w;
+          *reinterpret_cast<float4*>(ob + swz128(p, q)) = o;
+        }
+        fence_proxy_async_smem();
+        named_bar_sync(1, 128);
+        if (issuer) {
+          tma_store_4d(&out_map, ob, cc * 32, j0, i, b);
+          tma_store_commit();
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&bars->d_empty[s]);
     }
+    if (issuer) tma_store_wait_all();
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == 5) {
     tc_fence_after();
-    tmem_dealloc(tmem, 128);
+    tmem_dealloc(tmem, 256);
   }
 }
 
@@ -932,18 +1019,18 @@ int gtk_triatt_project(int starting, const float* z, const void* packed, void* w
   const TriattWs w = triatt_layout(B, N);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   const uint8_t* pk = static_cast<const uint8_t*>(packed);
-  CUtensorMap zm, wm, qm, km, vm, gm;
-  if (int e = make_pair_map(&zm, z, B, N, N, !starting)) return e;
+  const int64_t n_jt = (N + 127) / 128;
+  const int64_t n_tiles = B * N * n_jt;
+  if (n_tiles > 2147483647) return fail(GTK_ERR_INVALID_ARG, "triatt_project: too many tiles");
+  CUtensorMap wm;
   if (int e = make_weight_map(&wm, pk + tapack::kW3, 512, 128)) return e;
-  if (int e = make_head_map(&qm, ws + w.q, B, N)) return e;
-  if (int e = make_head_map(&km, ws + w.k, B, N)) return e;
-  if (int e = make_head_map(&vm, ws + w.v, B, N)) return e;
-  if (int e = make_hidden_map(&gm, ws + w.g, B, N)) return e;
   if (int e = ensure_smem(reinterpret_cast<const void*>(triatt_project_kernel), k3::kSmem)) return e;
-  dim3 grid(static_cast<unsigned>((N + 127) / 128), static_cast<unsigned>(N), static_cast<unsigned>(B));
-  triatt_project_kernel<<<grid, 128, k3::kSmem, static_cast<cudaStream_t>(stream)>>>(
-      zm, wm, qm, km, vm, gm, reinterpret_cast<const float*>(pk + tapack::kVec),
-      reinterpret_cast<__nv_bfloat16*>(ws + w.bias), static_cast<int>(N), static_cast<int>(round_up(N, 8)), status);
+  const int grid = static_cast<int>(n_tiles < num_sms() ? n_tiles : num_sms());
+  triatt_project_kernel<<<grid, k3::kThreads, k3::kSmem, static_cast<cudaStream_t>(stream)>>>(
+      wm, z, starting, reinterpret_cast<const float*>(pk + tapack::kVec), reinterpret_cast<__half*>(ws + w.q),
+      reinterpret_cast<__half*>(ws + w.k), reinterpret_cast<__half*>(ws + w.v), reinterpret_cast<__half*>(ws + w.g),
+      reinterpret_cast<__nv_bfloat16*>(ws + w.bias), static_cast<int>(N), static_cast<int>(round_up(N, 8)),
+      static_cast<int>(n_jt), static_cast<int>(n_tiles), status);
   return check_launch("triatt_project_kernel");
 }
 
@@ -998,15 +1085,18 @@ int gtk_triatt_finish(int starting, const float* z, const void* packed, void* wo
   const TriattWs w = triatt_layout(B, N);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   const uint8_t* pk = static_cast<const uint8_t*>(packed);
-  CUtensorMap am, wm, zm, om;
+  const int64_t n_jt = (N + 127) / 128;
+  const int64_t n_tiles = B * N * n_jt;
+  if (n_tiles > 2147483647) return fail(GTK_ERR_INVALID_ARG, "triatt_finish: too many tiles");
+  CUtensorMap am, wm, om;
   if (int e = make_hidden_map(&am, ws + w.og, B, N)) return e;
   if (int e = make_weight_map(&wm, pk + tapack::kW4, 128, 128)) return e;
-  if (int e = make_pair_map(&zm, add_residual ? z : out, B, N, N, !starting)) return e;
   if (int e = make_pair_map(&om, out, B, N, N, !starting)) return e;
   if (int e = ensure_smem(reinterpret_cast<const void*>(triatt_finish_kernel), k4e::kSmem)) return e;
-  dim3 grid(static_cast<unsigned>((N + 127) / 128), static_cast<unsigned>(N), static_cast<unsigned>(B));
-  triatt_finish_kernel<<<grid, 128, k4e::kSmem, static_cast<cudaStream_t>(stream)>>>(
-      am, wm, zm, om, reinterpret_cast<const float*>(pk + tapack::kVec), static_cast<int>(N), add_residual, status);
+  const int grid = static_cast<int>(n_tiles < num_sms() ? n_tiles : num_sms());
+  triatt_finish_kernel<<<grid, k4e::kThreads, k4e::kSmem, static_cast<cudaStream_t>(stream)>>>(
+      am, wm, om, z, starting, reinterpret_cast<const float*>(pk + tapack::kVec), static_cast<int>(N), add_residual,
+      static_cast<int>(n_jt), static_cast<int>(n_tiles), status);
   return check_launch("triatt_finish_kernel");
 }
 

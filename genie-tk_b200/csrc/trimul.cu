@@ -100,6 +100,7 @@ namespace k1 {
 constexpr int kThreads = 288;
 constexpr uint32_t kW = 0, kA = 131072, kMask = 196608, kBar = 197632;
 constexpr uint32_t kSmem = kBar + 128 + 1024;
+static_assert(kSmem <= 232448, "K1 shared memory");
 }  // namespace k1
 
 struct K1Bars {
@@ -302,6 +303,7 @@ constexpr int kStages = 4;
 constexpr uint32_t kStageBytes = 49152;  // A 128x64 (16 KB) + B 256x64 (32 KB)
 constexpr uint32_t kBar = kStages * kStageBytes;
 constexpr uint32_t kSmem = kBar + 128 + 1024;
+static_assert(kSmem <= 232448, "K2 shared memory");
 }  // namespace k2
 
 template <bool kOutgoing>
@@ -431,154 +433,268 @@ __global__ void __launch_bounds__(128, 1)
 }
 
 // ----------------------------------------------------------------------------------
-// K2e: LN_out + linear_z + output gate (+ residual). One CTA per 128-pair tile.
-// Shared memory: W2 64 KB | z 64 KB | x 32 KB | LN_in(z) 32 KB | vec 2.5 KB | barriers.
-// TMEM: cols 0-127 gate pre-activation G, cols 128-255 U = x (W_z*gamma)^T.
+// K2e: persistent LN_out + linear_z + output gate (+ residual). Tile = 128 consecutive
+// pairs; CTAs loop over tiles. 320 threads:
+//   warps 0-3  LayerNorm producers: LN_in(z) of the tile's pairs (warp per pair row,
+//              coalesced loads) into the fp16 operand A[s] (double buffered);
+//   warps 4-7  epilogue: thread = pair p (TMEM lane); LN_out statistics from the x tile
+//              in shared memory, gate, residual, staged in 32-channel fp32 slabs and
+//              written with TMA stores (2 slab buffers);
+//   warp 8     lane 0: MMA issuer; warp 9 lane 0: TMA producer (weights once, x tiles).
+// TMEM (double buffered per tile, 256 columns each): G = A W_g^T at +0, U = x^T (W_z gamma)^T
+// at +128. LN_out folds into the epilogue: out = g * (rstd (U - mu u) + v).
+// Shared memory: W2 64 KB | A 2 x 32 KB | x 2 x 32 KB | out slabs 2 x 16 KB | b_g,u,v | barriers.
 // ----------------------------------------------------------------------------------
 namespace k2e {
-constexpr uint32_t kW = 0, kZ = 65536, kX = 131072, kA = 163840, kVec = 196608, kBar = 196608 + 2560;
-constexpr uint32_t kSmem = kBar + 64 + 1024;
+constexpr int kThreads = 320;
+constexpr uint32_t kW = 0, kA = 65536, kX = 131072, kO = 196608, kVec = 229376, kBar = 229376 + 1536;
+constexpr uint32_t kSmem = kBar + 128 + 1024;
+static_assert(kSmem <= 232448, "K2e shared memory");
 }  // namespace k2e
 
-__global__ void __launch_bounds__(128, 1)
-    trimul_finish_kernel(const __grid_constant__ CUtensorMap z_map, const __grid_constant__ CUtensorMap w_map,
-                         const __grid_constant__ CUtensorMap x_map, const __grid_constant__ CUtensorMap out_map,
-                         const float* __restrict__ vec, int add_residual, float x_scale, uint32_t* status) {
+struct K2eBars {
+  uint64_t wbar;
+  uint64_t a_full[2], a_empty[2];
+  uint64_t x_full[2], x_empty[2];
+  uint64_t d_full[2], d_empty[2];
+  uint64_t drain;
+  uint32_t tslot;
+  CtaGuard guard;
+};
+static_assert(sizeof(K2eBars) <= 128, "K2e barrier block");
+
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+__global__ void __launch_bounds__(k2e::kThreads, 1)
+    trimul_finish_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap x_map,
+                         const __grid_constant__ CUtensorMap out_map, const float* __restrict__ z,
+                         const float* __restrict__ vec, int add_residual, float x_scale, int N, int rows, int n_jt,
+                         int n_tiles, uint32_t* status) {
   extern __shared__ uint8_t dsmem[];
   uint8_t* smem = align1024(dsmem);
-  uint64_t* lbar = reinterpret_cast<uint64_t*>(smem + k2e::kBar);
-  uint64_t* mbar = lbar + 1;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(lbar + 2);
-  CtaGuard* guard = reinterpret_cast<CtaGuard*>(tslot + 1);
-  float* svec = reinterpret_cast<float*>(smem + k2e::kVec);  // b_g | u | v | ln_w | ln_b
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int j0 = blockIdx.x * 128, r = blockIdx.y, b = blockIdx.z;
+  K2eBars* bars = reinterpret_cast<K2eBars*>(smem + k2e::kBar);
+  CtaGuard* guard = &bars->guard;
+  float* svec = reinterpret_cast<float*>(smem + k2e::kVec);  // b_g | u | v
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   if (tid == 0) {
     guard->abort = 0;
-    mbar_init(lbar, 1);
-    mbar_init(mbar, 1);
+    mbar_init(&bars->wbar, 1);
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(&bars->a_full[x], 128);
+      mbar_init(&bars->a_empty[x], 1);
+      mbar_init(&bars->x_full[x], 1);
+      mbar_init(&bars->x_empty[x], 1 + 128);  // MMA commit + epilogue threads (statistics)
+      mbar_init(&bars->d_full[x], 1);
+      mbar_init(&bars->d_empty[x], 128);
+    }
+    mbar_init(&bars->drain, 1);
     fence_barrier_init();
   }
-  if (warp == 0) {
-    tmem_alloc(tslot, 256);
+  if (tid < 128) {
+    svec[tid] = vec[tmpack::kVBg + tid];
+    svec[128 + tid] = vec[tmpack::kVU + tid];
+    svec[256 + tid] = vec[tmpack::kVV + tid];
+  }
+  if (warp == 8) {
+    tmem_alloc(&bars->tslot, 512);
     tmem_relinquish();
   }
-  svec[tid] = vec[tmpack::kVBg + tid];
-  svec[128 + tid] = vec[tmpack::kVU + tid];
-  svec[256 + tid] = vec[tmpack::kVV + tid];
-  svec[384 + tid] = vec[tmpack::kVLnW + tid];
-  svec[512 + tid] = vec[tmpack::kVLnB + tid];
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tslot;
+  const uint32_t tmem = bars->tslot;
 
-  if (tid == 0) {
-    mbar_arrive_expect_tx(lbar, 65536 + 65536 + 32768);
+  if (warp < 4) {
+    // ------------------------- LayerNorm producers -------------------------
+    const float4 gw = reinterpret_cast<const float4*>(vec + tmpack::kVLnW)[lane];
+    const float4 gb = reinterpret_cast<const float4*>(vec + tmpack::kVLnB)[lane];
+    int it = 0;
+    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+      const int s = it & 1;
+      const int jt = tile % n_jt, rb = tile / n_jt;
+      const int r = rb % rows, b = rb / rows, j0 = jt * 128;
+      if (it >= 2) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&bars->a_empty[s], ((it >> 1) - 1) & 1, guard, status,
+                                               kStatusTimeoutProducer)))
+          break;
+      }
+      const size_t rowbase = (static_cast<size_t>(b) * rows + r) * N;
+      float4 v[32];
 #pragma unroll
-    for (int kh = 0; kh < 2; ++kh) tma_load_2d(smem + k2e::kW + kh * 32768, &w_map, lbar, kh * 64, 0);
+      for (int k = 0; k < 32; ++k) {
+        const int j = j0 + warp * 32 + k;
+        v[k] = j < N ? __ldg(reinterpret_cast<const float4*>(z + (rowbase + j) * 128) + lane)
+                     : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      uint8_t* at = smem + k2e::kA + s * 32768 + (lane >> 4) * 16384;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) tma_load_4d(smem + k2e::kZ + q * 16384, &z_map, lbar, q * 32, j0, r, b);
-#pragma unroll
-    for (int h = 0; h < 2; ++h) tma_load_4d(smem + k2e::kX + h * 16384, &x_map, lbar, j0 + h * 64, 0, r, b);
-  }
-  const int p = tid;
-  float mu_x = 0.f, rstd_x = 0.f;
-  if (mbar_wait(lbar, 0, guard, status, kStatusTimeoutConsumer)) {
-    ln_row_to_operand(smem + k2e::kZ, smem + k2e::kA, p, svec + 384, svec + 512);
-    // LN_out statistics over the 128 channels of pair p, read from the [c][j] x tile.
-    const uint8_t* xb = smem + k2e::kX + (p >> 6) * 16384;
-    const int pj = p & 63;
-    float s = 0.f;
-#pragma unroll 8
-    for (int c = 0; c < 128; ++c) {
-      const uint16_t bits = *reinterpret_cast<const uint16_t*>(xb + swz128(c, pj >> 3) + (pj & 7) * 2);
-      s += __half2float(__ushort_as_half(bits));
+      for (int k = 0; k < 32; ++k) {
+        const float mean = warp_sum((v[k].x + v[k].y) + (v[k].z + v[k].w)) * (1.f / 128.f);
+        const float dx = v[k].x - mean, dy = v[k].y - mean, dz = v[k].z - mean, dw = v[k].w - mean;
+        const float var = warp_sum((dx * dx + dy * dy) + (dz * dz + dw * dw)) * (1.f / 128.f);
+        const float rstd = rsqrtf(var + 1e-5f);
+        uint2 o;
+        o.x = pack_f16x2(dx * rstd * gw.x + gb.x, dy * rstd * gw.y + gb.y);
+        o.y = pack_f16x2(dz * rstd * gw.z + gb.z, dw * rstd * gw.w + gb.w);
+        *reinterpret_cast<uint2*>(at + swz128(warp * 32 + k, (lane & 15) >> 1) + (lane & 1) * 8) = o;
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&bars->a_full[s]);
     }
-    mu_x = s * (1.f / 128.f);
-    float ss = 0.f;
-#pragma unroll 8
-    for (int c = 0; c < 128; ++c) {
-      const uint16_t bits = *reinterpret_cast<const uint16_t*>(xb + swz128(c, pj >> 3) + (pj & 7) * 2);
-      const float d = __half2float(__ushort_as_half(bits)) - mu_x;
-      ss += d * d;
-    }
-    // x is stored scaled by x_scale; LN(x) = LN_eps*s^2(x * s), so the eps scales with it.
-    rstd_x = rsqrtf(ss * (1.f / 128.f) + 1e-5f * x_scale * x_scale);
-  }
-  fence_proxy_async_smem();
-  __syncthreads();
-  if (tid == 0 && !guard->abort) {
-    tc_fence_after();
-    const uint32_t a0 = smem_u32(smem + k2e::kA), w0 = smem_u32(smem + k2e::kW), x0 = smem_u32(smem + k2e::kX);
-    const uint32_t id_g = make_idesc_f16(128, 128, 0, 0);
-    const uint32_t id_u = make_idesc_f16(128, 128, 1, 0);
+  } else if (warp == 8) {
+    // ------------------------------ MMA issuer ------------------------------
+    if (lane == 0) {
+      bool ok = mbar_wait(&bars->wbar, 0, guard, status, kStatusTimeoutMma);
+      const uint32_t id_g = make_idesc_f16(128, 128, 0, 0);
+      const uint32_t id_u = make_idesc_f16(128, 128, 1, 0);
+      const uint32_t w0 = smem_u32(smem + k2e::kW);
+      int it = 0;
+      for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++it) {
+        const int s = it & 1;
+        ok = mbar_wait(&bars->a_full[s], (it >> 1) & 1, guard, status, kStatusTimeoutMma);
+        ok = ok && mbar_wait(&bars->x_full[s], (it >> 1) & 1, guard, status, kStatusTimeoutMma);
+        if (ok && it >= 2) ok = mbar_wait(&bars->d_empty[s], ((it >> 1) - 1) & 1, guard, status, kStatusTimeoutMma);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(smem + k2e::kA + s * 32768), x0 = smem_u32(smem + k2e::kX + s * 32768);
+        const uint32_t d = tmem + s * 256;
 #pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      const int kh = ks >> 2, kin = ks & 3;
-      umma_ss(tmem, make_sdesc(a0 + kh * 16384 + kin * 32, 16, 1024, Swz::k128),
-              make_sdesc(w0 + kh * 32768 + kin * 32, 16, 1024, Swz::k128), id_g, ks > 0 ? 1u : 0u);
-    }
-#pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      const int kh = ks >> 2, kin = ks & 3;
-      umma_ss(tmem + 128, make_sdesc(x0 + ks * 2048, 16384, 1024, Swz::k128),
-              make_sdesc(w0 + kh * 32768 + 16384 + kin * 32, 16, 1024, Swz::k128), id_u, ks > 0 ? 1u : 0u);
-    }
-    umma_commit(mbar);
-  }
-  const bool ok = __all_sync(0xffffffffu, mbar_wait(mbar, 0, guard, status, kStatusTimeoutConsumer));
-  tc_fence_after();
-  if (ok) {
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-#pragma unroll 1
-    for (int cc = 0; cc < 4; ++cc) {
-      uint32_t g[32], u[32];
-      tmem_ld32(tmem + lane_base + cc * 32, g);
-      tmem_ld32(tmem + lane_base + 128 + cc * 32, u);
-      tmem_wait_ld();
-      uint8_t* zq = smem + k2e::kZ + cc * 16384;  // channels cc*32 .. cc*32+31
-#pragma unroll
-      for (int ch = 0; ch < 8; ++ch) {
-        float4 zv = lds_f4(zq + swz128(p, ch));
-        float res[4] = {zv.x, zv.y, zv.z, zv.w};
-        float o[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int t = ch * 4 + e, n = cc * 32 + t;
-          const float gate = sigmoidf_fast(__uint_as_float(g[t]) + svec[n]);
-          const float y = (rstd_x * (__uint_as_float(u[t]) - mu_x * svec[128 + n]) + svec[256 + n]) * gate;
-          o[e] = add_residual ? y + res[e] : y;
+        for (int ks = 0; ks < 8; ++ks) {
+          const int kh = ks >> 2, kin = ks & 3;
+          umma_ss(d, make_sdesc(a0 + kh * 16384 + kin * 32, 16, 1024, Swz::k128),
+                  make_sdesc(w0 + kh * 32768 + kin * 32, 16, 1024, Swz::k128), id_g, ks > 0 ? 1u : 0u);
         }
-        *reinterpret_cast<float4*>(zq + swz128(p, ch)) = make_float4(o[0], o[1], o[2], o[3]);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const int kh = ks >> 2, kin = ks & 3;
+          umma_ss(d + 128, make_sdesc(x0 + ks * 2048, 16384, 1024, Swz::k128),
+                  make_sdesc(w0 + kh * 32768 + 16384 + kin * 32, 16, 1024, Swz::k128), id_u, ks > 0 ? 1u : 0u);
+        }
+        umma_commit(&bars->d_full[s]);
+        umma_commit(&bars->a_empty[s]);
+        umma_commit(&bars->x_empty[s]);
+      }
+      if (!ok) {
+        umma_commit(&bars->drain);
+        mbar_wait_drain(&bars->drain, 0);
       }
     }
-  }
-  fence_proxy_async_smem();
-  __syncthreads();
-  if (tid == 0) {
-    if (ok && !guard->abort) {
+  } else if (warp == 9) {
+    // ------------------------------ TMA producer ------------------------------
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&bars->wbar, 65536);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) tma_store_4d(&out_map, smem + k2e::kZ + q * 16384, q * 32, j0, r, b);
-      tma_store_commit();
-      tma_store_wait_read();
-    } else {
-      mbar_wait_drain(lbar, 0);
+      for (int kh = 0; kh < 2; ++kh) tma_load_2d(smem + k2e::kW + kh * 32768, &w_map, &bars->wbar, kh * 64, 0);
+      bool ok = true;
+      int it = 0, issued = 0;
+      for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+        const int s = it & 1;
+        const int jt = tile % n_jt, rb = tile / n_jt;
+        const int r = rb % rows, b = rb / rows, j0 = jt * 128;
+        if (it >= 2 && !mbar_wait(&bars->x_empty[s], ((it >> 1) - 1) & 1, guard, status, kStatusTimeoutProducer)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&bars->x_full[s], 32768);
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh)
+          tma_load_4d(smem + k2e::kX + s * 32768 + hh * 16384, &x_map, &bars->x_full[s], j0 + hh * 64, 0, r, b);
+        ++issued;
+      }
+      if (!ok) {
+        for (int t = (issued > 2 ? issued - 2 : 0); t < issued; ++t) mbar_wait_drain(&bars->x_full[t & 1], (t >> 1) & 1);
+      }
+      mbar_wait_drain(&bars->wbar, 0);
     }
+  } else {
+    // ------------------------- epilogue: thread = pair -------------------------
+    const int q4 = warp & 3;
+    const int p = q4 * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
+    const bool issuer = (warp == 4 && lane == 0);
+    int it = 0;
+    int slab = 0;  // running slab counter (slab buffer = slab & 1)
+    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+      const int s = it & 1;
+      const int jt = tile % n_jt, rb = tile / n_jt;
+      const int r = rb % rows, b = rb / rows, j0 = jt * 128;
+      bool w = mbar_wait(&bars->x_full[s], (it >> 1) & 1, guard, status, kStatusTimeoutConsumer);
+      w = w && mbar_wait(&bars->d_full[s], (it >> 1) & 1, guard, status, kStatusTimeoutConsumer);
+      if (!__all_sync(0xffffffffu, w)) break;
+      // LN_out statistics over the 128 channels of pair p (x is stored times x_scale)
+      const uint8_t* xb = smem + k2e::kX + s * 32768 + (p >> 6) * 16384;
+      const int pj = p & 63;
+      const float x0 = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(xb + swz128(0, pj >> 3) + (pj & 7) * 2)));
+      float s1 = 0.f, s2 = 0.f;
+#pragma unroll 16
+      for (int c = 0; c < 128; ++c) {
+        const float xv = __half2float(
+                             __ushort_as_half(*reinterpret_cast<const uint16_t*>(xb + swz128(c, pj >> 3) + (pj & 7) * 2))) -
+                         x0;
+        s1 += xv;
+        s2 += xv * xv;
+      }
+      mbar_arrive(&bars->x_empty[s]);
+      const float d1 = s1 * (1.f / 128.f);
+      const float mu_x = x0 + d1;
+      const float var = fmaxf(s2 * (1.f / 128.f) - d1 * d1, 0.f);
+      const float rstd_x = rsqrtf(var + 1e-5f * x_scale * x_scale);
+      tc_fence_after();
+      const size_t pair = (static_cast<size_t>(b) * rows + r) * N + j0 + p;
+      const bool valid = j0 + p < N;
+#pragma unroll 1
+      for (int cc = 0; cc < 4; ++cc, ++slab) {
+        uint32_t g[32], u[32];
+        tmem_ld32(tmem + lane_off + s * 256 + cc * 32, g);
+        tmem_ld32(tmem + lane_off + s * 256 + 128 + cc * 32, u);
+        float4 res[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          res[q] = (add_residual && valid) ? __ldg(reinterpret_cast<const float4*>(z + pair * 128 + cc * 32) + q)
+                                           : make_float4(0.f, 0.f, 0.f, 0.f);
+        tmem_wait_ld();
+        // the slab buffer used two slabs ago must have been read by its TMA store
+        if (issuer) tma_store_wait_read_le1();
+        named_bar_sync(1, 128);
+        uint8_t* ob = smem + k2e::kO + (slab & 1) * 16384;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          float o[4];
+          const float rq[4] = {res[q].x, res[q].y, res[q].z, res[q].w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int t = q * 4 + e, n = cc * 32 + t;
+            const float gate = sigmoid_tanh(__uint_as_float(g[t]) + svec[n]);
+            o[e] = (rstd_x * (__uint_as_float(u[t]) - mu_x * svec[128 + n]) + svec[256 + n]) * gate + rq[e];
+          }
+          *reinterpret_cast<float4*>(ob + swz128(p, q)) = make_float4(o[0], o[1], o[2], o[3]);
+        }
+        fence_proxy_async_smem();
+        named_bar_sync(1, 128);
+        if (issuer) {
+          tma_store_4d(&out_map, ob, cc * 32, j0, r, b);
+          tma_store_commit();
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&bars->d_empty[s]);
+    }
+    if (issuer) tma_store_wait_all();
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == 8) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 512);
   }
 }
 
 // ----------------------------------------------------------------------------------
 // Host side
 // ----------------------------------------------------------------------------------
-
 }  // namespace gtk
 
 using namespace gtk;
@@ -681,21 +797,25 @@ int gtk_trimul_finish(const float* z, const void* x_planes, int64_t ldx, float x
   if (!dims_ok(B, 65535) || !dims_ok(rows, 65535) || !dims_ok(N, 1 << 20))
     return fail(GTK_ERR_INVALID_ARG, "trimul_finish: bad B/rows/N");
   if (ldx < N || ldx % 8) return fail(GTK_ERR_INVALID_ARG, "trimul_finish: bad plane pitch");
+  if (!(x_scale > 0.f)) return fail(GTK_ERR_INVALID_ARG, "trimul_finish: x_scale must be positive");
   if (int e = check_ptr(z, "z")) return e;
   if (int e = check_ptr(out, "out")) return e;
   if (int e = check_ptr(x_planes, "x_planes")) return e;
   if (int e = check_ptr(packed, "packed", 256)) return e;
   if (int e = check_device()) return e;
   const uint8_t* pk = static_cast<const uint8_t*>(packed);
-  CUtensorMap zm, wm, xm, om;
-  if (int e = make_pair_map(&zm, z, B, rows, N, false)) return e;
+  const int64_t n_jt = (N + 127) / 128;
+  const int64_t n_tiles = B * rows * n_jt;
+  if (n_tiles > 2147483647) return fail(GTK_ERR_INVALID_ARG, "trimul_finish: too many tiles");
+  CUtensorMap wm, xm, om;
   if (int e = make_weight_map(&wm, pk + tmpack::kW2, 256, 256)) return e;
   if (int e = make_plane_map(&xm, x_planes, B, rows, 128, N, ldx, 64, 128, 1, 128)) return e;
   if (int e = make_pair_map(&om, out, B, rows, N, false)) return e;
   if (int e = ensure_smem(reinterpret_cast<const void*>(trimul_finish_kernel), k2e::kSmem)) return e;
-  dim3 grid(static_cast<unsigned>((N + 127) / 128), static_cast<unsigned>(rows), static_cast<unsigned>(B));
-  trimul_finish_kernel<<<grid, 128, k2e::kSmem, static_cast<cudaStream_t>(stream)>>>(
-      zm, wm, xm, om, reinterpret_cast<const float*>(pk + tmpack::kVec), add_residual, x_scale, status);
+  const int grid = static_cast<int>(n_tiles < num_sms() ? n_tiles : num_sms());
+  trimul_finish_kernel<<<grid, k2e::kThreads, k2e::kSmem, static_cast<cudaStream_t>(stream)>>>(
+      wm, xm, om, z, reinterpret_cast<const float*>(pk + tmpack::kVec), add_residual, x_scale, static_cast<int>(N),
+      static_cast<int>(rows), static_cast<int>(n_jt), static_cast<int>(n_tiles), status);
   return check_launch("trimul_finish_kernel");
 }
 
