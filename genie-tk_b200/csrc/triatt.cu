@@ -738,17 +738,21 @@ __global__ void __launch_bounds__(k4::kThreads, 1)
 
 // ----------------------------------------------------------------------------------
 // K4e: persistent update = og W_o^T + b_o (+ residual), written through the (possibly
-// transposed) pair descriptor. Tile = 128 pairs of row i of the problem. 192 threads:
-//   warps 0-3  epilogue: thread = pair (TMEM lane); bias, residual, 32-channel fp32 slabs
-//              staged in shared memory and written with TMA stores (2 slab buffers);
-//   warp 4     lane 0: TMA producer (W_o once, og tiles double buffered);
+// transposed) pair descriptor. Tile = 128 pairs of row i of the problem; each tile is
+// handled as four 32-channel fp32 slabs [128 pairs][32] that travel through a ring of
+// four shared-memory buffers: the producer TMA-loads the residual slab of z into a
+// buffer, the epilogue adds the accumulator and bias in place, and a TMA store writes it
+// out, so every global access is a bulk tensor copy. 192 threads:
+//   warps 0-3  epilogue: thread = pair (TMEM lane);
+//   warp 4     lane 0: TMA producer (W_o once, og tiles double buffered, z slabs);
 //   warp 5     lane 0: MMA issuer (TMEM double buffered, 128 columns per tile).
-// Shared memory: W4 32 KB | og 2 x 32 KB | out slabs 2 x 16 KB | b_o | barriers.
+// Shared memory: W4 32 KB | og 2 x 32 KB | slabs 4 x 16 KB | b_o | barriers.
 // ----------------------------------------------------------------------------------
 namespace k4e {
 constexpr int kThreads = 192;
-constexpr uint32_t kW = 0, kA = 32768, kO = 98304, kVec = 131072, kBar = 131072 + 512;
-constexpr uint32_t kSmem = kBar + 128 + 1024;
+constexpr int kSlabs = 4;
+constexpr uint32_t kW = 0, kA = 32768, kO = 98304, kVec = 98304 + kSlabs * 16384, kBar = kVec + 512;
+constexpr uint32_t kSmem = kBar + 256 + 1024;
 static_assert(kSmem <= 232448, "K4e shared memory");
 }  // namespace k4e
 
@@ -756,11 +760,12 @@ struct K4eBars {
   uint64_t wbar;
   uint64_t a_full[2], a_empty[2];
   uint64_t d_full[2], d_empty[2];
+  uint64_t o_full[k4e::kSlabs], o_empty[k4e::kSlabs];
   uint64_t drain;
   uint32_t tslot;
   CtaGuard guard;
 };
-static_assert(sizeof(K4eBars) <= 128, "K4e barrier block");
+static_assert(sizeof(K4eBars) <= 256, "K4e barrier block");
 
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
@@ -768,14 +773,15 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
 
 __global__ void __launch_bounds__(k4e::kThreads, 1)
     triatt_finish_kernel(const __grid_constant__ CUtensorMap og_map, const __grid_constant__ CUtensorMap w_map,
-                         const __grid_constant__ CUtensorMap out_map, const float* __restrict__ z, int starting,
+                         const __grid_constant__ CUtensorMap z_map, const __grid_constant__ CUtensorMap out_map,
                          const float* __restrict__ vec, int N, int add_residual, int n_jt, int n_tiles,
                          uint32_t* status) {
+  using namespace k4e;
   extern __shared__ uint8_t dsmem[];
   uint8_t* smem = align1024(dsmem);
-  K4eBars* bars = reinterpret_cast<K4eBars*>(smem + k4e::kBar);
+  K4eBars* bars = reinterpret_cast<K4eBars*>(smem + kBar);
   CtaGuard* guard = &bars->guard;
-  float* sbo = reinterpret_cast<float*>(smem + k4e::kVec);
+  float* sbo = reinterpret_cast<float*>(smem + kVec);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   if (tid == 0) {
@@ -786,6 +792,10 @@ __global__ void __launch_bounds__(k4e::kThreads, 1)
       mbar_init(&bars->a_empty[x], 1);
       mbar_init(&bars->d_full[x], 1);
       mbar_init(&bars->d_empty[x], 128);
+    }
+    for (int x = 0; x < kSlabs; ++x) {
+      mbar_init(&bars->o_full[x], 1);
+      mbar_init(&bars->o_empty[x], 1);
     }
     mbar_init(&bars->drain, 1);
     fence_barrier_init();
@@ -805,12 +815,13 @@ __global__ void __launch_bounds__(k4e::kThreads, 1)
     if (lane == 0) {
       mbar_arrive_expect_tx(&bars->wbar, 32768);
 #pragma unroll
-      for (int kh = 0; kh < 2; ++kh) tma_load_2d(smem + k4e::kW + kh * 16384, &w_map, &bars->wbar, kh * 64, 0);
+      for (int kh = 0; kh < 2; ++kh) tma_load_2d(smem + kW + kh * 16384, &w_map, &bars->wbar, kh * 64, 0);
       bool ok = true;
-      int it = 0, issued = 0;
-      for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+      int it = 0, issued_a = 0, slab = 0;
+      for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++it) {
         const int s = it & 1;
         const int jt = tile % n_jt, bi = tile / n_jt;
+        const int i = bi % N, b = bi / N, j0 = jt * 128;
         if (it >= 2 && !mbar_wait(&bars->a_empty[s], ((it >> 1) - 1) & 1, guard, status, kStatusTimeoutProducer)) {
           ok = false;
           break;
@@ -818,11 +829,28 @@ __global__ void __launch_bounds__(k4e::kThreads, 1)
         mbar_arrive_expect_tx(&bars->a_full[s], 32768);
 #pragma unroll
         for (int kh = 0; kh < 2; ++kh)
-          tma_load_3d(smem + k4e::kA + s * 32768 + kh * 16384, &og_map, &bars->a_full[s], kh * 64, jt * 128, bi);
-        ++issued;
+          tma_load_3d(smem + kA + s * 32768 + kh * 16384, &og_map, &bars->a_full[s], kh * 64, jt * 128, bi);
+        ++issued_a;
+        for (int cc = 0; cc < 4; ++cc, ++slab) {
+          const int sl = slab % kSlabs;
+          if (slab >= kSlabs && !mbar_wait(&bars->o_empty[sl], ((slab / kSlabs) - 1) & 1, guard, status,
+                                           kStatusTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          if (add_residual) {
+            mbar_arrive_expect_tx(&bars->o_full[sl], 16384);
+            tma_load_4d(smem + kO + sl * 16384, &z_map, &bars->o_full[sl], cc * 32, j0, i, b);
+          } else {
+            mbar_arrive(&bars->o_full[sl]);
+          }
+        }
       }
       if (!ok) {
-        for (int t = (issued > 2 ? issued - 2 : 0); t < issued; ++t) mbar_wait_drain(&bars->a_full[t & 1], (t >> 1) & 1);
+        for (int t = (issued_a > 2 ? issued_a - 2 : 0); t < issued_a; ++t)
+          mbar_wait_drain(&bars->a_full[t & 1], (t >> 1) & 1);
+        for (int t = (slab > kSlabs ? slab - kSlabs : 0); t < slab; ++t)
+          mbar_wait_drain(&bars->o_full[t % kSlabs], (t / kSlabs) & 1);
       }
       mbar_wait_drain(&bars->wbar, 0);
     }
@@ -831,7 +859,7 @@ __global__ void __launch_bounds__(k4e::kThreads, 1)
     if (lane == 0) {
       bool ok = mbar_wait(&bars->wbar, 0, guard, status, kStatusTimeoutMma);
       const uint32_t idesc = make_idesc_f16(128, 128, 0, 0);
-      const uint32_t w0 = smem_u32(smem + k4e::kW);
+      const uint32_t w0 = smem_u32(smem + kW);
       int it = 0;
       for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++it) {
         const int s = it & 1;
@@ -839,7 +867,7 @@ __global__ void __launch_bounds__(k4e::kThreads, 1)
         if (ok && it >= 2) ok = mbar_wait(&bars->d_empty[s], ((it >> 1) - 1) & 1, guard, status, kStatusTimeoutMma);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t a0 = smem_u32(smem + k4e::kA + s * 32768);
+        const uint32_t a0 = smem_u32(smem + kA + s * 32768);
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
           const int kh = ks >> 2, kin = ks & 3;
@@ -860,37 +888,36 @@ __global__ void __launch_bounds__(k4e::kThreads, 1)
     const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
     const bool issuer = (tid == 0);
     int it = 0, slab = 0;
-    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++it) {
       const int s = it & 1;
       const int jt = tile % n_jt, bi = tile / n_jt;
       const int i = bi % N, b = bi / N, j0 = jt * 128;
-      if (!__all_sync(0xffffffffu, mbar_wait(&bars->d_full[s], (it >> 1) & 1, guard, status, kStatusTimeoutConsumer)))
-        break;
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars->d_full[s], (it >> 1) & 1, guard, status, kStatusTimeoutConsumer));
+      if (!ok) break;
       tc_fence_after();
-      const int j = j0 + p;
-      const bool valid = j < N;
-      const size_t zpair = starting ? (static_cast<size_t>(b) * N + i) * N + j : (static_cast<size_t>(b) * N + j) * N + i;
 #pragma unroll 1
       for (int cc = 0; cc < 4; ++cc, ++slab) {
+        const int sl = slab % kSlabs;
         uint32_t d[32];
         tmem_ld32(tmem + lane_off + s * 128 + cc * 32, d);
-        float4 res[8];
-#pragma unroll
-        for (int q = 0; q < 8; ++q)
-          res[q] = (add_residual && valid) ? __ldg(reinterpret_cast<const float4*>(z + zpair * 128 + cc * 32) + q)
-                                           : make_float4(0.f, 0.f, 0.f, 0.f);
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars->o_full[sl], (slab / kSlabs) & 1, guard, status,
+                                               kStatusTimeoutConsumer));
         tmem_wait_ld();
-        if (issuer) tma_store_wait_read_le1();
-        named_bar_sync(1, 128);
-        uint8_t* ob = smem + k4e::kO + (slab & 1) * 16384;
+        if (!ok) break;
+        uint8_t* ob = smem + kO + sl * 16384;
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
           const int n = cc * 32 + q * 4;
-          float4 o;
-          o.x = __uint_as_float(d[q * 4 + 0]) + sbo[n + 0] + res[q].x;
-          o.y = __uint_as_float(d[q * 4 + 1]) + sbo[n + 1] + res[q].y;
-          o.z = __uint_as_float(d[q * 4 + 2]) + sbo[n + 2] + res[q].z;
-          o.w = __uint_as_float(d[q * 4 + 3]) + sbo[n + 3] + res[q].w;
+          float4 o = make_float4(__uint_as_float(d[q * 4 + 0]) + sbo[n + 0], __uint_as_float(d[q * 4 + 1]) + sbo[n + 1],
+                                 __uint_as_float(d[q * 4 + 2]) + sbo[n + 2], __uint_as_float(d[q * 4 + 3]) + sbo[n + 3]);
+          if (add_residual) {
+            const float4 zv = lds_f4(ob + swz128(p, q));
+            o.x += zv.x;
+            o.y += zv.y;
+            o.z += zv.z;
+            o.w += zv.w;
+          }
           *reinterpret_cast<float4*>(ob + swz128(p, q)) = o;
         }
         fence_proxy_async_smem();
@@ -898,12 +925,18 @@ __global__ void __launch_bounds__(k4e::kThreads, 1)
         if (issuer) {
           tma_store_4d(&out_map, ob, cc * 32, j0, i, b);
           tma_store_commit();
+          // a slab buffer is free again once its store has read it; keep two stores in flight
+          tma_store_wait_read_le1();
+          if (slab >= 1) mbar_arrive(&bars->o_empty[(slab - 1) % kSlabs]);
         }
       }
       tc_fence_before();
       mbar_arrive(&bars->d_empty[s]);
     }
-    if (issuer) tma_store_wait_all();
+    if (issuer) {
+      tma_store_wait_all();
+      if (ok && slab >= 1) mbar_arrive(&bars->o_empty[(slab - 1) % kSlabs]);
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -1088,14 +1121,15 @@ int gtk_triatt_finish(int starting, const float* z, const void* packed, void* wo
   const int64_t n_jt = (N + 127) / 128;
   const int64_t n_tiles = B * N * n_jt;
   if (n_tiles > 2147483647) return fail(GTK_ERR_INVALID_ARG, "triatt_finish: too many tiles");
-  CUtensorMap am, wm, om;
+  CUtensorMap am, wm, zm, om;
   if (int e = make_hidden_map(&am, ws + w.og, B, N)) return e;
   if (int e = make_weight_map(&wm, pk + tapack::kW4, 128, 128)) return e;
+  if (int e = make_pair_map(&zm, add_residual ? z : out, B, N, N, !starting)) return e;
   if (int e = make_pair_map(&om, out, B, N, N, !starting)) return e;
   if (int e = ensure_smem(reinterpret_cast<const void*>(triatt_finish_kernel), k4e::kSmem)) return e;
   const int grid = static_cast<int>(n_tiles < num_sms() ? n_tiles : num_sms());
   triatt_finish_kernel<<<grid, k4e::kThreads, k4e::kSmem, static_cast<cudaStream_t>(stream)>>>(
-      am, wm, om, z, starting, reinterpret_cast<const float*>(pk + tapack::kVec), static_cast<int>(N), add_residual,
+      am, wm, zm, om, reinterpret_cast<const float*>(pk + tapack::kVec), static_cast<int>(N), add_residual,
       static_cast<int>(n_jt), static_cast<int>(n_tiles), status);
   return check_launch("triatt_finish_kernel");
 }
