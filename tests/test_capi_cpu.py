@@ -1,0 +1,95 @@
+"""CPU checks of the C ABI library: it loads, exports every symbol the public header
+declares, and its host-only entry points (sizes, layouts, argument validation) behave.
+No kernel is launched here."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(REPO, "include", "genie_tk_b200.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"GTK_API\s+[\w\s\*]+?\b(gtk_\w+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    import genie_tk._lib as L
+    if not os.path.exists(L.LIB_PATH):
+        import __graft_entry__ as g
+        g.build()
+    return L.load()
+
+
+def test_header_declares_entry_points():
+    syms = declared_symbols()
+    for name in ("gtk_trimul_forward", "gtk_triatt_forward", "gtk_trimul_contract", "gtk_triatt_core",
+                 "gtk_last_error_string", "gtk_version"):
+        assert name in syms
+
+
+def test_library_exports_every_declared_symbol(lib):
+    missing = [s for s in declared_symbols() if getattr(lib, s, None) is None]
+    assert not missing, missing
+
+
+def test_every_declared_symbol_has_a_ctypes_signature():
+    import genie_tk._lib as L
+    missing = [s for s in declared_symbols() if s not in L.exported_names()]
+    assert not missing, missing
+
+
+def test_host_queries(lib):
+    assert lib.gtk_version() >= 100
+    assert lib.gtk_trimul_packed_bytes(128, 128) > 0
+    assert lib.gtk_trimul_packed_bytes(64, 128) == 0
+    assert lib.gtk_triatt_packed_bytes(128, 128, 4) > 0
+    assert lib.gtk_triatt_packed_bytes(128, 32, 4) == 0
+    assert [lib.gtk_plane_pitch(n) for n in (1, 8, 10, 1024)] == [8, 8, 16, 1024]
+    w1 = lib.gtk_trimul_workspace_bytes(1, 100, 128, 128)
+    w2 = lib.gtk_trimul_workspace_bytes(1, 200, 128, 128)
+    assert 0 < w1 < w2 and w1 % 256 == 0
+    assert lib.gtk_triatt_workspace_bytes(2, 64, 128, 128, 4) > lib.gtk_triatt_workspace_bytes(1, 64, 128, 128, 4)
+
+
+def test_triatt_workspace_layout(lib):
+    B, N = 2, 100
+    offs = (ctypes.c_int64 * 6)()
+    assert lib.gtk_triatt_workspace_offsets(B, N, offs) == 0
+    o = list(offs)
+    pair16 = B * N * N * 128 * 2
+    assert o[0] == 0 and all(x % 256 == 0 for x in o)
+    assert all(o[k + 1] - o[k] >= pair16 for k in range(5))
+    total = lib.gtk_triatt_workspace_bytes(B, N, 128, 128, 4)
+    assert total - o[5] >= B * 4 * N * lib.gtk_plane_pitch(N) * 2
+
+
+def test_unsupported_shapes_fail_before_touching_the_device(lib):
+    rc = lib.gtk_trimul_forward(1, None, None, None, None, 0, None, 0, 1, 16, 64, 128, None, None)
+    assert rc == -2
+    assert b"c_z" in lib.gtk_last_error_string()
+    rc = lib.gtk_triatt_forward(1, None, None, None, None, 0, None, 0, 1, 16, 128, 128, 8, 1e9, None, None)
+    assert rc == -2
+    assert b"heads" in lib.gtk_last_error_string()
+
+
+def test_invalid_arguments_are_rejected(lib):
+    # workspace too small is detected from the sizes alone
+    rc = lib.gtk_trimul_forward(1, None, None, None, None, 0, None, 0, 1, 16, 128, 128, None, None)
+    assert rc == -4
+    # a NULL pair tensor is rejected before any launch
+    rc = lib.gtk_trimul_project(None, None, None, None, None, 16, 1, 16, 16, None, None)
+    assert rc == -1
+    # pitches must be multiples of 8
+    rc = lib.gtk_trimul_contract(1, ctypes.c_void_p(256), ctypes.c_void_p(256), ctypes.c_void_p(256), 1, 1, 16, 16,
+                                 16, 12, 16, 16, 1.0, None, None)
+    assert rc == -3
+    # the contraction output scale must be positive for the finish stage
+    rc = lib.gtk_trimul_finish(ctypes.c_void_p(256), ctypes.c_void_p(256), 16, 0.0, ctypes.c_void_p(256),
+                               ctypes.c_void_p(256), 0, 1, 16, 16, None, None)
+    assert rc == -1
