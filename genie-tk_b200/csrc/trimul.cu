@@ -19,6 +19,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <mutex>
 #include <string>
 
 #include "gtk_host.h"
@@ -695,6 +696,36 @@ __global__ void __launch_bounds__(k2e::kThreads, 1)
 // ----------------------------------------------------------------------------------
 // Host side
 // ----------------------------------------------------------------------------------
+// ----------------------------------------------------------------------------------
+// Built-in scratch for gtk_trimul_forward_noalloc: room for the a, b and x planes of
+// one call (3 * B * N * round_up(N, 8) * 128 fp16 values). It is allocated once per GPU
+// when the library's kernels are first loaded there and lives until the process exits.
+// ----------------------------------------------------------------------------------
+constexpr size_t kNoAllocScratchBytes = size_t(24) << 20;
+static __device__ __align__(256) uint8_t g_trimul_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of the scratch array on the current device, looked up once per device.
+// Host code must not use the array's name as a device pointer: on the host it names a
+// shadow variable, not device memory.
+static int noalloc_scratch_address(void** out) {
+  static std::mutex mu;
+  static void* addr[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return fail(GTK_ERR_CUDA, "trimul_forward_noalloc: no usable current device");
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_trimul_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(GTK_ERR_CUDA, std::string("trimul_forward_noalloc: cudaGetSymbolAddress failed: ") +
+                                    cudaGetErrorString(e));
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return GTK_OK;
+}
+
 }  // namespace gtk
 
 using namespace gtk;
@@ -838,6 +869,25 @@ int gtk_trimul_forward(int outgoing, const float* z, const float* mask, const vo
   const float xs = 1.0f / static_cast<float>(N);
   if (int e = gtk_trimul_contract(outgoing, ap, bp, xp, B, 128, N, N, N, ld, ld, ld, xs, status, stream)) return e;
   return gtk_trimul_finish(z, xp, ld, xs, packed, out, add_residual, B, N, N, status, stream);
+}
+
+int gtk_trimul_forward_noalloc(int outgoing, const float* z, const float* mask, const void* packed, float* out,
+                               int add_residual, int64_t B, int64_t N, int c_z, int c_hidden, uint32_t* status,
+                               void* stream) {
+  if (c_z != 128 || c_hidden != 128)
+    return fail(GTK_ERR_UNSUPPORTED, "trimul: only c_z = c_hidden = 128 is implemented");
+  if (!dims_ok(B, 65535) || !dims_ok(N, 65535)) return fail(GTK_ERR_INVALID_ARG, "trimul: bad B/N");
+  const size_t need = gtk_trimul_workspace_bytes(B, N, c_z, c_hidden);
+  if (need > kNoAllocScratchBytes)
+    return fail(GTK_ERR_WORKSPACE, "trimul_forward_noalloc: B=" + std::to_string(B) + ", N=" + std::to_string(N) +
+                                       " needs " + std::to_string(need) + " bytes of scratch; the built-in scratch "
+                                       "holds " + std::to_string(kNoAllocScratchBytes) +
+                                       " (B * N * round_up(N, 8) <= 32768). Use gtk_trimul_forward with a "
+                                       "caller-provided workspace instead.");
+  void* scratch = nullptr;
+  if (int e = noalloc_scratch_address(&scratch)) return e;
+  return gtk_trimul_forward(outgoing, z, mask, packed, out, add_residual, scratch, kNoAllocScratchBytes, B, N, c_z,
+                            c_hidden, status, stream);
 }
 
 }  // extern "C"

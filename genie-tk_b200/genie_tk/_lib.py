@@ -48,6 +48,8 @@ _SIGNATURES = {
     "gtk_trimul_workspace_bytes": (c_size, [c_i64, c_i64, c_int, c_int]),
     "gtk_trimul_forward": (c_int, [c_int, c_vp, c_vp, c_vp, c_vp, c_int, c_vp, c_size, c_i64, c_i64, c_int, c_int,
                                    c_vp, c_vp]),
+    "gtk_trimul_forward_noalloc": (c_int, [c_int, c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_int, c_int, c_vp,
+                                           c_vp]),
     "gtk_trimul_project": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp]),
     "gtk_trimul_contract": (c_int, [c_int, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64,
                                     ctypes.c_float, c_vp, c_vp]),

@@ -108,6 +108,24 @@ GTK_API int gtk_trimul_forward(int outgoing, const float* z, const float* mask, 
                        int add_residual, void* workspace, size_t workspace_bytes, int64_t B, int64_t N, int c_z,
                        int c_hidden, uint32_t* status, void* stream);
 
+/* gtk_trimul_forward without a workspace argument, for callers that cannot allocate
+ * device memory: plugin hosts that own every device allocation and give their plugins no
+ * allocator, serving processes that run under a fixed memory budget, and latency paths
+ * that must not call cudaMalloc (it can synchronise the device). The library brings its
+ * own scratch: a 24 MiB array in device memory, created on every GPU that loads the
+ * library and kept until the process exits. It covers B * N * round_up(N, 8) <= 32768
+ * (for example B = 1, N <= 176, or B = 2, N = 128); larger sizes return
+ * GTK_ERR_WORKSPACE with a message naming the limit. Nothing in the scratch needs to
+ * start at zero: every byte a call reads was written earlier in the same call.
+ * The first call on a device looks up the scratch address on that device (the device
+ * must be current); make that first call before any stream capture. All calls share the
+ * one array, so calls whose work overlaps on the GPU (different streams, or different
+ * host threads without ordering) race on it: serialise them.
+ * No counterpart in the reference (its `_C` functions allocate their outputs). */
+GTK_API int gtk_trimul_forward_noalloc(int outgoing, const float* z, const float* mask, const void* packed,
+                                       float* out, int add_residual, int64_t B, int64_t N, int c_z, int c_hidden,
+                                       uint32_t* status, void* stream);
+
 /* Stage entry points (used by tests and by the multi-GPU driver).
  *
  * Plane buffers hold one fp16 N-wide row per (pair row, channel):
