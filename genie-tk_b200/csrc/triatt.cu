@@ -104,14 +104,15 @@ __device__ __forceinline__ float warp_sum4_transposed(float v0, float v1, float 
 // (b, row i of the problem, j0..j0+127); CTAs loop over tiles. 288 threads:
 //   warps 0-3  LayerNorm producers: warp per pair (coalesced 512-B loads of z, or of z^T
 //              for the ending node), fp16 operand A[s] (double buffered), and the four
-//              triangle-bias dot products of the fp32 LN output (stored as bf16, log2 e);
+//              triangle-bias dot products of the fp32 LN output (stored bf16, times log2 e);
 //   warp 8     lane 0: loads the 128 KB of weights once, then issues the MMAs;
 //   warps 4-7  epilogue: thread = pair (TMEM lane): q, k, v rows of 64 B per head and the
 //              sigmoid gate row of 256 B, written straight to global memory.
 // TMEM: half 0 = (q, k) columns 0-255, half 1 = (v, g) columns 256-511; the epilogue of
 // one half overlaps the MMAs of the other and the LayerNorm of the next tile.
 // Outputs: q, k, v fp16 [B*N(i)][H][N(j)][32]; g fp16 [B*N*N][128]; bias bf16
-// [B][H][N][ldn] (log2 units; bf16 so that the attention core widens it with shifts).
+// [B][H][N][ldn] (log2 units; bf16 keeps the attention core's shared-memory reads of the
+// bias tile at 256 B per query row and step, and widens with one integer op).
 // ----------------------------------------------------------------------------------
 namespace k3 {
 constexpr int kThreads = 288;
@@ -324,7 +325,7 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
 //   warps 0-3   softmax warpgroup 0 (rows r = 0, 2), warps 4-7 warpgroup 1 (r = 1, 3);
 //               thread = query row j of the tile; 224 registers each (setmaxnreg);
 //   warp 8      producer: TMA for Q (once), K, V (4-stage ring) and the bias tile
-//               (2 stages, shared by the kR rows); all lanes stage the mask bias of each
+//               (bf16, 2 stages, shared by the kR rows); all lanes stage the mask bias of each
 //               step plus a flag telling whether the step has any masked / absent key;
 //   warp 9      TMEM allocator + MMA issuer (lane 0); warps 10-11 only donate registers.
 // Step t = kt * kR + r handles key tile kt of row r and uses S/P buffer t & 1, so each
@@ -332,9 +333,10 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
 // its whole S row slice into registers at once and frees the buffer, so the tensor core
 // computes S(t+2) while the softmax of step t runs; the MMA issuer is a non-blocking
 // state machine that issues S up to two steps ahead of P V.
-// The softmax threads add the bf16 triangle bias row (widened by integer shifts) and, on
-// flagged steps, the mask bias, take the max, exponentiate (base 2; q and the bias carry
-// log2 e) and pack P. The tensor core only computes Q K^T and P V.
+// The softmax threads add the bf16 triangle bias row (widened by an integer shift) and, on
+// flagged steps, the mask bias,
+// take the max, exponentiate (base 2; q and the bias carry log2 e) and pack P. The tensor
+// core only computes Q K^T and P V.
 // TMEM columns: O_r at 32r (0-127), S at 128 + 128*sb, P (fp16 pairs) at 384 + 64*pb.
 // The running max is raised lazily (only when a tile's max exceeds it by > 8, in log2
 // units), so O is rescaled rarely; P then stays <= 2^8, well inside fp16.
@@ -348,15 +350,20 @@ constexpr int kThreads = 384;
 constexpr int kLaunchRegs = 168, kSoftmaxRegs = 224, kOtherRegs = 56;
 static_assert(256 * kSoftmaxRegs + 128 * kOtherRegs <= kThreads * kLaunchRegs, "register split");
 constexpr uint32_t kQ = 0;
-constexpr uint32_t kI = 32768;
-constexpr uint32_t kKV = 65536;
+constexpr uint32_t kKV = 32768;
 constexpr uint32_t kKVStage = 17408;  // K 8 KB | V 8 KB | mask bias 128 fp32 | flag
 constexpr uint32_t kMB = 16384, kFlag = 16896;
-constexpr uint32_t kBias = kKV + kKVS * kKVStage;
+constexpr uint32_t kBias = kKV + kKVS * kKVStage;  // bf16 bias tile [128 j][128 k] as 2 swizzled 64-key boxes
 constexpr uint32_t kBiasStage = 32768;
 constexpr uint32_t kBar = kBias + 2 * kBiasStage;
 constexpr uint32_t kSmem = kBar + 256 + 1024;
+static_assert(kSmem <= 232448, "K4 shared memory");
+static_assert(kBias % 1024 == 0, "bias stage alignment");
 constexpr float kLazy = 8.0f;
+// Every kPolyEvery-th pair of exponentials is evaluated on the FMA pipe (exp2_poly2); 0
+// disables it. Measured on B200 at N = 1024: one pair in three made the kernel 6% slower
+// (2.15 vs 2.03 ms), because the kernel is latency-bound rather than MUFU-bound.
+constexpr int kPolyEvery = 0;
 }  // namespace k4
 
 struct K4Bars {
@@ -388,6 +395,35 @@ __device__ __forceinline__ float2 add_f32x2(float2 a, float2 b) {
       : "=l"(reinterpret_cast<uint64_t&>(d))
       : "l"(reinterpret_cast<const uint64_t&>(a)), "l"(reinterpret_cast<const uint64_t&>(b)));
   return d;
+}
+
+__device__ __forceinline__ float2 fma_f32x2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;"
+      : "=l"(reinterpret_cast<uint64_t&>(d))
+      : "l"(reinterpret_cast<const uint64_t&>(a)), "l"(reinterpret_cast<const uint64_t&>(b)),
+        "l"(reinterpret_cast<const uint64_t&>(c)));
+  return d;
+}
+
+// 2^x for two values on the FMA/ALU pipes. Range reduction: adding 1.5 * 2^23 rounds x to
+// the nearest integer j (held in the low mantissa bits of t); f = x - j lies in
+// [-0.5, 0.5]; 2^f is a cubic fitted here to 2^f on that interval (near-minimax,
+// relative error 7.5e-5, below fp16 rounding of P); j is added to the exponent bits.
+// Inputs are clamped at -126 so the exponent field never underflows (results there
+// are ~1e-38, i.e. zero after the fp16 conversion of P).
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  x.x = fmaxf(x.x, -126.f);
+  x.y = fmaxf(x.y, -126.f);
+  const float2 t = add_f32x2(x, make_float2(kRound, kRound));
+  const float2 j = add_f32x2(t, make_float2(-kRound, -kRound));
+  const float2 f = fma_f32x2(j, make_float2(-1.f, -1.f), x);
+  float2 p = fma_f32x2(make_float2(0.0551716045f, 0.0551716045f), f, make_float2(0.242611117f, 0.242611117f));
+  p = fma_f32x2(p, f, make_float2(0.693260997f, 0.693260997f));
+  p = fma_f32x2(p, f, make_float2(0.999928074f, 0.999928074f));
+  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
 }
 
 template <int N>
@@ -652,8 +688,12 @@ __global__ void __launch_bounds__(k4::kThreads, 1)
 #pragma unroll
         for (int k2 = 0; k2 < 64; ++k2) {
           float2 x = add_f32x2(make_float2(__uint_as_float(sv[2 * k2]), __uint_as_float(sv[2 * k2 + 1])), negm);
-          x.x = ex2f(x.x);
-          x.y = ex2f(x.y);
+          if (kPolyEvery > 0 && k2 % kPolyEvery == kPolyEvery - 1) {
+            x = exp2_poly2(x);
+          } else {
+            x.x = ex2f(x.x);
+            x.y = ex2f(x.y);
+          }
           acc = add_f32x2(acc, x);
           __half2 hp = __floats2half2_rn(x.x, x.y);
           sv[k2] = *reinterpret_cast<uint32_t*>(&hp);

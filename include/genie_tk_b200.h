@@ -194,7 +194,7 @@ GTK_API int gtk_triatt_forward(int starting, const float* z, const float* mask, 
 /* Stage entry points over the forward workspace. offsets[6] receives the byte offsets of
  * q, k, v ([B*N][H][N][32] fp16, q scaled by log2(e)/sqrt(32)), g ([B*N*N][128] fp16,
  * sigmoid applied), og ([B*N*N][128] fp16, gated attention output) and the triangle bias
- * ([B][H][N][round_up(N,8)] fp16, in log2 units). All in the orientation of the problem
+ * ([B][H][N][round_up(N,8)] bf16, in log2 units). All in the orientation of the problem
  * (z^T for the ending node). */
 GTK_API int gtk_triatt_workspace_offsets(int64_t B, int64_t N, int64_t* offsets);
 GTK_API int gtk_triatt_project(int starting, const float* z, const void* packed, void* workspace, int64_t B,
