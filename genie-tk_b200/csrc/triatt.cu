@@ -102,28 +102,32 @@ __device__ __forceinline__ float warp_sum4_transposed(float v0, float v1, float 
 // ----------------------------------------------------------------------------------
 // K3: persistent LN + q/k/v/g projections + triangle bias. Tile = 128 consecutive pairs
 // (b, row i of the problem, j0..j0+127); CTAs loop over tiles. 288 threads:
-//   warps 0-3  LayerNorm producers: warp per pair (coalesced 512-B loads of z, or of z^T
-//              for the ending node), fp16 operand A[s] (double buffered), and the four
-//              triangle-bias dot products of the fp32 LN output (stored bf16, times log2 e);
-//   warp 8     lane 0: loads the 128 KB of weights once, then issues the MMAs;
+//   warp 8     lane 0: TMA producer and MMA issuer. The 128 KB of weights are loaded
+//              once; each tile's 128 x 128 fp32 z block (z^T for the ending node, through
+//              the transposed descriptor) arrives by TMA, 64 KB in flight per tile;
+//   warps 0-3  LayerNorm producers: warp per pair row, read from the staged z tile,
+//              write the fp16 operand A and the four triangle-bias dot products of the
+//              fp32 LN output (stored bf16, times log2 e);
 //   warps 4-7  epilogue: thread = pair (TMEM lane): q, k, v rows of 64 B per head and the
 //              sigmoid gate row of 256 B, written straight to global memory.
 // TMEM: half 0 = (q, k) columns 0-255, half 1 = (v, g) columns 256-511; the epilogue of
-// one half overlaps the MMAs of the other and the LayerNorm of the next tile.
+// one half overlaps the MMAs of the other; the next tile's z load overlaps both.
+// Shared memory: W3 128 KB | z 64 KB | A 32 KB | barriers.
 // Outputs: q, k, v fp16 [B*N(i)][H][N(j)][32]; g fp16 [B*N*N][128]; bias bf16
 // [B][H][N][ldn] (log2 units; bf16 keeps the attention core's shared-memory reads of the
 // bias tile at 256 B per query row and step, and widens with one integer op).
 // ----------------------------------------------------------------------------------
 namespace k3 {
 constexpr int kThreads = 288;
-constexpr uint32_t kW = 0, kA = 131072, kBar = 196608;
+constexpr uint32_t kW = 0, kZ = 131072, kA = 196608, kBar = 229376;
 constexpr uint32_t kSmem = kBar + 128 + 1024;
 static_assert(kSmem <= 232448, "K3 shared memory");
 }  // namespace k3
 
 struct K3Bars {
   uint64_t wbar;
-  uint64_t a_full[2], a_empty[2];
+  uint64_t z_full, z_empty;
+  uint64_t a_full, a_empty;
   uint64_t d_full[2], d_empty[2];
   uint64_t drain;
   uint32_t tslot;
@@ -132,7 +136,7 @@ struct K3Bars {
 static_assert(sizeof(K3Bars) <= 128, "K3 barrier block");
 
 __global__ void __launch_bounds__(k3::kThreads, 1)
-    triatt_project_kernel(const __grid_constant__ CUtensorMap w_map, const float* __restrict__ z, int starting,
+    triatt_project_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap z_map,
                           const float* __restrict__ vec, __half* __restrict__ q_out, __half* __restrict__ k_out,
                           __half* __restrict__ v_out, __half* __restrict__ g_out, __nv_bfloat16* __restrict__ bias,
                           int N, int ldn, int n_jt, int n_tiles, uint32_t* status) {
@@ -145,9 +149,11 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
   if (tid == 0) {
     guard->abort = 0;
     mbar_init(&bars->wbar, 1);
+    mbar_init(&bars->z_full, 1);
+    mbar_init(&bars->z_empty, 128);
+    mbar_init(&bars->a_full, 128);
+    mbar_init(&bars->a_empty, 1);
     for (int x = 0; x < 2; ++x) {
-      mbar_init(&bars->a_full[x], 128);
-      mbar_init(&bars->a_empty[x], 1);
       mbar_init(&bars->d_full[x], 1);
       mbar_init(&bars->d_empty[x], 128);
     }
@@ -170,69 +176,74 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
     float4 wb[kHeads];
 #pragma unroll
     for (int h = 0; h < kHeads; ++h) wb[h] = reinterpret_cast<const float4*>(vec + tapack::kVWb + h * 128)[lane];
+    // lane l holds channels 4l..4l+3: box l / 8 (32 channels each), 16-B chunk l % 8
+    const uint8_t* zsrc = smem + k3::kZ + (lane >> 3) * 16384;
+    uint8_t* at = smem + k3::kA + (lane >> 4) * 16384;
     int it = 0;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
-      const int s = it & 1;
-      const int jt = tile % n_jt, bi = tile / n_jt;  // bi = b * N + i
+      const int jt = tile % n_jt, bi = tile / n_jt;
       const int i = bi % N, b = bi / N, j0 = jt * 128;
-      if (it >= 2) {
-        if (!__all_sync(0xffffffffu, mbar_wait(&bars->a_empty[s], ((it >> 1) - 1) & 1, guard, status,
-                                               kStatusTimeoutProducer)))
-          break;
+      bool w = mbar_wait(&bars->z_full, it & 1, guard, status, kStatusTimeoutProducer);
+      if (it >= 1) w = w && mbar_wait(&bars->a_empty, (it - 1) & 1, guard, status, kStatusTimeoutProducer);
+      if (!__all_sync(0xffffffffu, w)) break;
+#pragma unroll 4
+      for (int k = 0; k < 32; ++k) {
+        const int pr = warp * 32 + k;
+        const float4 v = lds_f4(zsrc + swz128(pr, lane & 7));
+        const float mean = warp_sum((v.x + v.y) + (v.z + v.w)) * (1.f / 128.f);
+        const float dx = v.x - mean, dy = v.y - mean, dz = v.z - mean, dw = v.w - mean;
+        const float var = warp_sum((dx * dx + dy * dy) + (dz * dz + dw * dw)) * (1.f / 128.f);
+        const float rstd = rsqrtf(var + 1e-5f);
+        const float y0 = dx * rstd * gw.x + gb.x, y1 = dy * rstd * gw.y + gb.y;
+        const float y2 = dz * rstd * gw.z + gb.z, y3 = dw * rstd * gw.w + gb.w;
+        uint2 o;
+        o.x = pack_f16x2(y0, y1);
+        o.y = pack_f16x2(y2, y3);
+        *reinterpret_cast<uint2*>(at + swz128(pr, (lane & 15) >> 1) + (lane & 1) * 8) = o;
+        float pb[kHeads];
+#pragma unroll
+        for (int h = 0; h < kHeads; ++h) pb[h] = y0 * wb[h].x + y1 * wb[h].y + y2 * wb[h].z + y3 * wb[h].w;
+        const float tot = warp_sum4_transposed(pb[0], pb[1], pb[2], pb[3], lane);
+        const int j = j0 + pr;
+        if ((lane & 7) == 0 && j < N)
+          bias[(static_cast<size_t>(b * kHeads + (lane >> 3)) * N + i) * ldn + j] = __float2bfloat16_rn(tot);
       }
-      uint8_t* at = smem + k3::kA + s * 32768 + (lane >> 4) * 16384;
-#pragma unroll 1
-      for (int half = 0; half < 2; ++half) {
-        float4 v[16];
-#pragma unroll
-        for (int k = 0; k < 16; ++k) {
-          const int j = j0 + warp * 32 + half * 16 + k;
-          const size_t pr =
-              starting ? (static_cast<size_t>(b) * N + i) * N + j : (static_cast<size_t>(b) * N + j) * N + i;
-          v[k] = j < N ? __ldg(reinterpret_cast<const float4*>(z + pr * 128) + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-#pragma unroll
-        for (int k = 0; k < 16; ++k) {
-          const float mean = warp_sum((v[k].x + v[k].y) + (v[k].z + v[k].w)) * (1.f / 128.f);
-          const float dx = v[k].x - mean, dy = v[k].y - mean, dz = v[k].z - mean, dw = v[k].w - mean;
-          const float var = warp_sum((dx * dx + dy * dy) + (dz * dz + dw * dw)) * (1.f / 128.f);
-          const float rstd = rsqrtf(var + 1e-5f);
-          const float y0 = dx * rstd * gw.x + gb.x, y1 = dy * rstd * gw.y + gb.y;
-          const float y2 = dz * rstd * gw.z + gb.z, y3 = dw * rstd * gw.w + gb.w;
-          uint2 o;
-          o.x = pack_f16x2(y0, y1);
-          o.y = pack_f16x2(y2, y3);
-          const int pr = warp * 32 + half * 16 + k;
-          *reinterpret_cast<uint2*>(at + swz128(pr, (lane & 15) >> 1) + (lane & 1) * 8) = o;
-          float pb[kHeads];
-#pragma unroll
-          for (int h = 0; h < kHeads; ++h) pb[h] = y0 * wb[h].x + y1 * wb[h].y + y2 * wb[h].z + y3 * wb[h].w;
-          const float tot = warp_sum4_transposed(pb[0], pb[1], pb[2], pb[3], lane);
-          const int j = j0 + pr;
-          if ((lane & 7) == 0 && j < N)
-            bias[(static_cast<size_t>(b * kHeads + (lane >> 3)) * N + i) * ldn + j] = __float2bfloat16_rn(tot);
-        }
-      }
+      mbar_arrive(&bars->z_empty);  // the z tile may be refilled
       fence_proxy_async_smem();
-      mbar_arrive(&bars->a_full[s]);
+      mbar_arrive(&bars->a_full);
     }
   } else if (warp == 8) {
-    // ------------------------- weights + MMA issuer -------------------------
+    // ------------------------- TMA producer + MMA issuer -------------------------
     if (lane == 0) {
+      auto load_z = [&](int tile) {
+        const int jt = tile % n_jt, bi = tile / n_jt;
+        const int i = bi % N, b = bi / N;
+        mbar_arrive_expect_tx(&bars->z_full, 65536);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          tma_load_4d(smem + k3::kZ + q * 16384, &z_map, &bars->z_full, q * 32, jt * 128, i, b);
+      };
       mbar_arrive_expect_tx(&bars->wbar, 131072);
 #pragma unroll
       for (int kh = 0; kh < 2; ++kh)
 #pragma unroll
         for (int rb = 0; rb < 4; ++rb)
           tma_load_2d(smem + k3::kW + kh * 65536 + rb * 16384, &w_map, &bars->wbar, kh * 64, rb * 128);
+      if (blockIdx.x < n_tiles) load_z(blockIdx.x);
       bool ok = mbar_wait(&bars->wbar, 0, guard, status, kStatusTimeoutMma);
       const uint32_t idesc = make_idesc_f16(128, 256, 0, 0);
-      const uint32_t w0 = smem_u32(smem + k3::kW);
-      int it = 0;
+      const uint32_t w0 = smem_u32(smem + k3::kW), a0 = smem_u32(smem + k3::kA);
+      int it = 0, loaded = blockIdx.x < n_tiles ? 1 : 0;
       for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++it) {
-        const int s = it & 1;
-        ok = mbar_wait(&bars->a_full[s], (it >> 1) & 1, guard, status, kStatusTimeoutMma);
-        const uint32_t a0 = smem_u32(smem + k3::kA + s * 32768);
+        // refill z for the next tile as soon as the LayerNorm producers released it
+        const int next = tile + gridDim.x;
+        if (next < n_tiles) {
+          ok = mbar_wait(&bars->z_empty, it & 1, guard, status, kStatusTimeoutMma);
+          if (!ok) break;
+          load_z(next);
+          ++loaded;
+        }
+        ok = mbar_wait(&bars->a_full, it & 1, guard, status, kStatusTimeoutMma);
         for (int h = 0; ok && h < 2; ++h) {
           if (it >= 1) ok = mbar_wait(&bars->d_empty[h], (it - 1) & 1, guard, status, kStatusTimeoutMma);
           if (!ok) break;
@@ -245,11 +256,12 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
           }
           umma_commit(&bars->d_full[h]);
         }
-        if (ok) umma_commit(&bars->a_empty[s]);
+        if (ok) umma_commit(&bars->a_empty);
       }
       if (!ok) {
         umma_commit(&bars->drain);
         mbar_wait_drain(&bars->drain, 0);
+        if (loaded > 0) mbar_wait_drain(&bars->z_full, (loaded - 1) & 1);
         mbar_wait_drain(&bars->wbar, 0);
       }
     }
@@ -1095,12 +1107,13 @@ int gtk_triatt_project(int starting, const float* z, const void* packed, void* w
   const int64_t n_jt = (N + 127) / 128;
   const int64_t n_tiles = B * N * n_jt;
   if (n_tiles > 2147483647) return fail(GTK_ERR_INVALID_ARG, "triatt_project: too many tiles");
-  CUtensorMap wm;
+  CUtensorMap wm, zm;
   if (int e = make_weight_map(&wm, pk + tapack::kW3, 512, 128)) return e;
+  if (int e = make_pair_map(&zm, z, B, N, N, !starting)) return e;
   if (int e = ensure_smem(reinterpret_cast<const void*>(triatt_project_kernel), k3::kSmem)) return e;
   const int grid = static_cast<int>(n_tiles < num_sms() ? n_tiles : num_sms());
   triatt_project_kernel<<<grid, k3::kThreads, k3::kSmem, static_cast<cudaStream_t>(stream)>>>(
-      wm, z, starting, reinterpret_cast<const float*>(pk + tapack::kVec), reinterpret_cast<__half*>(ws + w.q),
+      wm, zm, reinterpret_cast<const float*>(pk + tapack::kVec), reinterpret_cast<__half*>(ws + w.q),
       reinterpret_cast<__half*>(ws + w.k), reinterpret_cast<__half*>(ws + w.v), reinterpret_cast<__half*>(ws + w.g),
       reinterpret_cast<__nv_bfloat16*>(ws + w.bias), static_cast<int>(N), static_cast<int>(round_up(N, 8)),
       static_cast<int>(n_jt), static_cast<int>(n_tiles), status);
