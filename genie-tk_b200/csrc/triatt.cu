@@ -105,9 +105,11 @@ __device__ __forceinline__ float warp_sum4_transposed(float v0, float v1, float 
 //   warp 8     lane 0: TMA producer and MMA issuer. The 128 KB of weights are loaded
 //              once; each tile's 128 x 128 fp32 z block (z^T for the ending node, through
 //              the transposed descriptor) arrives by TMA, 64 KB in flight per tile;
-//   warps 0-3  LayerNorm producers: warp per pair row, read from the staged z tile,
+//   warps 0-3  LayerNorm producers: thread per pair row, read from the staged z tile,
 //              write the fp16 operand A and the four triangle-bias dot products of the
-//              fp32 LN output (stored bf16, times log2 e);
+//              fp32 LN output (stored bf16, times log2 e). Thread-per-row keeps every
+//              reduction in registers (a warp-per-row version spent ~700 cycles per row
+//              in dependent shuffle chains);
 //   warps 4-7  epilogue: thread = pair (TMEM lane): q, k, v rows of 64 B per head and the
 //              sigmoid gate row of 256 B, written straight to global memory.
 // TMEM: half 0 = (q, k) columns 0-255, half 1 = (v, g) columns 256-511; the epilogue of
@@ -170,15 +172,14 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
   const uint32_t tmem = bars->tslot;
 
   if (warp < 4) {
-    // ------------------------- LayerNorm + bias producers -------------------------
-    const float4 gw = reinterpret_cast<const float4*>(vec + tapack::kVLnW)[lane];
-    const float4 gb = reinterpret_cast<const float4*>(vec + tapack::kVLnB)[lane];
-    float4 wb[kHeads];
-#pragma unroll
-    for (int h = 0; h < kHeads; ++h) wb[h] = reinterpret_cast<const float4*>(vec + tapack::kVWb + h * 128)[lane];
-    // lane l holds channels 4l..4l+3: box l / 8 (32 channels each), 16-B chunk l % 8
-    const uint8_t* zsrc = smem + k3::kZ + (lane >> 3) * 16384;
-    uint8_t* at = smem + k3::kA + (lane >> 4) * 16384;
+    // ---------------- LayerNorm + bias producers: thread = pair row p ----------------
+    // Row p of the staged z tile is read from the 128-B-swizzled layout (conflict-free:
+    // each warp's 32 rows cover all bank groups); gamma, beta and the bias weights are
+    // warp-uniform loads served from L1.
+    const int p = tid;
+    const float* lnw = vec + tapack::kVLnW;
+    const float* lnb = vec + tapack::kVLnB;
+    const float* wbv = vec + tapack::kVWb;
     int it = 0;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
       const int jt = tile % n_jt, bi = tile / n_jt;
@@ -186,29 +187,61 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
       bool w = mbar_wait(&bars->z_full, it & 1, guard, status, kStatusTimeoutProducer);
       if (it >= 1) w = w && mbar_wait(&bars->a_empty, (it - 1) & 1, guard, status, kStatusTimeoutProducer);
       if (!__all_sync(0xffffffffu, w)) break;
-#pragma unroll 4
-      for (int k = 0; k < 32; ++k) {
-        const int pr = warp * 32 + k;
-        const float4 v = lds_f4(zsrc + swz128(pr, lane & 7));
-        const float mean = warp_sum((v.x + v.y) + (v.z + v.w)) * (1.f / 128.f);
-        const float dx = v.x - mean, dy = v.y - mean, dz = v.z - mean, dw = v.w - mean;
-        const float var = warp_sum((dx * dx + dy * dy) + (dz * dz + dw * dw)) * (1.f / 128.f);
-        const float rstd = rsqrtf(var + 1e-5f);
-        const float y0 = dx * rstd * gw.x + gb.x, y1 = dy * rstd * gw.y + gb.y;
-        const float y2 = dz * rstd * gw.z + gb.z, y3 = dw * rstd * gw.w + gb.w;
-        uint2 o;
-        o.x = pack_f16x2(y0, y1);
-        o.y = pack_f16x2(y2, y3);
-        *reinterpret_cast<uint2*>(at + swz128(pr, (lane & 15) >> 1) + (lane & 1) * 8) = o;
-        float pb[kHeads];
+      const uint8_t* zt = smem + k3::kZ;
+      float sum = 0.f;
 #pragma unroll
-        for (int h = 0; h < kHeads; ++h) pb[h] = y0 * wb[h].x + y1 * wb[h].y + y2 * wb[h].z + y3 * wb[h].w;
-        const float tot = warp_sum4_transposed(pb[0], pb[1], pb[2], pb[3], lane);
-        const int j = j0 + pr;
-        if ((lane & 7) == 0 && j < N)
-          bias[(static_cast<size_t>(b * kHeads + (lane >> 3)) * N + i) * ldn + j] = __float2bfloat16_rn(tot);
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch) {
+          const float4 v = lds_f4(zt + q * 16384 + swz128(p, ch));
+          sum += (v.x + v.y) + (v.z + v.w);
+        }
+      const float mean = sum * (1.f / 128.f);
+      float ss = 0.f;
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch) {
+          const float4 v = lds_f4(zt + q * 16384 + swz128(p, ch));
+          const float a = v.x - mean, bb = v.y - mean, c = v.z - mean, d = v.w - mean;
+          ss += (a * a + bb * bb) + (c * c + d * d);
+        }
+      const float rstd = rsqrtf(ss * (1.f / 128.f) + 1e-5f);
+      float bacc[kHeads] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+      for (int c8 = 0; c8 < 16; ++c8) {
+        const int c = c8 * 8;
+        const float4 v0 = lds_f4(zt + (c >> 5) * 16384 + swz128(p, (c & 31) >> 2));
+        const float4 v1 = lds_f4(zt + (c >> 5) * 16384 + swz128(p, ((c & 31) >> 2) + 1));
+        const float4 w0 = __ldg(reinterpret_cast<const float4*>(lnw + c));
+        const float4 w1 = __ldg(reinterpret_cast<const float4*>(lnw + c + 4));
+        const float4 b0 = __ldg(reinterpret_cast<const float4*>(lnb + c));
+        const float4 b1 = __ldg(reinterpret_cast<const float4*>(lnb + c + 4));
+        float y[8] = {(v0.x - mean) * rstd * w0.x + b0.x, (v0.y - mean) * rstd * w0.y + b0.y,
+                      (v0.z - mean) * rstd * w0.z + b0.z, (v0.w - mean) * rstd * w0.w + b0.w,
+                      (v1.x - mean) * rstd * w1.x + b1.x, (v1.y - mean) * rstd * w1.y + b1.y,
+                      (v1.z - mean) * rstd * w1.z + b1.z, (v1.w - mean) * rstd * w1.w + b1.w};
+#pragma unroll
+        for (int h = 0; h < kHeads; ++h) {
+          const float4 u0 = __ldg(reinterpret_cast<const float4*>(wbv + h * 128 + c));
+          const float4 u1 = __ldg(reinterpret_cast<const float4*>(wbv + h * 128 + c + 4));
+          bacc[h] += y[0] * u0.x + y[1] * u0.y + y[2] * u0.z + y[3] * u0.w + y[4] * u1.x + y[5] * u1.y +
+                     y[6] * u1.z + y[7] * u1.w;
+        }
+        uint4 o;
+        o.x = pack_f16x2(y[0], y[1]);
+        o.y = pack_f16x2(y[2], y[3]);
+        o.z = pack_f16x2(y[4], y[5]);
+        o.w = pack_f16x2(y[6], y[7]);
+        sts_u4(smem + k3::kA + (c8 >> 3) * 16384 + swz128(p, c8 & 7), o);
       }
       mbar_arrive(&bars->z_empty);  // the z tile may be refilled
+      const int j = j0 + p;
+      if (j < N) {
+#pragma unroll
+        for (int h = 0; h < kHeads; ++h)
+          bias[(static_cast<size_t>(b * kHeads + h) * N + i) * ldn + j] = __float2bfloat16_rn(bacc[h]);
+      }
       fence_proxy_async_smem();
       mbar_arrive(&bars->a_full);
     }
