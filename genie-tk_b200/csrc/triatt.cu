@@ -101,8 +101,8 @@ __device__ __forceinline__ float warp_sum4_transposed(float v0, float v1, float 
 
 // ----------------------------------------------------------------------------------
 // K3: persistent LN + q/k/v/g projections + triangle bias. Tile = 128 consecutive pairs
-// (b, row i of the problem, j0..j0+127); CTAs loop over tiles. 288 threads:
-//   warp 8     lane 0: TMA producer and MMA issuer. The 128 KB of weights are loaded
+// (b, row i of the problem, j0..j0+127); CTAs loop over tiles. 416 threads:
+//   warp 12    lane 0: TMA producer and MMA issuer. The 128 KB of weights are loaded
 //              once; each tile's 128 x 128 fp32 z block (z^T for the ending node, through
 //              the transposed descriptor) arrives by TMA, 64 KB in flight per tile;
 //   warps 0-3  LayerNorm producers: thread per pair row, read from the staged z tile,
@@ -110,17 +110,18 @@ __device__ __forceinline__ float warp_sum4_transposed(float v0, float v1, float 
 //              fp32 LN output (stored bf16, times log2 e). Thread-per-row keeps every
 //              reduction in registers (a warp-per-row version spent ~700 cycles per row
 //              in dependent shuffle chains);
-//   warps 4-7  epilogue: thread = pair (TMEM lane): q, k, v rows of 64 B per head and the
-//              sigmoid gate row of 256 B, written straight to global memory.
-// TMEM: half 0 = (q, k) columns 0-255, half 1 = (v, g) columns 256-511; the epilogue of
-// one half overlaps the MMAs of the other; the next tile's z load overlaps both.
+//   warps 4-11 epilogue, two warpgroups (warps 4-7: q and k, warps 8-11: v and the gate),
+//              thread = pair (TMEM lane): rows of 64 B per head and the sigmoid gate row
+//              of 256 B, written straight to global memory.
+// TMEM: half 0 = (q, k) columns 0-255, half 1 = (v, g) columns 256-511, one epilogue
+// warpgroup each; the next tile's LayerNorm and z load overlap both.
 // Shared memory: W3 128 KB | z 64 KB | A 32 KB | barriers.
 // Outputs: q, k, v fp16 [B*N(i)][H][N(j)][32]; g fp16 [B*N*N][128]; bias bf16
 // [B][H][N][ldn] (log2 units; bf16 keeps the attention core's shared-memory reads of the
 // bias tile at 256 B per query row and step, and widens with one integer op).
 // ----------------------------------------------------------------------------------
 namespace k3 {
-constexpr int kThreads = 288;
+constexpr int kThreads = 416;
 constexpr uint32_t kW = 0, kZ = 131072, kA = 196608, kBar = 229376;
 constexpr uint32_t kSmem = kBar + 128 + 1024;
 static_assert(kSmem <= 232448, "K3 shared memory");
@@ -162,7 +163,7 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
     mbar_init(&bars->drain, 1);
     fence_barrier_init();
   }
-  if (warp == 8) {
+  if (warp == 12) {
     tmem_alloc(&bars->tslot, 512);
     tmem_relinquish();
   }
@@ -245,7 +246,7 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
       fence_proxy_async_smem();
       mbar_arrive(&bars->a_full);
     }
-  } else if (warp == 8) {
+  } else if (warp == 12) {
     // ------------------------- TMA producer + MMA issuer -------------------------
     if (lane == 0) {
       auto load_z = [&](int tile) {
@@ -299,7 +300,8 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
       }
     }
   } else {
-    // ------------------------- epilogue: thread = pair -------------------------
+    // ------------------ epilogue: thread = pair; warpgroup = TMEM half ------------------
+    const int h = (warp - 4) >> 2;  // 0: q, k (warps 4-7); 1: v, gate (warps 8-11)
     const int q4 = warp & 3;
     const int p = q4 * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
@@ -310,8 +312,7 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
       const int j = jt * 128 + p;
       const bool valid = j < N;
       bool ok = true;
-#pragma unroll 1
-      for (int h = 0; h < 2; ++h) {
+      {
         ok = __all_sync(0xffffffffu, mbar_wait(&bars->d_full[h], it & 1, guard, status, kStatusTimeoutConsumer));
         if (!ok) break;
         tc_fence_after();
@@ -359,7 +360,7 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 8) {
+  if (warp == 12) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }

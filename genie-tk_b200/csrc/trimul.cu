@@ -85,28 +85,34 @@ __global__ void trimul_pack_kernel(gtk_trimul_params p, uint8_t* packed) {
 // ----------------------------------------------------------------------------------
 // K1: persistent, warp-specialised LN_in + gated projections + mask -> a, b planes.
 // Tile = 128 consecutive pairs (b, r, j0..j0+127); CTAs loop over tiles. 288 threads:
-//   warps 0-3  LayerNorm producers: warp w normalises pairs 32w..32w+31 one row at a
-//              time (coalesced 512-B loads, shuffle reductions) into the fp16 operand
-//              tile A[s] (double buffered), and stages the tile's mask values;
-//   warp 8     lane 0: loads the 128 KB of packed weights once, then issues the MMAs;
+//   warp 8     lane 0: TMA producer and MMA issuer. The 128 KB of packed weights are
+//              loaded once; each tile's 128 x 128 fp32 z block arrives by TMA (64 KB in
+//              flight per tile, refilled as soon as the LayerNorm has read it);
+//   warps 0-3  LayerNorm producers: thread p normalises pair row p from the staged,
+//              128-B-swizzled z tile (reductions in registers, conflict-free reads) into
+//              the fp16 operand tile A, and stages the pair's mask value;
 //   warps 4-7  epilogue: thread = channel c (TMEM lane), reads 32-pair slabs of the
 //              projection / gate accumulators, applies bias, sigmoid and mask, and writes
 //              64 contiguous bytes of its channel-plane row per slab.
 // MMA (transposed so that channels sit on TMEM lanes): D[c][j] = W_chunk[c][:] . A[j][:],
 // M = 128 channels, N = 128 pairs, K = 128. Chunks (a_p, a_g) -> TMEM columns 0-255
 // (half 0), (b_p, b_g) -> 256-511 (half 1); the epilogue of half 0 overlaps the MMAs of
-// half 1, and the LayerNorm of the next tile overlaps both.
+// half 1, and the next tile's z load overlaps both. (A second epilogue warpgroup, one per
+// half, was measured slower: 0.48 vs 0.39 ms at N = 1024, with the 416-thread launch
+// capping registers at 128.)
+// Shared memory: W1 128 KB | A 32 KB | z 64 KB | mask 2 x 512 B | barriers.
 // ----------------------------------------------------------------------------------
 namespace k1 {
 constexpr int kThreads = 288;
-constexpr uint32_t kW = 0, kA = 131072, kMask = 196608, kBar = 197632;
+constexpr uint32_t kW = 0, kA = 131072, kZ = 163840, kMask = 229376, kBar = 230400;
 constexpr uint32_t kSmem = kBar + 128 + 1024;
 static_assert(kSmem <= 232448, "K1 shared memory");
 }  // namespace k1
 
 struct K1Bars {
   uint64_t wbar;
-  uint64_t a_full[2], a_empty[2];
+  uint64_t z_full, z_empty;
+  uint64_t a_full, a_empty;
   uint64_t d_full[2], d_empty[2];
   uint64_t m_empty[2];
   uint64_t drain;
@@ -116,7 +122,7 @@ struct K1Bars {
 static_assert(sizeof(K1Bars) <= 128, "K1 barrier block");
 
 __global__ void __launch_bounds__(k1::kThreads, 1)
-    trimul_project_kernel(const __grid_constant__ CUtensorMap w_map, const float* __restrict__ z,
+    trimul_project_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap z_map,
                           const float* __restrict__ mask, const float* __restrict__ vec, __half* __restrict__ a_out,
                           __half* __restrict__ b_out, int64_t ld, int N, int rows, int n_jt, int n_tiles,
                           uint32_t* status) {
@@ -130,9 +136,11 @@ __global__ void __launch_bounds__(k1::kThreads, 1)
   if (tid == 0) {
     guard->abort = 0;
     mbar_init(&bars->wbar, 1);
+    mbar_init(&bars->z_full, 1);
+    mbar_init(&bars->z_empty, 128);
+    mbar_init(&bars->a_full, 128);
+    mbar_init(&bars->a_empty, 1);
     for (int x = 0; x < 2; ++x) {
-      mbar_init(&bars->a_full[x], 128);
-      mbar_init(&bars->a_empty[x], 1);
       mbar_init(&bars->d_full[x], 1);
       mbar_init(&bars->d_empty[x], 128);
       mbar_init(&bars->m_empty[x], 128);
@@ -150,63 +158,56 @@ __global__ void __launch_bounds__(k1::kThreads, 1)
   const uint32_t tmem = bars->tslot;
 
   if (warp < 4) {
-    // ------------------------- LayerNorm producers -------------------------
-    const float4 gw = reinterpret_cast<const float4*>(vec + tmpack::kVLnW)[lane];
-    const float4 gb = reinterpret_cast<const float4*>(vec + tmpack::kVLnB)[lane];
+    // ------------------- LayerNorm producers: thread = pair row -------------------
+    const int p = tid;
     int it = 0;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
       const int s = it & 1;
       const int jt = tile % n_jt, rb = tile / n_jt;
       const int r = rb % rows, b = rb / rows, j0 = jt * 128;
-      if (it >= 2) {
-        const uint32_t par = ((it >> 1) - 1) & 1;
-        bool w = mbar_wait(&bars->a_empty[s], par, guard, status, kStatusTimeoutProducer);
-        w = w && mbar_wait(&bars->m_empty[s], par, guard, status, kStatusTimeoutProducer);
-        if (!__all_sync(0xffffffffu, w)) break;
-      }
-      const size_t rowbase = (static_cast<size_t>(b) * rows + r) * N;
-      const int jm = j0 + warp * 32 + lane;
-      mask_s[s * 128 + warp * 32 + lane] = jm < N ? (mask ? mask[rowbase + jm] : 1.f) : 0.f;
-      float4 v[32];
-#pragma unroll
-      for (int k = 0; k < 32; ++k) {
-        const int j = j0 + warp * 32 + k;
-        v[k] = j < N ? __ldg(reinterpret_cast<const float4*>(z + (rowbase + j) * 128) + lane)
-                     : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-      uint8_t* at = smem + k1::kA + s * 32768 + (lane >> 4) * 16384;
-#pragma unroll
-      for (int k = 0; k < 32; ++k) {
-        const float mean = warp_sum((v[k].x + v[k].y) + (v[k].z + v[k].w)) * (1.f / 128.f);
-        const float dx = v[k].x - mean, dy = v[k].y - mean, dz = v[k].z - mean, dw = v[k].w - mean;
-        const float var = warp_sum((dx * dx + dy * dy) + (dz * dz + dw * dw)) * (1.f / 128.f);
-        const float rstd = rsqrtf(var + 1e-5f);
-        uint2 o;
-        o.x = pack_f16x2(dx * rstd * gw.x + gb.x, dy * rstd * gw.y + gb.y);
-        o.y = pack_f16x2(dz * rstd * gw.z + gb.z, dw * rstd * gw.w + gb.w);
-        const int p = warp * 32 + k;
-        *reinterpret_cast<uint2*>(at + swz128(p, (lane & 15) >> 1) + (lane & 1) * 8) = o;
-      }
+      bool w = mbar_wait(&bars->z_full, it & 1, guard, status, kStatusTimeoutProducer);
+      if (it >= 1) w = w && mbar_wait(&bars->a_empty, (it - 1) & 1, guard, status, kStatusTimeoutProducer);
+      if (it >= 2) w = w && mbar_wait(&bars->m_empty[s], ((it >> 1) - 1) & 1, guard, status, kStatusTimeoutProducer);
+      if (!__all_sync(0xffffffffu, w)) break;
+      const int j = j0 + p;
+      mask_s[s * 128 + p] = j < N ? (mask ? mask[(static_cast<size_t>(b) * rows + r) * N + j] : 1.f) : 0.f;
+      ln_row_to_operand(smem + k1::kZ, smem + k1::kA, p, vec + tmpack::kVLnW, vec + tmpack::kVLnB);
+      mbar_arrive(&bars->z_empty);  // the z tile may be refilled
       fence_proxy_async_smem();
-      mbar_arrive(&bars->a_full[s]);
+      mbar_arrive(&bars->a_full);
     }
   } else if (warp == 8) {
-    // ------------------------- weights + MMA issuer -------------------------
+    // ------------------------- TMA producer + MMA issuer -------------------------
     if (lane == 0) {
+      auto load_z = [&](int tile) {
+        const int jt = tile % n_jt, rb = tile / n_jt;
+        const int r = rb % rows, b = rb / rows;
+        mbar_arrive_expect_tx(&bars->z_full, 65536);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          tma_load_4d(smem + k1::kZ + q * 16384, &z_map, &bars->z_full, q * 32, jt * 128, r, b);
+      };
       mbar_arrive_expect_tx(&bars->wbar, 131072);
 #pragma unroll
       for (int kh = 0; kh < 2; ++kh)
 #pragma unroll
         for (int rb = 0; rb < 4; ++rb)
           tma_load_2d(smem + k1::kW + kh * 65536 + rb * 16384, &w_map, &bars->wbar, kh * 64, rb * 128);
+      if (blockIdx.x < n_tiles) load_z(blockIdx.x);
+      int loaded = blockIdx.x < n_tiles ? 1 : 0;
       bool ok = mbar_wait(&bars->wbar, 0, guard, status, kStatusTimeoutMma);
       const uint32_t idesc = make_idesc_f16(128, 128, 0, 0);
-      const uint32_t w0 = smem_u32(smem + k1::kW);
+      const uint32_t w0 = smem_u32(smem + k1::kW), a0 = smem_u32(smem + k1::kA);
       int it = 0;
       for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++it) {
-        const int s = it & 1;
-        ok = mbar_wait(&bars->a_full[s], (it >> 1) & 1, guard, status, kStatusTimeoutMma);
-        const uint32_t a0 = smem_u32(smem + k1::kA + s * 32768);
+        const int next = tile + gridDim.x;
+        if (next < n_tiles) {
+          ok = mbar_wait(&bars->z_empty, it & 1, guard, status, kStatusTimeoutMma);
+          if (!ok) break;
+          load_z(next);
+          ++loaded;
+        }
+        ok = mbar_wait(&bars->a_full, it & 1, guard, status, kStatusTimeoutMma);
         for (int h = 0; ok && h < 2; ++h) {
           if (it >= 1) ok = mbar_wait(&bars->d_empty[h], (it - 1) & 1, guard, status, kStatusTimeoutMma);
           if (!ok) break;
@@ -224,11 +225,12 @@ __global__ void __launch_bounds__(k1::kThreads, 1)
           }
           umma_commit(&bars->d_full[h]);
         }
-        if (ok) umma_commit(&bars->a_empty[s]);
+        if (ok) umma_commit(&bars->a_empty);
       }
       if (!ok) {
         umma_commit(&bars->drain);
         mbar_wait_drain(&bars->drain, 0);
+        if (loaded > 0) mbar_wait_drain(&bars->z_full, (loaded - 1) & 1);
         mbar_wait_drain(&bars->wbar, 0);
       }
     }
@@ -774,13 +776,14 @@ int gtk_trimul_project(const float* z, const float* mask, const void* packed, vo
   const int64_t n_jt = (N + 127) / 128;
   const int64_t n_tiles = B * rows * n_jt;
   if (n_tiles > 2147483647) return fail(GTK_ERR_INVALID_ARG, "trimul_project: too many tiles");
-  CUtensorMap wm;
+  CUtensorMap wm, zm;
   const uint8_t* pk = static_cast<const uint8_t*>(packed);
   if (int e = make_weight_map(&wm, pk + tmpack::kW1, 512, 128)) return e;
+  if (int e = make_pair_map(&zm, z, B, rows, N, false)) return e;
   if (int e = ensure_smem(reinterpret_cast<const void*>(trimul_project_kernel), k1::kSmem)) return e;
   const int grid = static_cast<int>(n_tiles < num_sms() ? n_tiles : num_sms());
   trimul_project_kernel<<<grid, k1::kThreads, k1::kSmem, static_cast<cudaStream_t>(stream)>>>(
-      wm, z, mask, reinterpret_cast<const float*>(pk + tmpack::kVec), static_cast<__half*>(a_planes),
+      wm, zm, mask, reinterpret_cast<const float*>(pk + tmpack::kVec), static_cast<__half*>(a_planes),
       static_cast<__half*>(b_planes), ld, static_cast<int>(N), static_cast<int>(rows), static_cast<int>(n_jt),
       static_cast<int>(n_tiles), status);
   return check_launch("trimul_project_kernel");
