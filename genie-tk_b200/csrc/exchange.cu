@@ -1,0 +1,99 @@
+// Data movement for the row-sharded pair stack (one process per GPU, the pair tensor
+// [B, N, N, 128] split over its first pair index i into P shards of R = N / P rows).
+//
+// The collectives themselves are NCCL calls made by the host driver; these kernels
+// prepare and scatter the contiguous per-peer chunks those calls exchange:
+//
+//   gtk_copy_2d            strided block copy (rows of `width` bytes between two pitches):
+//                          packs a column slice of every row into a contiguous chunk, or
+//                          scatters a received chunk into a column slice;
+//   gtk_pair_transpose_pack  the pair-grid transpose that turns a row shard into the
+//                          per-peer chunks of an all-to-all whose result, after one
+//                          gtk_copy_2d per peer, is the transposed shard (used by the
+//                          ending-node attention, which runs as the starting node of z^T).
+//
+// Both are pure HBM streams: 16-byte vector accesses, every pair vector (128 fp32 =
+// 512 B) moved by one warp as one fully coalesced transaction per side.
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "gtk_host.h"
+
+namespace gtk {
+
+__global__ void __launch_bounds__(256) copy_2d_kernel(uint8_t* __restrict__ dst, int64_t dpitch,
+                                                      const uint8_t* __restrict__ src, int64_t spitch, int64_t w16,
+                                                      int64_t total) {
+  for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = e / w16, c = e - r * w16;
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(src + r * spitch) + c);
+    reinterpret_cast<uint4*>(dst + r * dpitch)[c] = v;
+  }
+}
+
+// dst[q][b][x][y][:] = src[b][y][q * (C / P) + x][:] for a pair grid src [B][R][C][128] fp32,
+// x in [0, C/P), y in [0, R). One warp moves one 512-B pair vector; warps walk the
+// destination in order, so the writes stream and each read is one 512-B segment.
+__global__ void __launch_bounds__(256) pair_transpose_pack_kernel(const float4* __restrict__ src,
+                                                                  float4* __restrict__ dst, int64_t B, int64_t R,
+                                                                  int64_t C, int64_t P) {
+  const int lane = threadIdx.x & 31;
+  const int64_t CP = C / P;
+  const int64_t n_pairs = B * R * C;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t w = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); w < n_pairs;
+       w += warps) {
+    // destination pair index w = ((q * B + b) * CP + x) * R + y
+    const int64_t y = w % R;
+    int64_t t = w / R;
+    const int64_t x = t % CP;
+    t /= CP;
+    const int64_t b = t % B, q = t / B;
+    const int64_t s = (b * R + y) * C + q * CP + x;
+    dst[w * 32 + lane] = __ldg(src + s * 32 + lane);
+  }
+}
+
+static int grid_for(int64_t work_items, int per_block) {
+  const int64_t blocks = (work_items + per_block - 1) / per_block;
+  const int64_t cap = static_cast<int64_t>(num_sms()) * 8;
+  return static_cast<int>(blocks < cap ? (blocks > 0 ? blocks : 1) : cap);
+}
+
+}  // namespace gtk
+
+using namespace gtk;
+
+extern "C" {
+
+int gtk_copy_2d(void* dst, int64_t dpitch, const void* src, int64_t spitch, int64_t width, int64_t height,
+                void* stream) {
+  if (width < 0 || height < 0 || dpitch < width || spitch < width)
+    return fail(GTK_ERR_INVALID_ARG, "copy_2d: bad width/height/pitch");
+  if (width == 0 || height == 0) return GTK_OK;
+  if ((width | dpitch | spitch) & 15) return fail(GTK_ERR_ALIGNMENT, "copy_2d: width and pitches must be 16-B multiples");
+  if (int e = check_ptr(dst, "dst")) return e;
+  if (int e = check_ptr(src, "src")) return e;
+  if (int e = check_device()) return e;
+  const int64_t w16 = width / 16, total = w16 * height;
+  copy_2d_kernel<<<grid_for(total, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<uint8_t*>(dst), dpitch, static_cast<const uint8_t*>(src), spitch, w16, total);
+  return check_launch("copy_2d_kernel");
+}
+
+int gtk_pair_transpose_pack(const float* src, float* dst, int64_t B, int64_t R, int64_t C, int64_t P, void* stream) {
+  if (B < 1 || R < 1 || C < 1 || P < 1 || C % P)
+    return fail(GTK_ERR_INVALID_ARG, "pair_transpose_pack: need B, R, C, P >= 1 and C divisible by P");
+  if (int e = check_ptr(src, "src")) return e;
+  if (int e = check_ptr(dst, "dst")) return e;
+  if (src == dst) return fail(GTK_ERR_INVALID_ARG, "pair_transpose_pack: src and dst must not alias");
+  if (int e = check_device()) return e;
+  const int64_t n_pairs = B * R * C;
+  pair_transpose_pack_kernel<<<grid_for(n_pairs, 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const float4*>(src), reinterpret_cast<float4*>(dst), B, R, C, P);
+  return check_launch("pair_transpose_pack_kernel");
+}
+
+}  // extern "C"

@@ -116,8 +116,12 @@ __device__ __forceinline__ float warp_sum4_transposed(float v0, float v1, float 
 // TMEM: half 0 = (q, k) columns 0-255, half 1 = (v, g) columns 256-511, one epilogue
 // warpgroup each; the next tile's LayerNorm and z load overlap both.
 // Shared memory: W3 128 KB | z 64 KB | A 32 KB | barriers.
-// Outputs: q, k, v fp16 [B*N(i)][H][N(j)][32]; g fp16 [B*N*N][128]; bias bf16
-// [B][H][N][ldn] (log2 units; bf16 keeps the attention core's shared-memory reads of the
+// Rows: the tile grid covers `rows` problem rows i (all N when unsharded; one shard's rows
+// under row sharding, which only the starting orientation supports).
+// Outputs: q, k, v fp16 [B*rows(i)][H][N(j)][32]; g fp16 [B*rows*N][128]; bias bf16
+// [N(row)][B][H][ldn], rows row0.. row0+rows-1 written here (row-major over the problem
+// row, so that the shards of a row-sharded run are contiguous and can be all-gathered in
+// place; log2 units; bf16 keeps the attention core's shared-memory reads of the
 // bias tile at 256 B per query row and step, and widens with one integer op).
 // ----------------------------------------------------------------------------------
 namespace k3 {
@@ -142,7 +146,7 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
     triatt_project_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap z_map,
                           const float* __restrict__ vec, __half* __restrict__ q_out, __half* __restrict__ k_out,
                           __half* __restrict__ v_out, __half* __restrict__ g_out, __nv_bfloat16* __restrict__ bias,
-                          int N, int ldn, int n_jt, int n_tiles, uint32_t* status) {
+                          int N, int rows, int B, int row0, int ldn, int n_jt, int n_tiles, uint32_t* status) {
   extern __shared__ uint8_t dsmem[];
   uint8_t* smem = align1024(dsmem);
   K3Bars* bars = reinterpret_cast<K3Bars*>(smem + k3::kBar);
@@ -184,7 +188,7 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
     int it = 0;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
       const int jt = tile % n_jt, bi = tile / n_jt;
-      const int i = bi % N, b = bi / N, j0 = jt * 128;
+      const int i = bi % rows, b = bi / rows, j0 = jt * 128;
       bool w = mbar_wait(&bars->z_full, it & 1, guard, status, kStatusTimeoutProducer);
       if (it >= 1) w = w && mbar_wait(&bars->a_empty, (it - 1) & 1, guard, status, kStatusTimeoutProducer);
       if (!__all_sync(0xffffffffu, w)) break;
@@ -241,7 +245,7 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
       if (j < N) {
 #pragma unroll
         for (int h = 0; h < kHeads; ++h)
-          bias[(static_cast<size_t>(b * kHeads + h) * N + i) * ldn + j] = __float2bfloat16_rn(bacc[h]);
+          bias[((static_cast<size_t>(row0 + i) * B + b) * kHeads + h) * ldn + j] = __float2bfloat16_rn(bacc[h]);
       }
       fence_proxy_async_smem();
       mbar_arrive(&bars->a_full);
@@ -251,7 +255,7 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
     if (lane == 0) {
       auto load_z = [&](int tile) {
         const int jt = tile % n_jt, bi = tile / n_jt;
-        const int i = bi % N, b = bi / N;
+        const int i = bi % rows, b = bi / rows;
         mbar_arrive_expect_tx(&bars->z_full, 65536);
 #pragma unroll
         for (int q = 0; q < 4; ++q)
@@ -484,8 +488,9 @@ __device__ __forceinline__ void setmaxnreg_dec() {
 __global__ void __launch_bounds__(k4::kThreads, 1)
     triatt_core_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap k_map,
                        const __grid_constant__ CUtensorMap v_map, const __grid_constant__ CUtensorMap bias_map,
-                       const float* __restrict__ mask, int64_t mask_si, int64_t mask_sk, float mask_scale,
-                       const __half* __restrict__ gate, __half* __restrict__ og, int N, int n_igroups,
+                       const float* __restrict__ mask, int64_t mask_sb, int64_t mask_si, int64_t mask_sk,
+                       float mask_scale, const __half* __restrict__ gate, __half* __restrict__ og, int N, int rows,
+                       int n_igroups,
                        uint32_t* status) {
   using namespace k4;
   extern __shared__ uint8_t dsmem[];
@@ -536,8 +541,8 @@ __global__ void __launch_bounds__(k4::kThreads, 1)
         mbar_arrive_expect_tx(&bars->q_full, kR * 8192);
 #pragma unroll
         for (int r = 0; r < kR; ++r) {
-          const int i = min(ig * kR + r, N - 1);
-          tma_load_4d(smem + kQ + r * 8192, &q_map, &bars->q_full, 0, jt * 128, h, b * N + i);
+          const int i = min(ig * kR + r, rows - 1);
+          tma_load_4d(smem + kQ + r * 8192, &q_map, &bars->q_full, 0, jt * 128, h, b * rows + i);
         }
       }
       for (int kt = 0; kt < KT && ok; ++kt) {
@@ -557,7 +562,7 @@ __global__ void __launch_bounds__(k4::kThreads, 1)
         ++issued_bias;
         for (int r = 0; r < kR; ++r) {
           const int t = kt * kR + r, s = t % kKVS;
-          const int i = min(ig * kR + r, N - 1);
+          const int i = min(ig * kR + r, rows - 1);
           if (t >= kKVS) {
             ok = __all_sync(0xffffffffu, mbar_wait(&bars->kv_empty[s], ((t / kKVS) - 1) & 1, guard, status,
                                                    kStatusTimeoutProducer));
@@ -566,12 +571,12 @@ __global__ void __launch_bounds__(k4::kThreads, 1)
           uint8_t* stage = smem + kKV + s * kKVStage;
           if (lane == 0) {
             mbar_arrive_expect_tx(&bars->kv_full[s], 16384);
-            tma_load_4d(stage, &k_map, &bars->kv_full[s], 0, kt * 128, h, b * N + i);
-            tma_load_4d(stage + 8192, &v_map, &bars->kv_full[s], 0, kt * 128, h, b * N + i);
+            tma_load_4d(stage, &k_map, &bars->kv_full[s], 0, kt * 128, h, b * rows + i);
+            tma_load_4d(stage + 8192, &v_map, &bars->kv_full[s], 0, kt * 128, h, b * rows + i);
           }
           float* mb = reinterpret_cast<float*>(stage + kMB);
           const float* mrow =
-              mask ? mask + static_cast<int64_t>(b) * N * N + static_cast<int64_t>(i) * mask_si : nullptr;
+              mask ? mask + static_cast<int64_t>(b) * mask_sb + static_cast<int64_t>(i) * mask_si : nullptr;
           bool any = false;
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
@@ -792,9 +797,9 @@ __global__ void __launch_bounds__(k4::kThreads, 1)
         tmem_ld32(tmem + lane_off + r * 32, ov);
         tmem_wait_ld();
         const int i = ig * kR + r;
-        if (i < N && j < N) {
+        if (i < rows && j < N) {
           const float inv = 1.f / (rr == 0 ? l_run0 : l_run1);
-          const size_t pair = (static_cast<size_t>(b) * N + i) * N + j;
+          const size_t pair = (static_cast<size_t>(b) * rows + i) * N + j;
           const uint4* gp = reinterpret_cast<const uint4*>(gate + pair * 128 + h * kHeadDim);
           uint4* op = reinterpret_cast<uint4*>(og + pair * 128 + h * kHeadDim);
 #pragma unroll
@@ -860,8 +865,8 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
 __global__ void __launch_bounds__(k4e::kThreads, 1)
     triatt_finish_kernel(const __grid_constant__ CUtensorMap og_map, const __grid_constant__ CUtensorMap w_map,
                          const __grid_constant__ CUtensorMap z_map, const __grid_constant__ CUtensorMap out_map,
-                         const float* __restrict__ vec, int N, int add_residual, int n_jt, int n_tiles,
-                         uint32_t* status) {
+                         const float* __restrict__ vec, int N, int rows, int add_residual, int n_jt,
+                         int n_tiles, uint32_t* status) {
   using namespace k4e;
   extern __shared__ uint8_t dsmem[];
   uint8_t* smem = align1024(dsmem);
@@ -907,7 +912,7 @@ __global__ void __launch_bounds__(k4e::kThreads, 1)
       for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++it) {
         const int s = it & 1;
         const int jt = tile % n_jt, bi = tile / n_jt;
-        const int i = bi % N, b = bi / N, j0 = jt * 128;
+        const int i = bi % rows, b = bi / rows, j0 = jt * 128;
         if (it >= 2 && !mbar_wait(&bars->a_empty[s], ((it >> 1) - 1) & 1, guard, status, kStatusTimeoutProducer)) {
           ok = false;
           break;
@@ -978,7 +983,7 @@ __global__ void __launch_bounds__(k4e::kThreads, 1)
     for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++it) {
       const int s = it & 1;
       const int jt = tile % n_jt, bi = tile / n_jt;
-      const int i = bi % N, b = bi / N, j0 = jt * 128;
+      const int i = bi % rows, b = bi / rows, j0 = jt * 128;
       ok = __all_sync(0xffffffffu, mbar_wait(&bars->d_full[s], (it >> 1) & 1, guard, status, kStatusTimeoutConsumer));
       if (!ok) break;
       tc_fence_after();
@@ -1039,10 +1044,12 @@ struct TriattWs {
   size_t q, k, v, g, og, bias, total;
 };
 
-static TriattWs triatt_layout(int64_t B, int64_t N) {
+// q, k, v, g, og cover the `rows` local problem rows; the bias always covers all N rows
+// (the attention core reads every row j of it).
+static TriattWs triatt_layout(int64_t B, int64_t rows, int64_t N) {
   TriattWs w;
-  const size_t pair16 = round_up(static_cast<size_t>(B) * N * N * 128 * 2, 256);
-  const size_t bias = round_up(static_cast<size_t>(B) * kHeads * N * round_up(N, 8) * 2, 256);
+  const size_t pair16 = round_up(static_cast<size_t>(B) * rows * N * 128 * 2, 256);
+  const size_t bias = round_up(static_cast<size_t>(N) * B * kHeads * round_up(N, 8) * 2, 256);
   w.q = 0;
   w.k = w.q + pair16;
   w.v = w.k + pair16;
@@ -1053,29 +1060,42 @@ static TriattWs triatt_layout(int64_t B, int64_t N) {
   return w;
 }
 
-// q / k / v: [B*N(i)][H][N(j)][32] fp16, box (32, 128, 1, 1), 64-B swizzle.
-static int make_head_map(CUtensorMap* m, const void* base, int64_t B, int64_t N) {
-  uint64_t dims[4] = {32, static_cast<uint64_t>(N), static_cast<uint64_t>(kHeads), static_cast<uint64_t>(B * N)};
+// q / k / v: [B*rows(i)][H][N(j)][32] fp16, box (32, 128, 1, 1), 64-B swizzle.
+static int make_head_map(CUtensorMap* m, const void* base, int64_t BR, int64_t N) {
+  uint64_t dims[4] = {32, static_cast<uint64_t>(N), static_cast<uint64_t>(kHeads), static_cast<uint64_t>(BR)};
   uint64_t strides[3] = {64, static_cast<uint64_t>(N) * 64, static_cast<uint64_t>(N) * 64 * kHeads};
   uint32_t box[4] = {32, 128, 1, 1};
   return encode_tmap(m, TmaType::kF16, 4, base, dims, strides, box, 64);
 }
 
-// g / og: [B*N(i)][N(j)][128] fp16, box (64, 128, 1), 128-B swizzle.
-static int make_hidden_map(CUtensorMap* m, const void* base, int64_t B, int64_t N) {
-  uint64_t dims[3] = {128, static_cast<uint64_t>(N), static_cast<uint64_t>(B * N)};
+// g / og: [B*rows(i)][N(j)][128] fp16, box (64, 128, 1), 128-B swizzle.
+static int make_hidden_map(CUtensorMap* m, const void* base, int64_t BR, int64_t N) {
+  uint64_t dims[3] = {128, static_cast<uint64_t>(N), static_cast<uint64_t>(BR)};
   uint64_t strides[2] = {256, static_cast<uint64_t>(N) * 256};
   uint32_t box[3] = {64, 128, 1};
   return encode_tmap(m, TmaType::kF16, 3, base, dims, strides, box, 128);
 }
 
-// bias: [B*H][N(j)][ldn] bf16, box (64 k, 128 j, 1), 128-B swizzle.
+// bias: [N(j)][B*H][ldn] bf16, addressed as (k, j, b*H + h); box (64 k, 128 j, 1), 128-B swizzle.
 static int make_bias_map(CUtensorMap* m, const void* base, int64_t B, int64_t N) {
   const uint64_t ldn = round_up(static_cast<uint64_t>(N), 8);
-  uint64_t dims[3] = {static_cast<uint64_t>(N), static_cast<uint64_t>(N), static_cast<uint64_t>(B * kHeads)};
-  uint64_t strides[2] = {ldn * 2, ldn * 2 * N};
+  const uint64_t BH = static_cast<uint64_t>(B) * kHeads;
+  uint64_t dims[3] = {static_cast<uint64_t>(N), static_cast<uint64_t>(N), BH};
+  uint64_t strides[2] = {ldn * 2 * BH, ldn * 2};
   uint32_t box[3] = {64, 128, 1};
   return encode_tmap(m, TmaType::kBF16, 3, base, dims, strides, box, 128);
+}
+
+// Row-shard arguments shared by the stage entry points: `rows` local problem rows starting
+// at global row `row0` (all of them, rows = N and row0 = 0, when unsharded).
+static int rows_check(const char* who, int starting, int64_t B, int64_t rows, int64_t N, int64_t row0) {
+  if (!dims_ok(B, 65535) || !dims_ok(N, 65535) || !dims_ok(rows, 65535) || row0 < 0 || row0 + rows > N)
+    return fail(GTK_ERR_INVALID_ARG, std::string(who) + ": bad B/rows/N/row0");
+  if (!starting && (rows != N || row0 != 0))
+    return fail(GTK_ERR_UNSUPPORTED, std::string(who) + ": the ending orientation runs on whole (unsharded) pair "
+                                                         "tensors; a row-sharded caller transposes the shards and "
+                                                         "runs the starting orientation");
+  return GTK_OK;
 }
 
 static int triatt_check(int c_in, int c_hidden, int heads) {
@@ -1113,59 +1133,62 @@ int gtk_triatt_pack(const gtk_triatt_params* params, int c_in, int c_hidden, int
 
 size_t gtk_triatt_workspace_bytes(int64_t B, int64_t N, int c_in, int c_hidden, int heads) {
   if (c_in != 128 || c_hidden != 128 || heads != kHeads || B < 1 || N < 1) return 0;
-  return triatt_layout(B, N).total;
+  return triatt_layout(B, N, N).total;
 }
 
-int gtk_triatt_workspace_offsets(int64_t B, int64_t N, int64_t* offsets) {
-  if (!offsets || B < 1 || N < 1) return fail(GTK_ERR_INVALID_ARG, "triatt_workspace_offsets: bad arguments");
-  const TriattWs w = triatt_layout(B, N);
+int gtk_triatt_workspace_offsets(int64_t B, int64_t rows, int64_t N, int64_t* offsets) {
+  if (!offsets || B < 1 || N < 1 || rows < 1 || rows > N)
+    return fail(GTK_ERR_INVALID_ARG, "triatt_workspace_offsets: bad arguments");
+  const TriattWs w = triatt_layout(B, rows, N);
   offsets[0] = static_cast<int64_t>(w.q);
   offsets[1] = static_cast<int64_t>(w.k);
   offsets[2] = static_cast<int64_t>(w.v);
   offsets[3] = static_cast<int64_t>(w.g);
   offsets[4] = static_cast<int64_t>(w.og);
   offsets[5] = static_cast<int64_t>(w.bias);
+  offsets[6] = static_cast<int64_t>(w.total);
   return GTK_OK;
 }
 
-int gtk_triatt_project(int starting, const float* z, const void* packed, void* workspace, int64_t B, int64_t N,
-                       uint32_t* status, void* stream) {
-  if (!dims_ok(B, 65535) || !dims_ok(N, 65535)) return fail(GTK_ERR_INVALID_ARG, "triatt_project: bad B/N");
+int gtk_triatt_project(int starting, const float* z, const void* packed, void* workspace, int64_t B, int64_t rows,
+                       int64_t N, int64_t row0, uint32_t* status, void* stream) {
+  if (int e = rows_check("triatt_project", starting, B, rows, N, row0)) return e;
   if (int e = check_ptr(z, "z")) return e;
   if (int e = check_ptr(packed, "packed", 256)) return e;
   if (int e = check_ptr(workspace, "workspace", 256)) return e;
   if (int e = check_device()) return e;
-  const TriattWs w = triatt_layout(B, N);
+  const TriattWs w = triatt_layout(B, rows, N);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   const uint8_t* pk = static_cast<const uint8_t*>(packed);
   const int64_t n_jt = (N + 127) / 128;
-  const int64_t n_tiles = B * N * n_jt;
+  const int64_t n_tiles = B * rows * n_jt;
   if (n_tiles > 2147483647) return fail(GTK_ERR_INVALID_ARG, "triatt_project: too many tiles");
   CUtensorMap wm, zm;
   if (int e = make_weight_map(&wm, pk + tapack::kW3, 512, 128)) return e;
-  if (int e = make_pair_map(&zm, z, B, N, N, !starting)) return e;
+  if (int e = make_pair_map(&zm, z, B, rows, N, !starting)) return e;
   if (int e = ensure_smem(reinterpret_cast<const void*>(triatt_project_kernel), k3::kSmem)) return e;
   const int grid = static_cast<int>(n_tiles < num_sms() ? n_tiles : num_sms());
   triatt_project_kernel<<<grid, k3::kThreads, k3::kSmem, static_cast<cudaStream_t>(stream)>>>(
       wm, zm, reinterpret_cast<const float*>(pk + tapack::kVec), reinterpret_cast<__half*>(ws + w.q),
       reinterpret_cast<__half*>(ws + w.k), reinterpret_cast<__half*>(ws + w.v), reinterpret_cast<__half*>(ws + w.g),
-      reinterpret_cast<__nv_bfloat16*>(ws + w.bias), static_cast<int>(N), static_cast<int>(round_up(N, 8)),
-      static_cast<int>(n_jt), static_cast<int>(n_tiles), status);
+      reinterpret_cast<__nv_bfloat16*>(ws + w.bias), static_cast<int>(N), static_cast<int>(rows),
+      static_cast<int>(B), static_cast<int>(row0), static_cast<int>(round_up(N, 8)), static_cast<int>(n_jt),
+      static_cast<int>(n_tiles), status);
   return check_launch("triatt_project_kernel");
 }
 
-int gtk_triatt_core(int starting, const float* mask, void* workspace, int64_t B, int64_t N, float inf,
-                    uint32_t* status, void* stream) {
-  if (!dims_ok(B, 65535) || !dims_ok(N, 65535)) return fail(GTK_ERR_INVALID_ARG, "triatt_core: bad B/N");
+int gtk_triatt_core(int starting, const float* mask, void* workspace, int64_t B, int64_t rows, int64_t N,
+                    int64_t row0, float inf, uint32_t* status, void* stream) {
+  if (int e = rows_check("triatt_core", starting, B, rows, N, row0)) return e;
   if (int e = check_ptr(workspace, "workspace", 256)) return e;
   if (mask && (reinterpret_cast<uintptr_t>(mask) & 3)) return fail(GTK_ERR_ALIGNMENT, "mask is misaligned");
   if (int e = check_device()) return e;
-  const TriattWs w = triatt_layout(B, N);
+  const TriattWs w = triatt_layout(B, rows, N);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   CUtensorMap qm, km, vm, bm;
-  if (int e = make_head_map(&qm, ws + w.q, B, N)) return e;
-  if (int e = make_head_map(&km, ws + w.k, B, N)) return e;
-  if (int e = make_head_map(&vm, ws + w.v, B, N)) return e;
+  if (int e = make_head_map(&qm, ws + w.q, B * rows, N)) return e;
+  if (int e = make_head_map(&km, ws + w.k, B * rows, N)) return e;
+  if (int e = make_head_map(&vm, ws + w.v, B * rows, N)) return e;
   if (int e = make_bias_map(&bm, ws + w.bias, B, N)) return e;
   if (int e = ensure_smem(reinterpret_cast<const void*>(triatt_core_kernel), k4::kSmem)) return e;
   {
@@ -1183,41 +1206,43 @@ int gtk_triatt_core(int starting, const float* mask, void* workspace, int64_t B,
                                     " registers/thread; its register split needs " +
                                     std::to_string(k4::kLaunchRegs));
   }
-  const int n_ig = static_cast<int>((N + k4::kR - 1) / k4::kR);
-  if (static_cast<int64_t>(B) * n_ig > 2147483647) return fail(GTK_ERR_INVALID_ARG, "triatt_core: grid too large");
+  const int n_ig = static_cast<int>((rows + k4::kR - 1) / k4::kR);
+  if (static_cast<int64_t>(B) * n_ig > 65535) return fail(GTK_ERR_INVALID_ARG, "triatt_core: grid too large");
   dim3 grid(static_cast<unsigned>((N + 127) / 128), kHeads, static_cast<unsigned>(B * n_ig));
+  // the mask is the whole problem's [B][N][N]; a shard's rows start at row row0
   const int64_t si = starting ? N : 1, sk = starting ? 1 : N;
+  const float* mrow0 = mask ? mask + row0 * si : nullptr;
   triatt_core_kernel<<<grid, k4::kThreads, k4::kSmem, static_cast<cudaStream_t>(stream)>>>(
-      qm, km, vm, bm, mask, si, sk, inf * kLog2e, reinterpret_cast<const __half*>(ws + w.g),
-      reinterpret_cast<__half*>(ws + w.og), static_cast<int>(N), n_ig, status);
+      qm, km, vm, bm, mrow0, N * N, si, sk, inf * kLog2e, reinterpret_cast<const __half*>(ws + w.g),
+      reinterpret_cast<__half*>(ws + w.og), static_cast<int>(N), static_cast<int>(rows), n_ig, status);
   return check_launch("triatt_core_kernel");
 }
 
 int gtk_triatt_finish(int starting, const float* z, const void* packed, void* workspace, float* out, int add_residual,
-                      int64_t B, int64_t N, uint32_t* status, void* stream) {
-  if (!dims_ok(B, 65535) || !dims_ok(N, 65535)) return fail(GTK_ERR_INVALID_ARG, "triatt_finish: bad B/N");
+                      int64_t B, int64_t rows, int64_t N, uint32_t* status, void* stream) {
+  if (int e = rows_check("triatt_finish", starting, B, rows, N, 0)) return e;
   if (int e = check_ptr(out, "out")) return e;
   if (add_residual)
     if (int e = check_ptr(z, "z")) return e;
   if (int e = check_ptr(packed, "packed", 256)) return e;
   if (int e = check_ptr(workspace, "workspace", 256)) return e;
   if (int e = check_device()) return e;
-  const TriattWs w = triatt_layout(B, N);
+  const TriattWs w = triatt_layout(B, rows, N);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   const uint8_t* pk = static_cast<const uint8_t*>(packed);
   const int64_t n_jt = (N + 127) / 128;
-  const int64_t n_tiles = B * N * n_jt;
+  const int64_t n_tiles = B * rows * n_jt;
   if (n_tiles > 2147483647) return fail(GTK_ERR_INVALID_ARG, "triatt_finish: too many tiles");
   CUtensorMap am, wm, zm, om;
-  if (int e = make_hidden_map(&am, ws + w.og, B, N)) return e;
+  if (int e = make_hidden_map(&am, ws + w.og, B * rows, N)) return e;
   if (int e = make_weight_map(&wm, pk + tapack::kW4, 128, 128)) return e;
-  if (int e = make_pair_map(&zm, add_residual ? z : out, B, N, N, !starting)) return e;
-  if (int e = make_pair_map(&om, out, B, N, N, !starting)) return e;
+  if (int e = make_pair_map(&zm, add_residual ? z : out, B, rows, N, !starting)) return e;
+  if (int e = make_pair_map(&om, out, B, rows, N, !starting)) return e;
   if (int e = ensure_smem(reinterpret_cast<const void*>(triatt_finish_kernel), k4e::kSmem)) return e;
   const int grid = static_cast<int>(n_tiles < num_sms() ? n_tiles : num_sms());
   triatt_finish_kernel<<<grid, k4e::kThreads, k4e::kSmem, static_cast<cudaStream_t>(stream)>>>(
-      am, wm, zm, om, reinterpret_cast<const float*>(pk + tapack::kVec), static_cast<int>(N), add_residual,
-      static_cast<int>(n_jt), static_cast<int>(n_tiles), status);
+      am, wm, zm, om, reinterpret_cast<const float*>(pk + tapack::kVec), static_cast<int>(N), static_cast<int>(rows),
+      add_residual, static_cast<int>(n_jt), static_cast<int>(n_tiles), status);
   return check_launch("triatt_finish_kernel");
 }
 
@@ -1226,10 +1251,10 @@ int gtk_triatt_forward(int starting, const float* z, const float* mask, const vo
                        int c_hidden, int heads, float inf, uint32_t* status, void* stream) {
   if (int e = triatt_check(c_in, c_hidden, heads)) return e;
   if (!dims_ok(B, 65535) || !dims_ok(N, 65535)) return fail(GTK_ERR_INVALID_ARG, "triatt: bad B/N");
-  if (workspace_bytes < triatt_layout(B, N).total) return fail(GTK_ERR_WORKSPACE, "triatt: workspace too small");
-  if (int e = gtk_triatt_project(starting, z, packed, workspace, B, N, status, stream)) return e;
-  if (int e = gtk_triatt_core(starting, mask, workspace, B, N, inf, status, stream)) return e;
-  return gtk_triatt_finish(starting, z, packed, workspace, out, add_residual, B, N, status, stream);
+  if (workspace_bytes < triatt_layout(B, N, N).total) return fail(GTK_ERR_WORKSPACE, "triatt: workspace too small");
+  if (int e = gtk_triatt_project(starting, z, packed, workspace, B, N, N, 0, status, stream)) return e;
+  if (int e = gtk_triatt_core(starting, mask, workspace, B, N, N, 0, inf, status, stream)) return e;
+  return gtk_triatt_finish(starting, z, packed, workspace, out, add_residual, B, N, N, status, stream);
 }
 
 }  // extern "C"

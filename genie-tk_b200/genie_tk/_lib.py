@@ -60,10 +60,12 @@ _SIGNATURES = {
     "gtk_triatt_workspace_bytes": (c_size, [c_i64, c_i64, c_int, c_int, c_int]),
     "gtk_triatt_forward": (c_int, [c_int, c_vp, c_vp, c_vp, c_vp, c_int, c_vp, c_size, c_i64, c_i64, c_int, c_int,
                                    c_int, ctypes.c_float, c_vp, c_vp]),
-    "gtk_triatt_project": (c_int, [c_int, c_vp, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp]),
-    "gtk_triatt_core": (c_int, [c_int, c_vp, c_vp, c_i64, c_i64, ctypes.c_float, c_vp, c_vp]),
-    "gtk_triatt_finish": (c_int, [c_int, c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_vp, c_vp]),
-    "gtk_triatt_workspace_offsets": (c_int, [c_i64, c_i64, ctypes.POINTER(c_i64)]),
+    "gtk_triatt_project": (c_int, [c_int, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp]),
+    "gtk_triatt_core": (c_int, [c_int, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, ctypes.c_float, c_vp, c_vp]),
+    "gtk_triatt_finish": (c_int, [c_int, c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_i64, c_vp, c_vp]),
+    "gtk_triatt_workspace_offsets": (c_int, [c_i64, c_i64, c_i64, ctypes.POINTER(c_i64)]),
+    "gtk_copy_2d": (c_int, [c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_vp]),
+    "gtk_pair_transpose_pack": (c_int, [c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp]),
 }
 
 

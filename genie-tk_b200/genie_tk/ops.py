@@ -231,53 +231,63 @@ def triatt_forward(z: torch.Tensor, mask: Optional[torch.Tensor], packed: torch.
     return out
 
 
-def triatt_workspace(B: int, N: int, device: torch.device):
-    """The forward workspace and the byte offsets of q, k, v, g, og, bias inside it."""
+def triatt_workspace(B: int, N: int, device: torch.device, rows: Optional[int] = None):
+    """A stage workspace for ``rows`` problem rows (default all N) and the byte offsets of
+    q, k, v, g, og, bias inside it."""
     lib = _lib.load()
-    nbytes = lib.gtk_triatt_workspace_bytes(B, N, SUPPORTED_C, SUPPORTED_C, SUPPORTED_HEADS)
-    offs = (ctypes.c_int64 * 6)()
-    _lib.check(lib.gtk_triatt_workspace_offsets(B, N, offs), "gtk_triatt_workspace_offsets")
-    ws = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    rows = N if rows is None else rows
+    offs = (ctypes.c_int64 * 7)()
+    _lib.check(lib.gtk_triatt_workspace_offsets(B, rows, N, offs), "gtk_triatt_workspace_offsets")
+    ws = torch.empty(int(offs[6]), dtype=torch.uint8, device=device)
     return ws, {k: int(offs[n]) for n, k in enumerate(("q", "k", "v", "g", "og", "bias"))}
 
 
-def triatt_stage_views(ws: torch.Tensor, offs, B: int, N: int):
+def triatt_stage_views(ws: torch.Tensor, offs, B: int, N: int, rows: Optional[int] = None):
     """Views of the attention intermediates inside a workspace (problem orientation): q, k, v,
-    g, og fp16; the triangle bias bf16."""
+    g, og fp16 over the ``rows`` local rows; the triangle bias bf16 over all N rows, viewed
+    as [B, H, N, ldn] (it is stored [N][B][H][ldn])."""
+    rows = N if rows is None else rows
+
     def view(name, nelem, shape, dtype=torch.float16):
         o = offs[name]
         return ws[o:o + 2 * nelem].view(dtype).view(*shape)
     H, d = SUPPORTED_HEADS, SUPPORTED_C // SUPPORTED_HEADS
     ldn = plane_pitch(N)
     return {
-        "q": view("q", B * N * H * N * d, (B, N, H, N, d)),
-        "k": view("k", B * N * H * N * d, (B, N, H, N, d)),
-        "v": view("v", B * N * H * N * d, (B, N, H, N, d)),
-        "g": view("g", B * N * N * SUPPORTED_C, (B, N, N, SUPPORTED_C)),
-        "og": view("og", B * N * N * SUPPORTED_C, (B, N, N, SUPPORTED_C)),
-        "bias": view("bias", B * H * N * ldn, (B, H, N, ldn), torch.bfloat16),
+        "q": view("q", B * rows * H * N * d, (B, rows, H, N, d)),
+        "k": view("k", B * rows * H * N * d, (B, rows, H, N, d)),
+        "v": view("v", B * rows * H * N * d, (B, rows, H, N, d)),
+        "g": view("g", B * rows * N * SUPPORTED_C, (B, rows, N, SUPPORTED_C)),
+        "og": view("og", B * rows * N * SUPPORTED_C, (B, rows, N, SUPPORTED_C)),
+        "bias": view("bias", N * B * H * ldn, (N, B, H, ldn), torch.bfloat16).permute(1, 2, 0, 3),
     }
 
 
-def triatt_project(z: torch.Tensor, packed: torch.Tensor, starting: bool, ws: torch.Tensor) -> None:
+def triatt_project(z: torch.Tensor, packed: torch.Tensor, starting: bool, ws: torch.Tensor, N: Optional[int] = None,
+                   row0: int = 0) -> None:
+    """q, k, v, g and the triangle-bias rows of the pair rows in ``z`` ([B, rows, N, 128];
+    rows = N unless ``z`` is one shard of a row-sharded pair tensor starting at ``row0``)."""
     lib = _lib.load()
     _require_cuda(z, "z", torch.float32)
-    B, N = z.shape[0], z.shape[1]
-    _lib.check(lib.gtk_triatt_project(int(starting), _ptr(z), _ptr(packed), _ptr(ws), B, N,
+    B, R = z.shape[0], z.shape[1]
+    N = z.shape[2] if N is None else N
+    _lib.check(lib.gtk_triatt_project(int(starting), _ptr(z), _ptr(packed), _ptr(ws), B, R, N, row0,
                                       _ptr(status_buffer(z.device)), _stream(z.device)), "gtk_triatt_project")
 
 
 def triatt_core(mask: Optional[torch.Tensor], starting: bool, ws: torch.Tensor, B: int, N: int,
-                inf: float = 1e9) -> None:
+                inf: float = 1e9, rows: Optional[int] = None, row0: int = 0) -> None:
     lib = _lib.load()
-    _lib.check(lib.gtk_triatt_core(int(starting), _ptr(mask), _ptr(ws), B, N, float(inf),
+    rows = N if rows is None else rows
+    _lib.check(lib.gtk_triatt_core(int(starting), _ptr(mask), _ptr(ws), B, rows, N, row0, float(inf),
                                    _ptr(status_buffer(ws.device)), _stream(ws.device)), "gtk_triatt_core")
 
 
 def triatt_finish(z: Optional[torch.Tensor], packed: torch.Tensor, starting: bool, ws: torch.Tensor,
                   out: torch.Tensor, add_residual: bool = False) -> torch.Tensor:
     lib = _lib.load()
-    B, N = out.shape[0], out.shape[1]
+    B, R, N = out.shape[0], out.shape[1], out.shape[2]
     _lib.check(lib.gtk_triatt_finish(int(starting), _ptr(z), _ptr(packed), _ptr(ws), _ptr(out), int(add_residual), B,
-                                     N, _ptr(status_buffer(out.device)), _stream(out.device)), "gtk_triatt_finish")
+                                     R, N, _ptr(status_buffer(out.device)), _stream(out.device)),
+               "gtk_triatt_finish")
     return out

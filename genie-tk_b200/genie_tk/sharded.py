@@ -1,0 +1,352 @@
+"""Row-sharded triangle pair stack: the pair tensor [B, N, N, 128] split over its first
+pair index i across P ranks (one process per GPU), R = N / P rows per rank.
+
+Each op needs one exchange between the ranks; the kernels run on local data only and
+every exchange goes through the collective into local memory first:
+
+  TriMulOut   x[i,j] = sum_k a[i,k] b[j,k]: project the local rows, all-gather the b planes
+              (every rank needs all rows j), contract local rows i against all j, finish.
+  TriMulIn    x[i,j] = sum_k a[k,i] b[k,j]: project the local rows k; an all-to-all gives
+              each rank the columns i it owns of every row k of a (column slices packed
+              with gtk_copy_2d); the b planes are all-gathered; contract; finish.
+  TriAttStart local rows i; the triangle bias bias[h, j, k] is needed for all rows j, so
+              each rank computes its rows and the bias region is all-gathered.
+  TriAttEnd   End(z) = Start(z^T)^T with the mask transposed: an all-to-all transpose
+              (gtk_pair_transpose_pack + gtk_copy_2d) turns the row shard into the shard of
+              z^T, the starting-node stages run on it with the residual added in place,
+              and the same transpose brings the updated shard back.
+
+The per-rank program is a generator that yields its collectives (``("all_gather", out,
+inp)`` / ``("all_to_all", out, inp)`` on uint8 views), so the same code runs on real
+ranks (``forward_`` with ``torch.distributed``: NCCL on GPUs) and on P ranks emulated in
+one process (``run_emulated``, used to check the sharding on a single device). The stage
+computations go through a ``stage_ops`` object; the default, ``CudaStageOps``, calls the
+library's kernels, and there is no CPU implementation in this package.
+
+The reference has no multi-GPU path (its modules run on one device); this follows the
+row sharding of the pair stack over i with all-gather / all-to-all exchanges.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Dict, Generator, List, Optional, Tuple
+
+import torch
+from torch import Tensor
+
+from . import ops
+from .stack import OP_NAMES, TrianglePairStack
+
+C = 128
+H = 4
+PAIR_BYTES = C * 4
+
+Request = Tuple[str, Tensor, Tensor]
+
+
+class ShardSpec:
+    """Rows owned by ``rank`` out of ``world`` for a [B, N, N, 128] pair tensor."""
+
+    def __init__(self, B: int, N: int, world: int, rank: int):
+        if world < 1 or not 0 <= rank < world:
+            raise ValueError(f"bad world/rank {world}/{rank}")
+        if N % world:
+            raise ValueError(f"N = {N} is not divisible by the {world} ranks")
+        R = N // world
+        if R % 8:
+            raise ValueError(f"rows per rank N / P = {R} must be a multiple of 8 (16-byte plane slices)")
+        self.B, self.N, self.P, self.rank = B, N, world, rank
+        self.R = R
+        self.row0 = rank * R
+
+    def rows(self) -> slice:
+        return slice(self.row0, self.row0 + self.R)
+
+
+class CudaStageOps:
+    """The stage computations on this rank's GPU, through the C ABI."""
+
+    def __init__(self, device: torch.device):
+        self.device = device
+        self.lib = ops._lib.load()
+        self.status = ops.status_buffer(device)
+
+    def alloc(self, nbytes: int) -> Tensor:
+        return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=self.device)
+
+    def _s(self):
+        return ops._stream(self.device)
+
+    def _chk(self, rc, what):
+        ops._lib.check(rc, what)
+
+    def trimul_project(self, mod, z, mask, a, b, B, rows, N):
+        P = ops._ptr
+        self._chk(self.lib.gtk_trimul_project(P(z), P(mask), P(mod.packed_weights(self.device)), P(a), P(b), N, B,
+                                              rows, N, P(self.status), self._s()), "gtk_trimul_project")
+
+    def trimul_contract(self, outgoing, a, b, x, B, M, Nj, K, lda, ldb, ldx, xs):
+        P = ops._ptr
+        self._chk(self.lib.gtk_trimul_contract(int(outgoing), P(a), P(b), P(x), B, C, M, Nj, K, lda, ldb, ldx, xs,
+                                               P(self.status), self._s()), "gtk_trimul_contract")
+
+    def trimul_finish(self, mod, z, x, ldx, xs, B, rows, N, out):
+        P = ops._ptr
+        self._chk(self.lib.gtk_trimul_finish(P(z), P(x), ldx, xs, P(mod.packed_weights(self.device)), P(out), 1, B,
+                                             rows, N, P(self.status), self._s()), "gtk_trimul_finish")
+
+    def triatt_project(self, mod, z, ws, B, rows, N, row0):
+        P = ops._ptr
+        self._chk(self.lib.gtk_triatt_project(1, P(z), P(mod.packed_weights(self.device)), P(ws), B, rows, N, row0,
+                                              P(self.status), self._s()), "gtk_triatt_project")
+
+    def triatt_core(self, mod, mask, ws, B, rows, N, row0):
+        P = ops._ptr
+        self._chk(self.lib.gtk_triatt_core(1, P(mask), P(ws), B, rows, N, row0, float(mod.inf), P(self.status),
+                                           self._s()), "gtk_triatt_core")
+
+    def triatt_finish(self, mod, z, ws, B, rows, N):
+        P = ops._ptr
+        self._chk(self.lib.gtk_triatt_finish(1, P(z), P(mod.packed_weights(self.device)), P(ws), P(z), 1, B, rows,
+                                             N, P(self.status), self._s()), "gtk_triatt_finish")
+
+    def copy_2d(self, dst, dpitch, src, spitch, width, height):
+        self._chk(self.lib.gtk_copy_2d(ops._ptr(dst), dpitch, ops._ptr(src), spitch, width, height, self._s()),
+                  "gtk_copy_2d")
+
+    def pair_transpose_pack(self, src, dst, B, R, Cn, P):
+        self._chk(self.lib.gtk_pair_transpose_pack(ops._ptr(src), ops._ptr(dst), B, R, Cn, P, self._s()),
+                  "gtk_pair_transpose_pack")
+
+    def triatt_layout(self, B, rows, N) -> Dict[str, int]:
+        offs = (ctypes.c_int64 * 7)()
+        self._chk(self.lib.gtk_triatt_workspace_offsets(B, rows, N, offs), "gtk_triatt_workspace_offsets")
+        return {k: int(offs[n]) for n, k in enumerate(("q", "k", "v", "g", "og", "bias", "total"))}
+
+
+def _round256(n: int) -> int:
+    return (int(n) + 255) // 256 * 256
+
+
+class ShardedTrianglePairStack:
+    """One rank's share of a :class:`TrianglePairStack` whose pair tensor is row-sharded.
+
+    ``forward_(z_local, mask)`` updates this rank's rows ``z_local`` [B, N/P, N, 128] (fp32)
+    in place; ``mask`` is the whole [B, N, N] mask (or None), identical on every rank.
+    """
+
+    def __init__(self, stack: TrianglePairStack, world: int, rank: int, stage_ops=None):
+        self.stack = stack
+        self.world, self.rank = world, rank
+        self.stage_ops = stage_ops
+        self._key = None
+        self._buf: Dict[str, Tensor] = {}
+
+    # ---------------------------------------------------------------- buffers
+    def prepare(self, B: int, N: int, device: torch.device) -> ShardSpec:
+        spec = ShardSpec(B, N, self.world, self.rank)
+        if self.stage_ops is None:
+            self.stage_ops = CudaStageOps(device)
+        if self._key == (B, N):
+            return spec
+        so = self.stage_ops
+        R = spec.R
+        plane = B * R * C * N * 2          # local a / b / x planes, fp16, pitch N
+        lay = so.triatt_layout(B, R, N)
+        bias_rows = R * B * H * N * 2      # this rank's rows of the bias region
+        pair_loc = B * R * N * PAIR_BYTES  # one row shard of the pair tensor, fp32
+        sizes = {
+            "a": plane, "b": plane, "x": plane,
+            "a_send": plane, "a_recv": plane,          # [P][B][R][C][R] chunks / [B][N][C][R]
+            "b_all": B * N * C * N * 2,                # gathered b planes [B][N][C][N]
+            "tri": lay["total"], "bias_send": bias_rows,
+            "zT": pair_loc, "t_send": pair_loc, "t_recv": pair_loc,
+        }
+        self._buf = {k: so.alloc(_round256(v)) for k, v in sizes.items()}
+        self._lay = lay
+        self._key = (B, N)
+        if hasattr(self.stack, "layers"):
+            for layer in self.stack.layers:
+                for name in OP_NAMES:
+                    mod = getattr(layer, name)
+                    if hasattr(mod, "packed_weights") and isinstance(so, CudaStageOps):
+                        mod.packed_weights(device)
+        return spec
+
+    # ---------------------------------------------------------------- the per-rank program
+    def steps(self, z: Tensor, mask: Optional[Tensor], z_in: Optional[Tensor] = None
+              ) -> Generator[Request, None, None]:
+        """This rank's stack as a generator of collective requests (see module docstring).
+        ``z`` is updated in place; with ``z_in`` the first block reads ``z_in`` instead and
+        writes ``z`` (``z_in`` is left unchanged)."""
+        B, R, N = z.shape[0], z.shape[1], z.shape[2]
+        src = z if z_in is None else z_in
+        spec = self.prepare(B, N, z.device)
+        if R != spec.R:
+            raise ValueError(f"z_local has {R} rows; rank {self.rank} of {self.world} owns {spec.R}")
+        so, buf, lay = self.stage_ops, self._buf, self._lay
+        P, row0 = self.world, spec.row0
+        mask_loc = mask_t = None
+        if mask is not None:
+            mask_loc = mask[:, spec.rows()].contiguous()
+            mask_t = mask.transpose(1, 2).contiguous()
+        xs = 1.0 / N
+        plane_b = R * C * N * 2            # bytes of one batch element's local planes
+        chunk_a = R * C * R * 2            # a column slice for one peer, one batch element
+        tri = buf["tri"]
+        bias_all = tri[lay["bias"]:lay["bias"] + N * B * H * N * 2]
+        bias_mine = bias_all[row0 * B * H * N * 2:(row0 + R) * B * H * N * 2]
+        pair_chunk = B * R * R * PAIR_BYTES  # one peer's chunk of a pair-grid transpose
+        zT = buf["zT"][:B * R * N * PAIR_BYTES].view(torch.float32).view(B, R, N, C)
+        t_send, t_recv = buf["t_send"], buf["t_recv"]
+
+        def gather_b(b_planes):
+            for bb in range(B):
+                yield ("all_gather", buf["b_all"][bb * N * C * N * 2:(bb + 1) * N * C * N * 2],
+                       b_planes[bb * plane_b:(bb + 1) * plane_b])
+
+        def attention(mod, zz, mm):
+            so.triatt_project(mod, zz, tri, B, R, N, row0)
+            so.copy_2d(buf["bias_send"], bias_mine.numel(), bias_mine, bias_mine.numel(), bias_mine.numel(), 1)
+            yield ("all_gather", bias_all, buf["bias_send"][:bias_mine.numel()])
+            so.triatt_core(mod, mm, tri, B, R, N, row0)
+            so.triatt_finish(mod, zz, tri, B, R, N)
+
+        def transpose(src, dst):
+            # dst = the transposed shard of the pair grid whose row shard is src
+            so.pair_transpose_pack(src, t_send, B, R, N, P)
+            yield ("all_to_all", t_recv[:P * pair_chunk], t_send[:P * pair_chunk])
+            for p in range(P):
+                so.copy_2d(_bytes(dst)[p * R * PAIR_BYTES:], N * PAIR_BYTES, t_recv[p * pair_chunk:],
+                           R * PAIR_BYTES, R * PAIR_BYTES, B * R)
+
+        for layer in self.stack.layers:
+            # ---- TriMulOut
+            mod = layer.tri_mul_out
+            so.trimul_project(mod, src, mask_loc, buf["a"], buf["b"], B, R, N)
+            yield from gather_b(buf["b"])
+            so.trimul_contract(True, buf["a"], buf["b_all"], buf["x"], B, R, N, N, N, N, N, xs)
+            so.trimul_finish(mod, src, buf["x"], N, xs, B, R, N, z)
+            src = z
+            # ---- TriMulIn
+            mod = layer.tri_mul_in
+            so.trimul_project(mod, z, mask_loc, buf["a"], buf["b"], B, R, N)
+            for bb in range(B):
+                for q in range(P):  # columns i of peer q, every local row k and channel
+                    so.copy_2d(buf["a_send"][q * chunk_a:], R * 2, buf["a"][bb * plane_b + q * R * 2:], N * 2,
+                               R * 2, R * C)
+                yield ("all_to_all", buf["a_recv"][bb * P * chunk_a:(bb + 1) * P * chunk_a],
+                       buf["a_send"][:P * chunk_a])
+            yield from gather_b(buf["b"])
+            so.trimul_contract(False, buf["a_recv"], buf["b_all"], buf["x"], B, R, N, N, R, N, N, xs)
+            so.trimul_finish(mod, z, buf["x"], N, xs, B, R, N, z)
+            # ---- TriAttStart
+            yield from attention(layer.tri_att_start, z, mask)
+            # ---- TriAttEnd = Start(z^T, mask^T)^T, the residual added on the transposed shard
+            yield from transpose(z, zT)
+            yield from attention(layer.tri_att_end, zT, mask_t)
+            yield from transpose(zT, z)
+
+    # ---------------------------------------------------------------- runners
+    @torch.no_grad()
+    def forward_(self, z_local: Tensor, mask: Optional[Tensor] = None, group=None,
+                 z_in: Optional[Tensor] = None, hook=None) -> Tensor:
+        """Run this rank's share of the stack in place on ``z_local`` (reading ``z_in`` in
+        the first block when given); collectives over ``group``. ``hook(label)`` is called
+        before and after (label "end") every collective."""
+        import torch.distributed as dist
+        if dist.get_world_size(group) != self.world or dist.get_rank(group) != self.rank:
+            raise RuntimeError("ShardedTrianglePairStack: world/rank differ from the process group")
+        _check_local(z_local, mask)
+        if z_in is not None:
+            _check_local(z_in, mask)
+        h = hook or (lambda label: None)
+        for kind, out, inp in self.steps(z_local, mask, z_in):
+            h("nccl_" + kind)
+            if kind == "all_gather":
+                dist.all_gather_into_tensor(out, inp, group=group)
+            elif kind == "all_to_all":
+                dist.all_to_all_single(out, inp, group=group)
+            else:
+                raise RuntimeError(f"unknown collective {kind}")
+            h("end")
+        return z_local
+
+
+class TimedStageOps:
+    """Wraps a stage-ops object and calls ``hook(name)`` before and ``hook("end")`` after
+    every stage call (per-kernel timing with events) and counts the kernel launches."""
+
+    KERNELS = ("trimul_project", "trimul_contract", "trimul_finish", "triatt_project", "triatt_core",
+               "triatt_finish", "copy_2d", "pair_transpose_pack")
+
+    def __init__(self, inner, hook=None):
+        self.inner = inner
+        self.hook = hook
+        self.launches = 0
+
+    def __getattr__(self, name):
+        fn = getattr(self.inner, name)
+        if name not in self.KERNELS:
+            return fn
+
+        def wrapped(*a, **k):
+            self.launches += 1
+            if self.hook:
+                self.hook(name)
+            r = fn(*a, **k)
+            if self.hook:
+                self.hook("end")
+            return r
+        return wrapped
+
+
+def _bytes(t: Tensor) -> Tensor:
+    return t.view(-1).view(torch.uint8)
+
+
+def _check_local(z: Tensor, mask: Optional[Tensor]) -> None:
+    if not (z.dtype == torch.float32 and z.is_contiguous() and z.dim() == 4 and z.shape[-1] == C):
+        raise RuntimeError("z_local must be a contiguous fp32 [B, N/P, N, 128] tensor")
+    if mask is not None and (mask.dtype != torch.float32 or tuple(mask.shape) != (z.shape[0], z.shape[2], z.shape[2])):
+        raise RuntimeError("mask must be the whole fp32 [B, N, N] mask")
+
+
+@torch.no_grad()
+def run_emulated(shards: List[ShardedTrianglePairStack], z_locals: List[Tensor], mask: Optional[Tensor],
+                 z_ins: Optional[List[Tensor]] = None) -> None:
+    """Run P ranks' programs in one process, in lockstep, performing each collective by
+    copying between the ranks' buffers (all on one device). Updates ``z_locals`` in place
+    (reading ``z_ins`` in the first block when given)."""
+    for z in z_locals:
+        _check_local(z, mask)
+    z_ins = z_ins or [None] * len(z_locals)
+    _drive([s.steps(z, mask, zi) for s, z, zi in zip(shards, z_locals, z_ins)], len(shards))
+
+
+def _drive(gens, P: int) -> None:
+    """Step P rank generators in lockstep; every round all of them must request the same
+    collective, which is then carried out by copies."""
+    while True:
+        reqs = []
+        for g in gens:
+            try:
+                reqs.append(next(g))
+            except StopIteration:
+                reqs.append(None)
+        if all(r is None for r in reqs):
+            return
+        if any(r is None for r in reqs) or len({r[0] for r in reqs}) != 1:
+            raise RuntimeError("ranks diverged: " + str([None if r is None else r[0] for r in reqs]))
+        kind = reqs[0][0]
+        if kind == "all_gather":
+            ins = [r[2].clone() for r in reqs]
+            for r in reqs:
+                r[1].copy_(torch.cat(ins))
+        elif kind == "all_to_all":
+            chunks = [r[2].clone().chunk(P) for r in reqs]
+            for q, r in enumerate(reqs):
+                r[1].copy_(torch.cat([chunks[p][q] for p in range(P)]))
+        else:
+            raise RuntimeError(f"unknown collective {kind}")

@@ -101,14 +101,14 @@ class TrianglePairStack(nn.Module):
                 else:
                     starting = name == "tri_att_start"
                     h("triatt_project")
-                    ops._lib.check(lib.gtk_triatt_project(int(starting), P(src), P(packed), P(ws), B, N, P(st),
-                                                          stream), "gtk_triatt_project")
+                    ops._lib.check(lib.gtk_triatt_project(int(starting), P(src), P(packed), P(ws), B, N, N, 0,
+                                                          P(st), stream), "gtk_triatt_project")
                     h("triatt_core")
-                    ops._lib.check(lib.gtk_triatt_core(int(starting), P(mask), P(ws), B, N, float(mod.inf), P(st),
-                                                       stream), "gtk_triatt_core")
+                    ops._lib.check(lib.gtk_triatt_core(int(starting), P(mask), P(ws), B, N, N, 0, float(mod.inf),
+                                                       P(st), stream), "gtk_triatt_core")
                     h("triatt_finish")
                     ops._lib.check(lib.gtk_triatt_finish(int(starting), P(src), P(packed), P(ws), P(z), 1, B, N,
-                                                         P(st), stream), "gtk_triatt_finish")
+                                                         N, P(st), stream), "gtk_triatt_finish")
                     h("end")
                 src = z
 

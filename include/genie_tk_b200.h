@@ -191,18 +191,48 @@ GTK_API int gtk_triatt_forward(int starting, const float* z, const float* mask, 
                                int add_residual, void* workspace, size_t workspace_bytes, int64_t B, int64_t N,
                                int c_in, int c_hidden, int heads, float inf, uint32_t* status, void* stream);
 
-/* Stage entry points over the forward workspace. offsets[6] receives the byte offsets of
- * q, k, v ([B*N][H][N][32] fp16, q scaled by log2(e)/sqrt(32)), g ([B*N*N][128] fp16,
- * sigmoid applied), og ([B*N*N][128] fp16, gated attention output) and the triangle bias
- * ([B][H][N][round_up(N,8)] bf16, in log2 units). All in the orientation of the problem
+/* Stage entry points over a workspace, for `rows` problem rows starting at global row `row0`
+ * (rows = N, row0 = 0 for a whole pair tensor; a shard of a row-sharded pair tensor
+ * otherwise, starting orientation only: a row-sharded caller runs the ending node as the
+ * starting node of the transposed shards). offsets[7] receives the byte offsets of
+ *   q, k, v  [B*rows][H][N][32] fp16 (q scaled by log2(e)/sqrt(32)),
+ *   g        [B*rows*N][128] fp16 (sigmoid applied),
+ *   og       [B*rows*N][128] fp16 (gated attention output),
+ *   bias     [N][B][H][round_up(N,8)] bf16 (the triangle bias, log2 units, ALL N rows:
+ *            project writes rows row0..row0+rows-1; the core reads every row, so a
+ *            row-sharded caller all-gathers this region in place between the two),
+ * and offsets[6] the workspace size in bytes. All in the orientation of the problem
  * (z^T for the ending node). */
-GTK_API int gtk_triatt_workspace_offsets(int64_t B, int64_t N, int64_t* offsets);
+GTK_API int gtk_triatt_workspace_offsets(int64_t B, int64_t rows, int64_t N, int64_t* offsets);
+/* z: the shard's rows [B, rows, N, 128] fp32. */
 GTK_API int gtk_triatt_project(int starting, const float* z, const void* packed, void* workspace, int64_t B,
-                               int64_t N, uint32_t* status, void* stream);
-GTK_API int gtk_triatt_core(int starting, const float* mask, void* workspace, int64_t B, int64_t N, float inf,
-                            uint32_t* status, void* stream);
+                               int64_t rows, int64_t N, int64_t row0, uint32_t* status, void* stream);
+/* mask: the WHOLE problem's [B, N, N] fp32 (or NULL); the shard's rows start at row0. */
+GTK_API int gtk_triatt_core(int starting, const float* mask, void* workspace, int64_t B, int64_t rows, int64_t N,
+                            int64_t row0, float inf, uint32_t* status, void* stream);
+/* z, out: the shard's rows [B, rows, N, 128] fp32. */
 GTK_API int gtk_triatt_finish(int starting, const float* z, const void* packed, void* workspace, float* out,
-                              int add_residual, int64_t B, int64_t N, uint32_t* status, void* stream);
+                              int add_residual, int64_t B, int64_t rows, int64_t N, uint32_t* status, void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * Data movement for the row-sharded stack (one process per GPU; the pair tensor is split
+ * over its first pair index into P shards of R = N / P rows). The reference has no
+ * multi-GPU path; these serve the host driver that exchanges shards with NCCL
+ * (all-gather of the b planes and of the triangle-bias rows, all-to-all transposes for
+ * the incoming update and the ending-node attention).
+ * ------------------------------------------------------------------------------- */
+
+/* `height` rows of `width` bytes from src (row pitch spitch) to dst (row pitch dpitch).
+ * Width, pitches and both pointers must be multiples of 16 bytes. */
+GTK_API int gtk_copy_2d(void* dst, int64_t dpitch, const void* src, int64_t spitch, int64_t width, int64_t height,
+                        void* stream);
+
+/* Per-peer chunks of a pair-grid transpose: for src [B][R][C][128] fp32,
+ * dst[q][b][x][y][:] = src[b][y][q*(C/P) + x][:]  (q < P, x < C/P, y < R).
+ * Chunk q (B*(C/P)*R pair vectors) is what peer q receives in an all-to-all; peer q then
+ * places the chunk from peer p at pair-column offset p*R of its transposed shard. */
+GTK_API int gtk_pair_transpose_pack(const float* src, float* dst, int64_t B, int64_t R, int64_t C, int64_t P,
+                                    void* stream);
 
 #ifdef __cplusplus
 }

@@ -59,14 +59,29 @@ def test_host_queries(lib):
 
 def test_triatt_workspace_layout(lib):
     B, N = 2, 100
-    offs = (ctypes.c_int64 * 6)()
-    assert lib.gtk_triatt_workspace_offsets(B, N, offs) == 0
+    offs = (ctypes.c_int64 * 7)()
+    assert lib.gtk_triatt_workspace_offsets(B, N, N, offs) == 0
     o = list(offs)
     pair16 = B * N * N * 128 * 2
     assert o[0] == 0 and all(x % 256 == 0 for x in o)
     assert all(o[k + 1] - o[k] >= pair16 for k in range(5))
     total = lib.gtk_triatt_workspace_bytes(B, N, 128, 128, 4)
-    assert total - o[5] >= B * 4 * N * lib.gtk_plane_pitch(N) * 2
+    assert o[6] == total
+    assert total - o[5] >= N * B * 4 * lib.gtk_plane_pitch(N) * 2
+    # a shard of 25 rows: per-pair intermediates shrink, the bias still covers all N rows
+    assert lib.gtk_triatt_workspace_offsets(B, 25, N, offs) == 0
+    s = list(offs)
+    assert s[1] - s[0] >= B * 25 * N * 128 * 2 and s[1] < o[1]
+    assert s[6] - s[5] >= N * B * 4 * lib.gtk_plane_pitch(N) * 2
+    assert lib.gtk_triatt_workspace_offsets(B, N + 1, N, offs) == -1
+
+
+def test_row_shards_are_starting_orientation_only(lib):
+    P = ctypes.c_void_p
+    rc = lib.gtk_triatt_project(0, P(256), P(256), P(256), 1, 32, 64, 0, None, None)
+    assert rc == -2 and b"ending" in lib.gtk_last_error_string()
+    rc = lib.gtk_triatt_core(1, None, P(256), 1, 32, 64, 40, 1e9, None, None)
+    assert rc == -1 and b"row0" in lib.gtk_last_error_string()
 
 
 def test_unsupported_shapes_fail_before_touching_the_device(lib):

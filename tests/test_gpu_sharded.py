@@ -1,0 +1,147 @@
+"""The row-sharded stack on B200: the exchange kernels against their definitions
+(bit-exact), P ranks emulated on one GPU with the real stage kernels against the
+unsharded stack and the oracle, and, when the box has two GPUs, two NCCL ranks."""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from gpu_util import assert_parity, assert_status_clean, require_gpu
+from oracle import triangle_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def test_copy_2d_matches_strided_copy():
+    dev = require_gpu()
+    from genie_tk import _lib, ops
+    lib = _lib.load()
+    src = torch.randint(0, 255, (37 * 4096 + 64,), dtype=torch.uint8, device=dev)
+    dst = torch.zeros(37 * 2048 + 512, dtype=torch.uint8, device=dev)
+    # 37 rows of 1520 bytes: from pitch 4096 at offset 48 to pitch 2048 at offset 32
+    rc = lib.gtk_copy_2d(ops._ptr(dst[32:]), 2048, ops._ptr(src[48:]), 4096, 1520, 37, ops._stream(dev))
+    assert rc == 0, lib.gtk_last_error_string()
+    ref = torch.zeros_like(dst)
+    ref[32:32 + 37 * 2048].view(37, 2048)[:, :1520] = src[48:48 + 37 * 4096].view(37, 4096)[:, :1520]
+    torch.cuda.synchronize()
+    assert torch.equal(dst, ref)
+    assert lib.gtk_copy_2d(ops._ptr(dst), 2048, ops._ptr(src), 4096, 1000, 2, ops._stream(dev)) == -3
+
+
+@pytest.mark.parametrize("B,R,Cn,P", [(1, 16, 64, 4), (2, 8, 48, 3), (1, 128, 1024, 8)])
+def test_pair_transpose_pack_matches_permute(B, R, Cn, P):
+    dev = require_gpu()
+    from genie_tk import _lib, ops
+    lib = _lib.load()
+    src = torch.randn(B, R, Cn, 128, device=dev)
+    dst = torch.empty(P, B, Cn // P, R, 128, device=dev)
+    rc = lib.gtk_pair_transpose_pack(ops._ptr(src), ops._ptr(dst), B, R, Cn, P, ops._stream(dev))
+    assert rc == 0, lib.gtk_last_error_string()
+    ref = src.view(B, R, P, Cn // P, 128).permute(2, 0, 3, 1, 4)
+    torch.cuda.synchronize()
+    assert torch.equal(dst, ref)
+
+
+def _problem(N, layers, seed=21):
+    gen = torch.Generator().manual_seed(seed)
+    z = torch.randn(1, N, N, 128, generator=gen)
+    mask = torch.ones(1, N, N)
+    mask[0, -7:, :] = 0
+    mask[0, :, -5:] = 0
+    params = []
+    for _ in range(layers):
+        params.append({
+            "tri_mul_out": O.make_trimul_params(128, 128, gen, gate_bias=1.0, ln_random=True, bias_random=True),
+            "tri_mul_in": O.make_trimul_params(128, 128, gen, gate_bias=1.0, ln_random=True, bias_random=True),
+            "tri_att_start": O.make_triatt_params(128, 128, 4, gen, gate_bias=1.0, ln_random=True,
+                                                  bias_random=True),
+            "tri_att_end": O.make_triatt_params(128, 128, 4, gen, gate_bias=1.0, ln_random=True, bias_random=True),
+        })
+    return z, mask, params
+
+
+def _stack(params, dev):
+    import genie_tk
+    st = genie_tk.TrianglePairStack(len(params)).to(dev)
+    st.load_layer_params([{k: {n: t.to(dev) for n, t in v.items()} for k, v in lp.items()} for lp in params])
+    return st
+
+
+@pytest.mark.parametrize("N,P,layers", [(128, 2, 1), (128, 4, 2), (256, 8, 1)])
+def test_emulated_shards_match_unsharded(N, P, layers):
+    dev = require_gpu()
+    from genie_tk.sharded import ShardedTrianglePairStack, run_emulated
+    z, mask, params = _problem(N, layers)
+    st = _stack(params, dev)
+    zd, md = z.to(dev), mask.to(dev)
+    full = st.forward(zd, md)
+    R = N // P
+    shards = [ShardedTrianglePairStack(st, P, r) for r in range(P)]
+    zin = [zd[:, r * R:(r + 1) * R].clone() for r in range(P)]
+    out = [torch.empty_like(t) for t in zin]
+    run_emulated(shards, out, md, zin)
+    got = torch.cat(out, dim=1)
+    torch.cuda.synchronize()
+    assert torch.equal(torch.cat(zin, 1), zd), "the input shards must be left unchanged"
+    # same kernels, same per-element summation order: the sharding adds no error of its own
+    assert float((got - full).abs().max()) <= 1e-3
+    ref = O.stack_forward(z, mask, params, no_heads=4)
+    assert_parity(got, ref, what=f"sharded P={P}")
+    assert_status_clean(dev)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _nccl_rank(rank, world, port, z, mask, params, q):
+    import datetime
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        from genie_tk.sharded import ShardedTrianglePairStack
+        N = z.shape[1]
+        R = N // world
+        zl = z[:, rank * R:(rank + 1) * R].contiguous().to(dev)
+        sh = ShardedTrianglePairStack(_stack(params, dev), world, rank)
+        sh.forward_(zl, mask.to(dev))
+        torch.cuda.synchronize()
+        q.put((rank, zl.cpu()))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_nccl_ranks_match_single_gpu():
+    require_gpu()
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    z, mask, params = _problem(256, 1, seed=5)
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_nccl_rank, args=(r, world, port, z, mask, params, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    parts = dict(q.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    got = torch.cat([parts[r] for r in range(world)], dim=1)
+    dev = torch.device("cuda", 0)
+    full = _stack(params, dev).forward(z.to(dev), mask.to(dev)).cpu()
+    assert float((got - full).abs().max()) <= 1e-3
+    ref = O.stack_forward(z, mask, params, no_heads=4)
+    assert_parity(got, ref, what="two NCCL ranks")

@@ -1,0 +1,143 @@
+"""The row-sharded stack's host logic on CPU: P ranks emulated in one process and two
+real ``gloo`` ranks, with the stage computations done by the CPU stand-ins of
+``shard_cpu_ops`` (the oracle's math in the kernels' byte layouts). Checked against
+the unsharded oracle stack and against an unsharded (P = 1) run of the same program."""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from oracle import triangle_oracle as O
+from shard_cpu_ops import CpuStageOps
+
+MAX_ABS, MEAN_ABS = 2e-2, 2e-3
+
+
+def _problem(B, N, layers, seed=11, masked=True):
+    gen = torch.Generator().manual_seed(seed)
+    z = torch.randn(B, N, N, 128, generator=gen)
+    mask = torch.ones(B, N, N)
+    if masked:
+        mask[-1, -5:, :] = 0
+        mask[-1, :, -3:] = 0
+        mask[0, 2, :] = 0
+    params = []
+    for _ in range(layers):
+        params.append({
+            "tri_mul_out": O.make_trimul_params(128, 128, gen, gate_bias=1.0, ln_random=True, bias_random=True),
+            "tri_mul_in": O.make_trimul_params(128, 128, gen, gate_bias=1.0, ln_random=True, bias_random=True),
+            "tri_att_start": O.make_triatt_params(128, 128, 4, gen, gate_bias=1.0, ln_random=True,
+                                                  bias_random=True),
+            "tri_att_end": O.make_triatt_params(128, 128, 4, gen, gate_bias=1.0, ln_random=True, bias_random=True),
+        })
+    return z, mask, params
+
+
+def _stack(params):
+    import genie_tk
+    st = genie_tk.TrianglePairStack(len(params))
+    st.load_layer_params(params)
+    return st
+
+
+def _run_emulated(z, mask, params, P):
+    from genie_tk.sharded import ShardedTrianglePairStack, run_emulated
+    st = _stack(params)
+    N = z.shape[1]
+    R = N // P
+    shards = [ShardedTrianglePairStack(st, P, r, stage_ops=CpuStageOps()) for r in range(P)]
+    zl = [z[:, r * R:(r + 1) * R].clone() for r in range(P)]
+    run_emulated(shards, zl, mask)
+    return torch.cat(zl, dim=1)
+
+
+@pytest.mark.parametrize("B,N,P,layers", [(1, 32, 2, 1), (1, 32, 4, 2), (1, 64, 8, 1), (2, 32, 2, 1)])
+def test_emulated_ranks_match_oracle(B, N, P, layers):
+    z, mask, params = _problem(B, N, layers)
+    ref = O.stack_forward(z, mask, params, no_heads=4)
+    got = _run_emulated(z, mask, params, P)
+    err = (got - ref).abs()
+    assert float(err.max()) <= MAX_ABS and float(err.mean()) <= MEAN_ABS, (float(err.max()), float(err.mean()))
+    # the sharding itself is exact up to summation order: compare with the unsharded program
+    one = _run_emulated(z, mask, params, 1)
+    assert float((got - one).abs().max()) <= 2e-4
+
+
+def test_out_of_place_first_block():
+    from genie_tk.sharded import ShardedTrianglePairStack, run_emulated
+    z, mask, params = _problem(1, 32, 1)
+    st = _stack(params)
+    ref = _run_emulated(z, mask, params, 2)
+    sh = [ShardedTrianglePairStack(st, 2, r, stage_ops=CpuStageOps()) for r in range(2)]
+    zin = [z[:, r * 16:(r + 1) * 16].clone() for r in range(2)]
+    keep = [t.clone() for t in zin]
+    out = [torch.full_like(t, float("nan")) for t in zin]
+    run_emulated(sh, out, mask, zin)
+    assert all(torch.equal(a, b) for a, b in zip(zin, keep))
+    assert float((torch.cat(out, 1) - ref).abs().max()) == 0.0
+
+
+def test_unmasked_and_no_mask_agree():
+    z, mask, params = _problem(1, 32, 1, masked=False)
+    a = _run_emulated(z, mask, params, 2)
+    b = _run_emulated(z, None, params, 2)
+    assert float((a - b).abs().max()) <= 1e-5
+
+
+def test_shard_spec_validation():
+    from genie_tk.sharded import ShardSpec
+    s = ShardSpec(1, 1024, 8, 3)
+    assert (s.R, s.row0) == (128, 384)
+    with pytest.raises(ValueError):
+        ShardSpec(1, 100, 8, 0)      # not divisible
+    with pytest.raises(ValueError):
+        ShardSpec(1, 36, 3, 0)       # 12 rows per rank: not a multiple of 8
+    with pytest.raises(ValueError):
+        ShardSpec(1, 64, 4, 4)       # rank out of range
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _gloo_rank(rank, world, port, z, mask, params, out_q):
+    import torch.distributed as dist
+    from genie_tk.sharded import ShardedTrianglePairStack
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        N = z.shape[1]
+        R = N // world
+        zl = z[:, rank * R:(rank + 1) * R].clone()
+        sh = ShardedTrianglePairStack(_stack(params), world, rank, stage_ops=CpuStageOps())
+        sh.forward_(zl, mask)
+        out_q.put((rank, zl))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gloo_two_ranks_match_emulation():
+    z, mask, params = _problem(1, 32, 1)
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gloo_rank, args=(r, world, port, z, mask, params, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    parts = dict(q.get(timeout=240) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    got = torch.cat([parts[r] for r in range(world)], dim=1)
+    emu = _run_emulated(z, mask, params, world)
+    assert float((got - emu).abs().max()) <= 1e-5
+    ref = O.stack_forward(z, mask, params, no_heads=4)
+    err = (got - ref).abs()
+    assert float(err.max()) <= MAX_ABS and float(err.mean()) <= MEAN_ABS
