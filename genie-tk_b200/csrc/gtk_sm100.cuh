@@ -137,7 +137,7 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 
 // ----------------------------------------------------------------------------------
 // TMA (cp.async.bulk.tensor). Tensor maps are __grid_constant__ kernel parameters.
-// No multicast form is used anywhere in this library.
+// Every load and store here moves data between global memory and the issuing CTA alone.
 // ----------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
