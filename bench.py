@@ -388,7 +388,7 @@ def run_sharded(args, rank, world, device):
     z = torch.empty_like(z0)
     stack = make_stack(L, device)
     so = TimedStageOps(CudaStageOps(device))
-    shard = ShardedTrianglePairStack(stack, world, rank, stage_ops=so)
+    shard = ShardedTrianglePairStack(stack, world, rank, stage_ops=so, trimul_exchange=args.trimul_exchange)
     shard.prepare(B, N, device)
 
     def step(zin=None, hook=None):
@@ -485,6 +485,7 @@ def run_sharded(args, rank, world, device):
                                    f"{L} layers x [TriMulOut, TriMulIn, TriAttStart, TriAttEnd]",
                        "global_batch": B, "seq_len": N, "layers": L,
                        "parallelism": f"row-sharded over i, {world} ranks x {R} rows (NCCL)",
+                       "trimul_exchange": shard.trimul_exchange,
                        "l2": "inputs larger than L2 (each shard is >= 64 MB fp32); no flush"},
             "stack_tflops": round(stack_tflops, 1),
             "stack_frac_of_bf16_peak": round(stack_tflops / peaks["bf16_tflops"] / world, 4),
@@ -521,6 +522,8 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=16)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--trimul-exchange", default="auto", choices=["auto", "gather", "channels"],
+                    help="multi-GPU exchange of the multiplicative update (auto: gather for <= 3 GPUs)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -4,12 +4,14 @@
 // The collectives themselves are NCCL calls made by the host driver; these kernels
 // prepare and scatter the contiguous per-peer chunks those calls exchange:
 //
-//   gtk_copy_2d            strided block copy (rows of `width` bytes between two pitches):
-//                          packs a column slice of every row into a contiguous chunk, or
-//                          scatters a received chunk into a column slice;
+//   gtk_copy_3d            strided block copy (`depth` slabs of `height` rows of `width`
+//                          bytes, each side with its own row pitch and slab stride): packs
+//                          one slice per peer into the contiguous chunks of an all-to-all,
+//                          or scatters the received chunks back into slices, in one launch;
+//                          gtk_copy_2d is its one-slab form;
 //   gtk_pair_transpose_pack  the pair-grid transpose that turns a row shard into the
 //                          per-peer chunks of an all-to-all whose result, after one
-//                          gtk_copy_2d per peer, is the transposed shard (used by the
+//                          gtk_copy_3d over the peers, is the transposed shard (used by the
 //                          ending-node attention, which runs as the starting node of z^T).
 //
 // Both are pure HBM streams: 16-byte vector accesses, every pair vector (128 fp32 =
@@ -22,14 +24,15 @@
 
 namespace gtk {
 
-__global__ void __launch_bounds__(256) copy_2d_kernel(uint8_t* __restrict__ dst, int64_t dpitch,
-                                                      const uint8_t* __restrict__ src, int64_t spitch, int64_t w16,
-                                                      int64_t total) {
+__global__ void __launch_bounds__(256) copy_3d_kernel(uint8_t* __restrict__ dst, int64_t dpitch, int64_t dslab,
+                                                      const uint8_t* __restrict__ src, int64_t spitch, int64_t sslab,
+                                                      int64_t w16, int64_t height, int64_t total) {
   for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
        e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t r = e / w16, c = e - r * w16;
-    const uint4 v = __ldg(reinterpret_cast<const uint4*>(src + r * spitch) + c);
-    reinterpret_cast<uint4*>(dst + r * dpitch)[c] = v;
+    const int64_t row = e / w16, c = e - row * w16;
+    const int64_t k = row / height, r = row - k * height;
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(src + k * sslab + r * spitch) + c);
+    reinterpret_cast<uint4*>(dst + k * dslab + r * dpitch)[c] = v;
   }
 }
 
@@ -68,19 +71,25 @@ using namespace gtk;
 
 extern "C" {
 
-int gtk_copy_2d(void* dst, int64_t dpitch, const void* src, int64_t spitch, int64_t width, int64_t height,
-                void* stream) {
-  if (width < 0 || height < 0 || dpitch < width || spitch < width)
-    return fail(GTK_ERR_INVALID_ARG, "copy_2d: bad width/height/pitch");
-  if (width == 0 || height == 0) return GTK_OK;
-  if ((width | dpitch | spitch) & 15) return fail(GTK_ERR_ALIGNMENT, "copy_2d: width and pitches must be 16-B multiples");
+int gtk_copy_3d(void* dst, int64_t dpitch, int64_t dslab, const void* src, int64_t spitch, int64_t sslab,
+                int64_t width, int64_t height, int64_t depth, void* stream) {
+  if (width < 0 || height < 0 || depth < 0 || dpitch < width || spitch < width || dslab < 0 || sslab < 0)
+    return fail(GTK_ERR_INVALID_ARG, "copy_3d: bad width/height/depth/pitch");
+  if (width == 0 || height == 0 || depth == 0) return GTK_OK;
+  if ((width | dpitch | spitch | dslab | sslab) & 15)
+    return fail(GTK_ERR_ALIGNMENT, "copy_3d: width, pitches and slab strides must be 16-B multiples");
   if (int e = check_ptr(dst, "dst")) return e;
   if (int e = check_ptr(src, "src")) return e;
   if (int e = check_device()) return e;
-  const int64_t w16 = width / 16, total = w16 * height;
-  copy_2d_kernel<<<grid_for(total, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<uint8_t*>(dst), dpitch, static_cast<const uint8_t*>(src), spitch, w16, total);
-  return check_launch("copy_2d_kernel");
+  const int64_t w16 = width / 16, total = w16 * height * depth;
+  copy_3d_kernel<<<grid_for(total, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<uint8_t*>(dst), dpitch, dslab, static_cast<const uint8_t*>(src), spitch, sslab, w16, height, total);
+  return check_launch("copy_3d_kernel");
+}
+
+int gtk_copy_2d(void* dst, int64_t dpitch, const void* src, int64_t spitch, int64_t width, int64_t height,
+                void* stream) {
+  return gtk_copy_3d(dst, dpitch, 0, src, spitch, 0, width, height, 1, stream);
 }
 
 int gtk_pair_transpose_pack(const float* src, float* dst, int64_t B, int64_t R, int64_t C, int64_t P, void* stream) {

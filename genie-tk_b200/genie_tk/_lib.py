@@ -65,6 +65,7 @@ _SIGNATURES = {
     "gtk_triatt_finish": (c_int, [c_int, c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_i64, c_vp, c_vp]),
     "gtk_triatt_workspace_offsets": (c_int, [c_i64, c_i64, c_i64, ctypes.POINTER(c_i64)]),
     "gtk_copy_2d": (c_int, [c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_vp]),
+    "gtk_copy_3d": (c_int, [c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp]),
     "gtk_pair_transpose_pack": (c_int, [c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp]),
 }
 

@@ -4,11 +4,18 @@ pair index i across P ranks (one process per GPU), R = N / P rows per rank.
 Each op needs one exchange between the ranks; the kernels run on local data only and
 every exchange goes through the collective into local memory first:
 
-  TriMulOut   x[i,j] = sum_k a[i,k] b[j,k]: project the local rows, all-gather the b planes
-              (every rank needs all rows j), contract local rows i against all j, finish.
-  TriMulIn    x[i,j] = sum_k a[k,i] b[k,j]: project the local rows k; an all-to-all gives
-              each rank the columns i it owns of every row k of a (column slices packed
-              with gtk_copy_2d); the b planes are all-gathered; contract; finish.
+  TriMulOut / TriMulIn   x[i,j,c] = sum_k a[i,k,c] b[j,k,c] (outgoing) or a[k,i,c] b[k,j,c]
+              (incoming), two exchanges to choose from (``trimul_exchange``):
+              "channels": the per-channel contractions are independent, so after projecting
+              its rows each rank trades planes with an all-to-all from row shards to channel
+              shards (all N rows, its C/P channels), runs full N x N contractions for its
+              channels (outgoing and incoming alike), and an all-to-all of x brings the rows
+              back for the LN_out / gate epilogue: 3 (P-1)/P planes per rank and op (84 MB at
+              N = 1024, P = 8);
+              "gather": the b planes are all-gathered (every rank needs all rows j) and, for
+              the incoming update, an all-to-all gives each rank its columns i of every row
+              k of a; local rows i are contracted against all j: (P-1) planes (+ (P-1)/P).
+              "auto" takes the one that moves fewer bytes: gather for P <= 3.
   TriAttStart local rows i; the triangle bias bias[h, j, k] is needed for all rows j, so
               each rank computes its rows and the bias region is all-gathered.
   TriAttEnd   End(z) = Start(z^T)^T with the mask transposed: an all-to-all transpose
@@ -86,10 +93,10 @@ class CudaStageOps:
         self._chk(self.lib.gtk_trimul_project(P(z), P(mask), P(mod.packed_weights(self.device)), P(a), P(b), N, B,
                                               rows, N, P(self.status), self._s()), "gtk_trimul_project")
 
-    def trimul_contract(self, outgoing, a, b, x, B, M, Nj, K, lda, ldb, ldx, xs):
+    def trimul_contract(self, outgoing, a, b, x, B, M, Nj, K, lda, ldb, ldx, xs, channels=C):
         P = ops._ptr
-        self._chk(self.lib.gtk_trimul_contract(int(outgoing), P(a), P(b), P(x), B, C, M, Nj, K, lda, ldb, ldx, xs,
-                                               P(self.status), self._s()), "gtk_trimul_contract")
+        self._chk(self.lib.gtk_trimul_contract(int(outgoing), P(a), P(b), P(x), B, channels, M, Nj, K, lda, ldb, ldx,
+                                               xs, P(self.status), self._s()), "gtk_trimul_contract")
 
     def trimul_finish(self, mod, z, x, ldx, xs, B, rows, N, out):
         P = ops._ptr
@@ -115,6 +122,10 @@ class CudaStageOps:
         self._chk(self.lib.gtk_copy_2d(ops._ptr(dst), dpitch, ops._ptr(src), spitch, width, height, self._s()),
                   "gtk_copy_2d")
 
+    def copy_3d(self, dst, dpitch, dslab, src, spitch, sslab, width, height, depth):
+        self._chk(self.lib.gtk_copy_3d(ops._ptr(dst), dpitch, dslab, ops._ptr(src), spitch, sslab, width, height,
+                                       depth, self._s()), "gtk_copy_3d")
+
     def pair_transpose_pack(self, src, dst, B, R, Cn, P):
         self._chk(self.lib.gtk_pair_transpose_pack(ops._ptr(src), ops._ptr(dst), B, R, Cn, P, self._s()),
                   "gtk_pair_transpose_pack")
@@ -136,10 +147,17 @@ class ShardedTrianglePairStack:
     in place; ``mask`` is the whole [B, N, N] mask (or None), identical on every rank.
     """
 
-    def __init__(self, stack: TrianglePairStack, world: int, rank: int, stage_ops=None):
+    def __init__(self, stack: TrianglePairStack, world: int, rank: int, stage_ops=None,
+                 trimul_exchange: str = "auto"):
+        if trimul_exchange not in ("auto", "gather", "channels"):
+            raise ValueError(f"trimul_exchange must be auto, gather or channels, not {trimul_exchange!r}")
         self.stack = stack
         self.world, self.rank = world, rank
         self.stage_ops = stage_ops
+        # bytes each rank moves per multiplicative update: gather (P-1) planes (+ (P-1)/P for
+        # the incoming a), channels 3 (P-1)/P planes -> the gather wins for P <= 3
+        self.trimul_exchange = trimul_exchange if trimul_exchange != "auto" else (
+            "gather" if world <= 3 else "channels")
         self._key = None
         self._buf: Dict[str, Tensor] = {}
 
@@ -152,26 +170,28 @@ class ShardedTrianglePairStack:
             return spec
         so = self.stage_ops
         R = spec.R
-        plane = B * R * C * N * 2          # local a / b / x planes, fp16, pitch N
+        plane = B * R * C * N * 2          # one rank's planes, fp16, pitch N (row or channel shard)
         lay = so.triatt_layout(B, R, N)
         bias_rows = R * B * H * N * 2      # this rank's rows of the bias region
         pair_loc = B * R * N * PAIR_BYTES  # one row shard of the pair tensor, fp32
         sizes = {
-            "a": plane, "b": plane, "x": plane,
-            "a_send": plane, "a_recv": plane,          # [P][B][R][C][R] chunks / [B][N][C][R]
-            "b_all": B * N * C * N * 2,                # gathered b planes [B][N][C][N]
+            "a": plane, "b": plane, "x": plane,           # row shards [B][R][C][N]
+            "send": plane, "x_recv": plane,               # all-to-all staging
             "tri": lay["total"], "bias_send": bias_rows,
             "zT": pair_loc, "t_send": pair_loc, "t_recv": pair_loc,
         }
+        if self.trimul_exchange == "channels":
+            sizes.update({"a_ch": plane, "b_ch": plane, "x_ch": plane})   # channel shards [B][N][C/P][N]
+        else:
+            sizes.update({"a_recv": plane,                 # a columns of this rank, all rows: [B][N][C][R]
+                          "b_all": B * N * C * N * 2})    # gathered b planes [B][N][C][N]
         self._buf = {k: so.alloc(_round256(v)) for k, v in sizes.items()}
         self._lay = lay
         self._key = (B, N)
-        if hasattr(self.stack, "layers"):
+        if isinstance(so, CudaStageOps) or isinstance(getattr(so, "inner", None), CudaStageOps):
             for layer in self.stack.layers:
                 for name in OP_NAMES:
-                    mod = getattr(layer, name)
-                    if hasattr(mod, "packed_weights") and isinstance(so, CudaStageOps):
-                        mod.packed_weights(device)
+                    getattr(layer, name).packed_weights(device)
         return spec
 
     # ---------------------------------------------------------------- the per-rank program
@@ -181,19 +201,20 @@ class ShardedTrianglePairStack:
         ``z`` is updated in place; with ``z_in`` the first block reads ``z_in`` instead and
         writes ``z`` (``z_in`` is left unchanged)."""
         B, R, N = z.shape[0], z.shape[1], z.shape[2]
-        src = z if z_in is None else z_in
         spec = self.prepare(B, N, z.device)
         if R != spec.R:
             raise ValueError(f"z_local has {R} rows; rank {self.rank} of {self.world} owns {spec.R}")
         so, buf, lay = self.stage_ops, self._buf, self._lay
         P, row0 = self.world, spec.row0
+        CP = C // P
+        src = z if z_in is None else z_in
         mask_loc = mask_t = None
         if mask is not None:
             mask_loc = mask[:, spec.rows()].contiguous()
             mask_t = mask.transpose(1, 2).contiguous()
         xs = 1.0 / N
-        plane_b = R * C * N * 2            # bytes of one batch element's local planes
-        chunk_a = R * C * R * 2            # a column slice for one peer, one batch element
+        plane_b = R * C * N * 2            # bytes of one batch element's planes (row or channel shard)
+        chunk = R * CP * N * 2             # one peer's share of them
         tri = buf["tri"]
         bias_all = tri[lay["bias"]:lay["bias"] + N * B * H * N * 2]
         bias_mine = bias_all[row0 * B * H * N * 2:(row0 + R) * B * H * N * 2]
@@ -201,10 +222,50 @@ class ShardedTrianglePairStack:
         zT = buf["zT"][:B * R * N * PAIR_BYTES].view(torch.float32).view(B, R, N, C)
         t_send, t_recv = buf["t_send"], buf["t_recv"]
 
-        def gather_b(b_planes):
+        def to_channels(rows_planes, ch_planes):
+            # rows [R] x channels [C] -> all N rows x this rank's channel group [C/P]
+            for bb in range(B):
+                so.copy_3d(buf["send"], CP * N * 2, chunk, rows_planes[bb * plane_b:], C * N * 2, CP * N * 2,
+                           CP * N * 2, R, P)
+                yield ("all_to_all", ch_planes[bb * plane_b:(bb + 1) * plane_b], buf["send"][:plane_b])
+
+        def to_rows(ch_planes, rows_planes):
+            for bb in range(B):
+                yield ("all_to_all", buf["x_recv"][:plane_b], ch_planes[bb * plane_b:(bb + 1) * plane_b])
+                so.copy_3d(rows_planes[bb * plane_b:], C * N * 2, CP * N * 2, buf["x_recv"], CP * N * 2, chunk,
+                           CP * N * 2, R, P)
+
+        def multiply_channels(mod, outgoing, zz):
+            so.trimul_project(mod, zz, mask_loc, buf["a"], buf["b"], B, R, N)
+            yield from to_channels(buf["a"], buf["a_ch"])
+            yield from to_channels(buf["b"], buf["b_ch"])
+            # full N x N contractions for this rank's C/P channels
+            so.trimul_contract(outgoing, buf["a_ch"], buf["b_ch"], buf["x_ch"], B, N, N, N, N, N, N, xs, CP)
+            yield from to_rows(buf["x_ch"], buf["x"])
+            so.trimul_finish(mod, zz, buf["x"], N, xs, B, R, N, z)
+
+        def gather_b():
             for bb in range(B):
                 yield ("all_gather", buf["b_all"][bb * N * C * N * 2:(bb + 1) * N * C * N * 2],
-                       b_planes[bb * plane_b:(bb + 1) * plane_b])
+                       buf["b"][bb * plane_b:(bb + 1) * plane_b])
+
+        def multiply_gather(mod, outgoing, zz):
+            so.trimul_project(mod, zz, mask_loc, buf["a"], buf["b"], B, R, N)
+            if outgoing:
+                # x[i, j] for local rows i against all rows j of b
+                yield from gather_b()
+                so.trimul_contract(True, buf["a"], buf["b_all"], buf["x"], B, R, N, N, N, N, N, xs)
+            else:
+                # x[i, j] = sum_k a[k, i] b[k, j]: this rank's columns i of every row k of a
+                for bb in range(B):
+                    so.copy_3d(buf["send"], R * 2, R * C * R * 2, buf["a"][bb * plane_b:], N * 2, R * 2, R * 2, R * C,
+                               P)
+                    yield ("all_to_all", buf["a_recv"][bb * plane_b:(bb + 1) * plane_b], buf["send"][:plane_b])
+                yield from gather_b()
+                so.trimul_contract(False, buf["a_recv"], buf["b_all"], buf["x"], B, R, N, N, R, N, N, xs)
+            so.trimul_finish(mod, zz, buf["x"], N, xs, B, R, N, z)
+
+        multiply = multiply_channels if self.trimul_exchange == "channels" else multiply_gather
 
         def attention(mod, zz, mm):
             so.triatt_project(mod, zz, tri, B, R, N, row0)
@@ -213,40 +274,22 @@ class ShardedTrianglePairStack:
             so.triatt_core(mod, mm, tri, B, R, N, row0)
             so.triatt_finish(mod, zz, tri, B, R, N)
 
-        def transpose(src, dst):
+        def transpose(src_pairs, dst_pairs):
             # dst = the transposed shard of the pair grid whose row shard is src
-            so.pair_transpose_pack(src, t_send, B, R, N, P)
+            so.pair_transpose_pack(src_pairs, t_send, B, R, N, P)
             yield ("all_to_all", t_recv[:P * pair_chunk], t_send[:P * pair_chunk])
-            for p in range(P):
-                so.copy_2d(_bytes(dst)[p * R * PAIR_BYTES:], N * PAIR_BYTES, t_recv[p * pair_chunk:],
-                           R * PAIR_BYTES, R * PAIR_BYTES, B * R)
+            so.copy_3d(_bytes(dst_pairs), N * PAIR_BYTES, R * PAIR_BYTES, t_recv, R * PAIR_BYTES, pair_chunk,
+                       R * PAIR_BYTES, B * R, P)
 
         for layer in self.stack.layers:
-            # ---- TriMulOut
-            mod = layer.tri_mul_out
-            so.trimul_project(mod, src, mask_loc, buf["a"], buf["b"], B, R, N)
-            yield from gather_b(buf["b"])
-            so.trimul_contract(True, buf["a"], buf["b_all"], buf["x"], B, R, N, N, N, N, N, xs)
-            so.trimul_finish(mod, src, buf["x"], N, xs, B, R, N, z)
-            src = z
-            # ---- TriMulIn
-            mod = layer.tri_mul_in
-            so.trimul_project(mod, z, mask_loc, buf["a"], buf["b"], B, R, N)
-            for bb in range(B):
-                for q in range(P):  # columns i of peer q, every local row k and channel
-                    so.copy_2d(buf["a_send"][q * chunk_a:], R * 2, buf["a"][bb * plane_b + q * R * 2:], N * 2,
-                               R * 2, R * C)
-                yield ("all_to_all", buf["a_recv"][bb * P * chunk_a:(bb + 1) * P * chunk_a],
-                       buf["a_send"][:P * chunk_a])
-            yield from gather_b(buf["b"])
-            so.trimul_contract(False, buf["a_recv"], buf["b_all"], buf["x"], B, R, N, N, R, N, N, xs)
-            so.trimul_finish(mod, z, buf["x"], N, xs, B, R, N, z)
-            # ---- TriAttStart
+            yield from multiply(layer.tri_mul_out, True, src)
+            yield from multiply(layer.tri_mul_in, False, z)
             yield from attention(layer.tri_att_start, z, mask)
-            # ---- TriAttEnd = Start(z^T, mask^T)^T, the residual added on the transposed shard
+            # TriAttEnd = Start(z^T, mask^T)^T, the residual added on the transposed shard
             yield from transpose(z, zT)
             yield from attention(layer.tri_att_end, zT, mask_t)
             yield from transpose(zT, z)
+            src = z
 
     # ---------------------------------------------------------------- runners
     @torch.no_grad()
@@ -279,7 +322,7 @@ class TimedStageOps:
     every stage call (per-kernel timing with events) and counts the kernel launches."""
 
     KERNELS = ("trimul_project", "trimul_contract", "trimul_finish", "triatt_project", "triatt_core",
-               "triatt_finish", "copy_2d", "pair_transpose_pack")
+               "triatt_finish", "copy_2d", "copy_3d", "pair_transpose_pack")
 
     def __init__(self, inner, hook=None):
         self.inner = inner

@@ -218,14 +218,19 @@ GTK_API int gtk_triatt_finish(int starting, const float* z, const void* packed, 
  * Data movement for the row-sharded stack (one process per GPU; the pair tensor is split
  * over its first pair index into P shards of R = N / P rows). The reference has no
  * multi-GPU path; these serve the host driver that exchanges shards with NCCL
- * (all-gather of the b planes and of the triangle-bias rows, all-to-all transposes for
- * the incoming update and the ending-node attention).
+ * (all-to-alls between row shards and channel shards of the multiplicative update's
+ * planes, an all-gather of the triangle-bias rows, all-to-all transposes of the pair
+ * tensor for the ending-node attention).
  * ------------------------------------------------------------------------------- */
 
 /* `height` rows of `width` bytes from src (row pitch spitch) to dst (row pitch dpitch).
  * Width, pitches and both pointers must be multiples of 16 bytes. */
 GTK_API int gtk_copy_2d(void* dst, int64_t dpitch, const void* src, int64_t spitch, int64_t width, int64_t height,
                         void* stream);
+/* `depth` slabs of the 2D copy above; slab k starts at dst + k*dslab and src + k*sslab
+ * (slab strides are multiples of 16 bytes as well). */
+GTK_API int gtk_copy_3d(void* dst, int64_t dpitch, int64_t dslab, const void* src, int64_t spitch, int64_t sslab,
+                        int64_t width, int64_t height, int64_t depth, void* stream);
 
 /* Per-peer chunks of a pair-grid transpose: for src [B][R][C][128] fp32,
  * dst[q][b][x][y][:] = src[b][y][q*(C/P) + x][:]  (q < P, x < C/P, y < R).

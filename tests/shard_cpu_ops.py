@@ -55,16 +55,17 @@ class CpuStageOps:
         _typed(a, torch.float16, (B, rows, C, N)).copy_(av.permute(0, 1, 3, 2))
         _typed(b, torch.float16, (B, rows, C, N)).copy_(bv.permute(0, 1, 3, 2))
 
-    def trimul_contract(self, outgoing, a, b, x, B, M, Nj, K, lda, ldb, ldx, xs):
+    def trimul_contract(self, outgoing, a, b, x, B, M, Nj, K, lda, ldb, ldx, xs, channels=C):
+        Cc = channels
         if outgoing:
-            A = _typed(a, torch.float16, (B, M, C, lda))[..., :K].float()
-            Bm = _typed(b, torch.float16, (B, Nj, C, ldb))[..., :K].float()
+            A = _typed(a, torch.float16, (B, M, Cc, lda))[..., :K].float()
+            Bm = _typed(b, torch.float16, (B, Nj, Cc, ldb))[..., :K].float()
             X = torch.einsum("bmck,bnck->bmcn", A, Bm)
         else:
-            A = _typed(a, torch.float16, (B, K, C, lda))[..., :M].float()
-            Bm = _typed(b, torch.float16, (B, K, C, ldb))[..., :Nj].float()
+            A = _typed(a, torch.float16, (B, K, Cc, lda))[..., :M].float()
+            Bm = _typed(b, torch.float16, (B, K, Cc, ldb))[..., :Nj].float()
             X = torch.einsum("bkcm,bkcn->bmcn", A, Bm)
-        _typed(x, torch.float16, (B, M, C, ldx))[..., :Nj].copy_(X * xs)
+        _typed(x, torch.float16, (B, M, Cc, ldx))[..., :Nj].copy_(X * xs)
 
     def trimul_finish(self, mod, z, x, ldx, xs, B, rows, N, out):
         p = self._p(mod)
@@ -122,6 +123,10 @@ class CpuStageOps:
         assert (height - 1) * dpitch + width <= dst.numel() and (height - 1) * spitch + width <= src.numel()
         d = dst.as_strided((height, width), (dpitch, 1))
         d.copy_(src.as_strided((height, width), (spitch, 1)))
+
+    def copy_3d(self, dst, dpitch, dslab, src, spitch, sslab, width, height, depth):
+        for k in range(depth):
+            self.copy_2d(dst[k * dslab:], dpitch, src[k * sslab:], spitch, width, height)
 
     def pair_transpose_pack(self, src, dst, B, R, Cn, P):
         s = src.reshape(B, R, P, Cn // P, C).permute(2, 0, 3, 1, 4)     # [P][B][Cn/P][R][C]

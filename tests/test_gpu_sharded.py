@@ -31,6 +31,24 @@ def test_copy_2d_matches_strided_copy():
     assert lib.gtk_copy_2d(ops._ptr(dst), 2048, ops._ptr(src), 4096, 1000, 2, ops._stream(dev)) == -3
 
 
+def test_copy_3d_matches_strided_copy():
+    dev = require_gpu()
+    from genie_tk import _lib, ops
+    lib = _lib.load()
+    # 3 slabs of 5 rows of 96 bytes: source slabs 1024 apart with row pitch 160,
+    # destination slabs 512 apart with row pitch 96 (packed rows)
+    src = torch.randint(0, 255, (4096,), dtype=torch.uint8, device=dev)
+    dst = torch.zeros(2048, dtype=torch.uint8, device=dev)
+    rc = lib.gtk_copy_3d(ops._ptr(dst), 96, 512, ops._ptr(src), 160, 1024, 96, 5, 3, ops._stream(dev))
+    assert rc == 0, lib.gtk_last_error_string()
+    ref = torch.zeros_like(dst)
+    for k in range(3):
+        for r in range(5):
+            ref[k * 512 + r * 96:k * 512 + r * 96 + 96] = src[k * 1024 + r * 160:k * 1024 + r * 160 + 96]
+    torch.cuda.synchronize()
+    assert torch.equal(dst, ref)
+
+
 @pytest.mark.parametrize("B,R,Cn,P", [(1, 16, 64, 4), (2, 8, 48, 3), (1, 128, 1024, 8)])
 def test_pair_transpose_pack_matches_permute(B, R, Cn, P):
     dev = require_gpu()
@@ -70,8 +88,10 @@ def _stack(params, dev):
     return st
 
 
-@pytest.mark.parametrize("N,P,layers", [(128, 2, 1), (128, 4, 2), (256, 8, 1)])
-def test_emulated_shards_match_unsharded(N, P, layers):
+@pytest.mark.parametrize("N,P,layers,exchange", [(128, 2, 1, "gather"), (128, 2, 1, "channels"),
+                                                 (128, 4, 2, "channels"), (128, 4, 1, "gather"),
+                                                 (256, 8, 1, "channels")])
+def test_emulated_shards_match_unsharded(N, P, layers, exchange):
     dev = require_gpu()
     from genie_tk.sharded import ShardedTrianglePairStack, run_emulated
     z, mask, params = _problem(N, layers)
@@ -79,7 +99,7 @@ def test_emulated_shards_match_unsharded(N, P, layers):
     zd, md = z.to(dev), mask.to(dev)
     full = st.forward(zd, md)
     R = N // P
-    shards = [ShardedTrianglePairStack(st, P, r) for r in range(P)]
+    shards = [ShardedTrianglePairStack(st, P, r, trimul_exchange=exchange) for r in range(P)]
     zin = [zd[:, r * R:(r + 1) * R].clone() for r in range(P)]
     out = [torch.empty_like(t) for t in zin]
     run_emulated(shards, out, md, zin)

@@ -43,22 +43,26 @@ def _stack(params):
     return st
 
 
-def _run_emulated(z, mask, params, P):
+def _run_emulated(z, mask, params, P, exchange="auto"):
     from genie_tk.sharded import ShardedTrianglePairStack, run_emulated
     st = _stack(params)
     N = z.shape[1]
     R = N // P
-    shards = [ShardedTrianglePairStack(st, P, r, stage_ops=CpuStageOps()) for r in range(P)]
+    shards = [ShardedTrianglePairStack(st, P, r, stage_ops=CpuStageOps(), trimul_exchange=exchange)
+              for r in range(P)]
     zl = [z[:, r * R:(r + 1) * R].clone() for r in range(P)]
     run_emulated(shards, zl, mask)
     return torch.cat(zl, dim=1)
 
 
-@pytest.mark.parametrize("B,N,P,layers", [(1, 32, 2, 1), (1, 32, 4, 2), (1, 64, 8, 1), (2, 32, 2, 1)])
-def test_emulated_ranks_match_oracle(B, N, P, layers):
+@pytest.mark.parametrize("B,N,P,layers,exchange", [(1, 32, 2, 1, "auto"), (1, 32, 4, 2, "auto"),
+                                                   (1, 64, 8, 1, "auto"), (2, 32, 2, 1, "auto"),
+                                                   (1, 32, 2, 1, "channels"), (1, 32, 4, 1, "gather"),
+                                                   (2, 32, 4, 1, "channels"), (2, 32, 2, 1, "gather")])
+def test_emulated_ranks_match_oracle(B, N, P, layers, exchange):
     z, mask, params = _problem(B, N, layers)
     ref = O.stack_forward(z, mask, params, no_heads=4)
-    got = _run_emulated(z, mask, params, P)
+    got = _run_emulated(z, mask, params, P, exchange)
     err = (got - ref).abs()
     assert float(err.max()) <= MAX_ABS and float(err.mean()) <= MEAN_ABS, (float(err.max()), float(err.mean()))
     # the sharding itself is exact up to summation order: compare with the unsharded program
