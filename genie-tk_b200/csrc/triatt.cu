@@ -724,18 +724,22 @@ __global__ void __launch_bounds__(k4::kThreads, 1)
             sv[k4i * 4 + 3] = __float_as_uint(__uint_as_float(sv[k4i * 4 + 3]) + m4.w);
           }
         }
-        float mx0 = __uint_as_float(sv[0]), mx1 = __uint_as_float(sv[1]);
+        // row max over four independent chains (a single chain serialises on the FMNMX latency)
+        float mx4[4] = {__uint_as_float(sv[0]), __uint_as_float(sv[1]), __uint_as_float(sv[2]),
+                        __uint_as_float(sv[3])};
 #pragma unroll
-        for (int k = 2; k < 126; k += 4) {
-          mx0 = max3f(mx0, __uint_as_float(sv[k]), __uint_as_float(sv[k + 1]));
-          mx1 = max3f(mx1, __uint_as_float(sv[k + 2]), __uint_as_float(sv[k + 3]));
-        }
-        const float mx = max3f(mx0, mx1, fmaxf(__uint_as_float(sv[126]), __uint_as_float(sv[127])));
+        for (int k = 4; k < 124; k += 8)
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            mx4[c] = max3f(mx4[c], __uint_as_float(sv[k + 2 * c]), __uint_as_float(sv[k + 2 * c + 1]));
+        const float mx = max3f(max3f(mx4[0], mx4[1], __uint_as_float(sv[124])),
+                               max3f(mx4[2], mx4[3], __uint_as_float(sv[125])),
+                               fmaxf(__uint_as_float(sv[126]), __uint_as_float(sv[127])));
         const float m_old = rr == 0 ? m_run0 : m_run1;
         const float m_new = (mx > m_old + kLazy) ? mx : m_old;
         const float alpha = (m_new == m_old) ? 1.f : ex2f(m_old - m_new);
         const float2 negm = make_float2(-m_new, -m_new);
-        float2 acc = make_float2(0.f, 0.f);
+        float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
         for (int k2 = 0; k2 < 64; ++k2) {
           float2 x = add_f32x2(make_float2(__uint_as_float(sv[2 * k2]), __uint_as_float(sv[2 * k2 + 1])), negm);
@@ -745,11 +749,12 @@ __global__ void __launch_bounds__(k4::kThreads, 1)
             x.x = ex2f(x.x);
             x.y = ex2f(x.y);
           }
-          acc = add_f32x2(acc, x);
+          acc[k2 & 3] = add_f32x2(acc[k2 & 3], x);  // four independent partial sums
           __half2 hp = __floats2half2_rn(x.x, x.y);
           sv[k2] = *reinterpret_cast<uint32_t*>(&hp);
         }
-        const float sum = acc.x + acc.y;
+        const float2 a01 = add_f32x2(acc[0], acc[1]), a23 = add_f32x2(acc[2], acc[3]);
+        const float sum = (a01.x + a23.x) + (a01.y + a23.y);
         if (rr == 0) {
           l_run0 = l_run0 * alpha + sum;
           m_run0 = m_new;
