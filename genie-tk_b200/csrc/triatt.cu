@@ -857,15 +857,12 @@ struct K4eBars {
   uint64_t a_full[2], a_empty[2];
   uint64_t d_full[2], d_empty[2];
   uint64_t o_full[k4e::kSlabs], o_empty[k4e::kSlabs];
+  uint64_t slab_ready[k4e::kSlabs];  // 128 epilogue threads wrote the slab
   uint64_t drain;
   uint32_t tslot;
   CtaGuard guard;
 };
 static_assert(sizeof(K4eBars) <= 256, "K4e barrier block");
-
-__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
-}
 
 __global__ void __launch_bounds__(k4e::kThreads, 1)
     triatt_finish_kernel(const __grid_constant__ CUtensorMap og_map, const __grid_constant__ CUtensorMap w_map,
@@ -892,6 +889,7 @@ __global__ void __launch_bounds__(k4e::kThreads, 1)
     for (int x = 0; x < kSlabs; ++x) {
       mbar_init(&bars->o_full[x], 1);
       mbar_init(&bars->o_empty[x], 1);
+      mbar_init(&bars->slab_ready[x], 128);
     }
     mbar_init(&bars->drain, 1);
     fence_barrier_init();
@@ -1017,14 +1015,24 @@ __global__ void __launch_bounds__(k4e::kThreads, 1)
           *reinterpret_cast<float4*>(ob + swz128(p, q)) = o;
         }
         fence_proxy_async_smem();
-        named_bar_sync(1, 128);
-        if (issuer) {
-          tma_store_4d(&out_map, ob, cc * 32, j0, i, b);
-          tma_store_commit();
-          // a slab buffer is free again once its store has read it; keep two stores in flight
-          tma_store_wait_read_le1();
-          if (slab >= 1) mbar_arrive(&bars->o_empty[(slab - 1) % kSlabs]);
+        mbar_arrive(&bars->slab_ready[sl]);
+        if (warp == 0) {
+          // one thread stores the slab once all 128 have written it (a bounded wait, so
+          // that an abort elsewhere cannot leave threads parked at a barrier)
+          bool iok = true;
+          if (issuer) {
+            iok = mbar_wait(&bars->slab_ready[sl], (slab / kSlabs) & 1, guard, status, kStatusTimeoutConsumer);
+            if (iok) {
+              tma_store_4d(&out_map, ob, cc * 32, j0, i, b);
+              tma_store_commit();
+              // a slab buffer is free again once its store has read it; keep two stores in flight
+              tma_store_wait_read_le1();
+              if (slab >= 1) mbar_arrive(&bars->o_empty[(slab - 1) % kSlabs]);
+            }
+          }
+          ok = __shfl_sync(0xffffffffu, iok ? 1 : 0, 0) != 0;
         }
+        if (!ok) break;
       }
       tc_fence_before();
       mbar_arrive(&bars->d_empty[s]);

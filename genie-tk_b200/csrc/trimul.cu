@@ -437,61 +437,79 @@ __global__ void __launch_bounds__(128, 1)
 
 // ----------------------------------------------------------------------------------
 // K2e: persistent LN_out + linear_z + output gate (+ residual). Tile = 128 consecutive
-// pairs; CTAs loop over tiles. 320 threads:
-//   warps 0-3  LayerNorm producers: LN_in(z) of the tile's pairs (warp per pair row,
-//              coalesced loads) into the fp16 operand A[s] (double buffered);
-//   warps 4-7  epilogue: thread = pair p (TMEM lane); LN_out statistics from the x tile
-//              in shared memory, gate, residual, staged in 32-channel fp32 slabs and
-//              written with TMA stores (2 slab buffers);
-//   warp 8     lane 0: MMA issuer; warp 9 lane 0: TMA producer (weights once, x tiles).
+// pairs; CTAs loop over tiles. 480 threads:
+//   warps 0-7   LayerNorm producers for the gate: LN_in(z) of the tile's pairs, two threads
+//               per pair (64 channels each, combined with one shuffle), read from the
+//               TMA-staged z tile into registers and, once all 256 have read it, written as
+//               the fp16 operand A over the first half of the same buffer;
+//   warps 8-11  epilogue: thread = pair p (TMEM lane); LN_out statistics from the x tile
+//               in shared memory; then four 32-channel slabs: the residual slab of z arrives
+//               by TMA, is updated in place with gate * linear_z(LN_out(x)) and leaves by
+//               TMA store (a ring of 4 slab buffers, so residual loads run well ahead), so
+//               every global access is a bulk tensor copy;
+//   warp 12     lane 0: MMA issuer;
+//   warp 13     lane 0: TMA for the weights (once), the z tile and the x tile;
+//   warp 14     lane 0: TMA for the residual slabs.
 // TMEM (double buffered per tile, 256 columns each): G = A W_g^T at +0, U = x^T (W_z gamma)^T
 // at +128. LN_out folds into the epilogue: out = g * (rstd (U - mu u) + v).
-// Shared memory: W2 64 KB | A 2 x 32 KB | x 2 x 32 KB | out slabs 2 x 16 KB | b_g,u,v | barriers.
+// Shared memory: W2 64 KB | z tile / A 64 KB | x 32 KB | slabs 4 x 16 KB | b_g,u,v | barriers.
+// The z tile is reloaded once the gate GEMM has read A from the same buffer.
+// (A warp-per-pair LayerNorm read from global memory and per-thread residual loads, each
+// warp load touching 32 separate pairs, held this kernel at ~17k cycles per tile.)
 // ----------------------------------------------------------------------------------
 namespace k2e {
-constexpr int kThreads = 320;
-constexpr uint32_t kW = 0, kA = 65536, kX = 131072, kO = 196608, kVec = 229376, kBar = 229376 + 1536;
-constexpr uint32_t kSmem = kBar + 128 + 1024;
+constexpr int kThreads = 480;
+constexpr int kSlabs = 4;
+constexpr uint32_t kW = 0, kZ = 65536, kA = kZ, kX = 131072, kO = 163840, kVec = 229376, kBar = 229376 + 1536;
+constexpr uint32_t kSmem = kBar + 256 + 1024;
+static_assert(kO + kSlabs * 16384 <= kVec, "K2e slabs");
 static_assert(kSmem <= 232448, "K2e shared memory");
 }  // namespace k2e
 
 struct K2eBars {
   uint64_t wbar;
-  uint64_t a_full[2], a_empty[2];
-  uint64_t x_full[2], x_empty[2];
+  uint64_t z_full, z_read;   // z tile: TMA / all 256 LayerNorm threads have read it
+  uint64_t a_full, a_empty;  // 256 LayerNorm threads / MMA commit (the z tile may be reloaded)
+  uint64_t x_full, x_empty;  // TMA / MMA commit + 128 epilogue threads (statistics)
   uint64_t d_full[2], d_empty[2];
+  uint64_t o_full[k2e::kSlabs], o_empty[k2e::kSlabs];
+  uint64_t slab_ready[k2e::kSlabs];  // 128 epilogue threads wrote the slab
   uint64_t drain;
   uint32_t tslot;
   CtaGuard guard;
 };
-static_assert(sizeof(K2eBars) <= 128, "K2e barrier block");
-
-__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
-}
+static_assert(sizeof(K2eBars) <= 256, "K2e barrier block");
 
 __global__ void __launch_bounds__(k2e::kThreads, 1)
     trimul_finish_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap x_map,
-                         const __grid_constant__ CUtensorMap out_map, const float* __restrict__ z,
+                         const __grid_constant__ CUtensorMap z_map, const __grid_constant__ CUtensorMap out_map,
                          const float* __restrict__ vec, int add_residual, float x_scale, int N, int rows, int n_jt,
                          int n_tiles, uint32_t* status) {
+  using namespace k2e;
   extern __shared__ uint8_t dsmem[];
   uint8_t* smem = align1024(dsmem);
-  K2eBars* bars = reinterpret_cast<K2eBars*>(smem + k2e::kBar);
+  K2eBars* bars = reinterpret_cast<K2eBars*>(smem + kBar);
   CtaGuard* guard = &bars->guard;
-  float* svec = reinterpret_cast<float*>(smem + k2e::kVec);  // b_g | u | v
+  float* svec = reinterpret_cast<float*>(smem + kVec);  // b_g | u | v
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   if (tid == 0) {
     guard->abort = 0;
     mbar_init(&bars->wbar, 1);
+    mbar_init(&bars->z_full, 1);
+    mbar_init(&bars->z_read, 256);
+    mbar_init(&bars->a_full, 256);
+    mbar_init(&bars->a_empty, 1);
+    mbar_init(&bars->x_full, 1);
+    mbar_init(&bars->x_empty, 1 + 128);
     for (int x = 0; x < 2; ++x) {
-      mbar_init(&bars->a_full[x], 128);
-      mbar_init(&bars->a_empty[x], 1);
-      mbar_init(&bars->x_full[x], 1);
-      mbar_init(&bars->x_empty[x], 1 + 128);  // MMA commit + epilogue threads (statistics)
       mbar_init(&bars->d_full[x], 1);
       mbar_init(&bars->d_empty[x], 128);
+    }
+    for (int x = 0; x < kSlabs; ++x) {
+      mbar_init(&bars->o_full[x], 1);
+      mbar_init(&bars->o_empty[x], 1);
+      mbar_init(&bars->slab_ready[x], 128);
     }
     mbar_init(&bars->drain, 1);
     fence_barrier_init();
@@ -501,7 +519,7 @@ __global__ void __launch_bounds__(k2e::kThreads, 1)
     svec[128 + tid] = vec[tmpack::kVU + tid];
     svec[256 + tid] = vec[tmpack::kVV + tid];
   }
-  if (warp == 8) {
+  if (warp == 12) {
     tmem_alloc(&bars->tslot, 512);
     tmem_relinquish();
   }
@@ -510,59 +528,77 @@ __global__ void __launch_bounds__(k2e::kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = bars->tslot;
 
-  if (warp < 4) {
-    // ------------------------- LayerNorm producers -------------------------
-    const float4 gw = reinterpret_cast<const float4*>(vec + tmpack::kVLnW)[lane];
-    const float4 gb = reinterpret_cast<const float4*>(vec + tmpack::kVLnB)[lane];
+  if (warp < 8) {
+    // ---------------- LayerNorm producers: two threads per pair row ----------------
+    const int row = warp * 16 + (lane >> 1), half = lane & 1;
+    const float* lnw = vec + tmpack::kVLnW + half * 64;
+    const float* lnb = vec + tmpack::kVLnB + half * 64;
     int it = 0;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
-      const int s = it & 1;
-      const int jt = tile % n_jt, rb = tile / n_jt;
-      const int r = rb % rows, b = rb / rows, j0 = jt * 128;
-      if (it >= 2) {
-        if (!__all_sync(0xffffffffu, mbar_wait(&bars->a_empty[s], ((it >> 1) - 1) & 1, guard, status,
-                                               kStatusTimeoutProducer)))
-          break;
-      }
-      const size_t rowbase = (static_cast<size_t>(b) * rows + r) * N;
-      float4 v[32];
+      if (!__all_sync(0xffffffffu, mbar_wait(&bars->z_full, it & 1, guard, status, kStatusTimeoutProducer))) break;
+      // channels 64*half .. 64*half+63 are boxes 2*half, 2*half+1 of the staged tile
+      float v[64];
 #pragma unroll
-      for (int k = 0; k < 32; ++k) {
-        const int j = j0 + warp * 32 + k;
-        v[k] = j < N ? __ldg(reinterpret_cast<const float4*>(z + (rowbase + j) * 128) + lane)
-                     : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-      uint8_t* at = smem + k2e::kA + s * 32768 + (lane >> 4) * 16384;
+      for (int q = 0; q < 2; ++q)
 #pragma unroll
-      for (int k = 0; k < 32; ++k) {
-        const float mean = warp_sum((v[k].x + v[k].y) + (v[k].z + v[k].w)) * (1.f / 128.f);
-        const float dx = v[k].x - mean, dy = v[k].y - mean, dz = v[k].z - mean, dw = v[k].w - mean;
-        const float var = warp_sum((dx * dx + dy * dy) + (dz * dz + dw * dw)) * (1.f / 128.f);
-        const float rstd = rsqrtf(var + 1e-5f);
-        uint2 o;
-        o.x = pack_f16x2(dx * rstd * gw.x + gb.x, dy * rstd * gw.y + gb.y);
-        o.y = pack_f16x2(dz * rstd * gw.z + gb.z, dw * rstd * gw.w + gb.w);
-        *reinterpret_cast<uint2*>(at + swz128(warp * 32 + k, (lane & 15) >> 1) + (lane & 1) * 8) = o;
+        for (int ch = 0; ch < 8; ++ch) {
+          const float4 t = lds_f4(smem + kZ + (2 * half + q) * 16384 + swz128(row, ch));
+          v[q * 32 + ch * 4 + 0] = t.x;
+          v[q * 32 + ch * 4 + 1] = t.y;
+          v[q * 32 + ch * 4 + 2] = t.z;
+          v[q * 32 + ch * 4 + 3] = t.w;
+        }
+      mbar_arrive(&bars->z_read);
+      float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < 64; ++c) s4[c & 3] += v[c];
+      float sum = (s4[0] + s4[1]) + (s4[2] + s4[3]);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+      const float mean = sum * (1.f / 128.f);
+      float q4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        const float d = v[c] - mean;
+        q4[c & 3] += d * d;
+      }
+      float ss = (q4[0] + q4[1]) + (q4[2] + q4[3]);
+      ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+      const float rstd = rsqrtf(ss * (1.f / 128.f) + 1e-5f);
+      // A overwrites the z tile: wait until every LayerNorm thread has read its rows
+      if (!__all_sync(0xffffffffu, mbar_wait(&bars->z_read, it & 1, guard, status, kStatusTimeoutProducer))) break;
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        const int c = ch * 8;
+        const float4 w0 = __ldg(reinterpret_cast<const float4*>(lnw + c));
+        const float4 w1 = __ldg(reinterpret_cast<const float4*>(lnw + c + 4));
+        const float4 b0 = __ldg(reinterpret_cast<const float4*>(lnb + c));
+        const float4 b1 = __ldg(reinterpret_cast<const float4*>(lnb + c + 4));
+        uint4 o;
+        o.x = pack_f16x2((v[c + 0] - mean) * rstd * w0.x + b0.x, (v[c + 1] - mean) * rstd * w0.y + b0.y);
+        o.y = pack_f16x2((v[c + 2] - mean) * rstd * w0.z + b0.z, (v[c + 3] - mean) * rstd * w0.w + b0.w);
+        o.z = pack_f16x2((v[c + 4] - mean) * rstd * w1.x + b1.x, (v[c + 5] - mean) * rstd * w1.y + b1.y);
+        o.w = pack_f16x2((v[c + 6] - mean) * rstd * w1.z + b1.z, (v[c + 7] - mean) * rstd * w1.w + b1.w);
+        sts_u4(smem + kA + half * 16384 + swz128(row, ch), o);
       }
       fence_proxy_async_smem();
-      mbar_arrive(&bars->a_full[s]);
+      mbar_arrive(&bars->a_full);
     }
-  } else if (warp == 8) {
+  } else if (warp == 12) {
     // ------------------------------ MMA issuer ------------------------------
     if (lane == 0) {
       bool ok = mbar_wait(&bars->wbar, 0, guard, status, kStatusTimeoutMma);
       const uint32_t id_g = make_idesc_f16(128, 128, 0, 0);
       const uint32_t id_u = make_idesc_f16(128, 128, 1, 0);
-      const uint32_t w0 = smem_u32(smem + k2e::kW);
+      const uint32_t w0 = smem_u32(smem + kW);
+      const uint32_t a0 = smem_u32(smem + kA), x0 = smem_u32(smem + kX);
       int it = 0;
       for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++it) {
         const int s = it & 1;
-        ok = mbar_wait(&bars->a_full[s], (it >> 1) & 1, guard, status, kStatusTimeoutMma);
-        ok = ok && mbar_wait(&bars->x_full[s], (it >> 1) & 1, guard, status, kStatusTimeoutMma);
+        ok = mbar_wait(&bars->a_full, it & 1, guard, status, kStatusTimeoutMma);
+        ok = ok && mbar_wait(&bars->x_full, it & 1, guard, status, kStatusTimeoutMma);
         if (ok && it >= 2) ok = mbar_wait(&bars->d_empty[s], ((it >> 1) - 1) & 1, guard, status, kStatusTimeoutMma);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t a0 = smem_u32(smem + k2e::kA + s * 32768), x0 = smem_u32(smem + k2e::kX + s * 32768);
         const uint32_t d = tmem + s * 256;
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
@@ -577,58 +613,95 @@ __global__ void __launch_bounds__(k2e::kThreads, 1)
                   make_sdesc(w0 + kh * 32768 + 16384 + kin * 32, 16, 1024, Swz::k128), id_u, ks > 0 ? 1u : 0u);
         }
         umma_commit(&bars->d_full[s]);
-        umma_commit(&bars->a_empty[s]);
-        umma_commit(&bars->x_empty[s]);
+        umma_commit(&bars->a_empty);
+        umma_commit(&bars->x_empty);
       }
       if (!ok) {
         umma_commit(&bars->drain);
         mbar_wait_drain(&bars->drain, 0);
       }
     }
-  } else if (warp == 9) {
-    // ------------------------------ TMA producer ------------------------------
+  } else if (warp == 13) {
+    // ------------------- TMA producer: weights, z tiles, x tiles -------------------
     if (lane == 0) {
       mbar_arrive_expect_tx(&bars->wbar, 65536);
 #pragma unroll
-      for (int kh = 0; kh < 2; ++kh) tma_load_2d(smem + k2e::kW + kh * 32768, &w_map, &bars->wbar, kh * 64, 0);
+      for (int kh = 0; kh < 2; ++kh) tma_load_2d(smem + kW + kh * 32768, &w_map, &bars->wbar, kh * 64, 0);
       bool ok = true;
-      int it = 0, issued = 0;
+      int it = 0, zl = 0, xl = 0;  // z / x tiles loaded
       for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
-        const int s = it & 1;
         const int jt = tile % n_jt, rb = tile / n_jt;
         const int r = rb % rows, b = rb / rows, j0 = jt * 128;
-        if (it >= 2 && !mbar_wait(&bars->x_empty[s], ((it >> 1) - 1) & 1, guard, status, kStatusTimeoutProducer)) {
+        if (it >= 1 && !mbar_wait(&bars->a_empty, (it - 1) & 1, guard, status, kStatusTimeoutProducer)) {
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&bars->x_full[s], 32768);
+        mbar_arrive_expect_tx(&bars->z_full, 65536);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) tma_load_4d(smem + kZ + q * 16384, &z_map, &bars->z_full, q * 32, j0, r, b);
+        ++zl;
+        if (it >= 1 && !mbar_wait(&bars->x_empty, (it - 1) & 1, guard, status, kStatusTimeoutProducer)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&bars->x_full, 32768);
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh)
-          tma_load_4d(smem + k2e::kX + s * 32768 + hh * 16384, &x_map, &bars->x_full[s], j0 + hh * 64, 0, r, b);
-        ++issued;
+          tma_load_4d(smem + kX + hh * 16384, &x_map, &bars->x_full, j0 + hh * 64, 0, r, b);
+        ++xl;
       }
+      // after an abort, let the last copies land before the CTA's shared memory is released
       if (!ok) {
-        for (int t = (issued > 2 ? issued - 2 : 0); t < issued; ++t) mbar_wait_drain(&bars->x_full[t & 1], (t >> 1) & 1);
+        if (zl > 0) mbar_wait_drain(&bars->z_full, (zl - 1) & 1);
+        if (xl > 0) mbar_wait_drain(&bars->x_full, (xl - 1) & 1);
       }
       mbar_wait_drain(&bars->wbar, 0);
+    }
+  } else if (warp == 14) {
+    // ------------------------ TMA producer: residual slabs ------------------------
+    if (lane == 0) {
+      bool ok = true;
+      int slab = 0;
+      for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
+        const int jt = tile % n_jt, rb = tile / n_jt;
+        const int r = rb % rows, b = rb / rows, j0 = jt * 128;
+        for (int cc = 0; cc < 4; ++cc, ++slab) {
+          const int sl = slab % kSlabs;
+          if (slab >= kSlabs && !mbar_wait(&bars->o_empty[sl], ((slab / kSlabs) - 1) & 1, guard, status,
+                                           kStatusTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          if (add_residual) {
+            mbar_arrive_expect_tx(&bars->o_full[sl], 16384);
+            tma_load_4d(smem + kO + sl * 16384, &z_map, &bars->o_full[sl], cc * 32, j0, r, b);
+          } else {
+            mbar_arrive(&bars->o_full[sl]);
+          }
+        }
+      }
+      if (!ok)
+        for (int t = (slab > kSlabs ? slab - kSlabs : 0); t < slab; ++t)
+          mbar_wait_drain(&bars->o_full[t % kSlabs], (t / kSlabs) & 1);
     }
   } else {
     // ------------------------- epilogue: thread = pair -------------------------
     const int q4 = warp & 3;
     const int p = q4 * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
-    const bool issuer = (warp == 4 && lane == 0);
-    int it = 0;
-    int slab = 0;  // running slab counter (slab buffer = slab & 1)
-    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+    const bool issuer = (warp == 8 && lane == 0);
+    int it = 0, slab = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++it) {
       const int s = it & 1;
       const int jt = tile % n_jt, rb = tile / n_jt;
       const int r = rb % rows, b = rb / rows, j0 = jt * 128;
-      bool w = mbar_wait(&bars->x_full[s], (it >> 1) & 1, guard, status, kStatusTimeoutConsumer);
+      bool w = mbar_wait(&bars->x_full, it & 1, guard, status, kStatusTimeoutConsumer);
       w = w && mbar_wait(&bars->d_full[s], (it >> 1) & 1, guard, status, kStatusTimeoutConsumer);
-      if (!__all_sync(0xffffffffu, w)) break;
+      ok = __all_sync(0xffffffffu, w);
+      if (!ok) break;
       // LN_out statistics over the 128 channels of pair p (x is stored times x_scale)
-      const uint8_t* xb = smem + k2e::kX + s * 32768 + (p >> 6) * 16384;
+      const uint8_t* xb = smem + kX + (p >> 6) * 16384;
       const int pj = p & 63;
       const float x0 = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(xb + swz128(0, pj >> 3) + (pj & 7) * 2)));
       float s1 = 0.f, s2 = 0.f;
@@ -640,33 +713,28 @@ __global__ void __launch_bounds__(k2e::kThreads, 1)
         s1 += xv;
         s2 += xv * xv;
       }
-      mbar_arrive(&bars->x_empty[s]);
+      mbar_arrive(&bars->x_empty);
       const float d1 = s1 * (1.f / 128.f);
       const float mu_x = x0 + d1;
       const float var = fmaxf(s2 * (1.f / 128.f) - d1 * d1, 0.f);
       const float rstd_x = rsqrtf(var + 1e-5f * x_scale * x_scale);
       tc_fence_after();
-      const size_t pair = (static_cast<size_t>(b) * rows + r) * N + j0 + p;
-      const bool valid = j0 + p < N;
 #pragma unroll 1
       for (int cc = 0; cc < 4; ++cc, ++slab) {
+        const int sl = slab % kSlabs;
         uint32_t g[32], u[32];
         tmem_ld32(tmem + lane_off + s * 256 + cc * 32, g);
         tmem_ld32(tmem + lane_off + s * 256 + 128 + cc * 32, u);
-        float4 res[8];
-#pragma unroll
-        for (int q = 0; q < 8; ++q)
-          res[q] = (add_residual && valid) ? __ldg(reinterpret_cast<const float4*>(z + pair * 128 + cc * 32) + q)
-                                           : make_float4(0.f, 0.f, 0.f, 0.f);
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars->o_full[sl], (slab / kSlabs) & 1, guard, status,
+                                               kStatusTimeoutConsumer));
         tmem_wait_ld();
-        // the slab buffer used two slabs ago must have been read by its TMA store
-        if (issuer) tma_store_wait_read_le1();
-        named_bar_sync(1, 128);
-        uint8_t* ob = smem + k2e::kO + (slab & 1) * 16384;
+        if (!ok) break;
+        uint8_t* ob = smem + kO + sl * 16384;
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
           float o[4];
-          const float rq[4] = {res[q].x, res[q].y, res[q].z, res[q].w};
+          const float4 zv = add_residual ? lds_f4(ob + swz128(p, q)) : make_float4(0.f, 0.f, 0.f, 0.f);
+          const float rq[4] = {zv.x, zv.y, zv.z, zv.w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int t = q * 4 + e, n = cc * 32 + t;
@@ -676,20 +744,37 @@ __global__ void __launch_bounds__(k2e::kThreads, 1)
           *reinterpret_cast<float4*>(ob + swz128(p, q)) = make_float4(o[0], o[1], o[2], o[3]);
         }
         fence_proxy_async_smem();
-        named_bar_sync(1, 128);
-        if (issuer) {
-          tma_store_4d(&out_map, ob, cc * 32, j0, r, b);
-          tma_store_commit();
+        mbar_arrive(&bars->slab_ready[sl]);
+        if (warp == 8) {
+          // one thread stores the slab once all 128 have written it (a bounded wait, so
+          // that an abort elsewhere cannot leave threads parked at a barrier)
+          bool iok = true;
+          if (issuer) {
+            iok = mbar_wait(&bars->slab_ready[sl], (slab / kSlabs) & 1, guard, status, kStatusTimeoutConsumer);
+            if (iok) {
+              tma_store_4d(&out_map, ob, cc * 32, j0, r, b);
+              tma_store_commit();
+              // a slab buffer is free again once its store has read it; keep one store in flight
+              tma_store_wait_read_le1();
+              if (slab >= 1) mbar_arrive(&bars->o_empty[(slab - 1) % kSlabs]);
+            }
+          }
+          ok = __shfl_sync(0xffffffffu, iok ? 1 : 0, 0) != 0;
         }
+        if (!ok) break;
       }
+      if (!ok) break;
       tc_fence_before();
       mbar_arrive(&bars->d_empty[s]);
     }
-    if (issuer) tma_store_wait_all();
+    if (issuer) {
+      tma_store_wait_all();
+      if (ok && slab >= 1) mbar_arrive(&bars->o_empty[(slab - 1) % kSlabs]);
+    }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 8) {
+  if (warp == 12) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -841,14 +926,15 @@ int gtk_trimul_finish(const float* z, const void* x_planes, int64_t ldx, float x
   const int64_t n_jt = (N + 127) / 128;
   const int64_t n_tiles = B * rows * n_jt;
   if (n_tiles > 2147483647) return fail(GTK_ERR_INVALID_ARG, "trimul_finish: too many tiles");
-  CUtensorMap wm, xm, om;
+  CUtensorMap wm, xm, zm, om;
   if (int e = make_weight_map(&wm, pk + tmpack::kW2, 256, 256)) return e;
   if (int e = make_plane_map(&xm, x_planes, B, rows, 128, N, ldx, 64, 128, 1, 128)) return e;
+  if (int e = make_pair_map(&zm, z, B, rows, N, false)) return e;
   if (int e = make_pair_map(&om, out, B, rows, N, false)) return e;
   if (int e = ensure_smem(reinterpret_cast<const void*>(trimul_finish_kernel), k2e::kSmem)) return e;
   const int grid = static_cast<int>(n_tiles < num_sms() ? n_tiles : num_sms());
   trimul_finish_kernel<<<grid, k2e::kThreads, k2e::kSmem, static_cast<cudaStream_t>(stream)>>>(
-      wm, xm, om, z, reinterpret_cast<const float*>(pk + tmpack::kVec), add_residual, x_scale, static_cast<int>(N),
+      wm, xm, zm, om, reinterpret_cast<const float*>(pk + tmpack::kVec), add_residual, x_scale, static_cast<int>(N),
       static_cast<int>(rows), static_cast<int>(n_jt), static_cast<int>(n_tiles), status);
   return check_launch("trimul_finish_kernel");
 }
