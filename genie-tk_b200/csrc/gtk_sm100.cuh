@@ -385,6 +385,13 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
 }
 
 __device__ __forceinline__ float4 lds_f4(const uint8_t* p) { return *reinterpret_cast<const float4*>(p); }
+// 32-byte global store (sm_100); p must be 32-byte aligned.
+__device__ __forceinline__ void stg_v8(void* p, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t a4,
+                                       uint32_t a5, uint32_t a6, uint32_t a7) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(a0), "r"(a1), "r"(a2),
+               "r"(a3), "r"(a4), "r"(a5), "r"(a6), "r"(a7)
+               : "memory");
+}
 __device__ __forceinline__ void sts_u4(uint8_t* p, uint4 v) { *reinterpret_cast<uint4*>(p) = v; }
 
 // LayerNorm of one 128-channel fp32 row held in a 128-B-swizzled [128 rows][32 fp32] x4

@@ -328,33 +328,27 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
           tmem_wait_ld();
           if (!valid) continue;
           // first 128 columns of the half: q (h = 0) or v (h = 1), head cc: 64 contiguous bytes
+          // each destination row is 64 contiguous bytes, 64-byte aligned: two 32-byte stores
           __half* dst0 = (h == 0 ? q_out : v_out) + ((static_cast<size_t>(bi) * kHeads + cc) * N + j) * kHeadDim;
-          uint4* d0 = reinterpret_cast<uint4*>(dst0);
+          uint32_t w0[16];
 #pragma unroll
-          for (int u = 0; u < 4; ++u)
-            d0[u] = make_uint4(pack_f16x2(__uint_as_float(x0[u * 8 + 0]), __uint_as_float(x0[u * 8 + 1])),
-                               pack_f16x2(__uint_as_float(x0[u * 8 + 2]), __uint_as_float(x0[u * 8 + 3])),
-                               pack_f16x2(__uint_as_float(x0[u * 8 + 4]), __uint_as_float(x0[u * 8 + 5])),
-                               pack_f16x2(__uint_as_float(x0[u * 8 + 6]), __uint_as_float(x0[u * 8 + 7])));
+          for (int e = 0; e < 16; ++e) w0[e] = pack_f16x2(__uint_as_float(x0[2 * e]), __uint_as_float(x0[2 * e + 1]));
+          stg_v8(dst0, w0[0], w0[1], w0[2], w0[3], w0[4], w0[5], w0[6], w0[7]);
+          stg_v8(dst0 + 16, w0[8], w0[9], w0[10], w0[11], w0[12], w0[13], w0[14], w0[15]);
+          __half* dst1 = h == 0 ? k_out + ((static_cast<size_t>(bi) * kHeads + cc) * N + j) * kHeadDim
+                                : g_out + (static_cast<size_t>(bi) * N + j) * 128 + cc * 32;
+          uint32_t w1[16];
           if (h == 0) {
-            uint4* d1 = reinterpret_cast<uint4*>(k_out + ((static_cast<size_t>(bi) * kHeads + cc) * N + j) * kHeadDim);
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
-              d1[u] = make_uint4(pack_f16x2(__uint_as_float(x1[u * 8 + 0]), __uint_as_float(x1[u * 8 + 1])),
-                                 pack_f16x2(__uint_as_float(x1[u * 8 + 2]), __uint_as_float(x1[u * 8 + 3])),
-                                 pack_f16x2(__uint_as_float(x1[u * 8 + 4]), __uint_as_float(x1[u * 8 + 5])),
-                                 pack_f16x2(__uint_as_float(x1[u * 8 + 6]), __uint_as_float(x1[u * 8 + 7])));
+            for (int e = 0; e < 16; ++e) w1[e] = pack_f16x2(__uint_as_float(x1[2 * e]), __uint_as_float(x1[2 * e + 1]));
           } else {
-            uint4* d1 = reinterpret_cast<uint4*>(g_out + (static_cast<size_t>(bi) * N + j) * 128 + cc * 32);
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              float gv[8];
-#pragma unroll
-              for (int e = 0; e < 8; ++e) gv[e] = sigmoid_tanh(__uint_as_float(x1[u * 8 + e]) + bg[cc * 32 + u * 8 + e]);
-              d1[u] = make_uint4(pack_f16x2(gv[0], gv[1]), pack_f16x2(gv[2], gv[3]), pack_f16x2(gv[4], gv[5]),
-                                 pack_f16x2(gv[6], gv[7]));
-            }
+            for (int e = 0; e < 16; ++e)
+              w1[e] = pack_f16x2(sigmoid_tanh(__uint_as_float(x1[2 * e]) + bg[cc * 32 + 2 * e]),
+                                 sigmoid_tanh(__uint_as_float(x1[2 * e + 1]) + bg[cc * 32 + 2 * e + 1]));
           }
+          stg_v8(dst1, w1[0], w1[1], w1[2], w1[3], w1[4], w1[5], w1[6], w1[7]);
+          stg_v8(dst1 + 16, w1[8], w1[9], w1[10], w1[11], w1[12], w1[13], w1[14], w1[15]);
         }
         tc_fence_before();
         mbar_arrive(&bars->d_empty[h]);

@@ -84,14 +84,17 @@ __global__ void trimul_pack_kernel(gtk_trimul_params p, uint8_t* packed) {
 
 // ----------------------------------------------------------------------------------
 // K1: persistent, warp-specialised LN_in + gated projections + mask -> a, b planes.
-// Tile = 128 consecutive pairs (b, r, j0..j0+127); CTAs loop over tiles. 288 threads:
-//   warp 8     lane 0: TMA producer and MMA issuer. The 128 KB of packed weights are
+// Tile = 128 consecutive pairs (b, r, j0..j0+127); CTAs loop over tiles. 416 threads:
+//   warp 12    lane 0: TMA producer and MMA issuer. The 128 KB of packed weights are
 //              loaded once; each tile's 128 x 128 fp32 z block arrives by TMA (64 KB in
 //              flight per tile, refilled as soon as the LayerNorm has read it);
-//   warps 0-3  LayerNorm producers: thread p normalises pair row p from the staged,
-//              128-B-swizzled z tile (reductions in registers, conflict-free reads) into
-//              the fp16 operand tile A, and stages the pair's mask value;
-//   warps 4-7  epilogue: thread = channel c (TMEM lane), reads 32-pair slabs of the
+//   warps 0-7  LayerNorm producers, two threads per pair row (64 channels each, statistics
+//              combined with one shuffle): one pass reads the staged, 128-B-swizzled z tile
+//              into registers (conflict-free) and releases it, then the fp16 operand tile A
+//              is written; the pair's mask value is staged as well. (One thread per row
+//              with three passes over the tile kept the z buffer busy through the whole
+//              LayerNorm, serialising it with the next tile's load.)
+//   warps 8-11 epilogue: thread = channel c (TMEM lane), reads 32-pair slabs of the
 //              projection / gate accumulators, applies bias, sigmoid and mask, and writes
 //              64 contiguous bytes of its channel-plane row per slab.
 // MMA (transposed so that channels sit on TMEM lanes): D[c][j] = W_chunk[c][:] . A[j][:],
@@ -103,7 +106,7 @@ __global__ void trimul_pack_kernel(gtk_trimul_params p, uint8_t* packed) {
 // Shared memory: W1 128 KB | A 32 KB | z 64 KB | mask 2 x 512 B | barriers.
 // ----------------------------------------------------------------------------------
 namespace k1 {
-constexpr int kThreads = 288;
+constexpr int kThreads = 416;
 constexpr uint32_t kW = 0, kA = 131072, kZ = 163840, kMask = 229376, kBar = 230400;
 constexpr uint32_t kSmem = kBar + 128 + 1024;
 static_assert(kSmem <= 232448, "K1 shared memory");
@@ -137,8 +140,8 @@ __global__ void __launch_bounds__(k1::kThreads, 1)
     guard->abort = 0;
     mbar_init(&bars->wbar, 1);
     mbar_init(&bars->z_full, 1);
-    mbar_init(&bars->z_empty, 128);
-    mbar_init(&bars->a_full, 128);
+    mbar_init(&bars->z_empty, 256);
+    mbar_init(&bars->a_full, 256);
     mbar_init(&bars->a_empty, 1);
     for (int x = 0; x < 2; ++x) {
       mbar_init(&bars->d_full[x], 1);
@@ -148,7 +151,7 @@ __global__ void __launch_bounds__(k1::kThreads, 1)
     mbar_init(&bars->drain, 1);
     fence_barrier_init();
   }
-  if (warp == 8) {
+  if (warp == 12) {
     tmem_alloc(&bars->tslot, 512);
     tmem_relinquish();
   }
@@ -157,26 +160,72 @@ __global__ void __launch_bounds__(k1::kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = bars->tslot;
 
-  if (warp < 4) {
-    // ------------------- LayerNorm producers: thread = pair row -------------------
-    const int p = tid;
+  if (warp < 8) {
+    // --------------- LayerNorm producers: two threads per pair row ---------------
+    // Each thread reads its 64 channels of the staged z tile into registers once and
+    // releases the tile, so the next tile's z load overlaps the rest of the LayerNorm.
+    const int p = warp * 16 + (lane >> 1), half = lane & 1;
+    const float* lnw = vec + tmpack::kVLnW + half * 64;
+    const float* lnb = vec + tmpack::kVLnB + half * 64;
     int it = 0;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
       const int s = it & 1;
       const int jt = tile % n_jt, rb = tile / n_jt;
       const int r = rb % rows, b = rb / rows, j0 = jt * 128;
-      bool w = mbar_wait(&bars->z_full, it & 1, guard, status, kStatusTimeoutProducer);
-      if (it >= 1) w = w && mbar_wait(&bars->a_empty, (it - 1) & 1, guard, status, kStatusTimeoutProducer);
+      if (!__all_sync(0xffffffffu, mbar_wait(&bars->z_full, it & 1, guard, status, kStatusTimeoutProducer))) break;
+      float v[64];
+#pragma unroll
+      for (int q = 0; q < 2; ++q)
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch) {
+          const float4 t = lds_f4(smem + k1::kZ + (2 * half + q) * 16384 + swz128(p, ch));
+          v[q * 32 + ch * 4 + 0] = t.x;
+          v[q * 32 + ch * 4 + 1] = t.y;
+          v[q * 32 + ch * 4 + 2] = t.z;
+          v[q * 32 + ch * 4 + 3] = t.w;
+        }
+      mbar_arrive(&bars->z_empty);  // the z tile may be refilled
+      float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < 64; ++c) s4[c & 3] += v[c];
+      float sum = (s4[0] + s4[1]) + (s4[2] + s4[3]);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+      const float mean = sum * (1.f / 128.f);
+      float q4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        const float d = v[c] - mean;
+        q4[c & 3] += d * d;
+      }
+      float ss = (q4[0] + q4[1]) + (q4[2] + q4[3]);
+      ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+      const float rstd = rsqrtf(ss * (1.f / 128.f) + 1e-5f);
+      bool w = true;
+      if (it >= 1) w = mbar_wait(&bars->a_empty, (it - 1) & 1, guard, status, kStatusTimeoutProducer);
       if (it >= 2) w = w && mbar_wait(&bars->m_empty[s], ((it >> 1) - 1) & 1, guard, status, kStatusTimeoutProducer);
       if (!__all_sync(0xffffffffu, w)) break;
-      const int j = j0 + p;
-      mask_s[s * 128 + p] = j < N ? (mask ? mask[(static_cast<size_t>(b) * rows + r) * N + j] : 1.f) : 0.f;
-      ln_row_to_operand(smem + k1::kZ, smem + k1::kA, p, vec + tmpack::kVLnW, vec + tmpack::kVLnB);
-      mbar_arrive(&bars->z_empty);  // the z tile may be refilled
+      if (half == 0) {
+        const int j = j0 + p;
+        mask_s[s * 128 + p] = j < N ? (mask ? mask[(static_cast<size_t>(b) * rows + r) * N + j] : 1.f) : 0.f;
+      }
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        const int c = ch * 8;
+        const float4 w0 = __ldg(reinterpret_cast<const float4*>(lnw + c));
+        const float4 w1 = __ldg(reinterpret_cast<const float4*>(lnw + c + 4));
+        const float4 b0 = __ldg(reinterpret_cast<const float4*>(lnb + c));
+        const float4 b1 = __ldg(reinterpret_cast<const float4*>(lnb + c + 4));
+        uint4 o;
+        o.x = pack_f16x2((v[c + 0] - mean) * rstd * w0.x + b0.x, (v[c + 1] - mean) * rstd * w0.y + b0.y);
+        o.y = pack_f16x2((v[c + 2] - mean) * rstd * w0.z + b0.z, (v[c + 3] - mean) * rstd * w0.w + b0.w);
+        o.z = pack_f16x2((v[c + 4] - mean) * rstd * w1.x + b1.x, (v[c + 5] - mean) * rstd * w1.y + b1.y);
+        o.w = pack_f16x2((v[c + 6] - mean) * rstd * w1.z + b1.z, (v[c + 7] - mean) * rstd * w1.w + b1.w);
+        sts_u4(smem + k1::kA + half * 16384 + swz128(p, ch), o);
+      }
       fence_proxy_async_smem();
       mbar_arrive(&bars->a_full);
     }
-  } else if (warp == 8) {
+  } else if (warp == 12) {
     // ------------------------- TMA producer + MMA issuer -------------------------
     if (lane == 0) {
       auto load_z = [&](int tile) {
@@ -254,6 +303,8 @@ __global__ void __launch_bounds__(k1::kThreads, 1)
         if (!ok) break;
         tc_fence_after();
         __half* dst = (h ? b_out : a_out) + ((static_cast<size_t>(b) * rows + r) * 128 + c) * ld;
+        const bool wide = (ld & 15) == 0 && (reinterpret_cast<uintptr_t>(a_out) & 31) == 0 &&
+                          (reinterpret_cast<uintptr_t>(b_out) & 31) == 0;
         const float bp = h ? bias_p1 : bias_p0, bg = h ? bias_g1 : bias_g0;
 #pragma unroll 1
         for (int jc = 0; jc < 4; ++jc) {
@@ -261,24 +312,32 @@ __global__ void __launch_bounds__(k1::kThreads, 1)
           tmem_ld32(tmem + lane_off + h * 256 + jc * 32, pv);
           tmem_ld32(tmem + lane_off + h * 256 + 128 + jc * 32, gv);
           tmem_wait_ld();
+          uint32_t w[16];  // 32 pairs of this channel as fp16
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int jj = j0 + jc * 32 + u * 8;
-            const float4 m0 = *reinterpret_cast<const float4*>(ms + jc * 32 + u * 8);
-            const float4 m1 = *reinterpret_cast<const float4*>(ms + jc * 32 + u * 8 + 4);
-            const float mv[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
-            float o[8];
+          for (int u = 0; u < 8; ++u) {
+            const float4 m4 = *reinterpret_cast<const float4*>(ms + jc * 32 + u * 4);
+            const float mv[4] = {m4.x, m4.y, m4.z, m4.w};
+            float o[4];
 #pragma unroll
-            for (int e = 0; e < 8; ++e)
-              o[e] = (__uint_as_float(pv[u * 8 + e]) + bp) * sigmoid_tanh(__uint_as_float(gv[u * 8 + e]) + bg) * mv[e];
-            if (jj < ld) {
-              uint4 w;
-              w.x = pack_f16x2(o[0], o[1]);
-              w.y = pack_f16x2(o[2], o[3]);
-              w.z = pack_f16x2(o[4], o[5]);
-              w.w = pack_f16x2(o[6], o[7]);
-              *reinterpret_cast<uint4*>(dst + jj) = w;
-            }
+            for (int e = 0; e < 4; ++e)
+              o[e] = (__uint_as_float(pv[u * 4 + e]) + bp) * sigmoid_tanh(__uint_as_float(gv[u * 4 + e]) + bg) * mv[e];
+            w[2 * u] = pack_f16x2(o[0], o[1]);
+            w[2 * u + 1] = pack_f16x2(o[2], o[3]);
+          }
+          // 64 contiguous bytes of the channel row: 32-byte stores when the plane pitch keeps
+          // them 32-byte aligned (pitch a multiple of 16), 16-byte stores otherwise
+          const int jb = j0 + jc * 32;
+          if (wide) {
+#pragma unroll
+            for (int v = 0; v < 2; ++v)
+              if (jb + 16 * v < ld)
+                stg_v8(dst + jb + 16 * v, w[8 * v], w[8 * v + 1], w[8 * v + 2], w[8 * v + 3], w[8 * v + 4],
+                       w[8 * v + 5], w[8 * v + 6], w[8 * v + 7]);
+          } else {
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+              if (jb + 8 * v < ld)
+                *reinterpret_cast<uint4*>(dst + jb + 8 * v) = make_uint4(w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
           }
         }
         tc_fence_before();
@@ -290,7 +349,7 @@ __global__ void __launch_bounds__(k1::kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 8) {
+  if (warp == 12) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
