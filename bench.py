@@ -519,7 +519,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--N", type=int, default=1024)
     ap.add_argument("--layers", type=int, default=8)
-    ap.add_argument("--cpu-rows", type=int, default=16)
+    ap.add_argument("--cpu-rows", type=int, default=96)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--trimul-exchange", default="auto", choices=["auto", "gather", "channels"],
