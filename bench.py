@@ -388,8 +388,12 @@ def run_sharded(args, rank, world, device):
     z = torch.empty_like(z0)
     stack = make_stack(L, device)
     so = TimedStageOps(CudaStageOps(device))
-    shard = ShardedTrianglePairStack(stack, world, rank, stage_ops=so, trimul_exchange=args.trimul_exchange)
-    shard.prepare(B, N, device)
+    shard = ShardedTrianglePairStack(stack, world, rank, stage_ops=so, trimul_exchange=args.trimul_exchange,
+                                     exchange=args.exchange)
+    if args.exchange == "peer":
+        shard.connect(None, B, N, device)
+    else:
+        shard.prepare(B, N, device)
 
     def step(zin=None, hook=None):
         so.hook = hook
@@ -468,7 +472,9 @@ def run_sharded(args, rank, world, device):
                "ms_per_step": e_ms, "note": "each rank copies its own row shard in and out"}
     peaks = load_peaks()
     stack_tflops = B * N * N * L * layer_flops(N) / (ms_per_step / 1e3) / 1e12
-    dom = max((k for k in breakdown if not k.startswith("nccl_")), key=lambda k: breakdown[k]["ms"])
+    stage_kernels = ("triatt_core", "trimul_contract", "trimul_project", "trimul_finish", "triatt_project",
+                     "triatt_finish")
+    dom = max((k for k in breakdown if k in stage_kernels), key=lambda k: breakdown[k]["ms"])
     bound, work = kernel_work(dom, N, B)
     calls = sum(1 for lab, _ in labels if lab == dom)
     avg_ms = per[dom] / calls
@@ -485,7 +491,7 @@ def run_sharded(args, rank, world, device):
                                    f"{L} layers x [TriMulOut, TriMulIn, TriAttStart, TriAttEnd]",
                        "global_batch": B, "seq_len": N, "layers": L,
                        "parallelism": f"row-sharded over i, {world} ranks x {R} rows (NCCL)",
-                       "trimul_exchange": shard.trimul_exchange,
+                       "trimul_exchange": shard.trimul_exchange, "exchange": args.exchange,
                        "l2": "inputs larger than L2 (each shard is >= 64 MB fp32); no flush"},
             "stack_tflops": round(stack_tflops, 1),
             "stack_frac_of_bf16_peak": round(stack_tflops / peaks["bf16_tflops"] / world, 4),
@@ -494,6 +500,7 @@ def run_sharded(args, rank, world, device):
                 "frac": round(ach / peak, 4), "traffic": None, "peak_source": peaks["source"],
                 "note": "rank 0's eager per-kernel timing of one extra step"},
             "breakdown_rank0": breakdown, "clocks": clocks, "status_word": status}
+    shard.close()
     return line
 
 
@@ -522,6 +529,8 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=96)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                    help="multi-GPU exchanges: peer-memory push kernels over NVLink, or NCCL collectives")
     ap.add_argument("--trimul-exchange", default="auto", choices=["auto", "gather", "channels"],
                     help="multi-GPU exchange of the multiplicative update (auto: gather for <= 3 GPUs)")
     args = ap.parse_args()

@@ -20,7 +20,11 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cstring>
+#include <string>
+
 #include "gtk_host.h"
+#include "gtk_sm100.cuh"
 
 namespace gtk {
 
@@ -59,6 +63,72 @@ __global__ void __launch_bounds__(256) pair_transpose_pack_kernel(const float4* 
   }
 }
 
+// Push form of copy_3d: slab k goes to its own destination base dsts[k] (a peer GPU's
+// buffer mapped into this process, or a local buffer), so packing, transfer over NVLink and
+// placement are one pass. dsts lives in device memory (P pointers).
+__global__ void __launch_bounds__(256) push_3d_kernel(const uint64_t* __restrict__ dsts, int64_t doff, int64_t dpitch,
+                                                      const uint8_t* __restrict__ src, int64_t spitch, int64_t sslab,
+                                                      int64_t w16, int64_t height, int64_t total) {
+  for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = e / w16, c = e - row * w16;
+    const int64_t k = row / height, r = row - k * height;
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(src + k * sslab + r * spitch) + c);
+    uint8_t* dst = reinterpret_cast<uint8_t*>(__ldg(dsts + k)) + doff + r * dpitch;
+    reinterpret_cast<uint4*>(dst)[c] = v;
+  }
+}
+
+// Push form of the pair-grid transpose: pair (b, y, q*(C/P) + x) of src [B][R][C][128] fp32
+// goes to dsts[q] at pair ((b*(C/P) + x)*ndst + row0 + y), i.e. straight into row x,
+// column row0 + y of peer q's transposed shard [B][C/P][ndst][128]. One warp per 512-B
+// pair vector; warps walk the source in order (coalesced reads).
+__global__ void __launch_bounds__(256) push_pair_transpose_kernel(const float4* __restrict__ src,
+                                                                  const uint64_t* __restrict__ dsts, int64_t B,
+                                                                  int64_t R, int64_t C, int64_t P, int64_t ndst,
+                                                                  int64_t row0) {
+  const int lane = threadIdx.x & 31;
+  const int64_t CP = C / P;
+  const int64_t n_pairs = B * R * C;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t w = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); w < n_pairs;
+       w += warps) {
+    // source pair index w = (b * R + y) * C + col
+    const int64_t col = w % C;
+    const int64_t t = w / C;
+    const int64_t y = t % R, b = t / R;
+    const int64_t q = col / CP, x = col - q * CP;
+    float4* dst = reinterpret_cast<float4*>(__ldg(dsts + q)) + (((b * CP + x) * ndst + row0 + y) * 32 + lane);
+    *dst = __ldg(src + w * 32 + lane);
+  }
+}
+
+// Stream-ordered barrier over P ranks through flags in peer memory. Thread t publishes
+// `epoch` into slot `rank` of rank t's flag array (after a system-scope fence, so the
+// writes this rank's earlier kernels made into rank t's memory are visible first), then
+// waits until slot t of this rank's own array has reached `epoch`. The wait is bounded:
+// after 2 s it sets kStatusTimeoutPeer in the status word and returns.
+__global__ void peer_barrier_kernel(const uint64_t* __restrict__ flags, int rank, int P, uint32_t epoch,
+                                    uint32_t* status) {
+  const int t = threadIdx.x;
+  if (t >= P) return;
+  __threadfence_system();
+  uint32_t* remote = reinterpret_cast<uint32_t*>(flags[t]) + rank;
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(remote), "r"(epoch) : "memory");
+  const uint32_t* mine = reinterpret_cast<const uint32_t*>(flags[rank]) + t;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+    if (static_cast<int32_t>(v - epoch) >= 0) break;
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      if (status) atomicOr(status, kStatusTimeoutPeer);
+      break;
+    }
+    __nanosleep(64);
+  }
+}
+
 static int grid_for(int64_t work_items, int per_block) {
   const int64_t blocks = (work_items + per_block - 1) / per_block;
   const int64_t cap = static_cast<int64_t>(num_sms()) * 8;
@@ -90,6 +160,83 @@ int gtk_copy_3d(void* dst, int64_t dpitch, int64_t dslab, const void* src, int64
 int gtk_copy_2d(void* dst, int64_t dpitch, const void* src, int64_t spitch, int64_t width, int64_t height,
                 void* stream) {
   return gtk_copy_3d(dst, dpitch, 0, src, spitch, 0, width, height, 1, stream);
+}
+
+int gtk_peer_alloc(size_t bytes, void** ptr, void* handle) {
+  if (!ptr || !handle || bytes == 0) return fail(GTK_ERR_INVALID_ARG, "peer_alloc: bad arguments");
+  if (int e = check_device()) return e;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return fail(GTK_ERR_CUDA, std::string("peer_alloc: cudaMalloc: ") + cudaGetErrorString(e));
+  e = cudaMemset(p, 0, bytes);
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return fail(GTK_ERR_CUDA, std::string("peer_alloc: ") + cudaGetErrorString(e));
+  }
+  static_assert(sizeof(h) == GTK_PEER_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(handle, &h, sizeof(h));
+  *ptr = p;
+  return GTK_OK;
+}
+
+int gtk_peer_free(void* ptr) {
+  if (!ptr) return GTK_OK;
+  const cudaError_t e = cudaFree(ptr);
+  return e == cudaSuccess ? GTK_OK : fail(GTK_ERR_CUDA, std::string("peer_free: ") + cudaGetErrorString(e));
+}
+
+int gtk_peer_open(const void* handle, void** ptr) {
+  if (!ptr || !handle) return fail(GTK_ERR_INVALID_ARG, "peer_open: bad arguments");
+  if (int e = check_device()) return e;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  return e == cudaSuccess ? GTK_OK : fail(GTK_ERR_CUDA, std::string("peer_open: ") + cudaGetErrorString(e));
+}
+
+int gtk_peer_close(void* ptr) {
+  if (!ptr) return GTK_OK;
+  const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  return e == cudaSuccess ? GTK_OK : fail(GTK_ERR_CUDA, std::string("peer_close: ") + cudaGetErrorString(e));
+}
+
+int gtk_push_3d(const uint64_t* dsts, int P, int64_t doff, int64_t dpitch, const void* src, int64_t spitch,
+                int64_t sslab, int64_t width, int64_t height, void* stream) {
+  if (P < 1 || width < 0 || height < 0 || doff < 0 || dpitch < width || spitch < width || sslab < 0)
+    return fail(GTK_ERR_INVALID_ARG, "push_3d: bad sizes");
+  if (width == 0 || height == 0) return GTK_OK;
+  if ((width | dpitch | spitch | sslab | doff) & 15)
+    return fail(GTK_ERR_ALIGNMENT, "push_3d: width, pitches, offsets and slab strides must be 16-B multiples");
+  if (int e = check_ptr(dsts, "dsts", 8)) return e;
+  if (int e = check_ptr(src, "src")) return e;
+  if (int e = check_device()) return e;
+  const int64_t w16 = width / 16, total = w16 * height * P;
+  push_3d_kernel<<<grid_for(total, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      dsts, doff, dpitch, static_cast<const uint8_t*>(src), spitch, sslab, w16, height, total);
+  return check_launch("push_3d_kernel");
+}
+
+int gtk_push_pair_transpose(const float* src, const uint64_t* dsts, int64_t B, int64_t R, int64_t C, int64_t P,
+                            int64_t ndst, int64_t row0, void* stream) {
+  if (B < 1 || R < 1 || C < 1 || P < 1 || C % P || row0 < 0 || row0 + R > ndst)
+    return fail(GTK_ERR_INVALID_ARG, "push_pair_transpose: need C divisible by P and row0 + R <= ndst");
+  if (int e = check_ptr(src, "src")) return e;
+  if (int e = check_ptr(dsts, "dsts", 8)) return e;
+  if (int e = check_device()) return e;
+  push_pair_transpose_kernel<<<grid_for(B * R * C, 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const float4*>(src), dsts, B, R, C, P, ndst, row0);
+  return check_launch("push_pair_transpose_kernel");
+}
+
+int gtk_peer_barrier(const uint64_t* flag_ptrs, int rank, int P, uint32_t epoch, uint32_t* status, void* stream) {
+  if (P < 1 || P > 1024 || rank < 0 || rank >= P) return fail(GTK_ERR_INVALID_ARG, "peer_barrier: bad rank/P");
+  if (int e = check_ptr(flag_ptrs, "flag_ptrs", 8)) return e;
+  if (int e = check_device()) return e;
+  peer_barrier_kernel<<<1, ((P + 31) / 32) * 32, 0, static_cast<cudaStream_t>(stream)>>>(flag_ptrs, rank, P, epoch,
+                                                                                         status);
+  return check_launch("peer_barrier_kernel");
 }
 
 int gtk_pair_transpose_pack(const float* src, float* dst, int64_t B, int64_t R, int64_t C, int64_t P, void* stream) {

@@ -25,6 +25,7 @@ enum StatusBits : uint32_t {
   kStatusTimeoutConsumer = 1u << 2,
   kStatusTimeoutDrain = 1u << 3,
   kStatusBadLaunch = 1u << 4,
+  kStatusTimeoutPeer = 1u << 5,  // a cross-GPU barrier ran out (a peer never arrived)
 };
 
 // Wall-clock limit for any single wait: 2 s is orders of magnitude above any

@@ -67,6 +67,13 @@ _SIGNATURES = {
     "gtk_copy_2d": (c_int, [c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_vp]),
     "gtk_copy_3d": (c_int, [c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp]),
     "gtk_pair_transpose_pack": (c_int, [c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp]),
+    "gtk_peer_alloc": (c_int, [c_size, ctypes.POINTER(c_vp), c_vp]),
+    "gtk_peer_free": (c_int, [c_vp]),
+    "gtk_peer_open": (c_int, [c_vp, ctypes.POINTER(c_vp)]),
+    "gtk_peer_close": (c_int, [c_vp]),
+    "gtk_push_3d": (c_int, [c_vp, c_int, c_i64, c_i64, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp]),
+    "gtk_push_pair_transpose": (c_int, [c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp]),
+    "gtk_peer_barrier": (c_int, [c_vp, c_int, c_int, ctypes.c_uint32, c_vp, c_vp]),
 }
 
 

@@ -130,6 +130,14 @@ class CudaStageOps:
         self._chk(self.lib.gtk_pair_transpose_pack(ops._ptr(src), ops._ptr(dst), B, R, Cn, P, self._s()),
                   "gtk_pair_transpose_pack")
 
+    def push_3d(self, dst: "PeerBuffer", doff, dpitch, src, spitch, sslab, width, height):
+        self._chk(self.lib.gtk_push_3d(ops._ptr(dst.ptrs), dst.ptrs.numel(), doff, dpitch, ops._ptr(src), spitch, sslab,
+                                       width, height, self._s()), "gtk_push_3d")
+
+    def push_pair_transpose(self, src, dst: "PeerBuffer", B, R, Cn, P, ndst, row0):
+        self._chk(self.lib.gtk_push_pair_transpose(ops._ptr(src), ops._ptr(dst.ptrs), B, R, Cn, P, ndst, row0,
+                                                   self._s()), "gtk_push_pair_transpose")
+
     def triatt_layout(self, B, rows, N) -> Dict[str, int]:
         offs = (ctypes.c_int64 * 7)()
         self._chk(self.lib.gtk_triatt_workspace_offsets(B, rows, N, offs), "gtk_triatt_workspace_offsets")
@@ -140,17 +148,42 @@ def _round256(n: int) -> int:
     return (int(n) + 255) // 256 * 256
 
 
+class PeerBuffer:
+    """A receive buffer that every rank may write into: this rank's ``local`` uint8 tensor
+    and ``ptrs``, a device int64 tensor with the base address of the same buffer on every
+    rank (peer buffers mapped into this process, or, for ranks emulated in one process,
+    their local tensors, which are also listed in ``tensors``)."""
+
+    def __init__(self, local: Tensor, ptrs: Tensor, tensors: Optional[List[Tensor]] = None):
+        self.local, self.ptrs, self.tensors = local, ptrs, tensors
+
+
+class _CudaArray:
+    """Exposes a device allocation to ``torch.as_tensor`` (``__cuda_array_interface__``)."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
 class ShardedTrianglePairStack:
     """One rank's share of a :class:`TrianglePairStack` whose pair tensor is row-sharded.
 
     ``forward_(z_local, mask)`` updates this rank's rows ``z_local`` [B, N/P, N, 128] (fp32)
     in place; ``mask`` is the whole [B, N, N] mask (or None), identical on every rank.
+
+    ``exchange``: "nccl" runs the exchanges as NCCL collectives on packed chunks; "peer"
+    pushes every rank's share straight into the peers' buffers with the exchange kernels
+    (CUDA IPC mappings over NVLink) and orders them with a device-side barrier. Peer mode
+    needs ``connect(group, B, N)`` once (a collective) before ``forward_``, and ``close()``.
     """
 
     def __init__(self, stack: TrianglePairStack, world: int, rank: int, stage_ops=None,
-                 trimul_exchange: str = "auto"):
+                 trimul_exchange: str = "auto", exchange: str = "nccl"):
         if trimul_exchange not in ("auto", "gather", "channels"):
             raise ValueError(f"trimul_exchange must be auto, gather or channels, not {trimul_exchange!r}")
+        if exchange not in ("nccl", "peer"):
+            raise ValueError(f"exchange must be nccl or peer, not {exchange!r}")
         self.stack = stack
         self.world, self.rank = world, rank
         self.stage_ops = stage_ops
@@ -158,68 +191,169 @@ class ShardedTrianglePairStack:
         # the incoming a), channels 3 (P-1)/P planes -> the gather wins for P <= 3
         self.trimul_exchange = trimul_exchange if trimul_exchange != "auto" else (
             "gather" if world <= 3 else "channels")
+        self.exchange = exchange
         self._key = None
         self._buf: Dict[str, Tensor] = {}
+        self._peer: Dict[str, PeerBuffer] = {}
+        self._ipc_own: List[int] = []     # allocations made here (peer_alloc)
+        self._ipc_open: List[int] = []    # peer mappings opened here
+        self._epoch = 0
 
     # ---------------------------------------------------------------- buffers
+    def _sizes(self, spec: ShardSpec):
+        """(local buffers, buffers other ranks write into), name -> bytes."""
+        B, N, R = spec.B, spec.N, spec.R
+        plane = B * R * C * N * 2          # one rank's planes, fp16, pitch N (row or channel shard)
+        lay = self.stage_ops.triatt_layout(B, R, N)
+        pair_loc = B * R * N * PAIR_BYTES  # one row shard of the pair tensor, fp32
+        local = {"a": plane, "b": plane}
+        recv = {"tri": lay["total"], "zT": pair_loc}
+        if self.trimul_exchange == "channels":
+            local["x_ch"] = plane                                   # [B][N][C/P][N]
+            recv.update({"a_ch": plane, "b_ch": plane, "x": plane})
+        else:
+            local["x"] = plane
+            recv["a_recv"] = plane                                  # [B][N][C][R]
+            if self.exchange == "nccl":
+                recv["b_all"] = B * N * C * N * 2                  # [B][N][C][N]
+            else:
+                # two copies: a push for the incoming update must not land in the buffer the
+                # outgoing contraction of a slower rank may still be reading (no barrier
+                # separates them in this exchange)
+                recv["b_all0"] = recv["b_all1"] = B * N * C * N * 2
+        if self.exchange == "nccl":
+            local.update({"send": plane, "x_recv": plane, "bias_send": R * B * H * N * 2,
+                          "t_send": pair_loc, "t_recv": pair_loc})
+            local.update(recv)
+            recv = {}
+        else:
+            recv.update({"zs": pair_loc, "flags": 256})   # the residual stream; barrier flags
+        return local, recv, lay
+
     def prepare(self, B: int, N: int, device: torch.device) -> ShardSpec:
         spec = ShardSpec(B, N, self.world, self.rank)
         if self.stage_ops is None:
             self.stage_ops = CudaStageOps(device)
         if self._key == (B, N):
             return spec
+        if self.exchange == "peer":
+            raise RuntimeError("ShardedTrianglePairStack(exchange='peer'): call connect() (or connect_emulated) "
+                               "before running")
+        local, recv, lay = self._sizes(spec)
         so = self.stage_ops
-        R = spec.R
-        plane = B * R * C * N * 2          # one rank's planes, fp16, pitch N (row or channel shard)
-        lay = so.triatt_layout(B, R, N)
-        bias_rows = R * B * H * N * 2      # this rank's rows of the bias region
-        pair_loc = B * R * N * PAIR_BYTES  # one row shard of the pair tensor, fp32
-        sizes = {
-            "a": plane, "b": plane, "x": plane,           # row shards [B][R][C][N]
-            "send": plane, "x_recv": plane,               # all-to-all staging
-            "tri": lay["total"], "bias_send": bias_rows,
-            "zT": pair_loc, "t_send": pair_loc, "t_recv": pair_loc,
-        }
-        if self.trimul_exchange == "channels":
-            sizes.update({"a_ch": plane, "b_ch": plane, "x_ch": plane})   # channel shards [B][N][C/P][N]
-        else:
-            sizes.update({"a_recv": plane,                 # a columns of this rank, all rows: [B][N][C][R]
-                          "b_all": B * N * C * N * 2})    # gathered b planes [B][N][C][N]
-        self._buf = {k: so.alloc(_round256(v)) for k, v in sizes.items()}
+        self._buf = {k: so.alloc(_round256(v)) for k, v in local.items()}
         self._lay = lay
         self._key = (B, N)
+        self._pack_weights(device)
+        return spec
+
+    def _pack_weights(self, device):
+        so = self.stage_ops
         if isinstance(so, CudaStageOps) or isinstance(getattr(so, "inner", None), CudaStageOps):
             for layer in self.stack.layers:
                 for name in OP_NAMES:
                     getattr(layer, name).packed_weights(device)
-        return spec
+
+    @torch.no_grad()
+    def connect(self, group, B: int, N: int, device: torch.device) -> None:
+        """Peer mode, one process per GPU: allocate the receive buffers in IPC-shareable
+        memory, exchange their handles over ``group`` and map the peers' buffers. A
+        collective: every rank calls it with the same B and N."""
+        import torch.distributed as dist
+        if self.exchange != "peer":
+            raise RuntimeError("connect() is for exchange='peer'")
+        spec = ShardSpec(B, N, self.world, self.rank)
+        if self.stage_ops is None:
+            self.stage_ops = CudaStageOps(device)
+        self.close()
+        local, recv, lay = self._sizes(spec)
+        lib = ops._lib.load()
+        so = self.stage_ops
+        self._buf = {k: so.alloc(_round256(v)) for k, v in local.items()}
+        handles = {}
+        for name, nbytes in recv.items():
+            nbytes = _round256(nbytes)
+            ptr = ctypes.c_void_p()
+            h = ctypes.create_string_buffer(64)
+            ops._lib.check(lib.gtk_peer_alloc(nbytes, ctypes.byref(ptr), h), "gtk_peer_alloc")
+            self._ipc_own.append(ptr.value)
+            self._buf[name] = torch.as_tensor(_CudaArray(ptr.value, nbytes), device=device)
+            handles[name] = (h.raw, nbytes)
+        gathered = [None] * self.world
+        dist.all_gather_object(gathered, handles, group=group)
+        for name in recv:
+            addrs = []
+            for q in range(self.world):
+                if q == self.rank:
+                    addrs.append(self._buf[name].data_ptr())
+                    continue
+                ptr = ctypes.c_void_p()
+                ops._lib.check(lib.gtk_peer_open(gathered[q][name][0], ctypes.byref(ptr)), "gtk_peer_open")
+                self._ipc_open.append(ptr.value)
+                addrs.append(ptr.value)
+            self._peer[name] = PeerBuffer(self._buf[name],
+                                          torch.tensor(addrs, dtype=torch.int64, device=device))
+        self._lay = lay
+        self._key = (B, N)
+        self._epoch = 0
+        self._pack_weights(device)
+        dist.barrier(group=group)
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's IPC allocations (peer mode)."""
+        if not (self._ipc_open or self._ipc_own):
+            return
+        lib = ops._lib.load()
+        torch.cuda.synchronize()
+        for p in self._ipc_open:
+            lib.gtk_peer_close(ctypes.c_void_p(p))
+        self._peer.clear()
+        self._buf.clear()
+        for p in self._ipc_own:
+            lib.gtk_peer_free(ctypes.c_void_p(p))
+        self._ipc_open, self._ipc_own = [], []
+        self._key = None
 
     # ---------------------------------------------------------------- the per-rank program
     def steps(self, z: Tensor, mask: Optional[Tensor], z_in: Optional[Tensor] = None
               ) -> Generator[Request, None, None]:
-        """This rank's stack as a generator of collective requests (see module docstring).
+        """This rank's stack as a generator of exchange requests (see module docstring).
         ``z`` is updated in place; with ``z_in`` the first block reads ``z_in`` instead and
         writes ``z`` (``z_in`` is left unchanged)."""
         B, R, N = z.shape[0], z.shape[1], z.shape[2]
-        spec = self.prepare(B, N, z.device)
+        spec = self.prepare(B, N, z.device) if self.exchange == "nccl" else ShardSpec(B, N, self.world, self.rank)
+        if self._key != (B, N):
+            raise RuntimeError("ShardedTrianglePairStack: connect() was made for other sizes")
         if R != spec.R:
             raise ValueError(f"z_local has {R} rows; rank {self.rank} of {self.world} owns {spec.R}")
-        so, buf, lay = self.stage_ops, self._buf, self._lay
-        P, row0 = self.world, spec.row0
-        CP = C // P
-        src = z if z_in is None else z_in
+        if self.exchange == "peer":
+            yield from self._steps_peer(z, mask, z_in, spec)
+        else:
+            yield from self._steps_nccl(z, mask, z_in, spec)
+
+    def _common(self, z, mask, spec):
+        B, N, R = spec.B, spec.N, spec.R
         mask_loc = mask_t = None
         if mask is not None:
             mask_loc = mask[:, spec.rows()].contiguous()
             mask_t = mask.transpose(1, 2).contiguous()
+        tri = self._buf["tri"]
+        lay = self._lay
+        bias_all = tri[lay["bias"]:lay["bias"] + N * B * H * N * 2]
+        bias_mine = bias_all[spec.row0 * B * H * N * 2:(spec.row0 + R) * B * H * N * 2]
+        zT = self._buf["zT"][:B * R * N * PAIR_BYTES].view(torch.float32).view(B, R, N, C)
+        return mask_loc, mask_t, tri, bias_all, bias_mine, zT
+
+    def _steps_nccl(self, z, mask, z_in, spec):
+        so, buf = self.stage_ops, self._buf
+        B, N, R, P, row0 = spec.B, spec.N, spec.R, self.world, spec.row0
+        CP = C // P
+        src = z if z_in is None else z_in
+        mask_loc, mask_t, tri, bias_all, bias_mine, zT = self._common(z, mask, spec)
         xs = 1.0 / N
         plane_b = R * C * N * 2            # bytes of one batch element's planes (row or channel shard)
         chunk = R * CP * N * 2             # one peer's share of them
-        tri = buf["tri"]
-        bias_all = tri[lay["bias"]:lay["bias"] + N * B * H * N * 2]
-        bias_mine = bias_all[row0 * B * H * N * 2:(row0 + R) * B * H * N * 2]
         pair_chunk = B * R * R * PAIR_BYTES  # one peer's chunk of a pair-grid transpose
-        zT = buf["zT"][:B * R * N * PAIR_BYTES].view(torch.float32).view(B, R, N, C)
         t_send, t_recv = buf["t_send"], buf["t_recv"]
 
         def to_channels(rows_planes, ch_planes):
@@ -291,13 +425,93 @@ class ShardedTrianglePairStack:
             yield from transpose(zT, z)
             src = z
 
+    def _steps_peer(self, z_user, mask, z_in, spec):
+        """Peer-memory exchanges. A push may overwrite a peer's receive buffer only once every
+        rank has finished reading its previous contents; each exchange ends with a barrier
+        that every rank enters after its own consumers of the previous exchange have run
+        (stream order), so one barrier per exchange suffices for every buffer except the
+        gathered b planes, whose outgoing and incoming uses follow each other with a single
+        barrier in between and therefore alternate between two copies."""
+        so, buf, peer = self.stage_ops, self._buf, self._peer
+        B, N, R, P, row0, me = spec.B, spec.N, spec.R, self.world, spec.row0, self.rank
+        CP = C // P
+        mask_loc, mask_t, tri, bias_all, bias_mine, zT = self._common(z_user, mask, spec)
+        # the residual stream lives in peer memory (the transposed-back updates land there)
+        z = buf["zs"][:B * R * N * PAIR_BYTES].view(torch.float32).view(B, R, N, C)
+        src = z
+        if z_in is not None:
+            src = z_in
+        else:
+            so.copy_2d(_bytes(z), z.numel() * 4, _bytes(z_user), z.numel() * 4, z.numel() * 4, 1)
+        xs = 1.0 / N
+        plane_b = R * C * N * 2
+        tri_bias = self._lay["bias"]
+
+        def multiply_channels(mod, outgoing, zz):
+            so.trimul_project(mod, zz, mask_loc, buf["a"], buf["b"], B, R, N)
+            for bb in range(B):
+                # my rows, channel group q -> rows row0.. of peer q's channel shard
+                for name, planes in (("a_ch", buf["a"]), ("b_ch", buf["b"])):
+                    so.push_3d(peer[name], (bb * N + row0) * CP * N * 2, CP * N * 2, planes[bb * plane_b:], C * N * 2,
+                               CP * N * 2, CP * N * 2, R)
+            yield ("barrier",)
+            so.trimul_contract(outgoing, buf["a_ch"], buf["b_ch"], buf["x_ch"], B, N, N, N, N, N, N, xs, CP)
+            for bb in range(B):
+                # rows of peer p, my channel group -> channel group `me` of peer p's x rows
+                so.push_3d(peer["x"], (bb * R * C + me * CP) * N * 2, C * N * 2, buf["x_ch"][bb * plane_b:],
+                           CP * N * 2, R * CP * N * 2, CP * N * 2, R)
+            yield ("barrier",)
+            so.trimul_finish(mod, zz, buf["x"], N, xs, B, R, N, z)
+
+        def multiply_gather(mod, outgoing, zz):
+            so.trimul_project(mod, zz, mask_loc, buf["a"], buf["b"], B, R, N)
+            b_all = "b_all0" if outgoing else "b_all1"
+            for bb in range(B):
+                so.push_3d(peer[b_all], (bb * N + row0) * C * N * 2, plane_b, buf["b"][bb * plane_b:], plane_b, 0,
+                           plane_b, 1)
+                if not outgoing:
+                    # columns i of peer q, every local row k and channel -> rows row0.. of q's a
+                    so.push_3d(peer["a_recv"], (bb * N + row0) * C * R * 2, R * 2, buf["a"][bb * plane_b:], N * 2,
+                               R * 2, R * 2, R * C)
+            yield ("barrier",)
+            if outgoing:
+                so.trimul_contract(True, buf["a"], buf[b_all], buf["x"], B, R, N, N, N, N, N, xs)
+            else:
+                so.trimul_contract(False, buf["a_recv"], buf[b_all], buf["x"], B, R, N, N, R, N, N, xs)
+            so.trimul_finish(mod, zz, buf["x"], N, xs, B, R, N, z)
+
+        multiply = multiply_channels if self.trimul_exchange == "channels" else multiply_gather
+
+        def attention(mod, zz, mm):
+            so.triatt_project(mod, zz, tri, B, R, N, row0)
+            w = bias_mine.numel()
+            so.push_3d(peer["tri"], tri_bias + row0 * B * H * N * 2, w, bias_mine, w, 0, w, 1)
+            yield ("barrier",)
+            so.triatt_core(mod, mm, tri, B, R, N, row0)
+            so.triatt_finish(mod, zz, tri, B, R, N)
+
+        def transpose(src_pairs, dst_name):
+            so.push_pair_transpose(src_pairs, peer[dst_name], B, R, N, P, N, row0)
+            yield ("barrier",)
+
+        for layer in self.stack.layers:
+            yield from multiply(layer.tri_mul_out, True, src)
+            yield from multiply(layer.tri_mul_in, False, z)
+            yield from attention(layer.tri_att_start, z, mask)
+            # TriAttEnd = Start(z^T, mask^T)^T, the residual added on the transposed shard
+            yield from transpose(z, "zT")
+            yield from attention(layer.tri_att_end, zT, mask_t)
+            yield from transpose(zT, "zs")
+            src = z
+        so.copy_2d(_bytes(z_user), z.numel() * 4, _bytes(z), z.numel() * 4, z.numel() * 4, 1)
+
     # ---------------------------------------------------------------- runners
     @torch.no_grad()
     def forward_(self, z_local: Tensor, mask: Optional[Tensor] = None, group=None,
                  z_in: Optional[Tensor] = None, hook=None) -> Tensor:
         """Run this rank's share of the stack in place on ``z_local`` (reading ``z_in`` in
-        the first block when given); collectives over ``group``. ``hook(label)`` is called
-        before and after (label "end") every collective."""
+        the first block when given); exchanges over ``group``. ``hook(label)`` is called
+        before and after (label "end") every exchange step."""
         import torch.distributed as dist
         if dist.get_world_size(group) != self.world or dist.get_rank(group) != self.rank:
             raise RuntimeError("ShardedTrianglePairStack: world/rank differ from the process group")
@@ -305,16 +519,56 @@ class ShardedTrianglePairStack:
         if z_in is not None:
             _check_local(z_in, mask)
         h = hook or (lambda label: None)
-        for kind, out, inp in self.steps(z_local, mask, z_in):
-            h("nccl_" + kind)
-            if kind == "all_gather":
-                dist.all_gather_into_tensor(out, inp, group=group)
-            elif kind == "all_to_all":
-                dist.all_to_all_single(out, inp, group=group)
+        lib = ops._lib.load() if self.exchange == "peer" else None
+        for req in self.steps(z_local, mask, z_in):
+            kind = req[0]
+            if kind == "barrier":
+                h("peer_barrier")
+                self._epoch += 1
+                so = self.stage_ops
+                dev = z_local.device
+                ops._lib.check(lib.gtk_peer_barrier(ops._ptr(self._peer["flags"].ptrs), self.rank, self.world,
+                                                    self._epoch, ops._ptr(ops.status_buffer(dev)), ops._stream(dev)),
+                               "gtk_peer_barrier")
+                if hasattr(so, "launches"):
+                    so.launches += 1
             else:
-                raise RuntimeError(f"unknown collective {kind}")
+                h("nccl_" + kind)
+                _, out, inp = req
+                if kind == "all_gather":
+                    dist.all_gather_into_tensor(out, inp, group=group)
+                elif kind == "all_to_all":
+                    dist.all_to_all_single(out, inp, group=group)
+                else:
+                    raise RuntimeError(f"unknown exchange {kind}")
             h("end")
         return z_local
+
+
+def connect_emulated(shards: List["ShardedTrianglePairStack"], B: int, N: int, device: torch.device) -> None:
+    """Peer mode for P ranks emulated in one process: each shard's receive buffers are
+    ordinary local allocations and every shard's pointer tables list all P of them."""
+    P = len(shards)
+    spec0 = None
+    for s in shards:
+        if s.exchange != "peer":
+            raise RuntimeError("connect_emulated needs exchange='peer'")
+        spec = ShardSpec(B, N, P, s.rank)
+        spec0 = spec0 or spec
+        if s.stage_ops is None:
+            s.stage_ops = CudaStageOps(device)
+        local, recv, lay = s._sizes(spec)
+        so = s.stage_ops
+        s._buf = {k: so.alloc(_round256(v)) for k, v in {**local, **recv}.items()}
+        s._lay = lay
+        s._recv_names = list(recv)
+        s._key = (B, N)
+        s._pack_weights(device)
+    for name in shards[0]._recv_names:
+        tensors = [s._buf[name] for s in shards]
+        ptrs = torch.tensor([t.data_ptr() for t in tensors], dtype=torch.int64, device=tensors[0].device)
+        for s in shards:
+            s._peer[name] = PeerBuffer(s._buf[name], ptrs, tensors)
 
 
 class TimedStageOps:
@@ -322,7 +576,7 @@ class TimedStageOps:
     every stage call (per-kernel timing with events) and counts the kernel launches."""
 
     KERNELS = ("trimul_project", "trimul_contract", "trimul_finish", "triatt_project", "triatt_core",
-               "triatt_finish", "copy_2d", "copy_3d", "pair_transpose_pack")
+               "triatt_finish", "copy_2d", "copy_3d", "pair_transpose_pack", "push_3d", "push_pair_transpose")
 
     def __init__(self, inner, hook=None):
         self.inner = inner
@@ -383,6 +637,8 @@ def _drive(gens, P: int) -> None:
         if any(r is None for r in reqs) or len({r[0] for r in reqs}) != 1:
             raise RuntimeError("ranks diverged: " + str([None if r is None else r[0] for r in reqs]))
         kind = reqs[0][0]
+        if kind == "barrier":
+            continue  # the ranks run in lockstep on one stream: every push before it is done
         if kind == "all_gather":
             ins = [r[2].clone() for r in reqs]
             for r in reqs:

@@ -52,6 +52,7 @@ extern "C" {
 #define GTK_STATUS_TIMEOUT_MMA 0x2u
 #define GTK_STATUS_TIMEOUT_CONSUMER 0x4u
 #define GTK_STATUS_TIMEOUT_DRAIN 0x8u
+#define GTK_STATUS_TIMEOUT_PEER 0x20u /* a cross-GPU barrier ran out: a peer never arrived */
 
 /* Library version (major*10000 + minor*100 + patch). */
 GTK_API int gtk_version(void);
@@ -238,6 +239,36 @@ GTK_API int gtk_copy_3d(void* dst, int64_t dpitch, int64_t dslab, const void* sr
  * places the chunk from peer p at pair-column offset p*R of its transposed shard. */
 GTK_API int gtk_pair_transpose_pack(const float* src, float* dst, int64_t B, int64_t R, int64_t C, int64_t P,
                                     void* stream);
+
+/* Peer-memory exchange (one process per GPU on one NVLink/NVSwitch node). Buffers that
+ * other ranks write into are allocated here and shared by CUDA IPC handles; the push
+ * kernels write each peer's share straight into that peer's buffer (packing, transfer
+ * and placement in one pass), and gtk_peer_barrier orders the pushes across ranks on the
+ * stream. No multicast object and no cluster multicast is involved: plain stores to
+ * peer memory over NVLink. */
+#define GTK_PEER_HANDLE_BYTES 64
+/* cudaMalloc + zero fill + IPC handle (GTK_PEER_HANDLE_BYTES bytes written to `handle`). */
+GTK_API int gtk_peer_alloc(size_t bytes, void** ptr, void* handle);
+GTK_API int gtk_peer_free(void* ptr);
+/* Map a peer's buffer (from its handle) into this process; gtk_peer_close unmaps it. */
+GTK_API int gtk_peer_open(const void* handle, void** ptr);
+GTK_API int gtk_peer_close(void* ptr);
+/* Slab k (k < P) of `height` rows of `width` bytes at src + k*sslab (row pitch spitch) is
+ * written to dsts[k] + doff (row pitch dpitch). dsts: device array of P base addresses.
+ * All sizes, offsets and addresses are multiples of 16 bytes. */
+GTK_API int gtk_push_3d(const uint64_t* dsts, int P, int64_t doff, int64_t dpitch, const void* src, int64_t spitch,
+                        int64_t sslab, int64_t width, int64_t height, void* stream);
+/* Pair (b, y, q*(C/P) + x) of src [B][R][C][128] fp32 is written to peer q's transposed
+ * shard dsts[q] [B][C/P][ndst][128] at (b, x, row0 + y). */
+GTK_API int gtk_push_pair_transpose(const float* src, const uint64_t* dsts, int64_t B, int64_t R, int64_t C,
+                                    int64_t P, int64_t ndst, int64_t row0, void* stream);
+/* Barrier over P ranks: each rank publishes `epoch` into every rank's flag array (P uint32
+ * each, zero-initialised peer memory; flag_ptrs: device array of the P arrays' addresses)
+ * and waits until all P have published it. Stream-ordered: pushes enqueued before it on
+ * every rank are visible to work enqueued after it. Bounded: after 2 s the status word
+ * gets GTK_STATUS_TIMEOUT_PEER. Epochs must increase by one per barrier. */
+GTK_API int gtk_peer_barrier(const uint64_t* flag_ptrs, int rank, int P, uint32_t epoch, uint32_t* status,
+                             void* stream);
 
 #ifdef __cplusplus
 }

@@ -128,6 +128,17 @@ class CpuStageOps:
         for k in range(depth):
             self.copy_2d(dst[k * dslab:], dpitch, src[k * sslab:], spitch, width, height)
 
+    def push_3d(self, dst, doff, dpitch, src, spitch, sslab, width, height):
+        # slab k -> rank k's buffer (ranks emulated in one process: dst.tensors)
+        for k, t in enumerate(dst.tensors):
+            self.copy_2d(t[doff:], dpitch, src[k * sslab:], spitch, width, height)
+
+    def push_pair_transpose(self, src, dst, B, R, Cn, P, ndst, row0):
+        CP = Cn // P
+        s = src.reshape(B, R, P, CP, C)
+        for q, t in enumerate(dst.tensors):
+            _typed(t, torch.float32, (B, CP, ndst, C))[:, :, row0:row0 + R].copy_(s[:, :, q].permute(0, 2, 1, 3))
+
     def pair_transpose_pack(self, src, dst, B, R, Cn, P):
         s = src.reshape(B, R, P, Cn // P, C).permute(2, 0, 3, 1, 4)     # [P][B][Cn/P][R][C]
         _typed(dst, torch.float32, (P, B, Cn // P, R, C)).copy_(s)

@@ -63,6 +63,59 @@ def test_pair_transpose_pack_matches_permute(B, R, Cn, P):
     assert torch.equal(dst, ref)
 
 
+def test_push_kernels_match_their_definitions():
+    dev = require_gpu()
+    from genie_tk import _lib, ops
+    lib = _lib.load()
+    st = ops._stream(dev)
+    P = 3
+    # push_3d: slab k of src -> destination k at an offset, with its own row pitch
+    src = torch.randint(0, 255, (P * 4096,), dtype=torch.uint8, device=dev)
+    dsts = [torch.zeros(8192, dtype=torch.uint8, device=dev) for _ in range(P)]
+    ptrs = torch.tensor([d.data_ptr() for d in dsts], dtype=torch.int64, device=dev)
+    assert lib.gtk_push_3d(ops._ptr(ptrs), P, 256, 512, ops._ptr(src), 1024, 4096, 160, 4, st) == 0
+    torch.cuda.synchronize()
+    for k in range(P):
+        ref = torch.zeros(8192, dtype=torch.uint8, device=dev)
+        for r in range(4):
+            ref[256 + r * 512:256 + r * 512 + 160] = src[k * 4096 + r * 1024:k * 4096 + r * 1024 + 160]
+        assert torch.equal(dsts[k], ref)
+    # push_pair_transpose: pair (b, y, q*CP + x) -> dsts[q] at (b, x, row0 + y) of [B][CP][ndst][128]
+    B, R, Cn, ndst, row0 = 2, 8, 24, 40, 16
+    CP = Cn // P
+    zsrc = torch.randn(B, R, Cn, 128, device=dev)
+    outs = [torch.zeros(B, CP, ndst, 128, device=dev) for _ in range(P)]
+    ptrs = torch.tensor([o.data_ptr() for o in outs], dtype=torch.int64, device=dev)
+    assert lib.gtk_push_pair_transpose(ops._ptr(zsrc), ops._ptr(ptrs), B, R, Cn, P, ndst, row0, st) == 0
+    torch.cuda.synchronize()
+    for q in range(P):
+        ref = torch.zeros_like(outs[q])
+        ref[:, :, row0:row0 + R] = zsrc.view(B, R, P, CP, 128)[:, :, q].permute(0, 2, 1, 3)
+        assert torch.equal(outs[q], ref)
+
+
+def test_peer_barrier_passes_and_times_out_cleanly():
+    """One rank alone passes; a barrier waiting for a peer that never arrives gives up after
+    its bounded wait, sets GTK_STATUS_TIMEOUT_PEER and leaves the device usable."""
+    dev = require_gpu()
+    from genie_tk import _lib, ops
+    lib = _lib.load()
+    st = ops._stream(dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    flags = torch.zeros(64, dtype=torch.int32, device=dev)
+    one = torch.tensor([flags.data_ptr()], dtype=torch.int64, device=dev)
+    assert lib.gtk_peer_barrier(ops._ptr(one), 0, 1, 1, ops._ptr(status), st) == 0
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0 and int(flags[0].item()) == 1
+    other = torch.zeros(64, dtype=torch.int32, device=dev)   # a "peer" that never signals
+    two = torch.tensor([flags.data_ptr(), other.data_ptr()], dtype=torch.int64, device=dev)
+    assert lib.gtk_peer_barrier(ops._ptr(two), 0, 2, 2, ops._ptr(status), st) == 0
+    torch.cuda.synchronize()
+    assert int(status.item()) & 0x20
+    assert int(other[0].item()) == 2          # this rank still published its arrival
+    assert torch.equal(torch.ones(4, device=dev) * 2, torch.ones(4, device=dev) + 1)
+
+
 def _problem(N, layers, seed=21):
     gen = torch.Generator().manual_seed(seed)
     z = torch.randn(1, N, N, 128, generator=gen)
@@ -113,13 +166,32 @@ def test_emulated_shards_match_unsharded(N, P, layers, exchange):
     assert_status_clean(dev)
 
 
+@pytest.mark.parametrize("N,P,exchange", [(128, 2, "gather"), (128, 4, "channels"), (256, 8, "channels")])
+def test_emulated_peer_exchange_matches_unsharded(N, P, exchange):
+    dev = require_gpu()
+    from genie_tk.sharded import ShardedTrianglePairStack, connect_emulated, run_emulated
+    z, mask, params = _problem(N, 1)
+    st = _stack(params, dev)
+    zd, md = z.to(dev), mask.to(dev)
+    full = st.forward(zd, md)
+    R = N // P
+    shards = [ShardedTrianglePairStack(st, P, r, trimul_exchange=exchange, exchange="peer") for r in range(P)]
+    connect_emulated(shards, 1, N, dev)
+    zl = [zd[:, r * R:(r + 1) * R].clone() for r in range(P)]
+    run_emulated(shards, zl, md)
+    got = torch.cat(zl, dim=1)
+    torch.cuda.synchronize()
+    assert float((got - full).abs().max()) <= 1e-3
+    assert_status_clean(dev)
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         return s.getsockname()[1]
 
 
-def _nccl_rank(rank, world, port, z, mask, params, q):
+def _nccl_rank(rank, world, port, z, mask, params, q, exchange="nccl"):
     import datetime
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -134,16 +206,21 @@ def _nccl_rank(rank, world, port, z, mask, params, q):
         N = z.shape[1]
         R = N // world
         zl = z[:, rank * R:(rank + 1) * R].contiguous().to(dev)
-        sh = ShardedTrianglePairStack(_stack(params, dev), world, rank)
+        sh = ShardedTrianglePairStack(_stack(params, dev), world, rank, exchange=exchange)
+        if exchange == "peer":
+            sh.connect(None, 1, N, dev)
         sh.forward_(zl, mask.to(dev))
         torch.cuda.synchronize()
-        q.put((rank, zl.cpu()))
+        from genie_tk import ops
+        q.put((rank, zl.cpu(), ops.check_status(dev)))
         dist.barrier()
+        sh.close()
     finally:
         dist.destroy_process_group()
 
 
-def test_two_nccl_ranks_match_single_gpu():
+@pytest.mark.parametrize("exchange", ["nccl", "peer"])
+def test_two_ranks_match_single_gpu(exchange):
     require_gpu()
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
@@ -152,13 +229,16 @@ def test_two_nccl_ranks_match_single_gpu():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_nccl_rank, args=(r, world, port, z, mask, params, q)) for r in range(world)]
+    procs = [ctx.Process(target=_nccl_rank, args=(r, world, port, z, mask, params, q, exchange))
+             for r in range(world)]
     for p in procs:
         p.start()
-    parts = dict(q.get(timeout=300) for _ in range(world))
+    res = [q.get(timeout=300) for _ in range(world)]
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
+    assert all(r[2] == 0 for r in res), "a kernel or barrier timed out"
+    parts = {r[0]: r[1] for r in res}
     got = torch.cat([parts[r] for r in range(world)], dim=1)
     dev = torch.device("cuda", 0)
     full = _stack(params, dev).forward(z.to(dev), mask.to(dev)).cpu()
