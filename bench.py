@@ -56,7 +56,7 @@ def kernel_work(name: str, N: int, B: int = 1):
         return "tensor", 4.0 * B * N ** 3 * 4 * 32          # QK^T + PV, H=4, d=32
     if name == "trimul_contract":
         return "tensor", 2.0 * B * N ** 3 * 128             # 128 channel GEMMs of N^3
-    if name == "trimul_project":
+    if name in ("trimul_project", "trimul_project_to"):
         return "hbm", P * (512 + 4 + 2 * 128 * 2)           # z fp32 + mask in, a, b fp16 out
     if name == "trimul_finish":
         return "hbm", P * (128 * 2 + 512 + 512)             # x fp16 + z fp32 in, z fp32 out
@@ -472,8 +472,8 @@ def run_sharded(args, rank, world, device):
                "ms_per_step": e_ms, "note": "each rank copies its own row shard in and out"}
     peaks = load_peaks()
     stack_tflops = B * N * N * L * layer_flops(N) / (ms_per_step / 1e3) / 1e12
-    stage_kernels = ("triatt_core", "trimul_contract", "trimul_project", "trimul_finish", "triatt_project",
-                     "triatt_finish")
+    stage_kernels = ("triatt_core", "trimul_contract", "trimul_project", "trimul_project_to", "trimul_finish",
+                     "triatt_project", "triatt_finish")
     dom = max((k for k in breakdown if k in stage_kernels), key=lambda k: breakdown[k]["ms"])
     bound, work = kernel_work(dom, N, B)
     calls = sum(1 for lab, _ in labels if lab == dom)

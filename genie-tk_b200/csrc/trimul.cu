@@ -105,12 +105,24 @@ __global__ void trimul_pack_kernel(gtk_trimul_params p, uint8_t* packed) {
 // capping registers at 128.)
 // Shared memory: W1 128 KB | A 32 KB | z 64 KB | mask 2 x 512 B | barriers.
 // ----------------------------------------------------------------------------------
+constexpr int kMaxPlaneDsts = 8;
+
 namespace k1 {
 constexpr int kThreads = 416;
 constexpr uint32_t kW = 0, kA = 131072, kZ = 163840, kMask = 229376, kBar = 230400;
 constexpr uint32_t kSmem = kBar + 128 + 1024;
 static_assert(kSmem <= 232448, "K1 shared memory");
 }  // namespace k1
+
+// Destinations of the a / b planes. Channel c of pair row r goes to
+// ptr[c / group] + (((b * dst_rows + row0 + r) * group + c % group) * ld) halves: with one
+// group of 128 channels, dst_rows = rows and row0 = 0 this is the plain [B][rows][128][ld]
+// layout; with P groups the planes land directly in the channel shards [B][dst_rows][128/P][ld]
+// of P buffers (a peer GPU's memory mapped into this process, or local).
+struct PlaneDsts {
+  uint64_t ptr[kMaxPlaneDsts];
+  int group, dst_rows, row0;
+};
 
 struct K1Bars {
   uint64_t wbar;
@@ -126,9 +138,9 @@ static_assert(sizeof(K1Bars) <= 128, "K1 barrier block");
 
 __global__ void __launch_bounds__(k1::kThreads, 1)
     trimul_project_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap z_map,
-                          const float* __restrict__ mask, const float* __restrict__ vec, __half* __restrict__ a_out,
-                          __half* __restrict__ b_out, int64_t ld, int N, int rows, int n_jt, int n_tiles,
-                          uint32_t* status) {
+                          const float* __restrict__ mask, const float* __restrict__ vec,
+                          const __grid_constant__ PlaneDsts a_dst, const __grid_constant__ PlaneDsts b_dst, int64_t ld,
+                          int N, int rows, int n_jt, int n_tiles, uint32_t* status) {
   extern __shared__ uint8_t dsmem[];
   uint8_t* smem = align1024(dsmem);
   K1Bars* bars = reinterpret_cast<K1Bars*>(smem + k1::kBar);
@@ -288,6 +300,12 @@ __global__ void __launch_bounds__(k1::kThreads, 1)
     const int q4 = warp & 3;
     const int c = q4 * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
+    // this channel's destination rows (its group's buffer), resolved once
+    const int grp = c / a_dst.group;
+    const uint64_t a_align = a_dst.ptr[grp], b_align = b_dst.ptr[grp];
+    __half* const a_base = reinterpret_cast<__half*>(a_align) + static_cast<size_t>(c - grp * a_dst.group) * ld;
+    __half* const b_base = reinterpret_cast<__half*>(b_align) + static_cast<size_t>(c - grp * a_dst.group) * ld;
+    const size_t row_step = static_cast<size_t>(a_dst.group) * ld;  // halves between pair rows
     const float bias_p0 = vec[tmpack::kVB1 + c], bias_p1 = vec[tmpack::kVB1 + 256 + c];
     const float bias_g0 = vec[tmpack::kVB1 + 128 + c], bias_g1 = vec[tmpack::kVB1 + 384 + c];
     int it = 0;
@@ -302,9 +320,8 @@ __global__ void __launch_bounds__(k1::kThreads, 1)
         ok = __all_sync(0xffffffffu, mbar_wait(&bars->d_full[h], it & 1, guard, status, kStatusTimeoutConsumer));
         if (!ok) break;
         tc_fence_after();
-        __half* dst = (h ? b_out : a_out) + ((static_cast<size_t>(b) * rows + r) * 128 + c) * ld;
-        const bool wide = (ld & 15) == 0 && (reinterpret_cast<uintptr_t>(a_out) & 31) == 0 &&
-                          (reinterpret_cast<uintptr_t>(b_out) & 31) == 0;
+        __half* dst = (h ? b_base : a_base) + (static_cast<size_t>(b) * a_dst.dst_rows + a_dst.row0 + r) * row_step;
+        const bool wide = (ld & 15) == 0 && ((h ? b_align : a_align) & 31) == 0;
         const float bp = h ? bias_p1 : bias_p0, bg = h ? bias_g1 : bias_g0;
 #pragma unroll 1
         for (int jc = 0; jc < 4; ++jc) {
@@ -906,15 +923,14 @@ size_t gtk_trimul_workspace_bytes(int64_t B, int64_t N, int c_z, int c_hidden) {
   return 3 * plane;
 }
 
-int gtk_trimul_project(const float* z, const float* mask, const void* packed, void* a_planes, void* b_planes,
-                       int64_t ld, int64_t B, int64_t rows, int64_t N, uint32_t* status, void* stream) {
+static int trimul_project_launch(const float* z, const float* mask, const void* packed, const PlaneDsts& ad,
+                                 const PlaneDsts& bd, int64_t ld, int64_t B, int64_t rows, int64_t N,
+                                 uint32_t* status, void* stream) {
   if (!dims_ok(B, 65535) || !dims_ok(rows, 65535) || !dims_ok(N, 1 << 20))
     return fail(GTK_ERR_INVALID_ARG, "trimul_project: bad B/rows/N");
   if (ld < N || ld % 8) return fail(GTK_ERR_INVALID_ARG, "trimul_project: plane pitch must be >= N and a multiple of 8");
   if (int e = check_ptr(z, "z")) return e;
   if (int e = check_ptr(packed, "packed", 256)) return e;
-  if (int e = check_ptr(a_planes, "a_planes")) return e;
-  if (int e = check_ptr(b_planes, "b_planes")) return e;
   if (mask && (reinterpret_cast<uintptr_t>(mask) & 3)) return fail(GTK_ERR_ALIGNMENT, "mask is misaligned");
   if (int e = check_device()) return e;
   const int64_t n_jt = (N + 127) / 128;
@@ -927,10 +943,43 @@ int gtk_trimul_project(const float* z, const float* mask, const void* packed, vo
   if (int e = ensure_smem(reinterpret_cast<const void*>(trimul_project_kernel), k1::kSmem)) return e;
   const int grid = static_cast<int>(n_tiles < num_sms() ? n_tiles : num_sms());
   trimul_project_kernel<<<grid, k1::kThreads, k1::kSmem, static_cast<cudaStream_t>(stream)>>>(
-      wm, zm, mask, reinterpret_cast<const float*>(pk + tmpack::kVec), static_cast<__half*>(a_planes),
-      static_cast<__half*>(b_planes), ld, static_cast<int>(N), static_cast<int>(rows), static_cast<int>(n_jt),
-      static_cast<int>(n_tiles), status);
+      wm, zm, mask, reinterpret_cast<const float*>(pk + tmpack::kVec), ad, bd, ld, static_cast<int>(N),
+      static_cast<int>(rows), static_cast<int>(n_jt), static_cast<int>(n_tiles), status);
   return check_launch("trimul_project_kernel");
+}
+
+int gtk_trimul_project(const float* z, const float* mask, const void* packed, void* a_planes, void* b_planes,
+                       int64_t ld, int64_t B, int64_t rows, int64_t N, uint32_t* status, void* stream) {
+  if (int e = check_ptr(a_planes, "a_planes")) return e;
+  if (int e = check_ptr(b_planes, "b_planes")) return e;
+  PlaneDsts ad{}, bd{};
+  ad.ptr[0] = reinterpret_cast<uint64_t>(a_planes);
+  bd.ptr[0] = reinterpret_cast<uint64_t>(b_planes);
+  ad.group = bd.group = 128;
+  ad.dst_rows = bd.dst_rows = static_cast<int>(rows);
+  ad.row0 = bd.row0 = 0;
+  return trimul_project_launch(z, mask, packed, ad, bd, ld, B, rows, N, status, stream);
+}
+
+int gtk_trimul_project_sharded(const float* z, const float* mask, const void* packed, void* const* a_dsts,
+                               void* const* b_dsts, int P, int64_t dst_rows, int64_t row0, int64_t ld, int64_t B,
+                               int64_t rows, int64_t N, uint32_t* status, void* stream) {
+  if (P < 1 || P > kMaxPlaneDsts || 128 % P)
+    return fail(GTK_ERR_INVALID_ARG, "trimul_project_sharded: P must divide 128 and be at most 8");
+  if (!a_dsts || !b_dsts) return fail(GTK_ERR_INVALID_ARG, "trimul_project_sharded: NULL destination table");
+  if (row0 < 0 || row0 + rows > dst_rows || dst_rows > 65535)
+    return fail(GTK_ERR_INVALID_ARG, "trimul_project_sharded: rows row0..row0+rows must lie in dst_rows");
+  PlaneDsts ad{}, bd{};
+  for (int q = 0; q < P; ++q) {
+    if (int e = check_ptr(a_dsts[q], "a_dsts[q]")) return e;
+    if (int e = check_ptr(b_dsts[q], "b_dsts[q]")) return e;
+    ad.ptr[q] = reinterpret_cast<uint64_t>(a_dsts[q]);
+    bd.ptr[q] = reinterpret_cast<uint64_t>(b_dsts[q]);
+  }
+  ad.group = bd.group = 128 / P;
+  ad.dst_rows = bd.dst_rows = static_cast<int>(dst_rows);
+  ad.row0 = bd.row0 = static_cast<int>(row0);
+  return trimul_project_launch(z, mask, packed, ad, bd, ld, B, rows, N, status, stream);
 }
 
 int gtk_trimul_contract(int outgoing, const void* a_planes, const void* b_planes, void* x_planes, int64_t B,

@@ -51,6 +51,8 @@ _SIGNATURES = {
     "gtk_trimul_forward_noalloc": (c_int, [c_int, c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_int, c_int, c_vp,
                                            c_vp]),
     "gtk_trimul_project": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp]),
+    "gtk_trimul_project_sharded": (c_int, [c_vp, c_vp, c_vp, ctypes.POINTER(c_vp), ctypes.POINTER(c_vp), c_int,
+                                           c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp]),
     "gtk_trimul_contract": (c_int, [c_int, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64,
                                     ctypes.c_float, c_vp, c_vp]),
     "gtk_trimul_finish": (c_int, [c_vp, c_vp, c_i64, ctypes.c_float, c_vp, c_vp, c_int, c_i64, c_i64, c_i64, c_vp,

@@ -130,6 +130,17 @@ class CudaStageOps:
         self._chk(self.lib.gtk_pair_transpose_pack(ops._ptr(src), ops._ptr(dst), B, R, Cn, P, self._s()),
                   "gtk_pair_transpose_pack")
 
+    def trimul_project_to(self, mod, z, mask, a_dst: "PeerBuffer", b_dst: "PeerBuffer", B, rows, N, row0):
+        """K1 for a shard, writing channel group q of the planes straight into a_dst / b_dst
+        of rank q (rows row0.. of its [B][N][128/P][N] channel shard)."""
+        P = len(a_dst.addrs)
+        At = ctypes.c_void_p * P
+        a_tab = At(*[ctypes.c_void_p(a) for a in a_dst.addrs])
+        b_tab = At(*[ctypes.c_void_p(a) for a in b_dst.addrs])
+        self._chk(self.lib.gtk_trimul_project_sharded(ops._ptr(z), ops._ptr(mask), ops._ptr(mod.packed_weights(self.device)),
+                                                      a_tab, b_tab, P, N, row0, N, B, rows, N, ops._ptr(self.status),
+                                                      self._s()), "gtk_trimul_project_sharded")
+
     def push_3d(self, dst: "PeerBuffer", doff, dpitch, src, spitch, sslab, width, height):
         self._chk(self.lib.gtk_push_3d(ops._ptr(dst.ptrs), dst.ptrs.numel(), doff, dpitch, ops._ptr(src), spitch, sslab,
                                        width, height, self._s()), "gtk_push_3d")
@@ -154,8 +165,9 @@ class PeerBuffer:
     rank (peer buffers mapped into this process, or, for ranks emulated in one process,
     their local tensors, which are also listed in ``tensors``)."""
 
-    def __init__(self, local: Tensor, ptrs: Tensor, tensors: Optional[List[Tensor]] = None):
-        self.local, self.ptrs, self.tensors = local, ptrs, tensors
+    def __init__(self, local: Tensor, addrs: List[int], device, tensors: Optional[List[Tensor]] = None):
+        self.local, self.addrs, self.tensors = local, list(addrs), tensors
+        self.ptrs = torch.tensor(self.addrs, dtype=torch.int64, device=device)
 
 
 class _CudaArray:
@@ -179,7 +191,7 @@ class ShardedTrianglePairStack:
     """
 
     def __init__(self, stack: TrianglePairStack, world: int, rank: int, stage_ops=None,
-                 trimul_exchange: str = "auto", exchange: str = "nccl"):
+                 trimul_exchange: str = "auto", exchange: str = "nccl", k1_direct: bool = False):
         if trimul_exchange not in ("auto", "gather", "channels"):
             raise ValueError(f"trimul_exchange must be auto, gather or channels, not {trimul_exchange!r}")
         if exchange not in ("nccl", "peer"):
@@ -192,6 +204,11 @@ class ShardedTrianglePairStack:
         self.trimul_exchange = trimul_exchange if trimul_exchange != "auto" else (
             "gather" if world <= 3 else "channels")
         self.exchange = exchange
+        # peer mode, channel shards: K1 stores each channel group straight into its owner's
+        # buffer (no push pass). Measured slower on 8 B200s (14.7 vs 14.1 ms per step): the
+        # epilogue's 32-byte stores spread over the peers use NVLink less well than one bulk
+        # push, so it is off by default.
+        self.k1_direct = k1_direct
         self._key = None
         self._buf: Dict[str, Tensor] = {}
         self._peer: Dict[str, PeerBuffer] = {}
@@ -291,8 +308,7 @@ class ShardedTrianglePairStack:
                 ops._lib.check(lib.gtk_peer_open(gathered[q][name][0], ctypes.byref(ptr)), "gtk_peer_open")
                 self._ipc_open.append(ptr.value)
                 addrs.append(ptr.value)
-            self._peer[name] = PeerBuffer(self._buf[name],
-                                          torch.tensor(addrs, dtype=torch.int64, device=device))
+            self._peer[name] = PeerBuffer(self._buf[name], addrs, device)
         self._lay = lay
         self._key = (B, N)
         self._epoch = 0
@@ -448,12 +464,16 @@ class ShardedTrianglePairStack:
         tri_bias = self._lay["bias"]
 
         def multiply_channels(mod, outgoing, zz):
-            so.trimul_project(mod, zz, mask_loc, buf["a"], buf["b"], B, R, N)
-            for bb in range(B):
-                # my rows, channel group q -> rows row0.. of peer q's channel shard
-                for name, planes in (("a_ch", buf["a"]), ("b_ch", buf["b"])):
-                    so.push_3d(peer[name], (bb * N + row0) * CP * N * 2, CP * N * 2, planes[bb * plane_b:], C * N * 2,
-                               CP * N * 2, CP * N * 2, R)
+            if self.k1_direct:
+                # K1 writes channel group q of my rows straight into rank q's channel shard
+                so.trimul_project_to(mod, zz, mask_loc, peer["a_ch"], peer["b_ch"], B, R, N, row0)
+            else:
+                so.trimul_project(mod, zz, mask_loc, buf["a"], buf["b"], B, R, N)
+                for bb in range(B):
+                    # my rows, channel group q -> rows row0.. of rank q's channel shard
+                    for name, planes in (("a_ch", buf["a"]), ("b_ch", buf["b"])):
+                        so.push_3d(peer[name], (bb * N + row0) * CP * N * 2, CP * N * 2, planes[bb * plane_b:],
+                                   C * N * 2, CP * N * 2, CP * N * 2, R)
             yield ("barrier",)
             so.trimul_contract(outgoing, buf["a_ch"], buf["b_ch"], buf["x_ch"], B, N, N, N, N, N, N, xs, CP)
             for bb in range(B):
@@ -566,16 +586,17 @@ def connect_emulated(shards: List["ShardedTrianglePairStack"], B: int, N: int, d
         s._pack_weights(device)
     for name in shards[0]._recv_names:
         tensors = [s._buf[name] for s in shards]
-        ptrs = torch.tensor([t.data_ptr() for t in tensors], dtype=torch.int64, device=tensors[0].device)
+        addrs = [t.data_ptr() for t in tensors]
         for s in shards:
-            s._peer[name] = PeerBuffer(s._buf[name], ptrs, tensors)
+            s._peer[name] = PeerBuffer(s._buf[name], addrs, tensors[0].device, tensors)
 
 
 class TimedStageOps:
     """Wraps a stage-ops object and calls ``hook(name)`` before and ``hook("end")`` after
     every stage call (per-kernel timing with events) and counts the kernel launches."""
 
-    KERNELS = ("trimul_project", "trimul_contract", "trimul_finish", "triatt_project", "triatt_core",
+    KERNELS = ("trimul_project", "trimul_project_to", "trimul_contract", "trimul_finish", "triatt_project",
+               "triatt_core",
                "triatt_finish", "copy_2d", "copy_3d", "pair_transpose_pack", "push_3d", "push_pair_transpose")
 
     def __init__(self, inner, hook=None):

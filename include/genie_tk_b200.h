@@ -139,6 +139,15 @@ GTK_API int64_t gtk_plane_pitch(int64_t N);
  * writes a and b planes [B, rows, c, ld]. mask: [B, rows, N] or NULL. */
 GTK_API int gtk_trimul_project(const float* z, const float* mask, const void* packed, void* a_planes, void* b_planes,
                        int64_t ld, int64_t B, int64_t rows, int64_t N, uint32_t* status, void* stream);
+/* As gtk_trimul_project, for one shard of `rows` pair rows that starts at row `row0` of a
+ * row-sharded pair tensor with `dst_rows` rows in all: channel c of the a (b) planes is
+ * written to a_dsts[c / (128/P)] (b_dsts[...]), a [B][dst_rows][128/P][ld] channel shard,
+ * at its rows row0.., so each channel group lands directly in the buffer of the rank that
+ * contracts it (host arrays of P <= 8 device addresses; peer GPUs' buffers mapped into this
+ * process are allowed). */
+GTK_API int gtk_trimul_project_sharded(const float* z, const float* mask, const void* packed, void* const* a_dsts,
+                                       void* const* b_dsts, int P, int64_t dst_rows, int64_t row0, int64_t ld,
+                                       int64_t B, int64_t rows, int64_t N, uint32_t* status, void* stream);
 
 /* Per-channel contraction on plane buffers, for every (b, c):
  *  outgoing: x[b][i][c][j] = sum_k a[b][i][c][k] * bb[b][j][c][k]  (a: [B,M,C,lda], bb: [B,Nj,C,ldb])

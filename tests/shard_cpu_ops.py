@@ -55,6 +55,15 @@ class CpuStageOps:
         _typed(a, torch.float16, (B, rows, C, N)).copy_(av.permute(0, 1, 3, 2))
         _typed(b, torch.float16, (B, rows, C, N)).copy_(bv.permute(0, 1, 3, 2))
 
+    def trimul_project_to(self, mod, z, mask, a_dst, b_dst, B, rows, N, row0):
+        _, av, bv = O.trimul_prepare(z, mask, self._p(mod))
+        P = len(a_dst.tensors)
+        CP = C // P
+        for dst, val in ((a_dst, av), (b_dst, bv)):
+            planes = val.permute(0, 1, 3, 2)                       # [B][rows][C][N]
+            for q, t in enumerate(dst.tensors):
+                _typed(t, torch.float16, (B, N, CP, N))[:, row0:row0 + rows].copy_(planes[:, :, q * CP:(q + 1) * CP])
+
     def trimul_contract(self, outgoing, a, b, x, B, M, Nj, K, lda, ldb, ldx, xs, channels=C):
         Cc = channels
         if outgoing:

@@ -166,8 +166,9 @@ def test_emulated_shards_match_unsharded(N, P, layers, exchange):
     assert_status_clean(dev)
 
 
-@pytest.mark.parametrize("N,P,exchange", [(128, 2, "gather"), (128, 4, "channels"), (256, 8, "channels")])
-def test_emulated_peer_exchange_matches_unsharded(N, P, exchange):
+@pytest.mark.parametrize("N,P,exchange,k1_direct", [(128, 2, "gather", False), (128, 4, "channels", False),
+                                                     (256, 8, "channels", False), (256, 8, "channels", True)])
+def test_emulated_peer_exchange_matches_unsharded(N, P, exchange, k1_direct):
     dev = require_gpu()
     from genie_tk.sharded import ShardedTrianglePairStack, connect_emulated, run_emulated
     z, mask, params = _problem(N, 1)
@@ -175,7 +176,8 @@ def test_emulated_peer_exchange_matches_unsharded(N, P, exchange):
     zd, md = z.to(dev), mask.to(dev)
     full = st.forward(zd, md)
     R = N // P
-    shards = [ShardedTrianglePairStack(st, P, r, trimul_exchange=exchange, exchange="peer") for r in range(P)]
+    shards = [ShardedTrianglePairStack(st, P, r, trimul_exchange=exchange, exchange="peer", k1_direct=k1_direct)
+              for r in range(P)]
     connect_emulated(shards, 1, N, dev)
     zl = [zd[:, r * R:(r + 1) * R].clone() for r in range(P)]
     run_emulated(shards, zl, md)

@@ -84,26 +84,28 @@ def test_out_of_place_first_block():
     assert float((torch.cat(out, 1) - ref).abs().max()) == 0.0
 
 
-def _run_emulated_peer(z, mask, params, P, exchange="auto"):
+def _run_emulated_peer(z, mask, params, P, exchange="auto", k1_direct=False):
     from genie_tk.sharded import ShardedTrianglePairStack, connect_emulated, run_emulated
     st = _stack(params)
     B, N = z.shape[0], z.shape[1]
     R = N // P
-    shards = [ShardedTrianglePairStack(st, P, r, stage_ops=CpuStageOps(), trimul_exchange=exchange, exchange="peer")
-              for r in range(P)]
+    shards = [ShardedTrianglePairStack(st, P, r, stage_ops=CpuStageOps(), trimul_exchange=exchange, exchange="peer",
+                                       k1_direct=k1_direct) for r in range(P)]
     connect_emulated(shards, B, N, z.device)
     zl = [z[:, r * R:(r + 1) * R].clone() for r in range(P)]
     run_emulated(shards, zl, mask)
     return torch.cat(zl, dim=1)
 
 
-@pytest.mark.parametrize("B,N,P,exchange", [(1, 32, 2, "auto"), (1, 32, 4, "auto"), (1, 64, 8, "auto"),
-                                             (2, 32, 2, "channels"), (2, 32, 4, "gather")])
-def test_peer_exchange_matches_collectives(B, N, P, exchange):
+@pytest.mark.parametrize("B,N,P,exchange,k1_direct", [(1, 32, 2, "auto", False), (1, 32, 4, "auto", False),
+                                                       (1, 64, 8, "auto", False), (2, 32, 2, "channels", False),
+                                                       (2, 32, 4, "gather", False), (2, 32, 4, "channels", True),
+                                                       (1, 64, 8, "channels", True)])
+def test_peer_exchange_matches_collectives(B, N, P, exchange, k1_direct):
     """Pushing every rank's share straight into the peers' buffers gives the same stack
     as the collective exchanges (and the oracle)."""
     z, mask, params = _problem(B, N, 1)
-    got = _run_emulated_peer(z, mask, params, P, exchange)
+    got = _run_emulated_peer(z, mask, params, P, exchange, k1_direct)
     ref = _run_emulated(z, mask, params, P, exchange)
     assert float((got - ref).abs().max()) <= 1e-5
     err = (got - O.stack_forward(z, mask, params, no_heads=4)).abs()
