@@ -404,10 +404,6 @@ constexpr uint32_t kSmem = kBar + 256 + 1024;
 static_assert(kSmem <= 232448, "K4 shared memory");
 static_assert(kBias % 1024 == 0, "bias stage alignment");
 constexpr float kLazy = 8.0f;
-// Every kPolyEvery-th pair of exponentials is evaluated on the FMA pipe (exp2_poly2); 0
-// disables it. Measured on B200 at N = 1024: one pair in three made the kernel 6% slower
-// (2.15 vs 2.03 ms), because the kernel is latency-bound rather than MUFU-bound.
-constexpr int kPolyEvery = 0;
 }  // namespace k4
 
 struct K4Bars {
@@ -439,35 +435,6 @@ __device__ __forceinline__ float2 add_f32x2(float2 a, float2 b) {
       : "=l"(reinterpret_cast<uint64_t&>(d))
       : "l"(reinterpret_cast<const uint64_t&>(a)), "l"(reinterpret_cast<const uint64_t&>(b)));
   return d;
-}
-
-__device__ __forceinline__ float2 fma_f32x2(float2 a, float2 b, float2 c) {
-  float2 d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;"
-      : "=l"(reinterpret_cast<uint64_t&>(d))
-      : "l"(reinterpret_cast<const uint64_t&>(a)), "l"(reinterpret_cast<const uint64_t&>(b)),
-        "l"(reinterpret_cast<const uint64_t&>(c)));
-  return d;
-}
-
-// 2^x for two values on the FMA/ALU pipes. Range reduction: adding 1.5 * 2^23 rounds x to
-// the nearest integer j (held in the low mantissa bits of t); f = x - j lies in
-// [-0.5, 0.5]; 2^f is a cubic fitted here to 2^f on that interval (near-minimax,
-// relative error 7.5e-5, below fp16 rounding of P); j is added to the exponent bits.
-// Inputs are clamped at -126 so the exponent field never underflows (results there
-// are ~1e-38, i.e. zero after the fp16 conversion of P).
-__device__ __forceinline__ float2 exp2_poly2(float2 x) {
-  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
-  x.x = fmaxf(x.x, -126.f);
-  x.y = fmaxf(x.y, -126.f);
-  const float2 t = add_f32x2(x, make_float2(kRound, kRound));
-  const float2 j = add_f32x2(t, make_float2(-kRound, -kRound));
-  const float2 f = fma_f32x2(j, make_float2(-1.f, -1.f), x);
-  float2 p = fma_f32x2(make_float2(0.0551716045f, 0.0551716045f), f, make_float2(0.242611117f, 0.242611117f));
-  p = fma_f32x2(p, f, make_float2(0.693260997f, 0.693260997f));
-  p = fma_f32x2(p, f, make_float2(0.999928074f, 0.999928074f));
-  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
-                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
 }
 
 template <int N>
@@ -737,12 +704,8 @@ __global__ void __launch_bounds__(k4::kThreads, 1)
 #pragma unroll
         for (int k2 = 0; k2 < 64; ++k2) {
           float2 x = add_f32x2(make_float2(__uint_as_float(sv[2 * k2]), __uint_as_float(sv[2 * k2 + 1])), negm);
-          if (kPolyEvery > 0 && k2 % kPolyEvery == kPolyEvery - 1) {
-            x = exp2_poly2(x);
-          } else {
-            x.x = ex2f(x.x);
-            x.y = ex2f(x.y);
-          }
+          x.x = ex2f(x.x);
+          x.y = ex2f(x.y);
           acc[k2 & 3] = add_f32x2(acc[k2 & 3], x);  // four independent partial sums
           __half2 hp = __floats2half2_rn(x.x, x.y);
           sv[k2] = *reinterpret_cast<uint32_t*>(&hp);
@@ -783,37 +746,47 @@ __global__ void __launch_bounds__(k4::kThreads, 1)
       }
       if (ok) mbar_arrive(&bars->bias_empty[bs]);
     }
-    // epilogue: O / l, times the gate, to og (rows wg and wg + 2)
+    // epilogue: O / l, times the gate, to og (rows wg and wg + 2). The gate rows are loaded
+    // before waiting for the last P V, so their latency overlaps the drain.
+    const int j = jt * 128 + jrow;
+    uint4 gw[2][4];
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+      const int i = ig * kR + wg + 2 * rr;
+      const bool valid = ok && i < rows && j < N;
+      const uint4* gp = reinterpret_cast<const uint4*>(gate + ((static_cast<size_t>(b) * rows + i) * N + j) * 128 +
+                                                       h * kHeadDim);
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch) gw[rr][ch] = valid ? __ldg(gp + ch) : make_uint4(0u, 0u, 0u, 0u);
+    }
     const bool fin = __all_sync(0xffffffffu, ok && mbar_wait(&bars->o_final, 0, guard, status,
                                                              kStatusTimeoutConsumer) && !guard->abort);
     if (fin) {
       tc_fence_after();
-      const int j = jt * 128 + jrow;
+      uint32_t ov[2][32];
+      tmem_ld32(tmem + lane_off + wg * 32, ov[0]);
+      tmem_ld32(tmem + lane_off + (wg + 2) * 32, ov[1]);
+      tmem_wait_ld();
 #pragma unroll
       for (int rr = 0; rr < 2; ++rr) {
-        const int r = wg + 2 * rr;
-        uint32_t ov[32];
-        tmem_ld32(tmem + lane_off + r * 32, ov);
-        tmem_wait_ld();
-        const int i = ig * kR + r;
+        const int i = ig * kR + wg + 2 * rr;
         if (i < rows && j < N) {
           const float inv = 1.f / (rr == 0 ? l_run0 : l_run1);
           const size_t pair = (static_cast<size_t>(b) * rows + i) * N + j;
-          const uint4* gp = reinterpret_cast<const uint4*>(gate + pair * 128 + h * kHeadDim);
-          uint4* op = reinterpret_cast<uint4*>(og + pair * 128 + h * kHeadDim);
+          uint32_t o16[16];
 #pragma unroll
           for (int ch = 0; ch < 4; ++ch) {
-            const uint4 gw = gp[ch];
-            const __half2* gh = reinterpret_cast<const __half2*>(&gw);
-            uint32_t o4[4];
+            const __half2* gh = reinterpret_cast<const __half2*>(&gw[rr][ch]);
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const float2 gf = __half22float2(gh[e]);
-              o4[e] = pack_f16x2(__uint_as_float(ov[ch * 8 + 2 * e]) * inv * gf.x,
-                                 __uint_as_float(ov[ch * 8 + 2 * e + 1]) * inv * gf.y);
+              o16[ch * 4 + e] = pack_f16x2(__uint_as_float(ov[rr][ch * 8 + 2 * e]) * inv * gf.x,
+                                           __uint_as_float(ov[rr][ch * 8 + 2 * e + 1]) * inv * gf.y);
             }
-            op[ch] = make_uint4(o4[0], o4[1], o4[2], o4[3]);
           }
+          __half* op = og + pair * 128 + h * kHeadDim;  // 64 contiguous bytes, 64-byte aligned
+          stg_v8(op, o16[0], o16[1], o16[2], o16[3], o16[4], o16[5], o16[6], o16[7]);
+          stg_v8(op + 16, o16[8], o16[9], o16[10], o16[11], o16[12], o16[13], o16[14], o16[15]);
         }
       }
     }

@@ -300,12 +300,7 @@ __global__ void __launch_bounds__(k1::kThreads, 1)
     const int q4 = warp & 3;
     const int c = q4 * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
-    // this channel's destination rows (its group's buffer), resolved once
-    const int grp = c / a_dst.group;
-    const uint64_t a_align = a_dst.ptr[grp], b_align = b_dst.ptr[grp];
-    __half* const a_base = reinterpret_cast<__half*>(a_align) + static_cast<size_t>(c - grp * a_dst.group) * ld;
-    __half* const b_base = reinterpret_cast<__half*>(b_align) + static_cast<size_t>(c - grp * a_dst.group) * ld;
-    const size_t row_step = static_cast<size_t>(a_dst.group) * ld;  // halves between pair rows
+    const int grp = c / a_dst.group, c_in_grp = c - grp * a_dst.group;  // this channel's destination group
     const float bias_p0 = vec[tmpack::kVB1 + c], bias_p1 = vec[tmpack::kVB1 + 256 + c];
     const float bias_g0 = vec[tmpack::kVB1 + 128 + c], bias_g1 = vec[tmpack::kVB1 + 384 + c];
     int it = 0;
@@ -320,8 +315,11 @@ __global__ void __launch_bounds__(k1::kThreads, 1)
         ok = __all_sync(0xffffffffu, mbar_wait(&bars->d_full[h], it & 1, guard, status, kStatusTimeoutConsumer));
         if (!ok) break;
         tc_fence_after();
-        __half* dst = (h ? b_base : a_base) + (static_cast<size_t>(b) * a_dst.dst_rows + a_dst.row0 + r) * row_step;
-        const bool wide = (ld & 15) == 0 && ((h ? b_align : a_align) & 31) == 0;
+        // destination base re-read from the (constant-bank) parameters rather than kept live
+        const uint64_t base = h ? b_dst.ptr[grp] : a_dst.ptr[grp];
+        __half* dst = reinterpret_cast<__half*>(base) +
+                      ((static_cast<size_t>(b) * a_dst.dst_rows + a_dst.row0 + r) * a_dst.group + c_in_grp) * ld;
+        const bool wide = (ld & 15) == 0 && (base & 31) == 0;
         const float bp = h ? bias_p1 : bias_p0, bg = h ? bias_g1 : bias_g0;
 #pragma unroll 1
         for (int jc = 0; jc < 4; ++jc) {
