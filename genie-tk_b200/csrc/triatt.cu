@@ -105,16 +105,19 @@ __device__ __forceinline__ float warp_sum4_transposed(float v0, float v1, float 
 //   warp 12    lane 0: TMA producer and MMA issuer. The 128 KB of weights are loaded
 //              once; each tile's 128 x 128 fp32 z block (z^T for the ending node, through
 //              the transposed descriptor) arrives by TMA, 64 KB in flight per tile;
-//   warps 0-3  LayerNorm producers: thread per pair row, read from the staged z tile,
-//              write the fp16 operand A and the four triangle-bias dot products of the
-//              fp32 LN output (stored bf16, times log2 e). Thread-per-row keeps every
-//              reduction in registers (a warp-per-row version spent ~700 cycles per row
-//              in dependent shuffle chains);
-//   warps 4-11 epilogue, two warpgroups (warps 4-7: q and k, warps 8-11: v and the gate),
-//              thread = pair (TMEM lane): rows of 64 B per head and the sigmoid gate row
-//              of 256 B, written straight to global memory.
-// TMEM: half 0 = (q, k) columns 0-255, half 1 = (v, g) columns 256-511, one epilogue
-// warpgroup each; the next tile's LayerNorm and z load overlap both.
+//   warps 0-7  LayerNorm producers, two threads per pair row (64 channels each): one pass
+//              reads the staged z tile into registers and releases it, then the fp16
+//              operand A and the four triangle-bias dot products of the fp32 LN output
+//              (stored bf16, times log2 e) are formed; statistics and dot products combine
+//              with one shuffle each (a warp-per-row version spent ~700 cycles per row in
+//              dependent shuffle chains; one thread per row with three passes kept the z
+//              buffer busy through the whole LayerNorm);
+//   warps 8-11 epilogue, thread = pair (TMEM lane): TMEM half 0 (q, k), then half 1 (v and
+//              the gate): rows of 64 B per head and the sigmoid gate row of 256 B, written
+//              with 32-byte stores. (Thirteen warps keep 128 registers per thread: a
+//              seventeen-warp launch is allocated like twenty warps, 96 registers, and spills.)
+// TMEM: half 0 = (q, k) columns 0-255, half 1 = (v, g) columns 256-511; the epilogue of
+// half 0 overlaps the MMAs of half 1, and the next tile's LayerNorm and z load overlap both.
 // Shared memory: W3 128 KB | z 64 KB | A 32 KB | barriers.
 // Rows: the tile grid covers `rows` problem rows i (all N when unsharded; one shard's rows
 // under row sharding, which only the starting orientation supports).
@@ -157,8 +160,8 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
     guard->abort = 0;
     mbar_init(&bars->wbar, 1);
     mbar_init(&bars->z_full, 1);
-    mbar_init(&bars->z_empty, 128);
-    mbar_init(&bars->a_full, 128);
+    mbar_init(&bars->z_empty, 256);
+    mbar_init(&bars->a_full, 256);
     mbar_init(&bars->a_empty, 1);
     for (int x = 0; x < 2; ++x) {
       mbar_init(&bars->d_full[x], 1);
@@ -176,56 +179,64 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = bars->tslot;
 
-  if (warp < 4) {
-    // ---------------- LayerNorm + bias producers: thread = pair row p ----------------
-    // Row p of the staged z tile is read from the 128-B-swizzled layout (conflict-free:
-    // each warp's 32 rows cover all bank groups); gamma, beta and the bias weights are
-    // warp-uniform loads served from L1.
-    const int p = tid;
-    const float* lnw = vec + tapack::kVLnW;
-    const float* lnb = vec + tapack::kVLnB;
-    const float* wbv = vec + tapack::kVWb;
+  if (warp < 8) {
+    // ---------- LayerNorm + bias producers: two threads per pair row (64 channels each) ----------
+    // One pass reads the row half from the staged, 128-B-swizzled z tile into registers and
+    // releases the tile (the next tile's load overlaps the rest); statistics and the four
+    // triangle-bias dot products combine with one shuffle each. gamma, beta and the bias
+    // weights are warp-uniform loads served from L1.
+    const int p = warp * 16 + (lane >> 1), half = lane & 1;
+    const float* lnw = vec + tapack::kVLnW + half * 64;
+    const float* lnb = vec + tapack::kVLnB + half * 64;
+    const float* wbv = vec + tapack::kVWb + half * 64;
     int it = 0;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
       const int jt = tile % n_jt, bi = tile / n_jt;
       const int i = bi % rows, b = bi / rows, j0 = jt * 128;
-      bool w = mbar_wait(&bars->z_full, it & 1, guard, status, kStatusTimeoutProducer);
-      if (it >= 1) w = w && mbar_wait(&bars->a_empty, (it - 1) & 1, guard, status, kStatusTimeoutProducer);
-      if (!__all_sync(0xffffffffu, w)) break;
+      if (!__all_sync(0xffffffffu, mbar_wait(&bars->z_full, it & 1, guard, status, kStatusTimeoutProducer))) break;
       const uint8_t* zt = smem + k3::kZ;
-      float sum = 0.f;
+      float v[64];
 #pragma unroll
-      for (int q = 0; q < 4; ++q)
+      for (int q = 0; q < 2; ++q)
 #pragma unroll
         for (int ch = 0; ch < 8; ++ch) {
-          const float4 v = lds_f4(zt + q * 16384 + swz128(p, ch));
-          sum += (v.x + v.y) + (v.z + v.w);
+          const float4 t = lds_f4(zt + (2 * half + q) * 16384 + swz128(p, ch));
+          v[q * 32 + ch * 4 + 0] = t.x;
+          v[q * 32 + ch * 4 + 1] = t.y;
+          v[q * 32 + ch * 4 + 2] = t.z;
+          v[q * 32 + ch * 4 + 3] = t.w;
         }
+      mbar_arrive(&bars->z_empty);  // the z tile may be refilled
+      float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < 64; ++c) s4[c & 3] += v[c];
+      float sum = (s4[0] + s4[1]) + (s4[2] + s4[3]);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
       const float mean = sum * (1.f / 128.f);
-      float ss = 0.f;
+      float q4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int q = 0; q < 4; ++q)
-#pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-          const float4 v = lds_f4(zt + q * 16384 + swz128(p, ch));
-          const float a = v.x - mean, bb = v.y - mean, c = v.z - mean, d = v.w - mean;
-          ss += (a * a + bb * bb) + (c * c + d * d);
-        }
+      for (int c = 0; c < 64; ++c) {
+        const float d = v[c] - mean;
+        q4[c & 3] += d * d;
+      }
+      float ss = (q4[0] + q4[1]) + (q4[2] + q4[3]);
+      ss += __shfl_xor_sync(0xffffffffu, ss, 1);
       const float rstd = rsqrtf(ss * (1.f / 128.f) + 1e-5f);
+      if (it >= 1 &&
+          !__all_sync(0xffffffffu, mbar_wait(&bars->a_empty, (it - 1) & 1, guard, status, kStatusTimeoutProducer)))
+        break;
       float bacc[kHeads] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
-      for (int c8 = 0; c8 < 16; ++c8) {
-        const int c = c8 * 8;
-        const float4 v0 = lds_f4(zt + (c >> 5) * 16384 + swz128(p, (c & 31) >> 2));
-        const float4 v1 = lds_f4(zt + (c >> 5) * 16384 + swz128(p, ((c & 31) >> 2) + 1));
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        const int c = ch * 8;
         const float4 w0 = __ldg(reinterpret_cast<const float4*>(lnw + c));
         const float4 w1 = __ldg(reinterpret_cast<const float4*>(lnw + c + 4));
         const float4 b0 = __ldg(reinterpret_cast<const float4*>(lnb + c));
         const float4 b1 = __ldg(reinterpret_cast<const float4*>(lnb + c + 4));
-        float y[8] = {(v0.x - mean) * rstd * w0.x + b0.x, (v0.y - mean) * rstd * w0.y + b0.y,
-                      (v0.z - mean) * rstd * w0.z + b0.z, (v0.w - mean) * rstd * w0.w + b0.w,
-                      (v1.x - mean) * rstd * w1.x + b1.x, (v1.y - mean) * rstd * w1.y + b1.y,
-                      (v1.z - mean) * rstd * w1.z + b1.z, (v1.w - mean) * rstd * w1.w + b1.w};
+        const float y[8] = {(v[c + 0] - mean) * rstd * w0.x + b0.x, (v[c + 1] - mean) * rstd * w0.y + b0.y,
+                            (v[c + 2] - mean) * rstd * w0.z + b0.z, (v[c + 3] - mean) * rstd * w0.w + b0.w,
+                            (v[c + 4] - mean) * rstd * w1.x + b1.x, (v[c + 5] - mean) * rstd * w1.y + b1.y,
+                            (v[c + 6] - mean) * rstd * w1.z + b1.z, (v[c + 7] - mean) * rstd * w1.w + b1.w};
 #pragma unroll
         for (int h = 0; h < kHeads; ++h) {
           const float4 u0 = __ldg(reinterpret_cast<const float4*>(wbv + h * 128 + c));
@@ -238,11 +249,12 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
         o.y = pack_f16x2(y[2], y[3]);
         o.z = pack_f16x2(y[4], y[5]);
         o.w = pack_f16x2(y[6], y[7]);
-        sts_u4(smem + k3::kA + (c8 >> 3) * 16384 + swz128(p, c8 & 7), o);
+        sts_u4(smem + k3::kA + half * 16384 + swz128(p, ch), o);
       }
-      mbar_arrive(&bars->z_empty);  // the z tile may be refilled
+#pragma unroll
+      for (int h = 0; h < kHeads; ++h) bacc[h] += __shfl_xor_sync(0xffffffffu, bacc[h], 1);
       const int j = j0 + p;
-      if (j < N) {
+      if (half == 0 && j < N) {
 #pragma unroll
         for (int h = 0; h < kHeads; ++h)
           bias[((static_cast<size_t>(row0 + i) * B + b) * kHeads + h) * ldn + j] = __float2bfloat16_rn(bacc[h]);
@@ -304,8 +316,7 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
       }
     }
   } else {
-    // ------------------ epilogue: thread = pair; warpgroup = TMEM half ------------------
-    const int h = (warp - 4) >> 2;  // 0: q, k (warps 4-7); 1: v, gate (warps 8-11)
+    // ------------------ epilogue: thread = pair; TMEM half 0 (q, k), then 1 (v, gate) ------------------
     const int q4 = warp & 3;
     const int p = q4 * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
@@ -316,7 +327,8 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
       const int j = jt * 128 + p;
       const bool valid = j < N;
       bool ok = true;
-      {
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
         ok = __all_sync(0xffffffffu, mbar_wait(&bars->d_full[h], it & 1, guard, status, kStatusTimeoutConsumer));
         if (!ok) break;
         tc_fence_after();
