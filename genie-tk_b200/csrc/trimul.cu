@@ -371,141 +371,231 @@ __global__ void __launch_bounds__(k1::kThreads, 1)
 }
 
 // ----------------------------------------------------------------------------------
-// K2: per-channel contraction. CTA tile: 128 rows (i) x 256 columns (j) of one (b, c)
-// plane; K loop in blocks of 64 through a 4-stage TMA ring. Warp 0 lane 0 = TMA producer,
-// warp 1 lane 0 = MMA issuer (TMEM accumulator, 256 columns), all 4 warps = epilogue.
+// K2: per-channel contraction, persistent. One CTA per SM loops over output tiles of
+// 128 rows (i) x 256 columns (j) of one (b, c) plane (j fastest, so consecutive tiles of a
+// CTA wave share the A panel in L2). The K loop runs in blocks of 64 through a 4-stage TMA
+// ring that continues across tiles; the accumulator is double buffered in TMEM
+// (2 x 256 columns), so a tile's epilogue overlaps the next tile's MMAs. 192 threads:
+//   warps 0-3  epilogue: thread = row (TMEM lane); TMEM -> fp16 (times out_scale) ->
+//              two 16 KB staging buffers of 64 columns (128-B swizzle) -> TMA store;
+//   warp 4     lane 0: TMA producer;
+//   warp 5     lane 0: TMEM allocator and MMA issuer.
+// (One tile per CTA, with the load latency up front and an epilogue that nothing
+// overlapped, ran at 53% of the bf16 peak.)
 // ----------------------------------------------------------------------------------
 namespace k2 {
 constexpr int kStages = 4;
+constexpr int kThreads = 192;
 constexpr uint32_t kStageBytes = 49152;  // A 128x64 (16 KB) + B 256x64 (32 KB)
-constexpr uint32_t kBar = kStages * kStageBytes;
-constexpr uint32_t kSmem = kBar + 128 + 1024;
+constexpr uint32_t kOut = kStages * kStageBytes;  // 2 staging buffers [128 rows][64 cols] fp16
+constexpr uint32_t kBar = kOut + 2 * 16384;
+constexpr uint32_t kSmem = kBar + 256 + 1024;
 static_assert(kSmem <= 232448, "K2 shared memory");
 }  // namespace k2
 
+struct K2Bars {
+  uint64_t full[k2::kStages], empty[k2::kStages];
+  uint64_t d_full[2], d_empty[2];   // accumulator buffers: MMA commit / 128 epilogue threads
+  uint64_t o_ready[2], o_free[2];   // staging halves: 128 epilogue threads / the storing thread
+  uint64_t drain;
+  uint32_t tslot;
+  CtaGuard guard;
+};
+static_assert(sizeof(K2Bars) <= 256, "K2 barrier block");
+
 template <bool kOutgoing>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(k2::kThreads, 1)
     trimul_contract_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap b_map,
-                           const __grid_constant__ CUtensorMap x_map, int C, int K, float out_scale,
-                           uint32_t* status) {
+                           const __grid_constant__ CUtensorMap x_map, int C, int K, int n_jt, int n_it, int n_tiles,
+                           float out_scale, uint32_t* status) {
+  using namespace k2;
   extern __shared__ uint8_t dsmem[];
   uint8_t* smem = align1024(dsmem);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + k2::kBar);
-  uint64_t* empty = full + k2::kStages;
-  uint64_t* done = empty + k2::kStages;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(done + 1);
-  CtaGuard* guard = reinterpret_cast<CtaGuard*>(tslot + 1);
+  K2Bars* bars = reinterpret_cast<K2Bars*>(smem + kBar);
+  CtaGuard* guard = &bars->guard;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int jt = blockIdx.x, it = blockIdx.y;
-  const int c = blockIdx.z % C, b = blockIdx.z / C;
   const int KB = (K + 63) / 64;
+  auto decode = [&](int tile, int& jt, int& it, int& c, int& b) {
+    jt = tile % n_jt;
+    const int r = tile / n_jt;
+    it = r % n_it;
+    const int bc = r / n_it;
+    c = bc % C;
+    b = bc / C;
+  };
 
   if (tid == 0) {
     guard->abort = 0;
-    for (int s = 0; s < k2::kStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
     }
-    mbar_init(done, 1);
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(&bars->d_full[x], 1);
+      mbar_init(&bars->d_empty[x], 128);
+      mbar_init(&bars->o_ready[x], 128);
+      mbar_init(&bars->o_free[x], 1);
+    }
+    mbar_init(&bars->drain, 1);
     fence_barrier_init();
   }
-  if (warp == 1) {
-    tmem_alloc(tslot, 256);
+  if (warp == 5) {
+    tmem_alloc(&bars->tslot, 512);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tslot;
+  const uint32_t tmem = bars->tslot;
 
-  if (warp == 0 && lane == 0) {
-    int issued = 0;
-    for (int kb = 0; kb < KB; ++kb) {
-      const int s = kb % k2::kStages;
-      if (kb >= k2::kStages && !mbar_wait(&empty[s], ((kb / k2::kStages) - 1) & 1, guard, status,
-                                          kStatusTimeoutProducer))
-        break;
-      mbar_arrive_expect_tx(&full[s], k2::kStageBytes);
-      uint8_t* sa = smem + s * k2::kStageBytes;
-      uint8_t* sb = sa + 16384;
-      if (kOutgoing) {
-        tma_load_4d(sa, &a_map, &full[s], kb * 64, c, it * 128, b);
-        tma_load_4d(sb, &b_map, &full[s], kb * 64, c, jt * 256, b);
-      } else {
+  if (warp == 4) {
+    // ------------------------------ TMA producer ------------------------------
+    if (lane == 0) {
+      int g = 0;  // global k-block counter (ring position)
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
+        int jt, it, c, b;
+        decode(tile, jt, it, c, b);
+        for (int kb = 0; kb < KB; ++kb, ++g) {
+          const int s = g % kStages;
+          if (g >= kStages &&
+              !mbar_wait(&bars->empty[s], ((g / kStages) - 1) & 1, guard, status, kStatusTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&bars->full[s], kStageBytes);
+          uint8_t* sa = smem + s * kStageBytes;
+          uint8_t* sb = sa + 16384;
+          if (kOutgoing) {
+            tma_load_4d(sa, &a_map, &bars->full[s], kb * 64, c, it * 128, b);
+            tma_load_4d(sb, &b_map, &bars->full[s], kb * 64, c, jt * 256, b);
+          } else {
 #pragma unroll
-        for (int h = 0; h < 2; ++h) tma_load_4d(sa + h * 8192, &a_map, &full[s], it * 128 + h * 64, c, kb * 64, b);
+            for (int h = 0; h < 2; ++h)
+              tma_load_4d(sa + h * 8192, &a_map, &bars->full[s], it * 128 + h * 64, c, kb * 64, b);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) tma_load_4d(sb + q * 8192, &b_map, &full[s], jt * 256 + q * 64, c, kb * 64, b);
-      }
-      ++issued;
-    }
-    if (guard->abort) {
-      // drain: wait for every load this thread issued that may still be in flight
-      for (int kb = (issued > k2::kStages ? issued - k2::kStages : 0); kb < issued; ++kb)
-        mbar_wait_drain(&full[kb % k2::kStages], (kb / k2::kStages) & 1);
-    }
-  } else if (warp == 1 && lane == 0) {
-    const uint32_t idesc = make_idesc_f16(128, 256, kOutgoing ? 0u : 1u, kOutgoing ? 0u : 1u);
-    for (int kb = 0; kb < KB; ++kb) {
-      const int s = kb % k2::kStages;
-      if (!mbar_wait(&full[s], (kb / k2::kStages) & 1, guard, status, kStatusTimeoutMma)) break;
-      tc_fence_after();
-      const uint32_t sa = smem_u32(smem + s * k2::kStageBytes);
-      const uint32_t sb = sa + 16384;
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        uint64_t ad, bd;
-        if (kOutgoing) {
-          ad = make_sdesc(sa + ks * 32, 16, 1024, Swz::k128);
-          bd = make_sdesc(sb + ks * 32, 16, 1024, Swz::k128);
-        } else {
-          ad = make_sdesc(sa + ks * 2048, 8192, 1024, Swz::k128);
-          bd = make_sdesc(sb + ks * 2048, 8192, 1024, Swz::k128);
+            for (int q = 0; q < 4; ++q)
+              tma_load_4d(sb + q * 8192, &b_map, &bars->full[s], jt * 256 + q * 64, c, kb * 64, b);
+          }
         }
-        umma_ss(tmem, ad, bd, idesc, (kb | ks) != 0 ? 1u : 0u);
       }
-      umma_commit(&empty[s]);
+      if (!ok)  // after an abort, let the copies in flight land before shared memory is released
+        for (int t = (g > kStages ? g - kStages : 0); t < g; ++t)
+          mbar_wait_drain(&bars->full[t % kStages], (t / kStages) & 1);
     }
-    umma_commit(done);
-  }
-
-  const bool waited = mbar_wait(done, 0, guard, status, kStatusTimeoutConsumer);
-  const bool ok = __all_sync(0xffffffffu, waited && !guard->abort);
-  tc_fence_after();
-  if (ok) {
-    const int p = tid;
+  } else if (warp == 5) {
+    // ------------------------------ MMA issuer ------------------------------
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc_f16(128, 256, kOutgoing ? 0u : 1u, kOutgoing ? 0u : 1u);
+      int g = 0, n = 0;  // k-block counter, tile counter of this CTA
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++n) {
+        const int db = n & 1;
+        if (n >= 2 && !mbar_wait(&bars->d_empty[db], ((n >> 1) - 1) & 1, guard, status, kStatusTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        for (int kb = 0; kb < KB; ++kb, ++g) {
+          const int s = g % kStages;
+          if (!mbar_wait(&bars->full[s], (g / kStages) & 1, guard, status, kStatusTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * kStageBytes);
+          const uint32_t sb = sa + 16384;
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            uint64_t ad, bd;
+            if (kOutgoing) {
+              ad = make_sdesc(sa + ks * 32, 16, 1024, Swz::k128);
+              bd = make_sdesc(sb + ks * 32, 16, 1024, Swz::k128);
+            } else {
+              ad = make_sdesc(sa + ks * 2048, 8192, 1024, Swz::k128);
+              bd = make_sdesc(sb + ks * 2048, 8192, 1024, Swz::k128);
+            }
+            umma_ss(tmem + db * 256, ad, bd, idesc, (kb | ks) != 0 ? 1u : 0u);
+          }
+          umma_commit(&bars->empty[s]);
+        }
+        if (ok) umma_commit(&bars->d_full[db]);
+      }
+      umma_commit(&bars->drain);  // also drains whatever was issued before an abort
+      mbar_wait_drain(&bars->drain, 0);
+    }
+  } else {
+    // ------------------------- epilogue: thread = row -------------------------
+    const int p = tid;  // warps 0-3
     const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const bool issuer = (tid == 0);
+    bool ok = true;
+    int n = 0, half = 0;  // tile counter, staging-half counter
+    for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++n) {
+      int jt, it, c, b;
+      decode(tile, jt, it, c, b);
+      const int db = n & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars->d_full[db], (n >> 1) & 1, guard, status, kStatusTimeoutConsumer));
+      if (!ok) break;
+      tc_fence_after();
 #pragma unroll 1
-    for (int cc = 0; cc < 8; ++cc) {
-      uint32_t v[32];
-      tmem_ld32(tmem + lane_base + cc * 32, v);
-      tmem_wait_ld();
-      uint8_t* box = smem + (cc >> 1) * 16384;
-      const int chb = (cc & 1) * 4;
+      for (int hh = 0; hh < 4; ++hh, ++half) {
+        // staging buffer: columns hh*64 .. +63 as one box of [128 rows][128 B]
+        const int ob = half & 1;
+        if (half >= 2) {
+          ok = __all_sync(0xffffffffu, mbar_wait(&bars->o_free[ob], ((half >> 1) - 1) & 1, guard, status,
+                                                 kStatusTimeoutConsumer));
+          if (!ok) break;
+        }
+        uint8_t* stage = smem + kOut + ob * 16384;
+#pragma unroll 1
+        for (int cc = 0; cc < 2; ++cc) {
+          uint32_t v[32];
+          tmem_ld32(tmem + lane_base + db * 256 + hh * 64 + cc * 32, v);
+          tmem_wait_ld();
+          uint8_t* box = stage;
+          const int chb = cc * 4;
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        uint4 o;
-        o.x = pack_f16x2(__uint_as_float(v[u * 8 + 0]) * out_scale, __uint_as_float(v[u * 8 + 1]) * out_scale);
-        o.y = pack_f16x2(__uint_as_float(v[u * 8 + 2]) * out_scale, __uint_as_float(v[u * 8 + 3]) * out_scale);
-        o.z = pack_f16x2(__uint_as_float(v[u * 8 + 4]) * out_scale, __uint_as_float(v[u * 8 + 5]) * out_scale);
-        o.w = pack_f16x2(__uint_as_float(v[u * 8 + 6]) * out_scale, __uint_as_float(v[u * 8 + 7]) * out_scale);
-        sts_u4(box + swz128(p, chb + u), o);
+          for (int u = 0; u < 4; ++u) {
+            uint4 o;
+            o.x = pack_f16x2(__uint_as_float(v[u * 8 + 0]) * out_scale, __uint_as_float(v[u * 8 + 1]) * out_scale);
+            o.y = pack_f16x2(__uint_as_float(v[u * 8 + 2]) * out_scale, __uint_as_float(v[u * 8 + 3]) * out_scale);
+            o.z = pack_f16x2(__uint_as_float(v[u * 8 + 4]) * out_scale, __uint_as_float(v[u * 8 + 5]) * out_scale);
+            o.w = pack_f16x2(__uint_as_float(v[u * 8 + 6]) * out_scale, __uint_as_float(v[u * 8 + 7]) * out_scale);
+            sts_u4(box + swz128(p, chb + u), o);
+          }
+        }
+        if (hh == 3) {
+          tc_fence_before();
+          mbar_arrive(&bars->d_empty[db]);  // the accumulator buffer is read: next MMAs may start
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&bars->o_ready[ob]);
+        if (warp == 0) {
+          // one thread stores the half once all 128 have written it (bounded waits, so that an
+          // abort elsewhere cannot leave threads parked at a barrier)
+          bool iok = true;
+          if (issuer) {
+            iok = mbar_wait(&bars->o_ready[ob], (half >> 1) & 1, guard, status, kStatusTimeoutConsumer);
+            if (iok) {
+              tma_store_4d(&x_map, stage, jt * 256 + hh * 64, c, it * 128, b);
+              tma_store_commit();
+              tma_store_wait_read();
+              mbar_arrive(&bars->o_free[ob]);
+            }
+          }
+          ok = __shfl_sync(0xffffffffu, iok ? 1 : 0, 0) != 0;
+        }
+        if (!ok) break;
       }
     }
-  }
-  fence_proxy_async_smem();
-  __syncthreads();
-  if (tid == 0 && ok && !guard->abort) {
-#pragma unroll
-    for (int q = 0; q < 4; ++q) tma_store_4d(&x_map, smem + q * 16384, jt * 256 + q * 64, c, it * 128, b);
-    tma_store_commit();
-    tma_store_wait_read();
+    if (issuer) tma_store_wait_all();
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == 5) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -1004,15 +1094,19 @@ int gtk_trimul_contract(int outgoing, const void* a_planes, const void* b_planes
   const void* kern = outgoing ? reinterpret_cast<const void*>(trimul_contract_kernel<true>)
                               : reinterpret_cast<const void*>(trimul_contract_kernel<false>);
   if (int e = ensure_smem(kern, k2::kSmem)) return e;
-  dim3 grid(static_cast<unsigned>((Nj + 255) / 256), static_cast<unsigned>((M + 127) / 128),
-            static_cast<unsigned>(B * C));
+  const int64_t n_jt = (Nj + 255) / 256, n_it = (M + 127) / 128;
+  const int64_t n_tiles = n_jt * n_it * B * C;
+  if (n_tiles > 2147483647) return fail(GTK_ERR_INVALID_ARG, "trimul_contract: too many tiles");
+  const int grid = static_cast<int>(n_tiles < num_sms() ? n_tiles : num_sms());
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (outgoing)
-    trimul_contract_kernel<true><<<grid, 128, k2::kSmem, st>>>(am, bm, xm, static_cast<int>(C), static_cast<int>(K),
-                                                                out_scale, status);
+    trimul_contract_kernel<true><<<grid, k2::kThreads, k2::kSmem, st>>>(
+        am, bm, xm, static_cast<int>(C), static_cast<int>(K), static_cast<int>(n_jt), static_cast<int>(n_it),
+        static_cast<int>(n_tiles), out_scale, status);
   else
-    trimul_contract_kernel<false><<<grid, 128, k2::kSmem, st>>>(am, bm, xm, static_cast<int>(C),
-                                                                 static_cast<int>(K), out_scale, status);
+    trimul_contract_kernel<false><<<grid, k2::kThreads, k2::kSmem, st>>>(
+        am, bm, xm, static_cast<int>(C), static_cast<int>(K), static_cast<int>(n_jt), static_cast<int>(n_it),
+        static_cast<int>(n_tiles), out_scale, status);
   return check_launch("trimul_contract_kernel");
 }
 
