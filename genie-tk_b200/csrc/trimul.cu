@@ -33,18 +33,23 @@ namespace gtk {
 // LayerNorm outputs, fan-in-scaled weights, gated projections, the 1/K-scaled contraction --
 // and fp16 keeps 3 more mantissa bits than bf16 at the same tensor-core rate. Conversions
 // saturate to the finite fp16 range.
-//   W1  fp16 [512][128]: rows 0-127 linear_a_p, 128-255 linear_a_g, 256-383 linear_b_p,
-//                        384-511 linear_b_g  (nn.Linear [out, in] = K-major B operand)
-//   W2  fp16 [256][128]: rows 0-127 linear_g, 128-255 linear_z * gamma_out (LN_out scale folded)
-//   vec fp32: b1[512] (the four projection biases), ln_in_w[128], ln_in_b[128], b_g[128],
+//   W1  fp16 [512][128]: rows 0-127 linear_a_p, 128-255 linear_a_g / 2, 256-383 linear_b_p,
+//                        384-511 linear_b_g / 2, each times gamma_in (nn.Linear [out, in] =
+//                        K-major B operand; the gates' 1/2 feeds sigmoid(x) = (1 + tanh(x/2))/2)
+//   W2  fp16 [256][128]: rows 0-127 linear_g * gamma_in, 128-255 linear_z * gamma_out
+//   vec fp32: b1[512] = the four projection biases + W beta_in (gate entries halved too),
+//             b_g[128] = b_g + W_g beta_in,
 //             u[128] = sum_c W2[128+n][c] (fp16-rounded), v[128] = linear_z(beta_out) + b_z.
+// Both LayerNorm affines are folded into the weights: LN(x) W^T + b = xhat (W*gamma)^T +
+// (W beta + b) with xhat = (x - mu) * rstd, so the kernels' LayerNorm producers write xhat
+// alone; for LN_out the mean term is folded too:
 // LN_out(x) W_z^T + b_z = rstd * (x (W_z*gamma)^T - mu * u) + v for per-pair mean mu, rstd.
 // ----------------------------------------------------------------------------------
 namespace tmpack {
 constexpr size_t kW1 = 0;
 constexpr size_t kW2 = 512 * 128 * 2;
 constexpr size_t kVec = kW2 + 256 * 128 * 2;
-constexpr int kVB1 = 0, kVLnW = 512, kVLnB = 640, kVBg = 768, kVU = 896, kVV = 1024, kVecFloats = 1152;
+constexpr int kVB1 = 0, kVBg = 512, kVU = 640, kVV = 768, kVecFloats = 896;
 constexpr size_t kBytes = kVec + kVecFloats * 4;
 }  // namespace tmpack
 
@@ -57,21 +62,25 @@ __global__ void trimul_pack_kernel(gtk_trimul_params p, uint8_t* packed) {
   for (int e = tid; e < 512 * 128; e += nthreads) {
     const int r = e >> 7, c = e & 127;
     const float* src = r < 128 ? p.a_p_w : r < 256 ? p.a_g_w : r < 384 ? p.b_p_w : p.b_g_w;
-    w1[e] = f16_sat(src[(r & 127) * 128 + c]);
+    w1[e] = f16_sat(src[(r & 127) * 128 + c] * p.ln_in_w[c] * (((r >> 7) & 1) ? 0.5f : 1.f));
   }
   for (int e = tid; e < 256 * 128; e += nthreads) {
     const int r = e >> 7, c = e & 127;
-    const float val = r < 128 ? p.g_w[r * 128 + c] : p.z_w[(r - 128) * 128 + c] * p.ln_out_w[c];
+    const float val = r < 128 ? p.g_w[r * 128 + c] * p.ln_in_w[c] : p.z_w[(r - 128) * 128 + c] * p.ln_out_w[c];
     w2[e] = f16_sat(val);
   }
+  for (int e = tid; e < 512; e += nthreads) {
+    const int r = e & 127;
+    const float* w = e < 128 ? p.a_p_w : e < 256 ? p.a_g_w : e < 384 ? p.b_p_w : p.b_g_w;
+    const float* bb = e < 128 ? p.a_p_b : e < 256 ? p.a_g_b : e < 384 ? p.b_p_b : p.b_g_b;
+    float acc = bb[r];
+    for (int c = 0; c < 128; ++c) acc += w[r * 128 + c] * p.ln_in_b[c];
+    vec[tmpack::kVB1 + e] = acc * (((e >> 7) & 1) ? 0.5f : 1.f);
+  }
   for (int e = tid; e < 128; e += nthreads) {
-    vec[tmpack::kVB1 + e] = p.a_p_b[e];
-    vec[tmpack::kVB1 + 128 + e] = p.a_g_b[e];
-    vec[tmpack::kVB1 + 256 + e] = p.b_p_b[e];
-    vec[tmpack::kVB1 + 384 + e] = p.b_g_b[e];
-    vec[tmpack::kVLnW + e] = p.ln_in_w[e];
-    vec[tmpack::kVLnB + e] = p.ln_in_b[e];
-    vec[tmpack::kVBg + e] = p.g_b[e];
+    float bg = p.g_b[e];
+    for (int c = 0; c < 128; ++c) bg += p.g_w[e * 128 + c] * p.ln_in_b[c];
+    vec[tmpack::kVBg + e] = bg;
     float u = 0.f, v = p.z_b[e];
     for (int c = 0; c < 128; ++c) {
       u += __half2float(f16_sat(p.z_w[e * 128 + c] * p.ln_out_w[c]));
@@ -84,31 +93,37 @@ __global__ void trimul_pack_kernel(gtk_trimul_params p, uint8_t* packed) {
 
 // ----------------------------------------------------------------------------------
 // K1: persistent, warp-specialised LN_in + gated projections + mask -> a, b planes.
-// Tile = 128 consecutive pairs (b, r, j0..j0+127); CTAs loop over tiles. 416 threads:
-//   warp 12    lane 0: TMA producer and MMA issuer. The 128 KB of packed weights are
-//              loaded once; each tile's 128 x 128 fp32 z block arrives by TMA (64 KB in
-//              flight per tile, refilled as soon as the LayerNorm has read it);
+// Tile = 128 consecutive pairs (b, r, j0..j0+127); CTAs loop over tiles. 512 threads:
 //   warps 0-7  LayerNorm producers, two threads per pair row (64 channels each, statistics
 //              combined with one shuffle): one pass reads the staged, 128-B-swizzled z tile
 //              into registers (conflict-free) and releases it, then the fp16 operand tile A
-//              is written; the pair's mask value is staged as well. (One thread per row
-//              with three passes over the tile kept the z buffer busy through the whole
-//              LayerNorm, serialising it with the next tile's load.)
-//   warps 8-11 epilogue: thread = channel c (TMEM lane), reads 32-pair slabs of the
-//              projection / gate accumulators, applies bias, sigmoid and mask, and writes
-//              64 contiguous bytes of its channel-plane row per slab.
+//              (xhat; the affine is folded into W1) is written and the pair's mask value
+//              staged. (One thread per row with three passes over the tile kept the z
+//              buffer busy through the whole LayerNorm.)
+//              Thread 0 is also the TMA producer and MMA issuer: the 128 KB of packed
+//              weights are loaded once; each tile's 128 x 128 fp32 z block arrives by TMA
+//              (64 KB), refilled as soon as all producers have read it; after writing its
+//              part of A it issues the tile's MMAs. No warp is spent on issuing alone, so
+//              sixteen warps keep 128 registers per thread.
+//   warps 8-15 epilogue: thread = channel c (TMEM lane quarter = warp % 4), warps 8-11 take
+//              pairs 0-63 of the tile and warps 12-15 pairs 64-127, in 16-pair chunks of the
+//              projection / gate accumulators (the next chunk's TMEM loads in flight while
+//              one is computed); each writes 32 contiguous bytes of its channel-plane row per
+//              chunk. Two warps per scheduler: with one, the epilogue was latency-bound at
+//              ~4,000 cycles per accumulator half (clock64 trace).
 // MMA (transposed so that channels sit on TMEM lanes): D[c][j] = W_chunk[c][:] . A[j][:],
 // M = 128 channels, N = 128 pairs, K = 128. Chunks (a_p, a_g) -> TMEM columns 0-255
 // (half 0), (b_p, b_g) -> 256-511 (half 1); the epilogue of half 0 overlaps the MMAs of
-// half 1, and the next tile's z load overlaps both. (A second epilogue warpgroup, one per
-// half, was measured slower: 0.48 vs 0.39 ms at N = 1024, with the 416-thread launch
-// capping registers at 128.)
+// half 1, and the next tile's z load overlaps both.
+// Gate: W1's gate rows and biases carry a factor 1/2 and the staged mask value is m/2, so
+// with pm = (p + b_p) m / 2 the output is pm + pm tanh(g') = (p + b_p) sigmoid(g) m -- one
+// MUFU op and three FP32 ops per element.
 // Shared memory: W1 128 KB | A 32 KB | z 64 KB | mask 2 x 512 B | barriers.
 // ----------------------------------------------------------------------------------
 constexpr int kMaxPlaneDsts = 8;
 
 namespace k1 {
-constexpr int kThreads = 416;
+constexpr int kThreads = 512;
 constexpr uint32_t kW = 0, kA = 131072, kZ = 163840, kMask = 229376, kBar = 230400;
 constexpr uint32_t kSmem = kBar + 128 + 1024;
 static_assert(kSmem <= 232448, "K1 shared memory");
@@ -145,7 +160,7 @@ __global__ void __launch_bounds__(k1::kThreads, 1)
   uint8_t* smem = align1024(dsmem);
   K1Bars* bars = reinterpret_cast<K1Bars*>(smem + k1::kBar);
   CtaGuard* guard = &bars->guard;
-  float* mask_s = reinterpret_cast<float*>(smem + k1::kMask);  // [2][128]
+  float* mask_s = reinterpret_cast<float*>(smem + k1::kMask);  // [2][128], m / 2
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   if (tid == 0) {
@@ -157,13 +172,13 @@ __global__ void __launch_bounds__(k1::kThreads, 1)
     mbar_init(&bars->a_empty, 1);
     for (int x = 0; x < 2; ++x) {
       mbar_init(&bars->d_full[x], 1);
-      mbar_init(&bars->d_empty[x], 128);
-      mbar_init(&bars->m_empty[x], 128);
+      mbar_init(&bars->d_empty[x], 256);
+      mbar_init(&bars->m_empty[x], 256);
     }
     mbar_init(&bars->drain, 1);
     fence_barrier_init();
   }
-  if (warp == 12) {
+  if (warp == 8) {
     tmem_alloc(&bars->tslot, 512);
     tmem_relinquish();
   }
@@ -173,18 +188,42 @@ __global__ void __launch_bounds__(k1::kThreads, 1)
   const uint32_t tmem = bars->tslot;
 
   if (warp < 8) {
-    // --------------- LayerNorm producers: two threads per pair row ---------------
+    // ------- LayerNorm producers (two threads per pair row); thread 0 also issues -------
     // Each thread reads its 64 channels of the staged z tile into registers once and
     // releases the tile, so the next tile's z load overlaps the rest of the LayerNorm.
     const int p = warp * 16 + (lane >> 1), half = lane & 1;
-    const float* lnw = vec + tmpack::kVLnW + half * 64;
-    const float* lnb = vec + tmpack::kVLnB + half * 64;
+    auto load_z = [&](int tile) {
+      const int jt = tile % n_jt, rb = tile / n_jt;
+      const int r = rb % rows, b = rb / rows;
+      mbar_arrive_expect_tx(&bars->z_full, 65536);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) tma_load_4d(smem + k1::kZ + q * 16384, &z_map, &bars->z_full, q * 32, jt * 128, r, b);
+    };
+    int loaded = 0;  // z tiles requested (thread 0)
+    if (tid == 0) {
+      mbar_arrive_expect_tx(&bars->wbar, 131072);
+#pragma unroll
+      for (int kh = 0; kh < 2; ++kh)
+#pragma unroll
+        for (int rb = 0; rb < 4; ++rb)
+          tma_load_2d(smem + k1::kW + kh * 65536 + rb * 16384, &w_map, &bars->wbar, kh * 64, rb * 128);
+      load_z(blockIdx.x);  // the grid never exceeds the tile count
+      loaded = 1;
+    }
+    const uint32_t idesc = make_idesc_f16(128, 128, 0, 0);
+    const uint32_t w0 = smem_u32(smem + k1::kW), a0 = smem_u32(smem + k1::kA);
+    bool ok = true;
     int it = 0;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
       const int s = it & 1;
       const int jt = tile % n_jt, rb = tile / n_jt;
       const int r = rb % rows, b = rb / rows, j0 = jt * 128;
-      if (!__all_sync(0xffffffffu, mbar_wait(&bars->z_full, it & 1, guard, status, kStatusTimeoutProducer))) break;
+      // the pair's mask value, loaded before the waits so its DRAM latency is hidden
+      float mval = 0.f;
+      if (half == 0 && j0 + p < N)
+        mval = mask ? __ldg(mask + (static_cast<size_t>(b) * rows + r) * N + j0 + p) : 1.f;
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars->z_full, it & 1, guard, status, kStatusTimeoutProducer));
+      if (!ok) break;
       float v[64];
 #pragma unroll
       for (int q = 0; q < 2; ++q)
@@ -197,6 +236,19 @@ __global__ void __launch_bounds__(k1::kThreads, 1)
           v[q * 32 + ch * 4 + 3] = t.w;
         }
       mbar_arrive(&bars->z_empty);  // the z tile may be refilled
+      if (warp == 0) {
+        // thread 0: refill z with the next tile once every producer has read this one
+        bool w = true;
+        if (lane == 0 && tile + static_cast<int>(gridDim.x) < n_tiles) {
+          w = mbar_wait(&bars->z_empty, it & 1, guard, status, kStatusTimeoutMma);
+          if (w) {
+            load_z(tile + gridDim.x);
+            ++loaded;
+          }
+        }
+        ok = __all_sync(0xffffffffu, w);
+        if (!ok) break;
+      }
       float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < 64; ++c) s4[c & 3] += v[c];
@@ -215,89 +267,62 @@ __global__ void __launch_bounds__(k1::kThreads, 1)
       bool w = true;
       if (it >= 1) w = mbar_wait(&bars->a_empty, (it - 1) & 1, guard, status, kStatusTimeoutProducer);
       if (it >= 2) w = w && mbar_wait(&bars->m_empty[s], ((it >> 1) - 1) & 1, guard, status, kStatusTimeoutProducer);
-      if (!__all_sync(0xffffffffu, w)) break;
-      if (half == 0) {
-        const int j = j0 + p;
-        mask_s[s * 128 + p] = j < N ? (mask ? mask[(static_cast<size_t>(b) * rows + r) * N + j] : 1.f) : 0.f;
-      }
+      ok = __all_sync(0xffffffffu, w);
+      if (!ok) break;
+      if (half == 0) mask_s[s * 128 + p] = 0.5f * mval;
+      // xhat only: gamma_in and beta_in are folded into W1 and b1
 #pragma unroll
       for (int ch = 0; ch < 8; ++ch) {
         const int c = ch * 8;
-        const float4 w0 = __ldg(reinterpret_cast<const float4*>(lnw + c));
-        const float4 w1 = __ldg(reinterpret_cast<const float4*>(lnw + c + 4));
-        const float4 b0 = __ldg(reinterpret_cast<const float4*>(lnb + c));
-        const float4 b1 = __ldg(reinterpret_cast<const float4*>(lnb + c + 4));
         uint4 o;
-        o.x = pack_f16x2((v[c + 0] - mean) * rstd * w0.x + b0.x, (v[c + 1] - mean) * rstd * w0.y + b0.y);
-        o.y = pack_f16x2((v[c + 2] - mean) * rstd * w0.z + b0.z, (v[c + 3] - mean) * rstd * w0.w + b0.w);
-        o.z = pack_f16x2((v[c + 4] - mean) * rstd * w1.x + b1.x, (v[c + 5] - mean) * rstd * w1.y + b1.y);
-        o.w = pack_f16x2((v[c + 6] - mean) * rstd * w1.z + b1.z, (v[c + 7] - mean) * rstd * w1.w + b1.w);
+        o.x = pack_f16x2((v[c + 0] - mean) * rstd, (v[c + 1] - mean) * rstd);
+        o.y = pack_f16x2((v[c + 2] - mean) * rstd, (v[c + 3] - mean) * rstd);
+        o.z = pack_f16x2((v[c + 4] - mean) * rstd, (v[c + 5] - mean) * rstd);
+        o.w = pack_f16x2((v[c + 6] - mean) * rstd, (v[c + 7] - mean) * rstd);
         sts_u4(smem + k1::kA + half * 16384 + swz128(p, ch), o);
       }
       fence_proxy_async_smem();
       mbar_arrive(&bars->a_full);
-    }
-  } else if (warp == 12) {
-    // ------------------------- TMA producer + MMA issuer -------------------------
-    if (lane == 0) {
-      auto load_z = [&](int tile) {
-        const int jt = tile % n_jt, rb = tile / n_jt;
-        const int r = rb % rows, b = rb / rows;
-        mbar_arrive_expect_tx(&bars->z_full, 65536);
+      if (warp == 0) {
+        // thread 0: the tile's MMAs, half h once the epilogue has drained half h of the
+        // previous tile
+        bool mw = true;
+        if (lane == 0) {
+          mw = mbar_wait(&bars->a_full, it & 1, guard, status, kStatusTimeoutMma);
+          if (mw && it == 0) mw = mbar_wait(&bars->wbar, 0, guard, status, kStatusTimeoutMma);
+          for (int h = 0; mw && h < 2; ++h) {
+            if (it >= 1) mw = mbar_wait(&bars->d_empty[h], (it - 1) & 1, guard, status, kStatusTimeoutMma);
+            if (!mw) break;
+            tc_fence_after();
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-          tma_load_4d(smem + k1::kZ + q * 16384, &z_map, &bars->z_full, q * 32, jt * 128, r, b);
-      };
-      mbar_arrive_expect_tx(&bars->wbar, 131072);
+            for (int q = 0; q < 2; ++q) {
+              const int chunk = 2 * h + q;
 #pragma unroll
-      for (int kh = 0; kh < 2; ++kh)
-#pragma unroll
-        for (int rb = 0; rb < 4; ++rb)
-          tma_load_2d(smem + k1::kW + kh * 65536 + rb * 16384, &w_map, &bars->wbar, kh * 64, rb * 128);
-      if (blockIdx.x < n_tiles) load_z(blockIdx.x);
-      int loaded = blockIdx.x < n_tiles ? 1 : 0;
-      bool ok = mbar_wait(&bars->wbar, 0, guard, status, kStatusTimeoutMma);
-      const uint32_t idesc = make_idesc_f16(128, 128, 0, 0);
-      const uint32_t w0 = smem_u32(smem + k1::kW), a0 = smem_u32(smem + k1::kA);
-      int it = 0;
-      for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++it) {
-        const int next = tile + gridDim.x;
-        if (next < n_tiles) {
-          ok = mbar_wait(&bars->z_empty, it & 1, guard, status, kStatusTimeoutMma);
-          if (!ok) break;
-          load_z(next);
-          ++loaded;
-        }
-        ok = mbar_wait(&bars->a_full, it & 1, guard, status, kStatusTimeoutMma);
-        for (int h = 0; ok && h < 2; ++h) {
-          if (it >= 1) ok = mbar_wait(&bars->d_empty[h], (it - 1) & 1, guard, status, kStatusTimeoutMma);
-          if (!ok) break;
-          tc_fence_after();
-#pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            const int chunk = 2 * h + q;
-#pragma unroll
-            for (int ks = 0; ks < 8; ++ks) {
-              const int kh = ks >> 2, kin = ks & 3;
-              umma_ss(tmem + h * 256 + q * 128,
-                      make_sdesc(w0 + kh * 65536 + chunk * 16384 + kin * 32, 16, 1024, Swz::k128),
-                      make_sdesc(a0 + kh * 16384 + kin * 32, 16, 1024, Swz::k128), idesc, ks > 0 ? 1u : 0u);
+              for (int ks = 0; ks < 8; ++ks) {
+                const int kh = ks >> 2, kin = ks & 3;
+                umma_ss(tmem + h * 256 + q * 128,
+                        make_sdesc(w0 + kh * 65536 + chunk * 16384 + kin * 32, 16, 1024, Swz::k128),
+                        make_sdesc(a0 + kh * 16384 + kin * 32, 16, 1024, Swz::k128), idesc, ks > 0 ? 1u : 0u);
+              }
             }
+            umma_commit(&bars->d_full[h]);
           }
-          umma_commit(&bars->d_full[h]);
+          if (mw) umma_commit(&bars->a_empty);
         }
-        if (ok) umma_commit(&bars->a_empty);
+        ok = __all_sync(0xffffffffu, mw);
+        if (!ok) break;
       }
-      if (!ok) {
-        umma_commit(&bars->drain);
-        mbar_wait_drain(&bars->drain, 0);
-        if (loaded > 0) mbar_wait_drain(&bars->z_full, (loaded - 1) & 1);
-        mbar_wait_drain(&bars->wbar, 0);
-      }
+    }
+    if (!ok && tid == 0) {
+      // abort: wait (bounded) for this thread's MMAs and TMA loads still in flight
+      umma_commit(&bars->drain);
+      mbar_wait_drain(&bars->drain, 0);
+      if (loaded > 0) mbar_wait_drain(&bars->z_full, (loaded - 1) & 1);
+      mbar_wait_drain(&bars->wbar, 0);
     }
   } else {
     // ------------------------- epilogue: thread = channel -------------------------
-    const int q4 = warp & 3;
+    const int q4 = warp & 3, jh = (warp - 8) >> 2;  // TMEM lane quarter, pair half of the tile
     const int c = q4 * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
     const int grp = c / a_dst.group, c_in_grp = c - grp * a_dst.group;  // this channel's destination group
@@ -307,8 +332,8 @@ __global__ void __launch_bounds__(k1::kThreads, 1)
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
       const int s = it & 1;
       const int jt = tile % n_jt, rb = tile / n_jt;
-      const int r = rb % rows, b = rb / rows, j0 = jt * 128;
-      const float* ms = mask_s + s * 128;
+      const int r = rb % rows, b = rb / rows, j0 = jt * 128 + jh * 64;
+      const float* ms = mask_s + s * 128 + jh * 64;
       bool ok = true;
 #pragma unroll 1
       for (int h = 0; h < 2; ++h) {
@@ -321,36 +346,42 @@ __global__ void __launch_bounds__(k1::kThreads, 1)
                       ((static_cast<size_t>(b) * a_dst.dst_rows + a_dst.row0 + r) * a_dst.group + c_in_grp) * ld;
         const bool wide = (ld & 15) == 0 && (base & 31) == 0;
         const float bp = h ? bias_p1 : bias_p0, bg = h ? bias_g1 : bias_g0;
-#pragma unroll 1
-        for (int jc = 0; jc < 4; ++jc) {
-          uint32_t pv[32], gv[32];
-          tmem_ld32(tmem + lane_off + h * 256 + jc * 32, pv);
-          tmem_ld32(tmem + lane_off + h * 256 + 128 + jc * 32, gv);
-          tmem_wait_ld();
-          uint32_t w[16];  // 32 pairs of this channel as fp16
+        // 16-pair chunks of the projection / gate accumulators, software pipelined: the
+        // TMEM loads of chunk k+1 are in flight while chunk k is computed and stored.
+        const uint32_t tp = tmem + lane_off + h * 256 + jh * 64;
+        uint32_t pv[2][16], gv[2][16];
+        tmem_ld16(tp, pv[0]);
+        tmem_ld16(tp + 128, gv[0]);
 #pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const float4 m4 = *reinterpret_cast<const float4*>(ms + jc * 32 + u * 4);
+        for (int jc = 0; jc < 4; ++jc) {
+          const int cur = jc & 1;
+          tmem_wait_ld_regs(pv[cur], gv[cur]);
+          if (jc + 1 < 4) {
+            tmem_ld16(tp + (jc + 1) * 16, pv[cur ^ 1]);
+            tmem_ld16(tp + 128 + (jc + 1) * 16, gv[cur ^ 1]);
+          }
+          uint32_t w[8];  // 16 pairs of this channel as fp16
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const float4 m4 = *reinterpret_cast<const float4*>(ms + jc * 16 + u * 4);
             const float mv[4] = {m4.x, m4.y, m4.z, m4.w};
             float o[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e)
-              o[e] = (__uint_as_float(pv[u * 4 + e]) + bp) * sigmoid_tanh(__uint_as_float(gv[u * 4 + e]) + bg) * mv[e];
+            for (int e = 0; e < 4; ++e) {
+              const float pm = (__uint_as_float(pv[cur][u * 4 + e]) + bp) * mv[e];
+              o[e] = fmaf(pm, tanh_approx(__uint_as_float(gv[cur][u * 4 + e]) + bg), pm);
+            }
             w[2 * u] = pack_f16x2(o[0], o[1]);
             w[2 * u + 1] = pack_f16x2(o[2], o[3]);
           }
-          // 64 contiguous bytes of the channel row: 32-byte stores when the plane pitch keeps
-          // them 32-byte aligned (pitch a multiple of 16), 16-byte stores otherwise
-          const int jb = j0 + jc * 32;
+          // 32 contiguous bytes of the channel row: one 32-byte store when the plane pitch
+          // keeps it 32-byte aligned (pitch a multiple of 16), two 16-byte stores otherwise
+          const int jb = j0 + jc * 16;
           if (wide) {
-#pragma unroll
-            for (int v = 0; v < 2; ++v)
-              if (jb + 16 * v < ld)
-                stg_v8(dst + jb + 16 * v, w[8 * v], w[8 * v + 1], w[8 * v + 2], w[8 * v + 3], w[8 * v + 4],
-                       w[8 * v + 5], w[8 * v + 6], w[8 * v + 7]);
+            if (jb < ld) stg_v8(dst + jb, w[0], w[1], w[2], w[3], w[4], w[5], w[6], w[7]);
           } else {
 #pragma unroll
-            for (int v = 0; v < 4; ++v)
+            for (int v = 0; v < 2; ++v)
               if (jb + 8 * v < ld)
                 *reinterpret_cast<uint4*>(dst + jb + 8 * v) = make_uint4(w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
           }
@@ -364,7 +395,7 @@ __global__ void __launch_bounds__(k1::kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 12) {
+  if (warp == 8) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -695,8 +726,6 @@ __global__ void __launch_bounds__(k2e::kThreads, 1)
   if (warp < 8) {
     // ---------------- LayerNorm producers: two threads per pair row ----------------
     const int row = warp * 16 + (lane >> 1), half = lane & 1;
-    const float* lnw = vec + tmpack::kVLnW + half * 64;
-    const float* lnb = vec + tmpack::kVLnB + half * 64;
     int it = 0;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
       if (!__all_sync(0xffffffffu, mbar_wait(&bars->z_full, it & 1, guard, status, kStatusTimeoutProducer))) break;
@@ -730,18 +759,15 @@ __global__ void __launch_bounds__(k2e::kThreads, 1)
       const float rstd = rsqrtf(ss * (1.f / 128.f) + 1e-5f);
       // A overwrites the z tile: wait until every LayerNorm thread has read its rows
       if (!__all_sync(0xffffffffu, mbar_wait(&bars->z_read, it & 1, guard, status, kStatusTimeoutProducer))) break;
+      // xhat only: gamma_in and beta_in are folded into the gate weights and b_g
 #pragma unroll
       for (int ch = 0; ch < 8; ++ch) {
         const int c = ch * 8;
-        const float4 w0 = __ldg(reinterpret_cast<const float4*>(lnw + c));
-        const float4 w1 = __ldg(reinterpret_cast<const float4*>(lnw + c + 4));
-        const float4 b0 = __ldg(reinterpret_cast<const float4*>(lnb + c));
-        const float4 b1 = __ldg(reinterpret_cast<const float4*>(lnb + c + 4));
         uint4 o;
-        o.x = pack_f16x2((v[c + 0] - mean) * rstd * w0.x + b0.x, (v[c + 1] - mean) * rstd * w0.y + b0.y);
-        o.y = pack_f16x2((v[c + 2] - mean) * rstd * w0.z + b0.z, (v[c + 3] - mean) * rstd * w0.w + b0.w);
-        o.z = pack_f16x2((v[c + 4] - mean) * rstd * w1.x + b1.x, (v[c + 5] - mean) * rstd * w1.y + b1.y);
-        o.w = pack_f16x2((v[c + 6] - mean) * rstd * w1.z + b1.z, (v[c + 7] - mean) * rstd * w1.w + b1.w);
+        o.x = pack_f16x2((v[c + 0] - mean) * rstd, (v[c + 1] - mean) * rstd);
+        o.y = pack_f16x2((v[c + 2] - mean) * rstd, (v[c + 3] - mean) * rstd);
+        o.z = pack_f16x2((v[c + 4] - mean) * rstd, (v[c + 5] - mean) * rstd);
+        o.w = pack_f16x2((v[c + 6] - mean) * rstd, (v[c + 7] - mean) * rstd);
         sts_u4(smem + kA + half * 16384 + swz128(row, ch), o);
       }
       fence_proxy_async_smem();
