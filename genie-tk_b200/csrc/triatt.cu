@@ -39,9 +39,9 @@ constexpr float kLog2e = 1.4426950408889634f;
 // ----------------------------------------------------------------------------------
 // Packed weights (fp16 operands, fp32 vectors):
 //   W3 fp16 [512][128]: rows 0-127 linear_q * log2(e)/sqrt(d), 128-255 linear_k,
-//                       256-383 linear_v, 384-511 linear_g
+//                       256-383 linear_v, 384-511 linear_g / 2
 //   W4 fp16 [128][128]: linear_o
-//   vec fp32: ln_w[128], ln_b[128], w_bias[4][128] * log2(e), b_g[128], b_o[128]
+//   vec fp32: ln_w[128], ln_b[128], w_bias[4][128] * log2(e), b_g[128] / 2, b_o[128]
 // ----------------------------------------------------------------------------------
 namespace tapack {
 constexpr size_t kW3 = 0;
@@ -63,14 +63,14 @@ __global__ void triatt_pack_kernel(gtk_triatt_params p, uint8_t* packed, float q
     if (r < 128) v = p.q_w[r * 128 + c] * q_scale;
     else if (r < 256) v = p.k_w[(r - 128) * 128 + c];
     else if (r < 384) v = p.v_w[(r - 256) * 128 + c];
-    else v = p.g_w[(r - 384) * 128 + c];
+    else v = 0.5f * p.g_w[(r - 384) * 128 + c];  // sigmoid(x) = (1 + tanh(x/2)) / 2
     w3[e] = f16_sat(v);
   }
   for (int e = tid; e < 128 * 128; e += nthreads) w4[e] = f16_sat(p.o_w[e]);
   for (int e = tid; e < 128; e += nthreads) {
     vec[tapack::kVLnW + e] = p.ln_w[e];
     vec[tapack::kVLnB + e] = p.ln_b[e];
-    vec[tapack::kVBg + e] = p.g_b[e];
+    vec[tapack::kVBg + e] = 0.5f * p.g_b[e];
     vec[tapack::kVBo + e] = p.o_b[e];
     for (int h = 0; h < kHeads; ++h) vec[tapack::kVWb + h * 128 + e] = p.bias_w[h * 128 + e] * kLog2e;
   }
@@ -101,24 +101,31 @@ __device__ __forceinline__ float warp_sum4_transposed(float v0, float v1, float 
 
 // ----------------------------------------------------------------------------------
 // K3: persistent LN + q/k/v/g projections + triangle bias. Tile = 128 consecutive pairs
-// (b, row i of the problem, j0..j0+127); CTAs loop over tiles. 416 threads:
-//   warp 12    lane 0: TMA producer and MMA issuer. The 128 KB of weights are loaded
-//              once; each tile's 128 x 128 fp32 z block (z^T for the ending node, through
-//              the transposed descriptor) arrives by TMA, 64 KB in flight per tile;
+// (b, row i of the problem, j0..j0+127); CTAs loop over tiles. 512 threads:
 //   warps 0-7  LayerNorm producers, two threads per pair row (64 channels each): one pass
 //              reads the staged z tile into registers and releases it, then the fp16
 //              operand A and the four triangle-bias dot products of the fp32 LN output
 //              (stored bf16, times log2 e) are formed; statistics and dot products combine
 //              with one shuffle each (a warp-per-row version spent ~700 cycles per row in
 //              dependent shuffle chains; one thread per row with three passes kept the z
-//              buffer busy through the whole LayerNorm);
-//   warps 8-11 epilogue, thread = pair (TMEM lane): TMEM half 0 (q, k), then half 1 (v and
-//              the gate): rows of 64 B per head and the sigmoid gate row of 256 B, written
-//              with 32-byte stores. (Thirteen warps keep 128 registers per thread: a
-//              seventeen-warp launch is allocated like twenty warps, 96 registers, and spills.)
+//              buffer busy through the whole LayerNorm).
+//              Thread 0 is also the TMA producer and MMA issuer: the 128 KB of weights are
+//              loaded once; each tile's 128 x 128 fp32 z block (z^T for the ending node,
+//              through the transposed descriptor) arrives by TMA, refilled as soon as all
+//              producers have read it; after writing its part of A it issues the tile's
+//              MMAs. No warp is spent on issuing alone, so sixteen warps keep 128 registers
+//              per thread (a seventeen-warp launch is allocated like twenty warps, 96
+//              registers, and spills).
+//   warps 8-15 epilogue, thread = pair (TMEM lane quarter = warp % 4); warps 8-11 take heads
+//              0-1 and warps 12-15 heads 2-3 of TMEM half 0 (q, k), then of half 1 (v and
+//              the gate), in 16-column chunks whose TMEM loads run one chunk ahead; each
+//              chunk is one 32-byte store per output row (64 B per head row, 256 B gate row).
+//              Two warps per scheduler: with one, a K1 epilogue of the same shape was
+//              latency-bound (clock64 trace).
 // TMEM: half 0 = (q, k) columns 0-255, half 1 = (v, g) columns 256-511; the epilogue of
 // half 0 overlaps the MMAs of half 1, and the next tile's LayerNorm and z load overlap both.
-// Shared memory: W3 128 KB | z 64 KB | A 32 KB | barriers.
+// Gate: W3's gate rows and b_g carry a factor 1/2, sigmoid(x) = (1 + tanh(x/2)) / 2.
+// Shared memory: W3 128 KB | z 64 KB | A 32 KB | b_g/2 512 B | barriers.
 // Rows: the tile grid covers `rows` problem rows i (all N when unsharded; one shard's rows
 // under row sharding, which only the starting orientation supports).
 // Outputs: q, k, v fp16 [B*rows(i)][H][N(j)][32]; g fp16 [B*rows*N][128]; bias bf16
@@ -128,9 +135,14 @@ __device__ __forceinline__ float warp_sum4_transposed(float v0, float v1, float 
 // bias tile at 256 B per query row and step, and widens with one integer op).
 // ----------------------------------------------------------------------------------
 namespace k3 {
-constexpr int kThreads = 416;
-constexpr uint32_t kW = 0, kZ = 131072, kA = 196608, kBar = 229376;
-constexpr uint32_t kSmem = kBar + 128 + 1024;
+constexpr int kThreads = 512;
+// Parameters staged in shared memory: gamma / beta fp32 [8 chunks][2 halves][8] each,
+// the bias weights fp16 [8 chunks][4 heads][2 halves][8], b_g / 2 fp32 [128].
+constexpr uint32_t kW = 0, kZ = 131072, kA = 196608, kLnW = 229376, kLnB = 229888, kWb = 230400, kBg = 231424,
+                   kBar = 231936;
+// No alignment slack: the kernel requires a 1024-aligned dynamic shared-memory base (it
+// checks, and reports GTK_STATUS bit 4 without touching memory otherwise).
+constexpr uint32_t kSmem = kBar + 128;
 static_assert(kSmem <= 232448, "K3 shared memory");
 }  // namespace k3
 
@@ -150,10 +162,18 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
                           const float* __restrict__ vec, __half* __restrict__ q_out, __half* __restrict__ k_out,
                           __half* __restrict__ v_out, __half* __restrict__ g_out, __nv_bfloat16* __restrict__ bias,
                           int N, int rows, int B, int row0, int ldn, int n_jt, int n_tiles, uint32_t* status) {
-  extern __shared__ uint8_t dsmem[];
-  uint8_t* smem = align1024(dsmem);
+  extern __shared__ __align__(1024) uint8_t dsmem[];
+  if (smem_u32(dsmem) & 1023u) {  // uniform across the CTA: every thread leaves here
+    if (threadIdx.x == 0 && status) atomicOr(status, kStatusBadLaunch);
+    return;
+  }
+  uint8_t* smem = dsmem;
   K3Bars* bars = reinterpret_cast<K3Bars*>(smem + k3::kBar);
   CtaGuard* guard = &bars->guard;
+  float* lnw_s = reinterpret_cast<float*>(smem + k3::kLnW);
+  float* lnb_s = reinterpret_cast<float*>(smem + k3::kLnB);
+  __half* wb_s = reinterpret_cast<__half*>(smem + k3::kWb);
+  float* bg_s = reinterpret_cast<float*>(smem + k3::kBg);  // b_g / 2
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   if (tid == 0) {
@@ -165,12 +185,21 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
     mbar_init(&bars->a_empty, 1);
     for (int x = 0; x < 2; ++x) {
       mbar_init(&bars->d_full[x], 1);
-      mbar_init(&bars->d_empty[x], 128);
+      mbar_init(&bars->d_empty[x], 256);
     }
     mbar_init(&bars->drain, 1);
     fence_barrier_init();
   }
-  if (warp == 12) {
+  if (tid < 128) {
+    const int c = tid, hf = c >> 6, ch = (c & 63) >> 3, e = c & 7;  // channel c = 64 hf + 8 ch + e
+    bg_s[c] = vec[tapack::kVBg + c];
+    lnw_s[(ch * 2 + hf) * 8 + e] = vec[tapack::kVLnW + c];
+    lnb_s[(ch * 2 + hf) * 8 + e] = vec[tapack::kVLnB + c];
+#pragma unroll
+    for (int h = 0; h < kHeads; ++h)
+      wb_s[((ch * kHeads + h) * 2 + hf) * 8 + e] = __float2half_rn(vec[tapack::kVWb + h * 128 + c]);
+  }
+  if (warp == 8) {
     tmem_alloc(&bars->tslot, 512);
     tmem_relinquish();
   }
@@ -180,20 +209,40 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
   const uint32_t tmem = bars->tslot;
 
   if (warp < 8) {
-    // ---------- LayerNorm + bias producers: two threads per pair row (64 channels each) ----------
+    // ---------- LayerNorm + bias producers (two threads per pair row); thread 0 also issues ----------
     // One pass reads the row half from the staged, 128-B-swizzled z tile into registers and
     // releases the tile (the next tile's load overlaps the rest); statistics and the four
     // triangle-bias dot products combine with one shuffle each. gamma, beta and the bias
-    // weights are warp-uniform loads served from L1.
+    // weights are read from shared memory, laid out so that the two row halves of a warp
+    // read adjacent 16-byte blocks (one wavefront per load). (As L1-served global loads they
+    // missed: the epilogue's 128 KB of stores per tile pass through a small L1, and the
+    // LayerNorm's operand phase took ~11,500 cycles per tile, clock64 trace.)
     const int p = warp * 16 + (lane >> 1), half = lane & 1;
-    const float* lnw = vec + tapack::kVLnW + half * 64;
-    const float* lnb = vec + tapack::kVLnB + half * 64;
-    const float* wbv = vec + tapack::kVWb + half * 64;
+    auto load_z = [&](int tile) {
+      const int jt = tile % n_jt, bi = tile / n_jt;
+      const int i = bi % rows, b = bi / rows;
+      mbar_arrive_expect_tx(&bars->z_full, 65536);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) tma_load_4d(smem + k3::kZ + q * 16384, &z_map, &bars->z_full, q * 32, jt * 128, i, b);
+    };
+    int loaded = 0;  // z tiles requested (thread 0)
+    if (tid == 0) {
+      mbar_arrive_expect_tx(&bars->wbar, 131072);
+#pragma unroll
+      for (int kh = 0; kh < 2; ++kh)
+#pragma unroll
+        for (int rb = 0; rb < 4; ++rb)
+          tma_load_2d(smem + k3::kW + kh * 65536 + rb * 16384, &w_map, &bars->wbar, kh * 64, rb * 128);
+      load_z(blockIdx.x);  // the grid never exceeds the tile count
+      loaded = 1;
+    }
+    bool ok = true;
     int it = 0;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
       const int jt = tile % n_jt, bi = tile / n_jt;
       const int i = bi % rows, b = bi / rows, j0 = jt * 128;
-      if (!__all_sync(0xffffffffu, mbar_wait(&bars->z_full, it & 1, guard, status, kStatusTimeoutProducer))) break;
+      ok = __all_sync(0xffffffffu, mbar_wait(&bars->z_full, it & 1, guard, status, kStatusTimeoutProducer));
+      if (!ok) break;
       const uint8_t* zt = smem + k3::kZ;
       float v[64];
 #pragma unroll
@@ -207,6 +256,19 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
           v[q * 32 + ch * 4 + 3] = t.w;
         }
       mbar_arrive(&bars->z_empty);  // the z tile may be refilled
+      if (warp == 0) {
+        // thread 0: refill z with the next tile once every producer has read this one
+        bool w = true;
+        if (lane == 0 && tile + static_cast<int>(gridDim.x) < n_tiles) {
+          w = mbar_wait(&bars->z_empty, it & 1, guard, status, kStatusTimeoutMma);
+          if (w) {
+            load_z(tile + gridDim.x);
+            ++loaded;
+          }
+        }
+        ok = __all_sync(0xffffffffu, w);
+        if (!ok) break;
+      }
       float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < 64; ++c) s4[c & 3] += v[c];
@@ -222,27 +284,30 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
       float ss = (q4[0] + q4[1]) + (q4[2] + q4[3]);
       ss += __shfl_xor_sync(0xffffffffu, ss, 1);
       const float rstd = rsqrtf(ss * (1.f / 128.f) + 1e-5f);
-      if (it >= 1 &&
-          !__all_sync(0xffffffffu, mbar_wait(&bars->a_empty, (it - 1) & 1, guard, status, kStatusTimeoutProducer)))
-        break;
+      ok = it < 1 || __all_sync(0xffffffffu, mbar_wait(&bars->a_empty, (it - 1) & 1, guard, status,
+                                                      kStatusTimeoutProducer));
+      if (!ok) break;
       float bacc[kHeads] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int ch = 0; ch < 8; ++ch) {
         const int c = ch * 8;
-        const float4 w0 = __ldg(reinterpret_cast<const float4*>(lnw + c));
-        const float4 w1 = __ldg(reinterpret_cast<const float4*>(lnw + c + 4));
-        const float4 b0 = __ldg(reinterpret_cast<const float4*>(lnb + c));
-        const float4 b1 = __ldg(reinterpret_cast<const float4*>(lnb + c + 4));
+        const float* lw = lnw_s + (ch * 2 + half) * 8;
+        const float* lb = lnb_s + (ch * 2 + half) * 8;
+        const float4 w0 = *reinterpret_cast<const float4*>(lw), w1 = *reinterpret_cast<const float4*>(lw + 4);
+        const float4 b0 = *reinterpret_cast<const float4*>(lb), b1 = *reinterpret_cast<const float4*>(lb + 4);
         const float y[8] = {(v[c + 0] - mean) * rstd * w0.x + b0.x, (v[c + 1] - mean) * rstd * w0.y + b0.y,
                             (v[c + 2] - mean) * rstd * w0.z + b0.z, (v[c + 3] - mean) * rstd * w0.w + b0.w,
                             (v[c + 4] - mean) * rstd * w1.x + b1.x, (v[c + 5] - mean) * rstd * w1.y + b1.y,
                             (v[c + 6] - mean) * rstd * w1.z + b1.z, (v[c + 7] - mean) * rstd * w1.w + b1.w};
 #pragma unroll
         for (int h = 0; h < kHeads; ++h) {
-          const float4 u0 = __ldg(reinterpret_cast<const float4*>(wbv + h * 128 + c));
-          const float4 u1 = __ldg(reinterpret_cast<const float4*>(wbv + h * 128 + c + 4));
-          bacc[h] += y[0] * u0.x + y[1] * u0.y + y[2] * u0.z + y[3] * u0.w + y[4] * u1.x + y[5] * u1.y +
-                     y[6] * u1.z + y[7] * u1.w;
+          const uint4 u = *reinterpret_cast<const uint4*>(wb_s + ((ch * kHeads + h) * 2 + half) * 8);
+          const float2 u0 = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+          const float2 u1 = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+          const float2 u2 = __half22float2(*reinterpret_cast<const __half2*>(&u.z));
+          const float2 u3 = __half22float2(*reinterpret_cast<const __half2*>(&u.w));
+          bacc[h] += y[0] * u0.x + y[1] * u0.y + y[2] * u1.x + y[3] * u1.y + y[4] * u2.x + y[5] * u2.y +
+                     y[6] * u3.x + y[7] * u3.y;
         }
         uint4 o;
         o.x = pack_f16x2(y[0], y[1]);
@@ -261,66 +326,45 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
       }
       fence_proxy_async_smem();
       mbar_arrive(&bars->a_full);
-    }
-  } else if (warp == 12) {
-    // ------------------------- TMA producer + MMA issuer -------------------------
-    if (lane == 0) {
-      auto load_z = [&](int tile) {
-        const int jt = tile % n_jt, bi = tile / n_jt;
-        const int i = bi % rows, b = bi / rows;
-        mbar_arrive_expect_tx(&bars->z_full, 65536);
+      if (warp == 0) {
+        // thread 0: the tile's MMAs, half h once the epilogue has drained half h of the
+        // previous tile
+        bool mw = true;
+        if (lane == 0) {
+          const uint32_t idesc = make_idesc_f16(128, 256, 0, 0);
+          const uint32_t w0 = smem_u32(smem + k3::kW), a0 = smem_u32(smem + k3::kA);
+          mw = mbar_wait(&bars->a_full, it & 1, guard, status, kStatusTimeoutMma);
+          if (mw && it == 0) mw = mbar_wait(&bars->wbar, 0, guard, status, kStatusTimeoutMma);
+          for (int h = 0; mw && h < 2; ++h) {
+            if (it >= 1) mw = mbar_wait(&bars->d_empty[h], (it - 1) & 1, guard, status, kStatusTimeoutMma);
+            if (!mw) break;
+            tc_fence_after();
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-          tma_load_4d(smem + k3::kZ + q * 16384, &z_map, &bars->z_full, q * 32, jt * 128, i, b);
-      };
-      mbar_arrive_expect_tx(&bars->wbar, 131072);
-#pragma unroll
-      for (int kh = 0; kh < 2; ++kh)
-#pragma unroll
-        for (int rb = 0; rb < 4; ++rb)
-          tma_load_2d(smem + k3::kW + kh * 65536 + rb * 16384, &w_map, &bars->wbar, kh * 64, rb * 128);
-      if (blockIdx.x < n_tiles) load_z(blockIdx.x);
-      bool ok = mbar_wait(&bars->wbar, 0, guard, status, kStatusTimeoutMma);
-      const uint32_t idesc = make_idesc_f16(128, 256, 0, 0);
-      const uint32_t w0 = smem_u32(smem + k3::kW), a0 = smem_u32(smem + k3::kA);
-      int it = 0, loaded = blockIdx.x < n_tiles ? 1 : 0;
-      for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++it) {
-        // refill z for the next tile as soon as the LayerNorm producers released it
-        const int next = tile + gridDim.x;
-        if (next < n_tiles) {
-          ok = mbar_wait(&bars->z_empty, it & 1, guard, status, kStatusTimeoutMma);
-          if (!ok) break;
-          load_z(next);
-          ++loaded;
-        }
-        ok = mbar_wait(&bars->a_full, it & 1, guard, status, kStatusTimeoutMma);
-        for (int h = 0; ok && h < 2; ++h) {
-          if (it >= 1) ok = mbar_wait(&bars->d_empty[h], (it - 1) & 1, guard, status, kStatusTimeoutMma);
-          if (!ok) break;
-          tc_fence_after();
-#pragma unroll
-          for (int ks = 0; ks < 8; ++ks) {
-            const int kh = ks >> 2, kin = ks & 3;
-            umma_ss(tmem + h * 256, make_sdesc(a0 + kh * 16384 + kin * 32, 16, 1024, Swz::k128),
-                    make_sdesc(w0 + kh * 65536 + h * 32768 + kin * 32, 16, 1024, Swz::k128), idesc, ks > 0 ? 1u : 0u);
+            for (int ks = 0; ks < 8; ++ks) {
+              const int kh = ks >> 2, kin = ks & 3;
+              umma_ss(tmem + h * 256, make_sdesc(a0 + kh * 16384 + kin * 32, 16, 1024, Swz::k128),
+                      make_sdesc(w0 + kh * 65536 + h * 32768 + kin * 32, 16, 1024, Swz::k128), idesc, ks > 0 ? 1u : 0u);
+            }
+            umma_commit(&bars->d_full[h]);
           }
-          umma_commit(&bars->d_full[h]);
+          if (mw) umma_commit(&bars->a_empty);
         }
-        if (ok) umma_commit(&bars->a_empty);
+        ok = __all_sync(0xffffffffu, mw);
+        if (!ok) break;
       }
-      if (!ok) {
-        umma_commit(&bars->drain);
-        mbar_wait_drain(&bars->drain, 0);
-        if (loaded > 0) mbar_wait_drain(&bars->z_full, (loaded - 1) & 1);
-        mbar_wait_drain(&bars->wbar, 0);
-      }
+    }
+    if (!ok && tid == 0) {
+      // abort: wait (bounded) for this thread's MMAs and TMA loads still in flight
+      umma_commit(&bars->drain);
+      mbar_wait_drain(&bars->drain, 0);
+      if (loaded > 0) mbar_wait_drain(&bars->z_full, (loaded - 1) & 1);
+      mbar_wait_drain(&bars->wbar, 0);
     }
   } else {
-    // ------------------ epilogue: thread = pair; TMEM half 0 (q, k), then 1 (v, gate) ------------------
-    const int q4 = warp & 3;
+    // ---------- epilogue: thread = pair; heads 2*hh, 2*hh+1 of TMEM half 0 (q, k), then 1 (v, gate) ----------
+    const int q4 = warp & 3, hh = (warp - 8) >> 2;
     const int p = q4 * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
-    const float* bg = vec + tapack::kVBg;
     int it = 0;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
       const int jt = tile % n_jt, bi = tile / n_jt;
@@ -332,35 +376,47 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
         ok = __all_sync(0xffffffffu, mbar_wait(&bars->d_full[h], it & 1, guard, status, kStatusTimeoutConsumer));
         if (!ok) break;
         tc_fence_after();
-#pragma unroll 1
-        for (int cc = 0; cc < 4; ++cc) {
-          uint32_t x0[32], x1[32];
-          tmem_ld32(tmem + lane_off + h * 256 + cc * 32, x0);
-          tmem_ld32(tmem + lane_off + h * 256 + 128 + cc * 32, x1);
-          tmem_wait_ld();
-          if (!valid) continue;
-          // first 128 columns of the half: q (h = 0) or v (h = 1), head cc: 64 contiguous bytes
-          // each destination row is 64 contiguous bytes, 64-byte aligned: two 32-byte stores
-          __half* dst0 = (h == 0 ? q_out : v_out) + ((static_cast<size_t>(bi) * kHeads + cc) * N + j) * kHeadDim;
-          uint32_t w0[16];
+        // chunk k (0-3): head cc = 2*hh + k/2, columns 16*(k%2) .. +15 of that head; the
+        // first 128 columns of the half are q (h = 0) or v (h = 1), the next 128 k or the gate
+        const uint32_t tb = tmem + lane_off + h * 256 + hh * 64;
+        uint32_t x0[2][16], x1[2][16];
+        tmem_ld16(tb, x0[0]);
+        tmem_ld16(tb + 128, x1[0]);
 #pragma unroll
-          for (int e = 0; e < 16; ++e) w0[e] = pack_f16x2(__uint_as_float(x0[2 * e]), __uint_as_float(x0[2 * e + 1]));
+        for (int k = 0; k < 4; ++k) {
+          const int cur = k & 1;
+          tmem_wait_ld_regs(x0[cur], x1[cur]);
+          if (k + 1 < 4) {
+            tmem_ld16(tb + (k + 1) * 16, x0[cur ^ 1]);
+            tmem_ld16(tb + 128 + (k + 1) * 16, x1[cur ^ 1]);
+          }
+          if (!valid) continue;
+          const int cc = 2 * hh + (k >> 1), c16 = (k & 1) * 16;
+          uint32_t w0[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) w0[e] = pack_f16x2(__uint_as_float(x0[cur][2 * e]), __uint_as_float(x0[cur][2 * e + 1]));
+          __half* dst0 = (h == 0 ? q_out : v_out) + ((static_cast<size_t>(bi) * kHeads + cc) * N + j) * kHeadDim + c16;
           stg_v8(dst0, w0[0], w0[1], w0[2], w0[3], w0[4], w0[5], w0[6], w0[7]);
-          stg_v8(dst0 + 16, w0[8], w0[9], w0[10], w0[11], w0[12], w0[13], w0[14], w0[15]);
-          __half* dst1 = h == 0 ? k_out + ((static_cast<size_t>(bi) * kHeads + cc) * N + j) * kHeadDim
-                                : g_out + (static_cast<size_t>(bi) * N + j) * 128 + cc * 32;
-          uint32_t w1[16];
+          uint32_t w1[8];
           if (h == 0) {
 #pragma unroll
-            for (int e = 0; e < 16; ++e) w1[e] = pack_f16x2(__uint_as_float(x1[2 * e]), __uint_as_float(x1[2 * e + 1]));
+            for (int e = 0; e < 8; ++e) w1[e] = pack_f16x2(__uint_as_float(x1[cur][2 * e]), __uint_as_float(x1[cur][2 * e + 1]));
           } else {
+            const float* bgc = bg_s + cc * 32 + c16;
 #pragma unroll
-            for (int e = 0; e < 16; ++e)
-              w1[e] = pack_f16x2(sigmoid_tanh(__uint_as_float(x1[2 * e]) + bg[cc * 32 + 2 * e]),
-                                 sigmoid_tanh(__uint_as_float(x1[2 * e + 1]) + bg[cc * 32 + 2 * e + 1]));
+            for (int e4 = 0; e4 < 4; ++e4) {
+              const float4 g4 = *reinterpret_cast<const float4*>(bgc + e4 * 4);
+              const float t0 = tanh_approx(__uint_as_float(x1[cur][e4 * 4 + 0]) + g4.x);
+              const float t1 = tanh_approx(__uint_as_float(x1[cur][e4 * 4 + 1]) + g4.y);
+              const float t2 = tanh_approx(__uint_as_float(x1[cur][e4 * 4 + 2]) + g4.z);
+              const float t3 = tanh_approx(__uint_as_float(x1[cur][e4 * 4 + 3]) + g4.w);
+              w1[2 * e4] = pack_f16x2(fmaf(0.5f, t0, 0.5f), fmaf(0.5f, t1, 0.5f));
+              w1[2 * e4 + 1] = pack_f16x2(fmaf(0.5f, t2, 0.5f), fmaf(0.5f, t3, 0.5f));
+            }
           }
+          __half* dst1 = h == 0 ? k_out + ((static_cast<size_t>(bi) * kHeads + cc) * N + j) * kHeadDim + c16
+                                : g_out + (static_cast<size_t>(bi) * N + j) * 128 + cc * 32 + c16;
           stg_v8(dst1, w1[0], w1[1], w1[2], w1[3], w1[4], w1[5], w1[6], w1[7]);
-          stg_v8(dst1 + 16, w1[8], w1[9], w1[10], w1[11], w1[12], w1[13], w1[14], w1[15]);
         }
         tc_fence_before();
         mbar_arrive(&bars->d_empty[h]);
@@ -370,7 +426,7 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 12) {
+  if (warp == 8) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
