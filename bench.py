@@ -13,7 +13,10 @@ recorded between the kernels (captured into the graph) give each kernel's device
 * ``value``: layers*N^2/s over all ranks with inputs resident in HBM (device timing, CUDA
   events, max over ranks).
 * ``e2e``: the same metric through the public API with host buffers: every step copies z
-  from pinned host memory, runs the stack and copies the full result back.
+  from pinned host memory, runs the stack and copies the full result back. On one GPU the
+  copies run on their own streams, so the input copy of step s+1 and the result copy of
+  step s overlap the compute of step s (two device buffer pairs); the one-stream serial
+  figure is reported alongside (``e2e.serial``).
 * ``roofline``: the dominant kernel against MEASURED_PEAKS.json.
 * ``cpu_baseline``: the reference math (the fp32 PyTorch oracle) on this host's cores, on
   a row sample of one N=1024 layer (rank 0 at N=1 only).
@@ -209,6 +212,117 @@ def run_reference(args, rank):
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+
+def run_e2e(args, stack, mask, z_host, z_ref, device, world, B, L, N):
+    """End-to-end steps through the public API (``TrianglePairStack.forward_into``) with host
+    buffers. Every step copies its input z from pinned host memory to the device and its
+    result back to pinned host memory, inside the timed region.
+
+    Pipelined (the figure reported): two device input/output buffer pairs, one CUDA graph per
+    pair; the host->device copy of step s+1 and the device->host copy of step s run on their
+    own streams while step s computes (PCIe is full duplex), ordered by events so that no
+    copy touches a buffer a step is still using. Serial (reported alongside): copy in, run,
+    copy out on one stream, one step at a time."""
+    cur = torch.cuda.current_stream(device)
+    zin = [torch.empty_like(z_ref), torch.empty_like(z_ref)]
+    zout = [torch.empty_like(z_ref), torch.empty_like(z_ref)]
+    out_host = [torch.empty_like(z_host).pin_memory(), torch.empty_like(z_host).pin_memory()]
+    graphs = []
+    for b in range(2):
+        zin[b].copy_(z_host)
+        stack.forward_into(zin[b], zout[b], mask)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        cs = torch.cuda.Stream(device=device)
+        cs.wait_stream(cur)
+        with torch.cuda.stream(cs):
+            with torch.cuda.graph(g, stream=cs):
+                stack.forward_into(zin[b], zout[b], mask)
+        cur.wait_stream(cs)
+        graphs.append(g)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    def timed(fn):
+        barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(cur)
+        fn()
+        e1.record(cur)
+        torch.cuda.synchronize()
+        barrier()
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device=device)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms / args.steps
+
+    def serial():
+        for _ in range(args.steps):
+            zin[0].copy_(z_host, non_blocking=True)
+            graphs[0].replay()
+            out_host[0].copy_(zout[0], non_blocking=True)
+
+    h2d = torch.cuda.Stream(device=device)
+    d2h = torch.cuda.Stream(device=device)
+
+    def pipelined():
+        K = args.steps
+        in_ready = [torch.cuda.Event(), torch.cuda.Event()]
+        step_done = [torch.cuda.Event(), torch.cuda.Event()]
+        out_read = [torch.cuda.Event(), torch.cuda.Event()]
+        h2d.wait_stream(cur)
+        d2h.wait_stream(cur)
+        with torch.cuda.stream(h2d):
+            zin[0].copy_(z_host, non_blocking=True)
+            in_ready[0].record(h2d)
+        for s in range(K):
+            b = s & 1
+            if s + 1 < K:
+                nb = b ^ 1
+                with torch.cuda.stream(h2d):
+                    if s >= 1:
+                        h2d.wait_event(step_done[nb])  # step s-1 has finished reading zin[nb]
+                    zin[nb].copy_(z_host, non_blocking=True)
+                    in_ready[nb].record(h2d)
+            cur.wait_event(in_ready[b])
+            if s >= 2:
+                cur.wait_event(out_read[b])  # step s-2's result has left zout[b]
+            graphs[b].replay()
+            step_done[b].record(cur)
+            with torch.cuda.stream(d2h):
+                d2h.wait_event(step_done[b])
+                out_host[b].copy_(zout[b], non_blocking=True)
+                out_read[b].record(d2h)
+        cur.wait_stream(d2h)
+        cur.wait_stream(h2d)
+
+    serial()  # warm-up
+    ms_serial = timed(serial)
+    h2d_bytes = z_host.numel() * 4
+    serial_line = {"value": world * B * L * N * N / (ms_serial / 1e3), "ms_per_step": ms_serial}
+    try:
+        pipelined()  # warm-up of both graphs and streams
+        ms = timed(pipelined)
+        # the last step's result must equal the resident-input run's result
+        last = out_host[(args.steps - 1) & 1]
+        if not torch.equal(last[:, : min(N, 64)], z_ref[:, : min(N, 64)].cpu()):
+            raise RuntimeError("pipelined result differs from the device-resident run")
+    except RuntimeError as exc:  # report the serial figure rather than none
+        return {"value": serial_line["value"], "unit": UNIT, "h2d_bytes_per_step": h2d_bytes,
+                "d2h_bytes_per_step": h2d_bytes, "ms_per_step": ms_serial, "mode": "serial",
+                "pipelined_error": str(exc)[:200]}
+    return {"value": world * B * L * N * N / (ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d_bytes,
+            "d2h_bytes_per_step": h2d_bytes, "ms_per_step": ms,
+            "mode": "pipelined: H2D of step s+1 and D2H of step s on their own streams, overlapping step s",
+            "serial": serial_line}
+
 def run_ours(args, rank, world, device):
     import genie_tk
     from genie_tk import ops, stack as stack_mod
@@ -301,32 +415,7 @@ def run_ours(args, rank, world, device):
     # end to end through the public API with host buffers
     e2e = None
     if not args.no_e2e:
-        out_host = torch.empty_like(z_host).pin_memory()
-        cur = torch.cuda.current_stream(device)
-        for _ in range(1):
-            z0.copy_(z_host, non_blocking=True)
-            graph.replay()
-            out_host.copy_(z, non_blocking=True)
-        torch.cuda.synchronize()
-        barrier()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(cur)
-        for _ in range(args.steps):
-            z0.copy_(z_host, non_blocking=True)
-            graph.replay()
-            out_host.copy_(z, non_blocking=True)
-        e1.record(cur)
-        torch.cuda.synchronize()
-        barrier()
-        e_ms = e0.elapsed_time(e1)
-        if world > 1:
-            t = torch.tensor([e_ms], device=device)
-            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-            e_ms = float(t.item())
-        e2e = {"value": world * B * L * N * N / (e_ms / args.steps / 1e3), "unit": UNIT,
-               "h2d_bytes_per_step": z_host.numel() * 4, "d2h_bytes_per_step": out_host.numel() * 4,
-               "ms_per_step": e_ms / args.steps}
+        e2e = run_e2e(args, stack, mask, z_host, z, device, world, B, L, N)
 
     peaks = load_peaks()
     kernels = {}

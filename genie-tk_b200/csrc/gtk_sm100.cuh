@@ -140,10 +140,6 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 // TMA (cp.async.bulk.tensor). Tensor maps are __grid_constant__ kernel parameters.
 // Every load and store here moves data between global memory and the issuing CTA alone.
 // ----------------------------------------------------------------------------------
-__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
-  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
-}
-
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
@@ -168,20 +164,6 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
       "%6}], [%2];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
-}
-
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
-  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(smem_u32(src)), "r"(c0), "r"(c1)
-               : "memory");
-}
-
-__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int c0, int c1, int c2) {
-  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
-               : "memory");
 }
 
 __device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int c0, int c1, int c2,
@@ -352,8 +334,6 @@ __host__ __device__ constexpr uint32_t make_idesc_bf16(uint32_t M, uint32_t N, u
 // ----------------------------------------------------------------------------------
 // Small numeric helpers
 // ----------------------------------------------------------------------------------
-__device__ __forceinline__ float sigmoidf_fast(float x) { return 1.0f / (1.0f + __expf(-x)); }
-
 // Hardware tanh (one MUFU op); sigmoid(x) = 0.5 * tanh(x / 2) + 0.5.
 __device__ __forceinline__ float tanh_approx(float x) {
   float y;
@@ -361,18 +341,6 @@ __device__ __forceinline__ float tanh_approx(float x) {
   return y;
 }
 __device__ __forceinline__ float sigmoid_tanh(float x) { return fmaf(0.5f, tanh_approx(0.5f * x), 0.5f); }
-
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
-
-
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&v);
-}
 
 // fp16 pair with saturation to the finite range (values beyond +-65504 clamp).
 __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
@@ -393,14 +361,6 @@ __device__ __forceinline__ uint32_t swz128(uint32_t row, uint32_t chunk) {
   return row * 128u + ((chunk ^ (row & 7u)) << 4);
 }
 
-// Same for 64-byte rows (TMA SWIZZLE_64B; tile base 512-B aligned); chunk in 0..3.
-__device__ __forceinline__ uint32_t swz64(uint32_t row, uint32_t chunk) {
-  return row * 64u + ((chunk ^ ((row >> 1) & 3u)) << 4);
-}
-
-__device__ __forceinline__ int warp_id() { return threadIdx.x >> 5; }
-__device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
-
 // ----------------------------------------------------------------------------------
 // Shared-memory helpers used by several kernels
 // ----------------------------------------------------------------------------------
@@ -418,53 +378,5 @@ __device__ __forceinline__ void stg_v8(void* p, uint32_t a0, uint32_t a1, uint32
                : "memory");
 }
 __device__ __forceinline__ void sts_u4(uint8_t* p, uint4 v) { *reinterpret_cast<uint4*>(p) = v; }
-
-// LayerNorm of one 128-channel fp32 row held in a 128-B-swizzled [128 rows][32 fp32] x4
-// tile; writes the fp16 result as a K-major SW128 A operand ([128 rows][64] x2). LayerNorm
-// output is bounded by |gamma| * sqrt(128) + |beta|, well inside the fp16 range.
-__device__ __forceinline__ void ln_row_to_operand(const uint8_t* ztile, uint8_t* atile, int p, const float* lnw,
-                                                  const float* lnb, float* mean_out = nullptr,
-                                                  float* rstd_out = nullptr) {
-  float s = 0.f;
-#pragma unroll
-  for (int q = 0; q < 4; ++q)
-#pragma unroll
-    for (int ch = 0; ch < 8; ++ch) {
-      const float4 v = lds_f4(ztile + q * 16384 + swz128(p, ch));
-      s += (v.x + v.y) + (v.z + v.w);
-    }
-  const float mean = s * (1.f / 128.f);
-  float ss = 0.f;
-#pragma unroll
-  for (int q = 0; q < 4; ++q)
-#pragma unroll
-    for (int ch = 0; ch < 8; ++ch) {
-      const float4 v = lds_f4(ztile + q * 16384 + swz128(p, ch));
-      const float a = v.x - mean, b = v.y - mean, c = v.z - mean, d = v.w - mean;
-      ss += (a * a + b * b) + (c * c + d * d);
-    }
-  const float rstd = rsqrtf(ss * (1.f / 128.f) + 1e-5f);
-  if (mean_out) *mean_out = mean;
-  if (rstd_out) *rstd_out = rstd;
-#pragma unroll
-  for (int kh = 0; kh < 2; ++kh)
-#pragma unroll
-    for (int ch = 0; ch < 8; ++ch) {
-      const int c = kh * 64 + ch * 8;
-      const int q = c >> 5, zc = (c & 31) >> 2;
-      const float4 v0 = lds_f4(ztile + q * 16384 + swz128(p, zc));
-      const float4 v1 = lds_f4(ztile + q * 16384 + swz128(p, zc + 1));
-      const float4 w0 = *reinterpret_cast<const float4*>(lnw + c);
-      const float4 w1 = *reinterpret_cast<const float4*>(lnw + c + 4);
-      const float4 b0 = *reinterpret_cast<const float4*>(lnb + c);
-      const float4 b1 = *reinterpret_cast<const float4*>(lnb + c + 4);
-      uint4 o;
-      o.x = pack_f16x2((v0.x - mean) * rstd * w0.x + b0.x, (v0.y - mean) * rstd * w0.y + b0.y);
-      o.y = pack_f16x2((v0.z - mean) * rstd * w0.z + b0.z, (v0.w - mean) * rstd * w0.w + b0.w);
-      o.z = pack_f16x2((v1.x - mean) * rstd * w1.x + b1.x, (v1.y - mean) * rstd * w1.y + b1.y);
-      o.w = pack_f16x2((v1.z - mean) * rstd * w1.z + b1.z, (v1.w - mean) * rstd * w1.w + b1.w);
-      sts_u4(atile + kh * 16384 + swz128(p, ch), o);
-    }
-}
 
 }  // namespace gtk
