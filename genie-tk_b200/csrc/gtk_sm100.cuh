@@ -340,7 +340,6 @@ __device__ __forceinline__ float tanh_approx(float x) {
   asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-__device__ __forceinline__ float sigmoid_tanh(float x) { return fmaf(0.5f, tanh_approx(0.5f * x), 0.5f); }
 
 // fp16 pair with saturation to the finite range (values beyond +-65504 clamp).
 __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {

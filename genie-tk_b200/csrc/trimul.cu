@@ -36,9 +36,9 @@ namespace gtk {
 //   W1  fp16 [512][128]: rows 0-127 linear_a_p, 128-255 linear_a_g / 2, 256-383 linear_b_p,
 //                        384-511 linear_b_g / 2, each times gamma_in (nn.Linear [out, in] =
 //                        K-major B operand; the gates' 1/2 feeds sigmoid(x) = (1 + tanh(x/2))/2)
-//   W2  fp16 [256][128]: rows 0-127 linear_g * gamma_in, 128-255 linear_z * gamma_out
+//   W2  fp16 [256][128]: rows 0-127 linear_g * gamma_in / 2, 128-255 linear_z * gamma_out
 //   vec fp32: b1[512] = the four projection biases + W beta_in (gate entries halved too),
-//             b_g[128] = b_g + W_g beta_in,
+//             b_g[128] = (b_g + W_g beta_in) / 2,
 //             u[128] = sum_c W2[128+n][c] (fp16-rounded), v[128] = linear_z(beta_out) + b_z.
 // Both LayerNorm affines are folded into the weights: LN(x) W^T + b = xhat (W*gamma)^T +
 // (W beta + b) with xhat = (x - mu) * rstd, so the kernels' LayerNorm producers write xhat
@@ -66,7 +66,8 @@ __global__ void trimul_pack_kernel(gtk_trimul_params p, uint8_t* packed) {
   }
   for (int e = tid; e < 256 * 128; e += nthreads) {
     const int r = e >> 7, c = e & 127;
-    const float val = r < 128 ? p.g_w[r * 128 + c] * p.ln_in_w[c] : p.z_w[(r - 128) * 128 + c] * p.ln_out_w[c];
+    const float val =
+        r < 128 ? 0.5f * p.g_w[r * 128 + c] * p.ln_in_w[c] : p.z_w[(r - 128) * 128 + c] * p.ln_out_w[c];
     w2[e] = f16_sat(val);
   }
   for (int e = tid; e < 512; e += nthreads) {
@@ -80,7 +81,7 @@ __global__ void trimul_pack_kernel(gtk_trimul_params p, uint8_t* packed) {
   for (int e = tid; e < 128; e += nthreads) {
     float bg = p.g_b[e];
     for (int c = 0; c < 128; ++c) bg += p.g_w[e * 128 + c] * p.ln_in_b[c];
-    vec[tmpack::kVBg + e] = bg;
+    vec[tmpack::kVBg + e] = 0.5f * bg;
     float u = 0.f, v = p.z_b[e];
     for (int c = 0; c < 128; ++c) {
       u += __half2float(f16_sat(p.z_w[e * 128 + c] * p.ln_out_w[c]));
@@ -646,7 +647,8 @@ __global__ void __launch_bounds__(k2::kThreads, 1)
 //   warp 13     lane 0: TMA for the weights (once), the z tile and the x tile;
 //   warp 14     lane 0: TMA for the residual slabs.
 // TMEM (double buffered per tile, 256 columns each): G = A W_g^T at +0, U = x^T (W_z gamma)^T
-// at +128. LN_out folds into the epilogue: out = g * (rstd (U - mu u) + v).
+// at +128. LN_out folds into the epilogue: out = g * (rstd (U - mu u) + v), with the gate
+// g = (1 + tanh(G + b_g')) / 2 (W_g's rows and b_g' carry the 1/2 of sigmoid(x) = (1 + tanh(x/2)) / 2).
 // Shared memory: W2 64 KB | z tile / A 64 KB | x 32 KB | slabs 4 x 16 KB | b_g,u,v | barriers.
 // The z tile is reloaded once the gate GEMM has read A from the same buffer.
 // (A warp-per-pair LayerNorm read from global memory and per-thread residual loads, each
@@ -923,13 +925,20 @@ __global__ void __launch_bounds__(k2e::kThreads, 1)
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
           float o[4];
+          const int n0 = cc * 32 + q * 4;
           const float4 zv = add_residual ? lds_f4(ob + swz128(p, q)) : make_float4(0.f, 0.f, 0.f, 0.f);
+          const float4 bg4 = *reinterpret_cast<const float4*>(svec + n0);
+          const float4 u4 = *reinterpret_cast<const float4*>(svec + 128 + n0);
+          const float4 v4 = *reinterpret_cast<const float4*>(svec + 256 + n0);
           const float rq[4] = {zv.x, zv.y, zv.z, zv.w};
+          const float bgv[4] = {bg4.x, bg4.y, bg4.z, bg4.w}, uv[4] = {u4.x, u4.y, u4.z, u4.w},
+                      vv[4] = {v4.x, v4.y, v4.z, v4.w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const int t = q * 4 + e, n = cc * 32 + t;
-            const float gate = sigmoid_tanh(__uint_as_float(g[t]) + svec[n]);
-            o[e] = (rstd_x * (__uint_as_float(u[t]) - mu_x * svec[128 + n]) + svec[256 + n]) * gate + rq[e];
+            const int t = q * 4 + e;
+            const float gate = fmaf(0.5f, tanh_approx(__uint_as_float(g[t]) + bgv[e]), 0.5f);
+            const float y = fmaf(rstd_x, fmaf(-mu_x, uv[e], __uint_as_float(u[t])), vv[e]);
+            o[e] = fmaf(y, gate, rq[e]);
           }
           *reinterpret_cast<float4*>(ob + swz128(p, q)) = make_float4(o[0], o[1], o[2], o[3]);
         }
