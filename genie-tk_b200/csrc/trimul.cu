@@ -645,7 +645,8 @@ __global__ void __launch_bounds__(k2::kThreads, 1)
 //               every global access is a bulk tensor copy;
 //   warp 12     lane 0: MMA issuer;
 //   warp 13     lane 0: TMA for the weights (once), the z tile and the x tile;
-//   warp 14     lane 0: TMA for the residual slabs.
+//   warp 14     lane 0: slab manager -- TMA loads of the residual slabs and TMA stores of
+//               the finished ones (a slab buffer is reloaded once its store has read it).
 // TMEM (double buffered per tile, 256 columns each): G = A W_g^T at +0, U = x^T (W_z gamma)^T
 // at +128. LN_out folds into the epilogue: out = g * (rstd (U - mu u) + v), with the gate
 // g = (1 + tanh(G + b_g')) / 2 (W_g's rows and b_g' carry the 1/2 of sigmoid(x) = (1 + tanh(x/2)) / 2).
@@ -669,7 +670,7 @@ struct K2eBars {
   uint64_t a_full, a_empty;  // 256 LayerNorm threads / MMA commit (the z tile may be reloaded)
   uint64_t x_full, x_empty;  // TMA / MMA commit + 128 epilogue threads (statistics)
   uint64_t d_full[2], d_empty[2];
-  uint64_t o_full[k2e::kSlabs], o_empty[k2e::kSlabs];
+  uint64_t o_full[k2e::kSlabs];      // residual slab landed (TMA) / buffer handed to the epilogue
   uint64_t slab_ready[k2e::kSlabs];  // 128 epilogue threads wrote the slab
   uint64_t drain;
   uint32_t tslot;
@@ -705,7 +706,6 @@ __global__ void __launch_bounds__(k2e::kThreads, 1)
     }
     for (int x = 0; x < kSlabs; ++x) {
       mbar_init(&bars->o_full[x], 1);
-      mbar_init(&bars->o_empty[x], 1);
       mbar_init(&bars->slab_ready[x], 128);
     }
     mbar_init(&bars->drain, 1);
@@ -824,14 +824,26 @@ __global__ void __launch_bounds__(k2e::kThreads, 1)
       for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
         const int jt = tile % n_jt, rb = tile / n_jt;
         const int r = rb % rows, b = rb / rows, j0 = jt * 128;
-        if (it >= 1 && !mbar_wait(&bars->a_empty, (it - 1) & 1, guard, status, kStatusTimeoutProducer)) {
+        // Channels 64-127 (boxes 2, 3) as soon as every LayerNorm thread has read the previous
+        // tile (A never covers them); channels 0-63 once the gate GEMM has read A, which
+        // overwrites them. Only the second half of the load sits between that GEMM and the
+        // next LayerNorm.
+        if (it >= 1 && !mbar_wait(&bars->z_read, (it - 1) & 1, guard, status, kStatusTimeoutProducer)) {
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&bars->z_full, 65536);
+        mbar_expect_tx(&bars->z_full, 32768);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) tma_load_4d(smem + kZ + q * 16384, &z_map, &bars->z_full, q * 32, j0, r, b);
+        for (int q = 2; q < 4; ++q) tma_load_4d(smem + kZ + q * 16384, &z_map, &bars->z_full, q * 32, j0, r, b);
         ++zl;
+        if (it >= 1 && !mbar_wait(&bars->a_empty, (it - 1) & 1, guard, status, kStatusTimeoutProducer)) {
+          mbar_arrive(&bars->z_full);  // complete the phase on the half in flight, so the drain below can wait for it
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&bars->z_full, 32768);
+#pragma unroll
+        for (int q = 0; q < 2; ++q) tma_load_4d(smem + kZ + q * 16384, &z_map, &bars->z_full, q * 32, j0, r, b);
         if (it >= 1 && !mbar_wait(&bars->x_empty, (it - 1) & 1, guard, status, kStatusTimeoutProducer)) {
           ok = false;
           break;
@@ -850,30 +862,56 @@ __global__ void __launch_bounds__(k2e::kThreads, 1)
       mbar_wait_drain(&bars->wbar, 0);
     }
   } else if (warp == 14) {
-    // ------------------------ TMA producer: residual slabs ------------------------
+    // ---------------- slab manager: residual loads and output stores ----------------
+    // Slab sn (four per tile, 32 channels each) lives in buffer sn % 4. Its output store is
+    // issued once the 128 epilogue threads have written it; once that store has read the
+    // buffer, the residual of slab sn + 4 (the next tile's slab of the same channels) is
+    // loaded into it. Issuing here keeps the store and its wait off the epilogue warps.
     if (lane == 0) {
       bool ok = true;
-      int slab = 0;
-      for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
+      const int n_mine = (n_tiles - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
+                         static_cast<int>(gridDim.x);
+      const int total = 4 * n_mine;
+      auto coords = [&](int sn, int& cc, int& j0, int& r, int& b) {
+        const int tile = blockIdx.x + (sn >> 2) * gridDim.x;
         const int jt = tile % n_jt, rb = tile / n_jt;
-        const int r = rb % rows, b = rb / rows, j0 = jt * 128;
-        for (int cc = 0; cc < 4; ++cc, ++slab) {
-          const int sl = slab % kSlabs;
-          if (slab >= kSlabs && !mbar_wait(&bars->o_empty[sl], ((slab / kSlabs) - 1) & 1, guard, status,
-                                           kStatusTimeoutProducer)) {
-            ok = false;
-            break;
-          }
-          if (add_residual) {
-            mbar_arrive_expect_tx(&bars->o_full[sl], 16384);
-            tma_load_4d(smem + kO + sl * 16384, &z_map, &bars->o_full[sl], cc * 32, j0, r, b);
-          } else {
-            mbar_arrive(&bars->o_full[sl]);
-          }
+        cc = sn & 3;
+        j0 = jt * 128;
+        r = rb % rows;
+        b = rb / rows;
+      };
+      auto load = [&](int sn) {
+        const int sl = sn % kSlabs;
+        if (add_residual) {
+          int cc, j0, r, b;
+          coords(sn, cc, j0, r, b);
+          mbar_arrive_expect_tx(&bars->o_full[sl], 16384);
+          tma_load_4d(smem + kO + sl * 16384, &z_map, &bars->o_full[sl], cc * 32, j0, r, b);
+        } else {
+          mbar_arrive(&bars->o_full[sl]);
+        }
+      };
+      int loaded = 0;
+      for (; loaded < kSlabs && loaded < total; ++loaded) load(loaded);
+      for (int sn = 0; sn < total; ++sn) {
+        const int sl = sn % kSlabs;
+        if (!mbar_wait(&bars->slab_ready[sl], (sn / kSlabs) & 1, guard, status, kStatusTimeoutProducer)) {
+          ok = false;
+          break;
+        }
+        int cc, j0, r, b;
+        coords(sn, cc, j0, r, b);
+        tma_store_4d(&out_map, smem + kO + sl * 16384, cc * 32, j0, r, b);
+        tma_store_commit();
+        if (sn + kSlabs < total) {
+          tma_store_wait_read();  // the store has read the buffer
+          load(sn + kSlabs);
+          ++loaded;
         }
       }
-      if (!ok)
-        for (int t = (slab > kSlabs ? slab - kSlabs : 0); t < slab; ++t)
+      tma_store_wait_all();
+      if (!ok)  // let the residual loads still in flight land before shared memory is released
+        for (int t = (loaded > kSlabs ? loaded - kSlabs : 0); t < loaded; ++t)
           mbar_wait_drain(&bars->o_full[t % kSlabs], (t / kSlabs) & 1);
     }
   } else {
@@ -881,13 +919,10 @@ __global__ void __launch_bounds__(k2e::kThreads, 1)
     const int q4 = warp & 3;
     const int p = q4 * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
-    const bool issuer = (warp == 8 && lane == 0);
     int it = 0, slab = 0;
     bool ok = true;
     for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++it) {
       const int s = it & 1;
-      const int jt = tile % n_jt, rb = tile / n_jt;
-      const int r = rb % rows, b = rb / rows, j0 = jt * 128;
       bool w = mbar_wait(&bars->x_full, it & 1, guard, status, kStatusTimeoutConsumer);
       w = w && mbar_wait(&bars->d_full[s], (it >> 1) & 1, guard, status, kStatusTimeoutConsumer);
       ok = __all_sync(0xffffffffu, w);
@@ -896,16 +931,17 @@ __global__ void __launch_bounds__(k2e::kThreads, 1)
       const uint8_t* xb = smem + kX + (p >> 6) * 16384;
       const int pj = p & 63;
       const float x0 = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(xb + swz128(0, pj >> 3) + (pj & 7) * 2)));
-      float s1 = 0.f, s2 = 0.f;
+      float a1[4] = {0.f, 0.f, 0.f, 0.f}, a2[4] = {0.f, 0.f, 0.f, 0.f};  // four chains each
 #pragma unroll 16
       for (int c = 0; c < 128; ++c) {
         const float xv = __half2float(
                              __ushort_as_half(*reinterpret_cast<const uint16_t*>(xb + swz128(c, pj >> 3) + (pj & 7) * 2))) -
                          x0;
-        s1 += xv;
-        s2 += xv * xv;
+        a1[c & 3] += xv;
+        a2[c & 3] = fmaf(xv, xv, a2[c & 3]);
       }
       mbar_arrive(&bars->x_empty);
+      const float s1 = (a1[0] + a1[1]) + (a1[2] + a1[3]), s2 = (a2[0] + a2[1]) + (a2[2] + a2[3]);
       const float d1 = s1 * (1.f / 128.f);
       const float mu_x = x0 + d1;
       const float var = fmaxf(s2 * (1.f / 128.f) - d1 * d1, 0.f);
@@ -943,32 +979,11 @@ __global__ void __launch_bounds__(k2e::kThreads, 1)
           *reinterpret_cast<float4*>(ob + swz128(p, q)) = make_float4(o[0], o[1], o[2], o[3]);
         }
         fence_proxy_async_smem();
-        mbar_arrive(&bars->slab_ready[sl]);
-        if (warp == 8) {
-          // one thread stores the slab once all 128 have written it (a bounded wait, so
-          // that an abort elsewhere cannot leave threads parked at a barrier)
-          bool iok = true;
-          if (issuer) {
-            iok = mbar_wait(&bars->slab_ready[sl], (slab / kSlabs) & 1, guard, status, kStatusTimeoutConsumer);
-            if (iok) {
-              tma_store_4d(&out_map, ob, cc * 32, j0, r, b);
-              tma_store_commit();
-              // a slab buffer is free again once its store has read it; keep one store in flight
-              tma_store_wait_read_le1();
-              if (slab >= 1) mbar_arrive(&bars->o_empty[(slab - 1) % kSlabs]);
-            }
-          }
-          ok = __shfl_sync(0xffffffffu, iok ? 1 : 0, 0) != 0;
-        }
-        if (!ok) break;
+        mbar_arrive(&bars->slab_ready[sl]);  // warp 14 stores the slab
       }
       if (!ok) break;
       tc_fence_before();
       mbar_arrive(&bars->d_empty[s]);
-    }
-    if (issuer) {
-      tma_store_wait_all();
-      if (ok && slab >= 1) mbar_arrive(&bars->o_empty[(slab - 1) % kSlabs]);
     }
   }
   tc_fence_before();
