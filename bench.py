@@ -478,7 +478,7 @@ def run_sharded(args, rank, world, device):
     stack = make_stack(L, device)
     so = TimedStageOps(CudaStageOps(device))
     shard = ShardedTrianglePairStack(stack, world, rank, stage_ops=so, trimul_exchange=args.trimul_exchange,
-                                     exchange=args.exchange)
+                                     exchange=args.exchange, k1_direct=args.k1_direct)
     if args.exchange == "peer":
         shard.connect(None, B, N, device)
     else:
@@ -581,6 +581,7 @@ def run_sharded(args, rank, world, device):
                        "global_batch": B, "seq_len": N, "layers": L,
                        "parallelism": f"row-sharded over i, {world} ranks x {R} rows (NCCL)",
                        "trimul_exchange": shard.trimul_exchange, "exchange": args.exchange,
+                       "k1_direct": bool(args.k1_direct and args.exchange == "peer" and shard.trimul_exchange == "channels"),
                        "l2": "inputs larger than L2 (each shard is >= 64 MB fp32); no flush"},
             "stack_tflops": round(stack_tflops, 1),
             "stack_frac_of_bf16_peak": round(stack_tflops / peaks["bf16_tflops"] / world, 4),
@@ -622,6 +623,9 @@ def main():
                     help="multi-GPU exchanges: peer-memory push kernels over NVLink, or NCCL collectives")
     ap.add_argument("--trimul-exchange", default="auto", choices=["auto", "gather", "channels"],
                     help="multi-GPU exchange of the multiplicative update (auto: gather for <= 3 GPUs)")
+    ap.add_argument("--k1-direct", action="store_true",
+                    help="peer exchanges, channel mode: K1 writes the a/b channel shards straight into the "
+                         "peers' buffers instead of a separate push")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))

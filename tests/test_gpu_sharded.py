@@ -193,7 +193,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _nccl_rank(rank, world, port, z, mask, params, q, exchange="nccl"):
+def _nccl_rank(rank, world, port, z, mask, params, q, exchange="nccl", trimul_exchange="auto", k1_direct=False):
     import datetime
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -208,7 +208,8 @@ def _nccl_rank(rank, world, port, z, mask, params, q, exchange="nccl"):
         N = z.shape[1]
         R = N // world
         zl = z[:, rank * R:(rank + 1) * R].contiguous().to(dev)
-        sh = ShardedTrianglePairStack(_stack(params, dev), world, rank, exchange=exchange)
+        sh = ShardedTrianglePairStack(_stack(params, dev), world, rank, exchange=exchange,
+                                      trimul_exchange=trimul_exchange, k1_direct=k1_direct)
         if exchange == "peer":
             sh.connect(None, 1, N, dev)
         sh.forward_(zl, mask.to(dev))
@@ -221,8 +222,9 @@ def _nccl_rank(rank, world, port, z, mask, params, q, exchange="nccl"):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("exchange", ["nccl", "peer"])
-def test_two_ranks_match_single_gpu(exchange):
+@pytest.mark.parametrize("exchange,trimul_exchange,k1_direct", [("nccl", "auto", False), ("peer", "auto", False),
+                                                                ("peer", "channels", False), ("peer", "channels", True)])
+def test_two_ranks_match_single_gpu(exchange, trimul_exchange, k1_direct):
     require_gpu()
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
@@ -231,7 +233,8 @@ def test_two_ranks_match_single_gpu(exchange):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_nccl_rank, args=(r, world, port, z, mask, params, q, exchange))
+    procs = [ctx.Process(target=_nccl_rank, args=(r, world, port, z, mask, params, q, exchange, trimul_exchange,
+                                                  k1_direct))
              for r in range(world)]
     for p in procs:
         p.start()
