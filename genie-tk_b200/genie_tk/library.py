@@ -1,0 +1,73 @@
+"""The C-ABI entry points as PyTorch operators (``torch.ops.genie_tk.*``).
+
+Each operator is a ``torch.library.custom_op`` whose implementation enqueues the library's
+kernels on the current CUDA stream (``ops.trimul_forward`` / ``ops.triatt_forward``), with
+outputs from the caching allocator, so it can be captured in a CUDA graph and is opaque to
+``torch.compile`` (the fake implementations give it shapes without running anything). They
+replace the pybind functions the reference declares in ``kernels/bindings.cpp:13-65``
+(``triangle_mul_outgoing`` / ``_incoming``, ``triangle_attention_starting`` / ``_ending``),
+taking the module's packed weights instead of pre-projected operands because the B200
+kernels fuse the projections.
+
+  genie_tk::trimul_forward(z, mask, packed, outgoing) -> update
+  genie_tk::triatt_forward(z, mask, packed, starting, inf) -> update
+  genie_tk::trimul_residual_(z, mask, packed, outgoing)        z += update, in place
+  genie_tk::triatt_residual_(z, mask, packed, starting, inf)   z += update, in place
+
+``z`` is ``[B, N, N, 128]`` (any float dtype; fp32 in place), ``mask`` ``[B, N, N]`` or
+None, ``packed`` the uint8 buffer of ``ops.pack_trimul`` / ``ops.pack_triatt``. No
+operator has an autograd formula: the kernels are forward-only.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+from torch import Tensor
+
+from . import ops
+
+
+@torch.library.custom_op("genie_tk::trimul_forward", mutates_args=())
+def trimul_forward(z: Tensor, mask: Optional[Tensor], packed: Tensor, outgoing: bool) -> Tensor:
+    """Update of the triangle multiplicative block (fp32)."""
+    return ops.trimul_forward(z, mask, packed, outgoing)
+
+
+@trimul_forward.register_fake
+def _trimul_forward_fake(z, mask, packed, outgoing):
+    return torch.empty(z.shape, dtype=torch.float32, device=z.device)
+
+
+@torch.library.custom_op("genie_tk::triatt_forward", mutates_args=())
+def triatt_forward(z: Tensor, mask: Optional[Tensor], packed: Tensor, starting: bool, inf: float) -> Tensor:
+    """Update of triangle attention around the starting / ending node (fp32)."""
+    return ops.triatt_forward(z, mask, packed, starting, inf=inf)
+
+
+@triatt_forward.register_fake
+def _triatt_forward_fake(z, mask, packed, starting, inf):
+    return torch.empty(z.shape, dtype=torch.float32, device=z.device)
+
+
+@torch.library.custom_op("genie_tk::trimul_residual_", mutates_args=("z",))
+def trimul_residual_(z: Tensor, mask: Optional[Tensor], packed: Tensor, outgoing: bool) -> None:
+    """z += update of the triangle multiplicative block, in place (z fp32 contiguous)."""
+    ops.trimul_forward(z, mask, packed, outgoing, out=z, add_residual=True)
+
+
+@trimul_residual_.register_fake
+def _trimul_residual_fake(z, mask, packed, outgoing):
+    return None
+
+
+@torch.library.custom_op("genie_tk::triatt_residual_", mutates_args=("z",))
+def triatt_residual_(z: Tensor, mask: Optional[Tensor], packed: Tensor, starting: bool, inf: float) -> None:
+    """z += update of triangle attention, in place (z fp32 contiguous)."""
+    ops.triatt_forward(z, mask, packed, starting, inf=inf, out=z, add_residual=True)
+
+
+@triatt_residual_.register_fake
+def _triatt_residual_fake(z, mask, packed, starting, inf):
+    return None

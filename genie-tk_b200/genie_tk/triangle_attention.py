@@ -54,7 +54,10 @@ class TriangleAttention(nn.Module):
             raise NotImplementedError(
                 "genie_tk (B200): triangle attention needs c_in = c_hidden = 128 with 4 heads of 32")
         packed = self.packed_weights(x.device)
-        res = ops.triatt_forward(x, mask, packed, self.starting, inf=self.inf, out=out, add_residual=add_residual)
+        if out is None and not add_residual:
+            res = torch.ops.genie_tk.triatt_forward(x, mask, packed, self.starting, float(self.inf))
+        else:
+            res = ops.triatt_forward(x, mask, packed, self.starting, inf=self.inf, out=out, add_residual=add_residual)
         return res if res.dtype == x.dtype or out is not None else res.to(x.dtype)
 
 

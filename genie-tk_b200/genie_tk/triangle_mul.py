@@ -79,7 +79,10 @@ class TriangleMultiplicativeUpdate(nn.Module):
         if self.c_z != ops.SUPPORTED_C or self.c_hidden != ops.SUPPORTED_C:
             raise NotImplementedError("genie_tk (B200): triangle multiplication needs c_z = c_hidden = 128")
         packed = self.packed_weights(z.device)
-        res = ops.trimul_forward(z, mask, packed, self._outgoing, out=out, add_residual=add_residual)
+        if out is None and not add_residual:
+            res = torch.ops.genie_tk.trimul_forward(z, mask, packed, self._outgoing)
+        else:
+            res = ops.trimul_forward(z, mask, packed, self._outgoing, out=out, add_residual=add_residual)
         return res if res.dtype == z.dtype or out is not None else res.to(z.dtype)
 
 
