@@ -38,6 +38,12 @@ class TriattParams(ctypes.Structure):
         "ln_w", "ln_b", "bias_w", "q_w", "k_w", "v_w", "g_w", "g_b", "o_w", "o_b")]
 
 
+class TransitionParams(ctypes.Structure):
+    """Mirror of ``gtk_transition_params`` (include/genie_tk_b200.h)."""
+
+    _fields_ = [(name, c_vp) for name in ("ln_w", "ln_b", "w1", "b1", "w2", "b2")]
+
+
 # name -> (restype, argtypes)
 _SIGNATURES = {
     "gtk_version": (c_int, []),
@@ -76,6 +82,11 @@ _SIGNATURES = {
     "gtk_push_3d": (c_int, [c_vp, c_int, c_i64, c_i64, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp]),
     "gtk_push_pair_transpose": (c_int, [c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp]),
     "gtk_peer_barrier": (c_int, [c_vp, c_int, c_int, ctypes.c_uint32, c_vp, c_vp]),
+    "gtk_transition_packed_bytes": (c_size, [c_int, c_int]),
+    "gtk_transition_pack": (c_int, [ctypes.POINTER(TransitionParams), c_int, c_int, c_vp, c_size, c_vp]),
+    "gtk_transition_workspace_bytes": (c_size, [c_i64, c_i64, c_int, c_int]),
+    "gtk_transition_forward": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_vp, c_size, c_i64, c_i64, c_int, c_int, c_vp,
+                                       c_vp]),
 }
 
 

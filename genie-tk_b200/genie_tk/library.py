@@ -13,9 +13,12 @@ kernels fuse the projections.
   genie_tk::triatt_forward(z, mask, packed, starting, inf) -> update
   genie_tk::trimul_residual_(z, mask, packed, outgoing)        z += update, in place
   genie_tk::triatt_residual_(z, mask, packed, starting, inf)   z += update, in place
+  genie_tk::transition_forward(z, packed) -> update            the pair transition
+  genie_tk::transition_residual_(z, mask, packed)              z = (z + update) * mask, in place
 
 ``z`` is ``[B, N, N, 128]`` (any float dtype; fp32 in place), ``mask`` ``[B, N, N]`` or
-None, ``packed`` the uint8 buffer of ``ops.pack_trimul`` / ``ops.pack_triatt``. No
+None, ``packed`` the uint8 buffer of ``ops.pack_trimul`` / ``ops.pack_triatt`` /
+``ops.pack_transition``. No
 operator has an autograd formula: the kernels are forward-only.
 """
 
@@ -70,4 +73,26 @@ def triatt_residual_(z: Tensor, mask: Optional[Tensor], packed: Tensor, starting
 
 @triatt_residual_.register_fake
 def _triatt_residual_fake(z, mask, packed, starting, inf):
+    return None
+
+
+@torch.library.custom_op("genie_tk::transition_forward", mutates_args=())
+def transition_forward(z: Tensor, packed: Tensor) -> Tensor:
+    """Update of the pair transition (LN -> 4x expand -> ReLU -> project), fp32."""
+    return ops.transition_forward(z, None, packed)
+
+
+@transition_forward.register_fake
+def _transition_forward_fake(z, packed):
+    return torch.empty(z.shape, dtype=torch.float32, device=z.device)
+
+
+@torch.library.custom_op("genie_tk::transition_residual_", mutates_args=("z",))
+def transition_residual_(z: Tensor, mask: Optional[Tensor], packed: Tensor) -> None:
+    """z = (z + transition(z)) * mask, in place (z fp32 contiguous; no mask: just the residual)."""
+    ops.transition_forward(z, mask, packed, out=z, add_residual=True)
+
+
+@transition_residual_.register_fake
+def _transition_residual_fake(z, mask, packed):
     return None

@@ -291,3 +291,51 @@ def triatt_finish(z: Optional[torch.Tensor], packed: torch.Tensor, starting: boo
                                      R, N, _ptr(status_buffer(out.device)), _stream(out.device)),
                "gtk_triatt_finish")
     return out
+
+
+# --------------------------------------------------------------------------------------
+# Pair transition (LayerNorm -> 4x expand -> ReLU -> project), residual and mask folded in
+# --------------------------------------------------------------------------------------
+
+TRANSITION_KEYS = ("layer_norm.weight", "layer_norm.bias", "linear_1.weight", "linear_1.bias", "linear_2.weight",
+                   "linear_2.bias")
+
+
+def pack_transition(params: Dict[str, torch.Tensor], device: torch.device) -> torch.Tensor:
+    """Pack a PairTransition's fp32 parameters (reference state_dict keys)."""
+    lib = _lib.load()
+    c_p = params["layer_norm.weight"].shape[0]
+    hid = params["linear_1.weight"].shape[0]
+    if c_p != SUPPORTED_C or hid != 4 * SUPPORTED_C:
+        raise NotImplementedError("genie_tk (B200): the pair transition kernels need c_p = 128 and n = 4")
+    nbytes = lib.gtk_transition_packed_bytes(c_p, hid // c_p)
+    tensors = []
+    for k in TRANSITION_KEYS:
+        t = params[k].detach()
+        _require_cuda(t, k)
+        tensors.append(t.float().contiguous())
+    packed = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    st = _lib.TransitionParams(*[ctypes.c_void_p(t.data_ptr()) for t in tensors])
+    _lib.check(lib.gtk_transition_pack(ctypes.byref(st), c_p, hid // c_p, _ptr(packed), nbytes, _stream(device)),
+               "gtk_transition_pack")
+    packed._gtk_keepalive = tensors
+    return packed
+
+
+def transition_forward(z: torch.Tensor, mask: Optional[torch.Tensor], packed: torch.Tensor,
+                       out: Optional[torch.Tensor] = None, add_residual: bool = False) -> torch.Tensor:
+    """transition(z), or z + transition(z) (add_residual), times mask[b, i, j] when a mask
+    is given; fp32 [B, N, N, 128]. ``out=z`` updates in place."""
+    lib = _lib.load()
+    zf, mf = prepare_pair(z, mask, SUPPORTED_C)
+    B, N = zf.shape[0], zf.shape[1]
+    if out is None:
+        out = torch.empty_like(zf)
+    _require_cuda(out, "out", torch.float32)
+    nbytes = lib.gtk_transition_workspace_bytes(B, N, SUPPORTED_C, 4)
+    ws = workspace(zf.device, nbytes, tag="transition")
+    rc = lib.gtk_transition_forward(_ptr(zf), _ptr(mf), _ptr(packed), _ptr(out), int(add_residual), _ptr(ws),
+                                    ws.numel(), B, N, SUPPORTED_C, 4, _ptr(status_buffer(zf.device)),
+                                    _stream(zf.device))
+    _lib.check(rc, "gtk_transition_forward")
+    return out

@@ -2,9 +2,10 @@
 
 The four triangle blocks run on the B200 kernels with the residual add fused into
 their epilogues (``add_residual=True``) whenever the residual can be taken in place.
-``PairTransition`` (LN -> 4x expand -> ReLU -> project) and the row/column dropout
-are outside the triangle hot path; they are evaluated with cuBLAS-backed PyTorch ops
-on the same CUDA tensors.
+``PairTransition`` (LN -> 4x expand -> ReLU -> project) runs on the two transition
+kernels (``gtk_transition_forward``); inside ``PairTransformLayer`` its residual add and
+the layer's final mask multiply are folded into the second one. The training-mode
+row/column dropout is evaluated with PyTorch ops on the same CUDA tensors.
 """
 
 from __future__ import annotations
@@ -15,9 +16,10 @@ import torch
 import torch.nn as nn
 from torch import Tensor
 
+from . import ops
 from .primitives import Linear
 from .triangle_attention import TriangleAttentionEndingNode, TriangleAttentionStartingNode
-from .triangle_mul import TriangleMultiplicationIncoming, TriangleMultiplicationOutgoing
+from .triangle_mul import TriangleMultiplicationIncoming, TriangleMultiplicationOutgoing, _PackCache
 
 
 class DropoutRowwise(nn.Module):
@@ -53,7 +55,8 @@ class DropoutColumnwise(nn.Module):
 
 
 class PairTransition(nn.Module):
-    """Pair feed-forward (reference pair_transform.py:64-84)."""
+    """Pair feed-forward (reference pair_transform.py:64-84): LN -> Linear(c_p, n c_p) ->
+    ReLU -> Linear(n c_p, c_p). Runs on the transition kernels (c_p = 128, n = 4)."""
 
     def __init__(self, c_p: int, n: int = 4):
         super().__init__()
@@ -63,11 +66,29 @@ class PairTransition(nn.Module):
         self.linear_1 = Linear(c_p, c_p * n)
         self.relu = nn.ReLU()
         self.linear_2 = Linear(c_p * n, c_p, init="final")
+        self._pack = _PackCache()
 
-    def forward(self, p: Tensor, mask: Optional[Tensor] = None) -> Tensor:
+    def packed_weights(self, device: torch.device) -> Tensor:
+        sd = {k: v for k, v in self.state_dict(keep_vars=True).items()}
+        return self._pack.get(self, lambda: ops.pack_transition(sd, device))
+
+    def _check(self, p: Tensor) -> None:
         if not p.is_cuda:
             raise RuntimeError("genie_tk (B200): PairTransition runs on CUDA tensors only")
-        return self.linear_2(self.relu(self.linear_1(self.layer_norm(p))))
+        if self.c_p != ops.SUPPORTED_C or self.n != 4:
+            raise NotImplementedError("genie_tk (B200): the pair transition kernels need c_p = 128 and n = 4")
+
+    def forward(self, p: Tensor, mask: Optional[Tensor] = None) -> Tensor:
+        """The update (the reference ignores ``mask`` here, and so does this)."""
+        self._check(p)
+        res = torch.ops.genie_tk.transition_forward(p, self.packed_weights(p.device))
+        return res if res.dtype == p.dtype else res.to(p.dtype)
+
+    def residual_masked_(self, p: Tensor, p_mask: Optional[Tensor]) -> Tensor:
+        """p = (p + transition(p)) * p_mask, in place on a contiguous fp32 ``p`` (the tail of
+        PairTransformLayer.forward, pair_transform.py:190-193, in one kernel pass)."""
+        self._check(p)
+        return ops.transition_forward(p, p_mask, self.packed_weights(p.device), out=p, add_residual=True)
 
 
 class PairTransformLayer(nn.Module):
@@ -112,8 +133,8 @@ class PairTransformLayer(nn.Module):
                 block(p, p_mask, out=p, add_residual=True)
             else:
                 p = p + drop(block(p, p_mask))
-        p = p + self.pair_transition(p, p_mask)
-        p = p * p_mask.unsqueeze(-1).to(p.dtype)
+        # p = (p + transition(p)) * mask in one pass (p is a private contiguous fp32 copy)
+        self.pair_transition.residual_masked_(p, p_mask)
         return (p.to(dtype), p_mask)
 
 

@@ -21,7 +21,7 @@ from .primitives import Linear
 
 
 class _PackCache:
-    """Packed bf16 weights, rebuilt when a parameter tensor or its version changes."""
+    """Packed fp16 weights, rebuilt when a parameter tensor or its version changes."""
 
     def __init__(self):
         self.key = None

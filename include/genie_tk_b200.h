@@ -279,6 +279,31 @@ GTK_API int gtk_push_pair_transpose(const float* src, const uint64_t* dsts, int6
 GTK_API int gtk_peer_barrier(const uint64_t* flag_ptrs, int rank, int P, uint32_t epoch, uint32_t* status,
                              void* stream);
 
+/* ---------------------------------------------------------------------------------
+ * Pair transition (reference src/genie_tk/pair_transform.py:64-84, the feed-forward of
+ * PairTransformLayer; no counterpart in kernels/bindings.cpp) with the layer's residual and
+ * final mask multiply (pair_transform.py:190-193) folded in. c_p = 128, n = 4 only.
+ * ------------------------------------------------------------------------------- */
+typedef struct gtk_transition_params {
+  const float* ln_w; /* layer_norm.weight [c_p] */
+  const float* ln_b; /* layer_norm.bias [c_p] */
+  const float* w1;   /* linear_1.weight [n c_p, c_p] */
+  const float* b1;   /* linear_1.bias [n c_p] (NULL = zero) */
+  const float* w2;   /* linear_2.weight [c_p, n c_p] */
+  const float* b2;   /* linear_2.bias [c_p] (NULL = zero) */
+} gtk_transition_params;
+
+GTK_API size_t gtk_transition_packed_bytes(int c_p, int n);
+GTK_API int gtk_transition_pack(const gtk_transition_params* params, int c_p, int n, void* packed,
+                                size_t packed_bytes, void* stream);
+/* Workspace for the hidden rows: B*N*N*n*c_p fp16. */
+GTK_API size_t gtk_transition_workspace_bytes(int64_t B, int64_t N, int c_p, int n);
+/* out = (add_residual ? z : 0) + transition(z), then times mask[b, i, j] when mask is not
+ * NULL. z, out fp32 [B, N, N, 128] (out may equal z); mask fp32 [B, N, N] or NULL. */
+GTK_API int gtk_transition_forward(const float* z, const float* mask, const void* packed, float* out,
+                                   int add_residual, void* workspace, size_t workspace_bytes, int64_t B, int64_t N,
+                                   int c_p, int n, uint32_t* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

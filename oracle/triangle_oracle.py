@@ -170,6 +170,25 @@ def stack_forward(z: torch.Tensor, mask: Optional[torch.Tensor], layers: List[Di
 
 
 # --------------------------------------------------------------------------------------
+# Pair transition -- src/genie_tk/pair_transform.py:64-84, and the tail of
+# PairTransformLayer.forward (:190-193)
+# --------------------------------------------------------------------------------------
+
+def transition_forward(z: torch.Tensor, p: Params) -> torch.Tensor:
+    """PairTransition.forward (pair_transform.py:78-84): LN -> linear_1 -> ReLU -> linear_2.
+    The reference ignores its mask argument here."""
+    x = layer_norm(z.float(), p["layer_norm.weight"], p["layer_norm.bias"])
+    return linear(torch.relu(linear(x, p, "linear_1")), p, "linear_2")
+
+
+def layer_tail(z: torch.Tensor, mask: torch.Tensor, p: Params) -> torch.Tensor:
+    """The last two statements of PairTransformLayer.forward (pair_transform.py:190-193):
+    p = p + pair_transition(p, p_mask); p = p * p_mask.unsqueeze(-1)."""
+    z = z.float()
+    return (z + transition_forward(z, p)) * mask.float().unsqueeze(-1)
+
+
+# --------------------------------------------------------------------------------------
 # Seeded parameters and inputs of the benchmark configurations.
 # Weights ~ N(0, 1/fan_in) in the reference layout [out, in]; biases 0 unless a gate
 # bias of 1 is requested; LayerNorm gamma=1, beta=0 unless ``ln_random``.
@@ -221,6 +240,24 @@ def make_triatt_params(c_in: int, c_hidden: int, no_heads: int, gen: torch.Gener
     p["mha.linear_g.weight"] = _w(gen, c_hidden, c_in)
     p["mha.linear_g.bias"] = (0.1 * torch.randn(c_hidden, generator=gen) if bias_random
                               else torch.full((c_hidden,), gate_bias))
+    return p
+
+
+def make_transition_params(c_p: int, n: int, gen: torch.Generator, ln_random: bool = True,
+                           bias_random: bool = True) -> Params:
+    """Parameters of PairTransition (pair_transform.py:72-76), in module order. linear_2 is
+    drawn like linear_1 rather than the reference's zero "final" init, so that the update
+    is not identically zero."""
+    p: Params = {}
+    if ln_random:
+        p["layer_norm.weight"] = 1.0 + 0.1 * torch.randn(c_p, generator=gen)
+        p["layer_norm.bias"] = 0.1 * torch.randn(c_p, generator=gen)
+    else:
+        p["layer_norm.weight"] = torch.ones(c_p)
+        p["layer_norm.bias"] = torch.zeros(c_p)
+    for name, (o, i) in (("linear_1", (c_p * n, c_p)), ("linear_2", (c_p, c_p * n))):
+        p[name + ".weight"] = _w(gen, o, i)
+        p[name + ".bias"] = 0.1 * torch.randn(o, generator=gen) if bias_random else torch.zeros(o)
     return p
 
 

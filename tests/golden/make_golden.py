@@ -3,7 +3,8 @@
 Run in a container where the reference is mounted (it is read from
 ``$GTK_REFERENCE_ROOT``, default ``/root/reference``)::
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py              # triangle blocks and the 2-layer stack
+    python tests/golden/make_golden.py transition   # the pair transition
 
 The reference package is imported from a repaired copy (``oracle/reference_copy.py``:
 mechanical docstring repair only). For every case the script builds the reference
@@ -128,5 +129,31 @@ def main():
     print(f"stack2_c128: out |max| {z.abs().max():.4f}")
 
 
+def main_transition():
+    """Golden vectors of the reference's PairTransition (pair_transform.py:64-84), c_p = 128,
+    n = 4, with seeded parameters (regenerated by the tests, pinned by checksum)."""
+    ref = import_reference()
+    torch.set_grad_enabled(False)
+    for name, (B, N, seed) in {"transition_c128": (2, 8, 41)}.items():
+        gen = torch.Generator().manual_seed(seed)
+        z = torch.randn(B, N, N, 128, generator=gen)
+        mask = make_mask("ragged", B, N, gen)
+        p = O.make_transition_params(128, 4, torch.Generator().manual_seed(seed + 100))
+        mod = ref.pair_transform.PairTransition(128, 4) if hasattr(ref, "pair_transform") else ref.PairTransition(128, 4)
+        missing = set(mod.state_dict()) ^ set(p)
+        assert not missing, missing
+        mod.load_state_dict(p)
+        mod.eval()
+        upd = mod(z, mask)
+        np.savez_compressed(os.path.join(HERE, name + ".npz"), op=np.array("transition"), B=B, N=N, c_z=128,
+                            c_hidden=512, heads=0, param_seed=seed + 100, z=z.numpy(), mask=mask.numpy(),
+                            out=upd.numpy(), param_keys=np.array(sorted(p)),
+                            param_checksum=param_checksum(p), param_kwargs=np.array(repr({})))
+        print(f"{name}: out |max| {upd.abs().max():.4f}")
+
+
 if __name__ == "__main__":
-    main()
+    if sys.argv[1:] == ["transition"]:
+        main_transition()
+    else:
+        main()

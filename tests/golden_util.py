@@ -40,6 +40,15 @@ def load_case(name):
     return op, dims, torch.from_numpy(d["z"]), torch.from_numpy(d["mask"]), params, torch.from_numpy(d["out"])
 
 
+def load_transition(name="transition_c128"):
+    """(z, mask, params, out) of a pair-transition golden case; params regenerated and pinned."""
+    d = np.load(os.path.join(GOLDEN, name + ".npz"))
+    params = O.make_transition_params(int(d["c_z"]), int(d["c_hidden"]) // int(d["c_z"]),
+                                      torch.Generator().manual_seed(int(d["param_seed"])))
+    np.testing.assert_allclose(_checksum(params), d["param_checksum"], rtol=1e-6, atol=1e-6)
+    return torch.from_numpy(d["z"]), torch.from_numpy(d["mask"]), params, torch.from_numpy(d["out"])
+
+
 def load_stack():
     d = np.load(os.path.join(GOLDEN, "stack2_c128.npz"))
     gen = torch.Generator().manual_seed(int(d["param_seed"]))

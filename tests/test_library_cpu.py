@@ -13,7 +13,9 @@ def test_operators_registered_with_schemas():
     for name, args in (("trimul_forward", "Tensor z, Tensor? mask, Tensor packed, bool outgoing"),
                        ("triatt_forward", "Tensor z, Tensor? mask, Tensor packed, bool starting, float inf"),
                        ("trimul_residual_", "Tensor(a0!) z, Tensor? mask, Tensor packed, bool outgoing"),
-                       ("triatt_residual_", "Tensor(a0!) z, Tensor? mask, Tensor packed, bool starting, float inf")):
+                       ("triatt_residual_", "Tensor(a0!) z, Tensor? mask, Tensor packed, bool starting, float inf"),
+                       ("transition_forward", "Tensor z, Tensor packed"),
+                       ("transition_residual_", "Tensor(a0!) z, Tensor? mask, Tensor packed")):
         op = getattr(torch.ops.genie_tk, name).default
         assert args in str(op._schema), str(op._schema)
 
@@ -26,6 +28,9 @@ def test_fake_implementations_propagate_shapes():
     assert v.shape == z.shape and v.dtype == torch.float32
     assert torch.ops.genie_tk.trimul_residual_(z, m, p, False) is None
     assert torch.ops.genie_tk.triatt_residual_(z, None, p, True, 1e9) is None
+    t = torch.ops.genie_tk.transition_forward(z.half(), p)
+    assert t.shape == z.shape and t.dtype == torch.float32
+    assert torch.ops.genie_tk.transition_residual_(z, m, p) is None
 
 
 def test_operators_refuse_cpu_tensors():

@@ -3,7 +3,7 @@
 import pytest
 import torch
 
-from golden_util import SINGLE_CASES, load_case, load_stack, oracle_run
+from golden_util import SINGLE_CASES, load_case, load_stack, load_transition, oracle_run
 from oracle import triangle_oracle as O
 
 
@@ -26,6 +26,14 @@ def test_oracle_stack_matches_reference_golden():
     z, mask, layers, out = load_stack()
     got = O.stack_forward(z, mask, layers, no_heads=4)
     torch.testing.assert_close(got, out, rtol=1e-4, atol=5e-5)
+
+
+def test_oracle_transition_matches_reference_golden():
+    z, mask, params, out = load_transition()
+    torch.testing.assert_close(O.transition_forward(z, params), out, rtol=1e-4, atol=2e-5)
+    tail = O.layer_tail(z, mask, params)
+    torch.testing.assert_close(tail, (z + out) * mask.unsqueeze(-1), rtol=1e-5, atol=1e-6)
+    assert float(tail[mask == 0].abs().max()) == 0.0
 
 
 def test_known_answers():
