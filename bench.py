@@ -608,6 +608,58 @@ def read_traffic(kernel):
     return None
 
 
+def run_transition(args, device):
+    """``--op transition``: the pair transition (LN -> 4x expand -> ReLU -> project) with the
+    pair transform layer's residual and mask, p = (p + transition(p)) * mask, on one GPU
+    (N^2 pairs per step, B = 1, seeded synthetic z and weights). Not the BASELINE metric; it
+    measures the SURVEY 8(f) transition kernels against their HBM roofline and against
+    the same math as unfused fp32 PyTorch ops on the GPU."""
+    from genie_tk import ops
+    from oracle import triangle_oracle as O
+    N = args.N
+    gen = torch.Generator().manual_seed(5)
+    z = torch.randn(1, N, N, 128, generator=gen).to(device)
+    mask = torch.ones(1, N, N, device=device)
+    p = {k: v.to(device) for k, v in O.make_transition_params(128, 4, gen).items()}
+    packed = ops.pack_transition(p, device)
+    out = torch.empty_like(z)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def timed(fn, steps):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    ms = timed(lambda: ops.transition_forward(z, mask, packed, out=out, add_residual=True), args.steps)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    lw, lb = p["layer_norm.weight"], p["layer_norm.bias"]
+
+    def torch_path():
+        h = torch.relu(torch.nn.functional.linear(torch.nn.functional.layer_norm(z, (128,), lw, lb),
+                                                  p["linear_1.weight"], p["linear_1.bias"]))
+        return (z + torch.nn.functional.linear(h, p["linear_2.weight"], p["linear_2.bias"])) * mask.unsqueeze(-1)
+
+    ms_torch = timed(torch_path, max(2, args.steps // 4))
+    diff = float((out - torch_path()).abs().max())
+    peaks = load_peaks()
+    bytes_pair = 512 + 1024 + 1024 + 512 + 512 + 4  # z in, h out | h in, z in, out, mask
+    gbs = N * N * bytes_pair / (ms / 1e3) / 1e9
+    return {"metric": "pair transition N^2/s (residual + mask, one layer)", "value": N * N / (ms / 1e3),
+            "unit": "N^2/s", "ms_per_step": ms, "steps": args.steps, "warmup": args.warmup, "n_gpus": 1,
+            "higher_is_better": True, "dtype": "f16 tensor-core operands, f32 accumulate / f32 residual",
+            "data": "synthetic (z ~ N(0,1), seeded weights)", "config": {"workload": f"pair transition, B=1, N={N}"},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(gbs / peaks["hbm_gbs"], 4), "bytes_per_pair": bytes_pair},
+            "torch_fp32_unfused_ms": ms_torch, "max_abs_diff_vs_torch_fp32": diff,
+            "status_word": ops.check_status(device)}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -623,6 +675,8 @@ def main():
                     help="multi-GPU exchanges: peer-memory push kernels over NVLink, or NCCL collectives")
     ap.add_argument("--trimul-exchange", default="auto", choices=["auto", "gather", "channels"],
                     help="multi-GPU exchange of the multiplicative update (auto: gather for <= 3 GPUs)")
+    ap.add_argument("--op", default="stack", choices=["stack", "transition"],
+                    help="stack: the BASELINE workload (default); transition: the pair-transition kernels alone")
     ap.add_argument("--k1-direct", action="store_true",
                     help="peer exchanges, channel mode: K1 writes the a/b channel shards straight into the "
                          "peers' buffers instead of a separate push")
@@ -640,6 +694,9 @@ def main():
 
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
+    if args.op == "transition":
+        print(json.dumps(run_transition(args, device)), flush=True)
+        return 0
     if world > 1:
         from datetime import timedelta
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
