@@ -660,6 +660,50 @@ def run_transition(args, device):
             "status_word": ops.check_status(device)}
 
 
+def run_embed(args, device, c_s: int = 384):
+    """``--op embed``: the pair embedding producer (p_ij = Linear(2 c_s, 128)([s_i ; s_j]),
+    p_mask = m_i m_j) for one N x N grid, against HBM (512 + 4 B written per pair) and
+    against the reference's own operations (expand, cat, nn.Linear in fp32) on the GPU."""
+    from genie_tk import ops
+    N = args.N
+    gen = torch.Generator().manual_seed(6)
+    s = torch.randn(1, N, c_s, generator=gen).to(device)
+    mask = torch.ones(1, N, device=device)
+    w = (torch.randn(128, 2 * c_s, generator=gen) / (2 * c_s) ** 0.5).to(device)
+    b = (0.1 * torch.randn(128, generator=gen)).to(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def timed(fn, steps):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    ms = timed(lambda: ops.pair_embed(s, mask, w, b), args.steps)
+    torch.backends.cuda.matmul.allow_tf32 = False
+
+    def torch_path():
+        s_i = s.unsqueeze(2).expand(-1, -1, N, -1)
+        s_j = s.unsqueeze(1).expand(-1, N, -1, -1)
+        return torch.nn.functional.linear(torch.cat([s_i, s_j], dim=-1), w, b), mask.unsqueeze(1) * mask.unsqueeze(2)
+
+    ms_torch = timed(torch_path, max(2, args.steps // 4))
+    diff = float((ops.pair_embed(s, mask, w, b)[0] - torch_path()[0]).abs().max())
+    peaks = load_peaks()
+    gbs = N * N * (512 + 4) / (ms / 1e3) / 1e9
+    return {"metric": "pair embedding N^2/s (c_s = %d)" % c_s, "value": N * N / (ms / 1e3), "unit": "N^2/s",
+            "ms_per_step": ms, "steps": args.steps, "warmup": args.warmup, "n_gpus": 1, "higher_is_better": True,
+            "dtype": "f32", "data": "synthetic", "config": {"workload": f"pair embedding, B=1, N={N}, c_s={c_s}"},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(gbs / peaks["hbm_gbs"], 4), "bytes_per_pair": 516},
+            "torch_fp32_reference_ops_ms": ms_torch, "max_abs_diff_vs_torch_fp32": diff}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -675,8 +719,9 @@ def main():
                     help="multi-GPU exchanges: peer-memory push kernels over NVLink, or NCCL collectives")
     ap.add_argument("--trimul-exchange", default="auto", choices=["auto", "gather", "channels"],
                     help="multi-GPU exchange of the multiplicative update (auto: gather for <= 3 GPUs)")
-    ap.add_argument("--op", default="stack", choices=["stack", "transition"],
-                    help="stack: the BASELINE workload (default); transition: the pair-transition kernels alone")
+    ap.add_argument("--op", default="stack", choices=["stack", "transition", "embed"],
+                    help="stack: the BASELINE workload (default); transition / embed: the pair-transition or "
+                         "pair-embedding kernels alone")
     ap.add_argument("--k1-direct", action="store_true",
                     help="peer exchanges, channel mode: K1 writes the a/b channel shards straight into the "
                          "peers' buffers instead of a separate push")
@@ -694,8 +739,9 @@ def main():
 
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
-    if args.op == "transition":
-        print(json.dumps(run_transition(args, device)), flush=True)
+    if args.op in ("transition", "embed"):
+        print(json.dumps(run_transition(args, device) if args.op == "transition" else run_embed(args, device)),
+              flush=True)
         return 0
     if world > 1:
         from datetime import timedelta

@@ -17,7 +17,7 @@ from .triangle_attention import (  # noqa: F401
     TriangleAttentionStartingNode,
     TriangleAttentionEndingNode,
 )
-from .pair_transform import PairTransformLayer, PairTransformNet  # noqa: F401
+from .pair_transform import PairEmbedding, PairTransformLayer, PairTransformNet  # noqa: F401
 from .stack import TrianglePairStack  # noqa: F401
 from .utils import has_cuda_kernels, get_device_info  # noqa: F401
 from . import library  # noqa: F401  (registers torch.ops.genie_tk.*)
@@ -31,6 +31,7 @@ __all__ = [
     "TriangleAttentionEndingNode",
     "PairTransformLayer",
     "PairTransformNet",
+    "PairEmbedding",
     "TrianglePairStack",
     "has_cuda_kernels",
     "get_device_info",

@@ -87,6 +87,9 @@ _SIGNATURES = {
     "gtk_transition_workspace_bytes": (c_size, [c_i64, c_i64, c_int, c_int]),
     "gtk_transition_forward": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_vp, c_size, c_i64, c_i64, c_int, c_int, c_vp,
                                        c_vp]),
+    "gtk_pair_embed_workspace_bytes": (c_size, [c_i64, c_i64, c_int]),
+    "gtk_pair_embed": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_size, c_i64, c_i64, c_i64, c_i64, c_int,
+                               c_int, c_vp]),
 }
 
 

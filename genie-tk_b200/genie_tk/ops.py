@@ -339,3 +339,41 @@ def transition_forward(z: torch.Tensor, mask: Optional[torch.Tensor], packed: to
                                     _stream(zf.device))
     _lib.check(rc, "gtk_transition_forward")
     return out
+
+
+# --------------------------------------------------------------------------------------
+# Pair embedding producer: p[b,i,j] = Linear(2 c_s, c_p)([s_i ; s_j]), p_mask = m_i m_j
+# --------------------------------------------------------------------------------------
+
+def pair_embed(s: torch.Tensor, mask: Optional[torch.Tensor], weight: torch.Tensor, bias: Optional[torch.Tensor],
+               rows: Optional[int] = None, row0: int = 0, with_mask: bool = True):
+    """Pair representation [B, rows, N, 128] fp32 (rows row0 .. row0+rows-1 of the N x N
+    grid; all by default) and, with ``with_mask``, the pair mask [B, rows, N]."""
+    lib = _lib.load()
+    _require_cuda(s, "s")
+    if s.dim() != 3:
+        raise ValueError(f"s must be [B, N, c_s], got {tuple(s.shape)}")
+    B, N, c_s = s.shape
+    c_p = weight.shape[0]
+    if c_p != SUPPORTED_C:
+        raise NotImplementedError(f"genie_tk (B200): pair embedding needs c_p = {SUPPORTED_C}, got {c_p}")
+    if tuple(weight.shape) != (c_p, 2 * c_s):
+        raise ValueError(f"weight must be [c_p, 2 c_s] = [{c_p}, {2 * c_s}], got {tuple(weight.shape)}")
+    rows = N if rows is None else int(rows)
+    sf = s.float().contiguous()
+    wf = weight.detach().float().contiguous()
+    _require_cuda(wf, "weight")
+    bf = None if bias is None else bias.detach().float().contiguous()
+    mf = None
+    if mask is not None:
+        _require_cuda(mask, "mask")
+        if tuple(mask.shape) != (B, N):
+            raise ValueError(f"mask must be [B, N], got {tuple(mask.shape)}")
+        mf = mask.float().contiguous()
+    out = torch.empty(B, rows, N, c_p, dtype=torch.float32, device=s.device)
+    pm = torch.empty(B, rows, N, dtype=torch.float32, device=s.device) if with_mask else None
+    nbytes = lib.gtk_pair_embed_workspace_bytes(B, N, c_p)
+    ws = workspace(s.device, nbytes, tag="embed")
+    _lib.check(lib.gtk_pair_embed(_ptr(sf), _ptr(mf), _ptr(wf), _ptr(bf), _ptr(out), _ptr(pm), _ptr(ws), ws.numel(),
+                                  B, N, rows, int(row0), c_s, c_p, _stream(s.device)), "gtk_pair_embed")
+    return out, pm

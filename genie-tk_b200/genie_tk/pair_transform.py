@@ -91,6 +91,30 @@ class PairTransition(nn.Module):
         return ops.transition_forward(p, p_mask, self.packed_weights(p.device), out=p, add_residual=True)
 
 
+class PairEmbedding(nn.Module):
+    """Initial pair representation from the single representation (reference
+    examples/basic_usage.py:170-199): ``p[b,i,j] = Linear(2 c_s, c_p)([s_i ; s_j])`` and the
+    pair mask ``p_mask[b,i,j] = mask[b,i] * mask[b,j]``. Holds the ``weight`` / ``bias`` of
+    that ``nn.Linear(c_s * 2, c_p)`` (state-dict compatible with it) and runs on the pair
+    embedding kernels, which never form the concatenated [B, N, N, 2 c_s] tensor. c_p = 128.
+    """
+
+    def __init__(self, c_s: int, c_p: int):
+        super().__init__()
+        self.c_s = c_s
+        self.c_p = c_p
+        lin = nn.Linear(c_s * 2, c_p)
+        self.weight = lin.weight
+        self.bias = lin.bias
+
+    def forward(self, s: Tensor, mask: Optional[Tensor] = None) -> Tuple[Tensor, Optional[Tensor]]:
+        """(p [B, N, N, c_p] fp32, p_mask [B, N, N] or None when ``mask`` is None)."""
+        if not s.is_cuda:
+            raise RuntimeError("genie_tk (B200): PairEmbedding runs on CUDA tensors only")
+        p, pm = ops.pair_embed(s, mask, self.weight, self.bias, with_mask=mask is not None)
+        return p, pm
+
+
 class PairTransformLayer(nn.Module):
     """One pair transform layer (reference pair_transform.py:87-195)."""
 

@@ -304,6 +304,20 @@ GTK_API int gtk_transition_forward(const float* z, const float* mask, const void
                                    int add_residual, void* workspace, size_t workspace_bytes, int64_t B, int64_t N,
                                    int c_p, int n, uint32_t* status, void* stream);
 
+/* ---------------------------------------------------------------------------------
+ * Pair embedding producer (reference examples/basic_usage.py:181-199; no counterpart in
+ * kernels/bindings.cpp): p[b,i,j] = weight @ [s[b,i]; s[b,j]] + bias (nn.Linear(2 c_s, c_p)
+ * on the concatenation, never formed) and p_mask[b,i,j] = mask[b,i] * mask[b,j], written
+ * into the fp32 pair layout [B, rows, N, c_p] for rows row0 .. row0+rows-1 (all of them:
+ * rows = N, row0 = 0; a row shard otherwise). c_p = 128.
+ * s fp32 [B, N, c_s]; mask fp32 [B, N] or NULL; weight fp32 [c_p, 2 c_s]; bias [c_p] or
+ * NULL; pair_mask fp32 [B, rows, N] or NULL (not written).
+ * ------------------------------------------------------------------------------- */
+GTK_API size_t gtk_pair_embed_workspace_bytes(int64_t B, int64_t N, int c_p);
+GTK_API int gtk_pair_embed(const float* s, const float* mask, const float* weight, const float* bias, float* out,
+                           float* pair_mask, void* workspace, size_t workspace_bytes, int64_t B, int64_t N,
+                           int64_t rows, int64_t row0, int c_s, int c_p, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -243,6 +243,21 @@ def make_triatt_params(c_in: int, c_hidden: int, no_heads: int, gen: torch.Gener
     return p
 
 
+def pair_embed(s: torch.Tensor, mask: Optional[torch.Tensor], p: Params):
+    """The pair embedding of examples/basic_usage.py:188-196: p_ij = Linear([s_i ; s_j]) over
+    the concatenation (nn.Linear(2 c_s, c_p), keys ``weight`` / ``bias``) and
+    p_mask = mask_i * mask_j (None without a mask)."""
+    B, L, _ = s.shape
+    s = s.float()
+    s_i = s.unsqueeze(2).expand(-1, -1, L, -1)
+    s_j = s.unsqueeze(1).expand(-1, L, -1, -1)
+    pair = torch.cat([s_i, s_j], dim=-1) @ p["weight"].t()
+    if p.get("bias") is not None:
+        pair = pair + p["bias"]
+    pm = None if mask is None else mask.float().unsqueeze(1) * mask.float().unsqueeze(2)
+    return pair, pm
+
+
 def make_transition_params(c_p: int, n: int, gen: torch.Generator, ln_random: bool = True,
                            bias_random: bool = True) -> Params:
     """Parameters of PairTransition (pair_transform.py:72-76), in module order. linear_2 is
