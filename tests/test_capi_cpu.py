@@ -108,3 +108,34 @@ def test_invalid_arguments_are_rejected(lib):
     rc = lib.gtk_trimul_finish(ctypes.c_void_p(256), ctypes.c_void_p(256), 16, 0.0, ctypes.c_void_p(256),
                                ctypes.c_void_p(256), 0, 1, 16, 16, None, None)
     assert rc == -1
+
+
+def test_transition_entry_points(lib):
+    assert lib.gtk_transition_packed_bytes(128, 4) > 2 * 128 * 512 * 2
+    assert lib.gtk_transition_packed_bytes(64, 4) == 0
+    assert lib.gtk_transition_workspace_bytes(2, 10, 128, 4) == 2 * 10 * 10 * 512 * 2
+    assert lib.gtk_transition_workspace_bytes(1, 10, 128, 2) == 0
+    # unsupported width, then a NULL pair tensor, then a short workspace: all before any launch
+    assert lib.gtk_transition_forward(None, None, None, None, 0, None, 0, 1, 16, 96, 4, None, None) == -2
+    assert lib.gtk_transition_forward(None, None, None, None, 0, None, 0, 1, 16, 128, 4, None, None) == -1
+    p = ctypes.c_void_p(1 << 20)
+    rc = lib.gtk_transition_forward(p, None, p, p, 1, p, 100, 1, 16, 128, 4, None, None)
+    assert rc == -4 and b"workspace" in lib.gtk_last_error_string()
+    assert lib.gtk_transition_pack(None, 128, 4, p, 1 << 20, None) == -1
+
+
+def test_pair_embed_entry_points(lib):
+    assert lib.gtk_pair_embed_workspace_bytes(2, 10, 128) == 2 * 2 * 10 * 128 * 4
+    assert lib.gtk_pair_embed_workspace_bytes(1, 10, 64) == 0
+    p = ctypes.c_void_p(1 << 20)
+    ws = lib.gtk_pair_embed_workspace_bytes(1, 16, 128)
+    # c_p other than 128
+    assert lib.gtk_pair_embed(p, None, p, None, p, None, p, ws, 1, 16, 16, 0, 32, 64, None) == -2
+    # a row shard that runs past N
+    assert lib.gtk_pair_embed(p, None, p, None, p, None, p, ws, 1, 16, 8, 12, 32, 128, None) == -1
+    # workspace too small
+    rc = lib.gtk_pair_embed(p, None, p, None, p, None, p, ws - 4, 1, 16, 16, 0, 32, 128, None)
+    assert rc == -4 and b"workspace" in lib.gtk_last_error_string()
+    # misaligned mask
+    assert lib.gtk_pair_embed(p, ctypes.c_void_p((1 << 20) + 2), p, None, p, None, p, ws, 1, 16, 16, 0, 32, 128,
+                              None) == -3
