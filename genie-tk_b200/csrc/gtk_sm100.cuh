@@ -70,6 +70,18 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// Arrive on `bar` only once `dep` is available. Use it to release a buffer the thread has
+// just read with shared-memory loads: pass a value computed from every loaded element. An
+// arrive issued right after the loads can complete while some of them are still in flight,
+// and a producer that refills the buffer on that signal (a TMA load) would then overwrite
+// data not yet read. The opaque zero (IEEE rules keep dep * 0 from being folded; NaN and
+// infinities convert to 0) puts a true data dependency between the loads' consumers and
+// the arrive.
+__device__ __forceinline__ void mbar_arrive_after(uint64_t* bar, float dep) {
+  const int zero = __float2int_rz(dep * 0.0f);
+  mbar_arrive(reinterpret_cast<uint64_t*>(reinterpret_cast<char*>(bar) + zero));
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity) {
   uint32_t ok;
   asm volatile(

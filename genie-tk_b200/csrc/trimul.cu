@@ -236,7 +236,13 @@ __global__ void __launch_bounds__(k1::kThreads, 1)
           v[q * 32 + ch * 4 + 2] = t.z;
           v[q * 32 + ch * 4 + 3] = t.w;
         }
-      mbar_arrive(&bars->z_empty);  // the z tile may be refilled
+      // the z tile may be refilled once every loaded value has been consumed (see
+      // mbar_arrive_after): the local sum reads all 64 of them
+      float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < 64; ++c) s4[c & 3] += v[c];
+      float sum = (s4[0] + s4[1]) + (s4[2] + s4[3]);
+      mbar_arrive_after(&bars->z_empty, sum);
       if (warp == 0) {
         // thread 0: refill z with the next tile once every producer has read this one
         bool w = true;
@@ -250,10 +256,6 @@ __global__ void __launch_bounds__(k1::kThreads, 1)
         ok = __all_sync(0xffffffffu, w);
         if (!ok) break;
       }
-      float s4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int c = 0; c < 64; ++c) s4[c & 3] += v[c];
-      float sum = (s4[0] + s4[1]) + (s4[2] + s4[3]);
       sum += __shfl_xor_sync(0xffffffffu, sum, 1);
       const float mean = sum * (1.f / 128.f);
       float q4[4] = {0.f, 0.f, 0.f, 0.f};
@@ -743,11 +745,13 @@ __global__ void __launch_bounds__(k2e::kThreads, 1)
           v[q * 32 + ch * 4 + 2] = t.z;
           v[q * 32 + ch * 4 + 3] = t.w;
         }
-      mbar_arrive(&bars->z_read);
       float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < 64; ++c) s4[c & 3] += v[c];
       float sum = (s4[0] + s4[1]) + (s4[2] + s4[3]);
+      // the tile is released (A is written over it, the next z half is loaded into it) once
+      // every loaded value has been consumed, see mbar_arrive_after
+      mbar_arrive_after(&bars->z_read, sum);
       sum += __shfl_xor_sync(0xffffffffu, sum, 1);
       const float mean = sum * (1.f / 128.f);
       float q4[4] = {0.f, 0.f, 0.f, 0.f};
