@@ -944,8 +944,8 @@ __global__ void __launch_bounds__(k2e::kThreads, 1)
         a1[c & 3] += xv;
         a2[c & 3] = fmaf(xv, xv, a2[c & 3]);
       }
-      mbar_arrive(&bars->x_empty);
       const float s1 = (a1[0] + a1[1]) + (a1[2] + a1[3]), s2 = (a2[0] + a2[1]) + (a2[2] + a2[3]);
+      mbar_arrive_after(&bars->x_empty, s1 + s2);  // the x tile may be reloaded: its values are consumed
       const float d1 = s1 * (1.f / 128.f);
       const float mu_x = x0 + d1;
       const float var = fmaxf(s2 * (1.f / 128.f) - d1 * d1, 0.f);
