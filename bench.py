@@ -476,7 +476,7 @@ def run_sharded(args, rank, world, device):
     z0 = z_host.to(device)
     z = torch.empty_like(z0)
     stack = make_stack(L, device)
-    so = TimedStageOps(CudaStageOps(device))
+    so = TimedStageOps(CudaStageOps(device, push=args.push))
     shard = ShardedTrianglePairStack(stack, world, rank, stage_ops=so, trimul_exchange=args.trimul_exchange,
                                      exchange=args.exchange, k1_direct=args.k1_direct)
     if args.exchange == "peer":
@@ -582,6 +582,7 @@ def run_sharded(args, rank, world, device):
                        "parallelism": f"row-sharded over i, {world} ranks x {R} rows (NCCL)",
                        "trimul_exchange": shard.trimul_exchange, "exchange": args.exchange,
                        "k1_direct": bool(args.k1_direct and args.exchange == "peer" and shard.trimul_exchange == "channels"),
+                       "push": args.push,
                        "l2": "inputs larger than L2 (each shard is >= 64 MB fp32); no flush"},
             "stack_tflops": round(stack_tflops, 1),
             "stack_frac_of_bf16_peak": round(stack_tflops / peaks["bf16_tflops"] / world, 4),
@@ -722,6 +723,8 @@ def main():
     ap.add_argument("--op", default="stack", choices=["stack", "transition", "embed"],
                     help="stack: the BASELINE workload (default); transition / embed: the pair-transition or "
                          "pair-embedding kernels alone")
+    ap.add_argument("--push", default="kernel", choices=["kernel", "dma"],
+                    help="peer exchanges: slab pushes with the push kernel or the copy engines")
     ap.add_argument("--k1-direct", action="store_true",
                     help="peer exchanges, channel mode: K1 writes the a/b channel shards straight into the "
                          "peers' buffers instead of a separate push")

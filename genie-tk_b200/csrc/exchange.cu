@@ -162,6 +162,18 @@ int gtk_copy_2d(void* dst, int64_t dpitch, const void* src, int64_t spitch, int6
   return gtk_copy_3d(dst, dpitch, 0, src, spitch, 0, width, height, 1, stream);
 }
 
+int gtk_copy_2d_dma(void* dst, int64_t dpitch, const void* src, int64_t spitch, int64_t width, int64_t height,
+                    void* stream) {
+  if (!dst || !src || width < 0 || height < 0 || dpitch < width || spitch < width)
+    return fail(GTK_ERR_INVALID_ARG, "copy_2d_dma: bad arguments");
+  if (width == 0 || height == 0) return GTK_OK;
+  const cudaError_t e = cudaMemcpy2DAsync(dst, static_cast<size_t>(dpitch), src, static_cast<size_t>(spitch),
+                                          static_cast<size_t>(width), static_cast<size_t>(height), cudaMemcpyDefault,
+                                          static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(GTK_ERR_CUDA, std::string("copy_2d_dma: ") + cudaGetErrorString(e));
+  return GTK_OK;
+}
+
 int gtk_peer_alloc(size_t bytes, void** ptr, void* handle) {
   if (!ptr || !handle || bytes == 0) return fail(GTK_ERR_INVALID_ARG, "peer_alloc: bad arguments");
   if (int e = check_device()) return e;

@@ -74,6 +74,7 @@ _SIGNATURES = {
     "gtk_triatt_workspace_offsets": (c_int, [c_i64, c_i64, c_i64, ctypes.POINTER(c_i64)]),
     "gtk_copy_2d": (c_int, [c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_vp]),
     "gtk_copy_3d": (c_int, [c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp]),
+    "gtk_copy_2d_dma": (c_int, [c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_vp]),
     "gtk_pair_transpose_pack": (c_int, [c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp]),
     "gtk_peer_alloc": (c_int, [c_size, ctypes.POINTER(c_vp), c_vp]),
     "gtk_peer_free": (c_int, [c_vp]),

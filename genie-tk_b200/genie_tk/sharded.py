@@ -72,10 +72,17 @@ class ShardSpec:
 
 
 class CudaStageOps:
-    """The stage computations on this rank's GPU, through the C ABI."""
+    """The stage computations on this rank's GPU, through the C ABI.
 
-    def __init__(self, device: torch.device):
+    ``push``: "kernel" moves the peer pushes of strided slabs (``push_3d``) with the push
+    kernel; "dma" issues one ``cudaMemcpy2DAsync`` per destination rank on the same stream
+    (the copy engines, no SM time). The pair-grid transposes always use their kernel."""
+
+    def __init__(self, device: torch.device, push: str = "kernel"):
+        if push not in ("kernel", "dma"):
+            raise ValueError(f"push must be 'kernel' or 'dma', got {push!r}")
         self.device = device
+        self.push = push
         self.lib = ops._lib.load()
         self.status = ops.status_buffer(device)
 
@@ -142,6 +149,13 @@ class CudaStageOps:
                                                       self._s()), "gtk_trimul_project_sharded")
 
     def push_3d(self, dst: "PeerBuffer", doff, dpitch, src, spitch, sslab, width, height):
+        if self.push == "dma":
+            base = src.data_ptr()
+            for k, addr in enumerate(dst.addrs):
+                self._chk(self.lib.gtk_copy_2d_dma(ctypes.c_void_p(addr + doff), dpitch,
+                                                   ctypes.c_void_p(base + k * sslab), spitch, width, height,
+                                                   self._s()), "gtk_copy_2d_dma")
+            return
         self._chk(self.lib.gtk_push_3d(ops._ptr(dst.ptrs), dst.ptrs.numel(), doff, dpitch, ops._ptr(src), spitch, sslab,
                                        width, height, self._s()), "gtk_push_3d")
 
@@ -191,7 +205,8 @@ class ShardedTrianglePairStack:
     """
 
     def __init__(self, stack: TrianglePairStack, world: int, rank: int, stage_ops=None,
-                 trimul_exchange: str = "auto", exchange: str = "nccl", k1_direct: bool = False):
+                 trimul_exchange: str = "auto", exchange: str = "nccl", k1_direct: bool = False,
+                 push: str = "kernel"):
         if trimul_exchange not in ("auto", "gather", "channels"):
             raise ValueError(f"trimul_exchange must be auto, gather or channels, not {trimul_exchange!r}")
         if exchange not in ("nccl", "peer"):
@@ -209,6 +224,7 @@ class ShardedTrianglePairStack:
         # epilogue's 32-byte stores spread over the peers use NVLink less well than one bulk
         # push, so it is off by default.
         self.k1_direct = k1_direct
+        self.push = push  # slab pushes of the default stage ops: "kernel" or "dma" (CudaStageOps)
         self._key = None
         self._buf: Dict[str, Tensor] = {}
         self._peer: Dict[str, PeerBuffer] = {}
@@ -250,7 +266,7 @@ class ShardedTrianglePairStack:
     def prepare(self, B: int, N: int, device: torch.device) -> ShardSpec:
         spec = ShardSpec(B, N, self.world, self.rank)
         if self.stage_ops is None:
-            self.stage_ops = CudaStageOps(device)
+            self.stage_ops = CudaStageOps(device, push=self.push)
         if self._key == (B, N):
             return spec
         if self.exchange == "peer":
@@ -281,7 +297,7 @@ class ShardedTrianglePairStack:
             raise RuntimeError("connect() is for exchange='peer'")
         spec = ShardSpec(B, N, self.world, self.rank)
         if self.stage_ops is None:
-            self.stage_ops = CudaStageOps(device)
+            self.stage_ops = CudaStageOps(device, push=self.push)
         self.close()
         local, recv, lay = self._sizes(spec)
         lib = ops._lib.load()
@@ -576,7 +592,7 @@ def connect_emulated(shards: List["ShardedTrianglePairStack"], B: int, N: int, d
         spec = ShardSpec(B, N, P, s.rank)
         spec0 = spec0 or spec
         if s.stage_ops is None:
-            s.stage_ops = CudaStageOps(device)
+            s.stage_ops = CudaStageOps(device, push=s.push)
         local, recv, lay = s._sizes(spec)
         so = s.stage_ops
         s._buf = {k: so.alloc(_round256(v)) for k, v in {**local, **recv}.items()}
@@ -610,7 +626,8 @@ class TimedStageOps:
             return fn
 
         def wrapped(*a, **k):
-            self.launches += 1
+            if not (name == "push_3d" and getattr(self.inner, "push", "kernel") == "dma"):
+                self.launches += 1  # copy-engine pushes launch no kernel
             if self.hook:
                 self.hook(name)
             r = fn(*a, **k)

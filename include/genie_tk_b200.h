@@ -237,6 +237,11 @@ GTK_API int gtk_triatt_finish(int starting, const float* z, const void* packed, 
  * Width, pitches and both pointers must be multiples of 16 bytes. */
 GTK_API int gtk_copy_2d(void* dst, int64_t dpitch, const void* src, int64_t spitch, int64_t width, int64_t height,
                         void* stream);
+/* The same 2D copy on the GPU's copy engines (cudaMemcpy2DAsync on `stream`) instead of
+ * a kernel: no SM time. dst may be a peer GPU's memory mapped into this process (CUDA
+ * IPC); the copy is stream-ordered like a kernel. */
+GTK_API int gtk_copy_2d_dma(void* dst, int64_t dpitch, const void* src, int64_t spitch, int64_t width, int64_t height,
+                            void* stream);
 /* `depth` slabs of the 2D copy above; slab k starts at dst + k*dslab and src + k*sslab
  * (slab strides are multiples of 16 bytes as well). */
 GTK_API int gtk_copy_3d(void* dst, int64_t dpitch, int64_t dslab, const void* src, int64_t spitch, int64_t sslab,

@@ -193,7 +193,8 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _nccl_rank(rank, world, port, z, mask, params, q, exchange="nccl", trimul_exchange="auto", k1_direct=False):
+def _nccl_rank(rank, world, port, z, mask, params, q, exchange="nccl", trimul_exchange="auto", k1_direct=False,
+               push="kernel"):
     import datetime
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -209,7 +210,7 @@ def _nccl_rank(rank, world, port, z, mask, params, q, exchange="nccl", trimul_ex
         R = N // world
         zl = z[:, rank * R:(rank + 1) * R].contiguous().to(dev)
         sh = ShardedTrianglePairStack(_stack(params, dev), world, rank, exchange=exchange,
-                                      trimul_exchange=trimul_exchange, k1_direct=k1_direct)
+                                      trimul_exchange=trimul_exchange, k1_direct=k1_direct, push=push)
         if exchange == "peer":
             sh.connect(None, 1, N, dev)
         sh.forward_(zl, mask.to(dev))
@@ -222,9 +223,10 @@ def _nccl_rank(rank, world, port, z, mask, params, q, exchange="nccl", trimul_ex
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("exchange,trimul_exchange,k1_direct", [("nccl", "auto", False), ("peer", "auto", False),
-                                                                ("peer", "channels", False), ("peer", "channels", True)])
-def test_two_ranks_match_single_gpu(exchange, trimul_exchange, k1_direct):
+@pytest.mark.parametrize("exchange,trimul_exchange,k1_direct,push", [
+    ("nccl", "auto", False, "kernel"), ("peer", "auto", False, "kernel"), ("peer", "channels", False, "kernel"),
+    ("peer", "channels", True, "kernel"), ("peer", "auto", False, "dma"), ("peer", "channels", False, "dma")])
+def test_two_ranks_match_single_gpu(exchange, trimul_exchange, k1_direct, push):
     require_gpu()
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
@@ -234,7 +236,7 @@ def test_two_ranks_match_single_gpu(exchange, trimul_exchange, k1_direct):
     q = ctx.Queue()
     port = _free_port()
     procs = [ctx.Process(target=_nccl_rank, args=(r, world, port, z, mask, params, q, exchange, trimul_exchange,
-                                                  k1_direct))
+                                                  k1_direct, push))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -250,3 +252,24 @@ def test_two_ranks_match_single_gpu(exchange, trimul_exchange, k1_direct):
     assert float((got - full).abs().max()) <= 1e-3
     ref = O.stack_forward(z, mask, params, no_heads=4)
     assert_parity(got, ref, what="two NCCL ranks")
+
+
+def test_dma_push_matches_push_kernel():
+    """The copy-engine slab push writes exactly what the push kernel writes (ranks emulated
+    on one GPU: the destination buffers are local allocations)."""
+    dev = require_gpu()
+    from genie_tk.sharded import CudaStageOps, PeerBuffer
+    P, height, width, spitch, dpitch, doff = 3, 20, 96, 160, 128, 64
+    sslab = height * spitch
+    gen = torch.Generator().manual_seed(2)
+    src = torch.randint(0, 256, (P * sslab,), generator=gen, dtype=torch.uint8).to(dev)
+    outs = {}
+    for mode in ("kernel", "dma"):
+        bufs = [torch.zeros(doff + height * dpitch, dtype=torch.uint8, device=dev) for _ in range(P)]
+        peer = PeerBuffer(bufs[0], [b.data_ptr() for b in bufs], dev, bufs)
+        CudaStageOps(dev, push=mode).push_3d(peer, doff, dpitch, src, spitch, sslab, width, height)
+        torch.cuda.synchronize()
+        outs[mode] = torch.stack(bufs).cpu()
+    assert torch.equal(outs["kernel"], outs["dma"])
+    ref = src.cpu().view(P, height, spitch)[:, :, :width]
+    assert torch.equal(outs["dma"][:, doff:].view(P, height, dpitch)[:, :, :width], ref)
