@@ -46,3 +46,21 @@ def test_stack_matches_oracle_and_graph_replay(N, n_layers):
     torch.cuda.synchronize()
     assert torch.equal(out2, out)
     assert_status_clean(dev)
+
+
+def test_bench_layer_at_full_size_matches_oracle():
+    """The benchmark's workload at its real size: the first layer of the cfg5 stack (B = 1,
+    N = 1024, seeded weights and input of BASELINE config 5) against the fp32 oracle
+    (run on the GPU with fp32 matmuls)."""
+    dev = require_gpu()
+    z, mask, params = O.config_inputs(5, N=1024)
+    layers = params[:1]
+    st = _stack(layers, dev)
+    zd, md = z.to(dev), mask.to(dev)
+    out = torch.empty_like(zd)
+    st.forward_into(zd, out, md)
+    torch.cuda.synchronize()
+    assert_status_clean(dev)
+    ref = O.stack_forward(zd, md, [{k: to_dev(v, dev) for k, v in lp.items()} for lp in layers], no_heads=4,
+                          chunk_rows=32)
+    assert_parity(out, ref, what="cfg5 layer N=1024")

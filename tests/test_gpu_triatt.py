@@ -79,7 +79,7 @@ def test_module_matches_reference_golden(name):
 
 
 @pytest.mark.parametrize("cfg,N,starting", [(3, 96, True), (4, 96, False), (3, 200, False), (4, 257, True),
-                                            (3, 512, True), (4, 384, False)])
+                                            (3, 512, True), (4, 384, False), (4, 768, False)])
 def test_config_matches_oracle(cfg, N, starting):
     dev = require_gpu()
     import genie_tk
