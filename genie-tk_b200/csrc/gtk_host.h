@@ -57,4 +57,10 @@ int make_weight_map(CUtensorMap* m, const void* base, int64_t rows, uint32_t box
 int check_ptr(const void* p, const char* name, uintptr_t align = 16);
 bool dims_ok(int64_t v, int64_t max_v = (int64_t(1) << 31) - 1);
 
+// Validate a public dropout descriptor (NULL = no dropout) for a [B, N, N] pair problem and
+// fill the kernels' DropArgs (defined in gtk_sm100.cuh). `transposed`: the kernel walks the
+// pair tensor as z^T (the ending-node attention).
+struct DropArgs;
+int drop_args(const gtk_dropout* d, int64_t B, int64_t N, bool transposed, DropArgs* out);
+
 }  // namespace gtk

@@ -112,6 +112,29 @@ struct CtaGuard {
   volatile uint32_t abort;  // set when any wait of this CTA ran out
 };
 
+// Channel dropout applied by a residual epilogue: one 128-bit keep vector per (batch,
+// residue t), bit c (word c / 32, bit c % 32) set when channel c is kept; kept channels
+// are multiplied by `scale`. In a kernel's own pair frame (row r, column j) the vector is
+// t = by_row ? r : j, at keep[b * ld + t].
+struct DropArgs {
+  const uint4* keep;
+  float scale;
+  int by_row;
+  int64_t ld;
+};
+
+// Keep vector of pair (b, r, j) of the kernel frame; all zero (drop) for a column past the
+// end of the row (that pair is never stored).
+__device__ __forceinline__ uint4 drop_keep(const DropArgs& d, int b, int r, int j, int n_cols) {
+  if (!d.by_row && j >= n_cols) return make_uint4(0u, 0u, 0u, 0u);
+  return __ldg(d.keep + static_cast<int64_t>(b) * d.ld + (d.by_row ? r : j));
+}
+
+// Word w of a keep vector (w = 0..3, a runtime index).
+__device__ __forceinline__ uint32_t drop_word(const uint4& k, int w) {
+  return w == 0 ? k.x : (w == 1 ? k.y : (w == 2 ? k.z : k.w));
+}
+
 // Bounded wait on the phase with the given parity. Returns false (after recording
 // `code` in *status and raising guard->abort) when the limit passes or when another
 // role of the CTA has already aborted.

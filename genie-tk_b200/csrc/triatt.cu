@@ -901,11 +901,14 @@ struct K4eBars {
 };
 static_assert(sizeof(K4eBars) <= 256, "K4e barrier block");
 
+// kDrop: the update is multiplied by the channel dropout `drop` before the residual add
+// (out = z + keep * scale * update); the plain instantiation ignores `drop`.
+template <bool kDrop>
 __global__ void __launch_bounds__(k4e::kThreads, 1)
     triatt_finish_kernel(const __grid_constant__ CUtensorMap og_map, const __grid_constant__ CUtensorMap w_map,
                          const __grid_constant__ CUtensorMap z_map, const __grid_constant__ CUtensorMap out_map,
                          const float* __restrict__ vec, int N, int rows, int add_residual, int n_jt,
-                         int n_tiles, uint32_t* status) {
+                         int n_tiles, uint32_t* status, const DropArgs drop) {
   using namespace k4e;
   extern __shared__ uint8_t dsmem[];
   uint8_t* smem = align1024(dsmem);
@@ -1024,6 +1027,8 @@ __global__ void __launch_bounds__(k4e::kThreads, 1)
       const int s = it & 1;
       const int jt = tile % n_jt, bi = tile / n_jt;
       const int i = bi % rows, b = bi / rows, j0 = jt * 128;
+      uint4 keep = make_uint4(0u, 0u, 0u, 0u);
+      if constexpr (kDrop) keep = drop_keep(drop, b, i, j0 + p, N);  // latency hidden under the wait
       ok = __all_sync(0xffffffffu, mbar_wait(&bars->d_full[s], (it >> 1) & 1, guard, status, kStatusTimeoutConsumer));
       if (!ok) break;
       tc_fence_after();
@@ -1037,11 +1042,19 @@ __global__ void __launch_bounds__(k4e::kThreads, 1)
         tmem_wait_ld();
         if (!ok) break;
         uint8_t* ob = smem + kO + sl * 16384;
+        const uint32_t kw = kDrop ? drop_word(keep, cc) : 0u;
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
           const int n = cc * 32 + q * 4;
           float4 o = make_float4(__uint_as_float(d[q * 4 + 0]) + sbo[n + 0], __uint_as_float(d[q * 4 + 1]) + sbo[n + 1],
                                  __uint_as_float(d[q * 4 + 2]) + sbo[n + 2], __uint_as_float(d[q * 4 + 3]) + sbo[n + 3]);
+          if constexpr (kDrop) {
+            const float sc = drop.scale;
+            o.x *= ((kw >> (q * 4 + 0)) & 1u) ? sc : 0.f;
+            o.y *= ((kw >> (q * 4 + 1)) & 1u) ? sc : 0.f;
+            o.z *= ((kw >> (q * 4 + 2)) & 1u) ? sc : 0.f;
+            o.w *= ((kw >> (q * 4 + 3)) & 1u) ? sc : 0.f;
+          }
           if (add_residual) {
             const float4 zv = lds_f4(ob + swz128(p, q));
             o.x += zv.x;
@@ -1268,8 +1281,14 @@ int gtk_triatt_core(int starting, const float* mask, void* workspace, int64_t B,
   return check_launch("triatt_core_kernel");
 }
 
-int gtk_triatt_finish(int starting, const float* z, const void* packed, void* workspace, float* out, int add_residual,
-                      int64_t B, int64_t rows, int64_t N, uint32_t* status, void* stream) {
+}  // extern "C"
+
+namespace gtk {
+
+// K4e launch; `drop` with a NULL keep array selects the plain instantiation.
+static int triatt_finish_launch(int starting, const float* z, const void* packed, void* workspace, float* out,
+                                int add_residual, int64_t B, int64_t rows, int64_t N, uint32_t* status, void* stream,
+                                const DropArgs& drop) {
   if (int e = rows_check("triatt_finish", starting, B, rows, N, 0)) return e;
   if (int e = check_ptr(out, "out")) return e;
   if (add_residual)
@@ -1288,23 +1307,62 @@ int gtk_triatt_finish(int starting, const float* z, const void* packed, void* wo
   if (int e = make_weight_map(&wm, pk + tapack::kW4, 128, 128)) return e;
   if (int e = make_pair_map(&zm, add_residual ? z : out, B, rows, N, !starting)) return e;
   if (int e = make_pair_map(&om, out, B, rows, N, !starting)) return e;
-  if (int e = ensure_smem(reinterpret_cast<const void*>(triatt_finish_kernel), k4e::kSmem)) return e;
+  const bool dropping = drop.keep != nullptr;
+  const void* kern = dropping ? reinterpret_cast<const void*>(triatt_finish_kernel<true>)
+                              : reinterpret_cast<const void*>(triatt_finish_kernel<false>);
+  if (int e = ensure_smem(kern, k4e::kSmem)) return e;
   const int grid = static_cast<int>(n_tiles < num_sms() ? n_tiles : num_sms());
-  triatt_finish_kernel<<<grid, k4e::kThreads, k4e::kSmem, static_cast<cudaStream_t>(stream)>>>(
-      am, wm, zm, om, reinterpret_cast<const float*>(pk + tapack::kVec), static_cast<int>(N), static_cast<int>(rows),
-      add_residual, static_cast<int>(n_jt), static_cast<int>(n_tiles), status);
+  const float* vec = reinterpret_cast<const float*>(pk + tapack::kVec);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dropping)
+    triatt_finish_kernel<true><<<grid, k4e::kThreads, k4e::kSmem, st>>>(
+        am, wm, zm, om, vec, static_cast<int>(N), static_cast<int>(rows), add_residual, static_cast<int>(n_jt),
+        static_cast<int>(n_tiles), status, drop);
+  else
+    triatt_finish_kernel<false><<<grid, k4e::kThreads, k4e::kSmem, st>>>(
+        am, wm, zm, om, vec, static_cast<int>(N), static_cast<int>(rows), add_residual, static_cast<int>(n_jt),
+        static_cast<int>(n_tiles), status, drop);
   return check_launch("triatt_finish_kernel");
 }
 
-int gtk_triatt_forward(int starting, const float* z, const float* mask, const void* packed, float* out,
-                       int add_residual, void* workspace, size_t workspace_bytes, int64_t B, int64_t N, int c_in,
-                       int c_hidden, int heads, float inf, uint32_t* status, void* stream) {
+static int triatt_forward_impl(int starting, const float* z, const float* mask, const void* packed, float* out,
+                               int add_residual, const DropArgs& drop, void* workspace, size_t workspace_bytes,
+                               int64_t B, int64_t N, int c_in, int c_hidden, int heads, float inf, uint32_t* status,
+                               void* stream) {
   if (int e = triatt_check(c_in, c_hidden, heads)) return e;
   if (!dims_ok(B, 65535) || !dims_ok(N, 65535)) return fail(GTK_ERR_INVALID_ARG, "triatt: bad B/N");
   if (workspace_bytes < triatt_layout(B, N, N).total) return fail(GTK_ERR_WORKSPACE, "triatt: workspace too small");
   if (int e = gtk_triatt_project(starting, z, packed, workspace, B, N, N, 0, status, stream)) return e;
   if (int e = gtk_triatt_core(starting, mask, workspace, B, N, N, 0, inf, status, stream)) return e;
-  return gtk_triatt_finish(starting, z, packed, workspace, out, add_residual, B, N, N, status, stream);
+  return triatt_finish_launch(starting, z, packed, workspace, out, add_residual, B, N, N, status, stream, drop);
+}
+
+}  // namespace gtk
+
+extern "C" {
+
+int gtk_triatt_finish(int starting, const float* z, const void* packed, void* workspace, float* out, int add_residual,
+                      int64_t B, int64_t rows, int64_t N, uint32_t* status, void* stream) {
+  return triatt_finish_launch(starting, z, packed, workspace, out, add_residual, B, rows, N, status, stream,
+                              DropArgs{});
+}
+
+int gtk_triatt_forward(int starting, const float* z, const float* mask, const void* packed, float* out,
+                       int add_residual, void* workspace, size_t workspace_bytes, int64_t B, int64_t N, int c_in,
+                       int c_hidden, int heads, float inf, uint32_t* status, void* stream) {
+  return triatt_forward_impl(starting, z, mask, packed, out, add_residual, DropArgs{}, workspace, workspace_bytes, B,
+                             N, c_in, c_hidden, heads, inf, status, stream);
+}
+
+int gtk_triatt_forward_dropout(int starting, const float* z, const float* mask, const void* packed, float* out,
+                               int add_residual, const gtk_dropout* dropout, void* workspace, size_t workspace_bytes,
+                               int64_t B, int64_t N, int c_in, int c_hidden, int heads, float inf, uint32_t* status,
+                               void* stream) {
+  DropArgs d{};
+  // K4e works in the problem's frame, which is z^T for the ending node.
+  if (int e = drop_args(dropout, B, N, /*transposed=*/!starting, &d)) return e;
+  return triatt_forward_impl(starting, z, mask, packed, out, add_residual, d, workspace, workspace_bytes, B, N, c_in,
+                             c_hidden, heads, inf, status, stream);
 }
 
 }  // extern "C"

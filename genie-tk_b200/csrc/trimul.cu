@@ -680,11 +680,14 @@ struct K2eBars {
 };
 static_assert(sizeof(K2eBars) <= 256, "K2e barrier block");
 
+// kDrop: the update is multiplied by the channel dropout `drop` before the residual add
+// (out = z + keep * scale * update); the plain instantiation ignores `drop`.
+template <bool kDrop>
 __global__ void __launch_bounds__(k2e::kThreads, 1)
     trimul_finish_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap x_map,
                          const __grid_constant__ CUtensorMap z_map, const __grid_constant__ CUtensorMap out_map,
                          const float* __restrict__ vec, int add_residual, float x_scale, int N, int rows, int n_jt,
-                         int n_tiles, uint32_t* status) {
+                         int n_tiles, uint32_t* status, const DropArgs drop) {
   using namespace k2e;
   extern __shared__ uint8_t dsmem[];
   uint8_t* smem = align1024(dsmem);
@@ -927,6 +930,11 @@ __global__ void __launch_bounds__(k2e::kThreads, 1)
     bool ok = true;
     for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++it) {
       const int s = it & 1;
+      uint4 keep = make_uint4(0u, 0u, 0u, 0u);
+      if constexpr (kDrop) {  // issued before the waits so that its latency hides under them
+        const int jt = tile % n_jt, rb = tile / n_jt;
+        keep = drop_keep(drop, rb / rows, rb % rows, jt * 128 + p, N);
+      }
       bool w = mbar_wait(&bars->x_full, it & 1, guard, status, kStatusTimeoutConsumer);
       w = w && mbar_wait(&bars->d_full[s], (it >> 1) & 1, guard, status, kStatusTimeoutConsumer);
       ok = __all_sync(0xffffffffu, w);
@@ -962,6 +970,7 @@ __global__ void __launch_bounds__(k2e::kThreads, 1)
         tmem_wait_ld();
         if (!ok) break;
         uint8_t* ob = smem + kO + sl * 16384;
+        const uint32_t kw = kDrop ? drop_word(keep, cc) : 0u;
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
           float o[4];
@@ -978,7 +987,12 @@ __global__ void __launch_bounds__(k2e::kThreads, 1)
             const int t = q * 4 + e;
             const float gate = fmaf(0.5f, tanh_approx(__uint_as_float(g[t]) + bgv[e]), 0.5f);
             const float y = fmaf(rstd_x, fmaf(-mu_x, uv[e], __uint_as_float(u[t])), vv[e]);
-            o[e] = fmaf(y, gate, rq[e]);
+            if constexpr (kDrop) {
+              const float ds = ((kw >> t) & 1u) ? drop.scale : 0.f;
+              o[e] = fmaf(y * gate, ds, rq[e]);
+            } else {
+              o[e] = fmaf(y, gate, rq[e]);
+            }
           }
           *reinterpret_cast<float4*>(ob + swz128(p, q)) = make_float4(o[0], o[1], o[2], o[3]);
         }
@@ -1164,9 +1178,14 @@ int gtk_trimul_contract(int outgoing, const void* a_planes, const void* b_planes
   return check_launch("trimul_contract_kernel");
 }
 
-int gtk_trimul_finish(const float* z, const void* x_planes, int64_t ldx, float x_scale, const void* packed,
-                      float* out, int add_residual, int64_t B, int64_t rows, int64_t N, uint32_t* status,
-                      void* stream) {
+}  // extern "C"
+
+namespace gtk {
+
+// K2e launch; `drop` with a NULL keep array selects the plain instantiation.
+static int trimul_finish_launch(const float* z, const void* x_planes, int64_t ldx, float x_scale, const void* packed,
+                                float* out, int add_residual, int64_t B, int64_t rows, int64_t N, uint32_t* status,
+                                void* stream, const DropArgs& drop) {
   if (!dims_ok(B, 65535) || !dims_ok(rows, 65535) || !dims_ok(N, 1 << 20))
     return fail(GTK_ERR_INVALID_ARG, "trimul_finish: bad B/rows/N");
   if (ldx < N || ldx % 8) return fail(GTK_ERR_INVALID_ARG, "trimul_finish: bad plane pitch");
@@ -1185,17 +1204,27 @@ int gtk_trimul_finish(const float* z, const void* x_planes, int64_t ldx, float x
   if (int e = make_plane_map(&xm, x_planes, B, rows, 128, N, ldx, 64, 128, 1, 128)) return e;
   if (int e = make_pair_map(&zm, z, B, rows, N, false)) return e;
   if (int e = make_pair_map(&om, out, B, rows, N, false)) return e;
-  if (int e = ensure_smem(reinterpret_cast<const void*>(trimul_finish_kernel), k2e::kSmem)) return e;
+  const bool dropping = drop.keep != nullptr;
+  const void* kern = dropping ? reinterpret_cast<const void*>(trimul_finish_kernel<true>)
+                              : reinterpret_cast<const void*>(trimul_finish_kernel<false>);
+  if (int e = ensure_smem(kern, k2e::kSmem)) return e;
   const int grid = static_cast<int>(n_tiles < num_sms() ? n_tiles : num_sms());
-  trimul_finish_kernel<<<grid, k2e::kThreads, k2e::kSmem, static_cast<cudaStream_t>(stream)>>>(
-      wm, xm, zm, om, reinterpret_cast<const float*>(pk + tmpack::kVec), add_residual, x_scale, static_cast<int>(N),
-      static_cast<int>(rows), static_cast<int>(n_jt), static_cast<int>(n_tiles), status);
+  const float* vec = reinterpret_cast<const float*>(pk + tmpack::kVec);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dropping)
+    trimul_finish_kernel<true><<<grid, k2e::kThreads, k2e::kSmem, st>>>(
+        wm, xm, zm, om, vec, add_residual, x_scale, static_cast<int>(N), static_cast<int>(rows),
+        static_cast<int>(n_jt), static_cast<int>(n_tiles), status, drop);
+  else
+    trimul_finish_kernel<false><<<grid, k2e::kThreads, k2e::kSmem, st>>>(
+        wm, xm, zm, om, vec, add_residual, x_scale, static_cast<int>(N), static_cast<int>(rows),
+        static_cast<int>(n_jt), static_cast<int>(n_tiles), status, drop);
   return check_launch("trimul_finish_kernel");
 }
 
-int gtk_trimul_forward(int outgoing, const float* z, const float* mask, const void* packed, float* out,
-                       int add_residual, void* workspace, size_t workspace_bytes, int64_t B, int64_t N, int c_z,
-                       int c_hidden, uint32_t* status, void* stream) {
+static int trimul_forward_impl(int outgoing, const float* z, const float* mask, const void* packed, float* out,
+                               int add_residual, const DropArgs& drop, void* workspace, size_t workspace_bytes,
+                               int64_t B, int64_t N, int c_z, int c_hidden, uint32_t* status, void* stream) {
   if (c_z != 128 || c_hidden != 128)
     return fail(GTK_ERR_UNSUPPORTED, "trimul: only c_z = c_hidden = 128 is implemented");
   if (!dims_ok(B, 65535) || !dims_ok(N, 65535)) return fail(GTK_ERR_INVALID_ARG, "trimul: bad B/N");
@@ -1211,7 +1240,35 @@ int gtk_trimul_forward(int outgoing, const float* z, const float* mask, const vo
   if (int e = gtk_trimul_project(z, mask, packed, ap, bp, ld, B, N, N, status, stream)) return e;
   const float xs = 1.0f / static_cast<float>(N);
   if (int e = gtk_trimul_contract(outgoing, ap, bp, xp, B, 128, N, N, N, ld, ld, ld, xs, status, stream)) return e;
-  return gtk_trimul_finish(z, xp, ld, xs, packed, out, add_residual, B, N, N, status, stream);
+  return trimul_finish_launch(z, xp, ld, xs, packed, out, add_residual, B, N, N, status, stream, drop);
+}
+
+}  // namespace gtk
+
+extern "C" {
+
+int gtk_trimul_finish(const float* z, const void* x_planes, int64_t ldx, float x_scale, const void* packed,
+                      float* out, int add_residual, int64_t B, int64_t rows, int64_t N, uint32_t* status,
+                      void* stream) {
+  return trimul_finish_launch(z, x_planes, ldx, x_scale, packed, out, add_residual, B, rows, N, status, stream,
+                              DropArgs{});
+}
+
+int gtk_trimul_forward(int outgoing, const float* z, const float* mask, const void* packed, float* out,
+                       int add_residual, void* workspace, size_t workspace_bytes, int64_t B, int64_t N, int c_z,
+                       int c_hidden, uint32_t* status, void* stream) {
+  return trimul_forward_impl(outgoing, z, mask, packed, out, add_residual, DropArgs{}, workspace, workspace_bytes, B,
+                             N, c_z, c_hidden, status, stream);
+}
+
+int gtk_trimul_forward_dropout(int outgoing, const float* z, const float* mask, const void* packed, float* out,
+                               int add_residual, const gtk_dropout* dropout, void* workspace, size_t workspace_bytes,
+                               int64_t B, int64_t N, int c_z, int c_hidden, uint32_t* status, void* stream) {
+  DropArgs d{};
+  // The update's pair frame is z's own: DropoutRowwise's vector is the column j.
+  if (int e = drop_args(dropout, B, N, /*transposed=*/false, &d)) return e;
+  return trimul_forward_impl(outgoing, z, mask, packed, out, add_residual, d, workspace, workspace_bytes, B, N, c_z,
+                             c_hidden, status, stream);
 }
 
 int gtk_trimul_forward_noalloc(int outgoing, const float* z, const float* mask, const void* packed, float* out,

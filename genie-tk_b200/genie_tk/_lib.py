@@ -44,6 +44,12 @@ class TransitionParams(ctypes.Structure):
     _fields_ = [(name, c_vp) for name in ("ln_w", "ln_b", "w1", "b1", "w2", "b2")]
 
 
+class Dropout(ctypes.Structure):
+    """Mirror of ``gtk_dropout`` (include/genie_tk_b200.h)."""
+
+    _fields_ = [("keep_bits", c_vp), ("scale", ctypes.c_float), ("shared_across_rows", c_int)]
+
+
 # name -> (restype, argtypes)
 _SIGNATURES = {
     "gtk_version": (c_int, []),
@@ -91,6 +97,12 @@ _SIGNATURES = {
     "gtk_pair_embed_workspace_bytes": (c_size, [c_i64, c_i64, c_int]),
     "gtk_pair_embed": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_size, c_i64, c_i64, c_i64, c_i64, c_int,
                                c_int, c_vp]),
+    "gtk_dropout_keep_bits_philox": (c_int, [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_double, c_i64, c_vp, c_vp]),
+    "gtk_dropout_pack_keep_bits": (c_int, [c_vp, c_i64, c_vp, c_vp]),
+    "gtk_trimul_forward_dropout": (c_int, [c_int, c_vp, c_vp, c_vp, c_vp, c_int, ctypes.POINTER(Dropout), c_vp, c_size,
+                                           c_i64, c_i64, c_int, c_int, c_vp, c_vp]),
+    "gtk_triatt_forward_dropout": (c_int, [c_int, c_vp, c_vp, c_vp, c_vp, c_int, ctypes.POINTER(Dropout), c_vp, c_size,
+                                           c_i64, c_i64, c_int, c_int, c_int, ctypes.c_float, c_vp, c_vp]),
 }
 
 

@@ -15,11 +15,14 @@ kernels fuse the projections.
   genie_tk::triatt_residual_(z, mask, packed, starting, inf)   z += update, in place
   genie_tk::transition_forward(z, packed) -> update            the pair transition
   genie_tk::transition_residual_(z, mask, packed)              z = (z + update) * mask, in place
+  genie_tk::trimul_residual_dropout_(z, mask, packed, outgoing, keep_bits, scale, shared_across_rows)
+  genie_tk::triatt_residual_dropout_(z, mask, packed, starting, inf, keep_bits, scale, shared_across_rows)
+                                                               z += dropout(update), in place
 
 ``z`` is ``[B, N, N, 128]`` (any float dtype; fp32 in place), ``mask`` ``[B, N, N]`` or
 None, ``packed`` the uint8 buffer of ``ops.pack_trimul`` / ``ops.pack_triatt`` /
-``ops.pack_transition``. No
-operator has an autograd formula: the kernels are forward-only.
+``ops.pack_transition``; ``keep_bits`` the int32 [B, N, 4] keep bits of an
+``ops.DropoutMask``. No operator has an autograd formula: the kernels are forward-only.
 """
 
 from __future__ import annotations
@@ -95,4 +98,30 @@ def transition_residual_(z: Tensor, mask: Optional[Tensor], packed: Tensor) -> N
 
 @transition_residual_.register_fake
 def _transition_residual_fake(z, mask, packed):
+    return None
+
+
+@torch.library.custom_op("genie_tk::trimul_residual_dropout_", mutates_args=("z",))
+def trimul_residual_dropout_(z: Tensor, mask: Optional[Tensor], packed: Tensor, outgoing: bool, keep_bits: Tensor,
+                             scale: float, shared_across_rows: bool) -> None:
+    """z += dropout(update of the triangle multiplicative block), in place (z fp32 contiguous)."""
+    ops.trimul_forward(z, mask, packed, outgoing, out=z, add_residual=True,
+                       dropout=ops.DropoutMask(keep_bits, scale, shared_across_rows))
+
+
+@trimul_residual_dropout_.register_fake
+def _trimul_residual_dropout_fake(z, mask, packed, outgoing, keep_bits, scale, shared_across_rows):
+    return None
+
+
+@torch.library.custom_op("genie_tk::triatt_residual_dropout_", mutates_args=("z",))
+def triatt_residual_dropout_(z: Tensor, mask: Optional[Tensor], packed: Tensor, starting: bool, inf: float,
+                             keep_bits: Tensor, scale: float, shared_across_rows: bool) -> None:
+    """z += dropout(update of triangle attention), in place (z fp32 contiguous)."""
+    ops.triatt_forward(z, mask, packed, starting, inf=inf, out=z, add_residual=True,
+                       dropout=ops.DropoutMask(keep_bits, scale, shared_across_rows))
+
+
+@triatt_residual_dropout_.register_fake
+def _triatt_residual_dropout_fake(z, mask, packed, starting, inf, keep_bits, scale, shared_across_rows):
     return None

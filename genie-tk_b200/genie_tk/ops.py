@@ -10,6 +10,7 @@ unsupported shape or a missing library raises.
 from __future__ import annotations
 
 import ctypes
+from dataclasses import dataclass
 from typing import Dict, Optional
 
 import torch
@@ -90,6 +91,62 @@ def prepare_pair(z: torch.Tensor, mask: Optional[torch.Tensor], c_expected: int)
 
 
 # --------------------------------------------------------------------------------------
+# Training-mode channel dropout of the residual updates (reference pair_transform.py:26-61)
+# --------------------------------------------------------------------------------------
+
+@dataclass
+class DropoutMask:
+    """A DropoutRowwise / DropoutColumnwise mask as the residual epilogues consume it.
+
+    ``keep_bits`` is int32 [B, N, 4] on the GPU: 128 bits per (b, residue), bit c set when
+    channel c is kept. ``shared_across_rows``: DropoutRowwise (the mask [B, 1, N, C] varies
+    with the column j), else DropoutColumnwise ([B, N, 1, C], varies with the row i). Kept
+    channels of the update are multiplied by ``scale``."""
+
+    keep_bits: torch.Tensor
+    scale: float
+    shared_across_rows: bool
+
+    def _struct(self, B: int, N: int):
+        kb = self.keep_bits
+        _require_cuda(kb, "keep_bits", torch.int32)
+        if tuple(kb.shape) != (B, N, 4) or not kb.is_contiguous():
+            raise ValueError(f"keep_bits must be a contiguous int32 [B, N, 4] = [{B}, {N}, 4], got {tuple(kb.shape)}")
+        return _lib.Dropout(ctypes.c_void_p(kb.data_ptr()), float(self.scale), int(bool(self.shared_across_rows)))
+
+
+def dropout_mask_from_multipliers(mult: torch.Tensor, shared_across_rows: bool, scale: float) -> DropoutMask:
+    """Pack a multiplier tensor drawn the reference's way (``nn.Dropout`` applied to ones of
+    shape [B, 1, N, C] for rows, [B, N, 1, C] for columns; 0 = dropped) into keep bits."""
+    lib = _lib.load()
+    _require_cuda(mult, "multipliers")
+    if mult.dim() != 4 or mult.shape[-1] != SUPPORTED_C or mult.shape[1 if shared_across_rows else 2] != 1:
+        want = "[B, 1, N, 128]" if shared_across_rows else "[B, N, 1, 128]"
+        raise ValueError(f"dropout multipliers must be {want}, got {tuple(mult.shape)}")
+    B = mult.shape[0]
+    N = mult.shape[2] if shared_across_rows else mult.shape[1]
+    m = mult.reshape(B * N, SUPPORTED_C).float().contiguous()
+    bits = torch.empty(B, N, 4, dtype=torch.int32, device=mult.device)
+    _lib.check(lib.gtk_dropout_pack_keep_bits(_ptr(m), B * N, _ptr(bits), _stream(mult.device)),
+               "gtk_dropout_pack_keep_bits")
+    bits._gtk_keepalive = m
+    return DropoutMask(bits, float(scale), bool(shared_across_rows))
+
+
+def dropout_mask_philox(B: int, N: int, p: float, seed: int, offset: int, shared_across_rows: bool,
+                        device: torch.device) -> DropoutMask:
+    """A dropout mask from the library's Philox4x32-10 generator (gtk_dropout_keep_bits_philox):
+    reproducible from (seed, offset) alone, independent of torch's generator state."""
+    lib = _lib.load()
+    if not 0.0 <= p < 1.0:
+        raise ValueError("dropout probability must be in [0, 1)")
+    bits = torch.empty(B, N, 4, dtype=torch.int32, device=device)
+    _lib.check(lib.gtk_dropout_keep_bits_philox(int(seed) & (2**64 - 1), int(offset) & (2**64 - 1), float(p), B * N,
+                                                _ptr(bits), _stream(bits.device)), "gtk_dropout_keep_bits_philox")
+    return DropoutMask(bits, 1.0 / (1.0 - p), bool(shared_across_rows))
+
+
+# --------------------------------------------------------------------------------------
 # Triangle multiplicative update
 # --------------------------------------------------------------------------------------
 
@@ -119,8 +176,10 @@ def pack_trimul(params: Dict[str, torch.Tensor], device: torch.device) -> torch.
 
 
 def trimul_forward(z: torch.Tensor, mask: Optional[torch.Tensor], packed: torch.Tensor, outgoing: bool,
-                   out: Optional[torch.Tensor] = None, add_residual: bool = False) -> torch.Tensor:
-    """update (or z + update) of the triangle multiplicative block; fp32 [B, N, N, 128]."""
+                   out: Optional[torch.Tensor] = None, add_residual: bool = False,
+                   dropout: Optional[DropoutMask] = None) -> torch.Tensor:
+    """update (or z + update) of the triangle multiplicative block; fp32 [B, N, N, 128].
+    ``dropout`` multiplies the update by a channel dropout mask inside the epilogue."""
     lib = _lib.load()
     zf, mf = prepare_pair(z, mask, SUPPORTED_C)
     B, N = zf.shape[0], zf.shape[1]
@@ -129,10 +188,17 @@ def trimul_forward(z: torch.Tensor, mask: Optional[torch.Tensor], packed: torch.
     _require_cuda(out, "out", torch.float32)
     nbytes = lib.gtk_trimul_workspace_bytes(B, N, SUPPORTED_C, SUPPORTED_C)
     ws = workspace(zf.device, nbytes)
-    rc = lib.gtk_trimul_forward(int(outgoing), _ptr(zf), _ptr(mf), _ptr(packed), _ptr(out), int(add_residual),
-                                _ptr(ws), ws.numel(), B, N, SUPPORTED_C, SUPPORTED_C,
-                                _ptr(status_buffer(zf.device)), _stream(zf.device))
-    _lib.check(rc, "gtk_trimul_forward")
+    if dropout is None:
+        rc = lib.gtk_trimul_forward(int(outgoing), _ptr(zf), _ptr(mf), _ptr(packed), _ptr(out), int(add_residual),
+                                    _ptr(ws), ws.numel(), B, N, SUPPORTED_C, SUPPORTED_C,
+                                    _ptr(status_buffer(zf.device)), _stream(zf.device))
+        _lib.check(rc, "gtk_trimul_forward")
+        return out
+    d = dropout._struct(B, N)
+    rc = lib.gtk_trimul_forward_dropout(int(outgoing), _ptr(zf), _ptr(mf), _ptr(packed), _ptr(out), int(add_residual),
+                                        ctypes.byref(d), _ptr(ws), ws.numel(), B, N, SUPPORTED_C, SUPPORTED_C,
+                                        _ptr(status_buffer(zf.device)), _stream(zf.device))
+    _lib.check(rc, "gtk_trimul_forward_dropout")
     return out
 
 
@@ -214,8 +280,10 @@ def pack_triatt(params: Dict[str, torch.Tensor], device: torch.device, heads: in
 
 
 def triatt_forward(z: torch.Tensor, mask: Optional[torch.Tensor], packed: torch.Tensor, starting: bool,
-                   inf: float = 1e9, out: Optional[torch.Tensor] = None, add_residual: bool = False) -> torch.Tensor:
-    """update (or z + update) of triangle attention around the starting / ending node."""
+                   inf: float = 1e9, out: Optional[torch.Tensor] = None, add_residual: bool = False,
+                   dropout: Optional[DropoutMask] = None) -> torch.Tensor:
+    """update (or z + update) of triangle attention around the starting / ending node.
+    ``dropout`` multiplies the update by a channel dropout mask inside the epilogue."""
     lib = _lib.load()
     zf, mf = prepare_pair(z, mask, SUPPORTED_C)
     B, N = zf.shape[0], zf.shape[1]
@@ -224,10 +292,18 @@ def triatt_forward(z: torch.Tensor, mask: Optional[torch.Tensor], packed: torch.
     _require_cuda(out, "out", torch.float32)
     nbytes = lib.gtk_triatt_workspace_bytes(B, N, SUPPORTED_C, SUPPORTED_C, SUPPORTED_HEADS)
     ws = workspace(zf.device, nbytes)
-    rc = lib.gtk_triatt_forward(int(starting), _ptr(zf), _ptr(mf), _ptr(packed), _ptr(out), int(add_residual),
-                                _ptr(ws), ws.numel(), B, N, SUPPORTED_C, SUPPORTED_C, SUPPORTED_HEADS, float(inf),
-                                _ptr(status_buffer(zf.device)), _stream(zf.device))
-    _lib.check(rc, "gtk_triatt_forward")
+    if dropout is None:
+        rc = lib.gtk_triatt_forward(int(starting), _ptr(zf), _ptr(mf), _ptr(packed), _ptr(out), int(add_residual),
+                                    _ptr(ws), ws.numel(), B, N, SUPPORTED_C, SUPPORTED_C, SUPPORTED_HEADS, float(inf),
+                                    _ptr(status_buffer(zf.device)), _stream(zf.device))
+        _lib.check(rc, "gtk_triatt_forward")
+        return out
+    d = dropout._struct(B, N)
+    rc = lib.gtk_triatt_forward_dropout(int(starting), _ptr(zf), _ptr(mf), _ptr(packed), _ptr(out), int(add_residual),
+                                        ctypes.byref(d), _ptr(ws), ws.numel(), B, N, SUPPORTED_C, SUPPORTED_C,
+                                        SUPPORTED_HEADS, float(inf), _ptr(status_buffer(zf.device)),
+                                        _stream(zf.device))
+    _lib.check(rc, "gtk_triatt_forward_dropout")
     return out
 
 

@@ -4,8 +4,11 @@ The four triangle blocks run on the B200 kernels with the residual add fused int
 their epilogues (``add_residual=True``) whenever the residual can be taken in place.
 ``PairTransition`` (LN -> 4x expand -> ReLU -> project) runs on the two transition
 kernels (``gtk_transition_forward``); inside ``PairTransformLayer`` its residual add and
-the layer's final mask multiply are folded into the second one. The training-mode
-row/column dropout is evaluated with PyTorch ops on the same CUDA tensors.
+the layer's final mask multiply are folded into the second one. In training mode the
+row/column dropout of the four triangle updates is applied inside the same residual
+epilogues: each mask is drawn with the reference's own ``nn.Dropout`` call (same shape,
+dtype and generator, so a seeded run draws the reference's masks) and handed to the
+kernels as keep bits.
 """
 
 from __future__ import annotations
@@ -22,36 +25,47 @@ from .triangle_attention import TriangleAttentionEndingNode, TriangleAttentionSt
 from .triangle_mul import TriangleMultiplicationIncoming, TriangleMultiplicationOutgoing, _PackCache
 
 
-class DropoutRowwise(nn.Module):
+class _SharedDropout(nn.Module):
+    """Dropout whose mask is shared along one pair axis (``_shared_dim``: -3 rows, -2 columns)."""
+
+    _shared_dim = -3
+
+    def __init__(self, p: float):
+        super().__init__()
+        self.p = p
+        self.dropout = nn.Dropout(p)
+
+    def _multipliers(self, shape, dtype: torch.dtype, device: torch.device) -> Tensor:
+        shape = list(shape)
+        shape[self._shared_dim] = 1
+        return self.dropout(torch.ones(shape, dtype=dtype, device=device))
+
+    def forward(self, x: Tensor) -> Tensor:
+        if not self.training or self.p == 0:
+            return x
+        return x * self._multipliers(x.shape, x.dtype, x.device)
+
+    def keep_mask(self, shape, dtype: torch.dtype, device: torch.device) -> Optional[ops.DropoutMask]:
+        """The mask ``forward`` would draw for an update of ``shape`` / ``dtype`` (the same
+        ``nn.Dropout`` call, so the same random numbers), as keep bits for the residual
+        epilogues; None in eval mode or for p = 0."""
+        if not self.training or self.p == 0:
+            return None
+        mult = self._multipliers(shape, dtype, device)
+        scale = 0.0 if self.p >= 1 else float(torch.tensor(1.0 / (1.0 - self.p), dtype=torch.float64).to(dtype))
+        return ops.dropout_mask_from_multipliers(mult, shared_across_rows=self._shared_dim == -3, scale=scale)
+
+
+class DropoutRowwise(_SharedDropout):
     """Dropout with one mask shared across rows (reference pair_transform.py:26-42)."""
 
-    def __init__(self, p: float):
-        super().__init__()
-        self.p = p
-        self.dropout = nn.Dropout(p)
-
-    def forward(self, x: Tensor) -> Tensor:
-        if not self.training or self.p == 0:
-            return x
-        shape = list(x.shape)
-        shape[-3] = 1
-        return x * self.dropout(x.new_ones(shape))
+    _shared_dim = -3
 
 
-class DropoutColumnwise(nn.Module):
+class DropoutColumnwise(_SharedDropout):
     """Dropout with one mask shared across columns (reference pair_transform.py:45-61)."""
 
-    def __init__(self, p: float):
-        super().__init__()
-        self.p = p
-        self.dropout = nn.Dropout(p)
-
-    def forward(self, x: Tensor) -> Tensor:
-        if not self.training or self.p == 0:
-            return x
-        shape = list(x.shape)
-        shape[-2] = 1
-        return x * self.dropout(x.new_ones(shape))
+    _shared_dim = -2
 
 
 class PairTransition(nn.Module):
@@ -138,9 +152,6 @@ class PairTransformLayer(nn.Module):
         self.dropout_row = DropoutRowwise(tri_dropout)
         self.dropout_col = DropoutColumnwise(tri_dropout)
 
-    def _fused_residual(self) -> bool:
-        return not (self.training and self.dropout_row.p > 0)
-
     def forward(self, inputs: Tuple[Tensor, Tensor]) -> Tuple[Tensor, Tensor]:
         p, p_mask = inputs
         if not p.is_cuda:
@@ -153,10 +164,8 @@ class PairTransformLayer(nn.Module):
         if self.include_tri_att:
             blocks += [(self.tri_att_start, self.dropout_row), (self.tri_att_end, self.dropout_col)]
         for block, drop in blocks:
-            if self._fused_residual():
-                block(p, p_mask, out=p, add_residual=True)
-            else:
-                p = p + drop(block(p, p_mask))
+            # p += dropout(update), the dropout (training mode only) applied in the epilogue
+            block(p, p_mask, out=p, add_residual=True, dropout=drop.keep_mask(p.shape, dtype, p.device))
         # p = (p + transition(p)) * mask in one pass (p is a private contiguous fp32 copy)
         self.pair_transition.residual_masked_(p, p_mask)
         return (p.to(dtype), p_mask)

@@ -46,18 +46,24 @@ class TriangleAttention(nn.Module):
         return self._pack.get(self, lambda: ops.pack_triatt(sd, device, self.no_heads))
 
     def forward(self, x: Tensor, mask: Optional[Tensor] = None, *, out: Optional[Tensor] = None,
-                add_residual: bool = False) -> Tensor:
-        """Return the update for ``x`` ``[B, N, N, c_in]`` (``mask`` ``[B, N, N]``)."""
+                add_residual: bool = False, dropout: Optional[ops.DropoutMask] = None) -> Tensor:
+        """Return the update for ``x`` ``[B, N, N, c_in]`` (``mask`` ``[B, N, N]``).
+
+        ``add_residual=True`` returns ``x + update`` (``out=x`` updates in place, fp32).
+        ``dropout`` (an ``ops.DropoutMask``) multiplies the update by a training-mode channel
+        dropout mask before the residual add, inside the kernel's epilogue.
+        """
         if not x.is_cuda:
             raise RuntimeError("genie_tk (B200): TriangleAttention runs on CUDA tensors only")
         if self.c_in != ops.SUPPORTED_C or self.c_hidden != ops.SUPPORTED_C or self.no_heads != ops.SUPPORTED_HEADS:
             raise NotImplementedError(
                 "genie_tk (B200): triangle attention needs c_in = c_hidden = 128 with 4 heads of 32")
         packed = self.packed_weights(x.device)
-        if out is None and not add_residual:
+        if out is None and not add_residual and dropout is None:
             res = torch.ops.genie_tk.triatt_forward(x, mask, packed, self.starting, float(self.inf))
         else:
-            res = ops.triatt_forward(x, mask, packed, self.starting, inf=self.inf, out=out, add_residual=add_residual)
+            res = ops.triatt_forward(x, mask, packed, self.starting, inf=self.inf, out=out, add_residual=add_residual,
+                                     dropout=dropout)
         return res if res.dtype == x.dtype or out is not None else res.to(x.dtype)
 
 

@@ -69,20 +69,23 @@ class TriangleMultiplicativeUpdate(nn.Module):
         return self._pack.get(self, lambda: ops.pack_trimul(sd, device))
 
     def forward(self, z: Tensor, mask: Optional[Tensor] = None, *, out: Optional[Tensor] = None,
-                add_residual: bool = False) -> Tensor:
+                add_residual: bool = False, dropout: Optional[ops.DropoutMask] = None) -> Tensor:
         """Return the update for ``z`` ``[B, N, N, c_z]`` (``mask`` ``[B, N, N]``).
 
         ``add_residual=True`` returns ``z + update`` (``out=z`` updates in place, fp32).
+        ``dropout`` (an ``ops.DropoutMask``) multiplies the update by a training-mode channel
+        dropout mask before the residual add, inside the kernel's epilogue.
         """
         if not z.is_cuda:
             raise RuntimeError("genie_tk (B200): TriangleMultiplicativeUpdate runs on CUDA tensors only")
         if self.c_z != ops.SUPPORTED_C or self.c_hidden != ops.SUPPORTED_C:
             raise NotImplementedError("genie_tk (B200): triangle multiplication needs c_z = c_hidden = 128")
         packed = self.packed_weights(z.device)
-        if out is None and not add_residual:
+        if out is None and not add_residual and dropout is None:
             res = torch.ops.genie_tk.trimul_forward(z, mask, packed, self._outgoing)
         else:
-            res = ops.trimul_forward(z, mask, packed, self._outgoing, out=out, add_residual=add_residual)
+            res = ops.trimul_forward(z, mask, packed, self._outgoing, out=out, add_residual=add_residual,
+                                     dropout=dropout)
         return res if res.dtype == z.dtype or out is not None else res.to(z.dtype)
 
 

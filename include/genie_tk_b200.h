@@ -323,6 +323,48 @@ GTK_API int gtk_pair_embed(const float* s, const float* mask, const float* weigh
                            float* pair_mask, void* workspace, size_t workspace_bytes, int64_t B, int64_t N,
                            int64_t rows, int64_t row0, int c_s, int c_p, void* stream);
 
+/* ---------------------------------------------------------------------------------
+ * Training-mode channel dropout of the residual updates (reference
+ * src/genie_tk/pair_transform.py:26-61, applied at :182-189 as p = p + dropout(update)).
+ * DropoutRowwise draws one mask [B, 1, N, C] shared by every row i (it varies with the
+ * column j); DropoutColumnwise one mask [B, N, 1, C] shared by every column j (it varies
+ * with the row i). Here a mask is a keep-bit array of B * N vectors of 128 bits: vector
+ * (b, t) is the four uint32 words at (b * N + t) * 4, and its bit c (word c / 32, bit
+ * c % 32) is set when channel c is kept. Kept channels are multiplied by `scale`
+ * (1 / (1 - p)); dropped ones add nothing. The *_forward_dropout entry points apply the
+ * mask inside the residual epilogue: out = z + keep * scale * update (add_residual = 1) or
+ * out = keep * scale * update (add_residual = 0). C = 128.
+ * ------------------------------------------------------------------------------- */
+typedef struct gtk_dropout {
+  const uint32_t* keep_bits; /* device, 16-byte aligned, B * N * 4 words */
+  float scale;               /* multiplier of the kept channels: finite, >= 0 */
+  int shared_across_rows;    /* 1: DropoutRowwise (vector t = j); 0: DropoutColumnwise (t = i) */
+} gtk_dropout;
+
+/* Keep bits for n_vectors vectors from the counter-based generator Philox4x32-10 (Salmon,
+ * Moraes, Dror, Shaw, SC'11): channel c of vector v is kept when output word c % 4 of
+ * Philox(counter = {lo32(v*32 + c/4), hi32(v*32 + c/4), lo32(offset), hi32(offset)},
+ * key = {lo32(seed), hi32(seed)}) is >= floor(p * 2^32). 0 <= p < 1. Advance `offset`
+ * between draws of one seed. No counterpart in the reference (it draws with nn.Dropout). */
+GTK_API int gtk_dropout_keep_bits_philox(uint64_t seed, uint64_t offset, double p, int64_t n_vectors,
+                                         uint32_t* keep_bits, void* stream);
+
+/* Keep bits from a multiplier tensor fp32 [n_vectors][128] whose dropped channels are 0
+ * (the reference's own mask, nn.Dropout applied to ones, packed). */
+GTK_API int gtk_dropout_pack_keep_bits(const float* multipliers, int64_t n_vectors, uint32_t* keep_bits,
+                                       void* stream);
+
+/* gtk_trimul_forward / gtk_triatt_forward with the dropout applied to the update before
+ * the residual add; dropout = NULL is the plain entry point. */
+GTK_API int gtk_trimul_forward_dropout(int outgoing, const float* z, const float* mask, const void* packed,
+                                       float* out, int add_residual, const gtk_dropout* dropout, void* workspace,
+                                       size_t workspace_bytes, int64_t B, int64_t N, int c_z, int c_hidden,
+                                       uint32_t* status, void* stream);
+GTK_API int gtk_triatt_forward_dropout(int starting, const float* z, const float* mask, const void* packed,
+                                       float* out, int add_residual, const gtk_dropout* dropout, void* workspace,
+                                       size_t workspace_bytes, int64_t B, int64_t N, int c_in, int c_hidden,
+                                       int heads, float inf, uint32_t* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -49,10 +49,11 @@ def linear(x: torch.Tensor, p: Params, name: str) -> torch.Tensor:
 # Triangle multiplicative update -- src/genie_tk/triangle_mul.py:103-132
 # --------------------------------------------------------------------------------------
 
-def trimul_prepare(z: torch.Tensor, mask: Optional[torch.Tensor], p: Params):
+def trimul_prepare(z: torch.Tensor, mask: Optional[torch.Tensor], p: Params, dtype: torch.dtype = torch.float32):
     """Row-independent part: default mask (triangle_mul.py:105-106), LN_in (:111) and the
-    gated, masked projections a, b for every pair (:114-117)."""
-    z = z.float()
+    gated, masked projections a, b for every pair (:114-117). ``dtype`` is the compute
+    type (fp32 for parity; bf16 with bf16 params times the reference's bf16 GPU path)."""
+    z = z.to(dtype)
     if mask is None:
         mask = torch.ones(z.shape[:-1], dtype=z.dtype, device=z.device)
     m = mask.to(z.dtype).unsqueeze(-1)
@@ -78,9 +79,10 @@ def trimul_rows(zn: torch.Tensor, a: torch.Tensor, b: torch.Tensor, p: Params, o
     return x * g
 
 
-def trimul_forward(z: torch.Tensor, mask: Optional[torch.Tensor], p: Params, outgoing: bool) -> torch.Tensor:
+def trimul_forward(z: torch.Tensor, mask: Optional[torch.Tensor], p: Params, outgoing: bool,
+                   dtype: torch.dtype = torch.float32) -> torch.Tensor:
     """Update (not z + update) of the triangle multiplicative block (triangle_mul.py:103-132)."""
-    zn, a, b = trimul_prepare(z, mask, p)
+    zn, a, b = trimul_prepare(z, mask, p, dtype)
     return trimul_rows(zn, a, b, p, outgoing)
 
 
@@ -89,11 +91,12 @@ def trimul_forward(z: torch.Tensor, mask: Optional[torch.Tensor], p: Params, out
 # src/genie_tk/primitives.py:114-178
 # --------------------------------------------------------------------------------------
 
-def triatt_prepare(z: torch.Tensor, mask: Optional[torch.Tensor], p: Params, starting: bool):
+def triatt_prepare(z: torch.Tensor, mask: Optional[torch.Tensor], p: Params, starting: bool,
+                   dtype: torch.dtype = torch.float32):
     """Row-independent part: default mask (:106-107); ending node transposes x and mask
     (:110-112); LN (:115); triangle bias ``linear(x)`` permuted to ``[*,H,J,K]`` (query j,
-    key k), shared by every row i (:121-129)."""
-    x = z.float()
+    key k), shared by every row i (:121-129). ``dtype`` as in ``trimul_prepare``."""
+    x = z.to(dtype)
     if mask is None:
         mask = torch.ones(x.shape[:-1], dtype=x.dtype, device=x.device)
     mask = mask.to(x.dtype)
@@ -131,12 +134,13 @@ def triatt_rows(x: torch.Tensor, mask: torch.Tensor, tri: torch.Tensor, p: Param
 
 
 def triatt_forward(z: torch.Tensor, mask: Optional[torch.Tensor], p: Params, starting: bool,
-                   no_heads: int, inf: float = 1e9, chunk_rows: int = 0) -> torch.Tensor:
+                   no_heads: int, inf: float = 1e9, chunk_rows: int = 0,
+                   dtype: torch.dtype = torch.float32) -> torch.Tensor:
     """Update of the triangle attention block around the starting (or ending) node
     (triangle_attention.py:100-143). ``chunk_rows`` > 0 evaluates the rows i in chunks
     to bound memory (rows are independent); 0 evaluates all rows at once like the
     reference. The ending node transposes back (:140-141)."""
-    x, m, tri = triatt_prepare(z, mask, p, starting)
+    x, m, tri = triatt_prepare(z, mask, p, starting, dtype)
     N = x.shape[1]
     step = N if chunk_rows <= 0 else chunk_rows
     out = torch.cat([triatt_rows(x, m, tri, p, no_heads, inf, r0, min(N, r0 + step))
@@ -156,16 +160,17 @@ STACK_OPS = ("tri_mul_out", "tri_mul_in", "tri_att_start", "tri_att_end")
 
 
 def stack_forward(z: torch.Tensor, mask: Optional[torch.Tensor], layers: List[Dict[str, Params]],
-                  no_heads: int, chunk_rows: int = 0) -> torch.Tensor:
-    """``z += TriMulOut(z); z += TriMulIn(z); z += TriAttStart(z); z += TriAttEnd(z)`` per layer."""
-    z = z.float().clone()
+                  no_heads: int, chunk_rows: int = 0, dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    """``z += TriMulOut(z); z += TriMulIn(z); z += TriAttStart(z); z += TriAttEnd(z)`` per layer,
+    computed in ``dtype`` (the parameters must be of that type)."""
+    z = z.to(dtype).clone()
     for lp in layers:
-        z = z + trimul_forward(z, mask, lp["tri_mul_out"], outgoing=True)
-        z = z + trimul_forward(z, mask, lp["tri_mul_in"], outgoing=False)
+        z = z + trimul_forward(z, mask, lp["tri_mul_out"], outgoing=True, dtype=dtype)
+        z = z + trimul_forward(z, mask, lp["tri_mul_in"], outgoing=False, dtype=dtype)
         z = z + triatt_forward(z, mask, lp["tri_att_start"], starting=True, no_heads=no_heads,
-                               chunk_rows=chunk_rows)
+                               chunk_rows=chunk_rows, dtype=dtype)
         z = z + triatt_forward(z, mask, lp["tri_att_end"], starting=False, no_heads=no_heads,
-                               chunk_rows=chunk_rows)
+                               chunk_rows=chunk_rows, dtype=dtype)
     return z
 
 

@@ -4,7 +4,6 @@ real ``gloo`` ranks, with the stage computations done by the CPU stand-ins of
 the unsharded oracle stack and against an unsharded (P = 1) run of the same program."""
 
 import os
-import socket
 
 import pytest
 import torch
@@ -131,18 +130,11 @@ def test_shard_spec_validation():
         ShardSpec(1, 64, 4, 4)       # rank out of range
 
 
-def _free_port():
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
-
-
-def _gloo_rank(rank, world, port, z, mask, params, out_q):
+def _gloo_rank(rank, world, store_file, z, mask, params, out_q):
     import torch.distributed as dist
     from genie_tk.sharded import ShardedTrianglePairStack
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+    # a file store: no TCP port to pick, so no race with other processes for a free port
+    dist.init_process_group("gloo", init_method=f"file://{store_file}", rank=rank, world_size=world)
     try:
         N = z.shape[1]
         R = N // world
@@ -154,13 +146,13 @@ def _gloo_rank(rank, world, port, z, mask, params, out_q):
         dist.destroy_process_group()
 
 
-def test_gloo_two_ranks_match_emulation():
+def test_gloo_two_ranks_match_emulation(tmp_path):
     z, mask, params = _problem(1, 32, 1)
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_gloo_rank, args=(r, world, port, z, mask, params, q)) for r in range(world)]
+    store = str(tmp_path / "gloo_store")
+    procs = [ctx.Process(target=_gloo_rank, args=(r, world, store, z, mask, params, q)) for r in range(world)]
     for p in procs:
         p.start()
     parts = dict(q.get(timeout=240) for _ in range(world))
