@@ -219,3 +219,46 @@ def test_dropout_custom_ops_match_ops():
     torch.cuda.synchronize()
     assert torch.equal(a, b) and torch.equal(c, d)
     assert_status_clean(dev)
+
+
+@pytest.mark.parametrize("kind", ["trimul_out", "triatt_end"])
+def test_dropout_epilogue_cost_is_small(kind):
+    """The dropout instantiation of the residual epilogue reads 16 bytes of keep bits per pair
+    (L2-resident) beside the 1 KB of residual traffic: the op may not slow down by more than
+    10% at the benchmark size (the timings are printed, and appended as JSON lines to the
+    file GTK_TIMING_JSON names)."""
+    import json
+    import os
+    dev = require_gpu()
+    from genie_tk import ops
+    B, N = 1, 1024
+    z, mask, params = _block_case(kind, N, B, seed=21)
+    p = to_dev(params, dev)
+    packed = _pack(kind, p, dev)
+    zd, md = z.to(dev), mask.to(dev)
+    drop = ops.dropout_mask_philox(B, N, 0.25, seed=3, offset=0, shared_across_rows=(kind != "triatt_end"),
+                                   device=dev)
+    out = torch.empty_like(zd)
+
+    def timed(d):
+        for _ in range(2):
+            _run(kind, zd, md, packed, out, True, d)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(5):
+            _run(kind, zd, md, packed, out, True, d)
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / 5
+
+    t_plain = min(timed(None) for _ in range(2))
+    t_drop = min(timed(drop) for _ in range(2))
+    assert_status_clean(dev)
+    row = {"case": f"{kind} N={N} residual", "plain_ms": round(t_plain, 4), "dropout_ms": round(t_drop, 4),
+           "overhead": round(t_drop / t_plain - 1, 4)}
+    print(json.dumps(row))
+    if os.environ.get("GTK_TIMING_JSON"):
+        with open(os.environ["GTK_TIMING_JSON"], "a") as f:
+            f.write(json.dumps(row) + "\n")
+    assert t_drop <= 1.10 * t_plain
