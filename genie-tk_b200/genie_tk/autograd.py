@@ -1,0 +1,297 @@
+"""Training support: autograd for the blocks whose forward runs on the library's kernels.
+
+The reference trains through PyTorch autograd over its PyTorch path (its only working
+path; the gradient tests are tests/test_triangle_mul.py:69-90 and
+tests/test_triangle_attention.py:70-113). Here every forward still runs on the library's
+kernels. Each block is a ``torch.autograd.Function`` whose backward differentiates a
+recomputation of the block's math on the GPU:
+
+* Triangle multiplicative update (triangle_mul.py:103-132): the per-pair parts
+  (LayerNorms, gated projections, output gate, all O(N^2)) are recomputed with PyTorch
+  ops, and the two O(N^3) contractions of the backward, plus the one of the recompute,
+  run on the library's tcgen05 contraction kernel (``gtk_trimul_contract``). The
+  contraction's gradients are again contractions of the same two kinds:
+    outgoing  X = out(A, B):  dA = inc(dX^T, B),  dB = inc(dX, A)
+    incoming  X = inc(A, B):  dA = out(B, dX),    dB = out(A, dX^T)
+  where out(P, Q)[i,j] = sum_k P[i,k] Q[j,k], inc(P, Q)[i,j] = sum_k P[k,i] Q[k,j] and
+  ^T swaps the two pair axes. Operands go to the kernel as fp16 planes scaled by their
+  own max-abs, so gradients of any magnitude keep 11 significant bits.
+* Triangle attention (triangle_attention.py:100-143, primitives.py:114-178): the
+  attention is recomputed and differentiated in chunks of rows i with PyTorch ops,
+  so that at most one chunk's [rows, H, N, N] scores exist at a time. This part is not
+  yet a native kernel.
+* Pair transition (pair_transform.py:78-84): recomputed and differentiated with
+  PyTorch ops.
+
+The recomputations are fp32. A block with no input or parameter that requires a
+gradient never builds any of this: its forward is the plain kernel call.
+"""
+
+from __future__ import annotations
+
+from typing import Dict, List, Optional, Sequence
+
+import torch
+import torch.nn.functional as F
+from torch import Tensor
+
+from . import ops
+
+LN_EPS = 1e-5
+
+
+def needs_grad(x: Tensor, module: torch.nn.Module) -> bool:
+    """True when autograd must track a forward on ``x`` through ``module``."""
+    return torch.is_grad_enabled() and (x.requires_grad or any(p.requires_grad for p in module.parameters()))
+
+
+# --------------------------------------------------------------------------------------
+# The N^3 contraction on the library's kernel
+# --------------------------------------------------------------------------------------
+
+def _to_planes(t: Tensor, transpose: bool):
+    """fp32 pair tensor [B, N, N, C] -> (fp16 planes [B, N, C, ld] of t / amax, amax).
+    Plane row r, column col hold t[b, r, col, c] (``transpose``: t[b, col, r, c])."""
+    B, N, _, C = t.shape
+    amax = t.detach().abs().amax().clamp_min(1e-30)
+    view = t.permute(0, 2, 3, 1) if transpose else t.permute(0, 1, 3, 2)
+    planes = torch.zeros(B, N, C, ops.plane_pitch(N), dtype=torch.float16, device=t.device)
+    planes[..., :N] = (view / amax).to(torch.float16)
+    return planes, amax
+
+
+def _contract(p: Tensor, tp: bool, q: Tensor, tq: bool, outgoing: bool) -> Tensor:
+    """out(P, Q) (outgoing) or inc(P, Q) of fp32 pair tensors, P / Q optionally pair-
+    transposed first, on gtk_trimul_contract; fp32 [B, N, N, C]."""
+    N = p.shape[1]
+    pp, sp = _to_planes(p, tp)
+    qp, sq = _to_planes(q, tq)
+    x = ops.trimul_contract(pp, qp, outgoing, N, N, N, out_scale=1.0 / N)
+    return x[..., :N].permute(0, 1, 3, 2).float() * (sp * sq * N)
+
+
+class _Contract(torch.autograd.Function):
+    """x = out(a, b) (outgoing) or inc(a, b) (incoming), both operands fp32 [B, N, N, C]."""
+
+    @staticmethod
+    def forward(ctx, a: Tensor, b: Tensor, outgoing: bool) -> Tensor:
+        ctx.save_for_backward(a, b)
+        ctx.outgoing = outgoing
+        return _contract(a, False, b, False, outgoing)
+
+    @staticmethod
+    def backward(ctx, dx: Tensor):
+        a, b = ctx.saved_tensors
+        dx = dx.contiguous()
+        if ctx.outgoing:
+            da = _contract(dx, True, b, False, outgoing=False) if ctx.needs_input_grad[0] else None
+            db = _contract(dx, False, a, False, outgoing=False) if ctx.needs_input_grad[1] else None
+        else:
+            da = _contract(b, False, dx, False, outgoing=True) if ctx.needs_input_grad[0] else None
+            db = _contract(a, False, dx, True, outgoing=True) if ctx.needs_input_grad[1] else None
+        return da, db, None
+
+
+def contract(a: Tensor, b: Tensor, outgoing: bool) -> Tensor:
+    """Differentiable triangle contraction on the library's kernel (fp32 pair tensors)."""
+    return _Contract.apply(a, b, outgoing)
+
+
+# --------------------------------------------------------------------------------------
+# Recomputations (the reference math, differentiable)
+# --------------------------------------------------------------------------------------
+
+def _linear(x: Tensor, p: Dict[str, Tensor], name: str) -> Tensor:
+    return F.linear(x, p[name + ".weight"], p.get(name + ".bias"))
+
+
+def _mask_or_ones(z: Tensor, mask: Optional[Tensor]) -> Tensor:
+    return torch.ones(z.shape[:-1], dtype=z.dtype, device=z.device) if mask is None else mask.to(z.dtype)
+
+
+def trimul_recompute(z: Tensor, mask: Optional[Tensor], p: Dict[str, Tensor], outgoing: bool) -> Tensor:
+    """The update of the triangle multiplicative block (triangle_mul.py:103-132), fp32,
+    with the contraction on the library's kernel."""
+    m = _mask_or_ones(z, mask).unsqueeze(-1)
+    zn = F.layer_norm(z, (z.shape[-1],), p["layer_norm_in.weight"], p["layer_norm_in.bias"], LN_EPS)
+    a = _linear(zn, p, "linear_a_p") * torch.sigmoid(_linear(zn, p, "linear_a_g")) * m
+    b = _linear(zn, p, "linear_b_p") * torch.sigmoid(_linear(zn, p, "linear_b_g")) * m
+    x = contract(a, b, outgoing)
+    x = F.layer_norm(x, (x.shape[-1],), p["layer_norm_out.weight"], p["layer_norm_out.bias"], LN_EPS)
+    return _linear(x, p, "linear_z") * torch.sigmoid(_linear(zn, p, "linear_g"))
+
+
+def _triatt_rows(xn: Tensor, mask: Tensor, tri: Tensor, p: Dict[str, Tensor], heads: int, inf: float,
+                 r0: int, r1: int) -> Tensor:
+    """Rows [r0, r1) of the gated attention (primitives.py:134-176) in the problem frame."""
+    B, _, N, _ = xn.shape
+    hd = p["mha.linear_q.weight"].shape[0]
+    d = hd // heads
+    xs = xn[:, r0:r1]
+    R = xs.shape[1]
+    q = _linear(xs, p, "mha.linear_q").view(B, R, N, heads, d).transpose(-2, -3)
+    k = _linear(xs, p, "mha.linear_k").view(B, R, N, heads, d).transpose(-2, -3)
+    v = _linear(xs, p, "mha.linear_v").view(B, R, N, heads, d).transpose(-2, -3)
+    s = torch.matmul(q, k.transpose(-1, -2)) * (d ** -0.5)
+    s = s + (inf * (mask[:, r0:r1] - 1.0))[:, :, None, None, :] + tri[:, None]
+    o = torch.matmul(torch.softmax(s, dim=-1), v).transpose(-2, -3).reshape(B, R, N, hd)
+    o = o * torch.sigmoid(_linear(xs, p, "mha.linear_g"))
+    return _linear(o, p, "mha.linear_o")
+
+
+def _triatt_shared(z: Tensor, mask: Optional[Tensor], p: Dict[str, Tensor], starting: bool):
+    """Row-independent part (triangle_attention.py:106-129): orientation, LayerNorm, the
+    triangle bias [B, H, N, N] shared by every row."""
+    x, m = z, _mask_or_ones(z, mask)
+    if not starting:
+        x, m = x.transpose(-2, -3), m.transpose(-1, -2)
+    xn = F.layer_norm(x, (x.shape[-1],), p["layer_norm.weight"], p["layer_norm.bias"], LN_EPS)
+    tri = _linear(xn, p, "linear").permute(0, 3, 1, 2)
+    return xn, m, tri
+
+
+def triatt_backward(z: Tensor, mask: Optional[Tensor], p: Dict[str, Tensor], starting: bool, heads: int,
+                    inf: float, dU: Tensor, wanted: Sequence[Tensor], chunk_rows: int) -> List[Optional[Tensor]]:
+    """Gradients of <update(z), dU> with respect to ``wanted`` (leaves among z and p),
+    evaluating the attention in chunks of ``chunk_rows`` rows of the problem frame."""
+    xn, m, tri = _triatt_shared(z, mask, p, starting)
+    g = dU if starting else dU.transpose(-2, -3)
+    N = xn.shape[1]
+    xn_d, tri_d = xn.detach().requires_grad_(True), tri.detach().requires_grad_(True)
+    row_params = [t for t in wanted if t is not z and t.requires_grad]
+    dxn = torch.zeros_like(xn)
+    dtri = torch.zeros_like(tri)
+    dparams = [torch.zeros_like(t) for t in row_params]
+    for r0 in range(0, N, chunk_rows):
+        r1 = min(N, r0 + chunk_rows)
+        out = _triatt_rows(xn_d, m, tri_d, p, heads, inf, r0, r1)
+        got = torch.autograd.grad(out, [xn_d, tri_d] + row_params, g[:, r0:r1], allow_unused=True)
+        dxn += got[0]
+        dtri += got[1]
+        for acc, gr in zip(dparams, got[2:]):
+            if gr is not None:
+                acc += gr
+    shared = torch.autograd.grad([xn, tri], wanted, [dxn, dtri], allow_unused=True)
+    extra = dict(zip([id(t) for t in row_params], dparams))
+    res: List[Optional[Tensor]] = []
+    for t, gs in zip(wanted, shared):
+        ge = extra.get(id(t))
+        res.append(gs if ge is None else (ge if gs is None else gs + ge))
+    return res
+
+
+def transition_recompute(z: Tensor, p: Dict[str, Tensor]) -> Tensor:
+    """PairTransition.forward (pair_transform.py:78-84) in fp32."""
+    x = F.layer_norm(z, (z.shape[-1],), p["layer_norm.weight"], p["layer_norm.bias"], LN_EPS)
+    return _linear(torch.relu(_linear(x, p, "linear_1")), p, "linear_2")
+
+
+# --------------------------------------------------------------------------------------
+# Block functions: forward on the kernels, backward through the recomputation
+# --------------------------------------------------------------------------------------
+
+def _leaves(z: Tensor, params: Sequence[Tensor]):
+    zl = z.detach().requires_grad_(z.requires_grad)
+    pl = [t.detach().requires_grad_(t.requires_grad) for t in params]
+    return zl, pl
+
+
+def _grads(out: Tensor, zl: Tensor, pl: List[Tensor], dU: Tensor):
+    wanted = [t for t in [zl] + pl if t.requires_grad]
+    got = torch.autograd.grad(out, wanted, dU, allow_unused=True) if wanted else []
+    it = iter(got)
+    return [next(it) if t.requires_grad else None for t in [zl] + pl]
+
+
+class TriMulFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, z, mask, packed, outgoing, *params):
+        ctx.save_for_backward(z, mask, *params)
+        ctx.outgoing = outgoing
+        return ops.trimul_forward(z, mask, packed, outgoing)
+
+    @staticmethod
+    def backward(ctx, dU):
+        z, mask, *params = ctx.saved_tensors
+        with torch.enable_grad():
+            zl, pl = _leaves(z.float(), params)
+            out = trimul_recompute(zl, mask, dict(zip(ops.TRIMUL_KEYS, pl)), ctx.outgoing)
+            g = _grads(out, zl, pl, dU.float())
+        return (g[0], None, None, None, *g[1:])
+
+
+class TriAttFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, z, mask, packed, starting, inf, heads, chunk_rows, *params):
+        ctx.save_for_backward(z, mask, *params)
+        ctx.starting, ctx.inf, ctx.heads, ctx.chunk_rows = starting, inf, heads, chunk_rows
+        return ops.triatt_forward(z, mask, packed, starting, inf=inf)
+
+    @staticmethod
+    def backward(ctx, dU):
+        z, mask, *params = ctx.saved_tensors
+        with torch.enable_grad():
+            zl, pl = _leaves(z.float(), params)
+            wanted = [t for t in [zl] + pl if t.requires_grad]
+            got = triatt_backward(zl, mask, dict(zip(ops.TRIATT_KEYS, pl)), ctx.starting, ctx.heads, ctx.inf,
+                                  dU.float(), wanted, ctx.chunk_rows) if wanted else []
+            it = iter(got)
+            g = [next(it) if t.requires_grad else None for t in [zl] + pl]
+        return (g[0], None, None, None, None, None, None, *g[1:])
+
+
+class TransitionFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, z, packed, *params):
+        ctx.save_for_backward(z, *params)
+        return ops.transition_forward(z, None, packed)
+
+    @staticmethod
+    def backward(ctx, dU):
+        z, *params = ctx.saved_tensors
+        with torch.enable_grad():
+            zl, pl = _leaves(z.float(), params)
+            out = transition_recompute(zl, dict(zip(ops.TRANSITION_KEYS, pl)))
+            g = _grads(out, zl, pl, dU.float())
+        return (g[0], None, *g[1:])
+
+
+def attention_chunk_rows(N: int, heads: int, budget_bytes: int = 2 << 30) -> int:
+    """Rows per recompute chunk so that one chunk's fp32 scores (about six live copies of
+    [rows, H, N, N] during its backward) stay within ``budget_bytes``."""
+    per_row = 6 * heads * N * N * 4
+    return max(1, min(N, budget_bytes // max(per_row, 1)))
+
+
+class PairEmbedFn(torch.autograd.Function):
+    """p[b,i,j] = s_i W_a^T + s_j W_b^T + bias (examples/basic_usage.py:181-199) on the pair
+    embedding kernels. With p = U_i + V_j the backward is closed-form and O(N^2 c):
+    dU_i = sum_j dp_ij, dV_j = sum_i dp_ij, ds = dU W_a + dV W_b, dW = [dU^T s | dV^T s],
+    dbias = sum dV. The pair mask carries no gradient."""
+
+    @staticmethod
+    def forward(ctx, s, mask, weight, bias):
+        ctx.save_for_backward(s, weight)
+        ctx.has_bias = bias is not None
+        p, pm = ops.pair_embed(s, mask, weight, bias, with_mask=mask is not None)
+        if pm is not None:
+            ctx.mark_non_differentiable(pm)
+        return p, pm
+
+    @staticmethod
+    def backward(ctx, dp, dpm):
+        s, weight = ctx.saved_tensors
+        c_s, c_p = s.shape[-1], weight.shape[0]
+        dp = dp.float()
+        du = dp.sum(2)  # [B, N(i), c_p]
+        dv = dp.sum(1)  # [B, N(j), c_p]
+        sf = s.float().reshape(-1, c_s)
+        w = weight.float()
+        ds = dw = db = None
+        if ctx.needs_input_grad[0]:
+            ds = (du @ w[:, :c_s] + dv @ w[:, c_s:]).to(s.dtype)
+        if ctx.needs_input_grad[2]:
+            dw = torch.cat([du.reshape(-1, c_p).t() @ sf, dv.reshape(-1, c_p).t() @ sf], dim=1).to(weight.dtype)
+        if ctx.has_bias and ctx.needs_input_grad[3]:
+            db = dv.sum((0, 1))
+        return ds, None, dw, db

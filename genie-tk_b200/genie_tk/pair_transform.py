@@ -19,7 +19,7 @@ import torch
 import torch.nn as nn
 from torch import Tensor
 
-from . import ops
+from . import autograd, ops
 from .primitives import Linear
 from .triangle_attention import TriangleAttentionEndingNode, TriangleAttentionStartingNode
 from .triangle_mul import TriangleMultiplicationIncoming, TriangleMultiplicationOutgoing, _PackCache
@@ -95,7 +95,12 @@ class PairTransition(nn.Module):
     def forward(self, p: Tensor, mask: Optional[Tensor] = None) -> Tensor:
         """The update (the reference ignores ``mask`` here, and so does this)."""
         self._check(p)
-        res = torch.ops.genie_tk.transition_forward(p, self.packed_weights(p.device))
+        if autograd.needs_grad(p, self):
+            sd = dict(self.named_parameters())
+            res = autograd.TransitionFn.apply(p.float().contiguous(), self.packed_weights(p.device),
+                                              *[sd[k] for k in ops.TRANSITION_KEYS])
+        else:
+            res = torch.ops.genie_tk.transition_forward(p, self.packed_weights(p.device))
         return res if res.dtype == p.dtype else res.to(p.dtype)
 
     def residual_masked_(self, p: Tensor, p_mask: Optional[Tensor]) -> Tensor:
@@ -125,6 +130,9 @@ class PairEmbedding(nn.Module):
         """(p [B, N, N, c_p] fp32, p_mask [B, N, N] or None when ``mask`` is None)."""
         if not s.is_cuda:
             raise RuntimeError("genie_tk (B200): PairEmbedding runs on CUDA tensors only")
+        if autograd.needs_grad(s, self):
+            p, pm = autograd.PairEmbedFn.apply(s, mask, self.weight, self.bias)
+            return p, pm
         p, pm = ops.pair_embed(s, mask, self.weight, self.bias, with_mask=mask is not None)
         return p, pm
 
@@ -157,6 +165,8 @@ class PairTransformLayer(nn.Module):
         if not p.is_cuda:
             raise RuntimeError("genie_tk (B200): PairTransformLayer runs on CUDA tensors only")
         dtype = p.dtype
+        if autograd.needs_grad(p, self):
+            return self._forward_autograd(p, p_mask)
         p = p.float().clone()
         blocks = []
         if self.include_mul_update:
@@ -168,6 +178,21 @@ class PairTransformLayer(nn.Module):
             block(p, p_mask, out=p, add_residual=True, dropout=drop.keep_mask(p.shape, dtype, p.device))
         # p = (p + transition(p)) * mask in one pass (p is a private contiguous fp32 copy)
         self.pair_transition.residual_masked_(p, p_mask)
+        return (p.to(dtype), p_mask)
+
+    def _forward_autograd(self, p: Tensor, p_mask: Tensor) -> Tuple[Tensor, Tensor]:
+        """The reference's out-of-place chain (pair_transform.py:177-195), every block's forward
+        on the kernels and differentiable; the dropout draws exactly as the reference does."""
+        dtype = p.dtype
+        p = p.float()
+        if self.include_mul_update:
+            p = p + self.dropout_row(self.tri_mul_out(p, p_mask))
+            p = p + self.dropout_row(self.tri_mul_in(p, p_mask))
+        if self.include_tri_att:
+            p = p + self.dropout_row(self.tri_att_start(p, p_mask))
+            p = p + self.dropout_col(self.tri_att_end(p, p_mask))
+        p = p + self.pair_transition(p, p_mask)
+        p = p * p_mask.unsqueeze(-1).to(p.dtype)
         return (p.to(dtype), p_mask)
 
 

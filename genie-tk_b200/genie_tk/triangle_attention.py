@@ -19,7 +19,7 @@ import torch
 import torch.nn as nn
 from torch import Tensor
 
-from . import ops
+from . import autograd, ops
 from .primitives import Attention, Linear
 from .triangle_mul import _PackCache
 
@@ -59,6 +59,18 @@ class TriangleAttention(nn.Module):
             raise NotImplementedError(
                 "genie_tk (B200): triangle attention needs c_in = c_hidden = 128 with 4 heads of 32")
         packed = self.packed_weights(x.device)
+        if autograd.needs_grad(x, self):
+            # training: forward on the kernels, backward through a row-chunked recomputation
+            if out is not None or dropout is not None:
+                raise RuntimeError("genie_tk (B200): out= and dropout= are inference-only; under autograd "
+                                   "use the returned update (and nn.Dropout) instead")
+            sd = dict(self.named_parameters())
+            N = x.shape[1]
+            upd = autograd.TriAttFn.apply(x.float().contiguous(), mask, packed, self.starting, float(self.inf),
+                                          self.no_heads, autograd.attention_chunk_rows(N, self.no_heads),
+                                          *[sd[k] for k in ops.TRIATT_KEYS])
+            res = x.float() + upd if add_residual else upd
+            return res if res.dtype == x.dtype else res.to(x.dtype)
         if out is None and not add_residual and dropout is None:
             res = torch.ops.genie_tk.triatt_forward(x, mask, packed, self.starting, float(self.inf))
         else:

@@ -16,7 +16,7 @@ import torch
 import torch.nn as nn
 from torch import Tensor
 
-from . import ops
+from . import autograd, ops
 from .primitives import Linear
 
 
@@ -81,6 +81,17 @@ class TriangleMultiplicativeUpdate(nn.Module):
         if self.c_z != ops.SUPPORTED_C or self.c_hidden != ops.SUPPORTED_C:
             raise NotImplementedError("genie_tk (B200): triangle multiplication needs c_z = c_hidden = 128")
         packed = self.packed_weights(z.device)
+        if autograd.needs_grad(z, self):
+            # training: the forward still runs on the kernels; the backward differentiates a
+            # recomputation whose contractions run on the library's contraction kernel
+            if out is not None or dropout is not None:
+                raise RuntimeError("genie_tk (B200): out= and dropout= are inference-only; under autograd "
+                                   "use the returned update (and nn.Dropout) instead")
+            sd = dict(self.named_parameters())
+            upd = autograd.TriMulFn.apply(z.float().contiguous(), mask, packed, self._outgoing,
+                                          *[sd[k] for k in ops.TRIMUL_KEYS])
+            res = z.float() + upd if add_residual else upd
+            return res if res.dtype == z.dtype else res.to(z.dtype)
         if out is None and not add_residual and dropout is None:
             res = torch.ops.genie_tk.trimul_forward(z, mask, packed, self._outgoing)
         else:

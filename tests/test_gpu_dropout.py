@@ -160,7 +160,8 @@ def test_training_layer_draws_the_reference_masks():
     layer.train()
     zd, md = z.to(dev), mask.to(dev)
     torch.cuda.manual_seed(1234)
-    got, _ = layer((zd, md))
+    with torch.no_grad():  # the fused path: masks applied inside the residual epilogues
+        got, _ = layer((zd, md))
     torch.cuda.synchronize()
     assert_status_clean(dev)
     # replay the reference's draws: DropoutRowwise x3 then DropoutColumnwise (pair_transform.py:182-189)
@@ -172,7 +173,8 @@ def test_training_layer_draws_the_reference_masks():
     assert_parity(got, ref, what="training-mode PairTransformLayer")
     # and the masks really drop: eval mode gives a clearly different result
     layer.eval()
-    ev, _ = layer((zd, md))
+    with torch.no_grad():
+        ev, _ = layer((zd, md))
     assert float((ev - got).abs().max()) > 0.1
 
 
@@ -188,8 +190,9 @@ def test_training_layer_with_zero_dropout_equals_eval():
                                         tri_dropout=0.0).to(dev)
     layer.load_state_dict(sd)
     zd, md = z.to(dev), mask.to(dev)
-    tr, _ = layer.train()((zd, md))
-    ev, _ = layer.eval()((zd, md))
+    with torch.no_grad():
+        tr, _ = layer.train()((zd, md))
+        ev, _ = layer.eval()((zd, md))
     torch.cuda.synchronize()
     assert torch.equal(tr, ev)
     assert_status_clean(dev)

@@ -71,8 +71,12 @@ def test_pair_transform_layer_matches_oracle():
     missing = set(layer.state_dict()) ^ set(sd)
     assert not missing, missing
     layer.load_state_dict(sd)
-    got, _ = layer((z.to(dev), mask.to(dev)))
+    with torch.no_grad():  # the fused in-place path
+        got, _ = layer((z.to(dev), mask.to(dev)))
+    tracked, _ = layer((z.to(dev), mask.to(dev)))  # parameters require grad: the autograd path
     torch.cuda.synchronize()
     ref = O.layer_tail(O.stack_forward(z, mask, [lp], no_heads=4), mask, tp)
     assert_parity(got, ref, what="PairTransformLayer")
+    assert_parity(tracked, ref, what="PairTransformLayer under autograd")
+    assert tracked.requires_grad
     assert_status_clean(dev)

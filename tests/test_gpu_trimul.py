@@ -89,8 +89,9 @@ def test_config_matches_oracle(cfg, N, B, outgoing):
     got = mod(zd, md)
     ref = O.trimul_forward(zd, md, to_dev(params, dev), outgoing=outgoing)
     assert_parity(got, ref, what=f"cfg{cfg} N={N}")
-    # fused residual, in place
+    # fused residual, in place (a graph-less kernel call: inference mode)
     z2 = zd.clone()
-    mod(z2, md, out=z2, add_residual=True)
+    with torch.no_grad():
+        mod(z2, md, out=z2, add_residual=True)
     assert_parity(z2, zd + ref, what="residual in place")
     assert_status_clean(dev)
