@@ -101,3 +101,40 @@ def test_cfg5_layer_beats_reference_pytorch_on_the_same_gpu():
     _record({"case": "cfg5 one layer N=1024 B=1", "reference_pytorch_bf16_ms": round(t_ref, 3),
              "genie_tk_b200_ms": round(t_ours, 3), "speedup": round(t_ref / t_ours, 1)})
     assert t_ours < t_ref
+
+
+def test_cfg5_layer_training_step_against_reference_pytorch_on_the_same_gpu():
+    """Forward + backward of one cfg5 layer's four residual blocks at N = 1024: the library
+    (kernel forwards, backward through the recompute with kernel contractions) against the
+    reference's bf16 PyTorch autograd on the same GPU. Recorded, and required to finish;
+    not required to be faster (the attention backward is a PyTorch recompute)."""
+    dev = require_gpu()
+    import genie_tk
+    z, mask, params = O.config_inputs(5, N=1024)
+    lp = params[0]
+    zd, md = z.to(dev), mask.to(dev)
+    w = torch.randn(zd.shape, generator=torch.Generator().manual_seed(1)).to(dev)
+    mods = [genie_tk.TriangleMultiplicationOutgoing(128, 128), genie_tk.TriangleMultiplicationIncoming(128, 128),
+            genie_tk.TriangleAttentionStartingNode(128, 128, 4), genie_tk.TriangleAttentionEndingNode(128, 128, 4)]
+    for m, blk in zip(mods, O.STACK_OPS):
+        m.to(dev).load_state_dict(lp[blk])
+
+    def ours():
+        x = zd.clone().requires_grad_(True)
+        y = x
+        for m in mods:
+            y = y + m(y, md)
+        (y * w).sum().backward()
+
+    l16 = [{blk: {k: v.to(dev, torch.bfloat16).requires_grad_(True) for k, v in p.items()} for blk, p in lp.items()}]
+    z16, m16, w16 = zd.to(torch.bfloat16), md.to(torch.bfloat16), w.to(torch.bfloat16)
+
+    def reference():
+        x = z16.clone().requires_grad_(True)
+        (O.stack_forward(x, m16, l16, no_heads=4, dtype=torch.bfloat16) * w16).sum().backward()
+
+    t_ours = _time_ms(ours, warm=1, reps=2)
+    t_ref = _time_ms(reference, warm=1, reps=2)
+    _record({"case": "cfg5 one layer N=1024 B=1, forward + backward", "reference_pytorch_bf16_ms": round(t_ref, 2),
+             "genie_tk_b200_ms": round(t_ours, 2), "speedup": round(t_ref / t_ours, 2)})
+    assert all(p.grad is not None and torch.isfinite(p.grad).all() for m in mods for p in m.parameters())
