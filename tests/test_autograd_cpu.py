@@ -1,0 +1,114 @@
+"""CPU checks of the training support's host logic (genie_tk.autograd): the differentiable
+recomputations against the oracle and its autograd, the row-chunked attention backward,
+and the contraction-gradient identities of the multiplicative update. The library's
+contraction kernel is replaced here by an einsum with the same contract; the kernel
+itself is covered by tests/test_gpu_autograd.py."""
+
+import pytest
+import torch
+
+from oracle import triangle_oracle as O
+
+
+def _rel(a, b):
+    return float((a.detach() - b.detach()).norm() / b.detach().norm().clamp_min(1e-30))
+
+
+def _einsum_contract(p, tp, q, tq, outgoing):
+    """The contract of autograd._contract in fp32 einsums: out(P, Q) or inc(P, Q), with
+    P / Q pair-transposed first when asked."""
+    if tp:
+        p = p.transpose(1, 2)
+    if tq:
+        q = q.transpose(1, 2)
+    eq = "bikc,bjkc->bijc" if outgoing else "bkic,bkjc->bijc"
+    return torch.einsum(eq, p, q)
+
+
+@pytest.fixture
+def AG(monkeypatch):
+    from genie_tk import autograd
+    monkeypatch.setattr(autograd, "_contract", _einsum_contract)
+    return autograd
+
+
+def _case(seed, B=1, N=11):
+    gen = torch.Generator().manual_seed(seed)
+    z = torch.randn(B, N, N, 128, generator=gen, dtype=torch.float64).float()
+    mask = torch.ones(B, N, N)
+    mask[:, -2:, :] = 0
+    mask[:, :, -3:] = 0
+    w = torch.randn(B, N, N, 128, generator=gen)
+    return gen, z, mask, w
+
+
+@pytest.mark.parametrize("outgoing", [True, False])
+def test_contraction_gradient_identities(AG, outgoing):
+    gen, _, _, _ = _case(1)
+    a = torch.randn(2, 9, 9, 16, generator=gen, requires_grad=True)
+    b = torch.randn(2, 9, 9, 16, generator=gen, requires_grad=True)
+    w = torch.randn(2, 9, 9, 16, generator=gen)
+    ga, gb = torch.autograd.grad(AG.contract(a, b, outgoing), [a, b], w)
+    eq = "bikc,bjkc->bijc" if outgoing else "bkic,bkjc->bijc"
+    ga2, gb2 = torch.autograd.grad(torch.einsum(eq, a, b), [a, b], w)
+    assert _rel(ga, ga2) < 1e-6 and _rel(gb, gb2) < 1e-6
+
+
+@pytest.mark.parametrize("outgoing", [True, False])
+def test_trimul_recompute_and_gradients_match_oracle(AG, outgoing):
+    gen, z, mask, w = _case(2)
+    p = O.make_trimul_params(128, 128, gen, gate_bias=1.0)
+    z1 = z.clone().requires_grad_(True)
+    p1 = {k: v.clone().requires_grad_(True) for k, v in p.items()}
+    out = AG.trimul_recompute(z1, mask, p1, outgoing)
+    g1 = torch.autograd.grad((out * w).sum(), [z1] + list(p1.values()))
+    z2 = z.clone().requires_grad_(True)
+    p2 = {k: v.clone().requires_grad_(True) for k, v in p.items()}
+    ref = O.trimul_forward(z2, mask, p2, outgoing)
+    g2 = torch.autograd.grad((ref * w).sum(), [z2] + list(p2.values()))
+    assert float((out - ref).detach().abs().max()) < 1e-4
+    for a, b in zip(g1, g2):
+        assert _rel(a, b) < 1e-4
+
+
+@pytest.mark.parametrize("starting", [True, False])
+@pytest.mark.parametrize("chunk", [11, 4, 1])
+def test_chunked_attention_backward_matches_oracle_autograd(AG, starting, chunk):
+    gen, z, mask, w = _case(3 + int(starting))
+    p = O.make_triatt_params(128, 128, 4, gen, gate_bias=1.0)
+    zl = z.clone().requires_grad_(True)
+    pl = {k: v.clone().requires_grad_(True) for k, v in p.items()}
+    wanted = [zl] + list(pl.values())
+    got = AG.triatt_backward(zl, mask, pl, starting, 4, 1e9, w, wanted, chunk)
+    z2 = z.clone().requires_grad_(True)
+    p2 = {k: v.clone().requires_grad_(True) for k, v in p.items()}
+    ref = O.triatt_forward(z2, mask, p2, starting, no_heads=4)
+    g2 = torch.autograd.grad((ref * w).sum(), [z2] + list(p2.values()))
+    for name, a, b in zip(["z"] + list(p), got, g2):
+        assert a is not None, name
+        assert _rel(a, b) < 1e-4, (name, _rel(a, b))
+
+
+def test_transition_recompute_matches_oracle(AG):
+    gen, z, _, w = _case(5)
+    p = O.make_transition_params(128, 4, gen)
+    out = AG.transition_recompute(z, p)
+    assert float((out - O.transition_forward(z, p)).abs().max()) < 1e-4
+
+
+def test_chunk_rows_bound_the_score_memory(AG):
+    assert AG.attention_chunk_rows(1024, 4) == (2 << 30) // (6 * 4 * 1024 * 1024 * 4)
+    assert AG.attention_chunk_rows(16, 4) == 16
+    assert AG.attention_chunk_rows(100000, 4) == 1
+
+
+def test_needs_grad_follows_autograd_state(AG):
+    lin = torch.nn.Linear(2, 2)
+    x = torch.zeros(2)
+    assert AG.needs_grad(x, lin)
+    with torch.no_grad():
+        assert not AG.needs_grad(x, lin)
+    for q in lin.parameters():
+        q.requires_grad_(False)
+    assert not AG.needs_grad(x, lin)
+    assert AG.needs_grad(x.requires_grad_(True), lin)

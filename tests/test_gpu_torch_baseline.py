@@ -133,8 +133,17 @@ def test_cfg5_layer_training_step_against_reference_pytorch_on_the_same_gpu():
         x = z16.clone().requires_grad_(True)
         (O.stack_forward(x, m16, l16, no_heads=4, dtype=torch.bfloat16) * w16).sum().backward()
 
+    l32 = [{blk: {k: v.to(dev).requires_grad_(True) for k, v in p.items()} for blk, p in lp.items()}]
+
+    def reference_fp32():
+        x = zd.clone().requires_grad_(True)
+        (O.stack_forward(x, md, l32, no_heads=4) * w).sum().backward()
+
     t_ours = _time_ms(ours, warm=1, reps=2)
     t_ref = _time_ms(reference, warm=1, reps=2)
+    torch.cuda.empty_cache()
+    t_ref32 = _time_ms(reference_fp32, warm=1, reps=2)
     _record({"case": "cfg5 one layer N=1024 B=1, forward + backward", "reference_pytorch_bf16_ms": round(t_ref, 2),
-             "genie_tk_b200_ms": round(t_ours, 2), "speedup": round(t_ref / t_ours, 2)})
+             "reference_pytorch_fp32_ms": round(t_ref32, 2), "genie_tk_b200_ms": round(t_ours, 2),
+             "speedup_vs_bf16": round(t_ref / t_ours, 2), "speedup_vs_fp32": round(t_ref32 / t_ours, 2)})
     assert all(p.grad is not None and torch.isfinite(p.grad).all() for m in mods for p in m.parameters())
