@@ -132,11 +132,11 @@ def _triatt_rows(xn: Tensor, mask: Tensor, tri: Tensor, p: Dict[str, Tensor], he
     q = _linear(xs, p, "mha.linear_q").view(B, R, N, heads, d).transpose(-2, -3)
     k = _linear(xs, p, "mha.linear_k").view(B, R, N, heads, d).transpose(-2, -3)
     v = _linear(xs, p, "mha.linear_v").view(B, R, N, heads, d).transpose(-2, -3)
-    # scores = q k^T / sqrt(d) + inf * (mask - 1) + tri, with the scale and both additive
-    # terms applied by the GEMM (one pass over the [R, H, N, N] scores instead of four)
-    add = ((inf * (mask[:, r0:r1] - 1.0))[:, :, None, None, :] + tri[:, None]).reshape(-1, N, N)
-    s = torch.baddbmm(add, q.reshape(-1, N, d), k.reshape(-1, N, d).transpose(-1, -2), alpha=d ** -0.5)
-    s = s.view(B, R, heads, N, N)
+    # explicit scores: the memory-efficient scaled_dot_product_attention returned wrong
+    # bias gradients for some shapes (ending node, N = 67, B = 2), and one fused baddbmm
+    # for the scale and both additive terms measured slower than these separate passes
+    s = torch.matmul(q, k.transpose(-1, -2)) * (d ** -0.5)
+    s = s + (inf * (mask[:, r0:r1] - 1.0))[:, :, None, None, :] + tri[:, None]
     o = torch.matmul(torch.softmax(s, dim=-1), v).transpose(-2, -3).reshape(B, R, N, hd)
     o = o * torch.sigmoid(_linear(xs, p, "mha.linear_g"))
     return _linear(o, p, "mha.linear_o")
