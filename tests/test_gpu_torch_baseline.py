@@ -147,3 +147,43 @@ def test_cfg5_layer_training_step_against_reference_pytorch_on_the_same_gpu():
              "reference_pytorch_fp32_ms": round(t_ref32, 2), "genie_tk_b200_ms": round(t_ours, 2),
              "speedup_vs_bf16": round(t_ref / t_ours, 2), "speedup_vs_fp32": round(t_ref32 / t_ours, 2)})
     assert all(p.grad is not None and torch.isfinite(p.grad).all() for m in mods for p in m.parameters())
+
+
+@pytest.mark.parametrize("op", ["trimul_out", "triatt_start"])
+def test_peak_memory_against_reference_pytorch(op):
+    """Peak device memory of one forward at B = 1, N = 512 (the reference's README.md:343-344
+    reports 4.2 GB / 3.8 GB for its PyTorch path and 1.1 / 0.9 GB for its kernels, on an
+    H100): the bytes allocated above the inputs and parameters during the call, for the
+    library (its workspace included) and for the reference math in bf16."""
+    dev = require_gpu()
+    from genie_tk import ops
+    N = 512
+    gen = torch.Generator().manual_seed(N + 1)
+    z = torch.randn(1, N, N, 128, generator=gen).to(dev)
+    mask = torch.ones(1, N, N, device=dev)
+    p = {k: v.to(dev) for k, v in _op_params(op, gen).items()}
+    packed = ops.pack_trimul(p, dev) if op.startswith("trimul") else ops.pack_triatt(p, dev, 4)
+    p16 = {k: v.to(torch.bfloat16) for k, v in p.items()}
+    z16, m16 = z.to(torch.bfloat16), mask.to(torch.bfloat16)
+
+    def peak(fn):
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        base = torch.cuda.memory_allocated(dev)
+        torch.cuda.reset_peak_memory_stats(dev)
+        out = fn()
+        torch.cuda.synchronize()
+        used = torch.cuda.max_memory_allocated(dev) - base
+        del out
+        return used
+
+    ops.release_workspaces()
+    if op.startswith("trimul"):
+        ours = peak(lambda: ops.trimul_forward(z, mask, packed, True))
+    else:
+        ours = peak(lambda: ops.triatt_forward(z, mask, packed, True))
+    with torch.no_grad():
+        ref = peak(lambda: _reference_update(op, z16, m16, p16, torch.bfloat16))
+    _record({"case": f"{op} N={N} B=1 peak memory", "reference_pytorch_bf16_GB": round(ref / 1e9, 3),
+             "genie_tk_b200_GB": round(ours / 1e9, 3)})
+    assert ours < ref
