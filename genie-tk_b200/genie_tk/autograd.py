@@ -105,6 +105,12 @@ def _linear(x: Tensor, p: Dict[str, Tensor], name: str) -> Tensor:
     return F.linear(x, p[name + ".weight"], p.get(name + ".bias"))
 
 
+def _fp32(p: Dict[str, Tensor]) -> Dict[str, Tensor]:
+    """The parameters as fp32 (a differentiable cast: a bf16 / fp16 model gets its gradients
+    back in its own dtype)."""
+    return {k: v.float() for k, v in p.items()}
+
+
 def _mask_or_ones(z: Tensor, mask: Optional[Tensor]) -> Tensor:
     return torch.ones(z.shape[:-1], dtype=z.dtype, device=z.device) if mask is None else mask.to(z.dtype)
 
@@ -112,6 +118,7 @@ def _mask_or_ones(z: Tensor, mask: Optional[Tensor]) -> Tensor:
 def trimul_recompute(z: Tensor, mask: Optional[Tensor], p: Dict[str, Tensor], outgoing: bool) -> Tensor:
     """The update of the triangle multiplicative block (triangle_mul.py:103-132), fp32,
     with the contraction on the library's kernel."""
+    p = _fp32(p)
     m = _mask_or_ones(z, mask).unsqueeze(-1)
     zn = F.layer_norm(z, (z.shape[-1],), p["layer_norm_in.weight"], p["layer_norm_in.bias"], LN_EPS)
     a = _linear(zn, p, "linear_a_p") * torch.sigmoid(_linear(zn, p, "linear_a_g")) * m
@@ -156,18 +163,20 @@ def _triatt_shared(z: Tensor, mask: Optional[Tensor], p: Dict[str, Tensor], star
 def triatt_backward(z: Tensor, mask: Optional[Tensor], p: Dict[str, Tensor], starting: bool, heads: int,
                     inf: float, dU: Tensor, wanted: Sequence[Tensor], chunk_rows: int) -> List[Optional[Tensor]]:
     """Gradients of <update(z), dU> with respect to ``wanted`` (leaves among z and p),
-    evaluating the attention in chunks of ``chunk_rows`` rows of the problem frame."""
-    xn, m, tri = _triatt_shared(z, mask, p, starting)
+    evaluating the attention in chunks of ``chunk_rows`` rows of the problem frame. Each
+    chunk builds (and frees) its own graph from the leaves, so the parameters' fp32 casts
+    are redone per chunk; the per-chunk gradients accumulate in fp32."""
+    xn, m, tri = _triatt_shared(z, mask, _fp32(p), starting)
     g = dU if starting else dU.transpose(-2, -3)
     N = xn.shape[1]
     xn_d, tri_d = xn.detach().requires_grad_(True), tri.detach().requires_grad_(True)
     row_params = [t for t in wanted if t is not z and t.requires_grad]
     dxn = torch.zeros_like(xn)
     dtri = torch.zeros_like(tri)
-    dparams = [torch.zeros_like(t) for t in row_params]
+    dparams = [torch.zeros_like(t, dtype=torch.float32) for t in row_params]
     for r0 in range(0, N, chunk_rows):
         r1 = min(N, r0 + chunk_rows)
-        out = _triatt_rows(xn_d, m, tri_d, p, heads, inf, r0, r1)
+        out = _triatt_rows(xn_d, m, tri_d, _fp32(p), heads, inf, r0, r1)
         got = torch.autograd.grad(out, [xn_d, tri_d] + row_params, g[:, r0:r1], allow_unused=True)
         dxn += got[0]
         dtri += got[1]
@@ -179,12 +188,16 @@ def triatt_backward(z: Tensor, mask: Optional[Tensor], p: Dict[str, Tensor], sta
     res: List[Optional[Tensor]] = []
     for t, gs in zip(wanted, shared):
         ge = extra.get(id(t))
-        res.append(gs if ge is None else (ge if gs is None else gs + ge))
+        if ge is None:
+            res.append(gs)
+        else:
+            res.append((ge if gs is None else ge + gs.float()).to(t.dtype))
     return res
 
 
 def transition_recompute(z: Tensor, p: Dict[str, Tensor]) -> Tensor:
     """PairTransition.forward (pair_transform.py:78-84) in fp32."""
+    p = _fp32(p)
     x = F.layer_norm(z, (z.shape[-1],), p["layer_norm.weight"], p["layer_norm.bias"], LN_EPS)
     return _linear(torch.relu(_linear(x, p, "linear_1")), p, "linear_2")
 
@@ -276,6 +289,7 @@ class PairEmbedFn(torch.autograd.Function):
     def forward(ctx, s, mask, weight, bias):
         ctx.save_for_backward(s, weight)
         ctx.has_bias = bias is not None
+        ctx.bias_dtype = None if bias is None else bias.dtype
         p, pm = ops.pair_embed(s, mask, weight, bias, with_mask=mask is not None)
         if pm is not None:
             ctx.mark_non_differentiable(pm)
@@ -296,5 +310,5 @@ class PairEmbedFn(torch.autograd.Function):
         if ctx.needs_input_grad[2]:
             dw = torch.cat([du.reshape(-1, c_p).t() @ sf, dv.reshape(-1, c_p).t() @ sf], dim=1).to(weight.dtype)
         if ctx.has_bias and ctx.needs_input_grad[3]:
-            db = dv.sum((0, 1))
+            db = dv.sum((0, 1)).to(ctx.bias_dtype)
         return ds, None, dw, db

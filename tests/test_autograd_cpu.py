@@ -112,3 +112,34 @@ def test_needs_grad_follows_autograd_state(AG):
         q.requires_grad_(False)
     assert not AG.needs_grad(x, lin)
     assert AG.needs_grad(x.requires_grad_(True), lin)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_half_precision_parameters_get_gradients_in_their_dtype(AG, dtype):
+    """A model converted to bf16 / fp16: the fp32 recomputations cast its parameters
+    differentiably, so the gradients come back in the parameters' dtype and equal the fp32
+    model's gradients evaluated at the rounded parameters."""
+    gen, z, mask, w = _case(7, N=9)
+    for kind in ("trimul", "triatt", "transition"):
+        if kind == "trimul":
+            p = O.make_trimul_params(128, 128, gen, gate_bias=1.0)
+        elif kind == "triatt":
+            p = O.make_triatt_params(128, 128, 4, gen, gate_bias=1.0)
+        else:
+            p = O.make_transition_params(128, 4, gen)
+        half = {k: v.to(dtype).requires_grad_(True) for k, v in p.items()}
+        full = {k: v.detach().float().requires_grad_(True) for k, v in half.items()}
+        grads = []
+        for params in (half, full):
+            leaves = list(params.values())
+            if kind == "trimul":
+                out = AG.trimul_recompute(z, mask, params, True)
+                grads.append(torch.autograd.grad((out * w).sum(), leaves))
+            elif kind == "transition":
+                out = AG.transition_recompute(z, params)
+                grads.append(torch.autograd.grad((out * w).sum(), leaves))
+            else:
+                grads.append(AG.triatt_backward(z, mask, params, True, 4, 1e9, w, leaves, 4))
+        for gh, gf, t in zip(grads[0], grads[1], half.values()):
+            assert gh.dtype == t.dtype, (kind, gh.dtype)
+            assert _rel(gh.float(), gf) < 1e-2, (kind, _rel(gh.float(), gf))

@@ -222,3 +222,38 @@ def test_pair_transform_layer_training_step_matches_oracle():
     for blk, p in lp2.items():
         for k, v in p.items():
             assert _rel(named[f"{blk}.{k}"].grad, v.grad) < 3e-2, (blk, k, _rel(named[f"{blk}.{k}"].grad, v.grad))
+
+
+def test_bf16_model_trains_through_the_kernels():
+    """A model converted with .to(torch.bfloat16) trains: the kernels take the fp32 copy of
+    the pair tensor, the backward casts the bf16 parameters differentiably, and the
+    gradients come back as bf16 close to the fp32 model's."""
+    dev = require_gpu()
+    import copy
+
+    import genie_tk
+    gen = torch.Generator().manual_seed(55)
+    B, N = 1, 40
+    z = torch.randn(B, N, N, 128, generator=gen).to(dev)
+    mask = _masked(B, N, gen).to(dev)
+    w = torch.randn(B, N, N, 128, generator=gen).to(dev)
+    m1 = genie_tk.TriangleMultiplicationOutgoing(128, 128).to(dev)
+    m1.load_state_dict(to_dev(O.make_trimul_params(128, 128, gen, gate_bias=1.0), dev))
+    m2 = genie_tk.TriangleAttentionEndingNode(128, 128, 4).to(dev)
+    m2.load_state_dict(to_dev(O.make_triatt_params(128, 128, 4, gen, gate_bias=1.0), dev))
+    for m32 in (m1, m2):
+        m16 = copy.deepcopy(m32).to(torch.bfloat16)
+        with torch.no_grad():  # compare at the same (bf16-rounded) weights
+            for p16, p32 in zip(m16.parameters(), m32.parameters()):
+                p32.copy_(p16.float())
+        z32 = z.to(torch.bfloat16).float().requires_grad_(True)
+        (m32(z32, mask) * w).sum().backward()
+        z16 = z.to(torch.bfloat16).requires_grad_(True)
+        out16 = m16(z16, mask)
+        assert out16.dtype == torch.bfloat16
+        (out16.float() * w).sum().backward()
+        assert z16.grad.dtype == torch.bfloat16 and _rel(z16.grad, z32.grad) < 2e-2
+        for p16, p32 in zip(m16.parameters(), m32.parameters()):
+            assert p16.grad.dtype == torch.bfloat16
+            assert _rel(p16.grad, p32.grad) < 2e-2
+    assert_status_clean(dev)
