@@ -49,25 +49,9 @@ def needs_grad(x: Tensor, module: torch.nn.Module) -> bool:
 # The N^3 contraction on the library's kernel
 # --------------------------------------------------------------------------------------
 
-def _to_planes(t: Tensor, transpose: bool):
-    """fp32 pair tensor [B, N, N, C] -> (fp16 planes [B, N, C, ld] of t / amax, amax).
-    Plane row r, column col hold t[b, r, col, c] (``transpose``: t[b, col, r, c])."""
-    B, N, _, C = t.shape
-    amax = t.detach().abs().amax().clamp_min(1e-30)
-    view = t.permute(0, 2, 3, 1) if transpose else t.permute(0, 1, 3, 2)
-    planes = torch.zeros(B, N, C, ops.plane_pitch(N), dtype=torch.float16, device=t.device)
-    planes[..., :N] = (view / amax).to(torch.float16)
-    return planes, amax
-
-
-def _contract(p: Tensor, tp: bool, q: Tensor, tq: bool, outgoing: bool) -> Tensor:
-    """out(P, Q) (outgoing) or inc(P, Q) of fp32 pair tensors, P / Q optionally pair-
-    transposed first, on gtk_trimul_contract; fp32 [B, N, N, C]."""
-    N = p.shape[1]
-    pp, sp = _to_planes(p, tp)
-    qp, sq = _to_planes(q, tq)
-    x = ops.trimul_contract(pp, qp, outgoing, N, N, N, out_scale=1.0 / N)
-    return x[..., :N].permute(0, 1, 3, 2).float() * (sp * sq * N)
+# out(P, Q) / inc(P, Q) of fp32 pair tensors on the contraction kernel (module-level name,
+# so that tests on the CPU can put an einsum with the same contract in its place)
+_contract = ops.pair_contract
 
 
 class _Contract(torch.autograd.Function):

@@ -235,6 +235,35 @@ def trimul_contract(a: torch.Tensor, b: torch.Tensor, outgoing: bool, M: int, Nj
     return out
 
 
+def _pair_planes(t: torch.Tensor, transpose: bool):
+    """fp32 pair tensor [B, N, N, C] -> (fp16 planes [B, N, C, ld] of t / amax, amax).
+    Plane row r, column col hold t[b, r, col, c] (``transpose``: t[b, col, r, c])."""
+    B, N, _, C = t.shape
+    amax = t.detach().abs().amax().clamp_min(1e-30)
+    view = t.permute(0, 2, 3, 1) if transpose else t.permute(0, 1, 3, 2)
+    planes = torch.zeros(B, N, C, plane_pitch(N), dtype=torch.float16, device=t.device)
+    planes[..., :N] = (view / amax).to(torch.float16)
+    return planes, amax
+
+
+def pair_contract(p: torch.Tensor, transpose_p: bool, q: torch.Tensor, transpose_q: bool,
+                  outgoing: bool) -> torch.Tensor:
+    """The triangle contraction of two pair tensors [B, N, N, C] on the contraction kernel:
+    out(P, Q)[b,i,j,c] = sum_k P[b,i,k,c] Q[b,j,k,c] (``outgoing``) or
+    inc(P, Q)[b,i,j,c] = sum_k P[b,k,i,c] Q[b,k,j,c], with P / Q pair-transposed first when
+    asked. Each operand goes to the kernel as fp16 planes scaled by its own max-abs (11
+    significant bits at any magnitude); the result is fp32."""
+    _require_cuda(p, "p")
+    _require_cuda(q, "q")
+    if p.dim() != 4 or p.shape != q.shape or p.shape[1] != p.shape[2]:
+        raise ValueError(f"pair tensors must both be [B, N, N, C], got {tuple(p.shape)} and {tuple(q.shape)}")
+    N = p.shape[1]
+    pp, sp = _pair_planes(p.float(), transpose_p)
+    qp, sq = _pair_planes(q.float(), transpose_q)
+    x = trimul_contract(pp, qp, outgoing, N, N, N, out_scale=1.0 / N)
+    return x[..., :N].permute(0, 1, 3, 2).float() * (sp * sq * N)
+
+
 def trimul_finish(z: torch.Tensor, x: torch.Tensor, packed: torch.Tensor, x_scale: float,
                   out: Optional[torch.Tensor] = None, add_residual: bool = False) -> torch.Tensor:
     """Stage K2e: LN_out + linear_z + gate (+ residual) for z [B, R, N, 128] and x planes
@@ -414,6 +443,32 @@ def transition_forward(z: torch.Tensor, mask: Optional[torch.Tensor], packed: to
                                     ws.numel(), B, N, SUPPORTED_C, 4, _ptr(status_buffer(zf.device)),
                                     _stream(zf.device))
     _lib.check(rc, "gtk_transition_forward")
+    return out
+
+
+# --------------------------------------------------------------------------------------
+# LayerNorm over the last axis (the reference's _C.layernorm)
+# --------------------------------------------------------------------------------------
+
+def layernorm(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: float = 1e-5,
+              out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """LayerNorm over the last axis in fp32 (gtk_layernorm); returns fp32 of x's shape."""
+    lib = _lib.load()
+    _require_cuda(x, "x")
+    D = x.shape[-1]
+    xf = x.float().contiguous()
+    g = gamma.detach().float().contiguous()
+    b = beta.detach().float().contiguous()
+    _require_cuda(g, "gamma")
+    _require_cuda(b, "beta")
+    if g.numel() != D or b.numel() != D:
+        raise ValueError(f"gamma and beta must have {D} elements")
+    if out is None:
+        out = torch.empty_like(xf)
+    _require_cuda(out, "out", torch.float32)
+    rows = xf.numel() // D
+    _lib.check(lib.gtk_layernorm(_ptr(xf), _ptr(g), _ptr(b), _ptr(out), rows, D, float(eps), _stream(x.device)),
+               "gtk_layernorm")
     return out
 
 

@@ -365,6 +365,15 @@ GTK_API int gtk_triatt_forward_dropout(int starting, const float* z, const float
                                        size_t workspace_bytes, int64_t B, int64_t N, int c_in, int c_hidden,
                                        int heads, float inf, uint32_t* status, void* stream);
 
+/* ---------------------------------------------------------------------------------
+ * LayerNorm over the last axis: the reference's `_C.layernorm(x, gamma, beta, eps)`
+ * (kernels/bindings.cpp:93-95; host code kernels/fused_layernorm/layernorm.cu:17-44).
+ * x, out fp32 [rows, D] (out may equal x); gamma, beta fp32 [D]; biased variance.
+ * The Python `genie_tk._C.fused_layernorm_linear` is this plus one library GEMM.
+ * ------------------------------------------------------------------------------- */
+GTK_API int gtk_layernorm(const float* x, const float* gamma, const float* beta, float* out, int64_t rows,
+                          int64_t D, float eps, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
