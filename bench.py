@@ -705,7 +705,18 @@ def run_embed(args, device, c_s: int = 384):
             "torch_fp32_reference_ops_ms": ms_torch, "max_abs_diff_vs_torch_fp32": diff}
 
 
+def claim_stdout():
+    """Keep the process's stdout for the one JSON result line. Everything else written to
+    file descriptor 1 -- NCCL's version banner at communicator set-up, library messages,
+    stray prints -- goes to stderr instead. Returns the stream for the result."""
+    sys.stdout.flush()
+    result = os.fdopen(os.dup(1), "w", buffering=1)
+    os.dup2(2, 1)
+    return result
+
+
 def main():
+    result = claim_stdout()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
@@ -737,14 +748,14 @@ def main():
     if args.impl == "reference":
         line = run_reference(args, rank)
         if line is not None:
-            print(json.dumps(line), flush=True)
+            print(json.dumps(line), file=result, flush=True)
         return 0
 
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
     if args.op in ("transition", "embed"):
         print(json.dumps(run_transition(args, device) if args.op == "transition" else run_embed(args, device)),
-              flush=True)
+              file=result, flush=True)
         return 0
     if world > 1:
         from datetime import timedelta
@@ -767,7 +778,7 @@ def main():
                                           f"plus {args.cpu_rows} output rows per op, per-row part scaled to "
                                           f"{args.N} rows; mean of the per-layer estimates"}
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        print(json.dumps(line), file=result, flush=True)
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
