@@ -597,7 +597,7 @@ def run_sharded(args, rank, world, device):
 
 def read_traffic(kernel):
     """DRAM bytes per launch of `kernel` from the committed ncu summary, if present."""
-    path = os.path.join(REPO, "profiles", "traffic.txt")
+    path = os.path.join(REPO, "profiles", "triatt_core_dram_traffic_stack_cfg5_N1024.txt")
     try:
         with open(path) as f:
             for line in f:
