@@ -256,10 +256,10 @@ class TransitionFn(torch.autograd.Function):
         return (g[0], None, *g[1:])
 
 
-def attention_chunk_rows(N: int, heads: int, budget_bytes: int = 2 << 30) -> int:
+def attention_chunk_rows(N: int, heads: int, B: int = 1, budget_bytes: int = 2 << 30) -> int:
     """Rows per recompute chunk so that one chunk's fp32 scores (about six live copies of
-    [rows, H, N, N] during its backward) stay within ``budget_bytes``."""
-    per_row = 6 * heads * N * N * 4
+    [B, rows, H, N, N] during its backward) stay within ``budget_bytes``."""
+    per_row = 6 * B * heads * N * N * 4
     return max(1, min(N, budget_bytes // max(per_row, 1)))
 
 

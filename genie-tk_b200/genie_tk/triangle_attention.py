@@ -67,7 +67,7 @@ class TriangleAttention(nn.Module):
             sd = dict(self.named_parameters())
             N = x.shape[1]
             upd = autograd.TriAttFn.apply(x.float().contiguous(), mask, packed, self.starting, float(self.inf),
-                                          self.no_heads, autograd.attention_chunk_rows(N, self.no_heads),
+                                          self.no_heads, autograd.attention_chunk_rows(N, self.no_heads, x.shape[0]),
                                           *[sd[k] for k in ops.TRIATT_KEYS])
             res = x.float() + upd if add_residual else upd
             return res if res.dtype == x.dtype else res.to(x.dtype)

@@ -98,6 +98,7 @@ def test_transition_recompute_matches_oracle(AG):
 
 def test_chunk_rows_bound_the_score_memory(AG):
     assert AG.attention_chunk_rows(1024, 4) == (2 << 30) // (6 * 4 * 1024 * 1024 * 4)
+    assert AG.attention_chunk_rows(1024, 4, B=4) == (2 << 30) // (6 * 4 * 4 * 1024 * 1024 * 4)
     assert AG.attention_chunk_rows(16, 4) == 16
     assert AG.attention_chunk_rows(100000, 4) == 1
 
