@@ -22,8 +22,8 @@ def require_gpu():
 
 def assert_parity(got: torch.Tensor, ref: torch.Tensor, max_abs: float = MAX_ABS, mean_abs: float = MEAN_ABS,
                   what: str = ""):
-    got = got.float()
-    ref = ref.float().to(got.device)
+    got = got.detach().float()
+    ref = ref.detach().float().to(got.device)
     assert got.shape == ref.shape, (got.shape, ref.shape)
     assert torch.isfinite(got).all(), f"{what}: non-finite values"
     d = (got - ref).abs()
