@@ -613,15 +613,22 @@ def run_transition(args, device):
     """``--op transition``: the pair transition (LN -> 4x expand -> ReLU -> project) with the
     pair transform layer's residual and mask, p = (p + transition(p)) * mask, on one GPU
     (N^2 pairs per step, B = 1, seeded synthetic z and weights). Not the BASELINE metric; it
-    measures the SURVEY 8(f) transition kernels against their HBM roofline and against
-    the same math as unfused fp32 PyTorch ops on the GPU."""
+    measures the pair-transition kernels against their HBM roofline and against the same
+    math as unfused fp32 PyTorch ops on the GPU."""
     from genie_tk import ops
-    from oracle import triangle_oracle as O
     N = args.N
     gen = torch.Generator().manual_seed(5)
     z = torch.randn(1, N, N, 128, generator=gen).to(device)
     mask = torch.ones(1, N, N, device=device)
-    p = {k: v.to(device) for k, v in O.make_transition_params(128, 4, gen).items()}
+    # seeded PairTransition parameters: LayerNorm near identity, weights N(0, 1/fan_in),
+    # small biases (linear_2 is not the reference's zero init, so the update is not zero)
+    p = {"layer_norm.weight": 1.0 + 0.1 * torch.randn(128, generator=gen),
+         "layer_norm.bias": 0.1 * torch.randn(128, generator=gen),
+         "linear_1.weight": torch.randn(512, 128, generator=gen) / math.sqrt(128),
+         "linear_1.bias": 0.1 * torch.randn(512, generator=gen),
+         "linear_2.weight": torch.randn(128, 512, generator=gen) / math.sqrt(512),
+         "linear_2.bias": 0.1 * torch.randn(128, generator=gen)}
+    p = {k: v.to(device) for k, v in p.items()}
     packed = ops.pack_transition(p, device)
     out = torch.empty_like(z)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

@@ -1,7 +1,7 @@
 """Generate the golden vectors in this directory from the reference's own modules.
 
-Run in a container where the reference is mounted (it is read from
-``$GTK_REFERENCE_ROOT``, default ``/root/reference``)::
+Run where the reference is mounted (its root is ``$GTK_REFERENCE_ROOT``, defaulting to
+the mount point named in ``oracle/reference_copy.py``)::
 
     python tests/golden/make_golden.py              # triangle blocks and the 2-layer stack
     python tests/golden/make_golden.py transition   # the pair transition
