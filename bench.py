@@ -41,7 +41,6 @@ import statistics
 import subprocess
 import sys
 import tempfile
-import time
 
 REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(REPO, "genie-tk_b200"))

@@ -12,7 +12,6 @@ from __future__ import annotations
 import math
 from typing import List, Optional
 
-import torch
 import torch.nn as nn
 from torch import Tensor
 

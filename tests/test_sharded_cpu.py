@@ -3,7 +3,6 @@ real ``gloo`` ranks, with the stage computations done by the CPU stand-ins of
 ``shard_cpu_ops`` (the oracle's math in the kernels' byte layouts). Checked against
 the unsharded oracle stack and against an unsharded (P = 1) run of the same program."""
 
-import os
 
 import pytest
 import torch
