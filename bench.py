@@ -21,13 +21,20 @@ recorded between the kernels (captured into the graph) give each kernel's device
 * ``cpu_baseline``: the reference math (the fp32 PyTorch oracle) on this host's cores, on
   a row sample of one N=1024 layer (rank 0 at N=1 only).
 
-``--impl reference`` times that CPU implementation alone (rank 0), one layer sample per step.
+``--impl reference`` times that CPU implementation alone (rank 0). Each step is one row
+sample of one N=1024 layer (a quarter of the output rows by default); ``ms_per_step`` is the
+wall time the step took, and ``value`` is the full-layer throughput estimated from the sample
+(labelled as such in the line).
 
 With --gpus N > 1 (torchrun, one process per GPU) the same N=1024 problem is row-sharded
-over the ranks (``genie_tk.sharded``: NCCL all-gathers of the b planes and of the triangle
-bias, all-to-all transposes for the incoming update and the ending node), so the scaling
-is strong: ``value`` is the one problem's layers*N^2/s, timed on each rank's stream with
-CUDA events and reduced with MAX over ranks.
+over the ranks (``genie_tk.sharded``). By default the exchanges (the gathered or
+channel-sharded planes of the multiplicative update, the triangle bias, the ending node's
+pair transposes) are push kernels that store straight into the peers' buffers over NVLink,
+with NCCL used only for set-up (``--exchange nccl`` runs them as NCCL collectives). The
+scaling is strong: ``value`` is the one problem's layers*N^2/s, timed on each rank's stream
+with CUDA events and reduced with MAX over ranks. After the timed region the ranks' output
+shards are gathered on rank 0 and compared with a one-GPU run of the same stack on the same
+input (``parity`` in the line).
 """
 
 from __future__ import annotations
@@ -184,6 +191,14 @@ def cpu_model():
 
 
 def run_reference(args, rank):
+    """The reference arm: the reference's fp32 PyTorch math (oracle port) on all host cores.
+
+    Each step times one row sample of one N x N layer: the row-independent parts of the four
+    ops over all pairs, then ``--cpu-rows`` output rows of each op. ``ms_per_step`` is the
+    measured wall time of a step. ``value`` is the estimated full-layer throughput: the
+    per-row part scales linearly with the rows, so a layer takes sum(t_prepare + t_rows * N /
+    rows); it is labelled a row-sample estimate (``value_kind``)."""
+    import time
     if rank != 0:
         return None
     N = args.N
@@ -191,25 +206,32 @@ def run_reference(args, rank):
     fn = cpu_sample(N, args.cpu_rows, threads)
     for _ in range(args.warmup):
         fn()
-    ests, measured = [], 0.0
+    ests, walls = [], []
     for _ in range(args.steps):
+        t0 = time.perf_counter()
         est, parts, tot = fn()
+        walls.append(time.perf_counter() - t0)
         ests.append(est)
-        measured += tot
     layer_s = statistics.mean(ests)
     value = N * N / layer_s
+    frac = min(1.0, args.cpu_rows / N)
     sample = (f"one {N}x{N} layer (4 ops) of the reference fp32 PyTorch math per step: row-independent parts "
-              f"over all pairs plus {args.cpu_rows} output rows per op, per-row part scaled to {N} rows")
+              f"over all pairs plus {args.cpu_rows} of {N} output rows per op ({frac:.0%} of the rows); the "
+              f"per-row part is scaled to {N} rows for the value")
+    ms_step = statistics.mean(walls) * 1e3
     return {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": layer_s * 1e3 * args.layers,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "value_kind": f"row-sample estimate: {args.cpu_rows} of {N} rows timed per step, scaled to a full "
+                          f"layer",
+            "estimated_full_layer_ms": layer_s * 1e3,
+            "estimated_full_stack_ms": layer_s * 1e3 * args.layers,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "config": {"workload": f"cfg5 triangle pair stack, B=1 N={N} c_z=128, "
-                                                        f"{args.layers} layers (CPU row sample)",
+                                                        f"{args.layers} layers (CPU row sample of one layer)",
                                             "global_batch": 1, "seq_len": N, "parallelism": "cpu"},
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample,
-                             "cpu": cpu_model(), "measured_s": measured},
+                             "cpu": cpu_model(), "measured_s": round(sum(walls), 2)},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-
 
 
 def run_e2e(args, stack, mask, z_host, z_ref, device, world, B, L, N):
@@ -436,10 +458,10 @@ def run_ours(args, rank, world, device):
                         "unit": unit, "frac": round(ach / peak, 4)}
     dom = max(kernels, key=lambda k: kernels[k]["share"])
     dk = kernels[dom]
-    traffic = read_traffic(dom)
+    traffic, traffic_note = read_traffic(dom)
     roofline = {"kernel": dom, "bound": dk["bound"], "achieved": dk["achieved"],
                 "peak": peaks["bf16_tflops"] if dk["bound"] == "tensor" else peaks["hbm_gbs"],
-                "unit": dk["unit"], "frac": dk["frac"], "traffic": traffic,
+                "unit": dk["unit"], "frac": dk["frac"], "traffic": traffic, "traffic_source": traffic_note,
                 "peak_source": peaks["source"] + " (MEASURED_PEAKS.json burst)" if peaks["source"] == "measured"
                 else "fallback"}
     stack_tflops = B * N * N * L * layer_flops(N) / (ms_per_step / 1e3) / 1e12 * world
@@ -558,6 +580,8 @@ def run_sharded(args, rank, world, device):
         e2e = {"value": B * L * N * N / (e_ms / 1e3), "unit": UNIT,
                "h2d_bytes_per_step": z_host.numel() * 4 * world, "d2h_bytes_per_step": out_host.numel() * 4 * world,
                "ms_per_step": e_ms, "note": "each rank copies its own row shard in and out"}
+    parity = sharded_parity(stack, shard_step=step, z_out=z, rank=rank, world=world, device=device,
+                            mask=mask, N=N, B=B)
     peaks = load_peaks()
     stack_tflops = B * N * N * L * layer_flops(N) / (ms_per_step / 1e3) / 1e12
     stage_kernels = ("triatt_core", "trimul_contract", "trimul_project", "trimul_project_to", "trimul_finish",
@@ -578,7 +602,9 @@ def run_sharded(args, rank, world, device):
             "config": {"workload": f"cfg5 triangle pair stack: B={B}, N={N}, c_z=128, c=128, H=4, d=32, "
                                    f"{L} layers x [TriMulOut, TriMulIn, TriAttStart, TriAttEnd]",
                        "global_batch": B, "seq_len": N, "layers": L,
-                       "parallelism": f"row-sharded over i, {world} ranks x {R} rows (NCCL)",
+                       "parallelism": f"row-sharded over i, {world} ranks x {R} rows; exchanges: " + (
+                           "peer push kernels over NVLink (NCCL for set-up only)" if args.exchange == "peer"
+                           else "NCCL collectives"),
                        "trimul_exchange": shard.trimul_exchange, "exchange": args.exchange,
                        "k1_direct": bool(args.k1_direct and args.exchange == "peer" and shard.trimul_exchange == "channels"),
                        "push": args.push,
@@ -589,23 +615,81 @@ def run_sharded(args, rank, world, device):
                 "kernel": dom, "bound": bound, "achieved": round(ach, 1), "peak": peak, "unit": unit,
                 "frac": round(ach / peak, 4), "traffic": None, "peak_source": peaks["source"],
                 "note": "rank 0's eager per-kernel timing of one extra step"},
-            "breakdown_rank0": breakdown, "clocks": clocks, "status_word": status}
+            "breakdown_rank0": breakdown, "parity": parity, "clocks": clocks, "status_word": status}
     shard.close()
     return line
 
 
+def sharded_parity(stack, shard_step, z_out, rank, world, device, mask, N, B):
+    """Correctness of the row-sharded run: one more sharded step (every rank), its output
+    shards gathered on every rank, and on rank 0 a one-GPU run of the same stack (same
+    weights) on the same full input, compared element by element. The one-GPU stack is the
+    path the parity tests check against the fp32 oracle of the reference math."""
+    import torch.distributed as dist
+    shard_step()
+    torch.cuda.synchronize()
+    full = torch.empty((world,) + tuple(z_out.shape[1:]), dtype=z_out.dtype, device=device)
+    dist.all_gather_into_tensor(full, z_out.contiguous())
+    result = None
+    if rank == 0:
+        gen = torch.Generator(device="cpu").manual_seed(4)
+        z_in = torch.randn(B, N, N, 128, generator=gen).to(device)
+        ref = torch.empty_like(z_in)
+        stack.forward_into(z_in, ref, mask)
+        torch.cuda.synchronize()
+        got = full.view(B, N, N, 128)
+        d = (got - ref).abs()
+        mx, mn = float(d.max()), float(d.mean())
+        result = {"vs": "one-GPU TrianglePairStack run of the same weights and input on rank 0",
+                  "max_abs": mx, "mean_abs": mn, "bitwise_equal": bool(torch.equal(got, ref)),
+                  "finite": bool(torch.isfinite(got).all()),
+                  "bar": {"max_abs": 2e-2, "mean_abs": 2e-3}, "ok": bool(mx <= 2e-2 and mn <= 2e-3)}
+        del z_in, ref, d
+    del full
+    dist.barrier()
+    return result
+
+
+# CUDA sources each kernel is compiled from (its file and the shared device header)
+KERNEL_SOURCES = {
+    "triatt_core": ("triatt.cu", "gtk_sm100.cuh"), "triatt_project": ("triatt.cu", "gtk_sm100.cuh"),
+    "triatt_finish": ("triatt.cu", "gtk_sm100.cuh"), "trimul_project": ("trimul.cu", "gtk_sm100.cuh"),
+    "trimul_contract": ("trimul.cu", "gtk_sm100.cuh"), "trimul_finish": ("trimul.cu", "gtk_sm100.cuh"),
+}
+TRAFFIC_FILE = os.path.join(REPO, "profiles", "triatt_core_dram_traffic_stack_cfg5_N1024.txt")
+
+
+def source_sha16(kernel):
+    """First 16 hex digits of the SHA-256 of the CUDA sources ``kernel`` is built from."""
+    import hashlib
+    h = hashlib.sha256()
+    for f in KERNEL_SOURCES.get(kernel, ()):
+        with open(os.path.join(REPO, "genie-tk_b200", "csrc", f), "rb") as fh:
+            h.update(fh.read())
+    return h.hexdigest()[:16]
+
+
 def read_traffic(kernel):
-    """DRAM bytes per launch of `kernel` from the committed ncu summary, if present."""
-    path = os.path.join(REPO, "profiles", "triatt_core_dram_traffic_stack_cfg5_N1024.txt")
+    """DRAM bytes per launch of ``kernel`` at the bench workload, from the committed ncu
+    summary, and a note. The summary records the hash of the sources it was captured from;
+    when the kernel's sources have changed since, the figure is stale and not reported."""
+    vals, shas = {}, {}
     try:
-        with open(path) as f:
+        with open(TRAFFIC_FILE) as f:
             for line in f:
                 parts = line.split()
-                if len(parts) >= 2 and parts[0] == kernel:
-                    return float(parts[1])
+                if len(parts) >= 3 and parts[0] == "source_sha16":
+                    shas[parts[1]] = parts[2]
+                elif len(parts) >= 2 and not line.startswith("#"):
+                    vals[parts[0]] = float(parts[1])
     except OSError:
-        pass
-    return None
+        return None, "no ncu capture committed"
+    if kernel not in vals:
+        return None, "no ncu capture of this kernel committed"
+    if shas.get(kernel) != source_sha16(kernel):
+        return None, "the committed ncu capture is of older kernel sources; not reported"
+    return vals[kernel], "ncu dram__bytes_read.sum + dram__bytes_write.sum, per launch (" + \
+        os.path.relpath(TRAFFIC_FILE, REPO) + ")"
 
 
 def run_transition(args, device):
@@ -730,7 +814,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--N", type=int, default=1024)
     ap.add_argument("--layers", type=int, default=8)
-    ap.add_argument("--cpu-rows", type=int, default=96)
+    ap.add_argument("--cpu-rows", type=int, default=256,
+                    help="output rows per op timed by the CPU reference math (scaled to N rows)")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],

@@ -22,6 +22,17 @@ c_int = ctypes.c_int
 c_vp = ctypes.c_void_p
 c_size = ctypes.c_size_t
 
+# Return codes of include/genie_tk_b200.h (tests/test_capi_cpu.py checks that these match
+# the header).
+GTK_OK = 0
+GTK_ERR_INVALID_ARG = -1
+GTK_ERR_UNSUPPORTED = -2
+GTK_ERR_ALIGNMENT = -3
+GTK_ERR_WORKSPACE = -4
+GTK_ERR_CUDA = -5
+GTK_ERR_TMAP = -6
+GTK_ERR_DEVICE = -7
+
 
 class TrimulParams(ctypes.Structure):
     """Mirror of ``gtk_trimul_params`` (include/genie_tk_b200.h)."""

@@ -119,7 +119,9 @@ GTK_API int gtk_trimul_forward(int outgoing, const float* z, const float* mask, 
  * GTK_ERR_WORKSPACE with a message naming the limit. Nothing in the scratch needs to
  * start at zero: every byte a call reads was written earlier in the same call.
  * The first call on a device looks up the scratch address on that device (the device
- * must be current); make that first call before any stream capture. All calls share the
+ * must be current); make that first call before any stream capture. That address is kept
+ * for the life of the process, so after a cudaDeviceReset of a device this entry point
+ * must not be called on that device again in the same process. All calls share the
  * one array, so calls whose work overlaps on the GPU (different streams, or different
  * host threads without ordering) race on it: serialise them.
  * No counterpart in the reference (its `_C` functions allocate their outputs). */

@@ -8,6 +8,8 @@ import re
 
 import pytest
 
+import genie_tk._lib as L
+
 REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 HEADER = os.path.join(REPO, "include", "genie_tk_b200.h")
 
@@ -96,7 +98,7 @@ def test_unsupported_shapes_fail_before_touching_the_device(lib):
 def test_invalid_arguments_are_rejected(lib):
     # workspace too small is detected from the sizes alone
     rc = lib.gtk_trimul_forward(1, None, None, None, None, 0, None, 0, 1, 16, 128, 128, None, None)
-    assert rc == -4
+    assert rc == L.GTK_ERR_WORKSPACE
     # a NULL pair tensor is rejected before any launch
     rc = lib.gtk_trimul_project(None, None, None, None, None, 16, 1, 16, 16, None, None)
     assert rc == -1
@@ -120,7 +122,7 @@ def test_transition_entry_points(lib):
     assert lib.gtk_transition_forward(None, None, None, None, 0, None, 0, 1, 16, 128, 4, None, None) == -1
     p = ctypes.c_void_p(1 << 20)
     rc = lib.gtk_transition_forward(p, None, p, p, 1, p, 100, 1, 16, 128, 4, None, None)
-    assert rc == -4 and b"workspace" in lib.gtk_last_error_string()
+    assert rc == L.GTK_ERR_WORKSPACE and b"workspace" in lib.gtk_last_error_string()
     assert lib.gtk_transition_pack(None, 128, 4, p, 1 << 20, None) == -1
 
 
@@ -135,7 +137,27 @@ def test_pair_embed_entry_points(lib):
     assert lib.gtk_pair_embed(p, None, p, None, p, None, p, ws, 1, 16, 8, 12, 32, 128, None) == -1
     # workspace too small
     rc = lib.gtk_pair_embed(p, None, p, None, p, None, p, ws - 4, 1, 16, 16, 0, 32, 128, None)
-    assert rc == -4 and b"workspace" in lib.gtk_last_error_string()
+    assert rc == L.GTK_ERR_WORKSPACE and b"workspace" in lib.gtk_last_error_string()
     # misaligned mask
     assert lib.gtk_pair_embed(p, ctypes.c_void_p((1 << 20) + 2), p, None, p, None, p, ws, 1, 16, 16, 0, 32, 128,
                               None) == -3
+
+
+def test_return_codes_match_the_header():
+    text = open(HEADER).read()
+    codes = dict(re.findall(r"#define\s+(GTK_(?:OK|ERR_\w+))\s+\(?(-?\d+)\)?", text))
+    assert codes, "no return codes found in the header"
+    for name, value in codes.items():
+        assert getattr(L, name) == int(value), name
+
+
+def test_noalloc_limit_is_checked_from_the_sizes_alone(lib):
+    """gtk_trimul_forward_noalloc refuses sizes past its built-in scratch before it looks at
+    a pointer or a device: B * N * round_up(N, 8) <= 32768."""
+    for B, N in ((2, 129), (1, 256), (3, 128)):
+        rc = lib.gtk_trimul_forward_noalloc(1, None, None, None, None, 0, B, N, 128, 128, None, None)
+        assert rc == L.GTK_ERR_WORKSPACE, (B, N, rc)
+        assert b"32768" in lib.gtk_last_error_string()
+    # at the limit the size passes; the NULL pair tensor (or the missing device) is what fails
+    rc = lib.gtk_trimul_forward_noalloc(1, None, None, None, None, 0, 2, 128, 128, 128, None, None)
+    assert rc in (L.GTK_ERR_INVALID_ARG, L.GTK_ERR_CUDA), rc

@@ -1,5 +1,7 @@
-"""Known answers and edge cases through the kernels (the list of the survey's oracle
-section, checked on the CPU oracle in tests/test_oracle_golden.py, here on the B200):
+"""Known answers and edge cases through the kernels, derived from the reference math
+(src/genie_tk/triangle_mul.py:103-132, src/genie_tk/triangle_attention.py:100-143,
+src/genie_tk/primitives.py:114-178). The same list is checked on the CPU oracle in
+tests/test_oracle_golden.py, here on the B200:
 
 * tiny pair grids, N = 1, 2, 3 and 8 (one partial tile everywhere), for all four blocks;
 * an all-masked multiplicative update: a = b = 0, so x = 0 and LN_out(0) = beta_out, and the
