@@ -1,0 +1,777 @@
+// General-shape path of the triangle blocks and the pair transition (see general.h).
+//
+// Data flow (fp32 unless noted; P = B*N*N pairs in the block's own frame, which is z^T for
+// the ending-node attention):
+//   TriMul     zn[P][c_z] = LN_in(z)
+//              Y[P][4c + c_z] = zn (W_ap | W_ag | W_bp | W_bg | W_g)^T + b
+//              a, b fp16 planes [B][N][c][ld] = proj * sigmoid(gate) * mask, pair-transposed
+//              x planes = K2 contraction (the tcgen05 kernel of trimul.cu), stored times 1/N
+//              xn[P][c] = LN_out(x)                      (in zn's buffer)
+//              out = z + sigmoid(Y_g) * (xn W_z^T + b_z)
+//              (reference src/genie_tk/triangle_mul.py:103-132)
+//   TriAtt     zn[P][c_in] = LN(z or z^T)
+//              Y[P][4hd + H] = zn (W_q | W_k | W_v | W_g | W_b)^T + (0 | 0 | 0 | b_g | 0)
+//              tri[B][H][N][N] = triangle bias in log2 units
+//              og[P][hd] = softmax_k(q.k / sqrt(d) + inf (m - 1) + tri) v * sigmoid(g)
+//              out = z + og W_o^T + b_o, rows written back in z's frame
+//              (reference triangle_attention.py:100-143, primitives.py:114-178)
+//   Transition zn = LN(z); h[P][n c] = relu(zn W_1^T + b_1); out = (z + h W_2^T + b_2) * m
+//              (reference pair_transform.py:64-84, :190-193)
+// Everything but the contraction is fp32 arithmetic on the CUDA cores; LayerNorm and the
+// softmax use the reference's eps (1e-5) and additive mask value.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <string>
+
+#include "general.h"
+
+namespace gtk {
+namespace gen {
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+// Memory row of pair p = (b, r, c) of a block's frame: p itself, or (b, c, r) in the z^T frame.
+__device__ __forceinline__ int64_t frame_row(int64_t p, int64_t N, int tr) {
+  if (!tr) return p;
+  const int64_t NN = N * N;
+  const int64_t b = p / NN, rem = p - b * NN, r = rem / N, c = rem - r * N;
+  return b * NN + c * N + r;
+}
+
+__device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + expf(-x)); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// ---------------------------------------------------------------------------------------
+// LayerNorm of pair rows, one warp per row: out[p] = LN(x[frame_row(p)]) * gamma + beta.
+// ---------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+    ln_kernel(const float* __restrict__ x, const float* __restrict__ gamma, const float* __restrict__ beta,
+              float* __restrict__ out, int64_t rows, int D, int64_t N, int tr, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nw = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  const float inv = 1.f / static_cast<float>(D);
+  for (int64_t p = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; p < rows; p += nw) {
+    const float* xr = x + frame_row(p, N, tr) * D;
+    float s = 0.f;
+    for (int c = lane; c < D; c += 32) s += xr[c];
+    const float mean = warp_sum(s) * inv;
+    float v = 0.f;
+    for (int c = lane; c < D; c += 32) {
+      const float d = xr[c] - mean;
+      v = fmaf(d, d, v);
+    }
+    const float rstd = rsqrtf(warp_sum(v) * inv + eps);
+    float* o = out + p * D;
+    for (int c = lane; c < D; c += 32) o[c] = fmaf((xr[c] - mean) * rstd, gamma[c], beta[c]);
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// C = A W^T (+ epilogue): A [M][K] (pitch lda), W [n_out][K] (pitch ldw), fp32. 64 x 64
+// output tile per CTA, K in steps of 16 through shared memory, 4 x 4 outputs per thread.
+// ---------------------------------------------------------------------------------------
+enum EpiMode : int { kStore = 0, kRelu = 1, kGateRes = 2, kRes = 3, kResMask = 4 };
+
+struct Epi {
+  int mode;
+  const float* bias;  // [n_out] or nullptr
+  float* out;         // kStore / kRelu: [M][ldo]; else pair rows (frame_row), ldo = channels
+  int64_t ldo;
+  const float* z;     // residual pair tensor (may equal out; nullptr: no residual)
+  int64_t N;          // pairs per side, for the pair-row mapping and the dropout vector
+  int tr;             // rows of `out` / `z` are in the z^T frame
+  const float* gate;  // kGateRes: gate logits [M][ldg]
+  int64_t ldg;
+  const float* mask;  // kResMask: [M] (nullptr: ones)
+  DropArgs drop;      // kGateRes / kRes: channel dropout (keep == nullptr: none)
+};
+
+constexpr int kBM = 64, kBN = 64, kBK = 16;
+
+__global__ void __launch_bounds__(256)
+    gemm_kernel(const float* __restrict__ A, int64_t M, int K, int64_t lda, const float* __restrict__ W, int n_out,
+                int64_t ldw, const Epi e) {
+  __shared__ __align__(16) float As[kBK][kBM + 4];
+  __shared__ __align__(16) float Ws[kBK][kBN + 4];
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int64_t m0 = static_cast<int64_t>(blockIdx.x) * kBM;
+  const int n0 = blockIdx.y * kBN;
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+  for (int k0 = 0; k0 < K; k0 += kBK) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int idx = tid + u * 256, r = idx >> 4, kk = idx & 15;
+      const int64_t m = m0 + r;
+      const int k = k0 + kk, n = n0 + r;
+      As[kk][r] = (m < M && k < K) ? A[m * lda + k] : 0.f;
+      Ws[kk][r] = (n < n_out && k < K) ? W[static_cast<int64_t>(n) * ldw + k] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < kBK; ++kk) {
+      const float4 a = *reinterpret_cast<const float4*>(&As[kk][ty * 4]);
+      const float4 w = *reinterpret_cast<const float4*>(&Ws[kk][tx * 4]);
+      const float av[4] = {a.x, a.y, a.z, a.w}, wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], wv[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+  const int64_t NN = e.N * e.N;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t m = m0 + ty * 4 + i;
+    if (m >= M) continue;
+    uint4 keep = make_uint4(0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu);
+    const bool drop = e.drop.keep != nullptr && (e.mode == kGateRes || e.mode == kRes);
+    if (drop) {
+      const int64_t b = m / NN, rem = m - b * NN, r = rem / e.N, j = rem - r * e.N;
+      keep = __ldg(e.drop.keep + b * e.drop.ld + (e.drop.by_row ? r : j));
+    }
+    const int64_t row = (e.mode == kGateRes || e.mode == kRes) ? frame_row(m, e.N, e.tr) : m;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int n = n0 + tx * 4 + j;
+      if (n >= n_out) continue;
+      float v = acc[i][j] + (e.bias ? e.bias[n] : 0.f);
+      if (e.mode == kStore) {
+        e.out[m * e.ldo + n] = v;
+      } else if (e.mode == kRelu) {
+        e.out[m * e.ldo + n] = fmaxf(v, 0.f);
+      } else if (e.mode == kResMask) {
+        const float zr = e.z ? e.z[m * e.ldo + n] : 0.f;
+        e.out[m * e.ldo + n] = (zr + v) * (e.mask ? e.mask[m] : 1.f);
+      } else {
+        if (e.mode == kGateRes) v *= sigmoid_f(e.gate[m * e.ldg + n]);
+        if (drop) v *= ((drop_word(keep, n >> 5) >> (n & 31)) & 1u) ? e.drop.scale : 0.f;
+        const float zr = e.z ? e.z[row * e.ldo + n] : 0.f;
+        e.out[row * e.ldo + n] = zr + v;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// TriMul a, b planes: plane element ((b*N + i)*c + ch)*ld + k = a[b, i, k, ch] with
+// a = Y[p][ch] * sigmoid(Y[p][c + ch]) * m[p], p = (b*N + i)*N + k (b from columns 2c, 3c);
+// zero for k >= N. 32 x 32 tiles transposed through shared memory.
+// ---------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+    trimul_planes_kernel(const float* __restrict__ Y, int64_t ldy, const float* __restrict__ mask,
+                         __half* __restrict__ a, __half* __restrict__ b, int64_t N, int c, int64_t ld) {
+  __shared__ float ta[32][33], tb[32][33];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int64_t row = blockIdx.x;  // b*N + i
+  const int64_t k0 = static_cast<int64_t>(blockIdx.y) * 32;
+  const int c0 = blockIdx.z * 32;
+  for (int kk = ty; kk < 32; kk += 8) {
+    const int64_t k = k0 + kk;
+    const int ch = c0 + tx;
+    float va = 0.f, vb = 0.f;
+    if (k < N && ch < c) {
+      const int64_t p = row * N + k;
+      const float* y = Y + p * ldy;
+      const float m = mask ? mask[p] : 1.f;
+      va = y[ch] * sigmoid_f(y[c + ch]) * m;
+      vb = y[2 * c + ch] * sigmoid_f(y[3 * c + ch]) * m;
+    }
+    ta[kk][tx] = va;
+    tb[kk][tx] = vb;
+  }
+  __syncthreads();
+  for (int cc = ty; cc < 32; cc += 8) {
+    const int ch = c0 + cc;
+    const int64_t k = k0 + tx;
+    if (ch < c && k < ld) {
+      const int64_t o = (row * c + ch) * ld + k;
+      a[o] = f16_sat(ta[tx][cc]);
+      b[o] = f16_sat(tb[tx][cc]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// LN_out of the contraction: xn[p][ch] = LN over ch of x[b][i][ch][j] * gamma + beta, with
+// p = (b*N + i)*N + j. x is stored times 1/N; LayerNorm is scale-invariant once eps is
+// scaled by the same factor squared, which the caller does.
+// ---------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+    x_ln_kernel(const __half* __restrict__ x, int64_t ld, int64_t N, int c, const float* __restrict__ gamma,
+                const float* __restrict__ beta, float eps, float* __restrict__ xn) {
+  extern __shared__ float xs[];  // [c][33]
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int64_t row = blockIdx.x;
+  const int64_t j0 = static_cast<int64_t>(blockIdx.y) * 32;
+  for (int ch = ty; ch < c; ch += 8) {
+    const int64_t j = j0 + tx;
+    xs[ch * 33 + tx] = j < N ? __half2float(x[(row * c + ch) * ld + j]) : 0.f;
+  }
+  __syncthreads();
+  const float inv = 1.f / static_cast<float>(c);
+  for (int jj = ty; jj < 32; jj += 8) {
+    const int64_t j = j0 + jj;
+    if (j >= N) break;  // uniform across the warp
+    float s = 0.f;
+    for (int ch = tx; ch < c; ch += 32) s += xs[ch * 33 + jj];
+    const float mean = warp_sum(s) * inv;
+    float v = 0.f;
+    for (int ch = tx; ch < c; ch += 32) {
+      const float d = xs[ch * 33 + jj] - mean;
+      v = fmaf(d, d, v);
+    }
+    const float rstd = rsqrtf(warp_sum(v) * inv + eps);
+    float* o = xn + (row * N + j) * c;
+    for (int ch = tx; ch < c; ch += 32) o[ch] = fmaf((xs[ch * 33 + jj] - mean) * rstd, gamma[ch], beta[ch]);
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// Triangle bias tri[b][h][j][k] = Y[(b*N + j)*N + k][col0 + h] * log2 e.
+// ---------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+    tri_bias_kernel(const float* __restrict__ Y, int64_t ldy, int col0, int H, int64_t B, int64_t N,
+                    float* __restrict__ tri) {
+  const int64_t total = B * H * N * N;
+  for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t < total;
+       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t k = t % N;
+    int64_t r = t / N;
+    const int64_t j = r % N;
+    r /= N;
+    const int64_t h = r % H, b = r / H;
+    tri[t] = Y[((b * N + j) * N + k) * ldy + col0 + h] * kLog2e;
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// Attention core: CTA = (pair row i of batch b, head h, 128 queries j), thread = query.
+// Keys in tiles of 32 with their values, the bias block [128 j][32 k] and the mask bias
+// staged in shared memory; online softmax in base 2 (scores, bias and mask carry log2 e).
+// s = q.k / sqrt(d) + inf * (m_ik - 1) + tri[b, h, j, k]; og = (sum_k p v_k / sum_k p) *
+// sigmoid(g). The mask is read in the block's frame (m[b, k, i] for the ending node).
+// ---------------------------------------------------------------------------------------
+template <int D>
+__global__ void __launch_bounds__(128)
+    att_core_kernel(const float* __restrict__ Y, int64_t ldy, const float* __restrict__ tri,
+                    const float* __restrict__ mask, int64_t N, int H, int d, int hd, float qscale, float inf2, int tr,
+                    float* __restrict__ og) {
+  __shared__ float Ks[32][D], Vs[32][D];
+  __shared__ float Bs[128][33];
+  __shared__ float Ms[32];
+  const int t = threadIdx.x;
+  const int64_t row = blockIdx.x;  // b*N + i
+  const int h = blockIdx.y;
+  const int64_t j0 = static_cast<int64_t>(blockIdx.z) * 128;
+  const int64_t b = row / N, i = row - b * N;
+  const int64_t j = j0 + t;
+  const bool active = j < N;
+  float q[D], o[D];
+  {
+    const float* yq = Y + (row * N + (active ? j : 0)) * ldy + h * d;
+#pragma unroll
+    for (int e = 0; e < D; ++e) {
+      q[e] = (e < d && active) ? yq[e] * qscale : 0.f;
+      o[e] = 0.f;
+    }
+  }
+  float m = -INFINITY, l = 0.f;
+  const float* trib = tri + (b * H + h) * N * N;
+  for (int64_t k0 = 0; k0 < N; k0 += 32) {
+    __syncthreads();
+    for (int idx = t; idx < 32 * D; idx += 128) {
+      const int kk = idx / D, e = idx - kk * D;
+      const int64_t k = k0 + kk;
+      float kv = 0.f, vv = 0.f;
+      if (k < N && e < d) {
+        const float* y = Y + (row * N + k) * ldy + h * d + e;
+        kv = y[hd];
+        vv = y[2 * hd];
+      }
+      Ks[kk][e] = kv;
+      Vs[kk][e] = vv;
+    }
+    for (int idx = t; idx < 128 * 32; idx += 128) {
+      const int jj = idx >> 5, kk = idx & 31;
+      const int64_t jq = j0 + jj, k = k0 + kk;
+      Bs[jj][kk] = (jq < N && k < N) ? trib[jq * N + k] : 0.f;
+    }
+    if (t < 32) {
+      const int64_t k = k0 + t;
+      float mb = -INFINITY;  // past the last key: never counts
+      if (k < N) {
+        const float mv = mask ? mask[tr ? (b * N + k) * N + i : row * N + k] : 1.f;
+        mb = inf2 * (mv - 1.f);
+      }
+      Ms[t] = mb;
+    }
+    __syncthreads();
+    float s[32];
+    float tmax = -INFINITY;
+#pragma unroll
+    for (int kk = 0; kk < 32; ++kk) {
+      float acc = 0.f;
+#pragma unroll
+      for (int e = 0; e < D; ++e) acc = fmaf(q[e], Ks[kk][e], acc);
+      s[kk] = acc + Bs[t][kk] + Ms[kk];
+      tmax = fmaxf(tmax, s[kk]);
+    }
+    const float mnew = fmaxf(m, tmax);
+    const float corr = exp2f(m - mnew);  // 0 on the first tile (m = -inf)
+    l *= corr;
+#pragma unroll
+    for (int e = 0; e < D; ++e) o[e] *= corr;
+#pragma unroll
+    for (int kk = 0; kk < 32; ++kk) {
+      const float p = exp2f(s[kk] - mnew);  // 0 for keys past N (s = -inf)
+      l += p;
+#pragma unroll
+      for (int e = 0; e < D; ++e) o[e] = fmaf(p, Vs[kk][e], o[e]);
+    }
+    m = mnew;
+  }
+  if (active) {
+    const float* yg = Y + (row * N + j) * ldy + 3 * hd + h * d;
+    float* out = og + (row * N + j) * hd + h * d;
+    const float il = 1.f / l;
+#pragma unroll
+    for (int e = 0; e < D; ++e)
+      if (e < d) out[e] = o[e] * il * sigmoid_f(yg[e]);
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------------------
+static size_t a256(size_t x) { return (x + 255) / 256 * 256; }
+
+static int grid_rows(int64_t rows, int per_block) {
+  const int64_t need = (rows + per_block - 1) / per_block;
+  const int64_t cap = static_cast<int64_t>(num_sms()) * 16;
+  return static_cast<int>(need < 1 ? 1 : (need < cap ? need : cap));
+}
+
+static int launch_ln(const float* x, const float* gamma, const float* beta, float* out, int64_t rows, int D, int64_t N,
+                     int tr, cudaStream_t st) {
+  ln_kernel<<<grid_rows(rows, 8), 256, 0, st>>>(x, gamma, beta, out, rows, D, N, tr, 1e-5f);
+  return check_launch("general ln_kernel");
+}
+
+static int launch_gemm(const float* A, int64_t M, int K, int64_t lda, const float* W, int n_out, int64_t ldw,
+                       const Epi& e, cudaStream_t st) {
+  const int64_t mt = (M + kBM - 1) / kBM;
+  if (mt > 2147483647) return fail(GTK_ERR_INVALID_ARG, "general gemm: too many rows");
+  dim3 grid(static_cast<unsigned>(mt), static_cast<unsigned>((n_out + kBN - 1) / kBN));
+  gemm_kernel<<<grid, 256, 0, st>>>(A, M, K, lda, W, n_out, ldw, e);
+  return check_launch("general gemm_kernel");
+}
+
+static Epi epi(int mode, const float* bias, float* out, int64_t ldo) {
+  Epi e{};
+  e.mode = mode;
+  e.bias = bias;
+  e.out = out;
+  e.ldo = ldo;
+  e.N = 1;
+  return e;
+}
+
+static int copy_d2d(float* dst, const float* src, size_t n, cudaStream_t st) {
+  if (!src) return cudaMemsetAsync(dst, 0, n * 4, st) == cudaSuccess ? GTK_OK : fail(GTK_ERR_CUDA, "memset failed");
+  const cudaError_t e = cudaMemcpyAsync(dst, src, n * 4, cudaMemcpyDeviceToDevice, st);
+  return e == cudaSuccess ? GTK_OK : fail(GTK_ERR_CUDA, std::string("packing copy failed: ") + cudaGetErrorString(e));
+}
+
+static int common_args(const float* z, const float* out, const void* packed, void* workspace, const float* mask,
+                       int64_t B, int64_t N) {
+  if (!dims_ok(B, 65535) || !dims_ok(N, 65535)) return fail(GTK_ERR_INVALID_ARG, "bad B/N");
+  if (int e = check_ptr(z, "z", 4)) return e;
+  if (int e = check_ptr(out, "out", 4)) return e;
+  if (int e = check_ptr(packed, "packed", 256)) return e;
+  if (int e = check_ptr(workspace, "workspace", 256)) return e;
+  if (mask && (reinterpret_cast<uintptr_t>(mask) & 3)) return fail(GTK_ERR_ALIGNMENT, "mask is misaligned");
+  return GTK_OK;
+}
+
+static int drop_channels(const DropArgs& drop, int channels) {
+  if (drop.keep && channels > 128)
+    return fail(GTK_ERR_UNSUPPORTED, "dropout keep vectors hold 128 channels; this block has " +
+                                         std::to_string(channels));
+  return GTK_OK;
+}
+
+// ----------------------------- triangle multiplication ---------------------------------
+// packed floats: W1 [(4c + c_z) x c_z] | b1 [4c + c_z] | W_z [c_z x c] | b_z [c_z] |
+//                ln_in w, b [c_z] | ln_out w, b [c]
+struct TmPack {
+  size_t w1, b1, wz, bz, liw, lib, low, lob, floats;
+};
+static TmPack tm_pack(int cz, int c) {
+  TmPack p{};
+  const size_t rows = 4 * static_cast<size_t>(c) + cz;
+  p.w1 = 0;
+  p.b1 = p.w1 + rows * cz;
+  p.wz = p.b1 + rows;
+  p.bz = p.wz + static_cast<size_t>(cz) * c;
+  p.liw = p.bz + cz;
+  p.lib = p.liw + cz;
+  p.low = p.lib + cz;
+  p.lob = p.low + c;
+  p.floats = p.lob + c;
+  return p;
+}
+
+struct TmWs {
+  size_t zn, y, a, b, x, total;
+};
+static TmWs tm_ws(int64_t B, int64_t N, int cz, int c) {
+  TmWs w{};
+  const size_t P = static_cast<size_t>(B) * N * N;
+  const size_t plane = a256(static_cast<size_t>(B) * N * c * gtk_plane_pitch(N) * 2);
+  w.zn = 0;
+  w.y = a256(P * (cz > c ? cz : c) * 4);
+  w.a = w.y + a256(P * (4 * static_cast<size_t>(c) + cz) * 4);
+  w.b = w.a + plane;
+  w.x = w.b + plane;
+  w.total = w.x + plane;
+  return w;
+}
+
+int trimul_check(int c_z, int c_hidden) {
+  if (c_z < 1 || c_hidden < 1 || c_z > kMaxChannels || c_hidden > kMaxChannels)
+    return fail(GTK_ERR_UNSUPPORTED, "trimul: c_z and c_hidden must be in 1.." + std::to_string(kMaxChannels));
+  return GTK_OK;
+}
+
+size_t trimul_packed_bytes(int c_z, int c_hidden) {
+  if (c_z < 1 || c_hidden < 1 || c_z > kMaxChannels || c_hidden > kMaxChannels) return 0;
+  return a256(tm_pack(c_z, c_hidden).floats * 4);
+}
+
+int trimul_pack(const gtk_trimul_params* params, int c_z, int c_hidden, void* packed, size_t packed_bytes,
+                void* stream) {
+  if (int e = trimul_check(c_z, c_hidden)) return e;
+  if (!params) return fail(GTK_ERR_INVALID_ARG, "params is NULL");
+  if (int e = check_ptr(packed, "packed", 256)) return e;
+  if (packed_bytes < trimul_packed_bytes(c_z, c_hidden)) return fail(GTK_ERR_WORKSPACE, "packed buffer too small");
+  const float* const* pp = reinterpret_cast<const float* const*>(params);
+  for (int i = 0; i < 16; ++i)
+    if (!pp[i]) return fail(GTK_ERR_INVALID_ARG, "a trimul parameter pointer is NULL");
+  if (int e = check_device()) return e;
+  const TmPack L = tm_pack(c_z, c_hidden);
+  float* f = static_cast<float*>(packed);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t c = c_hidden, cz = c_z;
+  const gtk_trimul_params& p = *params;
+  const float* w1_src[5] = {p.a_p_w, p.a_g_w, p.b_p_w, p.b_g_w, p.g_w};
+  const float* b1_src[5] = {p.a_p_b, p.a_g_b, p.b_p_b, p.b_g_b, p.g_b};
+  for (int k = 0; k < 5; ++k) {
+    const size_t rows = k < 4 ? c : cz;
+    if (int e = copy_d2d(f + L.w1 + k * c * cz, w1_src[k], rows * cz, st)) return e;
+    if (int e = copy_d2d(f + L.b1 + k * c, b1_src[k], rows, st)) return e;
+  }
+  if (int e = copy_d2d(f + L.wz, p.z_w, cz * c, st)) return e;
+  if (int e = copy_d2d(f + L.bz, p.z_b, cz, st)) return e;
+  if (int e = copy_d2d(f + L.liw, p.ln_in_w, cz, st)) return e;
+  if (int e = copy_d2d(f + L.lib, p.ln_in_b, cz, st)) return e;
+  if (int e = copy_d2d(f + L.low, p.ln_out_w, c, st)) return e;
+  return copy_d2d(f + L.lob, p.ln_out_b, c, st);
+}
+
+size_t trimul_workspace_bytes(int64_t B, int64_t N, int c_z, int c_hidden) {
+  if (c_z < 1 || c_hidden < 1 || c_z > kMaxChannels || c_hidden > kMaxChannels || B < 1 || N < 1) return 0;
+  return tm_ws(B, N, c_z, c_hidden).total;
+}
+
+int trimul_forward(int outgoing, const float* z, const float* mask, const void* packed, float* out, int add_residual,
+                   const DropArgs& drop, void* workspace, size_t workspace_bytes, int64_t B, int64_t N, int c_z,
+                   int c_hidden, uint32_t* status, void* stream) {
+  if (int e = trimul_check(c_z, c_hidden)) return e;
+  if (int e = common_args(z, out, packed, workspace, mask, B, N)) return e;
+  if (int e = drop_channels(drop, c_z)) return e;
+  const TmWs w = tm_ws(B, N, c_z, c_hidden);
+  if (workspace_bytes < w.total) return fail(GTK_ERR_WORKSPACE, "trimul: workspace too small");
+  if (int e = check_device()) return e;
+  const TmPack L = tm_pack(c_z, c_hidden);
+  const float* pk = static_cast<const float*>(packed);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  float* zn = reinterpret_cast<float*>(ws + w.zn);
+  float* Y = reinterpret_cast<float*>(ws + w.y);
+  __half* ap = reinterpret_cast<__half*>(ws + w.a);
+  __half* bp = reinterpret_cast<__half*>(ws + w.b);
+  __half* xp = reinterpret_cast<__half*>(ws + w.x);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t P = B * N * N;
+  const int c = c_hidden;
+  const int64_t ldy = 4 * static_cast<int64_t>(c) + c_z, ld = gtk_plane_pitch(N);
+  if (int e = launch_ln(z, pk + L.liw, pk + L.lib, zn, P, c_z, N, 0, st)) return e;
+  if (int e = launch_gemm(zn, P, c_z, c_z, pk + L.w1, static_cast<int>(ldy), c_z, epi(kStore, pk + L.b1, Y, ldy), st))
+    return e;
+  {
+    const int64_t kb = (ld + 31) / 32;
+    if (B * N > 2147483647 || kb > 65535) return fail(GTK_ERR_INVALID_ARG, "trimul: N too large");
+    dim3 grid(static_cast<unsigned>(B * N), static_cast<unsigned>(kb), static_cast<unsigned>((c + 31) / 32));
+    trimul_planes_kernel<<<grid, 256, 0, st>>>(Y, ldy, mask, ap, bp, N, c, ld);
+    if (int e = check_launch("general trimul_planes_kernel")) return e;
+  }
+  const float xs = 1.f / static_cast<float>(N);
+  if (int e = gtk_trimul_contract(outgoing, ap, bp, xp, B, c, N, N, N, ld, ld, ld, xs, status, stream)) return e;
+  {
+    // the kernel's dynamic shared memory limit is set once, to the largest channel count
+    const int smem = c * 33 * 4;
+    if (int e = ensure_smem(reinterpret_cast<const void*>(x_ln_kernel), kMaxChannels * 33 * 4)) return e;
+    dim3 grid(static_cast<unsigned>(B * N), static_cast<unsigned>((N + 31) / 32));
+    x_ln_kernel<<<grid, 256, smem, st>>>(xp, ld, N, c, pk + L.low, pk + L.lob, 1e-5f * xs * xs, zn);
+    if (int e = check_launch("general x_ln_kernel")) return e;
+  }
+  Epi e = epi(kGateRes, pk + L.bz, out, c_z);
+  e.z = add_residual ? z : nullptr;
+  e.N = N;
+  e.tr = 0;
+  e.gate = Y + 4 * static_cast<int64_t>(c);
+  e.ldg = ldy;
+  e.drop = drop;
+  return launch_gemm(zn, P, c, c, pk + L.wz, c_z, c, e, st);
+}
+
+// --------------------------------- triangle attention -----------------------------------
+// packed floats: W [(4hd + H) x c_in] (q | k | v | g | bias) | b [4hd + H] (0 | 0 | 0 | b_g | 0) |
+//                W_o [c_in x hd] | b_o [c_in] | ln w, b [c_in]
+struct TaPack {
+  size_t w, b, wo, bo, lw, lb, floats;
+};
+static TaPack ta_pack(int cin, int hd, int H) {
+  TaPack p{};
+  const size_t rows = 4 * static_cast<size_t>(hd) + H;
+  p.w = 0;
+  p.b = rows * cin;
+  p.wo = p.b + rows;
+  p.bo = p.wo + static_cast<size_t>(cin) * hd;
+  p.lw = p.bo + cin;
+  p.lb = p.lw + cin;
+  p.floats = p.lb + cin;
+  return p;
+}
+
+struct TaWs {
+  size_t zn, y, tri, og, total;
+};
+static TaWs ta_ws(int64_t B, int64_t N, int cin, int hd, int H) {
+  TaWs w{};
+  const size_t P = static_cast<size_t>(B) * N * N;
+  w.zn = 0;
+  w.y = a256(P * cin * 4);
+  w.tri = w.y + a256(P * (4 * static_cast<size_t>(hd) + H) * 4);
+  w.og = w.tri + a256(static_cast<size_t>(B) * H * N * N * 4);
+  w.total = w.og + a256(P * hd * 4);
+  return w;
+}
+
+int triatt_check(int c_in, int c_hidden, int heads) {
+  if (c_in < 1 || c_in > kMaxChannels || heads < 1 || heads > kMaxHeads || c_hidden < heads ||
+      c_hidden > kMaxChannels || c_hidden % heads != 0 || c_hidden / heads > kMaxHeadDim)
+    return fail(GTK_ERR_UNSUPPORTED, "triatt: need c_in <= " + std::to_string(kMaxChannels) + ", 1 <= heads <= " +
+                                         std::to_string(kMaxHeads) + ", c_hidden a multiple of heads with head_dim <= " +
+                                         std::to_string(kMaxHeadDim));
+  return GTK_OK;
+}
+
+size_t triatt_packed_bytes(int c_in, int c_hidden, int heads) {
+  if (c_in < 1 || c_in > kMaxChannels || heads < 1 || heads > kMaxHeads || c_hidden < heads ||
+      c_hidden > kMaxChannels || c_hidden % heads != 0 || c_hidden / heads > kMaxHeadDim)
+    return 0;
+  return a256(ta_pack(c_in, c_hidden, heads).floats * 4);
+}
+
+int triatt_pack(const gtk_triatt_params* params, int c_in, int c_hidden, int heads, void* packed,
+                size_t packed_bytes, void* stream) {
+  if (int e = triatt_check(c_in, c_hidden, heads)) return e;
+  if (!params) return fail(GTK_ERR_INVALID_ARG, "params is NULL");
+  if (int e = check_ptr(packed, "packed", 256)) return e;
+  if (packed_bytes < triatt_packed_bytes(c_in, c_hidden, heads))
+    return fail(GTK_ERR_WORKSPACE, "packed buffer too small");
+  const float* const* pp = reinterpret_cast<const float* const*>(params);
+  for (int i = 0; i < 10; ++i)
+    if (!pp[i]) return fail(GTK_ERR_INVALID_ARG, "a triatt parameter pointer is NULL");
+  if (int e = check_device()) return e;
+  const TaPack L = ta_pack(c_in, c_hidden, heads);
+  float* f = static_cast<float*>(packed);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t hd = c_hidden, cin = c_in;
+  const gtk_triatt_params& p = *params;
+  const float* w_src[4] = {p.q_w, p.k_w, p.v_w, p.g_w};
+  for (int k = 0; k < 4; ++k)
+    if (int e = copy_d2d(f + L.w + k * hd * cin, w_src[k], hd * cin, st)) return e;
+  if (int e = copy_d2d(f + L.w + 4 * hd * cin, p.bias_w, static_cast<size_t>(heads) * cin, st)) return e;
+  if (int e = copy_d2d(f + L.b, nullptr, 3 * hd, st)) return e;
+  if (int e = copy_d2d(f + L.b + 3 * hd, p.g_b, hd, st)) return e;
+  if (int e = copy_d2d(f + L.b + 4 * hd, nullptr, heads, st)) return e;
+  if (int e = copy_d2d(f + L.wo, p.o_w, cin * hd, st)) return e;
+  if (int e = copy_d2d(f + L.bo, p.o_b, cin, st)) return e;
+  if (int e = copy_d2d(f + L.lw, p.ln_w, cin, st)) return e;
+  return copy_d2d(f + L.lb, p.ln_b, cin, st);
+}
+
+size_t triatt_workspace_bytes(int64_t B, int64_t N, int c_in, int c_hidden, int heads) {
+  if (triatt_packed_bytes(c_in, c_hidden, heads) == 0 || B < 1 || N < 1) return 0;
+  return ta_ws(B, N, c_in, c_hidden, heads).total;
+}
+
+template <int D>
+static void launch_att_core(dim3 grid, cudaStream_t st, const float* Y, int64_t ldy, const float* tri,
+                            const float* mask, int64_t N, int H, int d, int hd, float qscale, float inf2, int tr,
+                            float* og) {
+  att_core_kernel<D><<<grid, 128, 0, st>>>(Y, ldy, tri, mask, N, H, d, hd, qscale, inf2, tr, og);
+}
+
+int triatt_forward(int starting, const float* z, const float* mask, const void* packed, float* out,
+                   int add_residual, const DropArgs& drop, void* workspace, size_t workspace_bytes, int64_t B,
+                   int64_t N, int c_in, int c_hidden, int heads, float inf, uint32_t* status, void* stream) {
+  (void)status;
+  if (int e = triatt_check(c_in, c_hidden, heads)) return e;
+  if (int e = common_args(z, out, packed, workspace, mask, B, N)) return e;
+  if (int e = drop_channels(drop, c_in)) return e;
+  if (!std::isfinite(inf)) return fail(GTK_ERR_INVALID_ARG, "triatt: inf must be finite");
+  const TaWs w = ta_ws(B, N, c_in, c_hidden, heads);
+  if (workspace_bytes < w.total) return fail(GTK_ERR_WORKSPACE, "triatt: workspace too small");
+  if (int e = check_device()) return e;
+  const TaPack L = ta_pack(c_in, c_hidden, heads);
+  const float* pk = static_cast<const float*>(packed);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  float* zn = reinterpret_cast<float*>(ws + w.zn);
+  float* Y = reinterpret_cast<float*>(ws + w.y);
+  float* tri = reinterpret_cast<float*>(ws + w.tri);
+  float* og = reinterpret_cast<float*>(ws + w.og);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t P = B * N * N;
+  const int hd = c_hidden, H = heads, d = c_hidden / heads;
+  const int tr = starting ? 0 : 1;
+  const int64_t ldy = 4 * static_cast<int64_t>(hd) + H;
+  if (int e = launch_ln(z, pk + L.lw, pk + L.lb, zn, P, c_in, N, tr, st)) return e;
+  if (int e = launch_gemm(zn, P, c_in, c_in, pk + L.w, static_cast<int>(ldy), c_in, epi(kStore, pk + L.b, Y, ldy),
+                          st))
+    return e;
+  {
+    const int64_t total = B * H * N * N;
+    tri_bias_kernel<<<grid_rows(total, 256), 256, 0, st>>>(Y, ldy, 4 * hd, H, B, N, tri);
+    if (int e = check_launch("general tri_bias_kernel")) return e;
+  }
+  {
+    const int64_t jb = (N + 127) / 128;
+    if (B * N > 2147483647 || jb > 65535) return fail(GTK_ERR_INVALID_ARG, "triatt: N too large");
+    dim3 grid(static_cast<unsigned>(B * N), static_cast<unsigned>(H), static_cast<unsigned>(jb));
+    const float qscale = kLog2e / std::sqrt(static_cast<float>(d)), inf2 = inf * kLog2e;
+    if (d <= 8)
+      launch_att_core<8>(grid, st, Y, ldy, tri, mask, N, H, d, hd, qscale, inf2, tr, og);
+    else if (d <= 16)
+      launch_att_core<16>(grid, st, Y, ldy, tri, mask, N, H, d, hd, qscale, inf2, tr, og);
+    else if (d <= 32)
+      launch_att_core<32>(grid, st, Y, ldy, tri, mask, N, H, d, hd, qscale, inf2, tr, og);
+    else
+      launch_att_core<64>(grid, st, Y, ldy, tri, mask, N, H, d, hd, qscale, inf2, tr, og);
+    if (int e = check_launch("general att_core_kernel")) return e;
+  }
+  Epi e = epi(kRes, pk + L.bo, out, c_in);
+  e.z = add_residual ? z : nullptr;
+  e.N = N;
+  e.tr = tr;
+  e.drop = drop;
+  return launch_gemm(og, P, hd, hd, pk + L.wo, c_in, hd, e, st);
+}
+
+// ----------------------------------- pair transition -----------------------------------
+// packed floats: W1 [nc x c] | b1 [nc] | W2 [c x nc] | b2 [c] | ln w, b [c]
+struct TnPack {
+  size_t w1, b1, w2, b2, lw, lb, floats;
+};
+static TnPack tn_pack(int c, int n) {
+  TnPack p{};
+  const size_t h = static_cast<size_t>(c) * n;
+  p.w1 = 0;
+  p.b1 = h * c;
+  p.w2 = p.b1 + h;
+  p.b2 = p.w2 + h * c;
+  p.lw = p.b2 + c;
+  p.lb = p.lw + c;
+  p.floats = p.lb + c;
+  return p;
+}
+
+int transition_check(int c_p, int n) {
+  if (c_p < 1 || c_p > kMaxChannels || n < 1 || static_cast<int64_t>(c_p) * n > 4 * kMaxChannels)
+    return fail(GTK_ERR_UNSUPPORTED, "transition: need 1 <= c_p <= " + std::to_string(kMaxChannels) +
+                                         " and c_p * n <= " + std::to_string(4 * kMaxChannels));
+  return GTK_OK;
+}
+
+size_t transition_packed_bytes(int c_p, int n) {
+  if (c_p < 1 || c_p > kMaxChannels || n < 1 || static_cast<int64_t>(c_p) * n > 4 * kMaxChannels) return 0;
+  return a256(tn_pack(c_p, n).floats * 4);
+}
+
+int transition_pack(const gtk_transition_params* params, int c_p, int n, void* packed, size_t packed_bytes,
+                    void* stream) {
+  if (int e = transition_check(c_p, n)) return e;
+  if (!params || !params->ln_w || !params->ln_b || !params->w1 || !params->w2)
+    return fail(GTK_ERR_INVALID_ARG, "transition_pack: a required parameter pointer is NULL");
+  if (int e = check_ptr(packed, "packed", 256)) return e;
+  if (packed_bytes < transition_packed_bytes(c_p, n)) return fail(GTK_ERR_WORKSPACE, "packed buffer too small");
+  if (int e = check_device()) return e;
+  const TnPack L = tn_pack(c_p, n);
+  float* f = static_cast<float*>(packed);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t c = c_p, h = static_cast<size_t>(c_p) * n;
+  if (int e = copy_d2d(f + L.w1, params->w1, h * c, st)) return e;
+  if (int e = copy_d2d(f + L.b1, params->b1, h, st)) return e;
+  if (int e = copy_d2d(f + L.w2, params->w2, c * h, st)) return e;
+  if (int e = copy_d2d(f + L.b2, params->b2, c, st)) return e;
+  if (int e = copy_d2d(f + L.lw, params->ln_w, c, st)) return e;
+  return copy_d2d(f + L.lb, params->ln_b, c, st);
+}
+
+size_t transition_workspace_bytes(int64_t B, int64_t N, int c_p, int n) {
+  if (transition_packed_bytes(c_p, n) == 0 || B < 1 || N < 1) return 0;
+  const size_t P = static_cast<size_t>(B) * N * N;
+  return a256(P * c_p * 4) + a256(P * static_cast<size_t>(c_p) * n * 4);
+}
+
+int transition_forward(const float* z, const float* mask, const void* packed, float* out, int add_residual,
+                       void* workspace, size_t workspace_bytes, int64_t B, int64_t N, int c_p, int n,
+                       uint32_t* status, void* stream) {
+  (void)status;
+  if (int e = transition_check(c_p, n)) return e;
+  if (int e = common_args(z, out, packed, workspace, mask, B, N)) return e;
+  if (workspace_bytes < transition_workspace_bytes(B, N, c_p, n))
+    return fail(GTK_ERR_WORKSPACE, "transition: workspace too small");
+  if (int e = check_device()) return e;
+  const TnPack L = tn_pack(c_p, n);
+  const float* pk = static_cast<const float*>(packed);
+  const size_t P = static_cast<size_t>(B) * N * N;
+  float* zn = static_cast<float*>(workspace);
+  float* hbuf = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + a256(P * c_p * 4));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int h = c_p * n;
+  if (int e = launch_ln(z, pk + L.lw, pk + L.lb, zn, static_cast<int64_t>(P), c_p, N, 0, st)) return e;
+  if (int e = launch_gemm(zn, static_cast<int64_t>(P), c_p, c_p, pk + L.w1, h, c_p, epi(kRelu, pk + L.b1, hbuf, h), st))
+    return e;
+  Epi e = epi(kResMask, pk + L.b2, out, c_p);
+  e.z = add_residual ? z : nullptr;
+  e.mask = mask;
+  e.N = N;
+  return launch_gemm(hbuf, static_cast<int64_t>(P), h, h, pk + L.w2, c_p, h, e, st);
+}
+
+}  // namespace gen
+}  // namespace gtk

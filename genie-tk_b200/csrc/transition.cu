@@ -23,6 +23,7 @@
 
 #include "gtk_host.h"
 #include "gtk_sm100.cuh"
+#include "general.h"
 
 namespace gtk {
 
@@ -590,17 +591,21 @@ using namespace gtk;
 
 extern "C" {
 
+static bool transition_tuned(int c_p, int n) { return c_p == tnpack::kCp && n == tnpack::kHid / tnpack::kCp; }
+
 size_t gtk_transition_packed_bytes(int c_p, int n) {
-  return (c_p == tnpack::kCp && n == tnpack::kHid / tnpack::kCp) ? tnpack::kBytes : 0;
+  return transition_tuned(c_p, n) ? tnpack::kBytes : gen::transition_packed_bytes(c_p, n);
 }
 
 size_t gtk_transition_workspace_bytes(int64_t B, int64_t N, int c_p, int n) {
-  if (c_p != tnpack::kCp || n != tnpack::kHid / tnpack::kCp || B < 1 || N < 1) return 0;
+  if (!transition_tuned(c_p, n)) return gen::transition_workspace_bytes(B, N, c_p, n);
+  if (B < 1 || N < 1) return 0;
   return static_cast<size_t>(B) * N * N * tnpack::kHid * 2;
 }
 
 int gtk_transition_pack(const gtk_transition_params* params, int c_p, int n, void* packed, size_t packed_bytes,
                         void* stream) {
+  if (!transition_tuned(c_p, n)) return gen::transition_pack(params, c_p, n, packed, packed_bytes, stream);
   if (int e = transition_check(c_p, n)) return e;
   if (!params || !params->ln_w || !params->ln_b || !params->w1 || !params->w2)
     return fail(GTK_ERR_INVALID_ARG, "transition_pack: a required parameter pointer is NULL");
@@ -614,6 +619,9 @@ int gtk_transition_pack(const gtk_transition_params* params, int c_p, int n, voi
 int gtk_transition_forward(const float* z, const float* mask, const void* packed, float* out, int add_residual,
                            void* workspace, size_t workspace_bytes, int64_t B, int64_t N, int c_p, int n,
                            uint32_t* status, void* stream) {
+  if (!transition_tuned(c_p, n))  // every other shape: the general path
+    return gen::transition_forward(z, mask, packed, out, add_residual, workspace, workspace_bytes, B, N, c_p, n, status,
+                                   stream);
   if (int e = transition_check(c_p, n)) return e;
   if (!dims_ok(B, 65535) || !dims_ok(N, 65535)) return fail(GTK_ERR_INVALID_ARG, "transition: bad B/N");
   if (int e = check_ptr(z, "z")) return e;

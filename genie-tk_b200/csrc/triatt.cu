@@ -29,6 +29,7 @@
 
 #include "gtk_host.h"
 #include "gtk_sm100.cuh"
+#include "general.h"
 
 namespace gtk {
 
@@ -1173,13 +1174,19 @@ using namespace gtk;
 
 extern "C" {
 
+static bool triatt_tuned(int c_in, int c_hidden, int heads) {
+  return c_in == 128 && c_hidden == 128 && heads == kHeads;
+}
+
 size_t gtk_triatt_packed_bytes(int c_in, int c_hidden, int heads) {
-  if (c_in != 128 || c_hidden != 128 || heads != kHeads) return 0;
+  if (!triatt_tuned(c_in, c_hidden, heads)) return gen::triatt_packed_bytes(c_in, c_hidden, heads);
   return tapack::kBytes;
 }
 
 int gtk_triatt_pack(const gtk_triatt_params* params, int c_in, int c_hidden, int heads, void* packed,
                     size_t packed_bytes, void* stream) {
+  if (!triatt_tuned(c_in, c_hidden, heads))
+    return gen::triatt_pack(params, c_in, c_hidden, heads, packed, packed_bytes, stream);
   if (int e = triatt_check(c_in, c_hidden, heads)) return e;
   if (!params) return fail(GTK_ERR_INVALID_ARG, "params is NULL");
   if (int e = check_ptr(packed, "packed", 256)) return e;
@@ -1195,7 +1202,8 @@ int gtk_triatt_pack(const gtk_triatt_params* params, int c_in, int c_hidden, int
 }
 
 size_t gtk_triatt_workspace_bytes(int64_t B, int64_t N, int c_in, int c_hidden, int heads) {
-  if (c_in != 128 || c_hidden != 128 || heads != kHeads || B < 1 || N < 1) return 0;
+  if (!triatt_tuned(c_in, c_hidden, heads)) return gen::triatt_workspace_bytes(B, N, c_in, c_hidden, heads);
+  if (B < 1 || N < 1) return 0;
   return triatt_layout(B, N, N).total;
 }
 
@@ -1329,6 +1337,9 @@ static int triatt_forward_impl(int starting, const float* z, const float* mask, 
                                int add_residual, const DropArgs& drop, void* workspace, size_t workspace_bytes,
                                int64_t B, int64_t N, int c_in, int c_hidden, int heads, float inf, uint32_t* status,
                                void* stream) {
+  if (!triatt_tuned(c_in, c_hidden, heads))  // every other shape: the general path
+    return gen::triatt_forward(starting, z, mask, packed, out, add_residual, drop, workspace, workspace_bytes, B, N,
+                               c_in, c_hidden, heads, inf, status, stream);
   if (int e = triatt_check(c_in, c_hidden, heads)) return e;
   if (!dims_ok(B, 65535) || !dims_ok(N, 65535)) return fail(GTK_ERR_INVALID_ARG, "triatt: bad B/N");
   if (workspace_bytes < triatt_layout(B, N, N).total) return fail(GTK_ERR_WORKSPACE, "triatt: workspace too small");

@@ -24,6 +24,7 @@
 
 #include "gtk_host.h"
 #include "gtk_sm100.cuh"
+#include "general.h"
 
 namespace gtk {
 
@@ -1052,14 +1053,13 @@ using namespace gtk;
 extern "C" {
 
 size_t gtk_trimul_packed_bytes(int c_z, int c_hidden) {
-  if (c_z != 128 || c_hidden != 128) return 0;
+  if (c_z != 128 || c_hidden != 128) return gen::trimul_packed_bytes(c_z, c_hidden);
   return tmpack::kBytes;
 }
 
 int gtk_trimul_pack(const gtk_trimul_params* params, int c_z, int c_hidden, void* packed, size_t packed_bytes,
                     void* stream) {
-  if (c_z != 128 || c_hidden != 128)
-    return fail(GTK_ERR_UNSUPPORTED, "trimul: only c_z = c_hidden = 128 is implemented");
+  if (c_z != 128 || c_hidden != 128) return gen::trimul_pack(params, c_z, c_hidden, packed, packed_bytes, stream);
   if (!params) return fail(GTK_ERR_INVALID_ARG, "params is NULL");
   if (int e = check_ptr(packed, "packed", 256)) return e;
   if (packed_bytes < tmpack::kBytes) return fail(GTK_ERR_WORKSPACE, "packed buffer too small");
@@ -1074,7 +1074,8 @@ int gtk_trimul_pack(const gtk_trimul_params* params, int c_z, int c_hidden, void
 int64_t gtk_plane_pitch(int64_t N) { return static_cast<int64_t>(round_up(static_cast<uint64_t>(N), 8)); }
 
 size_t gtk_trimul_workspace_bytes(int64_t B, int64_t N, int c_z, int c_hidden) {
-  if (c_z != 128 || c_hidden != 128 || B < 1 || N < 1) return 0;
+  if (c_z != 128 || c_hidden != 128) return gen::trimul_workspace_bytes(B, N, c_z, c_hidden);
+  if (B < 1 || N < 1) return 0;
   const size_t plane = round_up(static_cast<size_t>(B) * N * 128 * gtk_plane_pitch(N) * 2, 256);
   return 3 * plane;
 }
@@ -1225,8 +1226,9 @@ static int trimul_finish_launch(const float* z, const void* x_planes, int64_t ld
 static int trimul_forward_impl(int outgoing, const float* z, const float* mask, const void* packed, float* out,
                                int add_residual, const DropArgs& drop, void* workspace, size_t workspace_bytes,
                                int64_t B, int64_t N, int c_z, int c_hidden, uint32_t* status, void* stream) {
-  if (c_z != 128 || c_hidden != 128)
-    return fail(GTK_ERR_UNSUPPORTED, "trimul: only c_z = c_hidden = 128 is implemented");
+  if (c_z != 128 || c_hidden != 128)  // every other shape: the general path
+    return gen::trimul_forward(outgoing, z, mask, packed, out, add_residual, drop, workspace, workspace_bytes, B, N,
+                               c_z, c_hidden, status, stream);
   if (!dims_ok(B, 65535) || !dims_ok(N, 65535)) return fail(GTK_ERR_INVALID_ARG, "trimul: bad B/N");
   const size_t need = gtk_trimul_workspace_bytes(B, N, c_z, c_hidden);
   if (workspace_bytes < need) return fail(GTK_ERR_WORKSPACE, "trimul: workspace too small");

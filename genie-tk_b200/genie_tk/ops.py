@@ -73,6 +73,12 @@ def _require_cuda(t: torch.Tensor, name: str, dtype=None) -> None:
         raise TypeError(f"genie_tk (B200): {name} must be {dtype}, got {t.dtype}")
 
 
+def packed_dims(packed: torch.Tensor, default: tuple) -> tuple:
+    """The shape a packed weight buffer was built for (recorded by the ``pack_*`` functions);
+    ``default`` for a buffer packed elsewhere."""
+    return tuple(getattr(packed, "_gtk_dims", default))
+
+
 def prepare_pair(z: torch.Tensor, mask: Optional[torch.Tensor], c_expected: int):
     """Validate a pair tensor [B, N, N, C] and its mask; return contiguous fp32 views."""
     _require_cuda(z, "z")
@@ -120,12 +126,18 @@ def dropout_mask_from_multipliers(mult: torch.Tensor, shared_across_rows: bool, 
     shape [B, 1, N, C] for rows, [B, N, 1, C] for columns; 0 = dropped) into keep bits."""
     lib = _lib.load()
     _require_cuda(mult, "multipliers")
-    if mult.dim() != 4 or mult.shape[-1] != SUPPORTED_C or mult.shape[1 if shared_across_rows else 2] != 1:
-        want = "[B, 1, N, 128]" if shared_across_rows else "[B, N, 1, 128]"
+    if mult.dim() != 4 or mult.shape[1 if shared_across_rows else 2] != 1:
+        want = "[B, 1, N, C]" if shared_across_rows else "[B, N, 1, C]"
         raise ValueError(f"dropout multipliers must be {want}, got {tuple(mult.shape)}")
+    C = mult.shape[-1]
+    if C > SUPPORTED_C:
+        raise NotImplementedError(f"genie_tk (B200): dropout keep vectors hold {SUPPORTED_C} channels, got {C}")
     B = mult.shape[0]
     N = mult.shape[2] if shared_across_rows else mult.shape[1]
-    m = mult.reshape(B * N, SUPPORTED_C).float().contiguous()
+    m = mult.reshape(B * N, C).float()
+    if C < SUPPORTED_C:  # channels past C do not exist; their bits are never read
+        m = torch.nn.functional.pad(m, (0, SUPPORTED_C - C), value=1.0)
+    m = m.contiguous()
     bits = torch.empty(B, N, 4, dtype=torch.int32, device=mult.device)
     _lib.check(lib.gtk_dropout_pack_keep_bits(_ptr(m), B * N, _ptr(bits), _stream(mult.device)),
                "gtk_dropout_pack_keep_bits")
@@ -159,44 +171,49 @@ TRIMUL_KEYS = ("layer_norm_in.weight", "layer_norm_in.bias", "linear_a_p.weight"
 def pack_trimul(params: Dict[str, torch.Tensor], device: torch.device) -> torch.Tensor:
     """Pack fp32 module parameters (reference state_dict keys) into the kernels' buffer."""
     lib = _lib.load()
-    nbytes = lib.gtk_trimul_packed_bytes(SUPPORTED_C, SUPPORTED_C)
+    c_hidden, c_z = (int(x) for x in params["linear_a_p.weight"].shape)
+    nbytes = lib.gtk_trimul_packed_bytes(c_z, c_hidden)
+    if nbytes == 0:
+        raise NotImplementedError(f"genie_tk (B200): triangle multiplication with c_z = {c_z}, c_hidden = {c_hidden} "
+                                  "is beyond the library's limits (1..512 channels)")
     tensors = []
     for k in TRIMUL_KEYS:
         t = params[k].detach()
         _require_cuda(t, k)
         tensors.append(t.float().contiguous())
-    if tuple(tensors[2].shape) != (SUPPORTED_C, SUPPORTED_C) or tuple(tensors[12].shape) != (SUPPORTED_C, SUPPORTED_C):
-        raise NotImplementedError("genie_tk (B200): triangle multiplication needs c_z = c_hidden = 128")
     packed = torch.empty(nbytes, dtype=torch.uint8, device=device)
     st = _lib.TrimulParams(*[ctypes.c_void_p(t.data_ptr()) for t in tensors])
-    _lib.check(lib.gtk_trimul_pack(ctypes.byref(st), SUPPORTED_C, SUPPORTED_C, _ptr(packed), nbytes, _stream(device)),
+    _lib.check(lib.gtk_trimul_pack(ctypes.byref(st), c_z, c_hidden, _ptr(packed), nbytes, _stream(device)),
                "gtk_trimul_pack")
     packed._gtk_keepalive = tensors  # fp32 copies must live until the pack kernel ran
+    packed._gtk_dims = (c_z, c_hidden)
     return packed
 
 
 def trimul_forward(z: torch.Tensor, mask: Optional[torch.Tensor], packed: torch.Tensor, outgoing: bool,
                    out: Optional[torch.Tensor] = None, add_residual: bool = False,
                    dropout: Optional[DropoutMask] = None) -> torch.Tensor:
-    """update (or z + update) of the triangle multiplicative block; fp32 [B, N, N, 128].
-    ``dropout`` multiplies the update by a channel dropout mask inside the epilogue."""
+    """update (or z + update) of the triangle multiplicative block; fp32 [B, N, N, c_z].
+    ``dropout`` multiplies the update by a channel dropout mask inside the epilogue. The
+    channel counts are those ``packed`` was built for (``pack_trimul``)."""
     lib = _lib.load()
-    zf, mf = prepare_pair(z, mask, SUPPORTED_C)
+    c_z, c_hidden = packed_dims(packed, (SUPPORTED_C, SUPPORTED_C))
+    zf, mf = prepare_pair(z, mask, c_z)
     B, N = zf.shape[0], zf.shape[1]
     if out is None:
         out = torch.empty_like(zf)
     _require_cuda(out, "out", torch.float32)
-    nbytes = lib.gtk_trimul_workspace_bytes(B, N, SUPPORTED_C, SUPPORTED_C)
+    nbytes = lib.gtk_trimul_workspace_bytes(B, N, c_z, c_hidden)
     ws = workspace(zf.device, nbytes)
     if dropout is None:
         rc = lib.gtk_trimul_forward(int(outgoing), _ptr(zf), _ptr(mf), _ptr(packed), _ptr(out), int(add_residual),
-                                    _ptr(ws), ws.numel(), B, N, SUPPORTED_C, SUPPORTED_C,
+                                    _ptr(ws), ws.numel(), B, N, c_z, c_hidden,
                                     _ptr(status_buffer(zf.device)), _stream(zf.device))
         _lib.check(rc, "gtk_trimul_forward")
         return out
     d = dropout._struct(B, N)
     rc = lib.gtk_trimul_forward_dropout(int(outgoing), _ptr(zf), _ptr(mf), _ptr(packed), _ptr(out), int(add_residual),
-                                        ctypes.byref(d), _ptr(ws), ws.numel(), B, N, SUPPORTED_C, SUPPORTED_C,
+                                        ctypes.byref(d), _ptr(ws), ws.numel(), B, N, c_z, c_hidden,
                                         _ptr(status_buffer(zf.device)), _stream(zf.device))
     _lib.check(rc, "gtk_trimul_forward_dropout")
     return out
@@ -290,11 +307,13 @@ TRIATT_KEYS = ("layer_norm.weight", "layer_norm.bias", "linear.weight", "mha.lin
 
 def pack_triatt(params: Dict[str, torch.Tensor], device: torch.device, heads: int) -> torch.Tensor:
     lib = _lib.load()
-    c_in = params["layer_norm.weight"].shape[0]
-    c_hidden = params["mha.linear_q.weight"].shape[0]
-    if c_in != SUPPORTED_C or c_hidden != SUPPORTED_C or heads != SUPPORTED_HEADS:
-        raise NotImplementedError("genie_tk (B200): triangle attention needs c_in = c_hidden = 128 and 4 heads")
+    c_in = int(params["layer_norm.weight"].shape[0])
+    c_hidden = int(params["mha.linear_q.weight"].shape[0])
     nbytes = lib.gtk_triatt_packed_bytes(c_in, c_hidden, heads)
+    if nbytes == 0:
+        raise NotImplementedError(f"genie_tk (B200): triangle attention with c_in = {c_in}, c_hidden = {c_hidden}, "
+                                  f"{heads} heads is beyond the library's limits (c_hidden a multiple of the heads, "
+                                  "head_dim <= 64, <= 32 heads, <= 512 channels)")
     tensors = []
     for k in TRIATT_KEYS:
         t = params[k].detach()
@@ -305,6 +324,7 @@ def pack_triatt(params: Dict[str, torch.Tensor], device: torch.device, heads: in
     _lib.check(lib.gtk_triatt_pack(ctypes.byref(st), c_in, c_hidden, heads, _ptr(packed), nbytes, _stream(device)),
                "gtk_triatt_pack")
     packed._gtk_keepalive = tensors
+    packed._gtk_dims = (c_in, c_hidden, heads)
     return packed
 
 
@@ -312,25 +332,27 @@ def triatt_forward(z: torch.Tensor, mask: Optional[torch.Tensor], packed: torch.
                    inf: float = 1e9, out: Optional[torch.Tensor] = None, add_residual: bool = False,
                    dropout: Optional[DropoutMask] = None) -> torch.Tensor:
     """update (or z + update) of triangle attention around the starting / ending node.
-    ``dropout`` multiplies the update by a channel dropout mask inside the epilogue."""
+    ``dropout`` multiplies the update by a channel dropout mask inside the epilogue. The
+    shape (c_in, c_hidden, heads) is the one ``packed`` was built for (``pack_triatt``)."""
     lib = _lib.load()
-    zf, mf = prepare_pair(z, mask, SUPPORTED_C)
+    c_in, c_hidden, heads = packed_dims(packed, (SUPPORTED_C, SUPPORTED_C, SUPPORTED_HEADS))
+    zf, mf = prepare_pair(z, mask, c_in)
     B, N = zf.shape[0], zf.shape[1]
     if out is None:
         out = torch.empty_like(zf)
     _require_cuda(out, "out", torch.float32)
-    nbytes = lib.gtk_triatt_workspace_bytes(B, N, SUPPORTED_C, SUPPORTED_C, SUPPORTED_HEADS)
+    nbytes = lib.gtk_triatt_workspace_bytes(B, N, c_in, c_hidden, heads)
     ws = workspace(zf.device, nbytes)
     if dropout is None:
         rc = lib.gtk_triatt_forward(int(starting), _ptr(zf), _ptr(mf), _ptr(packed), _ptr(out), int(add_residual),
-                                    _ptr(ws), ws.numel(), B, N, SUPPORTED_C, SUPPORTED_C, SUPPORTED_HEADS, float(inf),
+                                    _ptr(ws), ws.numel(), B, N, c_in, c_hidden, heads, float(inf),
                                     _ptr(status_buffer(zf.device)), _stream(zf.device))
         _lib.check(rc, "gtk_triatt_forward")
         return out
     d = dropout._struct(B, N)
     rc = lib.gtk_triatt_forward_dropout(int(starting), _ptr(zf), _ptr(mf), _ptr(packed), _ptr(out), int(add_residual),
-                                        ctypes.byref(d), _ptr(ws), ws.numel(), B, N, SUPPORTED_C, SUPPORTED_C,
-                                        SUPPORTED_HEADS, float(inf), _ptr(status_buffer(zf.device)),
+                                        ctypes.byref(d), _ptr(ws), ws.numel(), B, N, c_in, c_hidden,
+                                        heads, float(inf), _ptr(status_buffer(zf.device)),
                                         _stream(zf.device))
     _lib.check(rc, "gtk_triatt_forward_dropout")
     return out
@@ -409,11 +431,12 @@ TRANSITION_KEYS = ("layer_norm.weight", "layer_norm.bias", "linear_1.weight", "l
 def pack_transition(params: Dict[str, torch.Tensor], device: torch.device) -> torch.Tensor:
     """Pack a PairTransition's fp32 parameters (reference state_dict keys)."""
     lib = _lib.load()
-    c_p = params["layer_norm.weight"].shape[0]
-    hid = params["linear_1.weight"].shape[0]
-    if c_p != SUPPORTED_C or hid != 4 * SUPPORTED_C:
-        raise NotImplementedError("genie_tk (B200): the pair transition kernels need c_p = 128 and n = 4")
-    nbytes = lib.gtk_transition_packed_bytes(c_p, hid // c_p)
+    c_p = int(params["layer_norm.weight"].shape[0])
+    hid = int(params["linear_1.weight"].shape[0])
+    nbytes = lib.gtk_transition_packed_bytes(c_p, hid // c_p) if hid % c_p == 0 else 0
+    if nbytes == 0:
+        raise NotImplementedError(f"genie_tk (B200): pair transition with c_p = {c_p}, hidden {hid} is beyond the "
+                                  "library's limits (hidden a multiple of c_p, c_p <= 512, hidden <= 2048)")
     tensors = []
     for k in TRANSITION_KEYS:
         t = params[k].detach()
@@ -424,23 +447,26 @@ def pack_transition(params: Dict[str, torch.Tensor], device: torch.device) -> to
     _lib.check(lib.gtk_transition_pack(ctypes.byref(st), c_p, hid // c_p, _ptr(packed), nbytes, _stream(device)),
                "gtk_transition_pack")
     packed._gtk_keepalive = tensors
+    packed._gtk_dims = (c_p, hid // c_p)
     return packed
 
 
 def transition_forward(z: torch.Tensor, mask: Optional[torch.Tensor], packed: torch.Tensor,
                        out: Optional[torch.Tensor] = None, add_residual: bool = False) -> torch.Tensor:
     """transition(z), or z + transition(z) (add_residual), times mask[b, i, j] when a mask
-    is given; fp32 [B, N, N, 128]. ``out=z`` updates in place."""
+    is given; fp32 [B, N, N, c_p]. ``out=z`` updates in place. (c_p, n) are the ones
+    ``packed`` was built for (``pack_transition``)."""
     lib = _lib.load()
-    zf, mf = prepare_pair(z, mask, SUPPORTED_C)
+    c_p, n = packed_dims(packed, (SUPPORTED_C, 4))
+    zf, mf = prepare_pair(z, mask, c_p)
     B, N = zf.shape[0], zf.shape[1]
     if out is None:
         out = torch.empty_like(zf)
     _require_cuda(out, "out", torch.float32)
-    nbytes = lib.gtk_transition_workspace_bytes(B, N, SUPPORTED_C, 4)
+    nbytes = lib.gtk_transition_workspace_bytes(B, N, c_p, n)
     ws = workspace(zf.device, nbytes, tag="transition")
     rc = lib.gtk_transition_forward(_ptr(zf), _ptr(mf), _ptr(packed), _ptr(out), int(add_residual), _ptr(ws),
-                                    ws.numel(), B, N, SUPPORTED_C, 4, _ptr(status_buffer(zf.device)),
+                                    ws.numel(), B, N, c_p, n, _ptr(status_buffer(zf.device)),
                                     _stream(zf.device))
     _lib.check(rc, "gtk_transition_forward")
     return out

@@ -70,7 +70,8 @@ class DropoutColumnwise(_SharedDropout):
 
 class PairTransition(nn.Module):
     """Pair feed-forward (reference pair_transform.py:64-84): LN -> Linear(c_p, n c_p) ->
-    ReLU -> Linear(n c_p, c_p). Runs on the transition kernels (c_p = 128, n = 4)."""
+    ReLU -> Linear(n c_p, c_p). c_p = 128 with n = 4 runs on the tuned transition kernels,
+    other shapes on the general-shape path."""
 
     def __init__(self, c_p: int, n: int = 4):
         super().__init__()
@@ -89,8 +90,6 @@ class PairTransition(nn.Module):
     def _check(self, p: Tensor) -> None:
         if not p.is_cuda:
             raise RuntimeError("genie_tk (B200): PairTransition runs on CUDA tensors only")
-        if self.c_p != ops.SUPPORTED_C or self.n != 4:
-            raise NotImplementedError("genie_tk (B200): the pair transition kernels need c_p = 128 and n = 4")
 
     def forward(self, p: Tensor, mask: Optional[Tensor] = None) -> Tensor:
         """The update (the reference ignores ``mask`` here, and so does this)."""

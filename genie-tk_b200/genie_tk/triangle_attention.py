@@ -25,7 +25,9 @@ from .triangle_mul import _PackCache
 
 
 class TriangleAttention(nn.Module):
-    """Triangle attention (reference triangle_attention.py:34-199)."""
+    """Triangle attention (reference triangle_attention.py:34-199). c_in = c_hidden = 128 with
+    4 heads runs on the tuned kernels; every other shape (c_hidden a multiple of the heads,
+    head_dim <= 64, up to 32 heads and 512 channels) on the general-shape path."""
 
     def __init__(self, c_in: int, c_hidden: int, no_heads: int, starting: bool = True, inf: float = 1e9,
                  use_fused_kernel: bool = True):
@@ -55,9 +57,6 @@ class TriangleAttention(nn.Module):
         """
         if not x.is_cuda:
             raise RuntimeError("genie_tk (B200): TriangleAttention runs on CUDA tensors only")
-        if self.c_in != ops.SUPPORTED_C or self.c_hidden != ops.SUPPORTED_C or self.no_heads != ops.SUPPORTED_HEADS:
-            raise NotImplementedError(
-                "genie_tk (B200): triangle attention needs c_in = c_hidden = 128 with 4 heads of 32")
         packed = self.packed_weights(x.device)
         if autograd.needs_grad(x, self):
             # training: forward on the kernels, backward through a row-chunked recomputation

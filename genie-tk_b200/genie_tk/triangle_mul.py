@@ -40,8 +40,9 @@ class TriangleMultiplicativeUpdate(nn.Module):
     """Triangle multiplicative update (reference triangle_mul.py:33-185).
 
     Args:
-        c_z: pair channels (128 on the B200 kernels)
-        c_hidden: hidden channels of the projections (128)
+        c_z: pair channels
+        c_hidden: hidden channels of the projections. c_z = c_hidden = 128 runs on the tuned
+            kernels; every other shape up to 512 channels on the general-shape path
         _outgoing: Algorithm 11 (True) or 12 (False)
         use_fused_kernel: kept for signature compatibility; the fused kernels are the
             only implementation in this package
@@ -78,8 +79,6 @@ class TriangleMultiplicativeUpdate(nn.Module):
         """
         if not z.is_cuda:
             raise RuntimeError("genie_tk (B200): TriangleMultiplicativeUpdate runs on CUDA tensors only")
-        if self.c_z != ops.SUPPORTED_C or self.c_hidden != ops.SUPPORTED_C:
-            raise NotImplementedError("genie_tk (B200): triangle multiplication needs c_z = c_hidden = 128")
         packed = self.packed_weights(z.device)
         if autograd.needs_grad(z, self):
             # training: the forward still runs on the kernels; the backward differentiates a

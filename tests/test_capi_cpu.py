@@ -49,9 +49,18 @@ def test_every_declared_symbol_has_a_ctypes_signature():
 def test_host_queries(lib):
     assert lib.gtk_version() >= 100
     assert lib.gtk_trimul_packed_bytes(128, 128) > 0
-    assert lib.gtk_trimul_packed_bytes(64, 128) == 0
     assert lib.gtk_triatt_packed_bytes(128, 128, 4) > 0
-    assert lib.gtk_triatt_packed_bytes(128, 32, 4) == 0
+    # the general-shape path: any channel count up to 512, head_dim up to 64
+    for cz, c in ((64, 128), (64, 32), (32, 16), (128, 64), (96, 48)):
+        assert lib.gtk_trimul_packed_bytes(cz, c) > 0
+        assert lib.gtk_trimul_workspace_bytes(1, 10, cz, c) > 0
+    for cin, c, h in ((128, 32, 4), (64, 32, 4), (32, 16, 2), (128, 16, 4), (128, 128, 8), (48, 36, 3)):
+        assert lib.gtk_triatt_packed_bytes(cin, c, h) > 0
+        assert lib.gtk_triatt_workspace_bytes(1, 10, cin, c, h) > 0
+    assert lib.gtk_trimul_packed_bytes(1024, 128) == 0
+    assert lib.gtk_triatt_packed_bytes(128, 128, 3) == 0    # c_hidden not a multiple of heads
+    assert lib.gtk_triatt_packed_bytes(128, 256, 2) == 0    # head_dim 128 > 64
+    assert lib.gtk_transition_packed_bytes(64, 4) > 0 and lib.gtk_transition_packed_bytes(128, 2) > 0
     assert [lib.gtk_plane_pitch(n) for n in (1, 8, 10, 1024)] == [8, 8, 16, 1024]
     w1 = lib.gtk_trimul_workspace_bytes(1, 100, 128, 128)
     w2 = lib.gtk_trimul_workspace_bytes(1, 200, 128, 128)
@@ -87,12 +96,30 @@ def test_row_shards_are_starting_orientation_only(lib):
 
 
 def test_unsupported_shapes_fail_before_touching_the_device(lib):
-    rc = lib.gtk_trimul_forward(1, None, None, None, None, 0, None, 0, 1, 16, 64, 128, None, None)
-    assert rc == -2
+    rc = lib.gtk_trimul_forward(1, None, None, None, None, 0, None, 0, 1, 16, 1024, 128, None, None)
+    assert rc == L.GTK_ERR_UNSUPPORTED
     assert b"c_z" in lib.gtk_last_error_string()
-    rc = lib.gtk_triatt_forward(1, None, None, None, None, 0, None, 0, 1, 16, 128, 128, 8, 1e9, None, None)
-    assert rc == -2
+    rc = lib.gtk_triatt_forward(1, None, None, None, None, 0, None, 0, 1, 16, 128, 128, 3, 1e9, None, None)
+    assert rc == L.GTK_ERR_UNSUPPORTED
     assert b"heads" in lib.gtk_last_error_string()
+    rc = lib.gtk_triatt_forward(1, None, None, None, None, 0, None, 0, 1, 16, 128, 256, 2, 1e9, None, None)
+    assert rc == L.GTK_ERR_UNSUPPORTED and b"head_dim" in lib.gtk_last_error_string()
+    # the no-alloc entry point keeps to the tuned shape
+    rc = lib.gtk_trimul_forward_noalloc(1, None, None, None, None, 0, 1, 16, 64, 64, None, None)
+    assert rc == L.GTK_ERR_UNSUPPORTED
+
+
+def test_general_path_validates_before_touching_the_device(lib):
+    # a NULL pair tensor, then a short workspace, at a general shape
+    rc = lib.gtk_trimul_forward(1, None, None, None, None, 0, None, 0, 1, 16, 64, 32, None, None)
+    assert rc == L.GTK_ERR_INVALID_ARG
+    p = ctypes.c_void_p(1 << 20)
+    rc = lib.gtk_trimul_forward(1, p, None, p, p, 0, p, 256, 1, 16, 64, 32, None, None)
+    assert rc == L.GTK_ERR_WORKSPACE and b"workspace" in lib.gtk_last_error_string()
+    rc = lib.gtk_triatt_forward(0, p, None, p, p, 0, p, 256, 1, 16, 128, 32, 4, 1e9, None, None)
+    assert rc == L.GTK_ERR_WORKSPACE
+    rc = lib.gtk_transition_forward(p, None, p, p, 1, p, 256, 1, 16, 64, 4, None, None)
+    assert rc == L.GTK_ERR_WORKSPACE
 
 
 def test_invalid_arguments_are_rejected(lib):
@@ -114,11 +141,10 @@ def test_invalid_arguments_are_rejected(lib):
 
 def test_transition_entry_points(lib):
     assert lib.gtk_transition_packed_bytes(128, 4) > 2 * 128 * 512 * 2
-    assert lib.gtk_transition_packed_bytes(64, 4) == 0
     assert lib.gtk_transition_workspace_bytes(2, 10, 128, 4) == 2 * 10 * 10 * 512 * 2
-    assert lib.gtk_transition_workspace_bytes(1, 10, 128, 2) == 0
+    assert lib.gtk_transition_workspace_bytes(1, 10, 128, 2) > 0    # general path
     # unsupported width, then a NULL pair tensor, then a short workspace: all before any launch
-    assert lib.gtk_transition_forward(None, None, None, None, 0, None, 0, 1, 16, 96, 4, None, None) == -2
+    assert lib.gtk_transition_forward(None, None, None, None, 0, None, 0, 1, 16, 1024, 4, None, None) == -2
     assert lib.gtk_transition_forward(None, None, None, None, 0, None, 0, 1, 16, 128, 4, None, None) == -1
     p = ctypes.c_void_p(1 << 20)
     rc = lib.gtk_transition_forward(p, None, p, p, 1, p, 100, 1, 16, 128, 4, None, None)

@@ -3,11 +3,12 @@
 import pytest
 import torch
 
-from golden_util import SINGLE_CASES, load_case, load_stack, load_transition, oracle_run
+from golden_util import (GENERAL_CASES, LAYER_CASES, SINGLE_CASES, load_case, load_layer, load_stack,
+                         load_transition, oracle_layer, oracle_run)
 from oracle import triangle_oracle as O
 
 
-@pytest.mark.parametrize("name", SINGLE_CASES)
+@pytest.mark.parametrize("name", SINGLE_CASES + GENERAL_CASES)
 def test_oracle_matches_reference_golden(name):
     op, dims, z, mask, params, out = load_case(name)
     got = oracle_run(op, dims, z, mask, params)
@@ -34,6 +35,20 @@ def test_oracle_transition_matches_reference_golden():
     tail = O.layer_tail(z, mask, params)
     torch.testing.assert_close(tail, (z + out) * mask.unsqueeze(-1), rtol=1e-5, atol=1e-6)
     assert float(tail[mask == 0].abs().max()) == 0.0
+
+
+def test_oracle_transition_c64_matches_reference_golden():
+    z, mask, params, out = load_transition("gen_transition_c64")
+    torch.testing.assert_close(O.transition_forward(z, params), out, rtol=1e-4, atol=2e-5)
+
+
+@pytest.mark.parametrize("name", LAYER_CASES)
+def test_oracle_pair_transform_layer_matches_reference_golden(name):
+    """A whole PairTransformLayer of the reference (eval mode) at its default shapes and at the
+    shapes of its own layer test: the four triangle blocks, the transition and the mask."""
+    dims, z, mask, blocks, out = load_layer(name)
+    got = oracle_layer(z, mask, blocks, dims["heads"])
+    torch.testing.assert_close(got, out, rtol=1e-4, atol=5e-5)
 
 
 def test_known_answers():
