@@ -28,15 +28,36 @@
 
 namespace gtk {
 
-__global__ void __launch_bounds__(256) copy_3d_kernel(uint8_t* __restrict__ dst, int64_t dpitch, int64_t dslab,
-                                                      const uint8_t* __restrict__ src, int64_t spitch, int64_t sslab,
-                                                      int64_t w16, int64_t height, int64_t total) {
-  for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
-       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t row = e / w16, c = e - row * w16;
-    const int64_t k = row / height, r = row - k * height;
-    const uint4 v = __ldg(reinterpret_cast<const uint4*>(src + k * sslab + r * spitch) + c);
-    reinterpret_cast<uint4*>(dst + k * dslab + r * dpitch)[c] = v;
+// Rows of 16-byte vectors: grid.y walks the rows (slab k = row / height, row r within it;
+// one 32-bit division per row, none per element), grid.x the columns, and every thread keeps
+// kVec independent 16-byte loads in flight before its stores.
+constexpr int kVec = 4;
+constexpr int kRowThreads = 256;
+
+__device__ __forceinline__ void copy_row16(uint4* __restrict__ d, const uint4* __restrict__ s, int64_t w16) {
+  for (int64_t c0 = static_cast<int64_t>(blockIdx.x) * (kRowThreads * kVec) + threadIdx.x; c0 < w16;
+       c0 += static_cast<int64_t>(gridDim.x) * (kRowThreads * kVec)) {
+    uint4 v[kVec];
+#pragma unroll
+    for (int u = 0; u < kVec; ++u) {
+      const int64_t c = c0 + u * kRowThreads;
+      if (c < w16) v[u] = __ldg(s + c);
+    }
+#pragma unroll
+    for (int u = 0; u < kVec; ++u) {
+      const int64_t c = c0 + u * kRowThreads;
+      if (c < w16) d[c] = v[u];
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kRowThreads) copy_3d_kernel(uint8_t* __restrict__ dst, int64_t dpitch, int64_t dslab,
+                                                              const uint8_t* __restrict__ src, int64_t spitch,
+                                                              int64_t sslab, int64_t w16, int height, int rows) {
+  for (int row = blockIdx.y; row < rows; row += gridDim.y) {
+    const int k = row / height, r = row - k * height;
+    copy_row16(reinterpret_cast<uint4*>(dst + k * dslab + r * dpitch),
+               reinterpret_cast<const uint4*>(src + k * sslab + r * spitch), w16);
   }
 }
 
@@ -66,40 +87,44 @@ __global__ void __launch_bounds__(256) pair_transpose_pack_kernel(const float4* 
 // Push form of copy_3d: slab k goes to its own destination base dsts[k] (a peer GPU's
 // buffer mapped into this process, or a local buffer), so packing, transfer over NVLink and
 // placement are one pass. dsts lives in device memory (P pointers).
-__global__ void __launch_bounds__(256) push_3d_kernel(const uint64_t* __restrict__ dsts, int64_t doff, int64_t dpitch,
-                                                      const uint8_t* __restrict__ src, int64_t spitch, int64_t sslab,
-                                                      int64_t w16, int64_t height, int64_t total) {
-  for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
-       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t row = e / w16, c = e - row * w16;
-    const int64_t k = row / height, r = row - k * height;
-    const uint4 v = __ldg(reinterpret_cast<const uint4*>(src + k * sslab + r * spitch) + c);
-    uint8_t* dst = reinterpret_cast<uint8_t*>(__ldg(dsts + k)) + doff + r * dpitch;
-    reinterpret_cast<uint4*>(dst)[c] = v;
+__global__ void __launch_bounds__(kRowThreads) push_3d_kernel(const uint64_t* __restrict__ dsts, int64_t doff,
+                                                              int64_t dpitch, const uint8_t* __restrict__ src,
+                                                              int64_t spitch, int64_t sslab, int64_t w16, int height,
+                                                              int rows) {
+  for (int row = blockIdx.y; row < rows; row += gridDim.y) {
+    const int k = row / height, r = row - k * height;
+    uint8_t* d = reinterpret_cast<uint8_t*>(__ldg(dsts + k)) + doff + r * dpitch;
+    copy_row16(reinterpret_cast<uint4*>(d), reinterpret_cast<const uint4*>(src + k * sslab + r * spitch), w16);
   }
 }
 
 // Push form of the pair-grid transpose: pair (b, y, q*(C/P) + x) of src [B][R][C][128] fp32
 // goes to dsts[q] at pair ((b*(C/P) + x)*ndst + row0 + y), i.e. straight into row x,
-// column row0 + y of peer q's transposed shard [B][C/P][ndst][128]. One warp per 512-B
-// pair vector; warps walk the source in order (coalesced reads).
+// column row0 + y of peer q's transposed shard [B][C/P][ndst][128]. grid.y = source row
+// (b, y); one warp per 512-B pair vector of that row, two vectors in flight per warp, and
+// 32-bit index arithmetic per vector.
 __global__ void __launch_bounds__(256) push_pair_transpose_kernel(const float4* __restrict__ src,
-                                                                  const uint64_t* __restrict__ dsts, int64_t B,
-                                                                  int64_t R, int64_t C, int64_t P, int64_t ndst,
-                                                                  int64_t row0) {
-  const int lane = threadIdx.x & 31;
-  const int64_t CP = C / P;
-  const int64_t n_pairs = B * R * C;
-  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-  for (int64_t w = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); w < n_pairs;
-       w += warps) {
-    // source pair index w = (b * R + y) * C + col
-    const int64_t col = w % C;
-    const int64_t t = w / C;
-    const int64_t y = t % R, b = t / R;
-    const int64_t q = col / CP, x = col - q * CP;
-    float4* dst = reinterpret_cast<float4*>(__ldg(dsts + q)) + (((b * CP + x) * ndst + row0 + y) * 32 + lane);
-    *dst = __ldg(src + w * 32 + lane);
+                                                                  const uint64_t* __restrict__ dsts, int R, int C,
+                                                                  int CP, int64_t ndst, int row0, int n_rows) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int row = blockIdx.y; row < n_rows; row += gridDim.y) {  // row = b * R + y
+    const int b = row / R, y = row - b * R;
+    const float4* s = src + static_cast<int64_t>(row) * C * 32;
+    for (int c0 = (blockIdx.x * 8 + warp) * 2; c0 < C; c0 += gridDim.x * 16) {
+      float4 v[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u)
+        if (c0 + u < C) v[u] = __ldg(s + static_cast<int64_t>(c0 + u) * 32 + lane);
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int col = c0 + u;
+        if (col >= C) break;
+        const int q = col / CP, x = col - q * CP;
+        float4* d = reinterpret_cast<float4*>(__ldg(dsts + q)) +
+                    ((static_cast<int64_t>(b) * CP + x) * ndst + row0 + y) * 32 + lane;
+        *d = v[u];
+      }
+    }
   }
 }
 
@@ -129,6 +154,17 @@ __global__ void peer_barrier_kernel(const uint64_t* __restrict__ flags, int rank
   }
 }
 
+// Grid of a row copy: enough x-blocks to cover a row (256 threads x kVec vectors each), and
+// rows on y (grid-stride beyond 65535).
+static dim3 row_grid(int64_t w16, int64_t rows) {
+  const int64_t per_block = static_cast<int64_t>(kRowThreads) * kVec;
+  int64_t xb = (w16 + per_block - 1) / per_block;
+  if (xb < 1) xb = 1;
+  if (xb > 1024) xb = 1024;
+  const int64_t yb = rows < 65535 ? (rows > 0 ? rows : 1) : 65535;
+  return dim3(static_cast<unsigned>(xb), static_cast<unsigned>(yb));
+}
+
 static int grid_for(int64_t work_items, int per_block) {
   const int64_t blocks = (work_items + per_block - 1) / per_block;
   const int64_t cap = static_cast<int64_t>(num_sms()) * 8;
@@ -151,9 +187,12 @@ int gtk_copy_3d(void* dst, int64_t dpitch, int64_t dslab, const void* src, int64
   if (int e = check_ptr(dst, "dst")) return e;
   if (int e = check_ptr(src, "src")) return e;
   if (int e = check_device()) return e;
-  const int64_t w16 = width / 16, total = w16 * height * depth;
-  copy_3d_kernel<<<grid_for(total, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<uint8_t*>(dst), dpitch, dslab, static_cast<const uint8_t*>(src), spitch, sslab, w16, height, total);
+  if (height * depth > 2147483647) return fail(GTK_ERR_INVALID_ARG, "copy_3d: too many rows");
+  const int64_t w16 = width / 16;
+  const dim3 grid = row_grid(w16, height * depth);
+  copy_3d_kernel<<<grid, kRowThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<uint8_t*>(dst), dpitch, dslab, static_cast<const uint8_t*>(src), spitch, sslab, w16,
+      static_cast<int>(height), static_cast<int>(height * depth));
   return check_launch("copy_3d_kernel");
 }
 
@@ -224,9 +263,12 @@ int gtk_push_3d(const uint64_t* dsts, int P, int64_t doff, int64_t dpitch, const
   if (int e = check_ptr(dsts, "dsts", 8)) return e;
   if (int e = check_ptr(src, "src")) return e;
   if (int e = check_device()) return e;
-  const int64_t w16 = width / 16, total = w16 * height * P;
-  push_3d_kernel<<<grid_for(total, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      dsts, doff, dpitch, static_cast<const uint8_t*>(src), spitch, sslab, w16, height, total);
+  if (height * P > 2147483647) return fail(GTK_ERR_INVALID_ARG, "push_3d: too many rows");
+  const int64_t w16 = width / 16;
+  const dim3 grid = row_grid(w16, height * P);
+  push_3d_kernel<<<grid, kRowThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      dsts, doff, dpitch, static_cast<const uint8_t*>(src), spitch, sslab, w16, static_cast<int>(height),
+      static_cast<int>(height * P));
   return check_launch("push_3d_kernel");
 }
 
@@ -234,11 +276,18 @@ int gtk_push_pair_transpose(const float* src, const uint64_t* dsts, int64_t B, i
                             int64_t ndst, int64_t row0, void* stream) {
   if (B < 1 || R < 1 || C < 1 || P < 1 || C % P || row0 < 0 || row0 + R > ndst)
     return fail(GTK_ERR_INVALID_ARG, "push_pair_transpose: need C divisible by P and row0 + R <= ndst");
+  if (B * R > 2147483647 || C > 2147483647 || row0 > 2147483647)
+    return fail(GTK_ERR_INVALID_ARG, "push_pair_transpose: sizes too large");
   if (int e = check_ptr(src, "src")) return e;
   if (int e = check_ptr(dsts, "dsts", 8)) return e;
   if (int e = check_device()) return e;
-  push_pair_transpose_kernel<<<grid_for(B * R * C, 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const float4*>(src), dsts, B, R, C, P, ndst, row0);
+  const int n_rows = static_cast<int>(B * R);
+  const int64_t xb = (C + 15) / 16;  // 8 warps x 2 vectors per block and row
+  const int64_t cap_y = 65535;
+  dim3 grid(static_cast<unsigned>(xb < 64 ? xb : 64), static_cast<unsigned>(n_rows < cap_y ? n_rows : cap_y));
+  push_pair_transpose_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const float4*>(src), dsts, static_cast<int>(R), static_cast<int>(C), static_cast<int>(C / P),
+      ndst, static_cast<int>(row0), n_rows);
   return check_launch("push_pair_transpose_kernel");
 }
 

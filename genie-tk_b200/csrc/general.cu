@@ -171,7 +171,8 @@ __global__ void __launch_bounds__(256)
 // ---------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256)
     trimul_planes_kernel(const float* __restrict__ Y, int64_t ldy, const float* __restrict__ mask,
-                         __half* __restrict__ a, __half* __restrict__ b, int64_t N, int c, int64_t ld) {
+                         __half* __restrict__ a, __half* __restrict__ b, int64_t N, int c, int64_t ld,
+                         uint32_t* status) {
   __shared__ float ta[32][33], tb[32][33];
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   const int64_t row = blockIdx.x;  // b*N + i
@@ -192,15 +193,17 @@ __global__ void __launch_bounds__(256)
     tb[kk][tx] = vb;
   }
   __syncthreads();
+  uint32_t sat = 0;  // an a / b value beyond the fp16 range was clamped
   for (int cc = ty; cc < 32; cc += 8) {
     const int ch = c0 + cc;
     const int64_t k = k0 + tx;
     if (ch < c && k < ld) {
       const int64_t o = (row * c + ch) * ld + k;
-      a[o] = f16_sat(ta[tx][cc]);
-      b[o] = f16_sat(tb[tx][cc]);
+      a[o] = f16_sat_chk(ta[tx][cc], sat);
+      b[o] = f16_sat_chk(tb[tx][cc], sat);
     }
   }
+  flag_saturation(sat, status);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -523,7 +526,7 @@ int trimul_forward(int outgoing, const float* z, const float* mask, const void* 
     const int64_t kb = (ld + 31) / 32;
     if (B * N > 2147483647 || kb > 65535) return fail(GTK_ERR_INVALID_ARG, "trimul: N too large");
     dim3 grid(static_cast<unsigned>(B * N), static_cast<unsigned>(kb), static_cast<unsigned>((c + 31) / 32));
-    trimul_planes_kernel<<<grid, 256, 0, st>>>(Y, ldy, mask, ap, bp, N, c, ld);
+    trimul_planes_kernel<<<grid, 256, 0, st>>>(Y, ldy, mask, ap, bp, N, c, ld, status);
     if (int e = check_launch("general trimul_planes_kernel")) return e;
   }
   const float xs = 1.f / static_cast<float>(N);

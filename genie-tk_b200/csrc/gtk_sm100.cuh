@@ -26,6 +26,7 @@ enum StatusBits : uint32_t {
   kStatusTimeoutDrain = 1u << 3,
   kStatusBadLaunch = 1u << 4,
   kStatusTimeoutPeer = 1u << 5,  // a cross-GPU barrier ran out (a peer never arrived)
+  kStatusSaturated = 1u << 6,    // an fp16 intermediate was beyond +-65504 and was clamped
 };
 
 // Wall-clock limit for any single wait: 2 s is orders of magnitude above any
@@ -400,6 +401,21 @@ __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
 }
 
 __device__ __forceinline__ __half f16_sat(float x) { return __float2half_rn(fminf(fmaxf(x, -65504.f), 65504.f)); }
+
+// The same conversions for values that are not bounded by construction: `sat` records
+// whether either input was beyond the fp16 range (and so was clamped).
+__device__ __forceinline__ uint32_t pack_f16x2_chk(float lo, float hi, uint32_t& sat) {
+  sat |= static_cast<uint32_t>(fmaxf(fabsf(lo), fabsf(hi)) > 65504.f);
+  return pack_f16x2(lo, hi);
+}
+__device__ __forceinline__ __half f16_sat_chk(float x, uint32_t& sat) {
+  sat |= static_cast<uint32_t>(fabsf(x) > 65504.f);
+  return f16_sat(x);
+}
+// Report a clamp seen by this thread in the caller's status word (GTK_STATUS_FP16_SATURATED).
+__device__ __forceinline__ void flag_saturation(uint32_t sat, uint32_t* status) {
+  if (sat && status) atomicOr(status, kStatusSaturated);
+}
 
 __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }

@@ -261,6 +261,7 @@ __global__ void __launch_bounds__(k5a::kThreads, 1)
     const int q4 = warp & 3, hh = (warp - 8) >> 2;
     const int p = q4 * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
+    uint32_t sat = 0;  // a hidden value beyond the fp16 range was clamped
     int it = 0;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
       const int jt = tile % n_jt, rb = tile / n_jt;
@@ -287,10 +288,10 @@ __global__ void __launch_bounds__(k5a::kThreads, 1)
 #pragma unroll
             for (int e4 = 0; e4 < 4; ++e4) {
               const float4 bb = *reinterpret_cast<const float4*>(b1_s + u0 + k * 16 + e4 * 4);
-              w[2 * e4] = pack_f16x2(fmaxf(__uint_as_float(x[cur][e4 * 4 + 0]) + bb.x, 0.f),
-                                     fmaxf(__uint_as_float(x[cur][e4 * 4 + 1]) + bb.y, 0.f));
-              w[2 * e4 + 1] = pack_f16x2(fmaxf(__uint_as_float(x[cur][e4 * 4 + 2]) + bb.z, 0.f),
-                                         fmaxf(__uint_as_float(x[cur][e4 * 4 + 3]) + bb.w, 0.f));
+              w[2 * e4] = pack_f16x2_chk(fmaxf(__uint_as_float(x[cur][e4 * 4 + 0]) + bb.x, 0.f),
+                                         fmaxf(__uint_as_float(x[cur][e4 * 4 + 1]) + bb.y, 0.f), sat);
+              w[2 * e4 + 1] = pack_f16x2_chk(fmaxf(__uint_as_float(x[cur][e4 * 4 + 2]) + bb.z, 0.f),
+                                             fmaxf(__uint_as_float(x[cur][e4 * 4 + 3]) + bb.w, 0.f), sat);
             }
             stg_v8(hrow + u0 + k * 16, w[0], w[1], w[2], w[3], w[4], w[5], w[6], w[7]);
           }
@@ -300,6 +301,7 @@ __global__ void __launch_bounds__(k5a::kThreads, 1)
       }
       if (!ok) break;
     }
+    flag_saturation(sat, status);
   }
   tc_fence_before();
   __syncthreads();

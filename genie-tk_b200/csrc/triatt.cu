@@ -238,6 +238,7 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
       loaded = 1;
     }
     bool ok = true;
+    uint32_t sat = 0;  // a LayerNorm output beyond the fp16 range was clamped
     int it = 0;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
       const int jt = tile % n_jt, bi = tile / n_jt;
@@ -313,10 +314,10 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
                      y[6] * u3.x + y[7] * u3.y;
         }
         uint4 o;
-        o.x = pack_f16x2(y[0], y[1]);
-        o.y = pack_f16x2(y[2], y[3]);
-        o.z = pack_f16x2(y[4], y[5]);
-        o.w = pack_f16x2(y[6], y[7]);
+        o.x = pack_f16x2_chk(y[0], y[1], sat);
+        o.y = pack_f16x2_chk(y[2], y[3], sat);
+        o.z = pack_f16x2_chk(y[4], y[5], sat);
+        o.w = pack_f16x2_chk(y[6], y[7], sat);
         sts_u4(smem + k3::kA + half * 16384 + swz128(p, ch), o);
       }
 #pragma unroll
@@ -356,6 +357,7 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
         if (!ok) break;
       }
     }
+    flag_saturation(sat, status);
     if (!ok && tid == 0) {
       // abort: wait (bounded) for this thread's MMAs and TMA loads still in flight
       umma_commit(&bars->drain);
@@ -368,6 +370,7 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
     const int q4 = warp & 3, hh = (warp - 8) >> 2;
     const int p = q4 * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
+    uint32_t sat = 0;  // a q / k / v value beyond the fp16 range was clamped
     int it = 0;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
       const int jt = tile % n_jt, bi = tile / n_jt;
@@ -397,13 +400,15 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
           const int cc = 2 * hh + (k >> 1), c16 = (k & 1) * 16;
           uint32_t w0[8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) w0[e] = pack_f16x2(__uint_as_float(x0[cur][2 * e]), __uint_as_float(x0[cur][2 * e + 1]));
+          for (int e = 0; e < 8; ++e)
+            w0[e] = pack_f16x2_chk(__uint_as_float(x0[cur][2 * e]), __uint_as_float(x0[cur][2 * e + 1]), sat);
           __half* dst0 = (h == 0 ? q_out : v_out) + ((static_cast<size_t>(bi) * kHeads + cc) * N + j) * kHeadDim + c16;
           stg_v8(dst0, w0[0], w0[1], w0[2], w0[3], w0[4], w0[5], w0[6], w0[7]);
           uint32_t w1[8];
           if (h == 0) {
 #pragma unroll
-            for (int e = 0; e < 8; ++e) w1[e] = pack_f16x2(__uint_as_float(x1[cur][2 * e]), __uint_as_float(x1[cur][2 * e + 1]));
+            for (int e = 0; e < 8; ++e)
+              w1[e] = pack_f16x2_chk(__uint_as_float(x1[cur][2 * e]), __uint_as_float(x1[cur][2 * e + 1]), sat);
           } else {
             const float* bgc = bg_s + cc * 32 + c16;
 #pragma unroll
@@ -426,6 +431,7 @@ __global__ void __launch_bounds__(k3::kThreads, 1)
       }
       if (!ok) break;
     }
+    flag_saturation(sat, status);
   }
   tc_fence_before();
   __syncthreads();
@@ -833,6 +839,7 @@ __global__ void __launch_bounds__(k4::kThreads, 1)
     const bool fin = __all_sync(0xffffffffu, ok && mbar_wait(&bars->o_final, 0, guard, status,
                                                              kStatusTimeoutConsumer) && !guard->abort);
     if (fin) {
+      uint32_t sat = 0;  // a gated output beyond the fp16 range was clamped
       tc_fence_after();
       uint32_t ov[2][32];
       tmem_ld32(tmem + lane_off + wg * 32, ov[0]);
@@ -851,8 +858,8 @@ __global__ void __launch_bounds__(k4::kThreads, 1)
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const float2 gf = __half22float2(gh[e]);
-              o16[ch * 4 + e] = pack_f16x2(__uint_as_float(ov[rr][ch * 8 + 2 * e]) * inv * gf.x,
-                                           __uint_as_float(ov[rr][ch * 8 + 2 * e + 1]) * inv * gf.y);
+              o16[ch * 4 + e] = pack_f16x2_chk(__uint_as_float(ov[rr][ch * 8 + 2 * e]) * inv * gf.x,
+                                               __uint_as_float(ov[rr][ch * 8 + 2 * e + 1]) * inv * gf.y, sat);
             }
           }
           __half* op = og + pair * 128 + h * kHeadDim;  // 64 contiguous bytes, 64-byte aligned
@@ -860,6 +867,7 @@ __global__ void __launch_bounds__(k4::kThreads, 1)
           stg_v8(op + 16, o16[8], o16[9], o16[10], o16[11], o16[12], o16[13], o16[14], o16[15]);
         }
       }
+      flag_saturation(sat, status);
     }
   }
   tc_fence_before();

@@ -332,6 +332,7 @@ __global__ void __launch_bounds__(k1::kThreads, 1)
     const int grp = c / a_dst.group, c_in_grp = c - grp * a_dst.group;  // this channel's destination group
     const float bias_p0 = vec[tmpack::kVB1 + c], bias_p1 = vec[tmpack::kVB1 + 256 + c];
     const float bias_g0 = vec[tmpack::kVB1 + 128 + c], bias_g1 = vec[tmpack::kVB1 + 384 + c];
+    uint32_t sat = 0;  // an a / b value beyond the fp16 range was clamped
     int it = 0;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
       const int s = it & 1;
@@ -375,8 +376,8 @@ __global__ void __launch_bounds__(k1::kThreads, 1)
               const float pm = (__uint_as_float(pv[cur][u * 4 + e]) + bp) * mv[e];
               o[e] = fmaf(pm, tanh_approx(__uint_as_float(gv[cur][u * 4 + e]) + bg), pm);
             }
-            w[2 * u] = pack_f16x2(o[0], o[1]);
-            w[2 * u + 1] = pack_f16x2(o[2], o[3]);
+            w[2 * u] = pack_f16x2_chk(o[0], o[1], sat);
+            w[2 * u + 1] = pack_f16x2_chk(o[2], o[3], sat);
           }
           // 32 contiguous bytes of the channel row: one 32-byte store when the plane pitch
           // keeps it 32-byte aligned (pitch a multiple of 16), two 16-byte stores otherwise
@@ -396,6 +397,7 @@ __global__ void __launch_bounds__(k1::kThreads, 1)
       if (!ok) break;
       mbar_arrive(&bars->m_empty[s]);
     }
+    flag_saturation(sat, status);
   }
   tc_fence_before();
   __syncthreads();
@@ -565,6 +567,7 @@ __global__ void __launch_bounds__(k2::kThreads, 1)
     const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
     const bool issuer = (tid == 0);
     bool ok = true;
+    uint32_t sat = 0;     // an x value beyond the fp16 range was clamped
     int n = 0, half = 0;  // tile counter, staging-half counter
     for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++n) {
       int jt, it, c, b;
@@ -593,10 +596,14 @@ __global__ void __launch_bounds__(k2::kThreads, 1)
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             uint4 o;
-            o.x = pack_f16x2(__uint_as_float(v[u * 8 + 0]) * out_scale, __uint_as_float(v[u * 8 + 1]) * out_scale);
-            o.y = pack_f16x2(__uint_as_float(v[u * 8 + 2]) * out_scale, __uint_as_float(v[u * 8 + 3]) * out_scale);
-            o.z = pack_f16x2(__uint_as_float(v[u * 8 + 4]) * out_scale, __uint_as_float(v[u * 8 + 5]) * out_scale);
-            o.w = pack_f16x2(__uint_as_float(v[u * 8 + 6]) * out_scale, __uint_as_float(v[u * 8 + 7]) * out_scale);
+            o.x = pack_f16x2_chk(__uint_as_float(v[u * 8 + 0]) * out_scale, __uint_as_float(v[u * 8 + 1]) * out_scale,
+                                 sat);
+            o.y = pack_f16x2_chk(__uint_as_float(v[u * 8 + 2]) * out_scale, __uint_as_float(v[u * 8 + 3]) * out_scale,
+                                 sat);
+            o.z = pack_f16x2_chk(__uint_as_float(v[u * 8 + 4]) * out_scale, __uint_as_float(v[u * 8 + 5]) * out_scale,
+                                 sat);
+            o.w = pack_f16x2_chk(__uint_as_float(v[u * 8 + 6]) * out_scale, __uint_as_float(v[u * 8 + 7]) * out_scale,
+                                 sat);
             sts_u4(box + swz128(p, chb + u), o);
           }
         }
@@ -625,6 +632,7 @@ __global__ void __launch_bounds__(k2::kThreads, 1)
       }
     }
     if (issuer) tma_store_wait_all();
+    flag_saturation(sat, status);
   }
   tc_fence_before();
   __syncthreads();

@@ -111,6 +111,10 @@ _SIGNATURES = {
     "gtk_dropout_keep_bits_philox": (c_int, [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_double, c_i64, c_vp, c_vp]),
     "gtk_dropout_pack_keep_bits": (c_int, [c_vp, c_i64, c_vp, c_vp]),
     "gtk_layernorm": (c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, ctypes.c_float, c_vp]),
+    "gtk_attn_core_forward": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_int, c_int, ctypes.c_float,
+                                      c_vp, c_vp, c_vp]),
+    "gtk_attn_core_backward": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_int, c_int,
+                                       ctypes.c_float, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "gtk_trimul_forward_dropout": (c_int, [c_int, c_vp, c_vp, c_vp, c_vp, c_int, ctypes.POINTER(Dropout), c_vp, c_size,
                                            c_i64, c_i64, c_int, c_int, c_vp, c_vp]),
     "gtk_triatt_forward_dropout": (c_int, [c_int, c_vp, c_vp, c_vp, c_vp, c_int, ctypes.POINTER(Dropout), c_vp, c_size,

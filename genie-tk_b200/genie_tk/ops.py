@@ -473,6 +473,54 @@ def transition_forward(z: torch.Tensor, mask: Optional[torch.Tensor], packed: to
 
 
 # --------------------------------------------------------------------------------------
+# The attention core for training (gtk_attn_core_forward / gtk_attn_core_backward)
+# --------------------------------------------------------------------------------------
+
+def _core_args(q, k, v, tri, mask, heads):
+    for name, t in (("q", q), ("k", k), ("v", v), ("tri", tri)):
+        _require_cuda(t, name, torch.float32)
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+    B, N, N2, hd = q.shape
+    if N2 != N or k.shape != q.shape or v.shape != q.shape or hd % heads:
+        raise ValueError("q, k, v must be [B, N, N, heads * head_dim]")
+    if tuple(tri.shape) != (B, heads, N, N):
+        raise ValueError(f"tri must be [B, heads, N, N] = {(B, heads, N, N)}, got {tuple(tri.shape)}")
+    if mask is not None:
+        _require_cuda(mask, "mask", torch.float32)
+        if tuple(mask.shape) != (B, N, N) or not mask.is_contiguous():
+            raise ValueError("mask must be a contiguous fp32 [B, N, N] tensor")
+    return B, N, hd // heads
+
+
+def attn_core_forward(q, k, v, tri, mask, heads: int, inf: float = 1e9):
+    """o = softmax(q k^T / sqrt(d) + inf (mask - 1) + tri) v per (b, i, h) and the softmax
+    statistics [B, N, heads, N, 2], without forming the scores (fp32)."""
+    lib = _lib.load()
+    B, N, d = _core_args(q, k, v, tri, mask, heads)
+    o = torch.empty_like(q)
+    stats = torch.empty(B, N, heads, N, 2, dtype=torch.float32, device=q.device)
+    _lib.check(lib.gtk_attn_core_forward(_ptr(q), _ptr(k), _ptr(v), _ptr(tri), _ptr(mask), B, N, heads, d,
+                                         float(inf), _ptr(o), _ptr(stats), _stream(q.device)),
+               "gtk_attn_core_forward")
+    return o, stats
+
+
+def attn_core_backward(q, k, v, tri, mask, stats, o, do, heads: int, inf: float = 1e9):
+    """(dq, dk, dv, dtri) of the attention core for the output gradient ``do``."""
+    lib = _lib.load()
+    B, N, d = _core_args(q, k, v, tri, mask, heads)
+    do = do.float().contiguous()
+    dsum = (do * o).view(B, N, N, heads, d).sum(-1).permute(0, 1, 3, 2).contiguous()  # [B, N(i), H, N(j)]
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    dtri = torch.empty_like(tri)
+    _lib.check(lib.gtk_attn_core_backward(_ptr(q), _ptr(k), _ptr(v), _ptr(tri), _ptr(mask), _ptr(stats), _ptr(do),
+                                          _ptr(dsum), B, N, heads, d, float(inf), _ptr(dq), _ptr(dk), _ptr(dv),
+                                          _ptr(dtri), _stream(q.device)), "gtk_attn_core_backward")
+    return dq, dk, dv, dtri
+
+
+# --------------------------------------------------------------------------------------
 # LayerNorm over the last axis (the reference's _C.layernorm)
 # --------------------------------------------------------------------------------------
 

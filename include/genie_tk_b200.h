@@ -16,11 +16,16 @@
  *    fp32 [B, N, N] (NULL = all ones); parameters are the fp32 nn.Linear / LayerNorm
  *    tensors of the reference modules ([out, in] weights).
  *  - `status` (optional, may be NULL) is a device uint32 word. A kernel whose bounded
- *    wait ran out ORs a GTK_STATUS_* bit into it and exits cleanly instead of hanging.
- *    Read it after synchronising the stream.
- *  - Supported shapes: c_z = c_hidden = 128 for the multiplicative update; c_in = 128,
- *    c_hidden = 128 (4 heads x 32) for attention; any B >= 1 and N >= 1. Other shapes
- *    return GTK_ERR_UNSUPPORTED.
+ *    wait ran out, or that had to clamp an fp16 intermediate, ORs a GTK_STATUS_* bit into
+ *    it and finishes cleanly instead of hanging or failing silently. Read it after
+ *    synchronising the stream.
+ *  - Shapes: the multiplicative update with c_z = c_hidden = 128, attention with c_in =
+ *    c_hidden = 128 (4 heads x 32) and the transition with c_p = 128, n = 4 run on the
+ *    tuned tcgen05 kernels. Every other shape the reference's modules accept -- channel
+ *    counts 1..512, attention heads 1..32 with head_dim = c_hidden / heads <= 64, a
+ *    transition hidden width <= 2048 -- runs on the general-shape kernels behind the same
+ *    forward entry points (the stage entry points below are the tuned shape only). Beyond
+ *    those limits GTK_ERR_UNSUPPORTED. Any B >= 1 and N >= 1.
  *  - Thread safety: entry points may be called concurrently on different streams.
  */
 #ifndef GENIE_TK_B200_H_
@@ -53,6 +58,13 @@ extern "C" {
 #define GTK_STATUS_TIMEOUT_CONSUMER 0x4u
 #define GTK_STATUS_TIMEOUT_DRAIN 0x8u
 #define GTK_STATUS_TIMEOUT_PEER 0x20u /* a cross-GPU barrier ran out: a peer never arrived */
+/* An fp16 intermediate (a/b/x planes of the multiplicative update; the LayerNorm output,
+ * q, k, v and gated output of attention; the transition's hidden rows) was beyond
+ * +-65504 and was clamped, so the result is not the reference's. The tensor-core operands
+ * are fp16 (11 significant bits, 3 more than bf16) and in range for LayerNorm-normalised
+ * inputs and weights of the usual 1/fan_in scale; inputs or weights large enough to leave
+ * that range set this bit instead of returning a silently wrong answer. */
+#define GTK_STATUS_FP16_SATURATED 0x40u
 
 /* Library version (major*10000 + minor*100 + patch). */
 GTK_API int gtk_version(void);
@@ -366,6 +378,31 @@ GTK_API int gtk_triatt_forward_dropout(int starting, const float* z, const float
                                        float* out, int add_residual, const gtk_dropout* dropout, void* workspace,
                                        size_t workspace_bytes, int64_t B, int64_t N, int c_in, int c_hidden,
                                        int heads, float inf, uint32_t* status, void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * The attention core for training (the gradient the reference gets from PyTorch autograd
+ * through src/genie_tk/primitives.py:134-164 and triangle_attention.py:115-137), in the
+ * block's frame (z for the starting node, z^T for the ending node), pair row i, query j,
+ * key k, head h of head_dim d:
+ *   s = q[i,j,h] . k[i,k,h] / sqrt(d) + inf (mask[i,k] - 1) + tri[h,j,k],
+ *   o[i,j,h] = sum_k softmax_k(s) v[i,k,h].
+ * q, k, v, o and the gradients dq, dk, dv, dO: fp32 [B, N(i), N(j), heads * head_dim];
+ * tri, dtri: fp32 [B, heads, N(j), N(k)]; mask: fp32 [B, N(i), N(k)] in the block's frame,
+ * or NULL. Neither entry point forms the [B, N, heads, N, N] scores (fp32 CUDA-core
+ * kernels; head_dim <= 64). All pointers 4-byte aligned, `stats` 8-byte aligned.
+ * ------------------------------------------------------------------------------- */
+
+/* o and the softmax statistics: stats[b][i][h][j] = (max of the base-2 scores, 1 / sum of
+ * 2^(score - max)), two floats. */
+GTK_API int gtk_attn_core_forward(const float* q, const float* k, const float* v, const float* tri,
+                                  const float* mask, int64_t B, int64_t N, int heads, int head_dim, float inf,
+                                  float* o, float* stats, void* stream);
+/* dq, dk, dv and dtri from dO, the forward's stats and dsum[b][i][h][j] = sum_e dO o
+ * (over the head's d channels). dtri sums the score gradients over the rows i. */
+GTK_API int gtk_attn_core_backward(const float* q, const float* k, const float* v, const float* tri,
+                                   const float* mask, const float* stats, const float* dO, const float* dsum,
+                                   int64_t B, int64_t N, int heads, int head_dim, float inf, float* dq, float* dk,
+                                   float* dv, float* dtri, void* stream);
 
 /* ---------------------------------------------------------------------------------
  * LayerNorm over the last axis: the reference's `_C.layernorm(x, gamma, beta, eps)`
