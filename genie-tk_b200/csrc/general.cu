@@ -95,14 +95,53 @@ struct Epi {
 
 constexpr int kBM = 64, kBN = 64, kBK = 16;
 
+// What the GEMM applies to A's elements as it loads them: nothing, a LayerNorm of each row
+// (the CTA computes the 64 rows' mean and 1/std first), or a sigmoid gate.
+enum ProMode : int { kProNone = 0, kProLn = 1, kProGate = 2 };
+
+struct Pro {
+  const float* gamma;  // kProLn
+  const float* beta;
+  float eps;
+  const float* gate;   // kProGate: [M][ldg]
+  int64_t ldg;
+};
+
+template <int kPro>
 __global__ void __launch_bounds__(256)
     gemm_kernel(const float* __restrict__ A, int64_t M, int K, int64_t lda, const float* __restrict__ W, int n_out,
-                int64_t ldw, const Epi e) {
+                int64_t ldw, const Epi e, const Pro pro) {
   __shared__ __align__(16) float As[kBK][kBM + 4];
   __shared__ __align__(16) float Ws[kBK][kBN + 4];
+  __shared__ float mean_s[kPro == kProLn ? kBM : 1], rstd_s[kPro == kProLn ? kBM : 1];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   const int64_t m0 = static_cast<int64_t>(blockIdx.x) * kBM;
   const int n0 = blockIdx.y * kBN;
+  if constexpr (kPro == kProLn) {
+    const int lane = tid & 31;
+    const float inv = 1.f / static_cast<float>(K);
+    for (int r = tid >> 5; r < kBM; r += 8) {
+      const int64_t m = m0 + r;
+      float mean = 0.f, rstd = 0.f;
+      if (m < M) {
+        const float* xr = A + m * lda;
+        float sum = 0.f;
+        for (int k = lane; k < K; k += 32) sum += xr[k];
+        mean = warp_sum(sum) * inv;
+        float var = 0.f;
+        for (int k = lane; k < K; k += 32) {
+          const float dx = xr[k] - mean;
+          var = fmaf(dx, dx, var);
+        }
+        rstd = rsqrtf(warp_sum(var) * inv + pro.eps);
+      }
+      if (lane == 0) {
+        mean_s[r] = mean;
+        rstd_s[r] = rstd;
+      }
+    }
+    __syncthreads();
+  }
   float acc[4][4];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
@@ -114,7 +153,13 @@ __global__ void __launch_bounds__(256)
       const int idx = tid + u * 256, r = idx >> 4, kk = idx & 15;
       const int64_t m = m0 + r;
       const int k = k0 + kk, n = n0 + r;
-      As[kk][r] = (m < M && k < K) ? A[m * lda + k] : 0.f;
+      float x = 0.f;
+      if (m < M && k < K) {
+        x = A[m * lda + k];
+        if constexpr (kPro == kProLn) x = fmaf((x - mean_s[r]) * rstd_s[r], pro.gamma[k], pro.beta[k]);
+        if constexpr (kPro == kProGate) x *= sigmoid_f(pro.gate[m * pro.ldg + k]);
+      }
+      As[kk][r] = x;
       Ws[kk][r] = (n < n_out && k < K) ? W[static_cast<int64_t>(n) * ldw + k] : 0.f;
     }
     __syncthreads();
@@ -377,7 +422,7 @@ static int launch_gemm(const float* A, int64_t M, int K, int64_t lda, const floa
   const int64_t mt = (M + kBM - 1) / kBM;
   if (mt > 2147483647) return fail(GTK_ERR_INVALID_ARG, "general gemm: too many rows");
   dim3 grid(static_cast<unsigned>(mt), static_cast<unsigned>((n_out + kBN - 1) / kBN));
-  gemm_kernel<<<grid, 256, 0, st>>>(A, M, K, lda, W, n_out, ldw, e);
+  gemm_kernel<kProNone><<<grid, 256, 0, st>>>(A, M, K, lda, W, n_out, ldw, e, Pro{});
   return check_launch("general gemm_kernel");
 }
 
@@ -778,3 +823,77 @@ int transition_forward(const float* z, const float* mask, const void* packed, fl
 
 }  // namespace gen
 }  // namespace gtk
+
+// ---------------------------------------------------------------------------------------
+// Linear layers of the reference's modules outside the triangle blocks: the fused
+// LayerNorm + linear of its `_C` module and the (gated) projections of `Attention`.
+// ---------------------------------------------------------------------------------------
+namespace {
+
+int linear_args(const float* x, const float* weight, const float* bias, const float* out, int64_t rows, int64_t D_in,
+                int64_t D_out) {
+  using namespace gtk;
+  if (rows < 1 || !dims_ok(rows, int64_t(1) << 40) || D_in < 1 || D_out < 1 || D_in > (1 << 24) ||
+      D_out > (1 << 24) || (D_out + gen::kBN - 1) / gen::kBN > 65535)
+    return fail(GTK_ERR_INVALID_ARG, "linear: bad rows / D_in / D_out");
+  if (int e = check_ptr(x, "x", 4)) return e;
+  if (int e = check_ptr(weight, "weight", 4)) return e;
+  if (int e = check_ptr(out, "out", 4)) return e;
+  if (bias && (reinterpret_cast<uintptr_t>(bias) & 3)) return fail(GTK_ERR_ALIGNMENT, "bias is misaligned");
+  return GTK_OK;
+}
+
+int launch_linear(int pro_mode, const float* x, const float* weight, const float* bias, float* out, int64_t rows,
+                  int64_t D_in, int64_t D_out, const gtk::gen::Pro& pro, void* stream) {
+  using namespace gtk;
+  using namespace gtk::gen;
+  const int64_t mt = (rows + kBM - 1) / kBM;
+  if (mt > 2147483647) return fail(GTK_ERR_INVALID_ARG, "linear: too many rows");
+  const dim3 grid(static_cast<unsigned>(mt), static_cast<unsigned>((D_out + kBN - 1) / kBN));
+  const Epi e = epi(kStore, bias, out, D_out);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int K = static_cast<int>(D_in), n_out = static_cast<int>(D_out);
+  if (pro_mode == kProLn)
+    gemm_kernel<kProLn><<<grid, 256, 0, st>>>(x, rows, K, D_in, weight, n_out, D_in, e, pro);
+  else if (pro_mode == kProGate)
+    gemm_kernel<kProGate><<<grid, 256, 0, st>>>(x, rows, K, D_in, weight, n_out, D_in, e, pro);
+  else
+    gemm_kernel<kProNone><<<grid, 256, 0, st>>>(x, rows, K, D_in, weight, n_out, D_in, e, pro);
+  return check_launch("linear gemm_kernel");
+}
+
+}  // namespace
+
+extern "C" {
+
+int gtk_layernorm_linear(const float* x, const float* gamma, const float* beta, const float* weight,
+                         const float* bias, float* out, int64_t rows, int64_t D_in, int64_t D_out, float eps,
+                         void* stream) {
+  using namespace gtk;
+  if (int e = linear_args(x, weight, bias, out, rows, D_in, D_out)) return e;
+  if (!(eps >= 0.f) || !std::isfinite(eps)) return fail(GTK_ERR_INVALID_ARG, "layernorm_linear: eps must be >= 0");
+  if (int e = check_ptr(gamma, "gamma", 4)) return e;
+  if (int e = check_ptr(beta, "beta", 4)) return e;
+  if (x == out) return fail(GTK_ERR_INVALID_ARG, "layernorm_linear: out must not alias x");
+  if (int e = check_device()) return e;
+  gen::Pro pro{};
+  pro.gamma = gamma;
+  pro.beta = beta;
+  pro.eps = eps;
+  return launch_linear(gen::kProLn, x, weight, bias, out, rows, D_in, D_out, pro, stream);
+}
+
+int gtk_linear(const float* x, const float* gate, const float* weight, const float* bias, float* out, int64_t rows,
+               int64_t D_in, int64_t D_out, void* stream) {
+  using namespace gtk;
+  if (int e = linear_args(x, weight, bias, out, rows, D_in, D_out)) return e;
+  if (gate && (reinterpret_cast<uintptr_t>(gate) & 3)) return fail(GTK_ERR_ALIGNMENT, "gate is misaligned");
+  if (x == out || (gate && gate == out)) return fail(GTK_ERR_INVALID_ARG, "linear: out must not alias x or gate");
+  if (int e = check_device()) return e;
+  gen::Pro pro{};
+  pro.gate = gate;
+  pro.ldg = D_in;
+  return launch_linear(gate ? gen::kProGate : gen::kProNone, x, weight, bias, out, rows, D_in, D_out, pro, stream);
+}
+
+}  // extern "C"

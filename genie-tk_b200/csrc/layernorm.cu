@@ -1,9 +1,10 @@
 // LayerNorm over the last axis: the reference's `_C.layernorm` (kernels/bindings.cpp:93-95,
 // declared at :49-55, host code kernels/fused_layernorm/layernorm.cu:17-44):
 //   out[r, :] = (x[r, :] - mean_r) / sqrt(var_r + eps) * gamma + beta,
-// var the biased variance, fp32 in and out (the reference's tensors are fp32). It also
-// serves `_C.fused_layernorm_linear` (normalise here, then one library GEMM). The triangle
-// blocks do not use it: their LayerNorms are fused into the projection kernels.
+// var the biased variance, fp32 in and out (the reference's tensors are fp32).
+// `_C.fused_layernorm_linear` does not use it: gtk_layernorm_linear (general.cu) normalises
+// the rows inside its GEMM. The triangle blocks' LayerNorms are fused into their projection
+// kernels.
 //
 // One warp per row, grid-stride over rows. The row is read three times (sum, centred second
 // moment, output) from L1/L2 -- rows are short (c_z = 128 floats = 512 B) -- and written

@@ -17,7 +17,9 @@ attention ones, and the LayerNorm ones are not called at all. Code that imports
       o[b,h,i,j,:] = sum_k softmax_k(scale q[b,h,i,j].k[b,h,i,k] + bias[b,h,j,k]
                                      + 1e9 (mask[b,i,k] - 1)) v[b,h,i,k,:]
       q, k, v [B, H, N, N, D] (triangle_attention.cuh:110-112), bias [B, H, N, N], mask
-      [B, N, N]; H = 4, D = 32. Runs on the attention-core kernel. Returns q's dtype.
+      [B, N, N]. The reference kernel's H = 4, D = 32 runs on the tuned tcgen05 attention
+      core; any other H and D <= 64 on the tensor-core attention core of the training path
+      (gtk_attn_core_forward). Returns q's dtype.
   triangle_attention_ending(q, k, v, bias, mask, scale)
       the same around the ending node: the starting form on q, k, v and mask with their two
       pair axes swapped, the result swapped back; bias is in the problem frame, as the
@@ -26,7 +28,8 @@ attention ones, and the LayerNorm ones are not called at all. Code that imports
       LayerNorm over the last axis (kernels/fused_layernorm/layernorm.cu:17-44), fp32.
   fused_layernorm_linear(x, gamma, beta, weight, bias=None, eps=1e-5)
       LayerNorm(x) @ weight (+ bias) with weight [D_in, D_out], the reference's layout
-      (layernorm.cu:46-76): the LayerNorm kernel, then one library GEMM.
+      (layernorm.cu:46-76), in one kernel (gtk_layernorm_linear): the rows are normalised
+      as the GEMM loads them and never reach memory. fp32.
 
 Errors are ``RuntimeError``, as the reference's TORCH_CHECKs raise. CUDA tensors only.
 """
@@ -83,8 +86,7 @@ def _attention(q: Tensor, k: Tensor, v: Tensor, bias: Tensor, mask: Optional[Ten
     _check(q.dim() == 5 and q.shape == k.shape == v.shape, "q, k, v must be [B, H, N, N, D] of one shape")
     B, H, N, N2, D = q.shape
     _check(N == N2, "q, k, v must be [B, H, N, N, D]")
-    _check(H == ops.SUPPORTED_HEADS and H * D == ops.SUPPORTED_C,
-           f"the attention kernel supports H = {ops.SUPPORTED_HEADS} heads of {ops.SUPPORTED_C // ops.SUPPORTED_HEADS}")
+    _check(1 <= D <= 64, "the attention kernels support head dims up to 64")
     _check(tuple(bias.shape) == (B, H, N, N), "bias must be [B, H, N, N]")
     if mask is not None:
         _cuda(mask, "mask")
@@ -93,21 +95,36 @@ def _attention(q: Tensor, k: Tensor, v: Tensor, bias: Tensor, mask: Optional[Ten
         q, k, v = (t.transpose(2, 3) for t in (q, k, v))
         mask = None if mask is None else mask.transpose(1, 2)
     with torch.no_grad():
-        ws, offs = ops.triatt_workspace(B, N, q.device)
-        st = ops.triatt_stage_views(ws, offs, B, N)
-        # the core's operand layout: q, k, v [B, i, H, j, D] fp16, q times scale * log2(e)
-        # (the core's softmax is base 2); bias [B, H, j, k] bf16 in log2 units; gate = 1
-        st["q"].copy_((q.float() * (float(scale) * _LOG2E)).permute(0, 2, 1, 3, 4))
-        st["k"].copy_(k.permute(0, 2, 1, 3, 4))
-        st["v"].copy_(v.permute(0, 2, 1, 3, 4))
-        st["bias"][..., :N].copy_(bias.float() * _LOG2E)
-        st["g"].fill_(1.0)
-        m = None if mask is None else mask.float().contiguous()
-        ops.triatt_core(m, True, ws, B, N, inf=_INF)
-        o = st["og"].view(B, N, N, H, D).permute(0, 3, 1, 2, 4)  # [B, H, i, j, D]
+        if H == ops.SUPPORTED_HEADS and H * D == ops.SUPPORTED_C:
+            o = _tuned_core(q, k, v, bias, mask, scale)
+        else:
+            # the training core's layout: [B, i, j, H*D] fp32; it divides q.k by sqrt(D)
+            qf, kf, vf = (t.float().permute(0, 2, 3, 1, 4).reshape(B, N, N, H * D) for t in (q, k, v))
+            qf = (qf * (float(scale) * math.sqrt(D))).contiguous()
+            m = None if mask is None else mask.float().contiguous()
+            of, _, _ = ops.attn_core_forward(qf, kf.contiguous(), vf.contiguous(), bias.float().contiguous(), m, H,
+                                             _INF)
+            o = of.view(B, N, N, H, D).permute(0, 3, 1, 2, 4)  # [B, H, i, j, D]
         if not starting:
             o = o.transpose(2, 3)
         return o.to(q.dtype).contiguous()
+
+
+def _tuned_core(q: Tensor, k: Tensor, v: Tensor, bias: Tensor, mask: Optional[Tensor], scale: float) -> Tensor:
+    """The starting-node core at H = 4, D = 32 on the tuned kernel; o [B, H, i, j, D] fp32."""
+    B, H, N, _, D = q.shape
+    ws, offs = ops.triatt_workspace(B, N, q.device)
+    st = ops.triatt_stage_views(ws, offs, B, N)
+    # the core's operand layout: q, k, v [B, i, H, j, D] fp16, q times scale * log2(e)
+    # (the core's softmax is base 2); bias [B, H, j, k] bf16 in log2 units; gate = 1
+    st["q"].copy_((q.float() * (float(scale) * _LOG2E)).permute(0, 2, 1, 3, 4))
+    st["k"].copy_(k.permute(0, 2, 1, 3, 4))
+    st["v"].copy_(v.permute(0, 2, 1, 3, 4))
+    st["bias"][..., :N].copy_(bias.float() * _LOG2E)
+    st["g"].fill_(1.0)
+    m = None if mask is None else mask.float().contiguous()
+    ops.triatt_core(m, True, ws, B, N, inf=_INF)
+    return st["og"].view(B, N, N, H, D).permute(0, 3, 1, 2, 4).float()
 
 
 def triangle_attention_starting(q: Tensor, k: Tensor, v: Tensor, bias: Tensor, mask: Optional[Tensor],
@@ -138,15 +155,16 @@ def layernorm(x: Tensor, gamma: Tensor, beta: Tensor, eps: float = 1e-5) -> Tens
 
 def fused_layernorm_linear(x: Tensor, gamma: Tensor, beta: Tensor, weight: Tensor, bias: Optional[Tensor] = None,
                            eps: float = 1e-5) -> Tensor:
-    """LayerNorm(x) @ weight (+ bias), weight [D_in, D_out] as in the reference."""
-    _cuda(weight, "weight")
+    """LayerNorm(x) @ weight (+ bias), weight [D_in, D_out] as in the reference; one kernel."""
+    for t, n in ((x, "x"), (gamma, "gamma"), (beta, "beta"), (weight, "weight")):
+        _cuda(t, n)
+    _check(x.dim() >= 1 and x.shape[-1] >= 1, "x must have a last axis")
+    _check(gamma.numel() == x.shape[-1] and beta.numel() == x.shape[-1], "gamma and beta must match x's last axis")
     _check(weight.dim() == 2 and weight.shape[0] == x.shape[-1], "weight must be [D_in, D_out]")
     if bias is not None:
         _cuda(bias, "bias")
         _check(bias.numel() == weight.shape[1], "bias must have D_out elements")
-    y = _layernorm_fp32(x, gamma, beta, eps)
     with torch.no_grad():
-        w = weight.float()
-        out = y @ w if bias is None else torch.addmm(bias.float(), y.reshape(-1, w.shape[0]), w).view(
-            *y.shape[:-1], w.shape[1])
+        out = ops.layernorm_linear(x.float(), gamma.float(), beta.float(), weight.float().t().contiguous(),
+                                   None if bias is None else bias.float(), eps)
         return out.to(x.dtype)

@@ -113,8 +113,16 @@ _SIGNATURES = {
     "gtk_layernorm": (c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, ctypes.c_float, c_vp]),
     "gtk_attn_core_forward": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_int, c_int, ctypes.c_float,
                                       c_vp, c_vp, c_vp]),
-    "gtk_attn_core_backward": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_int, c_int,
-                                       ctypes.c_float, c_vp, c_vp, c_vp, c_vp, c_vp]),
+    "gtk_attn_core_backward": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, ctypes.c_float, c_i64, c_i64,
+                                       c_int, c_int, ctypes.c_float, c_vp, c_vp, c_vp, c_vp, c_vp]),
+    "gtk_attn_core_packed_bytes": (c_size, [c_i64, c_i64, c_int, c_int]),
+    "gtk_attn_core_bias_bytes": (c_size, [c_i64, c_i64, c_int]),
+    "gtk_attn_core_pack": (c_int, [c_vp, c_i64, c_i64, c_int, c_int, ctypes.c_float, c_vp, c_vp]),
+    "gtk_attn_core_pack_bias": (c_int, [c_vp, c_i64, c_i64, c_int, c_vp, c_vp]),
+    "gtk_mha_forward": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_int, c_int,
+                                ctypes.c_float, c_vp, c_vp]),
+    "gtk_layernorm_linear": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, ctypes.c_float, c_vp]),
+    "gtk_linear": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp]),
     "gtk_trimul_forward_dropout": (c_int, [c_int, c_vp, c_vp, c_vp, c_vp, c_int, ctypes.POINTER(Dropout), c_vp, c_size,
                                            c_i64, c_i64, c_int, c_int, c_vp, c_vp]),
     "gtk_triatt_forward_dropout": (c_int, [c_int, c_vp, c_vp, c_vp, c_vp, c_int, ctypes.POINTER(Dropout), c_vp, c_size,

@@ -17,9 +17,11 @@ recomputation of the block's math on the GPU:
   ^T swaps the two pair axes. Operands go to the kernel as fp16 planes scaled by their
   own max-abs, so gradients of any magnitude keep 11 significant bits.
 * Triangle attention (triangle_attention.py:100-143, primitives.py:114-178): the
-  attention is recomputed and differentiated in chunks of rows i with PyTorch ops,
-  so that at most one chunk's [rows, H, N, N] scores exist at a time. This part is not
-  yet a native kernel.
+  LayerNorm, the projections, the gate and the triangle bias are recomputed with PyTorch
+  ops; the attention core between them runs forward and backward on the library's
+  tensor-core kernels (``gtk_attn_core_forward`` / ``gtk_attn_core_backward``), which never
+  form the [B, N, H, N, N] scores: dq, dk, dv and the triangle bias's gradient come
+  straight from the kernels.
 * Pair transition (pair_transform.py:78-84): recomputed and differentiated with
   PyTorch ops.
 
@@ -112,71 +114,60 @@ def trimul_recompute(z: Tensor, mask: Optional[Tensor], p: Dict[str, Tensor], ou
     return _linear(x, p, "linear_z") * torch.sigmoid(_linear(zn, p, "linear_g"))
 
 
-def _triatt_rows(xn: Tensor, mask: Tensor, tri: Tensor, p: Dict[str, Tensor], heads: int, inf: float,
-                 r0: int, r1: int) -> Tensor:
-    """Rows [r0, r1) of the gated attention (primitives.py:134-176) in the problem frame."""
-    B, _, N, _ = xn.shape
-    hd = p["mha.linear_q.weight"].shape[0]
-    d = hd // heads
-    xs = xn[:, r0:r1]
-    R = xs.shape[1]
-    q = _linear(xs, p, "mha.linear_q").view(B, R, N, heads, d).transpose(-2, -3)
-    k = _linear(xs, p, "mha.linear_k").view(B, R, N, heads, d).transpose(-2, -3)
-    v = _linear(xs, p, "mha.linear_v").view(B, R, N, heads, d).transpose(-2, -3)
-    # explicit scores: the memory-efficient scaled_dot_product_attention returned wrong
-    # bias gradients for some shapes (ending node, N = 67, B = 2), and one fused baddbmm
-    # for the scale and both additive terms measured slower than these separate passes
-    s = torch.matmul(q, k.transpose(-1, -2)) * (d ** -0.5)
-    s = s + (inf * (mask[:, r0:r1] - 1.0))[:, :, None, None, :] + tri[:, None]
-    o = torch.matmul(torch.softmax(s, dim=-1), v).transpose(-2, -3).reshape(B, R, N, hd)
-    o = o * torch.sigmoid(_linear(xs, p, "mha.linear_g"))
-    return _linear(o, p, "mha.linear_o")
+class _AttnCore(torch.autograd.Function):
+    """The attention core o = softmax(q k^T / sqrt(d) + inf (mask - 1) + tri) v on the
+    library's kernels, with their backward. Keeps the fp16 operand planes of the forward
+    (half the bytes of q, k, v) for the backward."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, tri, mask, heads, inf):
+        o, stats, pk = ops.attn_core_forward(q, k, v, tri, mask, heads, inf)
+        ctx.save_for_backward(pk.q, pk.k, pk.v, pk.tri, mask, stats, o)
+        ctx.dims, ctx.inf = (pk.B, pk.N, pk.heads, pk.head_dim), inf
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        qh, kh, vh, th, mask, stats, o = ctx.saved_tensors
+        pk = ops.AttnCorePacked(qh, kh, vh, th, *ctx.dims)
+        dq, dk, dv, dtri = ops.attn_core_backward(pk, mask, stats, o, do, ctx.inf)
+        return dq, dk, dv, dtri, None, None, None
+
+
+def _native_attn_core(q: Tensor, k: Tensor, v: Tensor, tri: Tensor, mask: Optional[Tensor], heads: int,
+                      inf: float) -> Tensor:
+    return _AttnCore.apply(q, k, v, tri, mask, heads, inf)
+
+
+# q, k, v [B, N(i), N(j), H*d], tri [B, H, N(j), N(k)], mask [B, N(i), N(k)] or None -> o like q
+# (module-level name, so that tests on the CPU can put a PyTorch version in its place)
+_attn_core = _native_attn_core
 
 
 def _triatt_shared(z: Tensor, mask: Optional[Tensor], p: Dict[str, Tensor], starting: bool):
     """Row-independent part (triangle_attention.py:106-129): orientation, LayerNorm, the
-    triangle bias [B, H, N, N] shared by every row."""
-    x, m = z, _mask_or_ones(z, mask)
+    triangle bias [B, H, N, N] shared by every row; the mask in the block's frame (or None)."""
+    x, m = z, mask
     if not starting:
-        x, m = x.transpose(-2, -3), m.transpose(-1, -2)
+        x = x.transpose(-2, -3)
+        m = None if m is None else m.transpose(-1, -2)
     xn = F.layer_norm(x, (x.shape[-1],), p["layer_norm.weight"], p["layer_norm.bias"], LN_EPS)
     tri = _linear(xn, p, "linear").permute(0, 3, 1, 2)
     return xn, m, tri
 
 
-def triatt_backward(z: Tensor, mask: Optional[Tensor], p: Dict[str, Tensor], starting: bool, heads: int,
-                    inf: float, dU: Tensor, wanted: Sequence[Tensor], chunk_rows: int) -> List[Optional[Tensor]]:
-    """Gradients of <update(z), dU> with respect to ``wanted`` (leaves among z and p),
-    evaluating the attention in chunks of ``chunk_rows`` rows of the problem frame. Each
-    chunk builds (and frees) its own graph from the leaves, so the parameters' fp32 casts
-    are redone per chunk; the per-chunk gradients accumulate in fp32."""
-    xn, m, tri = _triatt_shared(z, mask, _fp32(p), starting)
-    g = dU if starting else dU.transpose(-2, -3)
-    N = xn.shape[1]
-    xn_d, tri_d = xn.detach().requires_grad_(True), tri.detach().requires_grad_(True)
-    row_params = [t for t in wanted if t is not z and t.requires_grad]
-    dxn = torch.zeros_like(xn)
-    dtri = torch.zeros_like(tri)
-    dparams = [torch.zeros_like(t, dtype=torch.float32) for t in row_params]
-    for r0 in range(0, N, chunk_rows):
-        r1 = min(N, r0 + chunk_rows)
-        out = _triatt_rows(xn_d, m, tri_d, _fp32(p), heads, inf, r0, r1)
-        got = torch.autograd.grad(out, [xn_d, tri_d] + row_params, g[:, r0:r1], allow_unused=True)
-        dxn += got[0]
-        dtri += got[1]
-        for acc, gr in zip(dparams, got[2:]):
-            if gr is not None:
-                acc += gr
-    shared = torch.autograd.grad([xn, tri], wanted, [dxn, dtri], allow_unused=True)
-    extra = dict(zip([id(t) for t in row_params], dparams))
-    res: List[Optional[Tensor]] = []
-    for t, gs in zip(wanted, shared):
-        ge = extra.get(id(t))
-        if ge is None:
-            res.append(gs)
-        else:
-            res.append((ge if gs is None else ge + gs.float()).to(t.dtype))
-    return res
+def triatt_recompute(z: Tensor, mask: Optional[Tensor], p: Dict[str, Tensor], starting: bool, heads: int,
+                     inf: float) -> Tensor:
+    """The update of the triangle attention block (triangle_attention.py:100-143), fp32, with
+    the attention core on the library's kernels."""
+    p = _fp32(p)
+    xn, m, tri = _triatt_shared(z, mask, p, starting)
+    q, k, v = (_linear(xn, p, f"mha.linear_{n}").contiguous() for n in "qkv")
+    m = None if m is None else m.float().contiguous()
+    o = _attn_core(q, k, v, tri.contiguous(), m, heads, inf)
+    o = o * torch.sigmoid(_linear(xn, p, "mha.linear_g"))
+    out = _linear(o, p, "mha.linear_o")
+    return out if starting else out.transpose(-2, -3)
 
 
 def transition_recompute(z: Tensor, p: Dict[str, Tensor]) -> Tensor:
@@ -222,9 +213,9 @@ class TriMulFn(torch.autograd.Function):
 
 class TriAttFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, z, mask, packed, starting, inf, heads, chunk_rows, *params):
+    def forward(ctx, z, mask, packed, starting, inf, heads, *params):
         ctx.save_for_backward(z, mask, *params)
-        ctx.starting, ctx.inf, ctx.heads, ctx.chunk_rows = starting, inf, heads, chunk_rows
+        ctx.starting, ctx.inf, ctx.heads = starting, inf, heads
         return ops.triatt_forward(z, mask, packed, starting, inf=inf)
 
     @staticmethod
@@ -232,12 +223,9 @@ class TriAttFn(torch.autograd.Function):
         z, mask, *params = ctx.saved_tensors
         with torch.enable_grad():
             zl, pl = _leaves(z.float(), params)
-            wanted = [t for t in [zl] + pl if t.requires_grad]
-            got = triatt_backward(zl, mask, dict(zip(ops.TRIATT_KEYS, pl)), ctx.starting, ctx.heads, ctx.inf,
-                                  dU.float(), wanted, ctx.chunk_rows) if wanted else []
-            it = iter(got)
-            g = [next(it) if t.requires_grad else None for t in [zl] + pl]
-        return (g[0], None, None, None, None, None, None, *g[1:])
+            out = triatt_recompute(zl, mask, dict(zip(ops.TRIATT_KEYS, pl)), ctx.starting, ctx.heads, ctx.inf)
+            g = _grads(out, zl, pl, dU.float())
+        return (g[0], None, None, None, None, None, *g[1:])
 
 
 class TransitionFn(torch.autograd.Function):
@@ -254,13 +242,6 @@ class TransitionFn(torch.autograd.Function):
             out = transition_recompute(zl, dict(zip(ops.TRANSITION_KEYS, pl)))
             g = _grads(out, zl, pl, dU.float())
         return (g[0], None, *g[1:])
-
-
-def attention_chunk_rows(N: int, heads: int, B: int = 1, budget_bytes: int = 2 << 30) -> int:
-    """Rows per recompute chunk so that one chunk's fp32 scores (about six live copies of
-    [B, rows, H, N, N] during its backward) stay within ``budget_bytes``."""
-    per_row = 6 * B * heads * N * N * 4
-    return max(1, min(N, budget_bytes // max(per_row, 1)))
 
 
 class PairEmbedFn(torch.autograd.Function):

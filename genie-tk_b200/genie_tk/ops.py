@@ -10,6 +10,7 @@ unsupported shape or a missing library raises.
 from __future__ import annotations
 
 import ctypes
+import math
 from dataclasses import dataclass
 from typing import Dict, Optional
 
@@ -493,30 +494,80 @@ def _core_args(q, k, v, tri, mask, heads):
     return B, N, hd // heads
 
 
+@dataclass
+class AttnCorePacked:
+    """The attention core's fp16 operand planes (gtk_attn_core_pack / _pack_bias)."""
+    q: torch.Tensor
+    k: torch.Tensor
+    v: torch.Tensor
+    tri: torch.Tensor
+    B: int
+    N: int
+    heads: int
+    head_dim: int
+
+
+def attn_core_pack(x: torch.Tensor, heads: int, scale: float = 1.0) -> torch.Tensor:
+    """fp32 [B, N, N, heads * d] -> the fp16 plane [B, N, heads, N, Dp] (times ``scale``)."""
+    lib = _lib.load()
+    B, N, _, hd = x.shape
+    d = hd // heads
+    nbytes = lib.gtk_attn_core_packed_bytes(B, N, heads, d)
+    if nbytes == 0:
+        raise ValueError("attention core: head_dim must be 1 .. 64")
+    out = torch.empty(nbytes // 2, dtype=torch.float16, device=x.device)
+    _lib.check(lib.gtk_attn_core_pack(_ptr(x), B, N, heads, d, float(scale), _ptr(out), _stream(x.device)),
+               "gtk_attn_core_pack")
+    return out
+
+
+def attn_core_pack_bias(tri: torch.Tensor) -> torch.Tensor:
+    """fp32 tri [B, H, N, N] -> the fp16 plane [B, H, N, Np]."""
+    lib = _lib.load()
+    B, H, N, _ = tri.shape
+    out = torch.empty(lib.gtk_attn_core_bias_bytes(B, N, H) // 2, dtype=torch.float16, device=tri.device)
+    _lib.check(lib.gtk_attn_core_pack_bias(_ptr(tri), B, N, H, _ptr(out), _stream(tri.device)),
+               "gtk_attn_core_pack_bias")
+    return out
+
+
 def attn_core_forward(q, k, v, tri, mask, heads: int, inf: float = 1e9):
-    """o = softmax(q k^T / sqrt(d) + inf (mask - 1) + tri) v per (b, i, h) and the softmax
-    statistics [B, N, heads, N, 2], without forming the scores (fp32)."""
+    """o = softmax(q k^T / sqrt(d) + inf (mask - 1) + tri) v per (b, i, h), the softmax
+    statistics [B, N, heads, N, 2] and the packed operands (for the backward), without
+    forming the scores. q, k, v fp32 [B, N, N, heads * d], tri fp32 [B, heads, N, N]."""
     lib = _lib.load()
     B, N, d = _core_args(q, k, v, tri, mask, heads)
+    pk = AttnCorePacked(attn_core_pack(q, heads), attn_core_pack(k, heads), attn_core_pack(v, heads),
+                        attn_core_pack_bias(tri), B, N, heads, d)
     o = torch.empty_like(q)
     stats = torch.empty(B, N, heads, N, 2, dtype=torch.float32, device=q.device)
-    _lib.check(lib.gtk_attn_core_forward(_ptr(q), _ptr(k), _ptr(v), _ptr(tri), _ptr(mask), B, N, heads, d,
-                                         float(inf), _ptr(o), _ptr(stats), _stream(q.device)),
+    _lib.check(lib.gtk_attn_core_forward(_ptr(pk.q), _ptr(pk.k), _ptr(pk.v), _ptr(pk.tri), _ptr(mask), B, N, heads,
+                                         d, float(inf), _ptr(o), _ptr(stats), _stream(q.device)),
                "gtk_attn_core_forward")
-    return o, stats
+    return o, stats, pk
 
 
-def attn_core_backward(q, k, v, tri, mask, stats, o, do, heads: int, inf: float = 1e9):
-    """(dq, dk, dv, dtri) of the attention core for the output gradient ``do``."""
+def attn_core_backward(pk: AttnCorePacked, mask, stats, o, do, inf: float = 1e9):
+    """(dq, dk, dv, dtri) of the attention core for the output gradient ``do``.
+
+    ``do`` enters its fp16 plane times a power of two that brings its largest element into
+    [0.5, 1), so gradients of any magnitude keep 11 bits."""
     lib = _lib.load()
-    B, N, d = _core_args(q, k, v, tri, mask, heads)
+    B, N, H, d = pk.B, pk.N, pk.heads, pk.head_dim
     do = do.float().contiguous()
-    dsum = (do * o).view(B, N, N, heads, d).sum(-1).permute(0, 1, 3, 2).contiguous()  # [B, N(i), H, N(j)]
-    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-    dtri = torch.empty_like(tri)
-    _lib.check(lib.gtk_attn_core_backward(_ptr(q), _ptr(k), _ptr(v), _ptr(tri), _ptr(mask), _ptr(stats), _ptr(do),
-                                          _ptr(dsum), B, N, heads, d, float(inf), _ptr(dq), _ptr(dk), _ptr(dv),
-                                          _ptr(dtri), _stream(q.device)), "gtk_attn_core_backward")
+    dq, dk, dv = (torch.empty(B, N, N, H * d, dtype=torch.float32, device=do.device) for _ in range(3))
+    dtri = torch.empty(B, H, N, N, dtype=torch.float32, device=do.device)
+    amax = float(do.abs().max())
+    if amax == 0.0:
+        return dq.zero_(), dk.zero_(), dv.zero_(), dtri.zero_()
+    if not math.isfinite(amax):
+        raise ValueError("attention core backward: the output gradient is not finite")
+    scale = math.ldexp(1.0, -math.frexp(amax)[1])  # amax * scale in [0.5, 1)
+    dsum = (do * o).view(B, N, N, H, d).sum(-1).permute(0, 1, 3, 2).contiguous()  # [B, N(i), H, N(j)]
+    doh = attn_core_pack(do, H, scale)
+    _lib.check(lib.gtk_attn_core_backward(_ptr(pk.q), _ptr(pk.k), _ptr(pk.v), _ptr(pk.tri), _ptr(mask), _ptr(stats),
+                                          _ptr(doh), _ptr(dsum), scale, B, N, H, d, float(inf), _ptr(dq), _ptr(dk),
+                                          _ptr(dv), _ptr(dtri), _stream(do.device)), "gtk_attn_core_backward")
     return dq, dk, dv, dtri
 
 
@@ -582,3 +633,138 @@ def pair_embed(s: torch.Tensor, mask: Optional[torch.Tensor], weight: torch.Tens
     _lib.check(lib.gtk_pair_embed(_ptr(sf), _ptr(mf), _ptr(wf), _ptr(bf), _ptr(out), _ptr(pm), _ptr(ws), ws.numel(),
                                   B, N, rows, int(row0), c_s, c_p, _stream(s.device)), "gtk_pair_embed")
     return out, pm
+
+
+# --------------------------------------------------------------------------------------
+# Linear layers and the generic attention core of the reference's Attention module
+# --------------------------------------------------------------------------------------
+
+def _rows_2d(x: torch.Tensor, name: str) -> torch.Tensor:
+    _require_cuda(x, name, torch.float32)
+    return x.reshape(-1, x.shape[-1]).contiguous()
+
+
+def _weight(weight: torch.Tensor, d_in: int) -> torch.Tensor:
+    _require_cuda(weight, "weight", torch.float32)
+    if weight.dim() != 2 or weight.shape[1] != d_in:
+        raise ValueError(f"weight must be [D_out, {d_in}], got {tuple(weight.shape)}")
+    return weight.contiguous()
+
+
+def _bias(bias: Optional[torch.Tensor], d_out: int) -> Optional[torch.Tensor]:
+    if bias is None:
+        return None
+    _require_cuda(bias, "bias", torch.float32)
+    if bias.numel() != d_out:
+        raise ValueError(f"bias must have {d_out} elements")
+    return bias.contiguous()
+
+
+def layernorm_linear(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, weight: torch.Tensor,
+                     bias: Optional[torch.Tensor] = None, eps: float = 1e-5) -> torch.Tensor:
+    """LayerNorm(x) weight^T + bias in one kernel (gtk_layernorm_linear); weight [D_out, D_in]."""
+    lib = _lib.load()
+    x2 = _rows_2d(x, "x")
+    D_in = x2.shape[1]
+    w = _weight(weight, D_in)
+    b = _bias(bias, w.shape[0])
+    for t, n in ((gamma, "gamma"), (beta, "beta")):
+        _require_cuda(t, n, torch.float32)
+        if t.numel() != D_in:
+            raise ValueError(f"{n} must have {D_in} elements")
+    out = torch.empty(x2.shape[0], w.shape[0], dtype=torch.float32, device=x.device)
+    _lib.check(lib.gtk_layernorm_linear(_ptr(x2), _ptr(gamma.contiguous()), _ptr(beta.contiguous()), _ptr(w), _ptr(b),
+                                        _ptr(out), x2.shape[0], D_in, w.shape[0], float(eps), _stream(x.device)),
+               "gtk_layernorm_linear")
+    return out.view(*x.shape[:-1], w.shape[0])
+
+
+def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None,
+           gate: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """(x * sigmoid(gate)) weight^T + bias (gtk_linear); weight [D_out, D_in], gate like x."""
+    lib = _lib.load()
+    x2 = _rows_2d(x, "x")
+    D_in = x2.shape[1]
+    w = _weight(weight, D_in)
+    b = _bias(bias, w.shape[0])
+    g = None
+    if gate is not None:
+        if gate.shape != x.shape:
+            raise ValueError("gate must have x's shape")
+        g = _rows_2d(gate, "gate")
+    out = torch.empty(x2.shape[0], w.shape[0], dtype=torch.float32, device=x.device)
+    _lib.check(lib.gtk_linear(_ptr(x2), _ptr(g), _ptr(w), _ptr(b), _ptr(out), x2.shape[0], D_in, w.shape[0],
+                              _stream(x.device)), "gtk_linear")
+    return out.view(*x.shape[:-1], w.shape[0])
+
+
+def _merged_stride(shape, strides):
+    """The one stride of axes that index memory as a single merged axis, or None."""
+    dims = [(n, st) for n, st in zip(shape, strides) if n != 1]
+    for (_, s_outer), (n_inner, s_inner) in zip(dims, dims[1:]):
+        if s_outer != s_inner * n_inner:
+            return None
+    return dims[-1][1] if dims else 0
+
+
+def _bias_layout(biases, batch: tuple, heads: int, Q: int, K: int):
+    """Biases broadcastable to [*batch, heads, Q, K] as tensors with five element strides
+    over (l0, l1, h, q, k), for one split of the batch axes into two levels L0 x L1:
+    broadcast axes read with stride 0, in place. A bias whose batch axes fit no common split
+    is made contiguous first."""
+    full = tuple(batch) + (heads, Q, K)
+    exp = []
+    for b in biases:
+        if b.dim() > len(full):
+            raise ValueError(f"bias of shape {tuple(b.shape)} does not broadcast to {full}")
+        exp.append(b.float().expand(*full))
+    nb = len(batch)
+
+    def split_ok(p, tensors):
+        return all(_merged_stride(batch[:p], t.stride()[:p]) is not None and
+                   _merged_stride(batch[p:], t.stride()[p:nb]) is not None for t in tensors)
+
+    split = next((p for p in range(nb + 1) if split_ok(p, exp)), None)
+    if split is None:
+        exp = [t if split_ok(0, [t]) else t.contiguous() for t in exp]
+        split = 0
+    L0 = math.prod(batch[:split])
+    L1 = math.prod(batch[split:])
+    out = []
+    for t in exp:
+        st = t.stride()
+        strides = torch.tensor([_merged_stride(batch[:split], st[:split]),
+                                _merged_stride(batch[split:], st[split:nb]), st[nb], st[nb + 1], st[nb + 2]],
+                               dtype=torch.int64)
+        out.append((t, strides))
+    return out, L0, L1
+
+
+def mha_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, scale: float,
+                biases: Optional[list] = None) -> torch.Tensor:
+    """o[*, Q, H*d] = softmax(scale q k^T + sum(biases)) v per head (gtk_mha_forward).
+
+    q [*, Q, H*d], k, v [*, K, H*d] fp32; each bias broadcastable to [*, H, Q, K] (at most
+    two; more are summed first)."""
+    lib = _lib.load()
+    for t, n in ((q, "q"), (k, "k"), (v, "v")):
+        _require_cuda(t, n, torch.float32)
+    batch = tuple(q.shape[:-2])
+    Q, hd = q.shape[-2], q.shape[-1]
+    K = k.shape[-2]
+    if tuple(k.shape[:-2]) != batch or k.shape != v.shape or k.shape[-1] != hd or hd % heads:
+        raise ValueError("q [*, Q, H*d], k and v [*, K, H*d] with one batch shape")
+    d = hd // heads
+    biases = [b.to(q.device) for b in (biases or []) if b is not None]
+    if len(biases) > 2:
+        biases = [sum(biases[1:], biases[0])]
+    L = math.prod(batch)
+    q3, k3, v3 = (t.reshape(L, -1, hd).contiguous() for t in (q, k, v))
+    o = torch.empty(L, Q, hd, dtype=torch.float32, device=q.device)
+    layout, L0, L1 = _bias_layout(biases, batch, heads, Q, K)
+    layout += [(None, None)] * (2 - len(layout))
+    (b0, s0), (b1, s1) = layout
+    sp = [None if st is None else ctypes.c_void_p(st.data_ptr()) for st in (s0, s1)]
+    _lib.check(lib.gtk_mha_forward(_ptr(q3), _ptr(k3), _ptr(v3), _ptr(b0), sp[0], _ptr(b1), sp[1], L0, L1, Q, K,
+                                   heads, d, float(scale), _ptr(o), _stream(q.device)), "gtk_mha_forward")
+    return o.view(*batch, Q, hd)

@@ -59,15 +59,14 @@ class TriangleAttention(nn.Module):
             raise RuntimeError("genie_tk (B200): TriangleAttention runs on CUDA tensors only")
         packed = self.packed_weights(x.device)
         if autograd.needs_grad(x, self):
-            # training: forward on the kernels, backward through a row-chunked recomputation
+            # training: forward on the kernels, backward through a recomputation whose
+            # attention core runs forward and backward on the tensor-core kernels
             if out is not None or dropout is not None:
                 raise RuntimeError("genie_tk (B200): out= and dropout= are inference-only; under autograd "
                                    "use the returned update (and nn.Dropout) instead")
             sd = dict(self.named_parameters())
-            N = x.shape[1]
             upd = autograd.TriAttFn.apply(x.float().contiguous(), mask, packed, self.starting, float(self.inf),
-                                          self.no_heads, autograd.attention_chunk_rows(N, self.no_heads, x.shape[0]),
-                                          *[sd[k] for k in ops.TRIATT_KEYS])
+                                          self.no_heads, *[sd[k] for k in ops.TRIATT_KEYS])
             res = x.float() + upd if add_residual else upd
             return res if res.dtype == x.dtype else res.to(x.dtype)
         if out is None and not add_residual and dropout is None:

@@ -386,32 +386,79 @@ GTK_API int gtk_triatt_forward_dropout(int starting, const float* z, const float
  * key k, head h of head_dim d:
  *   s = q[i,j,h] . k[i,k,h] / sqrt(d) + inf (mask[i,k] - 1) + tri[h,j,k],
  *   o[i,j,h] = sum_k softmax_k(s) v[i,k,h].
- * q, k, v, o and the gradients dq, dk, dv, dO: fp32 [B, N(i), N(j), heads * head_dim];
- * tri, dtri: fp32 [B, heads, N(j), N(k)]; mask: fp32 [B, N(i), N(k)] in the block's frame,
- * or NULL. Neither entry point forms the [B, N, heads, N, N] scores (fp32 CUDA-core
- * kernels; head_dim <= 64). All pointers 4-byte aligned, `stats` 8-byte aligned.
+ * The kernels never form the [B, N, heads, N, N] scores: 64-row tiles of fp16 operand planes
+ * are copied into shared memory (double buffered) and every product runs on the tensor cores
+ * (mma.sync m16n8k16, fp32 accumulation); scale, bias, mask and softmax are fp32.
+ * Operand planes (written by the two pack entry points, 16-byte aligned):
+ *   q, k, v, dO: fp16 [B, N(i), heads, N(j), Dp], Dp = head_dim rounded up to 16, 32 or 64
+ *                (zero-padded), gtk_attn_core_packed_bytes(B, N, heads, head_dim) bytes each;
+ *   tri:         fp16 [B, heads, N(j), Np], Np = N rounded up to a multiple of 8,
+ *                gtk_attn_core_bias_bytes(B, N, heads) bytes.
+ * mask: fp32 [B, N(i), N(k)] in the block's frame, or NULL. o, dq, dk, dv: fp32
+ * [B, N(i), N(j), heads * head_dim] (the projections' layout); dtri fp32 [B, heads, N, N];
+ * stats 8-byte aligned. head_dim <= 64.
  * ------------------------------------------------------------------------------- */
+GTK_API size_t gtk_attn_core_packed_bytes(int64_t B, int64_t N, int heads, int head_dim);
+GTK_API size_t gtk_attn_core_bias_bytes(int64_t B, int64_t N, int heads);
+/* fp32 [B, N, N, heads * head_dim] -> an fp16 operand plane, times `scale`. */
+GTK_API int gtk_attn_core_pack(const float* src, int64_t B, int64_t N, int heads, int head_dim, float scale,
+                               void* dst, void* stream);
+/* fp32 tri [B, heads, N, N] -> its fp16 plane. */
+GTK_API int gtk_attn_core_pack_bias(const float* tri, int64_t B, int64_t N, int heads, void* dst, void* stream);
 
 /* o and the softmax statistics: stats[b][i][h][j] = (max of the base-2 scores, 1 / sum of
- * 2^(score - max)), two floats. */
-GTK_API int gtk_attn_core_forward(const float* q, const float* k, const float* v, const float* tri,
+ * 2^(score - max)), two floats. q, k, v packed with scale 1. */
+GTK_API int gtk_attn_core_forward(const void* q, const void* k, const void* v, const void* tri,
                                   const float* mask, int64_t B, int64_t N, int heads, int head_dim, float inf,
                                   float* o, float* stats, void* stream);
-/* dq, dk, dv and dtri from dO, the forward's stats and dsum[b][i][h][j] = sum_e dO o
- * (over the head's d channels). dtri sums the score gradients over the rows i. */
-GTK_API int gtk_attn_core_backward(const float* q, const float* k, const float* v, const float* tri,
-                                   const float* mask, const float* stats, const float* dO, const float* dsum,
-                                   int64_t B, int64_t N, int heads, int head_dim, float inf, float* dq, float* dk,
-                                   float* dv, float* dtri, void* stream);
+/* dq, dk, dv and dtri from the output gradient, the forward's stats and
+ * dsum[b][i][h][j] = sum_e dO o (over the head's d channels, fp32, unscaled). dO is packed
+ * times dO_scale (> 0; a power of two near 1 / max|dO| keeps gradients of any magnitude at
+ * 11 bits); the results are divided by it again. dtri sums the score gradients over the rows i. */
+GTK_API int gtk_attn_core_backward(const void* q, const void* k, const void* v, const void* tri,
+                                   const float* mask, const float* stats, const void* dO, const float* dsum,
+                                   float dO_scale, int64_t B, int64_t N, int heads, int head_dim, float inf,
+                                   float* dq, float* dk, float* dv, float* dtri, void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * The generic multi-head attention core of the reference's `Attention` module
+ * (src/genie_tk/primitives.py:114-178, between its projections and its gate):
+ *   o[l, q, h, :] = sum_k softmax_k(scale q[l,q,h] . k[l,k,h] + bias0 + bias1) v[l, k, h, :]
+ * q, o fp32 [L0 * L1, Q, heads * head_dim]; k, v fp32 [L0 * L1, K, heads * head_dim];
+ * head_dim <= 64. Each bias is optional (NULL) and read through five element strides
+ * strides[0..4] over (l0, l1, h, q, k), l = l0 * L1 + l1: a zero stride broadcasts, so the
+ * reference's mask bias [*, 1, 1, K] and pair bias [*, H, Q, K] are read in place. A row
+ * whose scores are all -inf gives NaN, as softmax does. Same arithmetic as the core above.
+ * ------------------------------------------------------------------------------- */
+GTK_API int gtk_mha_forward(const float* q, const float* k, const float* v, const float* bias0,
+                            const int64_t* strides0, const float* bias1, const int64_t* strides1, int64_t L0,
+                            int64_t L1, int64_t Q, int64_t K, int heads, int head_dim, float scale, float* o,
+                            void* stream);
 
 /* ---------------------------------------------------------------------------------
  * LayerNorm over the last axis: the reference's `_C.layernorm(x, gamma, beta, eps)`
  * (kernels/bindings.cpp:93-95; host code kernels/fused_layernorm/layernorm.cu:17-44).
  * x, out fp32 [rows, D] (out may equal x); gamma, beta fp32 [D]; biased variance.
- * The Python `genie_tk._C.fused_layernorm_linear` is this plus one library GEMM.
  * ------------------------------------------------------------------------------- */
 GTK_API int gtk_layernorm(const float* x, const float* gamma, const float* beta, float* out, int64_t rows,
                           int64_t D, float eps, void* stream);
+
+/* The reference's `_C.fused_layernorm_linear(x, gamma, beta, weight, bias, eps)`
+ * (kernels/bindings.cpp:97-101; layernorm.cu:46-76): out = LayerNorm(x) weight^T + bias in
+ * one kernel -- each CTA normalises its 64 rows while loading them, so the normalised rows
+ * never reach memory. x fp32 [rows, D_in]; weight fp32 [D_out, D_in] (nn.Linear's layout:
+ * the reference's [D_in, D_out] operand transposed); bias fp32 [D_out] or NULL; out fp32
+ * [rows, D_out]; out must not alias x. fp32 CUDA-core arithmetic. */
+GTK_API int gtk_layernorm_linear(const float* x, const float* gamma, const float* beta, const float* weight,
+                                 const float* bias, float* out, int64_t rows, int64_t D_in, int64_t D_out, float eps,
+                                 void* stream);
+
+/* out = (x * sigmoid(gate) if gate else x) weight^T + bias: the projections of the
+ * reference's Linear / Attention modules (primitives.py:43-62, :124-178). x, gate fp32
+ * [rows, D_in] (gate may be NULL); weight fp32 [D_out, D_in]; bias fp32 [D_out] or NULL;
+ * out fp32 [rows, D_out], aliasing neither x nor gate. fp32 CUDA-core arithmetic. */
+GTK_API int gtk_linear(const float* x, const float* gate, const float* weight, const float* bias, float* out,
+                       int64_t rows, int64_t D_in, int64_t D_out, void* stream);
 
 #ifdef __cplusplus
 }

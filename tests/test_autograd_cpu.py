@@ -1,8 +1,8 @@
 """CPU checks of the training support's host logic (genie_tk.autograd): the differentiable
-recomputations against the oracle and its autograd, the row-chunked attention backward,
-and the contraction-gradient identities of the multiplicative update. The library's
-contraction kernel is replaced here by an einsum with the same contract; the kernel
-itself is covered by tests/test_gpu_autograd.py."""
+recomputations against the oracle and its autograd, and the contraction-gradient
+identities of the multiplicative update. The library's contraction kernel and attention
+core are replaced here by PyTorch functions with the same contracts; the kernels
+themselves are covered by tests/test_gpu_autograd.py."""
 
 import pytest
 import torch
@@ -25,10 +25,23 @@ def _einsum_contract(p, tp, q, tq, outgoing):
     return torch.einsum(eq, p, q)
 
 
+def _torch_attn_core(q, k, v, tri, mask, heads, inf):
+    """The contract of autograd._attn_core with explicit scores: q, k, v [B, N(i), N(j), H*d],
+    tri [B, H, N(j), N(k)], mask [B, N(i), N(k)] or None."""
+    B, N, _, hd = q.shape
+    d = hd // heads
+    qh, kh, vh = (t.view(B, N, N, heads, d).transpose(-2, -3) for t in (q, k, v))  # [B, i, H, j, d]
+    s = torch.matmul(qh, kh.transpose(-1, -2)) * d ** -0.5 + tri[:, None]
+    if mask is not None:
+        s = s + (inf * (mask - 1.0))[:, :, None, None, :]
+    return torch.matmul(torch.softmax(s, -1), vh).transpose(-2, -3).reshape(B, N, N, hd)
+
+
 @pytest.fixture
 def AG(monkeypatch):
     from genie_tk import autograd
     monkeypatch.setattr(autograd, "_contract", _einsum_contract)
+    monkeypatch.setattr(autograd, "_attn_core", _torch_attn_core)
     return autograd
 
 
@@ -72,18 +85,22 @@ def test_trimul_recompute_and_gradients_match_oracle(AG, outgoing):
 
 
 @pytest.mark.parametrize("starting", [True, False])
-@pytest.mark.parametrize("chunk", [11, 4, 1])
-def test_chunked_attention_backward_matches_oracle_autograd(AG, starting, chunk):
+@pytest.mark.parametrize("c_in,c,H", [(128, 128, 4), (64, 32, 4)])
+def test_attention_recompute_and_gradients_match_oracle(AG, starting, c_in, c, H):
+    """The recomputation around the attention core (orientation, LayerNorm, projections,
+    triangle bias, gate, output projection) and its gradients, against the oracle."""
     gen, z, mask, w = _case(3 + int(starting))
-    p = O.make_triatt_params(128, 128, 4, gen, gate_bias=1.0)
+    z, w = z[..., :c_in].contiguous(), w[..., :c_in].contiguous()
+    p = O.make_triatt_params(c_in, c, H, gen, gate_bias=1.0)
     zl = z.clone().requires_grad_(True)
     pl = {k: v.clone().requires_grad_(True) for k, v in p.items()}
-    wanted = [zl] + list(pl.values())
-    got = AG.triatt_backward(zl, mask, pl, starting, 4, 1e9, w, wanted, chunk)
+    out = AG.triatt_recompute(zl, mask, pl, starting, H, 1e9)
+    got = torch.autograd.grad((out * w).sum(), [zl] + list(pl.values()))
     z2 = z.clone().requires_grad_(True)
     p2 = {k: v.clone().requires_grad_(True) for k, v in p.items()}
-    ref = O.triatt_forward(z2, mask, p2, starting, no_heads=4)
+    ref = O.triatt_forward(z2, mask, p2, starting, no_heads=H)
     g2 = torch.autograd.grad((ref * w).sum(), [z2] + list(p2.values()))
+    assert float((out - ref).detach().abs().max()) < 1e-4
     for name, a, b in zip(["z"] + list(p), got, g2):
         assert a is not None, name
         assert _rel(a, b) < 1e-4, (name, _rel(a, b))
@@ -94,13 +111,6 @@ def test_transition_recompute_matches_oracle(AG):
     p = O.make_transition_params(128, 4, gen)
     out = AG.transition_recompute(z, p)
     assert float((out - O.transition_forward(z, p)).abs().max()) < 1e-4
-
-
-def test_chunk_rows_bound_the_score_memory(AG):
-    assert AG.attention_chunk_rows(1024, 4) == (2 << 30) // (6 * 4 * 1024 * 1024 * 4)
-    assert AG.attention_chunk_rows(1024, 4, B=4) == (2 << 30) // (6 * 4 * 4 * 1024 * 1024 * 4)
-    assert AG.attention_chunk_rows(16, 4) == 16
-    assert AG.attention_chunk_rows(100000, 4) == 1
 
 
 def test_needs_grad_follows_autograd_state(AG):
@@ -135,12 +145,11 @@ def test_half_precision_parameters_get_gradients_in_their_dtype(AG, dtype):
             leaves = list(params.values())
             if kind == "trimul":
                 out = AG.trimul_recompute(z, mask, params, True)
-                grads.append(torch.autograd.grad((out * w).sum(), leaves))
             elif kind == "transition":
                 out = AG.transition_recompute(z, params)
-                grads.append(torch.autograd.grad((out * w).sum(), leaves))
             else:
-                grads.append(AG.triatt_backward(z, mask, params, True, 4, 1e9, w, leaves, 4))
+                out = AG.triatt_recompute(z, mask, params, True, 4, 1e9)
+            grads.append(torch.autograd.grad((out * w).sum(), leaves))
         for gh, gf, t in zip(grads[0], grads[1], half.values()):
             assert gh.dtype == t.dtype, (kind, gh.dtype)
             assert _rel(gh.float(), gf) < 1e-2, (kind, _rel(gh.float(), gf))

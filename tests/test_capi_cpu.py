@@ -139,6 +139,32 @@ def test_invalid_arguments_are_rejected(lib):
     assert rc == -1
 
 
+def test_attention_and_linear_entry_points_validate_before_touching_the_device(lib):
+    p = ctypes.c_void_p(1 << 20)
+    # head_dim beyond 64, then a zero output-gradient scale, then bad sizes
+    rc = lib.gtk_attn_core_forward(p, p, p, p, None, 1, 16, 2, 65, 1e9, p, p, None)
+    assert rc == L.GTK_ERR_UNSUPPORTED and b"head_dim" in lib.gtk_last_error_string()
+    rc = lib.gtk_attn_core_backward(p, p, p, p, None, p, p, p, 0.0, 1, 16, 4, 8, 1e9, p, p, p, p, None)
+    assert rc == L.GTK_ERR_INVALID_ARG and b"dO_scale" in lib.gtk_last_error_string()
+    assert lib.gtk_attn_core_packed_bytes(2, 10, 4, 8) == 2 * 10 * 4 * 10 * 16 * 2  # head_dim 8 pads to 16
+    assert lib.gtk_attn_core_packed_bytes(1, 10, 4, 65) == 0
+    assert lib.gtk_attn_core_bias_bytes(2, 10, 4) == 2 * 4 * 10 * 16 * 2  # N = 10 pads to 16
+    rc = lib.gtk_attn_core_pack(p, 1, 16, 4, 65, 1.0, p, None)
+    assert rc == L.GTK_ERR_INVALID_ARG
+    rc = lib.gtk_attn_core_pack(p, 1, 16, 4, 8, 1.0, ctypes.c_void_p((1 << 20) + 8), None)
+    assert rc == L.GTK_ERR_ALIGNMENT
+    rc = lib.gtk_mha_forward(p, p, p, None, None, None, None, 1, 1, 0, 4, 2, 8, 0.3, p, None)
+    assert rc == L.GTK_ERR_INVALID_ARG
+    rc = lib.gtk_mha_forward(p, p, p, p, None, None, None, 1, 1, 4, 4, 2, 8, 0.3, p, None)
+    assert rc == L.GTK_ERR_INVALID_ARG and b"strides" in lib.gtk_last_error_string()
+    rc = lib.gtk_linear(p, None, p, None, p, 0, 8, 8, None)
+    assert rc == L.GTK_ERR_INVALID_ARG
+    rc = lib.gtk_linear(p, None, p, None, p, 4, 8, 8, None)
+    assert rc == L.GTK_ERR_INVALID_ARG and b"alias" in lib.gtk_last_error_string()
+    rc = lib.gtk_layernorm_linear(p, p, p, p, None, ctypes.c_void_p(1 << 21), 4, 8, 8, -1.0, None)
+    assert rc == L.GTK_ERR_INVALID_ARG and b"eps" in lib.gtk_last_error_string()
+
+
 def test_transition_entry_points(lib):
     assert lib.gtk_transition_packed_bytes(128, 4) > 2 * 128 * 512 * 2
     assert lib.gtk_transition_workspace_bytes(2, 10, 128, 4) == 2 * 10 * 10 * 512 * 2

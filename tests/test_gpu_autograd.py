@@ -3,9 +3,10 @@ oracle's autograd (fp32, the reference math), the reference's own gradient-flow 
 (tests/test_triangle_mul.py:69-90, tests/test_triangle_attention.py:70-113: finite
 gradients under masks), and a training step of PairTransformLayer with dropout.
 
-The multiplicative update's backward contracts fp16 planes on the library's kernel, so
-its gradients are held to a relative L2 error of 1e-2; the other blocks differentiate an
-fp32 recomputation and are held to 1e-3. A whole layer's gradients are evaluated at the
+The multiplicative update's backward contracts fp16 planes on the library's kernel and the
+attention core runs forward and backward on fp16 tensor-core operands, so their gradients
+are held to a relative L2 error of 1e-2; the transition and the embedding differentiate an
+fp32 recomputation and are held to 1e-3 / 1e-4. A whole layer's gradients are evaluated at the
 activations of the kernels' forward (bf16/fp16 operands, max-abs 2e-2 from fp32 per block)
 rather than at the oracle's, and the five blocks compound that: 3e-2 there.
 """
@@ -108,29 +109,54 @@ def test_triatt_gradients_match_oracle(starting, N, B):
     assert_status_clean(dev)
     assert float((out - ref).detach().abs().max()) <= 2e-2
     for k, v in gr.items():
-        assert _rel(g[k], v) < 1e-3, (k, _rel(g[k], v))
+        assert _rel(g[k], v) < 1e-2, (k, _rel(g[k], v))
 
 
-@pytest.mark.parametrize("starting", [True, False])
-def test_triatt_chunked_backward_equals_one_chunk(starting):
+def _explicit_core(q, k, v, tri, mask, heads, inf=1e9):
+    """o = softmax(q k^T / sqrt(d) + inf (mask - 1) + tri) v with explicit fp32 scores."""
+    B, N, _, hd = q.shape
+    d = hd // heads
+    qh, kh, vh = (t.view(B, N, N, heads, d).transpose(-2, -3) for t in (q, k, v))
+    s = torch.matmul(qh, kh.transpose(-1, -2)) * d ** -0.5 + tri[:, None]
+    if mask is not None:
+        s = s + (inf * (mask - 1.0))[:, :, None, None, :]
+    return torch.matmul(torch.softmax(s, -1), vh).transpose(-2, -3).reshape(B, N, N, hd)
+
+
+@pytest.mark.parametrize("B,N,H,d,with_mask,gscale", [(1, 70, 4, 32, True, 1.0), (2, 37, 4, 8, True, 1e-6),
+                                                      (1, 130, 2, 64, False, 1.0), (1, 50, 3, 12, True, 3e4),
+                                                      (1, 1, 1, 5, False, 1.0)])
+def test_attention_core_kernels_match_explicit_scores(B, N, H, d, with_mask, gscale):
+    """gtk_attn_core_forward / _backward against explicit fp32 scores and their autograd:
+    ragged N (partial 64-row tiles, more than one tile, N = 1), head_dim 5 ... 64, fully
+    masked rows, and output gradients scaled far from 1 (the kernels rescale them)."""
     dev = require_gpu()
-    from genie_tk import autograd as AG
     from genie_tk import ops
-    gen = torch.Generator().manual_seed(9)
-    B, N = 1, 50
-    z = torch.randn(B, N, N, 128, generator=gen).to(dev)
-    mask = _masked(B, N, gen).to(dev)
-    w = torch.randn(B, N, N, 128, generator=gen).to(dev)
-    params = to_dev(O.make_triatt_params(128, 128, 4, gen, gate_bias=1.0), dev)
-    packed = ops.pack_triatt(params, dev, 4)
-    res = []
-    for chunk in (N, 7):
-        zz = z.clone().requires_grad_(True)
-        pl = [params[k].clone().requires_grad_(True) for k in ops.TRIATT_KEYS]
-        out = AG.TriAttFn.apply(zz, mask, packed, starting, 1e9, 4, chunk, *pl)
-        res.append(torch.autograd.grad((out * w).sum(), [zz] + pl))
-    for a, b in zip(*res):
-        assert _rel(a, b) < 1e-5
+    gen = torch.Generator().manual_seed(N * 7 + d)
+    q, k, v = (torch.randn(B, N, N, H * d, generator=gen).to(dev) for _ in range(3))
+    tri = torch.randn(B, H, N, N, generator=gen).to(dev)
+    mask = None
+    if with_mask:
+        mask = torch.ones(B, N, N)
+        mask[:, -2:, :] = 0
+        mask[:, :, -3:] = 0
+        mask = mask.to(dev)
+    do = (torch.randn(B, N, N, H * d, generator=gen) * gscale).to(dev)
+    o, stats, pk = ops.attn_core_forward(q, k, v, tri, mask, H)
+    dq, dk, dv, dtri = ops.attn_core_backward(pk, mask, stats, o, do)
+    leaves = [t.clone().requires_grad_(True) for t in (q, k, v, tri)]
+    ref = _explicit_core(*leaves, mask, H)
+    grads = torch.autograd.grad(ref, leaves, do)
+    torch.cuda.synchronize()
+    assert_status_clean(dev)
+    assert _rel(o, ref) < 3e-3, _rel(o, ref)
+    # with one key the softmax is constant and dq, dk, dtri are exactly zero: their error is
+    # measured against a floor of 1e-2 of dv's norm (dv = do there) instead
+    floor = 1e-2 * float(grads[2].norm())
+    for name, a, b in zip(("dq", "dk", "dv", "dtri"), (dq, dk, dv, dtri), grads):
+        assert torch.isfinite(a).all(), name
+        err = float((a - b).norm())
+        assert err < 1e-2 * max(float(b.norm()), floor), (name, _rel(a, b))
 
 
 def test_transition_and_embedding_gradients_match_oracle():

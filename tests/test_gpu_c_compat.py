@@ -45,16 +45,19 @@ def _attention_reference(q, k, v, bias, mask, scale):
 
 
 @pytest.mark.parametrize("starting", [True, False])
-@pytest.mark.parametrize("B,N", [(1, 40), (2, 100), (1, 257)])
-def test_triangle_attention_matches_definition(starting, B, N):
+@pytest.mark.parametrize("B,N,H,D", [(1, 40, 4, 32), (2, 100, 4, 32), (1, 257, 4, 32), (2, 45, 4, 8),
+                                     (1, 70, 2, 16), (1, 33, 3, 64)])
+def test_triangle_attention_matches_definition(starting, B, N, H, D):
+    """The reference kernel's shape (4 heads of 32) on the tuned core, any other on the
+    tensor-core core of the training path (the reference module's default head_dim 8 among them)."""
     dev = require_gpu()
     from genie_tk import _C
-    gen = torch.Generator().manual_seed(3 * N + B + int(starting))
-    q, k, v = (torch.randn(B, 4, N, N, 32, generator=gen).to(dev, torch.bfloat16) for _ in range(3))
-    bias = torch.randn(B, 4, N, N, generator=gen).to(dev)
+    gen = torch.Generator().manual_seed(3 * N + B + int(starting) + D)
+    q, k, v = (torch.randn(B, H, N, N, D, generator=gen).to(dev, torch.bfloat16) for _ in range(3))
+    bias = torch.randn(B, H, N, N, generator=gen).to(dev)
     mask = (torch.rand(B, N, N, generator=gen) > 0.15).float().to(dev)
     mask[:, -2:, :] = 0  # fully masked rows
-    scale = 32 ** -0.5
+    scale = D ** -0.5
     fn = _C.triangle_attention_starting if starting else _C.triangle_attention_ending
     o = fn(q, k, v, bias, mask, scale)
     if starting:
