@@ -33,6 +33,7 @@
 #include <cmath>
 #include <string>
 
+#include "attn_core.h"
 #include "gtk_host.h"
 #include "gtk_sm100.cuh"
 
@@ -49,7 +50,7 @@ struct Args {
   const __half* k;
   const __half* v;
   const __half* tri;   // [B][H][N][Np]
-  const float* mask;   // [B][N][N] or NULL
+  const float* mask;   // [B] planes of N x N, element (i, k) at i * msi + k * msk; or NULL
   const float2* stat;  // (m, 1 / l) per [b][i][h][j]
   const __half* dO;    // [B][N][H][N][Dp], times gscale
   const float* dsum;   // D[b][i][h][j] (unscaled)
@@ -60,6 +61,7 @@ struct Args {
   float* dv;
   float* dtri;
   int64_t N, Np;
+  int64_t msi, msk;  // mask strides: (N, 1) in the block's frame, (1, N) for z^T's frame
   int H, d, hd;
   float qscale;   // log2 e / sqrt(d)
   float inf2;     // inf * log2 e
@@ -179,10 +181,17 @@ __device__ __forceinline__ void c_to_a(uint32_t (&a)[4], const float (&c)[2][4])
 __device__ __forceinline__ int c_row(int i) { return ((threadIdx.x & 31) >> 2) + ((i >> 1) << 3); }
 __device__ __forceinline__ int c_col(int i) { return 2 * (threadIdx.x & 3) + (i & 1); }
 
-// inf * (m - 1) in base-2 units for key k of pair row `row`; -inf past the last key.
-__device__ __forceinline__ float mask_bias2(const Args& a, int64_t row, int64_t k) {
+// The mask row of pair row `row` = b * N + i (NULL without a mask).
+__device__ __forceinline__ const float* mask_row(const Args& a, int64_t row) {
+  if (!a.mask) return nullptr;
+  const int64_t b = row / a.N, i = row - b * a.N;
+  return a.mask + b * a.N * a.N + i * a.msi;
+}
+
+// inf * (m - 1) in base-2 units for key k of a mask row; -inf past the last key.
+__device__ __forceinline__ float mask_bias2(const Args& a, const float* mrow, int64_t k) {
   if (k >= a.N) return -INFINITY;
-  return a.mask ? a.inf2 * (a.mask[row * a.N + k] - 1.f) : 0.f;
+  return mrow ? a.inf2 * (mrow[k * a.msk] - 1.f) : 0.f;
 }
 
 __device__ __forceinline__ float quad_max(float x) {
@@ -253,13 +262,14 @@ __global__ void __launch_bounds__(kThreads) fwd_kernel(const Args a) {
   const __half* kp = plane<D>(a.k, a, row, h);
   const __half* vp = plane<D>(a.v, a, row, h);
   const __half* bp = a.tri + (b * a.H + h) * N * a.Np;
+  const float* mrow = mask_row(a, row);
   const int nt = static_cast<int>((N + kRows - 1) / kRows);
   auto issue = [&](int t, int st) {
     const int64_t k0 = static_cast<int64_t>(t) * kRows;
     load_rows<D>(S.k[st], kp, k0, N);
     load_rows<D>(S.v[st], vp, k0, N);
     load_bias(S.b[st], bp, j0, k0, N, a.Np);
-    if (threadIdx.x < kRows) S.m[st][threadIdx.x] = mask_bias2(a, row, k0 + threadIdx.x);
+    if (threadIdx.x < kRows) S.m[st][threadIdx.x] = mask_bias2(a, mrow, k0 + threadIdx.x);
   };
   load_rows<D>(S.k[1], qp, j0, N);  // q passes through stage 1's key buffer
   issue(0, 0);
@@ -343,7 +353,7 @@ __global__ void __launch_bounds__(kThreads) fwd_kernel(const Args a) {
         const int e = n * 8 + 2 * (lane & 3) + x;
         if (e < a.d) out[e] = o[n][2 * r + x] * il;
       }
-    if ((lane & 3) == 0) a.out_stat[(row * a.H + h) * N + j] = make_float2(m[r], il);
+    if (a.out_stat && (lane & 3) == 0) a.out_stat[(row * a.H + h) * N + j] = make_float2(m[r], il);
   }
 }
 
@@ -361,13 +371,14 @@ __global__ void __launch_bounds__(kThreads) dq_kernel(const Args a) {
   const __half* kp = plane<D>(a.k, a, row, h);
   const __half* vp = plane<D>(a.v, a, row, h);
   const __half* bp = a.tri + (b * a.H + h) * N * a.Np;
+  const float* mrow = mask_row(a, row);
   const int nt = static_cast<int>((N + kRows - 1) / kRows);
   auto issue = [&](int t, int st) {
     const int64_t k0 = static_cast<int64_t>(t) * kRows;
     load_rows<D>(S.k[st], kp, k0, N);
     load_rows<D>(S.v[st], vp, k0, N);
     load_bias(S.b[st], bp, j0, k0, N, a.Np);
-    if (threadIdx.x < kRows) S.m[st][threadIdx.x] = mask_bias2(a, row, k0 + threadIdx.x);
+    if (threadIdx.x < kRows) S.m[st][threadIdx.x] = mask_bias2(a, mrow, k0 + threadIdx.x);
   };
   load_rows<D>(S.k[1], plane<D>(a.q, a, row, h), j0, N);
   load_rows<D>(S.v[1], plane<D>(a.dO, a, row, h), j0, N);
@@ -480,7 +491,7 @@ __global__ void __launch_bounds__(kThreads) dkv_kernel(const Args a) {
   const int kl0 = w * 16 + (lane >> 2);  // this thread's keys: kl0 and kl0 + 8 of the CTA's 64
   float mb[2];
 #pragma unroll
-  for (int r = 0; r < 2; ++r) mb[r] = mask_bias2(a, row, k0 + kl0 + 8 * r);  // -inf past the last key: p = 0
+  for (int r = 0; r < 2; ++r) mb[r] = mask_bias2(a, mask_row(a, row), k0 + kl0 + 8 * r);  // -inf past N: p = 0
   float dk[D / 8][4], dv[D / 8][4];
 #pragma unroll
   for (int n = 0; n < D / 8; ++n) {
@@ -561,7 +572,7 @@ __global__ void __launch_bounds__(kThreads) dtri_kernel(const Args a) {
     if (threadIdx.x < kRows) {
       const int t = threadIdx.x;
       const int64_t j = j0 + t;
-      S.m[st][t] = mask_bias2(a, row, k0 + t);
+      S.m[st][t] = mask_bias2(a, mask_row(a, row), k0 + t);
       S.l[st][t] = j < N ? a.stat[(row * a.H + h) * N + j] : make_float2(0.f, 0.f);
       S.dsum[st][t] = j < N ? a.dsum[(row * a.H + h) * N + j] * a.gscale : 0.f;
     }
@@ -630,10 +641,11 @@ __global__ void __launch_bounds__(kThreads) dtri_kernel(const Args a) {
 // the bias fp32 [B*H][N][N] -> fp16 [B*H][N][Np], zero past N. Eight halves per thread.
 // ---------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256)
-    pack_rows_kernel(const float* __restrict__ src, int64_t rows, int64_t N, int H, int d, int Dp, float scale,
-                     __half* __restrict__ dst) {
+    pack_rows_kernel(const float* __restrict__ src, int64_t ld, int64_t rows, int64_t N, int H, int d, int Dp,
+                     float scale, __half* __restrict__ dst, uint32_t* status) {
   const int C = Dp / 8;
   const int64_t total = rows * H * N * C;
+  uint32_t sat = 0;  // a value beyond the fp16 range was clamped
   for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
        idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int c = static_cast<int>(idx % C);
@@ -642,15 +654,16 @@ __global__ void __launch_bounds__(256)
     rest /= N;
     const int h = static_cast<int>(rest % H);
     const int64_t row = rest / H;
-    const float* s = src + (row * N + j) * static_cast<int64_t>(H) * d + static_cast<int64_t>(h) * d;
+    const float* s = src + (row * N + j) * ld + static_cast<int64_t>(h) * d;
     __align__(16) __half v[8];
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
       const int e = c * 8 + u;
-      v[u] = __float2half_rn(e < d ? s[e] * scale : 0.f);
+      v[u] = f16_sat_chk(e < d ? s[e] * scale : 0.f, sat);
     }
     *reinterpret_cast<uint4*>(dst + idx * 8) = *reinterpret_cast<const uint4*>(v);
   }
+  flag_saturation(sat, status);
 }
 
 __global__ void __launch_bounds__(256)
@@ -839,6 +852,8 @@ static Args core_args(int64_t N, int heads, int head_dim, float inf) {
   Args a{};
   a.N = N;
   a.Np = (N + 7) / 8 * 8;
+  a.msi = N;
+  a.msk = 1;
   a.H = heads;
   a.d = head_dim;
   a.hd = heads * head_dim;
@@ -880,6 +895,34 @@ static unsigned grid_1d(int64_t work, int per_block) {
   return static_cast<unsigned>(need < 1 ? 1 : (need < cap ? need : cap));
 }
 
+int padded_head_dim(int d) { return padded_dim(d); }
+
+int launch_pack(const float* src, int64_t ld, int64_t B, int64_t N, int H, int d, float scale, __half* dst,
+                uint32_t* status, cudaStream_t st) {
+  const int dp = padded_dim(d);
+  pack_rows_kernel<<<grid_1d(B * N * H * N * (dp / 8), 256), 256, 0, st>>>(src, ld, B * N, N, H, d, dp, scale, dst,
+                                                                          status);
+  return check_launch("attention core pack");
+}
+
+int launch_forward(const __half* q, const __half* k, const __half* v, const __half* tri, const float* mask,
+                   int64_t msi, int64_t msk, int64_t B, int64_t N, int H, int d, float inf, float* o,
+                   cudaStream_t st) {
+  Args a = core_args(N, H, d, inf);
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.tri = tri;
+  a.mask = mask;
+  a.msi = msi;
+  a.msk = msk;
+  a.out_o = o;
+  if (int e = check_core(a, B)) return e;
+  const dim3 grid(static_cast<unsigned>(B * N), static_cast<unsigned>(H), static_cast<unsigned>((N + kRows - 1) / kRows));
+  GTK_CORE_LAUNCH(fwd_kernel, RowSmem, grid, "attention core forward");
+  return GTK_OK;
+}
+
 }  // namespace attn
 }  // namespace gtk
 
@@ -909,7 +952,8 @@ int gtk_attn_core_pack(const float* src, int64_t B, int64_t N, int heads, int he
   const int dp = padded_dim(head_dim);
   const int64_t work = B * N * heads * N * (dp / 8);
   pack_rows_kernel<<<grid_1d(work, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      src, B * N, N, heads, head_dim, dp, scale, static_cast<__half*>(dst));
+      src, static_cast<int64_t>(heads) * head_dim, B * N, N, heads, head_dim, dp, scale, static_cast<__half*>(dst),
+      nullptr);
   return check_launch("attention core pack");
 }
 

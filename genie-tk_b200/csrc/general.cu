@@ -11,26 +11,29 @@
 //              (reference src/genie_tk/triangle_mul.py:103-132)
 //   TriAtt     zn[P][c_in] = LN(z or z^T)
 //              Y[P][4hd + H] = zn (W_q | W_k | W_v | W_g | W_b)^T + (0 | 0 | 0 | b_g | 0)
-//              tri[B][H][N][N] = triangle bias in log2 units
-//              og[P][hd] = softmax_k(q.k / sqrt(d) + inf (m - 1) + tri) v * sigmoid(g)
-//              out = z + og W_o^T + b_o, rows written back in z's frame
+//              q, k, v fp16 planes [B*N][H][N][Dp] and the triangle bias fp16 [B][H][N][Np]
+//              o[P][hd] = softmax_k(q.k / sqrt(d) + inf (m - 1) + tri) v on the tensor-core
+//              attention core of attn_bwd.cu (mma.sync, fp32 softmax)
+//              out = z + (o * sigmoid(g)) W_o^T + b_o (the gate applied as the GEMM loads o),
+//              rows written back in z's frame
 //              (reference triangle_attention.py:100-143, primitives.py:114-178)
 //   Transition zn = LN(z); h[P][n c] = relu(zn W_1^T + b_1); out = (z + h W_2^T + b_2) * m
 //              (reference pair_transform.py:64-84, :190-193)
-// Everything but the contraction is fp32 arithmetic on the CUDA cores; LayerNorm and the
-// softmax use the reference's eps (1e-5) and additive mask value.
+// LayerNorms, projections and the transition are fp32 arithmetic on the CUDA cores; the
+// contraction and the attention core run on tensor cores with fp16 operands (a clamp to the
+// fp16 range is reported in the status word). LayerNorm and the softmax use the reference's
+// eps (1e-5) and additive mask value.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <cmath>
 #include <string>
 
+#include "attn_core.h"
 #include "general.h"
 
 namespace gtk {
 namespace gen {
-
-constexpr float kLog2e = 1.4426950408889634f;
 
 // Memory row of pair p = (b, r, c) of a block's frame: p itself, or (b, c, r) in the z^T frame.
 __device__ __forceinline__ int64_t frame_row(int64_t p, int64_t N, int tr) {
@@ -287,116 +290,28 @@ __global__ void __launch_bounds__(256)
 }
 
 // ---------------------------------------------------------------------------------------
-// Triangle bias tri[b][h][j][k] = Y[(b*N + j)*N + k][col0 + h] * log2 e.
+// Triangle bias as the attention core's fp16 plane: trih[b][h][j][k] = Y[(b*N + j)*N + k][col0 + h]
+// for k < N, zero for N <= k < Np. Eight keys per thread.
 // ---------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256)
-    tri_bias_kernel(const float* __restrict__ Y, int64_t ldy, int col0, int H, int64_t B, int64_t N,
-                    float* __restrict__ tri) {
-  const int64_t total = B * H * N * N;
+    tri_bias_f16_kernel(const float* __restrict__ Y, int64_t ldy, int col0, int H, int64_t B, int64_t N, int64_t Np,
+                        __half* __restrict__ trih) {
+  const int64_t C = Np / 8;
+  const int64_t total = B * H * N * C;
   for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t < total;
        t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t k = t % N;
-    int64_t r = t / N;
+    const int64_t c = t % C;
+    int64_t r = t / C;
     const int64_t j = r % N;
     r /= N;
     const int64_t h = r % H, b = r / H;
-    tri[t] = Y[((b * N + j) * N + k) * ldy + col0 + h] * kLog2e;
-  }
-}
-
-// ---------------------------------------------------------------------------------------
-// Attention core: CTA = (pair row i of batch b, head h, 128 queries j), thread = query.
-// Keys in tiles of 32 with their values, the bias block [128 j][32 k] and the mask bias
-// staged in shared memory; online softmax in base 2 (scores, bias and mask carry log2 e).
-// s = q.k / sqrt(d) + inf * (m_ik - 1) + tri[b, h, j, k]; og = (sum_k p v_k / sum_k p) *
-// sigmoid(g). The mask is read in the block's frame (m[b, k, i] for the ending node).
-// ---------------------------------------------------------------------------------------
-template <int D>
-__global__ void __launch_bounds__(128)
-    att_core_kernel(const float* __restrict__ Y, int64_t ldy, const float* __restrict__ tri,
-                    const float* __restrict__ mask, int64_t N, int H, int d, int hd, float qscale, float inf2, int tr,
-                    float* __restrict__ og) {
-  __shared__ float Ks[32][D], Vs[32][D];
-  __shared__ float Bs[128][33];
-  __shared__ float Ms[32];
-  const int t = threadIdx.x;
-  const int64_t row = blockIdx.x;  // b*N + i
-  const int h = blockIdx.y;
-  const int64_t j0 = static_cast<int64_t>(blockIdx.z) * 128;
-  const int64_t b = row / N, i = row - b * N;
-  const int64_t j = j0 + t;
-  const bool active = j < N;
-  float q[D], o[D];
-  {
-    const float* yq = Y + (row * N + (active ? j : 0)) * ldy + h * d;
+    __align__(16) __half v[8];
 #pragma unroll
-    for (int e = 0; e < D; ++e) {
-      q[e] = (e < d && active) ? yq[e] * qscale : 0.f;
-      o[e] = 0.f;
+    for (int u = 0; u < 8; ++u) {
+      const int64_t k = c * 8 + u;
+      v[u] = __float2half_rn(k < N ? Y[((b * N + j) * N + k) * ldy + col0 + h] : 0.f);
     }
-  }
-  float m = -INFINITY, l = 0.f;
-  const float* trib = tri + (b * H + h) * N * N;
-  for (int64_t k0 = 0; k0 < N; k0 += 32) {
-    __syncthreads();
-    for (int idx = t; idx < 32 * D; idx += 128) {
-      const int kk = idx / D, e = idx - kk * D;
-      const int64_t k = k0 + kk;
-      float kv = 0.f, vv = 0.f;
-      if (k < N && e < d) {
-        const float* y = Y + (row * N + k) * ldy + h * d + e;
-        kv = y[hd];
-        vv = y[2 * hd];
-      }
-      Ks[kk][e] = kv;
-      Vs[kk][e] = vv;
-    }
-    for (int idx = t; idx < 128 * 32; idx += 128) {
-      const int jj = idx >> 5, kk = idx & 31;
-      const int64_t jq = j0 + jj, k = k0 + kk;
-      Bs[jj][kk] = (jq < N && k < N) ? trib[jq * N + k] : 0.f;
-    }
-    if (t < 32) {
-      const int64_t k = k0 + t;
-      float mb = -INFINITY;  // past the last key: never counts
-      if (k < N) {
-        const float mv = mask ? mask[tr ? (b * N + k) * N + i : row * N + k] : 1.f;
-        mb = inf2 * (mv - 1.f);
-      }
-      Ms[t] = mb;
-    }
-    __syncthreads();
-    float s[32];
-    float tmax = -INFINITY;
-#pragma unroll
-    for (int kk = 0; kk < 32; ++kk) {
-      float acc = 0.f;
-#pragma unroll
-      for (int e = 0; e < D; ++e) acc = fmaf(q[e], Ks[kk][e], acc);
-      s[kk] = acc + Bs[t][kk] + Ms[kk];
-      tmax = fmaxf(tmax, s[kk]);
-    }
-    const float mnew = fmaxf(m, tmax);
-    const float corr = exp2f(m - mnew);  // 0 on the first tile (m = -inf)
-    l *= corr;
-#pragma unroll
-    for (int e = 0; e < D; ++e) o[e] *= corr;
-#pragma unroll
-    for (int kk = 0; kk < 32; ++kk) {
-      const float p = exp2f(s[kk] - mnew);  // 0 for keys past N (s = -inf)
-      l += p;
-#pragma unroll
-      for (int e = 0; e < D; ++e) o[e] = fmaf(p, Vs[kk][e], o[e]);
-    }
-    m = mnew;
-  }
-  if (active) {
-    const float* yg = Y + (row * N + j) * ldy + 3 * hd + h * d;
-    float* out = og + (row * N + j) * hd + h * d;
-    const float il = 1.f / l;
-#pragma unroll
-    for (int e = 0; e < D; ++e)
-      if (e < d) out[e] = o[e] * il * sigmoid_f(yg[e]);
+    *reinterpret_cast<uint4*>(trih + t * 8) = *reinterpret_cast<const uint4*>(v);
   }
 }
 
@@ -613,17 +528,23 @@ static TaPack ta_pack(int cin, int hd, int H) {
   return p;
 }
 
+// zn (LayerNorm output) | Y (projections) | the fp16 bias plane | o (attention output) |
+// the fp16 q, k, v planes of the tensor-core attention core.
 struct TaWs {
-  size_t zn, y, tri, og, total;
+  size_t zn, y, tri, og, q, k, v, total;
 };
 static TaWs ta_ws(int64_t B, int64_t N, int cin, int hd, int H) {
   TaWs w{};
   const size_t P = static_cast<size_t>(B) * N * N;
+  const size_t plane = a256(P * H * attn::padded_head_dim(hd / H) * 2);
   w.zn = 0;
   w.y = a256(P * cin * 4);
   w.tri = w.y + a256(P * (4 * static_cast<size_t>(hd) + H) * 4);
-  w.og = w.tri + a256(static_cast<size_t>(B) * H * N * N * 4);
-  w.total = w.og + a256(P * hd * 4);
+  w.og = w.tri + a256(static_cast<size_t>(B) * H * N * ((N + 7) / 8 * 8) * 2);
+  w.q = w.og + a256(P * hd * 4);
+  w.k = w.q + plane;
+  w.v = w.k + plane;
+  w.total = w.v + plane;
   return w;
 }
 
@@ -677,17 +598,10 @@ size_t triatt_workspace_bytes(int64_t B, int64_t N, int c_in, int c_hidden, int 
   return ta_ws(B, N, c_in, c_hidden, heads).total;
 }
 
-template <int D>
-static void launch_att_core(dim3 grid, cudaStream_t st, const float* Y, int64_t ldy, const float* tri,
-                            const float* mask, int64_t N, int H, int d, int hd, float qscale, float inf2, int tr,
-                            float* og) {
-  att_core_kernel<D><<<grid, 128, 0, st>>>(Y, ldy, tri, mask, N, H, d, hd, qscale, inf2, tr, og);
-}
 
 int triatt_forward(int starting, const float* z, const float* mask, const void* packed, float* out,
                    int add_residual, const DropArgs& drop, void* workspace, size_t workspace_bytes, int64_t B,
                    int64_t N, int c_in, int c_hidden, int heads, float inf, uint32_t* status, void* stream) {
-  (void)status;
   if (int e = triatt_check(c_in, c_hidden, heads)) return e;
   if (int e = common_args(z, out, packed, workspace, mask, B, N)) return e;
   if (int e = drop_channels(drop, c_in)) return e;
@@ -700,7 +614,6 @@ int triatt_forward(int starting, const float* z, const float* mask, const void* 
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   float* zn = reinterpret_cast<float*>(ws + w.zn);
   float* Y = reinterpret_cast<float*>(ws + w.y);
-  float* tri = reinterpret_cast<float*>(ws + w.tri);
   float* og = reinterpret_cast<float*>(ws + w.og);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int64_t P = B * N * N;
@@ -711,32 +624,37 @@ int triatt_forward(int starting, const float* z, const float* mask, const void* 
   if (int e = launch_gemm(zn, P, c_in, c_in, pk + L.w, static_cast<int>(ldy), c_in, epi(kStore, pk + L.b, Y, ldy),
                           st))
     return e;
+  // the attention core on the tensor cores: q, k, v and the bias as fp16 planes
+  __half* qh = reinterpret_cast<__half*>(ws + w.q);
+  __half* kh = reinterpret_cast<__half*>(ws + w.k);
+  __half* vh = reinterpret_cast<__half*>(ws + w.v);
+  __half* trih = reinterpret_cast<__half*>(ws + w.tri);
+  if (int e = attn::launch_pack(Y, ldy, B, N, H, d, 1.f, qh, status, st)) return e;
+  if (int e = attn::launch_pack(Y + hd, ldy, B, N, H, d, 1.f, kh, status, st)) return e;
+  if (int e = attn::launch_pack(Y + 2 * hd, ldy, B, N, H, d, 1.f, vh, status, st)) return e;
   {
-    const int64_t total = B * H * N * N;
-    tri_bias_kernel<<<grid_rows(total, 256), 256, 0, st>>>(Y, ldy, 4 * hd, H, B, N, tri);
-    if (int e = check_launch("general tri_bias_kernel")) return e;
+    const int64_t Np = (N + 7) / 8 * 8;
+    tri_bias_f16_kernel<<<grid_rows(B * H * N * (Np / 8), 256), 256, 0, st>>>(Y, ldy, 4 * hd, H, B, N, Np, trih);
+    if (int e = check_launch("general tri_bias_f16_kernel")) return e;
   }
-  {
-    const int64_t jb = (N + 127) / 128;
-    if (B * N > 2147483647 || jb > 65535) return fail(GTK_ERR_INVALID_ARG, "triatt: N too large");
-    dim3 grid(static_cast<unsigned>(B * N), static_cast<unsigned>(H), static_cast<unsigned>(jb));
-    const float qscale = kLog2e / std::sqrt(static_cast<float>(d)), inf2 = inf * kLog2e;
-    if (d <= 8)
-      launch_att_core<8>(grid, st, Y, ldy, tri, mask, N, H, d, hd, qscale, inf2, tr, og);
-    else if (d <= 16)
-      launch_att_core<16>(grid, st, Y, ldy, tri, mask, N, H, d, hd, qscale, inf2, tr, og);
-    else if (d <= 32)
-      launch_att_core<32>(grid, st, Y, ldy, tri, mask, N, H, d, hd, qscale, inf2, tr, og);
-    else
-      launch_att_core<64>(grid, st, Y, ldy, tri, mask, N, H, d, hd, qscale, inf2, tr, og);
-    if (int e = check_launch("general att_core_kernel")) return e;
-  }
+  // the mask in the block's frame: m[b, i, k] (starting) or m[b, k, i] (ending)
+  if (int e = attn::launch_forward(qh, kh, vh, trih, mask, starting ? N : 1, starting ? 1 : N, B, N, H, d, inf, og,
+                                   st))
+    return e;
+  // out = z + (o * sigmoid(g)) W_o^T + b_o, the gate applied as the GEMM loads o
   Epi e = epi(kRes, pk + L.bo, out, c_in);
   e.z = add_residual ? z : nullptr;
   e.N = N;
   e.tr = tr;
   e.drop = drop;
-  return launch_gemm(og, P, hd, hd, pk + L.wo, c_in, hd, e, st);
+  Pro pro{};
+  pro.gate = Y + 3 * hd;
+  pro.ldg = ldy;
+  const int64_t mt = (P + kBM - 1) / kBM;
+  if (mt > 2147483647) return fail(GTK_ERR_INVALID_ARG, "triatt: too many rows");
+  const dim3 grid(static_cast<unsigned>(mt), static_cast<unsigned>((c_in + kBN - 1) / kBN));
+  gemm_kernel<kProGate><<<grid, 256, 0, st>>>(og, P, hd, hd, pk + L.wo, c_in, hd, e, pro);
+  return check_launch("general gemm_kernel (gated output)");
 }
 
 // ----------------------------------- pair transition -----------------------------------

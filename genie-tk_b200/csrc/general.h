@@ -5,7 +5,8 @@
 // reference's modules accept -- its own defaults (c_hidden_tri_att = 32 with 4 heads, so
 // head_dim 8), the c_hidden_mul = 64 of its examples, the c_z = 32 / 64 of its tests --
 // runs here: fp32 LayerNorms and projections, the per-channel contraction on the tcgen05
-// contraction kernel (K2) through fp16 planes, and an online-softmax attention kernel. The
+// contraction kernel (K2) through fp16 planes, and the attention on the tensor-core
+// attention core of attn_bwd.cu through fp16 planes. The
 // public entry points of those files dispatch here when the shape is not the tuned one,
 // so the C ABI is unchanged.
 #pragma once

@@ -25,7 +25,11 @@ recomputation of the block's math on the GPU:
 * Pair transition (pair_transform.py:78-84): recomputed and differentiated with
   PyTorch ops.
 
-The recomputations are fp32. A block with no input or parameter that requires a
+The recomputations are fp32. Their GEMMs in the multiplicative update and the attention
+run on TF32 tensor cores while ``RECOMPUTE_TF32`` is true (the default): products with a
+10-bit mantissa and fp32 accumulation, relative error ~1e-3 against fp32, where the
+reference's bf16 autograd has ~1e-2. Set it to False for fp32 CUDA-core GEMMs. The
+transition's recompute is always fp32. A block with no input or parameter that requires a
 gradient never builds any of this: its forward is the plain kernel call.
 """
 
@@ -40,6 +44,23 @@ from torch import Tensor
 from . import ops
 
 LN_EPS = 1e-5
+
+# TF32 tensor cores for the GEMMs of the multiplicative-update and attention recomputes
+RECOMPUTE_TF32 = True
+
+
+class _Tf32:
+    """Enables TF32 matmuls for the enclosed recompute (when RECOMPUTE_TF32), then restores."""
+
+    def __enter__(self):
+        self._old = torch.backends.cuda.matmul.allow_tf32
+        if RECOMPUTE_TF32:
+            torch.backends.cuda.matmul.allow_tf32 = True
+        return self
+
+    def __exit__(self, *exc):
+        torch.backends.cuda.matmul.allow_tf32 = self._old
+        return False
 
 
 def needs_grad(x: Tensor, module: torch.nn.Module) -> bool:
@@ -204,7 +225,7 @@ class TriMulFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dU):
         z, mask, *params = ctx.saved_tensors
-        with torch.enable_grad():
+        with torch.enable_grad(), _Tf32():
             zl, pl = _leaves(z.float(), params)
             out = trimul_recompute(zl, mask, dict(zip(ops.TRIMUL_KEYS, pl)), ctx.outgoing)
             g = _grads(out, zl, pl, dU.float())
@@ -221,7 +242,7 @@ class TriAttFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dU):
         z, mask, *params = ctx.saved_tensors
-        with torch.enable_grad():
+        with torch.enable_grad(), _Tf32():
             zl, pl = _leaves(z.float(), params)
             out = triatt_recompute(zl, mask, dict(zip(ops.TRIATT_KEYS, pl)), ctx.starting, ctx.heads, ctx.inf)
             g = _grads(out, zl, pl, dU.float())

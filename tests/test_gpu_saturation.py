@@ -58,13 +58,9 @@ def test_attention_projections_beyond_fp16_range_are_reported(c_in, c, H):
     mod.load_state_dict(to_dev(p, dev))
     with torch.no_grad():
         mod(z)
-    st = _status(dev)
-    if (c_in, c, H) == (128, 128, 4):
-        # the tuned path stores v in fp16: the clamp is reported
-        assert st & SATURATED
-    else:
-        # the general path keeps q, k, v in fp32: nothing to clamp, nothing reported
-        assert st == 0
+    # both paths give the tensor cores v as fp16 (the tuned one from K3, the general one
+    # through its fp16 operand planes): the clamp is reported
+    assert _status(dev) & SATURATED
 
 
 def test_transition_hidden_beyond_fp16_range_is_reported():
