@@ -898,8 +898,9 @@ static unsigned grid_1d(int64_t work, int per_block) {
 int padded_head_dim(int d) { return padded_dim(d); }
 
 int launch_pack(const float* src, int64_t ld, int64_t B, int64_t N, int H, int d, float scale, __half* dst,
-                uint32_t* status, cudaStream_t st) {
-  const int dp = padded_dim(d);
+                uint32_t* status, cudaStream_t st, int Dp) {
+  const int dp = Dp > 0 ? Dp : padded_dim(d);
+  if (dp % 8 || dp < d) return fail(GTK_ERR_INVALID_ARG, "attention core pack: bad plane width");
   pack_rows_kernel<<<grid_1d(B * N * H * N * (dp / 8), 256), 256, 0, st>>>(src, ld, B * N, N, H, d, dp, scale, dst,
                                                                           status);
   return check_launch("attention core pack");

@@ -12,9 +12,10 @@ namespace attn {
 int padded_head_dim(int d);
 
 // fp32 rows [B*N][N] of pitch `ld` floats, head h's d columns at h * d -> the fp16 plane
-// [B*N][H][N][Dp] times `scale`; a clamp to the fp16 range sets the saturation bit in `status`.
+// [B*N][H][N][Dp] times `scale` (Dp = padded_head_dim(d), or `Dp` when given: 16, 32 or 64,
+// at least d); a clamp to the fp16 range sets the saturation bit in `status`.
 int launch_pack(const float* src, int64_t ld, int64_t B, int64_t N, int H, int d, float scale, __half* dst,
-                uint32_t* status, cudaStream_t st);
+                uint32_t* status, cudaStream_t st, int Dp = 0);
 
 // o [B*N][N][H*d] fp32 = softmax(q k^T / sqrt(d) + inf (mask - 1) + tri) v from packed planes,
 // without the statistics; mask element (b, i, k) at b*N*N + i*msi + k*msk (or NULL).

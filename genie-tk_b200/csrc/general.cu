@@ -23,6 +23,7 @@
 // contraction and the attention core run on tensor cores with fp16 operands (a clamp to the
 // fp16 range is reported in the status word). LayerNorm and the softmax use the reference's
 // eps (1e-5) and additive mask value.
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -34,6 +35,8 @@
 
 namespace gtk {
 namespace gen {
+
+constexpr float kLog2eF = 1.4426950408889634f;
 
 // Memory row of pair p = (b, r, c) of a block's frame: p itself, or (b, c, r) in the z^T frame.
 __device__ __forceinline__ int64_t frame_row(int64_t p, int64_t N, int tr) {
@@ -100,7 +103,7 @@ constexpr int kBM = 64, kBN = 64, kBK = 16;
 
 // What the GEMM applies to A's elements as it loads them: nothing, a LayerNorm of each row
 // (the CTA computes the 64 rows' mean and 1/std first), or a sigmoid gate.
-enum ProMode : int { kProNone = 0, kProLn = 1, kProGate = 2 };
+enum ProMode : int { kProNone = 0, kProLn = 1, kProGate = 2, kProHalf = 3 };
 
 struct Pro {
   const float* gamma;  // kProLn
@@ -108,6 +111,7 @@ struct Pro {
   float eps;
   const float* gate;   // kProGate: [M][ldg]
   int64_t ldg;
+  const __half* ah;    // kProHalf: A is fp16 (this pointer, pitch lda) instead of fp32
 };
 
 template <int kPro>
@@ -158,7 +162,10 @@ __global__ void __launch_bounds__(256)
       const int k = k0 + kk, n = n0 + r;
       float x = 0.f;
       if (m < M && k < K) {
-        x = A[m * lda + k];
+        if constexpr (kPro == kProHalf)
+          x = __half2float(pro.ah[m * lda + k]);
+        else
+          x = A[m * lda + k];
         if constexpr (kPro == kProLn) x = fmaf((x - mean_s[r]) * rstd_s[r], pro.gamma[k], pro.beta[k]);
         if constexpr (kPro == kProGate) x *= sigmoid_f(pro.gate[m * pro.ldg + k]);
       }
@@ -312,6 +319,58 @@ __global__ void __launch_bounds__(256)
       v[u] = __float2half_rn(k < N ? Y[((b * N + j) * N + k) * ldy + col0 + h] : 0.f);
     }
     *reinterpret_cast<uint4*>(trih + t * 8) = *reinterpret_cast<const uint4*>(v);
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// Operands of the tuned attention core (triatt.cu, 4 heads of 32) for a general block with
+// 4 heads of d <= 32, zero-padded to 32:
+//   gate[p][h*32 + e] = sigmoid(Y[p][3hd + h*d + e]) (0 for e >= d), fp16 [P][128];
+//   bias[(j*B*4 + b*4 + h)*ldn + k] = Y[(b*N + j)*N + k][4hd + h] * log2 e, bf16, 0 for k >= N;
+//   wpad[o][h*32 + e] = W_o[o][h*d + e] (0 for e >= d), so og [P][128] multiplies it directly.
+// ---------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+    k4_gate_kernel(const float* __restrict__ Y, int64_t ldy, int col0, int d, int64_t P, __half* __restrict__ gate) {
+  const int64_t total = P * 16;  // 16 chunks of 8 channels per pair
+  for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t < total;
+       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t p = t >> 4;
+    const int c = static_cast<int>(t & 15), h = c >> 2, e0 = (c & 3) * 8;
+    const float* y = Y + p * ldy + col0 + h * d;
+    __align__(16) __half v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = __float2half_rn(e0 + u < d ? sigmoid_f(y[e0 + u]) : 0.f);
+    *reinterpret_cast<uint4*>(gate + t * 8) = *reinterpret_cast<const uint4*>(v);
+  }
+}
+
+__global__ void __launch_bounds__(256)
+    k4_bias_kernel(const float* __restrict__ Y, int64_t ldy, int col0, int64_t B, int64_t N, int64_t ldn,
+                   __nv_bfloat16* __restrict__ bias) {
+  const int64_t C = ldn / 8;
+  const int64_t total = N * B * 4 * C;
+  for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t < total;
+       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t c = t % C;
+    int64_t r = t / C;  // r = j * B * 4 + b * 4 + h
+    const int h = static_cast<int>(r & 3);
+    r >>= 2;
+    const int64_t b = r % B, j = r / B;
+    __align__(16) __nv_bfloat16 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int64_t k = c * 8 + u;
+      v[u] = __float2bfloat16_rn(k < N ? Y[((b * N + j) * N + k) * ldy + col0 + h] * 1.4426950408889634f : 0.f);
+    }
+    *reinterpret_cast<uint4*>(bias + t * 8) = *reinterpret_cast<const uint4*>(v);
+  }
+}
+
+__global__ void __launch_bounds__(128)
+    wo_pad_kernel(const float* __restrict__ wo, int cin, int d, float* __restrict__ wpad) {
+  for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < cin * 128; t += gridDim.x * blockDim.x) {
+    const int o = t >> 7, c = t & 127, h = c >> 5, e = c & 31;
+    wpad[t] = e < d ? wo[static_cast<int64_t>(o) * 4 * d + h * d + e] : 0.f;
   }
 }
 
@@ -528,18 +587,31 @@ static TaPack ta_pack(int cin, int hd, int H) {
   return p;
 }
 
-// zn (LayerNorm output) | Y (projections) | the fp16 bias plane | o (attention output) |
-// the fp16 q, k, v planes of the tensor-core attention core.
+// The general attention's core runs on the tuned tcgen05 core (triatt.cu) when it has that
+// core's 4 heads and head_dim <= 32 (zero-padded to 32; the reference's default 32 = 4 x 8
+// among them), else on the mma.sync core of attn_bwd.cu.
+static bool ta_tuned_core(int hd, int H) { return H == 4 && hd % 4 == 0 && hd / 4 <= 32; }
+
+// zn (LayerNorm output) | Y (projections) | then either the tuned core's workspace
+// (q, k, v, gate, og, bias) and the head-padded W_o, or the fp16 bias plane, o and the fp16
+// q, k, v planes of the mma.sync core.
 struct TaWs {
-  size_t zn, y, tri, og, q, k, v, total;
+  size_t zn, y, tri, og, q, k, v, k4, wpad, total;
 };
 static TaWs ta_ws(int64_t B, int64_t N, int cin, int hd, int H) {
   TaWs w{};
   const size_t P = static_cast<size_t>(B) * N * N;
-  const size_t plane = a256(P * H * attn::padded_head_dim(hd / H) * 2);
   w.zn = 0;
   w.y = a256(P * cin * 4);
-  w.tri = w.y + a256(P * (4 * static_cast<size_t>(hd) + H) * 4);
+  const size_t rest = w.y + a256(P * (4 * static_cast<size_t>(hd) + H) * 4);
+  if (ta_tuned_core(hd, H)) {
+    w.k4 = rest;
+    w.wpad = w.k4 + a256(gtk_triatt_workspace_bytes(B, N, 128, 128, 4));
+    w.total = w.wpad + a256(static_cast<size_t>(cin) * 128 * 4);
+    return w;
+  }
+  const size_t plane = a256(P * H * attn::padded_head_dim(hd / H) * 2);
+  w.tri = rest;
   w.og = w.tri + a256(static_cast<size_t>(B) * H * N * ((N + 7) / 8 * 8) * 2);
   w.q = w.og + a256(P * hd * 4);
   w.k = w.q + plane;
@@ -624,6 +696,46 @@ int triatt_forward(int starting, const float* z, const float* mask, const void* 
   if (int e = launch_gemm(zn, P, c_in, c_in, pk + L.w, static_cast<int>(ldy), c_in, epi(kStore, pk + L.b, Y, ldy),
                           st))
     return e;
+  if (ta_tuned_core(hd, H)) {
+    // the tuned tcgen05 core: q (times log2 e / sqrt(d)), k, v as its [B*N][4][N][32]
+    // fp16 planes, the sigmoid gate and the bf16 log2 bias in its layouts
+    int64_t off[7];
+    if (int e = gtk_triatt_workspace_offsets(B, N, N, off)) return e;
+    uint8_t* w4 = ws + w.k4;
+    const float qs = kLog2eF / std::sqrt(static_cast<float>(d));
+    if (int e = attn::launch_pack(Y, ldy, B, N, H, d, qs, reinterpret_cast<__half*>(w4 + off[0]), status, st, 32))
+      return e;
+    if (int e = attn::launch_pack(Y + hd, ldy, B, N, H, d, 1.f, reinterpret_cast<__half*>(w4 + off[1]), status, st,
+                                  32))
+      return e;
+    if (int e = attn::launch_pack(Y + 2 * hd, ldy, B, N, H, d, 1.f, reinterpret_cast<__half*>(w4 + off[2]), status,
+                                  st, 32))
+      return e;
+    k4_gate_kernel<<<grid_rows(P * 16, 256), 256, 0, st>>>(Y, ldy, 3 * hd, d, P,
+                                                          reinterpret_cast<__half*>(w4 + off[3]));
+    if (int e = check_launch("general k4_gate_kernel")) return e;
+    const int64_t ldn = (N + 7) / 8 * 8;
+    k4_bias_kernel<<<grid_rows(N * B * 4 * (ldn / 8), 256), 256, 0, st>>>(
+        Y, ldy, 4 * hd, B, N, ldn, reinterpret_cast<__nv_bfloat16*>(w4 + off[5]));
+    if (int e = check_launch("general k4_bias_kernel")) return e;
+    if (int e = gtk_triatt_core(starting, mask, w4, B, N, N, 0, inf, status, stream)) return e;
+    float* wpad = reinterpret_cast<float*>(ws + w.wpad);
+    wo_pad_kernel<<<(c_in * 128 + 127) / 128, 128, 0, st>>>(pk + L.wo, c_in, d, wpad);
+    if (int e = check_launch("general wo_pad_kernel")) return e;
+    // out = z + og W_pad^T + b_o; og already carries the gate
+    Epi e = epi(kRes, pk + L.bo, out, c_in);
+    e.z = add_residual ? z : nullptr;
+    e.N = N;
+    e.tr = tr;
+    e.drop = drop;
+    Pro pro{};
+    pro.ah = reinterpret_cast<const __half*>(w4 + off[4]);
+    const int64_t mt = (P + kBM - 1) / kBM;
+    if (mt > 2147483647) return fail(GTK_ERR_INVALID_ARG, "triatt: too many rows");
+    const dim3 grid(static_cast<unsigned>(mt), static_cast<unsigned>((c_in + kBN - 1) / kBN));
+    gemm_kernel<kProHalf><<<grid, 256, 0, st>>>(nullptr, P, 128, 128, wpad, c_in, 128, e, pro);
+    return check_launch("general gemm_kernel (tuned-core output)");
+  }
   // the attention core on the tensor cores: q, k, v and the bias as fp16 planes
   __half* qh = reinterpret_cast<__half*>(ws + w.q);
   __half* kh = reinterpret_cast<__half*>(ws + w.k);

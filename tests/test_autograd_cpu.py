@@ -153,3 +153,16 @@ def test_half_precision_parameters_get_gradients_in_their_dtype(AG, dtype):
         for gh, gf, t in zip(grads[0], grads[1], half.values()):
             assert gh.dtype == t.dtype, (kind, gh.dtype)
             assert _rel(gh.float(), gf) < 1e-2, (kind, _rel(gh.float(), gf))
+
+
+def test_tf32_switch_restores_the_global_flag(AG, monkeypatch):
+    """The recompute enables TF32 matmuls only inside its own scope, and not at all when
+    RECOMPUTE_TF32 is off."""
+    torch.backends.cuda.matmul.allow_tf32 = False
+    with AG._Tf32():
+        assert torch.backends.cuda.matmul.allow_tf32
+    assert not torch.backends.cuda.matmul.allow_tf32
+    monkeypatch.setattr(AG, "RECOMPUTE_TF32", False)
+    with AG._Tf32():
+        assert not torch.backends.cuda.matmul.allow_tf32
+    assert not torch.backends.cuda.matmul.allow_tf32
