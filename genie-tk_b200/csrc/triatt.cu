@@ -910,14 +910,26 @@ struct K4eBars {
 };
 static_assert(sizeof(K4eBars) <= 256, "K4e barrier block");
 
+// Destinations of the peer form of K4e: the pair-grid transpose of a row shard, straight into
+// the P ranks' shards. Tile (b, i, j0..j0+127) goes to rank q = j0 / R as its pairs
+// (b, j - q*R, row0 + i): map[q] addresses rank q's shard [B][R][N][128] as (channel, row,
+// column, b) with a box of 32 channels x 128 rows, so the tile's slabs are TMA stores into
+// the peer's memory over NVLink (plain stores, no multicast).
+constexpr int kMaxPeers = 8;
+struct K4ePeers {
+  CUtensorMap map[kMaxPeers];
+  int R, row0;
+};
+
 // kDrop: the update is multiplied by the channel dropout `drop` before the residual add
 // (out = z + keep * scale * update); the plain instantiation ignores `drop`.
-template <bool kDrop>
+// kPeer: the finished tile goes to the peers' transposed shards (K4ePeers), not to out_map.
+template <bool kDrop, bool kPeer>
 __global__ void __launch_bounds__(k4e::kThreads, 1)
     triatt_finish_kernel(const __grid_constant__ CUtensorMap og_map, const __grid_constant__ CUtensorMap w_map,
                          const __grid_constant__ CUtensorMap z_map, const __grid_constant__ CUtensorMap out_map,
                          const float* __restrict__ vec, int N, int rows, int add_residual, int n_jt,
-                         int n_tiles, uint32_t* status, const DropArgs drop) {
+                         int n_tiles, uint32_t* status, const DropArgs drop, const __grid_constant__ K4ePeers peers) {
   using namespace k4e;
   extern __shared__ uint8_t dsmem[];
   uint8_t* smem = align1024(dsmem);
@@ -1082,7 +1094,12 @@ __global__ void __launch_bounds__(k4e::kThreads, 1)
           if (issuer) {
             iok = mbar_wait(&bars->slab_ready[sl], (slab / kSlabs) & 1, guard, status, kStatusTimeoutConsumer);
             if (iok) {
-              tma_store_4d(&out_map, ob, cc * 32, j0, i, b);
+              if constexpr (kPeer) {
+                const int q = j0 / peers.R;
+                tma_store_4d(&peers.map[q], ob, cc * 32, j0 - q * peers.R, peers.row0 + i, b);
+              } else {
+                tma_store_4d(&out_map, ob, cc * 32, j0, i, b);
+              }
               tma_store_commit();
               // a slab buffer is free again once its store has read it; keep two stores in flight
               tma_store_wait_read_le1();
@@ -1324,21 +1341,31 @@ static int triatt_finish_launch(int starting, const float* z, const void* packed
   if (int e = make_pair_map(&zm, add_residual ? z : out, B, rows, N, !starting)) return e;
   if (int e = make_pair_map(&om, out, B, rows, N, !starting)) return e;
   const bool dropping = drop.keep != nullptr;
-  const void* kern = dropping ? reinterpret_cast<const void*>(triatt_finish_kernel<true>)
-                              : reinterpret_cast<const void*>(triatt_finish_kernel<false>);
+  const void* kern = dropping ? reinterpret_cast<const void*>(triatt_finish_kernel<true, false>)
+                              : reinterpret_cast<const void*>(triatt_finish_kernel<false, false>);
   if (int e = ensure_smem(kern, k4e::kSmem)) return e;
   const int grid = static_cast<int>(n_tiles < num_sms() ? n_tiles : num_sms());
   const float* vec = reinterpret_cast<const float*>(pk + tapack::kVec);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const K4ePeers none{};
   if (dropping)
-    triatt_finish_kernel<true><<<grid, k4e::kThreads, k4e::kSmem, st>>>(
+    triatt_finish_kernel<true, false><<<grid, k4e::kThreads, k4e::kSmem, st>>>(
         am, wm, zm, om, vec, static_cast<int>(N), static_cast<int>(rows), add_residual, static_cast<int>(n_jt),
-        static_cast<int>(n_tiles), status, drop);
+        static_cast<int>(n_tiles), status, drop, none);
   else
-    triatt_finish_kernel<false><<<grid, k4e::kThreads, k4e::kSmem, st>>>(
+    triatt_finish_kernel<false, false><<<grid, k4e::kThreads, k4e::kSmem, st>>>(
         am, wm, zm, om, vec, static_cast<int>(N), static_cast<int>(rows), add_residual, static_cast<int>(n_jt),
-        static_cast<int>(n_tiles), status, drop);
+        static_cast<int>(n_tiles), status, drop, none);
   return check_launch("triatt_finish_kernel");
+}
+
+// Rank q's shard [B][R][N][128] fp32 addressed as (channel, row, column, b), box 32 x 128 rows.
+static int make_shard_rows_map(CUtensorMap* m, const void* base, int64_t B, int64_t R, int64_t N) {
+  const uint64_t row = 128 * 4;
+  uint64_t dims[4] = {128, static_cast<uint64_t>(R), static_cast<uint64_t>(N), static_cast<uint64_t>(B)};
+  uint64_t strides[3] = {row * N, row, row * N * R};
+  uint32_t box[4] = {32, 128, 1, 1};
+  return encode_tmap(m, TmaType::kF32, 4, base, dims, strides, box, 128);
 }
 
 static int triatt_forward_impl(int starting, const float* z, const float* mask, const void* packed, float* out,
@@ -1364,6 +1391,44 @@ int gtk_triatt_finish(int starting, const float* z, const void* packed, void* wo
                       int64_t B, int64_t rows, int64_t N, uint32_t* status, void* stream) {
   return triatt_finish_launch(starting, z, packed, workspace, out, add_residual, B, rows, N, status, stream,
                               DropArgs{});
+}
+
+int gtk_triatt_finish_to_peers(const float* z, const void* packed, void* workspace, const uint64_t* dst_bases, int P,
+                               int64_t B, int64_t rows, int64_t N, int64_t row0, int add_residual, uint32_t* status,
+                               void* stream) {
+  if (P < 1 || P > kMaxPeers || !dst_bases) return fail(GTK_ERR_INVALID_ARG, "triatt_finish_to_peers: bad P");
+  if (!dims_ok(B, 65535) || !dims_ok(N, 65535) || rows < 1 || rows * P != N || row0 < 0 || row0 % rows ||
+      row0 + rows > N)
+    return fail(GTK_ERR_INVALID_ARG, "triatt_finish_to_peers: rows * P must equal N, row0 a multiple of rows");
+  if (rows % 128) return fail(GTK_ERR_UNSUPPORTED, "triatt_finish_to_peers: rows per rank must be a multiple of 128");
+  if (int e = check_ptr(z, "z")) return e;
+  if (int e = check_ptr(packed, "packed", 256)) return e;
+  if (int e = check_ptr(workspace, "workspace", 256)) return e;
+  for (int q = 0; q < P; ++q)
+    if (int e = check_ptr(reinterpret_cast<const void*>(dst_bases[q]), "peer shard")) return e;
+  if (int e = check_device()) return e;
+  const TriattWs w = triatt_layout(B, rows, N);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const uint8_t* pk = static_cast<const uint8_t*>(packed);
+  const int64_t n_jt = N / 128;
+  const int64_t n_tiles = B * rows * n_jt;
+  CUtensorMap am, wm, zm;
+  if (int e = make_hidden_map(&am, ws + w.og, B * rows, N)) return e;
+  if (int e = make_weight_map(&wm, pk + tapack::kW4, 128, 128)) return e;
+  if (int e = make_pair_map(&zm, z, B, rows, N, false)) return e;
+  K4ePeers peers{};
+  peers.R = static_cast<int>(rows);
+  peers.row0 = static_cast<int>(row0);
+  for (int q = 0; q < P; ++q)
+    if (int e = make_shard_rows_map(&peers.map[q], reinterpret_cast<const void*>(dst_bases[q]), B, rows, N)) return e;
+  const void* kern = reinterpret_cast<const void*>(triatt_finish_kernel<false, true>);
+  if (int e = ensure_smem(kern, k4e::kSmem)) return e;
+  const int grid = static_cast<int>(n_tiles < num_sms() ? n_tiles : num_sms());
+  const float* vec = reinterpret_cast<const float*>(pk + tapack::kVec);
+  triatt_finish_kernel<false, true><<<grid, k4e::kThreads, k4e::kSmem, static_cast<cudaStream_t>(stream)>>>(
+      am, wm, zm, zm, vec, static_cast<int>(N), static_cast<int>(rows), add_residual, static_cast<int>(n_jt),
+      static_cast<int>(n_tiles), status, DropArgs{}, peers);
+  return check_launch("triatt_finish_kernel (to peers)");
 }
 
 int gtk_triatt_forward(int starting, const float* z, const float* mask, const void* packed, float* out,

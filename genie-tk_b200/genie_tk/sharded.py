@@ -125,6 +125,15 @@ class CudaStageOps:
         self._chk(self.lib.gtk_triatt_finish(1, P(z), P(mod.packed_weights(self.device)), P(ws), P(z), 1, B, rows,
                                              N, P(self.status), self._s()), "gtk_triatt_finish")
 
+    def triatt_finish_to(self, mod, z, ws, B, rows, N, row0, dst: "PeerBuffer"):
+        """K4e with the pair-grid transpose fused into its stores: z + update, transposed,
+        straight into every rank's shard of ``dst``."""
+        P = ops._ptr
+        bases = (ctypes.c_uint64 * len(dst.addrs))(*dst.addrs)
+        self._chk(self.lib.gtk_triatt_finish_to_peers(P(z), P(mod.packed_weights(self.device)), P(ws), bases,
+                                                      len(dst.addrs), B, rows, N, row0, 1, P(self.status),
+                                                      self._s()), "gtk_triatt_finish_to_peers")
+
     def copy_2d(self, dst, dpitch, src, spitch, width, height):
         self._chk(self.lib.gtk_copy_2d(ops._ptr(dst), dpitch, ops._ptr(src), spitch, width, height, self._s()),
                   "gtk_copy_2d")
@@ -206,7 +215,7 @@ class ShardedTrianglePairStack:
 
     def __init__(self, stack: TrianglePairStack, world: int, rank: int, stage_ops=None,
                  trimul_exchange: str = "auto", exchange: str = "nccl", k1_direct: bool = False,
-                 push: str = "kernel"):
+                 push: str = "kernel", fused_transpose: bool = True):
         if trimul_exchange not in ("auto", "gather", "channels"):
             raise ValueError(f"trimul_exchange must be auto, gather or channels, not {trimul_exchange!r}")
         if exchange not in ("nccl", "peer"):
@@ -225,6 +234,10 @@ class ShardedTrianglePairStack:
         # push, so it is off by default.
         self.k1_direct = k1_direct
         self.push = push  # slab pushes of the default stage ops: "kernel" or "dma" (CudaStageOps)
+        # peer mode: the attention blocks' K4e writes its output transposed straight into the
+        # peers' shards (one kernel instead of K4e + a transpose push), when each rank's rows
+        # are a multiple of 128
+        self.fused_transpose = fused_transpose
         self._key = None
         self._buf: Dict[str, Tensor] = {}
         self._peer: Dict[str, PeerBuffer] = {}
@@ -518,13 +531,20 @@ class ShardedTrianglePairStack:
 
         multiply = multiply_channels if self.trimul_exchange == "channels" else multiply_gather
 
-        def attention(mod, zz, mm):
+        fuse = self.fused_transpose and R % 128 == 0 and hasattr(so, "triatt_finish_to")
+
+        def attention(mod, zz, mm, dst_name=None):
             so.triatt_project(mod, zz, tri, B, R, N, row0)
             w = bias_mine.numel()
             so.push_3d(peer["tri"], tri_bias + row0 * B * H * N * 2, w, bias_mine, w, 0, w, 1)
             yield ("barrier",)
             so.triatt_core(mod, mm, tri, B, R, N, row0)
-            so.triatt_finish(mod, zz, tri, B, R, N)
+            if dst_name is None:
+                so.triatt_finish(mod, zz, tri, B, R, N)
+            else:
+                # zz + update, transposed, straight into every rank's `dst_name` shard
+                so.triatt_finish_to(mod, zz, tri, B, R, N, row0, peer[dst_name])
+                yield ("barrier",)
 
         def transpose(src_pairs, dst_name):
             so.push_pair_transpose(src_pairs, peer[dst_name], B, R, N, P, N, row0)
@@ -533,11 +553,15 @@ class ShardedTrianglePairStack:
         for layer in self.stack.layers:
             yield from multiply(layer.tri_mul_out, True, src)
             yield from multiply(layer.tri_mul_in, False, z)
-            yield from attention(layer.tri_att_start, z, mask)
             # TriAttEnd = Start(z^T, mask^T)^T, the residual added on the transposed shard
-            yield from transpose(z, "zT")
-            yield from attention(layer.tri_att_end, zT, mask_t)
-            yield from transpose(zT, "zs")
+            if fuse:
+                yield from attention(layer.tri_att_start, z, mask, "zT")
+                yield from attention(layer.tri_att_end, zT, mask_t, "zs")
+            else:
+                yield from attention(layer.tri_att_start, z, mask)
+                yield from transpose(z, "zT")
+                yield from attention(layer.tri_att_end, zT, mask_t)
+                yield from transpose(zT, "zs")
             src = z
         so.copy_2d(_bytes(z_user), z.numel() * 4, _bytes(z), z.numel() * 4, z.numel() * 4, 1)
 

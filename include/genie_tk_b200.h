@@ -290,6 +290,17 @@ GTK_API int gtk_push_3d(const uint64_t* dsts, int P, int64_t doff, int64_t dpitc
  * shard dsts[q] [B][C/P][ndst][128] at (b, x, row0 + y). */
 GTK_API int gtk_push_pair_transpose(const float* src, const uint64_t* dsts, int64_t B, int64_t R, int64_t C,
                                     int64_t P, int64_t ndst, int64_t row0, void* stream);
+/* K4e of a row shard with the pair-grid transpose fused into its stores: the finished
+ * update out = z + og W_o^T + b_o (+ z when add_residual) of the starting-orientation shard
+ * (rows local rows from global row row0, the workspace of gtk_triatt_core) is written
+ * straight into the P ranks' transposed shards, pair (b, y, j) to rank q = j / rows at
+ * (b, j - q*rows, row0 + y), by TMA stores into the peers' memory. dst_bases: HOST array of
+ * the P shards' device addresses ([B][rows][N][128] fp32 each, 16-byte aligned); rows * P
+ * = N, rows a multiple of 128, P <= 8. Replaces gtk_triatt_finish + gtk_push_pair_transpose
+ * in the sharded stack (no reference counterpart: the reference runs on one device). */
+GTK_API int gtk_triatt_finish_to_peers(const float* z, const void* packed, void* workspace,
+                                       const uint64_t* dst_bases, int P, int64_t B, int64_t rows, int64_t N,
+                                       int64_t row0, int add_residual, uint32_t* status, void* stream);
 /* Barrier over P ranks: each rank publishes `epoch` into every rank's flag array (P uint32
  * each, zero-initialised peer memory; flag_ptrs: device array of the P arrays' addresses)
  * and waits until all P have published it. Stream-ordered: pushes enqueued before it on

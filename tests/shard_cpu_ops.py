@@ -126,6 +126,12 @@ class CpuStageOps:
         v = self._views(ws, B, rows, N)
         z.add_(O.linear(v["og"].float(), self._p(mod), "mha.linear_o"))
 
+    def triatt_finish_to(self, mod, z, ws, B, rows, N, row0, dst):
+        # gtk_triatt_finish_to_peers: z + update, pair-transposed into every rank's shard
+        v = self._views(ws, B, rows, N)
+        out = z + O.linear(v["og"].float(), self._p(mod), "mha.linear_o")
+        self.push_pair_transpose(out.contiguous(), dst, B, rows, N, len(dst.tensors), N, row0)
+
     # ------------------------------------------------------------------ data movement
     def copy_2d(self, dst, dpitch, src, spitch, width, height):
         assert dst.dtype == torch.uint8 and src.dtype == torch.uint8

@@ -82,13 +82,13 @@ def test_out_of_place_first_block():
     assert float((torch.cat(out, 1) - ref).abs().max()) == 0.0
 
 
-def _run_emulated_peer(z, mask, params, P, exchange="auto", k1_direct=False):
+def _run_emulated_peer(z, mask, params, P, exchange="auto", k1_direct=False, fused_transpose=True):
     from genie_tk.sharded import ShardedTrianglePairStack, connect_emulated, run_emulated
     st = _stack(params)
     B, N = z.shape[0], z.shape[1]
     R = N // P
     shards = [ShardedTrianglePairStack(st, P, r, stage_ops=CpuStageOps(), trimul_exchange=exchange, exchange="peer",
-                                       k1_direct=k1_direct) for r in range(P)]
+                                       k1_direct=k1_direct, fused_transpose=fused_transpose) for r in range(P)]
     connect_emulated(shards, B, N, z.device)
     zl = [z[:, r * R:(r + 1) * R].clone() for r in range(P)]
     run_emulated(shards, zl, mask)
@@ -106,6 +106,18 @@ def test_peer_exchange_matches_collectives(B, N, P, exchange, k1_direct):
     got = _run_emulated_peer(z, mask, params, P, exchange, k1_direct)
     ref = _run_emulated(z, mask, params, P, exchange)
     assert float((got - ref).abs().max()) <= 1e-5
+    err = (got - O.stack_forward(z, mask, params, no_heads=4)).abs()
+    assert float(err.max()) <= MAX_ABS and float(err.mean()) <= MEAN_ABS
+
+
+def test_fused_attention_transpose_matches_separate_pushes():
+    """With 128 rows per rank the attention blocks' output goes transposed straight into the
+    peers' shards (gtk_triatt_finish_to_peers); the result equals the separate K4e + transpose
+    push program and the oracle."""
+    z, mask, params = _problem(1, 256, 1)
+    got = _run_emulated_peer(z, mask, params, 2, "gather")
+    sep = _run_emulated_peer(z, mask, params, 2, "gather", fused_transpose=False)
+    assert float((got - sep).abs().max()) <= 1e-5
     err = (got - O.stack_forward(z, mask, params, no_heads=4)).abs()
     assert float(err.max()) <= MAX_ABS and float(err.mean()) <= MEAN_ABS
 
