@@ -29,7 +29,8 @@ wall time the step took, and ``value`` is the full-layer throughput estimated fr
 With --gpus N > 1 (torchrun, one process per GPU) the same N=1024 problem is row-sharded
 over the ranks (``genie_tk.sharded``). By default the exchanges (the gathered or
 channel-sharded planes of the multiplicative update, the triangle bias, the ending node's
-pair transposes) are push kernels that store straight into the peers' buffers over NVLink,
+pair transposes, which the attention blocks' K4e stores directly when a rank's rows are a
+multiple of 128) are push kernels that store straight into the peers' buffers over NVLink,
 with NCCL used only for set-up (``--exchange nccl`` runs them as NCCL collectives). The
 scaling is strong: ``value`` is the one problem's layers*N^2/s, timed on each rank's stream
 with CUDA events and reduced with MAX over ranks. After the timed region the ranks' output
@@ -499,7 +500,8 @@ def run_sharded(args, rank, world, device):
     stack = make_stack(L, device)
     so = TimedStageOps(CudaStageOps(device, push=args.push))
     shard = ShardedTrianglePairStack(stack, world, rank, stage_ops=so, trimul_exchange=args.trimul_exchange,
-                                     exchange=args.exchange, k1_direct=args.k1_direct)
+                                     exchange=args.exchange, k1_direct=args.k1_direct,
+                                     fused_transpose=not args.separate_transpose)
     if args.exchange == "peer":
         shard.connect(None, B, N, device)
     else:
@@ -585,7 +587,7 @@ def run_sharded(args, rank, world, device):
     peaks = load_peaks()
     stack_tflops = B * N * N * L * layer_flops(N) / (ms_per_step / 1e3) / 1e12
     stage_kernels = ("triatt_core", "trimul_contract", "trimul_project", "trimul_project_to", "trimul_finish",
-                     "triatt_project", "triatt_finish")
+                     "triatt_project", "triatt_finish", "triatt_finish_to")
     dom = max((k for k in breakdown if k in stage_kernels), key=lambda k: breakdown[k]["ms"])
     bound, work = kernel_work(dom, N, B)
     calls = sum(1 for lab, _ in labels if lab == dom)
@@ -607,6 +609,9 @@ def run_sharded(args, rank, world, device):
                            else "NCCL collectives"),
                        "trimul_exchange": shard.trimul_exchange, "exchange": args.exchange,
                        "k1_direct": bool(args.k1_direct and args.exchange == "peer" and shard.trimul_exchange == "channels"),
+                       "attention_transpose": ("fused into K4e's stores" if args.exchange == "peer" and
+                                               not args.separate_transpose and (N // world) % 128 == 0
+                                               else "separate push"),
                        "push": args.push,
                        "l2": "inputs larger than L2 (each shard is >= 64 MB fp32); no flush"},
             "stack_tflops": round(stack_tflops, 1),
@@ -825,6 +830,8 @@ def main():
     ap.add_argument("--op", default="stack", choices=["stack", "transition", "embed"],
                     help="stack: the BASELINE workload (default); transition / embed: the pair-transition or "
                          "pair-embedding kernels alone")
+    ap.add_argument("--separate-transpose", action="store_true",
+                    help="peer exchange: K4e then a transpose push, instead of K4e storing transposed into the peers")
     ap.add_argument("--push", default="kernel", choices=["kernel", "dma"],
                     help="peer exchanges: slab pushes with the push kernel or the copy engines")
     ap.add_argument("--k1-direct", action="store_true",

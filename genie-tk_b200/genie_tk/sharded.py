@@ -637,7 +637,7 @@ class TimedStageOps:
 
     KERNELS = ("trimul_project", "trimul_project_to", "trimul_contract", "trimul_finish", "triatt_project",
                "triatt_core",
-               "triatt_finish", "copy_2d", "copy_3d", "pair_transpose_pack", "push_3d", "push_pair_transpose")
+               "triatt_finish", "triatt_finish_to", "copy_2d", "copy_3d", "pair_transpose_pack", "push_3d", "push_pair_transpose")
 
     def __init__(self, inner, hook=None):
         self.inner = inner
