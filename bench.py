@@ -64,7 +64,7 @@ def kernel_work(name: str, N: int, B: int = 1):
     P = B * N * N
     if name == "triatt_core":
         return "tensor", 4.0 * B * N ** 3 * 4 * 32          # QK^T + PV, H=4, d=32
-    if name == "trimul_contract":
+    if name in ("trimul_contract", "trimul_contract_to"):
         return "tensor", 2.0 * B * N ** 3 * 128             # 128 channel GEMMs of N^3
     if name in ("trimul_project", "trimul_project_to"):
         return "hbm", P * (512 + 4 + 2 * 128 * 2)           # z fp32 + mask in, a, b fp16 out
@@ -72,7 +72,7 @@ def kernel_work(name: str, N: int, B: int = 1):
         return "hbm", P * (128 * 2 + 512 + 512)             # x fp16 + z fp32 in, z fp32 out
     if name == "triatt_project":
         return "hbm", P * (512 + 4 * 128 * 2 + 4 * 2)       # z in; q, k, v, g fp16 + bias out
-    if name == "triatt_finish":
+    if name in ("triatt_finish", "triatt_finish_to"):
         return "hbm", P * (128 * 2 + 512 + 512)             # og fp16 + z in, z out
     raise KeyError(name)
 
@@ -501,7 +501,7 @@ def run_sharded(args, rank, world, device):
     so = TimedStageOps(CudaStageOps(device, push=args.push))
     shard = ShardedTrianglePairStack(stack, world, rank, stage_ops=so, trimul_exchange=args.trimul_exchange,
                                      exchange=args.exchange, k1_direct=args.k1_direct,
-                                     fused_transpose=not args.separate_transpose)
+                                     fused_transpose=not args.separate_transpose, fused_x=not args.separate_x)
     if args.exchange == "peer":
         shard.connect(None, B, N, device)
     else:
@@ -587,7 +587,7 @@ def run_sharded(args, rank, world, device):
     peaks = load_peaks()
     stack_tflops = B * N * N * L * layer_flops(N) / (ms_per_step / 1e3) / 1e12
     stage_kernels = ("triatt_core", "trimul_contract", "trimul_project", "trimul_project_to", "trimul_finish",
-                     "triatt_project", "triatt_finish", "triatt_finish_to")
+                     "triatt_project", "triatt_finish", "triatt_finish_to", "trimul_contract_to")
     dom = max((k for k in breakdown if k in stage_kernels), key=lambda k: breakdown[k]["ms"])
     bound, work = kernel_work(dom, N, B)
     calls = sum(1 for lab, _ in labels if lab == dom)
@@ -612,6 +612,9 @@ def run_sharded(args, rank, world, device):
                        "attention_transpose": ("fused into K4e's stores" if args.exchange == "peer" and
                                                not args.separate_transpose and (N // world) % 128 == 0
                                                else "separate push"),
+                       "x_scatter": ("fused into K2's stores" if args.exchange == "peer" and not args.separate_x and
+                                     shard.trimul_exchange == "channels" and (N // world) % 128 == 0
+                                     else "separate push"),
                        "push": args.push,
                        "l2": "inputs larger than L2 (each shard is >= 64 MB fp32); no flush"},
             "stack_tflops": round(stack_tflops, 1),
@@ -830,6 +833,8 @@ def main():
     ap.add_argument("--op", default="stack", choices=["stack", "transition", "embed"],
                     help="stack: the BASELINE workload (default); transition / embed: the pair-transition or "
                          "pair-embedding kernels alone")
+    ap.add_argument("--separate-x", action="store_true",
+                    help="peer exchange, channel shards: K2 then the x push, instead of K2 storing into the owners")
     ap.add_argument("--separate-transpose", action="store_true",
                     help="peer exchange: K4e then a transpose push, instead of K4e storing transposed into the peers")
     ap.add_argument("--push", default="kernel", choices=["kernel", "dma"],

@@ -80,8 +80,14 @@ __global__ void __launch_bounds__(256)
 }
 
 // ---------------------------------------------------------------------------------------
-// C = A W^T (+ epilogue): A [M][K] (pitch lda), W [n_out][K] (pitch ldw), fp32. 64 x 64
-// output tile per CTA, K in steps of 16 through shared memory, 4 x 4 outputs per thread.
+// C = A W^T (+ epilogue): A [M][K] (pitch lda), W [n_out][K] (pitch ldw), fp32 in memory.
+// Tensor cores: mma.sync m16n8k8 with TF32 operands and fp32 accumulation. kSplit = 1 rounds
+// each operand to TF32 (10-bit mantissa, the precision class of the tuned kernels' fp16
+// operands); kSplit = 3 splits each operand into a TF32 head and a TF32 tail, x = hi + lo,
+// and accumulates hi*hi + hi*lo + lo*hi (3xTF32: products to ~2^-22, fp32-level results).
+// CTA tile 128 x 128 (8 warps of 32 x 64), K in steps of 32 through shared memory (double
+// buffered; the next step's global loads -- 16-byte vectors when the pitches allow -- are in
+// flight while this one multiplies).
 // ---------------------------------------------------------------------------------------
 enum EpiMode : int { kStore = 0, kRelu = 1, kGateRes = 2, kRes = 3, kResMask = 4 };
 
@@ -99,10 +105,12 @@ struct Epi {
   DropArgs drop;      // kGateRes / kRes: channel dropout (keep == nullptr: none)
 };
 
-constexpr int kBM = 64, kBN = 64, kBK = 16;
+constexpr int kBM = 128, kBN = 128, kBK = 32;
+constexpr int kBP = kBK + 4;  // shared pitch (floats): conflict-free fragment loads
+constexpr int kGemmSmem = 2 * (kBM + kBN) * kBP * 4;  // two stages of the A and W tiles
 
 // What the GEMM applies to A's elements as it loads them: nothing, a LayerNorm of each row
-// (the CTA computes the 64 rows' mean and 1/std first), or a sigmoid gate.
+// (the CTA computes its rows' mean and 1/std first), a sigmoid gate, or fp16 A.
 enum ProMode : int { kProNone = 0, kProLn = 1, kProGate = 2, kProHalf = 3 };
 
 struct Pro {
@@ -114,20 +122,37 @@ struct Pro {
   const __half* ah;    // kProHalf: A is fp16 (this pointer, pitch lda) instead of fp32
 };
 
-template <int kPro>
-__global__ void __launch_bounds__(256)
+__device__ __forceinline__ uint32_t tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
+__device__ __forceinline__ void mma_tf32(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+template <int kPro, int kSplit>
+__global__ void __launch_bounds__(256, kSplit == 1 ? 2 : 1)
     gemm_kernel(const float* __restrict__ A, int64_t M, int K, int64_t lda, const float* __restrict__ W, int n_out,
-                int64_t ldw, const Epi e, const Pro pro) {
-  __shared__ __align__(16) float As[kBK][kBM + 4];
-  __shared__ __align__(16) float Ws[kBK][kBN + 4];
+                int64_t ldw, const Epi e, const Pro pro, int n_tiles_n, int vec) {
+  extern __shared__ __align__(16) float gsm[];
+  float (*As)[kBM][kBP] = reinterpret_cast<float (*)[kBM][kBP]>(gsm);
+  float (*Ws)[kBN][kBP] = reinterpret_cast<float (*)[kBN][kBP]>(gsm + 2 * kBM * kBP);
   __shared__ float mean_s[kPro == kProLn ? kBM : 1], rstd_s[kPro == kProLn ? kBM : 1];
-  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
-  const int64_t m0 = static_cast<int64_t>(blockIdx.x) * kBM;
-  const int n0 = blockIdx.y * kBN;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int wm = warp & 3, wn = warp >> 2, g = lane >> 2, t = lane & 3;
+  const int64_t tile = blockIdx.x;
+  const int nt_idx = static_cast<int>(tile % n_tiles_n);  // the N tiles of one M block run side by side
+  const int64_t m0 = (tile / n_tiles_n) * kBM;
+  const int n0 = nt_idx * kBN;
   if constexpr (kPro == kProLn) {
-    const int lane = tid & 31;
     const float inv = 1.f / static_cast<float>(K);
-    for (int r = tid >> 5; r < kBM; r += 8) {
+    for (int r = warp; r < kBM; r += 8) {
       const int64_t m = m0 + r;
       float mean = 0.f, rstd = 0.f;
       if (m < M) {
@@ -149,72 +174,180 @@ __global__ void __launch_bounds__(256)
     }
     __syncthreads();
   }
-  float acc[4][4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
-  for (int k0 = 0; k0 < K; k0 += kBK) {
+  // global -> registers. Thread: rows (tid >> 3) + 32 u, columns 4 (tid & 7) .. +3 of the
+  // 32-column step (16-byte vectors when `vec`: pitches and bases 16-byte aligned, K % 4 == 0).
+  float ra[4][4], rw[4][4];
+  const int lr = tid >> 3, lc = (tid & 7) * 4;
+  auto xform = [&](float x, int64_t m, int r, int k) {
+    if constexpr (kPro == kProLn) x = fmaf((x - mean_s[r]) * rstd_s[r], pro.gamma[k], pro.beta[k]);
+    if constexpr (kPro == kProGate) x *= sigmoid_f(pro.gate[m * pro.ldg + k]);
+    return x;
+  };
+  auto load = [&](int k0) {
+    const int k = k0 + lc;
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-      const int idx = tid + u * 256, r = idx >> 4, kk = idx & 15;
+      const int r = lr + 32 * u;
       const int64_t m = m0 + r;
-      const int k = k0 + kk, n = n0 + r;
-      float x = 0.f;
-      if (m < M && k < K) {
-        if constexpr (kPro == kProHalf)
-          x = __half2float(pro.ah[m * lda + k]);
-        else
-          x = A[m * lda + k];
-        if constexpr (kPro == kProLn) x = fmaf((x - mean_s[r]) * rstd_s[r], pro.gamma[k], pro.beta[k]);
-        if constexpr (kPro == kProGate) x *= sigmoid_f(pro.gate[m * pro.ldg + k]);
+      const int n = n0 + r;
+      float x[4] = {0.f, 0.f, 0.f, 0.f}, y[4] = {0.f, 0.f, 0.f, 0.f};
+      if (m < M) {
+        if (vec && k < K) {
+          if constexpr (kPro == kProHalf) {
+            const uint2 h = *reinterpret_cast<const uint2*>(pro.ah + m * lda + k);
+            const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&h.x));
+            const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&h.y));
+            x[0] = f0.x, x[1] = f0.y, x[2] = f1.x, x[3] = f1.y;
+          } else {
+            const float4 f = *reinterpret_cast<const float4*>(A + m * lda + k);
+            x[0] = f.x, x[1] = f.y, x[2] = f.z, x[3] = f.w;
+          }
+        } else {
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            if (k + q < K) {
+              if constexpr (kPro == kProHalf)
+                x[q] = __half2float(pro.ah[m * lda + k + q]);
+              else
+                x[q] = A[m * lda + k + q];
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) x[q] = k + q < K ? xform(x[q], m, r, k + q) : 0.f;
       }
-      As[kk][r] = x;
-      Ws[kk][r] = (n < n_out && k < K) ? W[static_cast<int64_t>(n) * ldw + k] : 0.f;
+      if (n < n_out) {
+        if (vec && k < K) {
+          const float4 f = *reinterpret_cast<const float4*>(W + static_cast<int64_t>(n) * ldw + k);
+          y[0] = f.x, y[1] = f.y, y[2] = f.z, y[3] = f.w;
+        } else {
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            if (k + q < K) y[q] = W[static_cast<int64_t>(n) * ldw + k + q];
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        ra[u][q] = x[q];
+        rw[u][q] = y[q];
+      }
     }
-    __syncthreads();
+  };
+  auto store = [&](int buf) {
 #pragma unroll
-    for (int kk = 0; kk < kBK; ++kk) {
-      const float4 a = *reinterpret_cast<const float4*>(&As[kk][ty * 4]);
-      const float4 w = *reinterpret_cast<const float4*>(&Ws[kk][tx * 4]);
-      const float av[4] = {a.x, a.y, a.z, a.w}, wv[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], wv[j], acc[i][j]);
+    for (int u = 0; u < 4; ++u) {
+      const int r = lr + 32 * u;
+      *reinterpret_cast<float4*>(&As[buf][r][lc]) = make_float4(ra[u][0], ra[u][1], ra[u][2], ra[u][3]);
+      *reinterpret_cast<float4*>(&Ws[buf][r][lc]) = make_float4(rw[u][0], rw[u][1], rw[u][2], rw[u][3]);
     }
+  };
+  float acc[2][8][4];
+#pragma unroll
+  for (int a = 0; a < 2; ++a)
+#pragma unroll
+    for (int b = 0; b < 8; ++b) acc[a][b][0] = acc[a][b][1] = acc[a][b][2] = acc[a][b][3] = 0.f;
+  load(0);
+  store(0);
+  __syncthreads();
+  int buf = 0;
+  for (int k0 = 0; k0 < K; k0 += kBK, buf ^= 1) {
+    const bool more = k0 + kBK < K;
+    if (more) load(k0 + kBK);
+#pragma unroll
+    for (int k8 = 0; k8 < kBK; k8 += 8) {
+      uint32_t ah[2][4], al[2][4];
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+        const int r = wm * 32 + mt * 16 + g;
+        const float x[4] = {As[buf][r][k8 + t], As[buf][r + 8][k8 + t], As[buf][r][k8 + t + 4],
+                            As[buf][r + 8][k8 + t + 4]};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          ah[mt][q] = tf32_rna(x[q]);
+          if constexpr (kSplit == 3) al[mt][q] = tf32_rna(x[q] - __uint_as_float(ah[mt][q]));
+        }
+      }
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        const int c = wn * 64 + nt * 8 + g;
+        const float y0 = Ws[buf][c][k8 + t], y1 = Ws[buf][c][k8 + t + 4];
+        const uint32_t bh0 = tf32_rna(y0), bh1 = tf32_rna(y1);
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+          if constexpr (kSplit == 3) {
+            const uint32_t bl0 = tf32_rna(y0 - __uint_as_float(bh0)), bl1 = tf32_rna(y1 - __uint_as_float(bh1));
+            mma_tf32(acc[mt][nt], al[mt], bh0, bh1);
+            mma_tf32(acc[mt][nt], ah[mt], bl0, bl1);
+          }
+          mma_tf32(acc[mt][nt], ah[mt], bh0, bh1);
+        }
+      }
+    }
+    if (more) store(buf ^ 1);  // buf ^ 1 was last read before the previous barrier
     __syncthreads();
   }
-  const int64_t NN = e.N * e.N;
+  // the tile through shared memory (the operand stages are free now), then row by row: a warp
+  // owns 16 rows, a lane 4 consecutive columns, so each row leaves as 512 contiguous bytes
+  float (*Cs)[kBN + 4] = reinterpret_cast<float (*)[kBN + 4]>(gsm);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int64_t m = m0 + ty * 4 + i;
-    if (m >= M) continue;
-    uint4 keep = make_uint4(0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu);
-    const bool drop = e.drop.keep != nullptr && (e.mode == kGateRes || e.mode == kRes);
-    if (drop) {
-      const int64_t b = m / NN, rem = m - b * NN, r = rem / e.N, j = rem - r * e.N;
-      keep = __ldg(e.drop.keep + b * e.drop.ld + (e.drop.by_row ? r : j));
-    }
-    const int64_t row = (e.mode == kGateRes || e.mode == kRes) ? frame_row(m, e.N, e.tr) : m;
+  for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int n = n0 + tx * 4 + j;
-      if (n >= n_out) continue;
-      float v = acc[i][j] + (e.bias ? e.bias[n] : 0.f);
-      if (e.mode == kStore) {
-        e.out[m * e.ldo + n] = v;
-      } else if (e.mode == kRelu) {
-        e.out[m * e.ldo + n] = fmaxf(v, 0.f);
-      } else if (e.mode == kResMask) {
-        const float zr = e.z ? e.z[m * e.ldo + n] : 0.f;
-        e.out[m * e.ldo + n] = (zr + v) * (e.mask ? e.mask[m] : 1.f);
-      } else {
-        if (e.mode == kGateRes) v *= sigmoid_f(e.gate[m * e.ldg + n]);
-        if (drop) v *= ((drop_word(keep, n >> 5) >> (n & 31)) & 1u) ? e.drop.scale : 0.f;
-        const float zr = e.z ? e.z[row * e.ldo + n] : 0.f;
-        e.out[row * e.ldo + n] = zr + v;
+    for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+        *reinterpret_cast<float2*>(&Cs[wm * 32 + mt * 16 + g + h * 8][wn * 64 + nt * 8 + 2 * t]) =
+            make_float2(acc[mt][nt][2 * h], acc[mt][nt][2 * h + 1]);
+  __syncthreads();
+  const int c0 = lane * 4, n = n0 + c0;
+  if (n >= n_out) return;
+  const bool full = n + 3 < n_out;
+  float bv[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) bv[q] = (e.bias && n + q < n_out) ? e.bias[n + q] : 0.f;
+  const bool vec_out = full && (e.ldo % 4 == 0) && !(reinterpret_cast<uintptr_t>(e.out) & 15);
+  for (int rr = 0; rr < 16; ++rr) {
+    const int r = warp * 16 + rr;
+    const int64_t m = m0 + r;
+    if (m >= M) break;
+    const float4 cv = *reinterpret_cast<const float4*>(&Cs[r][c0]);
+    float v[4] = {cv.x + bv[0], cv.y + bv[1], cv.z + bv[2], cv.w + bv[3]};
+    int64_t row = m;
+    float mul = 1.f;
+    const float* zr = nullptr;
+    if (e.mode == kRelu) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) v[q] = fmaxf(v[q], 0.f);
+    } else if (e.mode == kResMask) {
+      zr = e.z;
+      mul = e.mask ? e.mask[m] : 1.f;
+    } else if (e.mode == kGateRes || e.mode == kRes) {
+      row = frame_row(m, e.N, e.tr);
+      zr = e.z;
+      if (e.mode == kGateRes)
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if (n + q < n_out) v[q] *= sigmoid_f(e.gate[m * e.ldg + n + q]);
+      if (e.drop.keep != nullptr) {
+        const int64_t NN = e.N * e.N;
+        const int64_t b = m / NN, rem = m - b * NN, ri = rem / e.N, j = rem - ri * e.N;
+        const uint4 keep = __ldg(e.drop.keep + b * e.drop.ld + (e.drop.by_row ? ri : j));
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int nq = n + q;
+          v[q] *= ((drop_word(keep, nq >> 5) >> (nq & 31)) & 1u) ? e.drop.scale : 0.f;
+        }
       }
+    }
+    float* o = e.out + row * e.ldo + n;
+    if (vec_out) {
+      if (zr) {
+        const float4 zv = *reinterpret_cast<const float4*>(zr + row * e.ldo + n);
+        v[0] += zv.x, v[1] += zv.y, v[2] += zv.z, v[3] += zv.w;
+      }
+      *reinterpret_cast<float4*>(o) = make_float4(v[0] * mul, v[1] * mul, v[2] * mul, v[3] * mul);
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        if (n + q < n_out) o[q] = ((zr ? zr[row * e.ldo + n + q] : 0.f) + v[q]) * mul;
     }
   }
 }
@@ -391,13 +524,27 @@ static int launch_ln(const float* x, const float* gamma, const float* beta, floa
   return check_launch("general ln_kernel");
 }
 
+// The general blocks' GEMMs (TF32 operands) and the fp32-accurate form (3xTF32) of
+// gtk_linear / gtk_layernorm_linear, with any prologue.
+template <int kPro, int kSplit>
+static int launch_gemm_t(const float* A, int64_t M, int K, int64_t lda, const float* W, int n_out, int64_t ldw,
+                         const Epi& e, const Pro& pro, cudaStream_t st, const char* what) {
+  const int64_t mt = (M + kBM - 1) / kBM, ntn = (n_out + kBN - 1) / kBN;
+  if (mt * ntn > 2147483647) return fail(GTK_ERR_INVALID_ARG, std::string(what) + ": too many rows");
+  const void* abase = kPro == kProHalf ? static_cast<const void*>(pro.ah) : static_cast<const void*>(A);
+  const uintptr_t amask = kPro == kProHalf ? 7 : 15;
+  const int vec = (K % 4 == 0) && (lda % 4 == 0) && (ldw % 4 == 0) && !(reinterpret_cast<uintptr_t>(abase) & amask) &&
+                  !(reinterpret_cast<uintptr_t>(W) & 15);
+  const void* kern = reinterpret_cast<const void*>(gemm_kernel<kPro, kSplit>);
+  if (int e2 = ensure_smem(kern, kGemmSmem)) return e2;
+  gemm_kernel<kPro, kSplit><<<static_cast<unsigned>(mt * ntn), 256, kGemmSmem, st>>>(A, M, K, lda, W, n_out, ldw, e,
+                                                                                  pro, static_cast<int>(ntn), vec);
+  return check_launch(what);
+}
+
 static int launch_gemm(const float* A, int64_t M, int K, int64_t lda, const float* W, int n_out, int64_t ldw,
                        const Epi& e, cudaStream_t st) {
-  const int64_t mt = (M + kBM - 1) / kBM;
-  if (mt > 2147483647) return fail(GTK_ERR_INVALID_ARG, "general gemm: too many rows");
-  dim3 grid(static_cast<unsigned>(mt), static_cast<unsigned>((n_out + kBN - 1) / kBN));
-  gemm_kernel<kProNone><<<grid, 256, 0, st>>>(A, M, K, lda, W, n_out, ldw, e, Pro{});
-  return check_launch("general gemm_kernel");
+  return launch_gemm_t<kProNone, 1>(A, M, K, lda, W, n_out, ldw, e, Pro{}, st, "general gemm_kernel");
 }
 
 static Epi epi(int mode, const float* bias, float* out, int64_t ldo) {
@@ -730,11 +877,8 @@ int triatt_forward(int starting, const float* z, const float* mask, const void* 
     e.drop = drop;
     Pro pro{};
     pro.ah = reinterpret_cast<const __half*>(w4 + off[4]);
-    const int64_t mt = (P + kBM - 1) / kBM;
-    if (mt > 2147483647) return fail(GTK_ERR_INVALID_ARG, "triatt: too many rows");
-    const dim3 grid(static_cast<unsigned>(mt), static_cast<unsigned>((c_in + kBN - 1) / kBN));
-    gemm_kernel<kProHalf><<<grid, 256, 0, st>>>(nullptr, P, 128, 128, wpad, c_in, 128, e, pro);
-    return check_launch("general gemm_kernel (tuned-core output)");
+      return launch_gemm_t<kProHalf, 1>(nullptr, P, 128, 128, wpad, c_in, 128, e, pro, st,
+                                      "general gemm_kernel (tuned-core output)");
   }
   // the attention core on the tensor cores: q, k, v and the bias as fp16 planes
   __half* qh = reinterpret_cast<__half*>(ws + w.q);
@@ -762,11 +906,8 @@ int triatt_forward(int starting, const float* z, const float* mask, const void* 
   Pro pro{};
   pro.gate = Y + 3 * hd;
   pro.ldg = ldy;
-  const int64_t mt = (P + kBM - 1) / kBM;
-  if (mt > 2147483647) return fail(GTK_ERR_INVALID_ARG, "triatt: too many rows");
-  const dim3 grid(static_cast<unsigned>(mt), static_cast<unsigned>((c_in + kBN - 1) / kBN));
-  gemm_kernel<kProGate><<<grid, 256, 0, st>>>(og, P, hd, hd, pk + L.wo, c_in, hd, e, pro);
-  return check_launch("general gemm_kernel (gated output)");
+  return launch_gemm_t<kProGate, 1>(og, P, hd, hd, pk + L.wo, c_in, hd, e, pro, st,
+                                    "general gemm_kernel (gated output)");
 }
 
 // ----------------------------------- pair transition -----------------------------------
@@ -877,19 +1018,15 @@ int launch_linear(int pro_mode, const float* x, const float* weight, const float
                   int64_t D_in, int64_t D_out, const gtk::gen::Pro& pro, void* stream) {
   using namespace gtk;
   using namespace gtk::gen;
-  const int64_t mt = (rows + kBM - 1) / kBM;
-  if (mt > 2147483647) return fail(GTK_ERR_INVALID_ARG, "linear: too many rows");
-  const dim3 grid(static_cast<unsigned>(mt), static_cast<unsigned>((D_out + kBN - 1) / kBN));
   const Epi e = epi(kStore, bias, out, D_out);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int K = static_cast<int>(D_in), n_out = static_cast<int>(D_out);
+  // 3xTF32: these entry points promise fp32 results
   if (pro_mode == kProLn)
-    gemm_kernel<kProLn><<<grid, 256, 0, st>>>(x, rows, K, D_in, weight, n_out, D_in, e, pro);
-  else if (pro_mode == kProGate)
-    gemm_kernel<kProGate><<<grid, 256, 0, st>>>(x, rows, K, D_in, weight, n_out, D_in, e, pro);
-  else
-    gemm_kernel<kProNone><<<grid, 256, 0, st>>>(x, rows, K, D_in, weight, n_out, D_in, e, pro);
-  return check_launch("linear gemm_kernel");
+    return launch_gemm_t<kProLn, 3>(x, rows, K, D_in, weight, n_out, D_in, e, pro, st, "linear gemm_kernel");
+  if (pro_mode == kProGate)
+    return launch_gemm_t<kProGate, 3>(x, rows, K, D_in, weight, n_out, D_in, e, pro, st, "linear gemm_kernel");
+  return launch_gemm_t<kProNone, 3>(x, rows, K, D_in, weight, n_out, D_in, e, pro, st, "linear gemm_kernel");
 }
 
 }  // namespace

@@ -440,11 +440,21 @@ struct K2Bars {
 };
 static_assert(sizeof(K2Bars) <= 256, "K2 barrier block");
 
-template <bool kOutgoing>
+// Destinations of the peer form of K2 (the channel-sharded contraction of a row-sharded
+// stack): the x tile of rows it*128.. goes to their owner p = it*128 / R, into p's x planes
+// [B][R][C_dst][ld] at channel c_off + c. map[p] addresses them as (col, channel, row, b),
+// box 64 columns x 1 channel x 128 rows: plain TMA stores into the peer's memory.
+constexpr int kMaxK2Peers = 8;
+struct K2Peers {
+  CUtensorMap map[kMaxK2Peers];
+  int R, c_off;
+};
+
+template <bool kOutgoing, bool kPeer>
 __global__ void __launch_bounds__(k2::kThreads, 1)
     trimul_contract_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap b_map,
                            const __grid_constant__ CUtensorMap x_map, int C, int K, int n_jt, int n_it, int n_tiles,
-                           float out_scale, uint32_t* status) {
+                           float out_scale, uint32_t* status, const __grid_constant__ K2Peers peers) {
   using namespace k2;
   extern __shared__ uint8_t dsmem[];
   uint8_t* smem = align1024(dsmem);
@@ -620,7 +630,12 @@ __global__ void __launch_bounds__(k2::kThreads, 1)
           if (issuer) {
             iok = mbar_wait(&bars->o_ready[ob], (half >> 1) & 1, guard, status, kStatusTimeoutConsumer);
             if (iok) {
-              tma_store_4d(&x_map, stage, jt * 256 + hh * 64, c, it * 128, b);
+              if constexpr (kPeer) {
+                const int p = (it * 128) / peers.R;
+                tma_store_4d(&peers.map[p], stage, jt * 256 + hh * 64, peers.c_off + c, it * 128 - p * peers.R, b);
+              } else {
+                tma_store_4d(&x_map, stage, jt * 256 + hh * 64, c, it * 128, b);
+              }
               tma_store_commit();
               tma_store_wait_read();
               mbar_arrive(&bars->o_free[ob]);
@@ -1168,23 +1183,76 @@ int gtk_trimul_contract(int outgoing, const void* a_planes, const void* b_planes
     if (int e = make_plane_map(&bm, b_planes, B, K, C, Nj, ldb, 64, 1, 64, 128)) return e;
   }
   if (int e = make_plane_map(&xm, x_planes, B, M, C, Nj, ldx, 64, 1, 128, 128)) return e;
-  const void* kern = outgoing ? reinterpret_cast<const void*>(trimul_contract_kernel<true>)
-                              : reinterpret_cast<const void*>(trimul_contract_kernel<false>);
+  const void* kern = outgoing ? reinterpret_cast<const void*>(trimul_contract_kernel<true, false>)
+                              : reinterpret_cast<const void*>(trimul_contract_kernel<false, false>);
   if (int e = ensure_smem(kern, k2::kSmem)) return e;
   const int64_t n_jt = (Nj + 255) / 256, n_it = (M + 127) / 128;
   const int64_t n_tiles = n_jt * n_it * B * C;
   if (n_tiles > 2147483647) return fail(GTK_ERR_INVALID_ARG, "trimul_contract: too many tiles");
   const int grid = static_cast<int>(n_tiles < num_sms() ? n_tiles : num_sms());
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const K2Peers none{};
   if (outgoing)
-    trimul_contract_kernel<true><<<grid, k2::kThreads, k2::kSmem, st>>>(
+    trimul_contract_kernel<true, false><<<grid, k2::kThreads, k2::kSmem, st>>>(
         am, bm, xm, static_cast<int>(C), static_cast<int>(K), static_cast<int>(n_jt), static_cast<int>(n_it),
-        static_cast<int>(n_tiles), out_scale, status);
+        static_cast<int>(n_tiles), out_scale, status, none);
   else
-    trimul_contract_kernel<false><<<grid, k2::kThreads, k2::kSmem, st>>>(
+    trimul_contract_kernel<false, false><<<grid, k2::kThreads, k2::kSmem, st>>>(
         am, bm, xm, static_cast<int>(C), static_cast<int>(K), static_cast<int>(n_jt), static_cast<int>(n_it),
-        static_cast<int>(n_tiles), out_scale, status);
+        static_cast<int>(n_tiles), out_scale, status, none);
   return check_launch("trimul_contract_kernel");
+}
+
+int gtk_trimul_contract_to_peers(int outgoing, const void* a_planes, const void* b_planes, const uint64_t* dst_bases,
+                                 int P, int64_t B, int64_t C, int64_t M, int64_t Nj, int64_t K, int64_t lda,
+                                 int64_t ldb, int64_t C_dst, int64_t c_off, int64_t ld_dst, float out_scale,
+                                 uint32_t* status, void* stream) {
+  if (P < 1 || P > kMaxK2Peers || !dst_bases) return fail(GTK_ERR_INVALID_ARG, "trimul_contract_to_peers: bad P");
+  if (!dims_ok(B) || !dims_ok(C) || !dims_ok(M) || !dims_ok(Nj) || !dims_ok(K) || B * C > 65535 * 1024 ||
+      c_off < 0 || c_off + C > C_dst || M % P)
+    return fail(GTK_ERR_INVALID_ARG, "trimul_contract_to_peers: bad sizes");
+  const int64_t R = M / P;
+  if (R % 128) return fail(GTK_ERR_UNSUPPORTED, "trimul_contract_to_peers: rows per rank must be a multiple of 128");
+  if (lda % 8 || ldb % 8 || ld_dst % 8) return fail(GTK_ERR_ALIGNMENT, "trimul_contract_to_peers: pitches must be multiples of 8");
+  if (outgoing ? (lda < K || ldb < K) : (lda < M || ldb < Nj)) return fail(GTK_ERR_INVALID_ARG, "pitch too small");
+  if (ld_dst < Nj) return fail(GTK_ERR_INVALID_ARG, "trimul_contract_to_peers: ld_dst < Nj");
+  if (int e = check_ptr(a_planes, "a_planes")) return e;
+  if (int e = check_ptr(b_planes, "b_planes")) return e;
+  for (int p = 0; p < P; ++p)
+    if (int e = check_ptr(reinterpret_cast<const void*>(dst_bases[p]), "peer x planes")) return e;
+  if (int e = check_device()) return e;
+  CUtensorMap am, bm;
+  if (outgoing) {
+    if (int e = make_plane_map(&am, a_planes, B, M, C, K, lda, 64, 1, 128, 128)) return e;
+    if (int e = make_plane_map(&bm, b_planes, B, Nj, C, K, ldb, 64, 1, 256, 128)) return e;
+  } else {
+    if (int e = make_plane_map(&am, a_planes, B, K, C, M, lda, 64, 1, 64, 128)) return e;
+    if (int e = make_plane_map(&bm, b_planes, B, K, C, Nj, ldb, 64, 1, 64, 128)) return e;
+  }
+  K2Peers peers{};
+  peers.R = static_cast<int>(R);
+  peers.c_off = static_cast<int>(c_off);
+  for (int p = 0; p < P; ++p)
+    if (int e = make_plane_map(&peers.map[p], reinterpret_cast<const void*>(dst_bases[p]), B, R, C_dst, Nj, ld_dst, 64,
+                               1, 128, 128))
+      return e;
+  const void* kern = outgoing ? reinterpret_cast<const void*>(trimul_contract_kernel<true, true>)
+                              : reinterpret_cast<const void*>(trimul_contract_kernel<false, true>);
+  if (int e = ensure_smem(kern, k2::kSmem)) return e;
+  const int64_t n_jt = (Nj + 255) / 256, n_it = M / 128;
+  const int64_t n_tiles = n_jt * n_it * B * C;
+  if (n_tiles > 2147483647) return fail(GTK_ERR_INVALID_ARG, "trimul_contract_to_peers: too many tiles");
+  const int grid = static_cast<int>(n_tiles < num_sms() ? n_tiles : num_sms());
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (outgoing)
+    trimul_contract_kernel<true, true><<<grid, k2::kThreads, k2::kSmem, st>>>(
+        am, bm, am, static_cast<int>(C), static_cast<int>(K), static_cast<int>(n_jt), static_cast<int>(n_it),
+        static_cast<int>(n_tiles), out_scale, status, peers);
+  else
+    trimul_contract_kernel<false, true><<<grid, k2::kThreads, k2::kSmem, st>>>(
+        am, bm, am, static_cast<int>(C), static_cast<int>(K), static_cast<int>(n_jt), static_cast<int>(n_it),
+        static_cast<int>(n_tiles), out_scale, status, peers);
+  return check_launch("trimul_contract_kernel (to peers)");
 }
 
 }  // extern "C"

@@ -119,6 +119,8 @@ _SIGNATURES = {
     "gtk_attn_core_bias_bytes": (c_size, [c_i64, c_i64, c_int]),
     "gtk_attn_core_pack": (c_int, [c_vp, c_i64, c_i64, c_int, c_int, ctypes.c_float, c_vp, c_vp]),
     "gtk_attn_core_pack_bias": (c_int, [c_vp, c_i64, c_i64, c_int, c_vp, c_vp]),
+    "gtk_trimul_contract_to_peers": (c_int, [c_int, c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_i64,
+                                             c_i64, c_i64, c_i64, c_i64, c_i64, ctypes.c_float, c_vp, c_vp]),
     "gtk_triatt_finish_to_peers": (c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_int, c_vp,
                                            c_vp]),
     "gtk_mha_forward": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_int, c_int,

@@ -125,6 +125,16 @@ class CudaStageOps:
         self._chk(self.lib.gtk_triatt_finish(1, P(z), P(mod.packed_weights(self.device)), P(ws), P(z), 1, B, rows,
                                              N, P(self.status), self._s()), "gtk_triatt_finish")
 
+    def trimul_contract_to(self, outgoing, a, b, B, M, Nj, K, lda, ldb, xs, channels, dst: "PeerBuffer", c_off,
+                           ld_dst):
+        """K2 of the channel-sharded exchange with the x scatter fused into its stores: the x
+        tiles of rows owned by rank p go straight into p's x planes at channels c_off.."""
+        P = ops._ptr
+        bases = (ctypes.c_uint64 * len(dst.addrs))(*dst.addrs)
+        self._chk(self.lib.gtk_trimul_contract_to_peers(int(outgoing), P(a), P(b), bases, len(dst.addrs), B, channels,
+                                                        M, Nj, K, lda, ldb, C, c_off, ld_dst, xs, P(self.status),
+                                                        self._s()), "gtk_trimul_contract_to_peers")
+
     def triatt_finish_to(self, mod, z, ws, B, rows, N, row0, dst: "PeerBuffer"):
         """K4e with the pair-grid transpose fused into its stores: z + update, transposed,
         straight into every rank's shard of ``dst``."""
@@ -215,7 +225,7 @@ class ShardedTrianglePairStack:
 
     def __init__(self, stack: TrianglePairStack, world: int, rank: int, stage_ops=None,
                  trimul_exchange: str = "auto", exchange: str = "nccl", k1_direct: bool = False,
-                 push: str = "kernel", fused_transpose: bool = True):
+                 push: str = "kernel", fused_transpose: bool = True, fused_x: bool = True):
         if trimul_exchange not in ("auto", "gather", "channels"):
             raise ValueError(f"trimul_exchange must be auto, gather or channels, not {trimul_exchange!r}")
         if exchange not in ("nccl", "peer"):
@@ -238,6 +248,10 @@ class ShardedTrianglePairStack:
         # peers' shards (one kernel instead of K4e + a transpose push), when each rank's rows
         # are a multiple of 128
         self.fused_transpose = fused_transpose
+        # peer mode, channel shards: K2 stores the x tiles straight into their row owners'
+        # planes (one kernel instead of K2 + the x push), when each rank's rows are a
+        # multiple of 128
+        self.fused_x = fused_x
         self._key = None
         self._buf: Dict[str, Tensor] = {}
         self._peer: Dict[str, PeerBuffer] = {}
@@ -504,11 +518,16 @@ class ShardedTrianglePairStack:
                         so.push_3d(peer[name], (bb * N + row0) * CP * N * 2, CP * N * 2, planes[bb * plane_b:],
                                    C * N * 2, CP * N * 2, CP * N * 2, R)
             yield ("barrier",)
-            so.trimul_contract(outgoing, buf["a_ch"], buf["b_ch"], buf["x_ch"], B, N, N, N, N, N, N, xs, CP)
-            for bb in range(B):
-                # rows of peer p, my channel group -> channel group `me` of peer p's x rows
-                so.push_3d(peer["x"], (bb * R * C + me * CP) * N * 2, C * N * 2, buf["x_ch"][bb * plane_b:],
-                           CP * N * 2, R * CP * N * 2, CP * N * 2, R)
+            if self.fused_x and R % 128 == 0 and hasattr(so, "trimul_contract_to"):
+                # x tiles of peer p's rows straight into channel group `me` of p's x planes
+                so.trimul_contract_to(outgoing, buf["a_ch"], buf["b_ch"], B, N, N, N, N, N, xs, CP, peer["x"],
+                                      me * CP, N)
+            else:
+                so.trimul_contract(outgoing, buf["a_ch"], buf["b_ch"], buf["x_ch"], B, N, N, N, N, N, N, xs, CP)
+                for bb in range(B):
+                    # rows of peer p, my channel group -> channel group `me` of peer p's x rows
+                    so.push_3d(peer["x"], (bb * R * C + me * CP) * N * 2, C * N * 2, buf["x_ch"][bb * plane_b:],
+                               CP * N * 2, R * CP * N * 2, CP * N * 2, R)
             yield ("barrier",)
             so.trimul_finish(mod, zz, buf["x"], N, xs, B, R, N, z)
 
@@ -637,7 +656,7 @@ class TimedStageOps:
 
     KERNELS = ("trimul_project", "trimul_project_to", "trimul_contract", "trimul_finish", "triatt_project",
                "triatt_core",
-               "triatt_finish", "triatt_finish_to", "copy_2d", "copy_3d", "pair_transpose_pack", "push_3d", "push_pair_transpose")
+               "triatt_finish", "triatt_finish_to", "trimul_contract_to", "copy_2d", "copy_3d", "pair_transpose_pack", "push_3d", "push_pair_transpose")
 
     def __init__(self, inner, hook=None):
         self.inner = inner

@@ -290,6 +290,17 @@ GTK_API int gtk_push_3d(const uint64_t* dsts, int P, int64_t doff, int64_t dpitc
  * shard dsts[q] [B][C/P][ndst][128] at (b, x, row0 + y). */
 GTK_API int gtk_push_pair_transpose(const float* src, const uint64_t* dsts, int64_t B, int64_t R, int64_t C,
                                     int64_t P, int64_t ndst, int64_t row0, void* stream);
+/* The channel-sharded contraction of a row-sharded stack with its scatter back to the row
+ * owners fused into its stores: x tiles of the C channels computed here (over all M rows) are
+ * TMA-stored into the owner of their rows, p = row / (M/P), as channels c_off .. c_off+C-1 of
+ * p's x planes [B][M/P][C_dst][ld_dst] (fp16, scaled by out_scale as gtk_trimul_contract).
+ * dst_bases: HOST array of the P ranks' x-plane addresses; M/P a multiple of 128, P <= 8.
+ * Replaces gtk_trimul_contract + the x push of the sharded stack (no reference counterpart). */
+GTK_API int gtk_trimul_contract_to_peers(int outgoing, const void* a_planes, const void* b_planes,
+                                         const uint64_t* dst_bases, int P, int64_t B, int64_t C, int64_t M,
+                                         int64_t Nj, int64_t K, int64_t lda, int64_t ldb, int64_t C_dst,
+                                         int64_t c_off, int64_t ld_dst, float out_scale, uint32_t* status,
+                                         void* stream);
 /* K4e of a row shard with the pair-grid transpose fused into its stores: the finished
  * update out = z + og W_o^T + b_o (+ z when add_residual) of the starting-orientation shard
  * (rows local rows from global row row0, the workspace of gtk_triatt_core) is written

@@ -126,6 +126,16 @@ class CpuStageOps:
         v = self._views(ws, B, rows, N)
         z.add_(O.linear(v["og"].float(), self._p(mod), "mha.linear_o"))
 
+    def trimul_contract_to(self, outgoing, a, b, B, M, Nj, K, lda, ldb, xs, channels, dst, c_off, ld_dst):
+        # gtk_trimul_contract_to_peers: the contraction, then rows of rank p -> p's x planes
+        P = len(dst.tensors)
+        R = M // P
+        x = torch.empty(B * M * channels * ld_dst * 2, dtype=torch.uint8)
+        self.trimul_contract(outgoing, a, b, x, B, M, Nj, K, lda, ldb, ld_dst, xs, channels)
+        X = _typed(x, torch.float16, (B, M, channels, ld_dst))
+        for p, t in enumerate(dst.tensors):
+            _typed(t, torch.float16, (B, R, C, ld_dst))[:, :, c_off:c_off + channels].copy_(X[:, p * R:(p + 1) * R])
+
     def triatt_finish_to(self, mod, z, ws, B, rows, N, row0, dst):
         # gtk_triatt_finish_to_peers: z + update, pair-transposed into every rank's shard
         v = self._views(ws, B, rows, N)

@@ -187,22 +187,23 @@ def test_emulated_peer_exchange_matches_unsharded(N, P, exchange, k1_direct):
     assert_status_clean(dev)
 
 
-def test_emulated_fused_transpose_equals_separate_pushes():
+@pytest.mark.parametrize("N,P,exchange", [(256, 2, "gather"), (512, 4, "channels")])
+def test_emulated_fused_stores_equal_separate_pushes(N, P, exchange):
     """With 128 rows per rank the attention blocks' K4e stores its output transposed straight
-    into the ranks' shards (TMA stores through per-rank tensor maps; emulated ranks on one
-    GPU, so the shards are local allocations). Same arithmetic as K4e followed by the
-    transpose push: the results are bitwise equal."""
+    into the ranks' shards, and (channel shards) K2 stores each x tile straight into its row
+    owner's planes: TMA stores through per-rank tensor maps (emulated ranks on one GPU, so the
+    shards are local allocations). Same arithmetic as the kernels followed by the pushes: the
+    results are bitwise equal."""
     dev = require_gpu()
     from genie_tk.sharded import ShardedTrianglePairStack, connect_emulated, run_emulated
-    N, P = 256, 2
     z, mask, params = _problem(N, 1)
     st = _stack(params, dev)
     zd, md = z.to(dev), mask.to(dev)
     R = N // P
     res = []
     for fused in (True, False):
-        shards = [ShardedTrianglePairStack(st, P, r, trimul_exchange="gather", exchange="peer",
-                                           fused_transpose=fused) for r in range(P)]
+        shards = [ShardedTrianglePairStack(st, P, r, trimul_exchange=exchange, exchange="peer",
+                                           fused_transpose=fused, fused_x=fused) for r in range(P)]
         connect_emulated(shards, 1, N, dev)
         zl = [zd[:, r * R:(r + 1) * R].clone() for r in range(P)]
         run_emulated(shards, zl, md)

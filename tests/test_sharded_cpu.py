@@ -82,13 +82,14 @@ def test_out_of_place_first_block():
     assert float((torch.cat(out, 1) - ref).abs().max()) == 0.0
 
 
-def _run_emulated_peer(z, mask, params, P, exchange="auto", k1_direct=False, fused_transpose=True):
+def _run_emulated_peer(z, mask, params, P, exchange="auto", k1_direct=False, fused_transpose=True, fused_x=True):
     from genie_tk.sharded import ShardedTrianglePairStack, connect_emulated, run_emulated
     st = _stack(params)
     B, N = z.shape[0], z.shape[1]
     R = N // P
     shards = [ShardedTrianglePairStack(st, P, r, stage_ops=CpuStageOps(), trimul_exchange=exchange, exchange="peer",
-                                       k1_direct=k1_direct, fused_transpose=fused_transpose) for r in range(P)]
+                                       k1_direct=k1_direct, fused_transpose=fused_transpose, fused_x=fused_x)
+              for r in range(P)]
     connect_emulated(shards, B, N, z.device)
     zl = [z[:, r * R:(r + 1) * R].clone() for r in range(P)]
     run_emulated(shards, zl, mask)
@@ -117,6 +118,17 @@ def test_fused_attention_transpose_matches_separate_pushes():
     z, mask, params = _problem(1, 256, 1)
     got = _run_emulated_peer(z, mask, params, 2, "gather")
     sep = _run_emulated_peer(z, mask, params, 2, "gather", fused_transpose=False)
+    assert float((got - sep).abs().max()) <= 1e-5
+    err = (got - O.stack_forward(z, mask, params, no_heads=4)).abs()
+    assert float(err.max()) <= MAX_ABS and float(err.mean()) <= MEAN_ABS
+
+
+def test_fused_x_scatter_matches_separate_push():
+    """Channel shards with 128 rows per rank: K2 stores each x tile straight into its row
+    owner's planes (gtk_trimul_contract_to_peers); equal to K2 + the x push, and the oracle."""
+    z, mask, params = _problem(1, 512, 1)
+    got = _run_emulated_peer(z, mask, params, 4, "channels")
+    sep = _run_emulated_peer(z, mask, params, 4, "channels", fused_transpose=False, fused_x=False)
     assert float((got - sep).abs().max()) <= 1e-5
     err = (got - O.stack_forward(z, mask, params, no_heads=4)).abs()
     assert float(err.max()) <= MAX_ABS and float(err.mean()) <= MEAN_ABS
