@@ -52,26 +52,39 @@ constexpr int kVLnW = 0, kVLnB = 128, kVWb = 256, kVBg = 768, kVBo = 896, kVecFl
 constexpr size_t kBytes = kVec + kVecFloats * 4;
 }  // namespace tapack
 
-__global__ void triatt_pack_kernel(gtk_triatt_params p, uint8_t* packed, float q_scale) {
+// Packs the parameters of 4 heads of head_dim d <= 32 (c_hidden = 4d) into the tuned
+// layout of 4 heads of 32: hidden channel h*32 + e is the module's channel h*d + e for e < d
+// and zero above (zero rows of W_q / W_k / W_v / W_g and b_g, zero columns of W_o), so the
+// padded q, k, v, gated output and their products are exact. q carries log2 e / sqrt(d).
+__global__ void triatt_pack_kernel(gtk_triatt_params p, uint8_t* packed, float q_scale, int d) {
   __half* w3 = reinterpret_cast<__half*>(packed + tapack::kW3);
   __half* w4 = reinterpret_cast<__half*>(packed + tapack::kW4);
   float* vec = reinterpret_cast<float*>(packed + tapack::kVec);
   const int tid = blockIdx.x * blockDim.x + threadIdx.x;
   const int nthreads = gridDim.x * blockDim.x;
+  const int hd = 4 * d;
+  auto src_row = [d](int r) { return (r & 31) < d ? (r >> 5) * d + (r & 31) : -1; };  // padded -> module channel
   for (int e = tid; e < 512 * 128; e += nthreads) {
     const int r = e >> 7, c = e & 127;
-    float v;
-    if (r < 128) v = p.q_w[r * 128 + c] * q_scale;
-    else if (r < 256) v = p.k_w[(r - 128) * 128 + c];
-    else if (r < 384) v = p.v_w[(r - 256) * 128 + c];
-    else v = 0.5f * p.g_w[(r - 384) * 128 + c];  // sigmoid(x) = (1 + tanh(x/2)) / 2
+    const int sr = src_row(r & 127);
+    float v = 0.f;
+    if (sr >= 0) {
+      if (r < 128) v = p.q_w[sr * 128 + c] * q_scale;
+      else if (r < 256) v = p.k_w[sr * 128 + c];
+      else if (r < 384) v = p.v_w[sr * 128 + c];
+      else v = 0.5f * p.g_w[sr * 128 + c];  // sigmoid(x) = (1 + tanh(x/2)) / 2
+    }
     w3[e] = f16_sat(v);
   }
-  for (int e = tid; e < 128 * 128; e += nthreads) w4[e] = f16_sat(p.o_w[e]);
+  for (int e = tid; e < 128 * 128; e += nthreads) {
+    const int o = e >> 7, sc = src_row(e & 127);
+    w4[e] = f16_sat(sc >= 0 ? p.o_w[o * hd + sc] : 0.f);
+  }
   for (int e = tid; e < 128; e += nthreads) {
+    const int sr = src_row(e);
     vec[tapack::kVLnW + e] = p.ln_w[e];
     vec[tapack::kVLnB + e] = p.ln_b[e];
-    vec[tapack::kVBg + e] = 0.5f * p.g_b[e];
+    vec[tapack::kVBg + e] = sr >= 0 ? 0.5f * p.g_b[sr] : 0.f;
     vec[tapack::kVBo + e] = p.o_b[e];
     for (int h = 0; h < kHeads; ++h) vec[tapack::kVWb + h * 128 + e] = p.bias_w[h * 128 + e] * kLog2e;
   }
@@ -1188,8 +1201,8 @@ static int rows_check(const char* who, int starting, int64_t B, int64_t rows, in
 }
 
 static int triatt_check(int c_in, int c_hidden, int heads) {
-  if (c_in != 128 || c_hidden != 128 || heads != kHeads)
-    return fail(GTK_ERR_UNSUPPORTED, "triatt: only c_in = c_hidden = 128 with 4 heads of 32 is implemented");
+  if (c_in != 128 || heads != kHeads || c_hidden % kHeads || c_hidden < kHeads || c_hidden > 128)
+    return fail(GTK_ERR_UNSUPPORTED, "triatt: the tuned kernels take c_in = 128 with 4 heads of head_dim <= 32");
   return GTK_OK;
 }
 
@@ -1199,8 +1212,11 @@ using namespace gtk;
 
 extern "C" {
 
+// The tuned kernels: c_in = 128 and 4 heads of head_dim <= 32 (the 4 x 32 of the benchmark,
+// and, with the heads zero-padded to 32 in the packed weights, the reference's default
+// c_hidden_tri_att = 32 with 4 heads and any other 4 x d).
 static bool triatt_tuned(int c_in, int c_hidden, int heads) {
-  return c_in == 128 && c_hidden == 128 && heads == kHeads;
+  return c_in == 128 && heads == kHeads && c_hidden % kHeads == 0 && c_hidden >= kHeads && c_hidden <= 128;
 }
 
 size_t gtk_triatt_packed_bytes(int c_in, int c_hidden, int heads) {
@@ -1220,9 +1236,10 @@ int gtk_triatt_pack(const gtk_triatt_params* params, int c_in, int c_hidden, int
   for (int i = 0; i < 10; ++i)
     if (!pp[i]) return fail(GTK_ERR_INVALID_ARG, "a triatt parameter pointer is NULL");
   if (int e = check_device()) return e;
-  const float q_scale = kLog2e / std::sqrt(static_cast<float>(c_hidden / heads));
+  const int d = c_hidden / heads;
+  const float q_scale = kLog2e / std::sqrt(static_cast<float>(d));
   triatt_pack_kernel<<<64, 256, 0, static_cast<cudaStream_t>(stream)>>>(*params, static_cast<uint8_t*>(packed),
-                                                                         q_scale);
+                                                                         q_scale, d);
   return check_launch("triatt_pack_kernel");
 }
 
