@@ -45,7 +45,10 @@ constexpr int kVB1 = 0, kVB2 = 512, kVecFloats = 640;
 constexpr size_t kBytes = kVec + kVecFloats * 4;
 }  // namespace tnpack
 
-__global__ void transition_pack_kernel(gtk_transition_params p, uint8_t* packed) {
+// Packs a transition of expansion n <= 4 (hidden = 128 n) into the tuned 512-unit layout:
+// hidden units past 128 n have zero W1 rows and b1, so ReLU makes them exactly 0, and zero W2
+// columns, so the result is the n-unit transition's.
+__global__ void transition_pack_kernel(gtk_transition_params p, uint8_t* packed, int hid) {
   using namespace tnpack;
   __half* w1 = reinterpret_cast<__half*>(packed + kW1);
   __half* w2 = reinterpret_cast<__half*>(packed + kW2);
@@ -53,13 +56,19 @@ __global__ void transition_pack_kernel(gtk_transition_params p, uint8_t* packed)
   const int tid = blockIdx.x * blockDim.x + threadIdx.x;
   const int nthreads = gridDim.x * blockDim.x;
   for (int e = tid; e < kHid * kCp; e += nthreads) {
-    const int c = e % kCp;
-    w1[e] = f16_sat(p.w1[e] * p.ln_w[c]);
+    const int r = e / kCp, c = e % kCp;
+    w1[e] = f16_sat(r < hid ? p.w1[e] * p.ln_w[c] : 0.f);
   }
-  for (int e = tid; e < kCp * kHid; e += nthreads) w2[e] = f16_sat(p.w2[e]);
+  for (int e = tid; e < kCp * kHid; e += nthreads) {
+    const int o = e / kHid, r = e % kHid;
+    w2[e] = f16_sat(r < hid ? p.w2[o * hid + r] : 0.f);
+  }
   for (int r = tid; r < kHid; r += nthreads) {
-    float acc = p.b1 ? p.b1[r] : 0.f;
-    for (int c = 0; c < kCp; ++c) acc += p.w1[r * kCp + c] * p.ln_b[c];
+    float acc = 0.f;
+    if (r < hid) {
+      acc = p.b1 ? p.b1[r] : 0.f;
+      for (int c = 0; c < kCp; ++c) acc += p.w1[r * kCp + c] * p.ln_b[c];
+    }
     vec[kVB1 + r] = acc;
   }
   for (int r = tid; r < kCp; r += nthreads) vec[kVB2 + r] = p.b2 ? p.b2[r] : 0.f;
@@ -582,8 +591,8 @@ static int make_w2_map(CUtensorMap* m, const void* base) {
 }
 
 static int transition_check(int c_p, int n) {
-  if (c_p != tnpack::kCp || n != tnpack::kHid / tnpack::kCp)
-    return fail(GTK_ERR_UNSUPPORTED, "transition: the kernels support c_p = 128 with n = 4");
+  if (c_p != tnpack::kCp || n < 1 || n > tnpack::kHid / tnpack::kCp)
+    return fail(GTK_ERR_UNSUPPORTED, "transition: the tuned kernels take c_p = 128 with n <= 4");
   return GTK_OK;
 }
 
@@ -593,7 +602,8 @@ using namespace gtk;
 
 extern "C" {
 
-static bool transition_tuned(int c_p, int n) { return c_p == tnpack::kCp && n == tnpack::kHid / tnpack::kCp; }
+// The tuned kernels: c_p = 128 with n <= 4 (n < 4 zero-padded to 512 hidden units when packed).
+static bool transition_tuned(int c_p, int n) { return c_p == tnpack::kCp && n >= 1 && n <= tnpack::kHid / tnpack::kCp; }
 
 size_t gtk_transition_packed_bytes(int c_p, int n) {
   return transition_tuned(c_p, n) ? tnpack::kBytes : gen::transition_packed_bytes(c_p, n);
@@ -614,7 +624,8 @@ int gtk_transition_pack(const gtk_transition_params* params, int c_p, int n, voi
   if (int e = check_ptr(packed, "packed", 256)) return e;
   if (packed_bytes < tnpack::kBytes) return fail(GTK_ERR_WORKSPACE, "packed buffer too small");
   if (int e = check_device()) return e;
-  transition_pack_kernel<<<64, 256, 0, static_cast<cudaStream_t>(stream)>>>(*params, static_cast<uint8_t*>(packed));
+  transition_pack_kernel<<<64, 256, 0, static_cast<cudaStream_t>(stream)>>>(*params, static_cast<uint8_t*>(packed),
+                                                                            n * tnpack::kCp);
   return check_launch("transition_pack_kernel");
 }
 

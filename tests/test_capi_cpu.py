@@ -168,7 +168,8 @@ def test_attention_and_linear_entry_points_validate_before_touching_the_device(l
 def test_transition_entry_points(lib):
     assert lib.gtk_transition_packed_bytes(128, 4) > 2 * 128 * 512 * 2
     assert lib.gtk_transition_workspace_bytes(2, 10, 128, 4) == 2 * 10 * 10 * 512 * 2
-    assert lib.gtk_transition_workspace_bytes(1, 10, 128, 2) > 0    # general path
+    assert lib.gtk_transition_workspace_bytes(1, 10, 128, 2) == 10 * 10 * 512 * 2  # tuned, hidden padded to 512
+    assert lib.gtk_transition_workspace_bytes(1, 10, 64, 2) > 0     # general path
     # unsupported width, then a NULL pair tensor, then a short workspace: all before any launch
     assert lib.gtk_transition_forward(None, None, None, None, 0, None, 0, 1, 16, 1024, 4, None, None) == -2
     assert lib.gtk_transition_forward(None, None, None, None, 0, None, 0, 1, 16, 128, 4, None, None) == -1

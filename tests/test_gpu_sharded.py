@@ -187,7 +187,7 @@ def test_emulated_peer_exchange_matches_unsharded(N, P, exchange, k1_direct):
     assert_status_clean(dev)
 
 
-@pytest.mark.parametrize("N,P,exchange", [(256, 2, "gather"), (512, 4, "channels")])
+@pytest.mark.parametrize("N,P,exchange", [(256, 2, "gather"), (512, 4, "channels"), (1024, 8, "channels")])
 def test_emulated_fused_stores_equal_separate_pushes(N, P, exchange):
     """With 128 rows per rank the attention blocks' K4e stores its output transposed straight
     into the ranks' shards, and (channel shards) K2 stores each x tile straight into its row

@@ -52,6 +52,25 @@ def test_transition_matches_oracle(B, N):
     assert_status_clean(dev)
 
 
+@pytest.mark.parametrize("n", [1, 2, 3])
+def test_narrower_transition_runs_on_the_tuned_kernels(n):
+    """c_p = 128 with an expansion n < 4: the hidden layer is zero-padded to 512 units in the
+    packed weights (ReLU(0) = 0, zero W2 columns), so the result is the n-unit transition's."""
+    dev = require_gpu()
+    from genie_tk import ops
+    gen = torch.Generator().manual_seed(70 + n)
+    B, N = 1, 77
+    z = torch.randn(B, N, N, 128, generator=gen)
+    mask = (torch.rand(B, N, N, generator=gen) > 0.2).float()
+    params = O.make_transition_params(128, n, gen)
+    packed = ops.pack_transition(to_dev(params, dev), dev)
+    zz = z.to(dev)
+    ops.transition_forward(zz, mask.to(dev), packed, out=zz, add_residual=True)
+    torch.cuda.synchronize()
+    assert_parity(zz, O.layer_tail(z, mask, params), what=f"transition n={n}")
+    assert_status_clean(dev)
+
+
 def test_pair_transform_layer_matches_oracle():
     dev = require_gpu()
     B, N = 1, 64
