@@ -236,6 +236,7 @@ struct TriSmem {
   __half g[2][kRows][D + 8];
   __half k[2][kRows][D + 8];
   __half v[2][kRows][D + 8];
+  __half bias[kRows][kBP];  // the CTA's 64 x 64 bias block, loaded once
   float m[2][kRows];
   float2 l[2][kRows];
   float dsum[2][kRows];
@@ -553,7 +554,7 @@ __global__ void __launch_bounds__(kThreads) dkv_kernel(const Args a) {
 // queries; loops over the pair rows i with that row's q, do, k, v tiles double buffered.
 // ---------------------------------------------------------------------------------------
 template <int D>
-__global__ void __launch_bounds__(kThreads) dtri_kernel(const Args a) {
+__global__ void __launch_bounds__(kThreads, D <= 32 ? 4 : 2) dtri_kernel(const Args a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   TriSmem<D>& S = *reinterpret_cast<TriSmem<D>*>(smem_raw);
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
@@ -577,20 +578,16 @@ __global__ void __launch_bounds__(kThreads) dtri_kernel(const Args a) {
       S.dsum[st][t] = j < N ? a.dsum[(row * a.H + h) * N + j] * a.gscale : 0.f;
     }
   };
+  // the bias block (zero past N) rides with the first row's tiles; kept in shared memory so
+  // that registers allow four CTAs per SM
+  load_bias(S.bias, a.tri + bh * N * a.Np, j0, k0, N, a.Np);
   issue(0, 0);
   cp_commit();
-  float acc[4][2][4], bias[4][2][4];
-  const __half* trib = a.tri + bh * N * a.Np;
+  float acc[4][2][4];
 #pragma unroll
   for (int np = 0; np < 4; ++np)
 #pragma unroll
-    for (int x = 0; x < 2; ++x)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int64_t j = j0 + jl0 + 8 * (i >> 1), k = k0 + np * 16 + x * 8 + c_col(i);
-        acc[np][x][i] = 0.f;
-        bias[np][x][i] = (j < N && k < N) ? __half2float(trib[j * a.Np + k]) * kLog2e : 0.f;
-      }
+    for (int x = 0; x < 2; ++x) acc[np][x][0] = acc[np][x][1] = acc[np][x][2] = acc[np][x][3] = 0.f;
   for (int64_t i = 0; i < N; ++i) {
     const int st = static_cast<int>(i & 1);
     if (i + 1 < N) issue(i + 1, st ^ 1);
@@ -615,11 +612,16 @@ __global__ void __launch_bounds__(kThreads) dtri_kernel(const Args a) {
 #pragma unroll
       for (int x = 0; x < 2; ++x)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int r = e >> 1;
-          const float mk = S.m[st][np * 16 + x * 8 + c_col(e)];
-          const float p = exp2f(fmaf(s[x][e], a.qscale, bias[np][x][e] + mk) - L[r].x) * L[r].y;
-          acc[np][x][e] = fmaf(p, dp[x][e] - d0[r], acc[np][x][e]);
+        for (int r = 0; r < 2; ++r) {
+          const int kl = np * 16 + x * 8 + 2 * (lane & 3);
+          const float2 bb = bias_pair(S.bias, jl0 + 8 * r, kl);
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int e = 2 * r + u;
+            const float mk = S.m[st][kl + u];
+            const float p = exp2f(fmaf(s[x][e], a.qscale, fmaf(u ? bb.y : bb.x, kLog2e, mk)) - L[r].x) * L[r].y;
+            acc[np][x][e] = fmaf(p, dp[x][e] - d0[r], acc[np][x][e]);
+          }
         }
     }
     __syncthreads();

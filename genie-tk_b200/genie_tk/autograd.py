@@ -122,17 +122,32 @@ def _mask_or_ones(z: Tensor, mask: Optional[Tensor]) -> Tensor:
     return torch.ones(z.shape[:-1], dtype=z.dtype, device=z.device) if mask is None else mask.to(z.dtype)
 
 
+def _linear_cat(x: Tensor, p: Dict[str, Tensor], names: Sequence[str]) -> List[Tensor]:
+    """The projections `names` of one input as one GEMM over their concatenated weights (the
+    input is read once, and its gradient comes out of one GEMM instead of a sum of several);
+    the results are views of the one output, in order."""
+    ws = [p[n + ".weight"] for n in names]
+    bs = [p.get(n + ".bias") for n in names]
+    if all(b is None for b in bs):
+        bias = None
+    else:
+        bias = torch.cat([b if b is not None else w.new_zeros(w.shape[0]) for w, b in zip(ws, bs)])
+    y = F.linear(x, torch.cat(ws), bias)
+    return list(torch.split(y, [w.shape[0] for w in ws], dim=-1))
+
+
 def trimul_recompute(z: Tensor, mask: Optional[Tensor], p: Dict[str, Tensor], outgoing: bool) -> Tensor:
     """The update of the triangle multiplicative block (triangle_mul.py:103-132), fp32,
     with the contraction on the library's kernel."""
     p = _fp32(p)
     m = _mask_or_ones(z, mask).unsqueeze(-1)
     zn = F.layer_norm(z, (z.shape[-1],), p["layer_norm_in.weight"], p["layer_norm_in.bias"], LN_EPS)
-    a = _linear(zn, p, "linear_a_p") * torch.sigmoid(_linear(zn, p, "linear_a_g")) * m
-    b = _linear(zn, p, "linear_b_p") * torch.sigmoid(_linear(zn, p, "linear_b_g")) * m
+    ap, ag, bp, bg, g = _linear_cat(zn, p, ["linear_a_p", "linear_a_g", "linear_b_p", "linear_b_g", "linear_g"])
+    a = ap * torch.sigmoid(ag) * m
+    b = bp * torch.sigmoid(bg) * m
     x = contract(a, b, outgoing)
     x = F.layer_norm(x, (x.shape[-1],), p["layer_norm_out.weight"], p["layer_norm_out.bias"], LN_EPS)
-    return _linear(x, p, "linear_z") * torch.sigmoid(_linear(zn, p, "linear_g"))
+    return _linear(x, p, "linear_z") * torch.sigmoid(g)
 
 
 class _AttnCore(torch.autograd.Function):
@@ -165,28 +180,22 @@ def _native_attn_core(q: Tensor, k: Tensor, v: Tensor, tri: Tensor, mask: Option
 _attn_core = _native_attn_core
 
 
-def _triatt_shared(z: Tensor, mask: Optional[Tensor], p: Dict[str, Tensor], starting: bool):
-    """Row-independent part (triangle_attention.py:106-129): orientation, LayerNorm, the
-    triangle bias [B, H, N, N] shared by every row; the mask in the block's frame (or None)."""
+def triatt_recompute(z: Tensor, mask: Optional[Tensor], p: Dict[str, Tensor], starting: bool, heads: int,
+                     inf: float) -> Tensor:
+    """The update of the triangle attention block (triangle_attention.py:100-143), fp32, with
+    the attention core on the library's kernels: orientation, LayerNorm, the projections
+    q, k, v, g and the triangle bias [B, H, N, N] (one GEMM), the core, the gate and W_o."""
+    p = _fp32(p)
     x, m = z, mask
     if not starting:
         x = x.transpose(-2, -3)
         m = None if m is None else m.transpose(-1, -2)
     xn = F.layer_norm(x, (x.shape[-1],), p["layer_norm.weight"], p["layer_norm.bias"], LN_EPS)
-    tri = _linear(xn, p, "linear").permute(0, 3, 1, 2)
-    return xn, m, tri
-
-
-def triatt_recompute(z: Tensor, mask: Optional[Tensor], p: Dict[str, Tensor], starting: bool, heads: int,
-                     inf: float) -> Tensor:
-    """The update of the triangle attention block (triangle_attention.py:100-143), fp32, with
-    the attention core on the library's kernels."""
-    p = _fp32(p)
-    xn, m, tri = _triatt_shared(z, mask, p, starting)
-    q, k, v = (_linear(xn, p, f"mha.linear_{n}").contiguous() for n in "qkv")
+    q, k, v, g, tri = _linear_cat(xn, p, ["mha.linear_q", "mha.linear_k", "mha.linear_v", "mha.linear_g", "linear"])
     m = None if m is None else m.float().contiguous()
-    o = _attn_core(q, k, v, tri.contiguous(), m, heads, inf)
-    o = o * torch.sigmoid(_linear(xn, p, "mha.linear_g"))
+    o = _attn_core(q.contiguous(), k.contiguous(), v.contiguous(), tri.permute(0, 3, 1, 2).contiguous(), m, heads,
+                   inf)
+    o = o * torch.sigmoid(g)
     out = _linear(o, p, "mha.linear_o")
     return out if starting else out.transpose(-2, -3)
 
