@@ -1,9 +1,9 @@
 #!/usr/bin/env python
-"""Benchmark of the triangle pair stack (BASELINE metric: pair-stack layers*N^2/s at N=1024).
+"""Benchmark of the triangle pair stack (headline metric: pair-stack layers*N^2/s at N=1024).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload: B=1, N=1024, c_z=128, 8 layers of
+Workload (benchmark configuration 5): B=1, N=1024, c_z=128, 8 layers of
 [TriMulOut, TriMulIn, TriAttStart, TriAttEnd] with residual adds, all-ones mask, synthetic
 z ~ N(0,1) and weights ~ N(0, 1/fan_in) (gate biases 1). One step = one full 8-layer
 stack forward. The pair tensor (512 MB fp32) is larger than the 126 MB L2, so no flush is
@@ -703,7 +703,7 @@ def read_traffic(kernel):
 def run_transition(args, device):
     """``--op transition``: the pair transition (LN -> 4x expand -> ReLU -> project) with the
     pair transform layer's residual and mask, p = (p + transition(p)) * mask, on one GPU
-    (N^2 pairs per step, B = 1, seeded synthetic z and weights). Not the BASELINE metric; it
+    (N^2 pairs per step, B = 1, seeded synthetic z and weights). Not the headline metric; it
     measures the pair-transition kernels against their HBM roofline and against the same
     math as unfused fp32 PyTorch ops on the GPU."""
     from genie_tk import ops
@@ -831,7 +831,7 @@ def main():
     ap.add_argument("--trimul-exchange", default="auto", choices=["auto", "gather", "channels"],
                     help="multi-GPU exchange of the multiplicative update (auto: gather for <= 3 GPUs)")
     ap.add_argument("--op", default="stack", choices=["stack", "transition", "embed"],
-                    help="stack: the BASELINE workload (default); transition / embed: the pair-transition or "
+                    help="stack: the headline workload (default); transition / embed: the pair-transition or "
                          "pair-embedding kernels alone")
     ap.add_argument("--separate-x", action="store_true",
                     help="peer exchange, channel shards: K2 then the x push, instead of K2 storing into the owners")

@@ -50,7 +50,7 @@ def test_stack_matches_oracle_and_graph_replay(N, n_layers):
 
 def test_bench_layer_at_full_size_matches_oracle():
     """The benchmark's workload at its real size: the first layer of the cfg5 stack (B = 1,
-    N = 1024, seeded weights and input of BASELINE config 5) against the fp32 oracle
+    N = 1024, seeded weights and input of benchmark configuration 5) against the fp32 oracle
     (run on the GPU with fp32 matmuls)."""
     dev = require_gpu()
     z, mask, params = O.config_inputs(5, N=1024)
@@ -68,7 +68,7 @@ def test_bench_layer_at_full_size_matches_oracle():
 
 def test_bench_stack_all_layers_at_full_size(capsys):
     """The benchmarked workload itself: all 8 layers of the cfg5 stack (B = 1, N = 1024, the
-    seeded input and per-layer weights of BASELINE config 5) against the fp32 oracle of the
+    seeded input and per-layer weights of benchmark configuration 5) against the fp32 oracle of the
     reference's residual chain (examples/basic_usage.py:44-78, pair_transform.py:162-195).
     The oracle runs on the GPU with fp32 matmuls (TF32 off) and chunked attention rows.
 
