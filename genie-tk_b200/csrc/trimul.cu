@@ -50,47 +50,56 @@ namespace tmpack {
 constexpr size_t kW1 = 0;
 constexpr size_t kW2 = 512 * 128 * 2;
 constexpr size_t kVec = kW2 + 256 * 128 * 2;
-constexpr int kVB1 = 0, kVBg = 512, kVU = 640, kVV = 768, kVecFloats = 896;
+constexpr int kVB1 = 0, kVBg = 512, kVU = 640, kVV = 768, kVC = 896, kVecFloats = 900;  // kVC: real c_hidden
 constexpr size_t kBytes = kVec + kVecFloats * 4;
 }  // namespace tmpack
 
-__global__ void trimul_pack_kernel(gtk_trimul_params p, uint8_t* packed) {
+// Packs a multiplicative update of c_hidden = c <= 128 (c_z = 128) into the tuned 128-channel
+// layout: hidden channels past c have zero projection rows and biases, so their a / b planes,
+// and with them their x planes, are exactly zero; W_z gets zero columns there, and K2e takes
+// LN_out's statistics over the c real channels (kVC).
+__global__ void trimul_pack_kernel(gtk_trimul_params p, uint8_t* packed, int c) {
   __half* w1 = reinterpret_cast<__half*>(packed + tmpack::kW1);
   __half* w2 = reinterpret_cast<__half*>(packed + tmpack::kW2);
   float* vec = reinterpret_cast<float*>(packed + tmpack::kVec);
   const int tid = blockIdx.x * blockDim.x + threadIdx.x;
   const int nthreads = gridDim.x * blockDim.x;
   for (int e = tid; e < 512 * 128; e += nthreads) {
-    const int r = e >> 7, c = e & 127;
+    const int r = e >> 7, col = e & 127, h = r & 127;
     const float* src = r < 128 ? p.a_p_w : r < 256 ? p.a_g_w : r < 384 ? p.b_p_w : p.b_g_w;
-    w1[e] = f16_sat(src[(r & 127) * 128 + c] * p.ln_in_w[c] * (((r >> 7) & 1) ? 0.5f : 1.f));
+    w1[e] = f16_sat(h < c ? src[h * 128 + col] * p.ln_in_w[col] * (((r >> 7) & 1) ? 0.5f : 1.f) : 0.f);
   }
   for (int e = tid; e < 256 * 128; e += nthreads) {
-    const int r = e >> 7, c = e & 127;
-    const float val =
-        r < 128 ? 0.5f * p.g_w[r * 128 + c] * p.ln_in_w[c] : p.z_w[(r - 128) * 128 + c] * p.ln_out_w[c];
+    const int r = e >> 7, col = e & 127;
+    float val;
+    if (r < 128) val = 0.5f * p.g_w[r * 128 + col] * p.ln_in_w[col];
+    else val = col < c ? p.z_w[(r - 128) * c + col] * p.ln_out_w[col] : 0.f;
     w2[e] = f16_sat(val);
   }
   for (int e = tid; e < 512; e += nthreads) {
     const int r = e & 127;
     const float* w = e < 128 ? p.a_p_w : e < 256 ? p.a_g_w : e < 384 ? p.b_p_w : p.b_g_w;
     const float* bb = e < 128 ? p.a_p_b : e < 256 ? p.a_g_b : e < 384 ? p.b_p_b : p.b_g_b;
-    float acc = bb[r];
-    for (int c = 0; c < 128; ++c) acc += w[r * 128 + c] * p.ln_in_b[c];
+    float acc = 0.f;
+    if (r < c) {
+      acc = bb[r];
+      for (int col = 0; col < 128; ++col) acc += w[r * 128 + col] * p.ln_in_b[col];
+    }
     vec[tmpack::kVB1 + e] = acc * (((e >> 7) & 1) ? 0.5f : 1.f);
   }
   for (int e = tid; e < 128; e += nthreads) {
     float bg = p.g_b[e];
-    for (int c = 0; c < 128; ++c) bg += p.g_w[e * 128 + c] * p.ln_in_b[c];
+    for (int col = 0; col < 128; ++col) bg += p.g_w[e * 128 + col] * p.ln_in_b[col];
     vec[tmpack::kVBg + e] = 0.5f * bg;
     float u = 0.f, v = p.z_b[e];
-    for (int c = 0; c < 128; ++c) {
-      u += __half2float(f16_sat(p.z_w[e * 128 + c] * p.ln_out_w[c]));
-      v += p.z_w[e * 128 + c] * p.ln_out_b[c];
+    for (int col = 0; col < c; ++col) {
+      u += __half2float(f16_sat(p.z_w[e * c + col] * p.ln_out_w[col]));
+      v += p.z_w[e * c + col] * p.ln_out_b[col];
     }
     vec[tmpack::kVU + e] = u;
     vec[tmpack::kVV + e] = v;
   }
+  if (tid == 0) vec[tmpack::kVC] = static_cast<float>(c);
 }
 
 // ----------------------------------------------------------------------------------
@@ -713,6 +722,8 @@ __global__ void __launch_bounds__(k2e::kThreads, 1)
                          const float* __restrict__ vec, int add_residual, float x_scale, int N, int rows, int n_jt,
                          int n_tiles, uint32_t* status, const DropArgs drop) {
   using namespace k2e;
+  const int c_real = static_cast<int>(__ldg(vec + tmpack::kVC));  // real hidden channels (<= 128)
+  const float inv_c = 1.f / static_cast<float>(c_real);
   extern __shared__ uint8_t dsmem[];
   uint8_t* smem = align1024(dsmem);
   K2eBars* bars = reinterpret_cast<K2eBars*>(smem + kBar);
@@ -963,13 +974,14 @@ __global__ void __launch_bounds__(k2e::kThreads, 1)
       w = w && mbar_wait(&bars->d_full[s], (it >> 1) & 1, guard, status, kStatusTimeoutConsumer);
       ok = __all_sync(0xffffffffu, w);
       if (!ok) break;
-      // LN_out statistics over the 128 channels of pair p (x is stored times x_scale)
+      // LN_out statistics over the c_real channels of pair p (x is stored times x_scale; the
+      // channels past c_real of a narrower update are zero padding)
       const uint8_t* xb = smem + kX + (p >> 6) * 16384;
       const int pj = p & 63;
       const float x0 = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(xb + swz128(0, pj >> 3) + (pj & 7) * 2)));
       float a1[4] = {0.f, 0.f, 0.f, 0.f}, a2[4] = {0.f, 0.f, 0.f, 0.f};  // four chains each
 #pragma unroll 16
-      for (int c = 0; c < 128; ++c) {
+      for (int c = 0; c < c_real; ++c) {
         const float xv = __half2float(
                              __ushort_as_half(*reinterpret_cast<const uint16_t*>(xb + swz128(c, pj >> 3) + (pj & 7) * 2))) -
                          x0;
@@ -978,9 +990,9 @@ __global__ void __launch_bounds__(k2e::kThreads, 1)
       }
       const float s1 = (a1[0] + a1[1]) + (a1[2] + a1[3]), s2 = (a2[0] + a2[1]) + (a2[2] + a2[3]);
       mbar_arrive_after(&bars->x_empty, s1 + s2);  // the x tile may be reloaded: its values are consumed
-      const float d1 = s1 * (1.f / 128.f);
+      const float d1 = s1 * inv_c;
       const float mu_x = x0 + d1;
-      const float var = fmaxf(s2 * (1.f / 128.f) - d1 * d1, 0.f);
+      const float var = fmaxf(s2 * inv_c - d1 * d1, 0.f);
       const float rstd_x = rsqrtf(var + 1e-5f * x_scale * x_scale);
       tc_fence_after();
 #pragma unroll 1
@@ -1075,14 +1087,18 @@ using namespace gtk;
 
 extern "C" {
 
+// The tuned kernels: c_z = 128 and c_hidden <= 128 (a narrower hidden width zero-padded to 128
+// channels when packed).
+static bool trimul_tuned(int c_z, int c_hidden) { return c_z == 128 && c_hidden >= 1 && c_hidden <= 128; }
+
 size_t gtk_trimul_packed_bytes(int c_z, int c_hidden) {
-  if (c_z != 128 || c_hidden != 128) return gen::trimul_packed_bytes(c_z, c_hidden);
+  if (!trimul_tuned(c_z, c_hidden)) return gen::trimul_packed_bytes(c_z, c_hidden);
   return tmpack::kBytes;
 }
 
 int gtk_trimul_pack(const gtk_trimul_params* params, int c_z, int c_hidden, void* packed, size_t packed_bytes,
                     void* stream) {
-  if (c_z != 128 || c_hidden != 128) return gen::trimul_pack(params, c_z, c_hidden, packed, packed_bytes, stream);
+  if (!trimul_tuned(c_z, c_hidden)) return gen::trimul_pack(params, c_z, c_hidden, packed, packed_bytes, stream);
   if (!params) return fail(GTK_ERR_INVALID_ARG, "params is NULL");
   if (int e = check_ptr(packed, "packed", 256)) return e;
   if (packed_bytes < tmpack::kBytes) return fail(GTK_ERR_WORKSPACE, "packed buffer too small");
@@ -1090,14 +1106,15 @@ int gtk_trimul_pack(const gtk_trimul_params* params, int c_z, int c_hidden, void
   for (int i = 0; i < 16; ++i)
     if (!pp[i]) return fail(GTK_ERR_INVALID_ARG, "a trimul parameter pointer is NULL");
   if (int e = check_device()) return e;
-  trimul_pack_kernel<<<64, 256, 0, static_cast<cudaStream_t>(stream)>>>(*params, static_cast<uint8_t*>(packed));
+  trimul_pack_kernel<<<64, 256, 0, static_cast<cudaStream_t>(stream)>>>(*params, static_cast<uint8_t*>(packed),
+                                                                         c_hidden);
   return check_launch("trimul_pack_kernel");
 }
 
 int64_t gtk_plane_pitch(int64_t N) { return static_cast<int64_t>(round_up(static_cast<uint64_t>(N), 8)); }
 
 size_t gtk_trimul_workspace_bytes(int64_t B, int64_t N, int c_z, int c_hidden) {
-  if (c_z != 128 || c_hidden != 128) return gen::trimul_workspace_bytes(B, N, c_z, c_hidden);
+  if (!trimul_tuned(c_z, c_hidden)) return gen::trimul_workspace_bytes(B, N, c_z, c_hidden);
   if (B < 1 || N < 1) return 0;
   const size_t plane = round_up(static_cast<size_t>(B) * N * 128 * gtk_plane_pitch(N) * 2, 256);
   return 3 * plane;
@@ -1302,7 +1319,7 @@ static int trimul_finish_launch(const float* z, const void* x_planes, int64_t ld
 static int trimul_forward_impl(int outgoing, const float* z, const float* mask, const void* packed, float* out,
                                int add_residual, const DropArgs& drop, void* workspace, size_t workspace_bytes,
                                int64_t B, int64_t N, int c_z, int c_hidden, uint32_t* status, void* stream) {
-  if (c_z != 128 || c_hidden != 128)  // every other shape: the general path
+  if (!trimul_tuned(c_z, c_hidden))  // every other shape: the general path
     return gen::trimul_forward(outgoing, z, mask, packed, out, add_residual, drop, workspace, workspace_bytes, B, N,
                                c_z, c_hidden, status, stream);
   if (!dims_ok(B, 65535) || !dims_ok(N, 65535)) return fail(GTK_ERR_INVALID_ARG, "trimul: bad B/N");

@@ -19,9 +19,10 @@
  *    wait ran out, or that had to clamp an fp16 intermediate, ORs a GTK_STATUS_* bit into
  *    it and finishes cleanly instead of hanging or failing silently. Read it after
  *    synchronising the stream.
- *  - Shapes: the multiplicative update with c_z = c_hidden = 128, attention with c_in =
- *    c_hidden = 128 (4 heads x 32) and the transition with c_p = 128, n = 4 run on the
- *    tuned tcgen05 kernels. Every other shape the reference's modules accept -- channel
+ *  - Shapes: the multiplicative update with c_z = 128, c_hidden <= 128, attention with
+ *    c_in = 128 and 4 heads of head_dim <= 32, and the transition with c_p = 128, n <= 4
+ *    run on the tuned tcgen05 kernels (narrower hidden widths and head dims are
+ *    zero-padded in the packed weights, which changes no result). Every other shape the reference's modules accept -- channel
  *    counts 1..512, attention heads 1..32 with head_dim = c_hidden / heads <= 64, a
  *    transition hidden width <= 2048 -- runs on the general-shape kernels behind the same
  *    forward entry points (the stage entry points below are the tuned shape only). Beyond

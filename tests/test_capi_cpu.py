@@ -58,6 +58,9 @@ def test_host_queries(lib):
         assert lib.gtk_triatt_packed_bytes(cin, c, h) > 0
         assert lib.gtk_triatt_workspace_bytes(1, 10, cin, c, h) > 0
     assert lib.gtk_trimul_packed_bytes(1024, 128) == 0
+    # c_z = 128 with a narrower hidden width packs into the tuned 128-channel layout
+    assert lib.gtk_trimul_packed_bytes(128, 64) == lib.gtk_trimul_packed_bytes(128, 128)
+    assert lib.gtk_trimul_workspace_bytes(1, 10, 128, 1) == lib.gtk_trimul_workspace_bytes(1, 10, 128, 128)
     assert lib.gtk_triatt_packed_bytes(128, 128, 3) == 0    # c_hidden not a multiple of heads
     assert lib.gtk_triatt_packed_bytes(128, 256, 2) == 0    # head_dim 128 > 64
     assert lib.gtk_transition_packed_bytes(64, 4) > 0 and lib.gtk_transition_packed_bytes(128, 2) > 0

@@ -95,3 +95,33 @@ def test_config_matches_oracle(cfg, N, B, outgoing):
         mod(z2, md, out=z2, add_residual=True)
     assert_parity(z2, zd + ref, what="residual in place")
     assert_status_clean(dev)
+
+
+@pytest.mark.parametrize("c,N,B,outgoing", [(64, 150, 2, True), (64, 150, 1, False), (1, 40, 1, True),
+                                            (17, 77, 1, False), (127, 130, 1, True)])
+def test_narrower_hidden_runs_on_the_tuned_kernels(c, N, B, outgoing):
+    """c_z = 128 with c_hidden = c < 128 (the c_hidden_mul = 64 of examples/basic_usage.py:140):
+    the packed projections are zero past c, so the padded a / b / x channels are exactly zero,
+    W_z has zero columns there and LN_out's statistics cover the c real channels."""
+    dev = require_gpu()
+    import genie_tk
+    from genie_tk import _lib
+    lib = _lib.load()
+    assert lib.gtk_trimul_packed_bytes(128, c) == lib.gtk_trimul_packed_bytes(128, 128)
+    gen = torch.Generator().manual_seed(300 + c + N)
+    z = torch.randn(B, N, N, 128, generator=gen)
+    mask = (torch.rand(B, N, N, generator=gen) > 0.2).float()
+    params = O.make_trimul_params(128, c, gen, ln_random=True, bias_random=True)
+    cls = genie_tk.TriangleMultiplicationOutgoing if outgoing else genie_tk.TriangleMultiplicationIncoming
+    mod = cls(128, c).to(dev)
+    mod.load_state_dict(to_dev(params, dev))
+    zd, md = z.to(dev), mask.to(dev)
+    with torch.no_grad():
+        got = mod(zd, md)
+        z2 = zd.clone()
+        mod(z2, md, out=z2, add_residual=True)
+    ref = O.trimul_forward(zd, md, to_dev(params, dev), outgoing=outgoing)
+    torch.cuda.synchronize()
+    assert_parity(got, ref, what=f"trimul c_hidden={c} N={N}")
+    assert_parity(z2, zd + ref, what="residual in place")
+    assert_status_clean(dev)
