@@ -1,5 +1,6 @@
-"""GPU parity of the general-shape path: every shape the reference's modules accept other than
-the tuned 128-channel one (its own defaults c_hidden_tri_att = 32 with 4 heads, head_dim 8 --
+"""GPU parity at the shapes other than the benchmark's 128-channel one: those the tuned
+kernels take with zero-padded weights and those the general-shape kernels run (the
+reference's defaults c_hidden_tri_att = 32 with 4 heads, head_dim 8 --
 src/genie_tk/pair_transform.py:113-119; the c_hidden_mul = 64 and c_hidden_tri_att = 16 of
 examples/basic_usage.py:140-142; the c_z = 64 / 32 widths of tests/test_triangle_mul.py:37 and
 tests/test_triangle_attention.py:36,74,127-137), through the same C ABI entry points
