@@ -2,7 +2,8 @@
 // src/genie_tk/pair_transform.py:26-61, applied at :182-189 as p = p + dropout(update)).
 // DropoutRowwise draws one mask [B, 1, N, C] shared by every row i, DropoutColumnwise one
 // mask [B, N, 1, C] shared by every column j. The residual epilogues (K2e, K4e) take such a
-// mask as keep bits, B * N vectors of 128 bits, and apply it while they add the residual,
+// mask as keep bits, B * N vectors of ceil(C / 128) groups of 128 bits (generated and packed
+// here as that many 128-bit vectors), and apply it while they add the residual,
 // so the masked update is never written out. This file makes the bit vectors:
 //   dropout_philox_kernel  from a counter-based generator, Philox4x32-10 (Salmon, Moraes,
 //                          Dror, Shaw, "Parallel random numbers: as easy as 1, 2, 3", SC'11):
@@ -79,7 +80,7 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-int drop_args(const gtk_dropout* d, int64_t B, int64_t N, bool transposed, DropArgs* out) {
+int drop_args(const gtk_dropout* d, int64_t B, int64_t N, bool transposed, int channels, DropArgs* out) {
   *out = DropArgs{};
   if (!d) return GTK_OK;  // no dropout
   if (!d->keep_bits) return fail(GTK_ERR_INVALID_ARG, "dropout: keep_bits is NULL");
@@ -93,6 +94,7 @@ int drop_args(const gtk_dropout* d, int64_t B, int64_t N, bool transposed, DropA
   // transposed kernel frame (rows = j) the two swap.
   out->by_row = ((d->shared_across_rows != 0) == transposed) ? 1 : 0;
   out->ld = N;
+  out->groups = (channels + 127) / 128;
   return GTK_OK;
 }
 

@@ -329,11 +329,12 @@ __global__ void __launch_bounds__(256, kSplit == 1 ? 2 : 1)
       if (e.drop.keep != nullptr) {
         const int64_t NN = e.N * e.N;
         const int64_t b = m / NN, rem = m - b * NN, ri = rem / e.N, j = rem - ri * e.N;
-        const uint4 keep = __ldg(e.drop.keep + b * e.drop.ld + (e.drop.by_row ? ri : j));
+        // n .. n+3 lie in one 128-channel group of the keep vector
+        const uint4 keep = __ldg(e.drop.keep + (b * e.drop.ld + (e.drop.by_row ? ri : j)) * e.drop.groups + (n >> 7));
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const int nq = n + q;
-          v[q] *= ((drop_word(keep, nq >> 5) >> (nq & 31)) & 1u) ? e.drop.scale : 0.f;
+          v[q] *= ((drop_word(keep, (nq & 127) >> 5) >> (nq & 31)) & 1u) ? e.drop.scale : 0.f;
         }
       }
     }
@@ -575,9 +576,9 @@ static int common_args(const float* z, const float* out, const void* packed, voi
 }
 
 static int drop_channels(const DropArgs& drop, int channels) {
-  if (drop.keep && channels > 128)
-    return fail(GTK_ERR_UNSUPPORTED, "dropout keep vectors hold 128 channels; this block has " +
-                                         std::to_string(channels));
+  if (drop.keep && drop.groups * 128 < channels)
+    return fail(GTK_ERR_INVALID_ARG, "dropout keep vectors hold " + std::to_string(drop.groups * 128) +
+                                         " channels; this block has " + std::to_string(channels));
   return GTK_OK;
 }
 

@@ -59,8 +59,9 @@ bool dims_ok(int64_t v, int64_t max_v = (int64_t(1) << 31) - 1);
 
 // Validate a public dropout descriptor (NULL = no dropout) for a [B, N, N] pair problem and
 // fill the kernels' DropArgs (defined in gtk_sm100.cuh). `transposed`: the kernel walks the
-// pair tensor as z^T (the ending-node attention).
+// pair tensor as z^T (the ending-node attention). `channels`: the block's channel count; its
+// keep vectors are ceil(channels / 128) groups of 128 bits.
 struct DropArgs;
-int drop_args(const gtk_dropout* d, int64_t B, int64_t N, bool transposed, DropArgs* out);
+int drop_args(const gtk_dropout* d, int64_t B, int64_t N, bool transposed, int channels, DropArgs* out);
 
 }  // namespace gtk

@@ -113,14 +113,16 @@ struct CtaGuard {
   volatile uint32_t abort;  // set when any wait of this CTA ran out
 };
 
-// Channel dropout applied by a residual epilogue: one 128-bit keep vector per (batch,
-// residue t), bit c (word c / 32, bit c % 32) set when channel c is kept; kept channels
-// are multiplied by `scale`. In a kernel's own pair frame (row r, column j) the vector is
-// t = by_row ? r : j, at keep[b * ld + t].
+// Channel dropout applied by a residual epilogue: one keep vector of `groups` x 128 bits
+// per (batch, residue t), channel c at bit c % 32 of word (c % 128) / 32 of its 128-bit group
+// c / 128, set when the channel is kept; kept channels are multiplied by `scale`. In a
+// kernel's own pair frame (row r, column j) the vector is t = by_row ? r : j, at
+// keep[(b * ld + t) * groups].
 struct DropArgs {
   const uint4* keep;
   float scale;
   int by_row;
+  int groups;
   int64_t ld;
 };
 
@@ -128,7 +130,7 @@ struct DropArgs {
 // end of the row (that pair is never stored).
 __device__ __forceinline__ uint4 drop_keep(const DropArgs& d, int b, int r, int j, int n_cols) {
   if (!d.by_row && j >= n_cols) return make_uint4(0u, 0u, 0u, 0u);
-  return __ldg(d.keep + static_cast<int64_t>(b) * d.ld + (d.by_row ? r : j));
+  return __ldg(d.keep + (static_cast<int64_t>(b) * d.ld + (d.by_row ? r : j)) * d.groups);
 }
 
 // Word w of a keep vector (w = 0..3, a runtime index).

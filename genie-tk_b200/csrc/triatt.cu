@@ -1461,7 +1461,7 @@ int gtk_triatt_forward_dropout(int starting, const float* z, const float* mask, 
                                void* stream) {
   DropArgs d{};
   // K4e works in the problem's frame, which is z^T for the ending node.
-  if (int e = drop_args(dropout, B, N, /*transposed=*/!starting, &d)) return e;
+  if (int e = drop_args(dropout, B, N, /*transposed=*/!starting, c_in, &d)) return e;
   return triatt_forward_impl(starting, z, mask, packed, out, add_residual, d, workspace, workspace_bytes, B, N, c_in,
                              c_hidden, heads, inf, status, stream);
 }

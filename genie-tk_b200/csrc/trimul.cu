@@ -1361,7 +1361,7 @@ int gtk_trimul_forward_dropout(int outgoing, const float* z, const float* mask, 
                                int64_t B, int64_t N, int c_z, int c_hidden, uint32_t* status, void* stream) {
   DropArgs d{};
   // The update's pair frame is z's own: DropoutRowwise's vector is the column j.
-  if (int e = drop_args(dropout, B, N, /*transposed=*/false, &d)) return e;
+  if (int e = drop_args(dropout, B, N, /*transposed=*/false, c_z, &d)) return e;
   return trimul_forward_impl(outgoing, z, mask, packed, out, add_residual, d, workspace, workspace_bytes, B, N, c_z,
                              c_hidden, status, stream);
 }

@@ -19,9 +19,9 @@ kernels fuse the projections.
   genie_tk::triatt_residual_dropout_(z, mask, packed, starting, inf, keep_bits, scale, shared_across_rows)
                                                                z += dropout(update), in place
 
-``z`` is ``[B, N, N, 128]`` (any float dtype; fp32 in place), ``mask`` ``[B, N, N]`` or
+``z`` is ``[B, N, N, C]`` (any float dtype; fp32 in place), ``mask`` ``[B, N, N]`` or
 None, ``packed`` the uint8 buffer of ``ops.pack_trimul`` / ``ops.pack_triatt`` /
-``ops.pack_transition``; ``keep_bits`` the int32 [B, N, 4] keep bits of an
+``ops.pack_transition``; ``keep_bits`` the int32 [B, N, 4 ceil(C / 128)] keep bits of an
 ``ops.DropoutMask``. No operator has an autograd formula: the kernels are forward-only.
 """
 

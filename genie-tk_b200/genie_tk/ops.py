@@ -105,8 +105,8 @@ def prepare_pair(z: torch.Tensor, mask: Optional[torch.Tensor], c_expected: int)
 class DropoutMask:
     """A DropoutRowwise / DropoutColumnwise mask as the residual epilogues consume it.
 
-    ``keep_bits`` is int32 [B, N, 4] on the GPU: 128 bits per (b, residue), bit c set when
-    channel c is kept. ``shared_across_rows``: DropoutRowwise (the mask [B, 1, N, C] varies
+    ``keep_bits`` is int32 [B, N, 4 G] on the GPU, G = ceil(C / 128): 128 G bits per
+    (b, residue), bit c % 32 of word c // 32 set when channel c is kept. ``shared_across_rows``: DropoutRowwise (the mask [B, 1, N, C] varies
     with the column j), else DropoutColumnwise ([B, N, 1, C], varies with the row i). Kept
     channels of the update are multiplied by ``scale``."""
 
@@ -114,11 +114,13 @@ class DropoutMask:
     scale: float
     shared_across_rows: bool
 
-    def _struct(self, B: int, N: int):
+    def _struct(self, B: int, N: int, C: int = SUPPORTED_C):
         kb = self.keep_bits
         _require_cuda(kb, "keep_bits", torch.int32)
-        if tuple(kb.shape) != (B, N, 4) or not kb.is_contiguous():
-            raise ValueError(f"keep_bits must be a contiguous int32 [B, N, 4] = [{B}, {N}, 4], got {tuple(kb.shape)}")
+        W = 4 * ((C + 127) // 128)
+        if tuple(kb.shape) != (B, N, W) or not kb.is_contiguous():
+            raise ValueError(f"keep_bits must be a contiguous int32 [B, N, {W}] for {C} channels, "
+                             f"got {tuple(kb.shape)}")
         return _lib.Dropout(ctypes.c_void_p(kb.data_ptr()), float(self.scale), int(bool(self.shared_across_rows)))
 
 
@@ -131,30 +133,31 @@ def dropout_mask_from_multipliers(mult: torch.Tensor, shared_across_rows: bool, 
         want = "[B, 1, N, C]" if shared_across_rows else "[B, N, 1, C]"
         raise ValueError(f"dropout multipliers must be {want}, got {tuple(mult.shape)}")
     C = mult.shape[-1]
-    if C > SUPPORTED_C:
-        raise NotImplementedError(f"genie_tk (B200): dropout keep vectors hold {SUPPORTED_C} channels, got {C}")
+    G = (C + 127) // 128  # 128-channel groups per keep vector
     B = mult.shape[0]
     N = mult.shape[2] if shared_across_rows else mult.shape[1]
     m = mult.reshape(B * N, C).float()
-    if C < SUPPORTED_C:  # channels past C do not exist; their bits are never read
-        m = torch.nn.functional.pad(m, (0, SUPPORTED_C - C), value=1.0)
+    if C < 128 * G:  # channels past C do not exist; their bits are never read
+        m = torch.nn.functional.pad(m, (0, 128 * G - C), value=1.0)
     m = m.contiguous()
-    bits = torch.empty(B, N, 4, dtype=torch.int32, device=mult.device)
-    _lib.check(lib.gtk_dropout_pack_keep_bits(_ptr(m), B * N, _ptr(bits), _stream(mult.device)),
+    bits = torch.empty(B, N, 4 * G, dtype=torch.int32, device=mult.device)
+    _lib.check(lib.gtk_dropout_pack_keep_bits(_ptr(m), B * N * G, _ptr(bits), _stream(mult.device)),
                "gtk_dropout_pack_keep_bits")
     bits._gtk_keepalive = m
     return DropoutMask(bits, float(scale), bool(shared_across_rows))
 
 
 def dropout_mask_philox(B: int, N: int, p: float, seed: int, offset: int, shared_across_rows: bool,
-                        device: torch.device) -> DropoutMask:
-    """A dropout mask from the library's Philox4x32-10 generator (gtk_dropout_keep_bits_philox):
-    reproducible from (seed, offset) alone, independent of torch's generator state."""
+                        device: torch.device, channels: int = SUPPORTED_C) -> DropoutMask:
+    """A dropout mask for ``channels`` channels from the library's Philox4x32-10 generator
+    (gtk_dropout_keep_bits_philox): reproducible from (seed, offset) alone, independent of
+    torch's generator state."""
     lib = _lib.load()
     if not 0.0 <= p < 1.0:
         raise ValueError("dropout probability must be in [0, 1)")
-    bits = torch.empty(B, N, 4, dtype=torch.int32, device=device)
-    _lib.check(lib.gtk_dropout_keep_bits_philox(int(seed) & (2**64 - 1), int(offset) & (2**64 - 1), float(p), B * N,
+    G = (int(channels) + 127) // 128
+    bits = torch.empty(B, N, 4 * G, dtype=torch.int32, device=device)
+    _lib.check(lib.gtk_dropout_keep_bits_philox(int(seed) & (2**64 - 1), int(offset) & (2**64 - 1), float(p), B * N * G,
                                                 _ptr(bits), _stream(bits.device)), "gtk_dropout_keep_bits_philox")
     return DropoutMask(bits, 1.0 / (1.0 - p), bool(shared_across_rows))
 
@@ -212,7 +215,7 @@ def trimul_forward(z: torch.Tensor, mask: Optional[torch.Tensor], packed: torch.
                                     _ptr(status_buffer(zf.device)), _stream(zf.device))
         _lib.check(rc, "gtk_trimul_forward")
         return out
-    d = dropout._struct(B, N)
+    d = dropout._struct(B, N, c_z)
     rc = lib.gtk_trimul_forward_dropout(int(outgoing), _ptr(zf), _ptr(mf), _ptr(packed), _ptr(out), int(add_residual),
                                         ctypes.byref(d), _ptr(ws), ws.numel(), B, N, c_z, c_hidden,
                                         _ptr(status_buffer(zf.device)), _stream(zf.device))
@@ -350,7 +353,7 @@ def triatt_forward(z: torch.Tensor, mask: Optional[torch.Tensor], packed: torch.
                                     _ptr(status_buffer(zf.device)), _stream(zf.device))
         _lib.check(rc, "gtk_triatt_forward")
         return out
-    d = dropout._struct(B, N)
+    d = dropout._struct(B, N, c_in)
     rc = lib.gtk_triatt_forward_dropout(int(starting), _ptr(zf), _ptr(mf), _ptr(packed), _ptr(out), int(add_residual),
                                         ctypes.byref(d), _ptr(ws), ws.numel(), B, N, c_in, c_hidden,
                                         heads, float(inf), _ptr(status_buffer(zf.device)),
@@ -603,7 +606,7 @@ def layernorm(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: flo
 
 def pair_embed(s: torch.Tensor, mask: Optional[torch.Tensor], weight: torch.Tensor, bias: Optional[torch.Tensor],
                rows: Optional[int] = None, row0: int = 0, with_mask: bool = True):
-    """Pair representation [B, rows, N, 128] fp32 (rows row0 .. row0+rows-1 of the N x N
+    """Pair representation [B, rows, N, c_p] fp32 (rows row0 .. row0+rows-1 of the N x N
     grid; all by default) and, with ``with_mask``, the pair mask [B, rows, N]."""
     lib = _lib.load()
     _require_cuda(s, "s")
@@ -611,8 +614,8 @@ def pair_embed(s: torch.Tensor, mask: Optional[torch.Tensor], weight: torch.Tens
         raise ValueError(f"s must be [B, N, c_s], got {tuple(s.shape)}")
     B, N, c_s = s.shape
     c_p = weight.shape[0]
-    if c_p != SUPPORTED_C:
-        raise NotImplementedError(f"genie_tk (B200): pair embedding needs c_p = {SUPPORTED_C}, got {c_p}")
+    if not 1 <= c_p <= 4096:
+        raise NotImplementedError(f"genie_tk (B200): pair embedding takes c_p in 1..4096, got {c_p}")
     if tuple(weight.shape) != (c_p, 2 * c_s):
         raise ValueError(f"weight must be [c_p, 2 c_s] = [{c_p}, {2 * c_s}], got {tuple(weight.shape)}")
     rows = N if rows is None else int(rows)

@@ -114,7 +114,8 @@ class PairEmbedding(nn.Module):
     examples/basic_usage.py:170-199): ``p[b,i,j] = Linear(2 c_s, c_p)([s_i ; s_j])`` and the
     pair mask ``p_mask[b,i,j] = mask[b,i] * mask[b,j]``. Holds the ``weight`` / ``bias`` of
     that ``nn.Linear(c_s * 2, c_p)`` (state-dict compatible with it) and runs on the pair
-    embedding kernels, which never form the concatenated [B, N, N, 2 c_s] tensor. c_p = 128.
+    embedding kernels, which never form the concatenated [B, N, N, 2 c_s] tensor. Any c_p
+    in 1..4096.
     """
 
     def __init__(self, c_s: int, c_p: int):

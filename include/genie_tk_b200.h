@@ -324,7 +324,9 @@ GTK_API int gtk_peer_barrier(const uint64_t* flag_ptrs, int rank, int P, uint32_
 /* ---------------------------------------------------------------------------------
  * Pair transition (reference src/genie_tk/pair_transform.py:64-84, the feed-forward of
  * PairTransformLayer; no counterpart in kernels/bindings.cpp) with the layer's residual and
- * final mask multiply (pair_transform.py:190-193) folded in. c_p = 128, n = 4 only.
+ * final mask multiply (pair_transform.py:190-193) folded in. c_p = 128 with n <= 4 runs on
+ * the tuned kernels (a narrower hidden layer zero-padded to 512 units); other widths (c_p
+ * <= 512, hidden n c_p <= 2048) on the general-shape kernels.
  * ------------------------------------------------------------------------------- */
 typedef struct gtk_transition_params {
   const float* ln_w; /* layer_norm.weight [c_p] */
@@ -338,10 +340,10 @@ typedef struct gtk_transition_params {
 GTK_API size_t gtk_transition_packed_bytes(int c_p, int n);
 GTK_API int gtk_transition_pack(const gtk_transition_params* params, int c_p, int n, void* packed,
                                 size_t packed_bytes, void* stream);
-/* Workspace for the hidden rows: B*N*N*n*c_p fp16. */
+/* Workspace for the hidden rows (fp16). */
 GTK_API size_t gtk_transition_workspace_bytes(int64_t B, int64_t N, int c_p, int n);
 /* out = (add_residual ? z : 0) + transition(z), then times mask[b, i, j] when mask is not
- * NULL. z, out fp32 [B, N, N, 128] (out may equal z); mask fp32 [B, N, N] or NULL. */
+ * NULL. z, out fp32 [B, N, N, c_p] (out may equal z); mask fp32 [B, N, N] or NULL. */
 GTK_API int gtk_transition_forward(const float* z, const float* mask, const void* packed, float* out,
                                    int add_residual, void* workspace, size_t workspace_bytes, int64_t B, int64_t N,
                                    int c_p, int n, uint32_t* status, void* stream);
@@ -351,7 +353,8 @@ GTK_API int gtk_transition_forward(const float* z, const float* mask, const void
  * kernels/bindings.cpp): p[b,i,j] = weight @ [s[b,i]; s[b,j]] + bias (nn.Linear(2 c_s, c_p)
  * on the concatenation, never formed) and p_mask[b,i,j] = mask[b,i] * mask[b,j], written
  * into the fp32 pair layout [B, rows, N, c_p] for rows row0 .. row0+rows-1 (all of them:
- * rows = N, row0 = 0; a row shard otherwise). c_p = 128.
+ * rows = N, row0 = 0; a row shard otherwise). c_p in 1..4096; out 16-byte aligned when c_p
+ * is a multiple of 4 (4-byte aligned otherwise).
  * s fp32 [B, N, c_s]; mask fp32 [B, N] or NULL; weight fp32 [c_p, 2 c_s]; bias [c_p] or
  * NULL; pair_mask fp32 [B, rows, N] or NULL (not written).
  * ------------------------------------------------------------------------------- */
@@ -365,15 +368,17 @@ GTK_API int gtk_pair_embed(const float* s, const float* mask, const float* weigh
  * src/genie_tk/pair_transform.py:26-61, applied at :182-189 as p = p + dropout(update)).
  * DropoutRowwise draws one mask [B, 1, N, C] shared by every row i (it varies with the
  * column j); DropoutColumnwise one mask [B, N, 1, C] shared by every column j (it varies
- * with the row i). Here a mask is a keep-bit array of B * N vectors of 128 bits: vector
- * (b, t) is the four uint32 words at (b * N + t) * 4, and its bit c (word c / 32, bit
- * c % 32) is set when channel c is kept. Kept channels are multiplied by `scale`
+ * with the row i). Here a mask is a keep-bit array of B * N vectors of G = ceil(C / 128)
+ * groups of 128 bits: vector (b, t) is the 4 G uint32 words at (b * N + t) * 4 G, and
+ * channel c is kept when bit c % 32 of word c / 32 of it is set. (For C <= 128 that is four
+ * words per vector; the generator and the packer below make 128-bit groups, so a C-channel
+ * mask is n_vectors = B * N * G of them.) Kept channels are multiplied by `scale`
  * (1 / (1 - p)); dropped ones add nothing. The *_forward_dropout entry points apply the
  * mask inside the residual epilogue: out = z + keep * scale * update (add_residual = 1) or
- * out = keep * scale * update (add_residual = 0). C = 128.
+ * out = keep * scale * update (add_residual = 0).
  * ------------------------------------------------------------------------------- */
 typedef struct gtk_dropout {
-  const uint32_t* keep_bits; /* device, 16-byte aligned, B * N * 4 words */
+  const uint32_t* keep_bits; /* device, 16-byte aligned, B * N * 4 * ceil(C / 128) words */
   float scale;               /* multiplier of the kept channels: finite, >= 0 */
   int shared_across_rows;    /* 1: DropoutRowwise (vector t = j); 0: DropoutColumnwise (t = i) */
 } gtk_dropout;

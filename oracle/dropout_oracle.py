@@ -83,9 +83,10 @@ def unpack_keep(bits: np.ndarray) -> np.ndarray:
 
 
 def multipliers_from_bits(bits: np.ndarray, scale: float, B: int, N: int, rowwise: bool) -> torch.Tensor:
-    """The multiplier tensor a keep-bit array stands for: [B, 1, N, 128] (rowwise) or
-    [B, N, 1, 128] (columnwise), kept channels = scale, dropped = 0."""
-    m = torch.from_numpy(unpack_keep(bits).astype(np.float32) * np.float32(scale)).reshape(B, N, 128)
+    """The multiplier tensor a keep-bit array stands for: [B, 1, N, 128 G] (rowwise) or
+    [B, N, 1, 128 G] (columnwise) for G 128-bit groups per (b, residue), kept channels =
+    scale, dropped = 0."""
+    m = torch.from_numpy(unpack_keep(bits).astype(np.float32) * np.float32(scale)).reshape(B, N, -1)
     return m.unsqueeze(1) if rowwise else m.unsqueeze(2)
 
 

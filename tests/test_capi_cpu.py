@@ -184,11 +184,12 @@ def test_transition_entry_points(lib):
 
 def test_pair_embed_entry_points(lib):
     assert lib.gtk_pair_embed_workspace_bytes(2, 10, 128) == 2 * 2 * 10 * 128 * 4
-    assert lib.gtk_pair_embed_workspace_bytes(1, 10, 64) == 0
+    assert lib.gtk_pair_embed_workspace_bytes(1, 10, 64) == 2 * 10 * 64 * 4
+    assert lib.gtk_pair_embed_workspace_bytes(1, 10, 4097) == 0
     p = ctypes.c_void_p(1 << 20)
     ws = lib.gtk_pair_embed_workspace_bytes(1, 16, 128)
-    # c_p other than 128
-    assert lib.gtk_pair_embed(p, None, p, None, p, None, p, ws, 1, 16, 16, 0, 32, 64, None) == -2
+    # c_p beyond 4096
+    assert lib.gtk_pair_embed(p, None, p, None, p, None, p, ws, 1, 16, 16, 0, 32, 4097, None) == -2
     # a row shard that runs past N
     assert lib.gtk_pair_embed(p, None, p, None, p, None, p, ws, 1, 16, 8, 12, 32, 128, None) == -1
     # workspace too small

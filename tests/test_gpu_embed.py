@@ -44,3 +44,31 @@ def test_module_forward():
     torch.testing.assert_close(p.cpu(), ref, rtol=1e-4, atol=1e-4)
     p2, pm2 = emb(s)
     assert pm2 is None and torch.equal(p2, p)
+
+
+@pytest.mark.parametrize("c_p,c_s", [(64, 32), (256, 48), (96, 16), (130, 20), (7, 9)])
+def test_pair_embed_other_widths(c_p, c_s):
+    """c_p other than 128: several 128-output chunks (256), a partial chunk (96, 130), and
+    widths that are not a multiple of 4 (130, 7: the single-float path), with a row shard."""
+    dev = require_gpu()
+    from genie_tk import ops
+    B, N = 2, 45
+    gen = torch.Generator().manual_seed(c_p * 3 + c_s)
+    s = torch.randn(B, N, c_s, generator=gen)
+    mask = (torch.rand(B, N, generator=gen) > 0.2).float()
+    w = torch.randn(c_p, 2 * c_s, generator=gen) / (2 * c_s) ** 0.5
+    b = 0.1 * torch.randn(c_p, generator=gen)
+    ref, ref_mask = O.pair_embed(s, mask, {"weight": w, "bias": b})
+    p, pm = ops.pair_embed(s.to(dev), mask.to(dev), w.to(dev), b.to(dev))
+    ps, _ = ops.pair_embed(s.to(dev), mask.to(dev), w.to(dev), None, rows=11, row0=30, with_mask=False)
+    torch.cuda.synchronize()
+    assert p.shape == (B, N, N, c_p)
+    torch.testing.assert_close(p.cpu(), ref, rtol=1e-4, atol=1e-4)
+    assert torch.equal(pm.cpu(), ref_mask)
+    torch.testing.assert_close(ps.cpu(), (ref - b)[:, 30:41], rtol=1e-4, atol=1e-4)
+    emb = genie_tk.PairEmbedding(c_s=c_s, c_p=c_p).to(dev)
+    with torch.no_grad():
+        emb.weight.copy_(w)
+        emb.bias.copy_(b)
+    pe, _ = emb(s.to(dev), mask.to(dev))
+    assert torch.equal(pe, p)

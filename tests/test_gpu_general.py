@@ -224,3 +224,43 @@ def test_general_shape_gradients_match_oracle(op, c_z, c, H):
     named = dict(mod.named_parameters())
     for k, g in zip(pp.keys(), grads[1:]):
         assert _rel(named[k].grad, g) < 1e-2, (k, _rel(named[k].grad, g))
+
+
+@pytest.mark.parametrize("kind", ["trimul_out", "triatt_end"])
+@pytest.mark.parametrize("c_z", [256, 200])
+def test_dropout_wider_than_128_channels(kind, c_z):
+    """Keep vectors of ceil(C / 128) 128-bit groups: C = 256 (two whole groups) and 200 (a
+    partial second group), both dropout axes, the reference's own nn.Dropout draw packed
+    (dropout_mask_from_multipliers) and the library's generator (dropout_mask_philox)."""
+    dev = require_gpu()
+    from genie_tk import ops
+    B, N = 2, 37
+    gen = torch.Generator().manual_seed(c_z + len(kind))
+    z = torch.randn(B, N, N, c_z, generator=gen).to(dev)
+    mask = torch.ones(B, N, N, device=dev)
+    mask[-1, -3:, :] = 0
+    params = to_dev(O.make_trimul_params(c_z, 32, gen, gate_bias=1.0) if kind.startswith("trimul")
+                    else O.make_triatt_params(c_z, 32, 4, gen, gate_bias=1.0), dev)
+    packed = ops.pack_trimul(params, dev) if kind.startswith("trimul") else ops.pack_triatt(params, dev, 4)
+    upd = _oracle(kind, z, mask, params, 4)
+    for rowwise in (True, False):
+        shape = (B, 1, N, c_z) if rowwise else (B, N, 1, c_z)
+        mult = (torch.rand(shape, generator=gen) > 0.3).float().to(dev) / 0.7
+        drops = [(ops.dropout_mask_from_multipliers(mult, rowwise, 1 / 0.7), mult),
+                 (ops.dropout_mask_philox(B, N, 0.3, seed=5, offset=int(rowwise), shared_across_rows=rowwise,
+                                          device=dev, channels=c_z), None)]
+        for drop, m in drops:
+            assert tuple(drop.keep_bits.shape) == (B, N, 4 * ((c_z + 127) // 128))
+            if m is None:
+                bits = drop.keep_bits.cpu().numpy().view(np.uint32).reshape(-1, 4)
+                m = D.multipliers_from_bits(bits, drop.scale, B, N, rowwise)[..., :c_z].to(dev)
+            out = torch.empty_like(z)
+            if kind.startswith("trimul"):
+                ops.trimul_forward(z, mask, packed, True, out=out, add_residual=True, dropout=drop)
+            else:
+                ops.triatt_forward(z, mask, packed, False, out=out, add_residual=True, dropout=drop)
+            torch.cuda.synchronize()
+            assert_status_clean(dev)
+            assert_parity(out, z + upd * m, what=f"{kind} c_z={c_z} dropout rowwise={rowwise}")
+            dropped = (m == 0).expand_as(out)
+            assert torch.equal(out[dropped], z[dropped])
