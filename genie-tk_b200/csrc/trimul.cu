@@ -722,8 +722,8 @@ __global__ void __launch_bounds__(k2e::kThreads, 1)
                          const float* __restrict__ vec, int add_residual, float x_scale, int N, int rows, int n_jt,
                          int n_tiles, uint32_t* status, const DropArgs drop) {
   using namespace k2e;
-  const int c_real = static_cast<int>(__ldg(vec + tmpack::kVC));  // real hidden channels (<= 128)
-  const float inv_c = 1.f / static_cast<float>(c_real);
+  const float c_real = __ldg(vec + tmpack::kVC);  // real hidden channels (<= 128)
+  const float n_pad = 128.f - c_real, inv_c = 1.f / c_real;
   extern __shared__ uint8_t dsmem[];
   uint8_t* smem = align1024(dsmem);
   K2eBars* bars = reinterpret_cast<K2eBars*>(smem + kBar);
@@ -974,21 +974,24 @@ __global__ void __launch_bounds__(k2e::kThreads, 1)
       w = w && mbar_wait(&bars->d_full[s], (it >> 1) & 1, guard, status, kStatusTimeoutConsumer);
       ok = __all_sync(0xffffffffu, w);
       if (!ok) break;
-      // LN_out statistics over the c_real channels of pair p (x is stored times x_scale; the
-      // channels past c_real of a narrower update are zero padding)
+      // LN_out statistics over the c_real channels of pair p (x is stored times x_scale). The
+      // channels past c_real of a narrower update are exact zeros: the loop runs over all 128
+      // (a constant trip count keeps the chains in registers) and the n_pad zero channels'
+      // terms, -x0 and x0^2 each, are taken out again (nothing to take out at 128 channels).
       const uint8_t* xb = smem + kX + (p >> 6) * 16384;
       const int pj = p & 63;
       const float x0 = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(xb + swz128(0, pj >> 3) + (pj & 7) * 2)));
       float a1[4] = {0.f, 0.f, 0.f, 0.f}, a2[4] = {0.f, 0.f, 0.f, 0.f};  // four chains each
 #pragma unroll 16
-      for (int c = 0; c < c_real; ++c) {
+      for (int c = 0; c < 128; ++c) {
         const float xv = __half2float(
                              __ushort_as_half(*reinterpret_cast<const uint16_t*>(xb + swz128(c, pj >> 3) + (pj & 7) * 2))) -
                          x0;
         a1[c & 3] += xv;
         a2[c & 3] = fmaf(xv, xv, a2[c & 3]);
       }
-      const float s1 = (a1[0] + a1[1]) + (a1[2] + a1[3]), s2 = (a2[0] + a2[1]) + (a2[2] + a2[3]);
+      const float s1 = ((a1[0] + a1[1]) + (a1[2] + a1[3])) + n_pad * x0;
+      const float s2 = ((a2[0] + a2[1]) + (a2[2] + a2[3])) - n_pad * x0 * x0;
       mbar_arrive_after(&bars->x_empty, s1 + s2);  // the x tile may be reloaded: its values are consumed
       const float d1 = s1 * inv_c;
       const float mu_x = x0 + d1;
