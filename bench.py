@@ -94,17 +94,69 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle-reason sampling while the timed region runs."""
+    """SM clocks and throttle reasons of this process's GPU while the timed region runs.
+
+    NVML (read-only queries) is polled every 20 ms from a thread, so even a timed region of
+    a tenth of a second (8 GPUs x 10 steps) gets samples; without NVML, nvidia-smi samples at
+    200 ms. The GPU is found by its UUID (then PCI bus id, then index), so a job that was
+    given a subset of a node's GPUs samples its own."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event (throttle) reason bits
+    REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+                   "hw_thermal_slowdown": 0x40}
 
-    def __init__(self):
+    def __init__(self, device=None):
+        self.device = torch.device("cuda", 0) if device is None else torch.device(device)
         self.proc = None
         self.path = None
+        self.thread = None
+        self.samples = []  # (sm MHz, max sm MHz, reason bits)
+
+    def _nvml_handle(self, nv):
+        props = torch.cuda.get_device_properties(self.device)
+        tries = []
+        uuid = getattr(props, "uuid", None)
+        if uuid is not None:
+            tries.append(lambda: nv.nvmlDeviceGetHandleByUUID("GPU-" + str(uuid)))
+        if hasattr(props, "pci_bus_id"):
+            bus = f"{getattr(props, 'pci_domain_id', 0):08x}:{props.pci_bus_id:02x}:{getattr(props, 'pci_device_id', 0):02x}.0"
+            tries.append(lambda: nv.nvmlDeviceGetHandleByPciBusId(bus))
+        tries.append(lambda: nv.nvmlDeviceGetHandleByIndex(self.device.index or 0))
+        for t in tries:
+            try:
+                return t()
+            except Exception:
+                continue
+        return None
 
     def start(self):
+        import threading
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            h = self._nvml_handle(nv)
+            if h is None:
+                raise RuntimeError("no NVML handle")
+            reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
+            mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            self.stop_flag = threading.Event()
+
+            def poll():
+                while not self.stop_flag.is_set():
+                    try:
+                        self.samples.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM), mx, int(reasons(h))))
+                    except Exception:
+                        pass
+                    self.stop_flag.wait(0.02)
+            self.thread = threading.Thread(target=poll, daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.thread = None
         exe = shutil.which("nvidia-smi")
         if not exe:
             return
@@ -114,35 +166,47 @@ class ClockSampler:
         self.proc = subprocess.Popen([exe, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                                       "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
 
-    def stop(self, gpus):
+    def stop(self):
+        """This GPU's samples: a list of (sm MHz, max sm MHz, reason bits)."""
+        if self.thread is not None:
+            self.stop_flag.set()
+            self.thread.join(timeout=5)
+            return list(self.samples)
         if not self.proc:
-            return None
+            return []
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
         self.f.close()
-        sm, mx, reasons = [], [], set()
+        out = []
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         with open(self.path) as f:
             for line in f:
                 parts = [p.strip() for p in line.split(",")]
-                if len(parts) < 9 or not parts[0].isdigit() or int(parts[0]) not in gpus:
+                if len(parts) < 9 or not parts[0].isdigit() or int(parts[0]) != (self.device.index or 0):
                     continue
                 try:
-                    sm.append(float(parts[1]))
-                    mx.append(float(parts[2]))
+                    sm, mxc = float(parts[1]), float(parts[2])
                 except ValueError:
                     continue
+                bits = 0
                 for n, v in zip(names, parts[5:9]):
                     if v.lower().startswith("active"):
-                        reasons.add(n)
+                        bits |= self.REASON_BITS[n]
+                out.append((sm, mxc, bits))
         os.unlink(self.path)
-        if not sm:
+        return out
+
+    @classmethod
+    def summary(cls, samples):
+        """Median SM clock, max clock and the reasons seen, over samples of one or more GPUs."""
+        if not samples:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        reasons = sorted(n for n, bit in cls.REASON_BITS.items() if any(s[2] & bit for s in samples))
+        return {"sm_mhz": statistics.median(s[0] for s in samples), "sm_max_mhz": max(s[1] for s in samples),
+                "reasons": reasons, "samples": len(samples)}
 
 
 def make_stack(n_layers: int, device, seed: int = 1005):
@@ -392,9 +456,8 @@ def run_ours(args, rank, world, device):
     torch.cuda.synchronize()
     ops.check_status(device)
 
-    sampler = ClockSampler()
-    if rank == 0:
-        sampler.start()
+    sampler = ClockSampler(device)
+    sampler.start()
     per_kernel = {}
     timing_mode = "graph-events"
     barrier()
@@ -417,7 +480,7 @@ def run_ours(args, rank, world, device):
     torch.cuda.synchronize()
     barrier()
     elapsed_ms = t_start.elapsed_time(t_stop)
-    clocks = sampler.stop(set(range(world))) if rank == 0 else None
+    clocks = ClockSampler.summary(sampler.stop())
     if timing_mode == "eager-events":
         for _ in range(args.steps):
             labels.clear()
@@ -518,9 +581,8 @@ def run_sharded(args, rank, world, device):
     ops.check_status(device)
     so.launches = 0
 
-    sampler = ClockSampler()
-    if rank == 0:
-        sampler.start()
+    sampler = ClockSampler(device)
+    sampler.start()
     dist.barrier()
     torch.cuda.synchronize()
     t0 = torch.cuda.Event(enable_timing=True)
@@ -531,7 +593,10 @@ def run_sharded(args, rank, world, device):
     t1.record()
     torch.cuda.synchronize()
     dist.barrier()
-    clocks = sampler.stop(set(range(world))) if rank == 0 else None
+    # every rank samples its own GPU; rank 0 reports all of them together
+    per_rank = [None] * world
+    dist.all_gather_object(per_rank, sampler.stop())
+    clocks = ClockSampler.summary([x for r in per_rank for x in r])
     launches = so.launches
     elapsed = torch.tensor([t0.elapsed_time(t1)], device=device)
     dist.all_reduce(elapsed, op=dist.ReduceOp.MAX)
