@@ -668,19 +668,22 @@ __global__ void __launch_bounds__(k2::kThreads, 1)
 
 // ----------------------------------------------------------------------------------
 // K2e: persistent LN_out + linear_z + output gate (+ residual). Tile = 128 consecutive
-// pairs; CTAs loop over tiles. 480 threads:
+// pairs; CTAs loop over tiles. 608 threads:
 //   warps 0-7   LayerNorm producers for the gate: LN_in(z) of the tile's pairs, two threads
 //               per pair (64 channels each, combined with one shuffle), read from the
 //               TMA-staged z tile into registers and, once all 256 have read it, written as
 //               the fp16 operand A over the first half of the same buffer;
-//   warps 8-11  epilogue: thread = pair p (TMEM lane); LN_out statistics from the x tile
-//               in shared memory; then four 32-channel slabs: the residual slab of z arrives
-//               by TMA, is updated in place with gate * linear_z(LN_out(x)) and leaves by
-//               TMA store (a ring of 4 slab buffers, so residual loads run well ahead), so
-//               every global access is a bulk tensor copy;
-//   warp 12     lane 0: MMA issuer;
-//   warp 13     lane 0: TMA for the weights (once), the z tile and the x tile;
-//   warp 14     lane 0: slab manager -- TMA loads of the residual slabs and TMA stores of
+//   warps 8-15  epilogue: thread = pair p (TMEM lane), two warps per lane quarter; each
+//               takes the pair's LN_out statistics from the x tile in shared memory, then
+//               warps 8-11 finish the 32-channel slabs 0 and 1 and warps 12-15 slabs 2 and 3:
+//               the residual slab of z arrives by TMA, is updated in place with
+//               gate * linear_z(LN_out(x)) and leaves by TMA store (one buffer per slab, so
+//               the next tile's residual loads run ahead), so every global access is a bulk
+//               tensor copy. (With one epilogue warp per scheduler, warps 8-11 only, the
+//               epilogue was the critical path at ~9,800 cycles per tile, clock64 trace.)
+//   warp 16     lane 0: MMA issuer;
+//   warp 17     lane 0: TMA for the weights (once), the z tile and the x tile;
+//   warp 18     lane 0: slab manager -- TMA loads of the residual slabs and TMA stores of
 //               the finished ones (a slab buffer is reloaded once its store has read it).
 // TMEM (double buffered per tile, 256 columns each): G = A W_g^T at +0, U = x^T (W_z gamma)^T
 // at +128. LN_out folds into the epilogue: out = g * (rstd (U - mu u) + v), with the gate
@@ -691,11 +694,12 @@ __global__ void __launch_bounds__(k2::kThreads, 1)
 // warp load touching 32 separate pairs, held this kernel at ~17k cycles per tile.)
 // ----------------------------------------------------------------------------------
 namespace k2e {
-constexpr int kThreads = 480;
+constexpr int kThreads = 608;
 constexpr int kSlabs = 4;
 constexpr uint32_t kW = 0, kZ = 65536, kA = kZ, kX = 131072, kO = 163840, kVec = 229376, kBar = 229376 + 1536;
 constexpr uint32_t kSmem = kBar + 256 + 1024;
 static_assert(kO + kSlabs * 16384 <= kVec, "K2e slabs");
+static_assert(kSlabs == 4, "one slab buffer per 32-channel slab of a tile");
 static_assert(kSmem <= 232448, "K2e shared memory");
 }  // namespace k2e
 
@@ -739,10 +743,10 @@ __global__ void __launch_bounds__(k2e::kThreads, 1)
     mbar_init(&bars->a_full, 256);
     mbar_init(&bars->a_empty, 1);
     mbar_init(&bars->x_full, 1);
-    mbar_init(&bars->x_empty, 1 + 128);
+    mbar_init(&bars->x_empty, 1 + 256);
     for (int x = 0; x < 2; ++x) {
       mbar_init(&bars->d_full[x], 1);
-      mbar_init(&bars->d_empty[x], 128);
+      mbar_init(&bars->d_empty[x], 256);
     }
     for (int x = 0; x < kSlabs; ++x) {
       mbar_init(&bars->o_full[x], 1);
@@ -756,7 +760,7 @@ __global__ void __launch_bounds__(k2e::kThreads, 1)
     svec[128 + tid] = vec[tmpack::kVU + tid];
     svec[256 + tid] = vec[tmpack::kVV + tid];
   }
-  if (warp == 12) {
+  if (warp == 16) {
     tmem_alloc(&bars->tslot, 512);
     tmem_relinquish();
   }
@@ -817,7 +821,7 @@ __global__ void __launch_bounds__(k2e::kThreads, 1)
       fence_proxy_async_smem();
       mbar_arrive(&bars->a_full);
     }
-  } else if (warp == 12) {
+  } else if (warp == 16) {
     // ------------------------------ MMA issuer ------------------------------
     if (lane == 0) {
       bool ok = mbar_wait(&bars->wbar, 0, guard, status, kStatusTimeoutMma);
@@ -855,7 +859,7 @@ __global__ void __launch_bounds__(k2e::kThreads, 1)
         mbar_wait_drain(&bars->drain, 0);
       }
     }
-  } else if (warp == 13) {
+  } else if (warp == 17) {
     // ------------------- TMA producer: weights, z tiles, x tiles -------------------
     if (lane == 0) {
       mbar_arrive_expect_tx(&bars->wbar, 65536);
@@ -903,7 +907,7 @@ __global__ void __launch_bounds__(k2e::kThreads, 1)
       }
       mbar_wait_drain(&bars->wbar, 0);
     }
-  } else if (warp == 14) {
+  } else if (warp == 18) {
     // ---------------- slab manager: residual loads and output stores ----------------
     // Slab sn (four per tile, 32 channels each) lives in buffer sn % 4. Its output store is
     // issued once the 128 epilogue threads have written it; once that store has read the
@@ -958,10 +962,12 @@ __global__ void __launch_bounds__(k2e::kThreads, 1)
     }
   } else {
     // ------------------------- epilogue: thread = pair -------------------------
-    const int q4 = warp & 3;
+    // Two warps per TMEM lane quarter: warps 8-11 finish slabs 0, 1 (channels 0-63) and
+    // warps 12-15 slabs 2, 3 of every tile; both take the pair's LN_out statistics.
+    const int q4 = warp & 3, hh = (warp - 8) >> 2;
     const int p = q4 * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
-    int it = 0, slab = 0;
+    int it = 0;
     bool ok = true;
     for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++it) {
       const int s = it & 1;
@@ -999,12 +1005,12 @@ __global__ void __launch_bounds__(k2e::kThreads, 1)
       const float rstd_x = rsqrtf(var + 1e-5f * x_scale * x_scale);
       tc_fence_after();
 #pragma unroll 1
-      for (int cc = 0; cc < 4; ++cc, ++slab) {
-        const int sl = slab % kSlabs;
+      for (int cc = 2 * hh; cc < 2 * hh + 2; ++cc) {
+        const int sl = cc;  // slab it * 4 + cc of this CTA lives in buffer cc
         uint32_t g[32], u[32];
         tmem_ld32(tmem + lane_off + s * 256 + cc * 32, g);
         tmem_ld32(tmem + lane_off + s * 256 + 128 + cc * 32, u);
-        ok = __all_sync(0xffffffffu, mbar_wait(&bars->o_full[sl], (slab / kSlabs) & 1, guard, status,
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars->o_full[sl], it & 1, guard, status,
                                                kStatusTimeoutConsumer));
         tmem_wait_ld();
         if (!ok) break;
@@ -1036,7 +1042,7 @@ __global__ void __launch_bounds__(k2e::kThreads, 1)
           *reinterpret_cast<float4*>(ob + swz128(p, q)) = make_float4(o[0], o[1], o[2], o[3]);
         }
         fence_proxy_async_smem();
-        mbar_arrive(&bars->slab_ready[sl]);  // warp 14 stores the slab
+        mbar_arrive(&bars->slab_ready[sl]);  // warp 18 stores the slab
       }
       if (!ok) break;
       tc_fence_before();
@@ -1045,7 +1051,7 @@ __global__ void __launch_bounds__(k2e::kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 12) {
+  if (warp == 16) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
