@@ -223,6 +223,25 @@ __global__ void __launch_bounds__(k1::kThreads, 1)
     }
     const uint32_t idesc = make_idesc_f16(128, 128, 0, 0);
     const uint32_t w0 = smem_u32(smem + k1::kW), a0 = smem_u32(smem + k1::kA);
+    // thread 0: the MMAs of accumulator half h of tile ti, once the epilogue has drained
+    // half h of tile ti - 1; the second half also releases A
+    auto issue_half = [&](int h, int ti) -> bool {
+      if (ti >= 1 && !mbar_wait(&bars->d_empty[h], (ti - 1) & 1, guard, status, kStatusTimeoutMma)) return false;
+      tc_fence_after();
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int chunk = 2 * h + q;
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const int kh = ks >> 2, kin = ks & 3;
+          umma_ss(tmem + h * 256 + q * 128, make_sdesc(w0 + kh * 65536 + chunk * 16384 + kin * 32, 16, 1024, Swz::k128),
+                  make_sdesc(a0 + kh * 16384 + kin * 32, 16, 1024, Swz::k128), idesc, ks > 0 ? 1u : 0u);
+        }
+      }
+      umma_commit(&bars->d_full[h]);
+      if (h == 1) umma_commit(&bars->a_empty);
+      return true;
+    };
     bool ok = true;
     int it = 0;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
@@ -263,6 +282,11 @@ __global__ void __launch_bounds__(k1::kThreads, 1)
             ++loaded;
           }
         }
+        // the previous tile's second-half MMAs, issued only now that this tile's z has been
+        // read: thread 0 blocks on the tensor-core queue while it issues, and with all of a
+        // tile's MMAs issued before the next z read, the z refill (which waits for every
+        // producer) started ~4,000 cycles later (clock64 trace)
+        if (w && lane == 0 && it >= 1) w = issue_half(1, it - 1);
         ok = __all_sync(0xffffffffu, w);
         if (!ok) break;
       }
@@ -297,34 +321,22 @@ __global__ void __launch_bounds__(k1::kThreads, 1)
       fence_proxy_async_smem();
       mbar_arrive(&bars->a_full);
       if (warp == 0) {
-        // thread 0: the tile's MMAs, half h once the epilogue has drained half h of the
-        // previous tile
+        // thread 0: the tile's first-half MMAs (the second half follows the next z read)
         bool mw = true;
         if (lane == 0) {
           mw = mbar_wait(&bars->a_full, it & 1, guard, status, kStatusTimeoutMma);
           if (mw && it == 0) mw = mbar_wait(&bars->wbar, 0, guard, status, kStatusTimeoutMma);
-          for (int h = 0; mw && h < 2; ++h) {
-            if (it >= 1) mw = mbar_wait(&bars->d_empty[h], (it - 1) & 1, guard, status, kStatusTimeoutMma);
-            if (!mw) break;
-            tc_fence_after();
-#pragma unroll
-            for (int q = 0; q < 2; ++q) {
-              const int chunk = 2 * h + q;
-#pragma unroll
-              for (int ks = 0; ks < 8; ++ks) {
-                const int kh = ks >> 2, kin = ks & 3;
-                umma_ss(tmem + h * 256 + q * 128,
-                        make_sdesc(w0 + kh * 65536 + chunk * 16384 + kin * 32, 16, 1024, Swz::k128),
-                        make_sdesc(a0 + kh * 16384 + kin * 32, 16, 1024, Swz::k128), idesc, ks > 0 ? 1u : 0u);
-              }
-            }
-            umma_commit(&bars->d_full[h]);
-          }
-          if (mw) umma_commit(&bars->a_empty);
+          if (mw) mw = issue_half(0, it);
         }
         ok = __all_sync(0xffffffffu, mw);
         if (!ok) break;
       }
+    }
+    if (ok && warp == 0) {
+      // the last tile's second half
+      bool mw = true;
+      if (lane == 0) mw = issue_half(1, it - 1);
+      ok = __all_sync(0xffffffffu, mw);
     }
     if (!ok && tid == 0) {
       // abort: wait (bounded) for this thread's MMAs and TMA loads still in flight
