@@ -125,3 +125,28 @@ def test_narrower_hidden_runs_on_the_tuned_kernels(c, N, B, outgoing):
     assert_parity(got, ref, what=f"trimul c_hidden={c} N={N}")
     assert_parity(z2, zd + ref, what="residual in place")
     assert_status_clean(dev)
+
+
+@pytest.mark.parametrize("outgoing", [True, False])
+def test_narrower_hidden_with_dropout(outgoing):
+    """The tuned kernels' dropout instantiation (K2e<1>) at c_hidden = 64: the keep bits act on
+    the 128 output channels, the zero-padded hidden channels only on LN_out's statistics."""
+    dev = require_gpu()
+    import numpy as np
+    from genie_tk import ops
+    from oracle import dropout_oracle as D
+    B, N, c = 2, 96, 64
+    gen = torch.Generator().manual_seed(17 + int(outgoing))
+    z = torch.randn(B, N, N, 128, generator=gen).to(dev)
+    mask = (torch.rand(B, N, N, generator=gen) > 0.2).float().to(dev)
+    params = to_dev(O.make_trimul_params(128, c, gen, ln_random=True, bias_random=True), dev)
+    packed = ops.pack_trimul(params, dev)
+    drop = ops.dropout_mask_philox(B, N, 0.25, seed=3, offset=1, shared_across_rows=True, device=dev)
+    out = torch.empty_like(z)
+    ops.trimul_forward(z, mask, packed, outgoing, out=out, add_residual=True, dropout=drop)
+    torch.cuda.synchronize()
+    assert_status_clean(dev)
+    bits = drop.keep_bits.cpu().numpy().view(np.uint32).reshape(-1, 4)
+    mult = D.multipliers_from_bits(bits, drop.scale, B, N, True).to(dev)
+    ref = z + O.trimul_forward(z, mask, params, outgoing=outgoing) * mult
+    assert_parity(out, ref, what=f"trimul c_hidden={c} dropout outgoing={outgoing}")
