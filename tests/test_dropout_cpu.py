@@ -141,3 +141,23 @@ def test_dropout_entry_points_validate_arguments(lib):
         assert call(L.Dropout(fake, -1.0, 0)) == -1
         msg = lib.gtk_last_error_string().decode()
         assert "dropout" in msg
+
+
+def test_multipliers_from_bits_with_channel_groups():
+    """A C-channel mask is ceil(C / 128) consecutive 128-bit groups per (b, residue): group g
+    of vector (b, t) holds channels 128 g .. 128 g + 127."""
+    rng = np.random.default_rng(5)
+    B, N, C = 2, 3, 200
+    G = (C + 127) // 128
+    keep = rng.random((B * N, G * 128)) > 0.3
+    keep[:, C:] = True  # channels past C do not exist
+    bits = D.pack_keep(keep.reshape(-1, 128))            # [B * N * G, 4]
+    assert bits.shape == (B * N * G, 4)
+    m = D.multipliers_from_bits(bits, 2.0, B, N, rowwise=False)
+    assert tuple(m.shape) == (B, N, 1, G * 128)
+    want = torch.from_numpy(keep.astype(np.float32) * 2.0).reshape(B, N, 1, G * 128)
+    assert torch.equal(m, want)
+    # the same bits read as int32 [B, N, 4 G] (the library's keep_bits tensor) unpack alike
+    kb = bits.view(np.int32).reshape(B, N, 4 * G)
+    m2 = D.multipliers_from_bits(kb.view(np.uint32).reshape(-1, 4), 2.0, B, N, rowwise=True)
+    assert tuple(m2.shape) == (B, 1, N, G * 128) and torch.equal(m2[:, 0], want[:, :, 0])
