@@ -15,7 +15,9 @@ every exchange goes through the collective into local memory first:
               "gather": the b planes are all-gathered (every rank needs all rows j) and, for
               the incoming update, an all-to-all gives each rank its columns i of every row
               k of a; local rows i are contracted against all j: (P-1) planes (+ (P-1)/P).
-              "auto" takes the one that moves fewer bytes: gather for P <= 3.
+              "auto": channels whenever the x exchange is fused into the contraction's stores
+              (peer exchange, rows per rank a multiple of 128), else the one that moves
+              fewer bytes (gather for P <= 3).
   TriAttStart local rows i; the triangle bias bias[h, j, k] is needed for all rows j, so
               each rank computes its rows and the bias region is all-gathered.
   TriAttEnd   End(z) = Start(z^T)^T with the mask transposed: an all-to-all transpose
@@ -233,10 +235,6 @@ class ShardedTrianglePairStack:
         self.stack = stack
         self.world, self.rank = world, rank
         self.stage_ops = stage_ops
-        # bytes each rank moves per multiplicative update: gather (P-1) planes (+ (P-1)/P for
-        # the incoming a), channels 3 (P-1)/P planes -> the gather wins for P <= 3
-        self.trimul_exchange = trimul_exchange if trimul_exchange != "auto" else (
-            "gather" if world <= 3 else "channels")
         self.exchange = exchange
         # peer mode, channel shards: K1 stores each channel group straight into its owner's
         # buffer (no push pass). Measured slower on 8 B200s (14.7 vs 14.1 ms per step): the
@@ -252,6 +250,9 @@ class ShardedTrianglePairStack:
         # planes (one kernel instead of K2 + the x push), when each rank's rows are a
         # multiple of 128
         self.fused_x = fused_x
+        # "auto" is settled once N is known (the buffers are sized); until then the byte rule
+        self._trimul_request = trimul_exchange
+        self.trimul_exchange = self._resolve_trimul_exchange(None) if trimul_exchange == "auto" else trimul_exchange
         self._key = None
         self._buf: Dict[str, Tensor] = {}
         self._peer: Dict[str, PeerBuffer] = {}
@@ -259,10 +260,26 @@ class ShardedTrianglePairStack:
         self._ipc_open: List[int] = []    # peer mappings opened here
         self._epoch = 0
 
+    def _resolve_trimul_exchange(self, N: Optional[int]) -> str:
+        """The multiplicative update's exchange for "auto" (N = None: not known yet).
+
+        Bytes each rank moves per update outside the kernels: the gather (P-1) planes (+
+        (P-1)/P for the incoming a), the channel shards 3 (P-1)/P -- the gather wins for
+        P <= 3. With the peer exchange and a multiple of 128 rows per rank, the channel
+        shards' x exchange is fused into the contraction's stores, leaving 2 (P-1)/P planes
+        of pushes, fewer than the gather's at every P: 33.0-33.3 against 33.6 ms per step on
+        2 B200s at N = 1024, both bitwise equal to the one-GPU result."""
+        fused = self.exchange == "peer" and self.fused_x and N is not None and (N // self.world) % 128 == 0
+        if fused:
+            return "channels"
+        return "gather" if self.world <= 3 else "channels"
+
     # ---------------------------------------------------------------- buffers
     def _sizes(self, spec: ShardSpec):
         """(local buffers, buffers other ranks write into), name -> bytes."""
         B, N, R = spec.B, spec.N, spec.R
+        if self._trimul_request == "auto":
+            self.trimul_exchange = self._resolve_trimul_exchange(N)
         plane = B * R * C * N * 2          # one rank's planes, fp16, pitch N (row or channel shard)
         lay = self.stage_ops.triatt_layout(B, R, N)
         pair_loc = B * R * N * PAIR_BYTES  # one row shard of the pair tensor, fp32

@@ -188,3 +188,19 @@ def test_gloo_two_ranks_match_emulation(tmp_path):
     ref = O.stack_forward(z, mask, params, no_heads=4)
     err = (got - ref).abs()
     assert float(err.max()) <= MAX_ABS and float(err.mean()) <= MEAN_ABS
+
+
+def test_auto_trimul_exchange_prefers_fused_channel_shards():
+    """"auto": the channel shards whenever their x exchange is fused into the contraction's
+    stores (peer exchange, a multiple of 128 rows per rank); otherwise the exchange that
+    moves fewer bytes (the gather for P <= 3)."""
+    import genie_tk
+    from genie_tk.sharded import ShardedTrianglePairStack
+    st = genie_tk.TrianglePairStack(1)
+    peer = ShardedTrianglePairStack(st, 2, 0, exchange="peer")
+    assert peer._resolve_trimul_exchange(1024) == "channels"      # 512 rows per rank
+    assert peer._resolve_trimul_exchange(200) == "gather"         # 100 rows: no fused stores
+    assert ShardedTrianglePairStack(st, 2, 0, exchange="peer", fused_x=False)._resolve_trimul_exchange(1024) == "gather"
+    assert ShardedTrianglePairStack(st, 2, 0, exchange="nccl")._resolve_trimul_exchange(1024) == "gather"
+    assert ShardedTrianglePairStack(st, 8, 0, exchange="nccl")._resolve_trimul_exchange(1024) == "channels"
+    assert ShardedTrianglePairStack(st, 2, 0, exchange="peer", trimul_exchange="gather").trimul_exchange == "gather"
