@@ -126,9 +126,9 @@ def test_fused_attention_transpose_matches_separate_pushes():
 def test_fused_x_scatter_matches_separate_push():
     """Channel shards with 128 rows per rank: K2 stores each x tile straight into its row
     owner's planes (gtk_trimul_contract_to_peers); equal to K2 + the x push, and the oracle."""
-    z, mask, params = _problem(1, 512, 1)
-    got = _run_emulated_peer(z, mask, params, 4, "channels")
-    sep = _run_emulated_peer(z, mask, params, 4, "channels", fused_transpose=False, fused_x=False)
+    z, mask, params = _problem(1, 256, 1)  # two ranks of 128 rows (the smallest fused case)
+    got = _run_emulated_peer(z, mask, params, 2, "channels")
+    sep = _run_emulated_peer(z, mask, params, 2, "channels", fused_transpose=False, fused_x=False)
     assert float((got - sep).abs().max()) <= 1e-5
     err = (got - O.stack_forward(z, mask, params, no_heads=4)).abs()
     assert float(err.max()) <= MAX_ABS and float(err.mean()) <= MEAN_ABS
