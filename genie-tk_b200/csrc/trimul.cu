@@ -114,8 +114,10 @@ __global__ void trimul_pack_kernel(gtk_trimul_params p, uint8_t* packed, int c) 
 //              Thread 0 is also the TMA producer and MMA issuer: the 128 KB of packed
 //              weights are loaded once; each tile's 128 x 128 fp32 z block arrives by TMA
 //              (64 KB), refilled as soon as all producers have read it; after writing its
-//              part of A it issues the tile's MMAs. No warp is spent on issuing alone, so
-//              sixteen warps keep 128 registers per thread.
+//              part of A it issues the tile's first-half MMAs, and the second half after
+//              it has read the next tile's z (the issuing thread blocks on the tensor-core
+//              queue, and the z refill waits for every producer). No warp is spent on
+//              issuing alone, so sixteen warps keep 128 registers per thread.
 //   warps 8-15 epilogue: thread = channel c (TMEM lane quarter = warp % 4), warps 8-11 take
 //              pairs 0-63 of the tile and warps 12-15 pairs 64-127, in 16-pair chunks of the
 //              projection / gate accumulators (the next chunk's TMEM loads in flight while
