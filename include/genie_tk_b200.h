@@ -22,11 +22,12 @@
  *  - Shapes: the multiplicative update with c_z = 128, c_hidden <= 128, attention with
  *    c_in = 128 and 4 heads of head_dim <= 32, and the transition with c_p = 128, n <= 4
  *    run on the tuned tcgen05 kernels (narrower hidden widths and head dims are
- *    zero-padded in the packed weights, which changes no result). Every other shape the reference's modules accept -- channel
- *    counts 1..512, attention heads 1..32 with head_dim = c_hidden / heads <= 64, a
- *    transition hidden width <= 2048 -- runs on the general-shape kernels behind the same
- *    forward entry points (the stage entry points below are the tuned shape only). Beyond
- *    those limits GTK_ERR_UNSUPPORTED. Any B >= 1 and N >= 1.
+ *    zero-padded in the packed weights, which changes no result). Every other shape the
+ *    reference's modules accept -- channel counts 1..512, attention heads 1..32 with
+ *    head_dim = c_hidden / heads <= 64, a transition hidden width <= 2048 -- runs on the
+ *    general-shape kernels behind the same forward entry points (the stage entry points
+ *    below are the tuned shape only). Beyond those limits GTK_ERR_UNSUPPORTED. Any B >= 1
+ *    and N >= 1.
  *  - Thread safety: entry points may be called concurrently on different streams.
  */
 #ifndef GENIE_TK_B200_H_
@@ -211,7 +212,8 @@ GTK_API int gtk_triatt_pack(const gtk_triatt_params* params, int c_in, int c_hid
 GTK_API size_t gtk_triatt_workspace_bytes(int64_t B, int64_t N, int c_in, int c_hidden, int heads);
 
 /* out = update(z) or z + update(z) (add_residual; out may equal z). `inf` is the module's
- * mask constant (1e9 in the reference). z, out fp32 [B, N, N, 128]; mask fp32 [B, N, N] or NULL. */
+ * mask constant (1e9 in the reference). z, out fp32 [B, N, N, c_in]; mask fp32 [B, N, N] or
+ * NULL. */
 GTK_API int gtk_triatt_forward(int starting, const float* z, const float* mask, const void* packed, float* out,
                                int add_residual, void* workspace, size_t workspace_bytes, int64_t B, int64_t N,
                                int c_in, int c_hidden, int heads, float inf, uint32_t* status, void* stream);
