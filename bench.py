@@ -894,7 +894,8 @@ def main():
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                     help="multi-GPU exchanges: peer-memory push kernels over NVLink, or NCCL collectives")
     ap.add_argument("--trimul-exchange", default="auto", choices=["auto", "gather", "channels"],
-                    help="multi-GPU exchange of the multiplicative update (auto: gather for <= 3 GPUs)")
+                    help="multi-GPU exchange of the multiplicative update (auto: the channel shards when "
+                         "their x exchange is fused into the contraction's stores, else gather for <= 3 GPUs)")
     ap.add_argument("--op", default="stack", choices=["stack", "transition", "embed"],
                     help="stack: the headline workload (default); transition / embed: the pair-transition or "
                          "pair-embedding kernels alone")
