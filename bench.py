@@ -570,9 +570,9 @@ def run_sharded(args, rank, world, device):
     else:
         shard.prepare(B, N, device)
 
-    def step(zin=None, hook=None):
+    def step(zin=None, hook=None, zout=None):
         so.hook = hook
-        shard.forward_(z, mask, z_in=z0 if zin is None else zin, hook=hook)
+        shard.forward_(z if zout is None else zout, mask, z_in=z0 if zin is None else zin, hook=hook)
         so.hook = None
 
     for _ in range(args.warmup):
@@ -624,29 +624,81 @@ def run_sharded(args, rank, world, device):
 
     e2e = None
     if not args.no_e2e:
-        out_host = torch.empty_like(z_host).pin_memory()
+        # Each rank copies its own row shard in from pinned host memory and its result out,
+        # every step. Pipelined (the figure reported): two input and two output buffers, the
+        # H2D of step s+1 and the D2H of step s on their own streams while step s runs; the
+        # serial form (copy in, step, copy out on one stream) is reported beside it.
         cur = torch.cuda.current_stream(device)
-        z0.copy_(z_host, non_blocking=True)
-        step()
-        out_host.copy_(z, non_blocking=True)
-        torch.cuda.synchronize()
-        dist.barrier()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(cur)
-        for _ in range(args.steps):
-            z0.copy_(z_host, non_blocking=True)
-            step()
-            out_host.copy_(z, non_blocking=True)
-        e1.record(cur)
-        torch.cuda.synchronize()
-        dist.barrier()
-        t = torch.tensor([e0.elapsed_time(e1)], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e_ms = float(t.item()) / args.steps
-        e2e = {"value": B * L * N * N / (e_ms / 1e3), "unit": UNIT,
-               "h2d_bytes_per_step": z_host.numel() * 4 * world, "d2h_bytes_per_step": out_host.numel() * 4 * world,
-               "ms_per_step": e_ms, "note": "each rank copies its own row shard in and out"}
+        h2d, d2h = torch.cuda.Stream(device), torch.cuda.Stream(device)
+        out_host = [torch.empty_like(z_host).pin_memory() for _ in range(2)]
+        zin, zout = [z0, torch.empty_like(z0)], [z, torch.empty_like(z)]
+
+        def timed(fn):
+            torch.cuda.synchronize()
+            dist.barrier()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(cur)
+            fn()
+            e1.record(cur)
+            torch.cuda.synchronize()
+            dist.barrier()
+            t = torch.tensor([e0.elapsed_time(e1)], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return float(t.item()) / args.steps
+
+        def serial():
+            for _ in range(args.steps):
+                z0.copy_(z_host, non_blocking=True)
+                step()
+                out_host[0].copy_(z, non_blocking=True)
+
+        def pipelined():
+            K = args.steps
+            in_ready = [torch.cuda.Event(), torch.cuda.Event()]
+            step_done = [torch.cuda.Event(), torch.cuda.Event()]
+            out_read = [torch.cuda.Event(), torch.cuda.Event()]
+            h2d.wait_stream(cur)
+            d2h.wait_stream(cur)
+            with torch.cuda.stream(h2d):
+                zin[0].copy_(z_host, non_blocking=True)
+                in_ready[0].record(h2d)
+            for s in range(K):
+                b = s & 1
+                if s + 1 < K:
+                    nb = b ^ 1
+                    with torch.cuda.stream(h2d):
+                        if s >= 1:
+                            h2d.wait_event(step_done[nb])  # step s-1 has finished reading zin[nb]
+                        zin[nb].copy_(z_host, non_blocking=True)
+                        in_ready[nb].record(h2d)
+                cur.wait_event(in_ready[b])
+                if s >= 2:
+                    cur.wait_event(out_read[b])  # step s-2's result has left zout[b]
+                step(zin[b], zout=zout[b])
+                step_done[b].record(cur)
+                with torch.cuda.stream(d2h):
+                    d2h.wait_event(step_done[b])
+                    out_host[b].copy_(zout[b], non_blocking=True)
+                    out_read[b].record(d2h)
+            cur.wait_stream(d2h)
+            cur.wait_stream(h2d)
+
+        serial()  # warm-up
+        ms_serial = timed(serial)
+        serial_out = out_host[0].clone()
+        pipelined()  # warm-up of the second buffers and the copy streams
+        ms_pipe = timed(pipelined)
+        # every step has the same input, so the last pipelined result equals the serial one
+        same = torch.equal(out_host[(args.steps - 1) & 1], serial_out)
+        bytes_step = z_host.numel() * 4 * world
+        serial_line = {"value": B * L * N * N / (ms_serial / 1e3), "ms_per_step": ms_serial}
+        e_ms = ms_pipe if same else ms_serial
+        e2e = {"value": B * L * N * N / (e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": bytes_step,
+               "d2h_bytes_per_step": bytes_step, "ms_per_step": e_ms,
+               "mode": ("pipelined: H2D of step s+1 and D2H of step s on their own streams, overlapping step s"
+                        if same else "serial (the pipelined result differed)"),
+               "serial": serial_line, "note": "each rank copies its own row shard in and out"}
     parity = sharded_parity(stack, shard_step=step, z_out=z, rank=rank, world=world, device=device,
                             mask=mask, N=N, B=B)
     peaks = load_peaks()
