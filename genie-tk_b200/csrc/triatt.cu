@@ -729,7 +729,9 @@ __global__ void __launch_bounds__(k4::kThreads, 1)
                       mbar_wait(&bars->bias_full[bs], (kt >> 1) & 1, guard, status, kStatusTimeoutConsumer));
       if (!ok) break;
       const uint8_t* brow = smem + kBias + bs * kBiasStage;
-#pragma unroll
+      // not unrolled: one copy of the row step's long straight-line body keeps the
+      // instruction footprint small
+#pragma unroll 1
       for (int rr = 0; rr < 2; ++rr) {
         const int r = wg + 2 * rr;
         const int t = kt * kR + r, s = t % kKVS;
